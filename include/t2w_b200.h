@@ -1,0 +1,172 @@
+/* C ABI of the B200 Token2Wav DiT/CFM solver (libt2w_b200.so).
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*); every entry point returns an int status (T2W_OK == 0,
+ * negative on error) and never aborts the process.  Device pointers are CUDA global memory on the current device.
+ * The solver enqueues all work on the given stream and does not synchronise unless a function says so.
+ *
+ * Reference interfaces replaced (paths inside InferMatrixLab/minicpm-o-4.5-single-gpu-engine):
+ *   t2w_create            FastDiT.__init__            engine/runtime/dit_fast.py:100-155 (weights cast once, adaLN
+ *                                                      modulations precomputed per step: dit_fast.py:157-178)
+ *   t2w_solve_packed      FastDiT.solve               engine/runtime/dit_fast.py:432-495, and
+ *                         BatchedToken2Wav._solve     engine/runtime/token2wav_batch.py:632-702 (CFG Euler solve)
+ *   t2w_mods              FastDiT._modulations        engine/runtime/dit_fast.py:157-178
+ *   t2w_ln_mod            ln_mod / add_ln_mod         engine/runtime/dit_kernels.py:13-60
+ *   t2w_ln_mish           ln_mish                     engine/runtime/dit_kernels.py:145-164
+ *   t2w_gemm              F.linear calls of the block engine/runtime/dit_fast.py:283-301 (cuBLAS in the reference)
+ *   t2w_attn_varlen       BatchPrefillWithPagedKVCacheWrapper.run  engine/runtime/dit_fast.py:291,347-367
+ *   t2w_euler_cfg         the CFG combine + Euler step engine/runtime/dit_fast.py:302 / token2wav_batch.py:689-690
+ */
+#ifndef T2W_B200_H_
+#define T2W_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define T2W_API __attribute__((visibility("default")))
+#else
+#define T2W_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define T2W_OK 0
+#define T2W_ERR_INVALID (-1)     /* bad argument or shape */
+#define T2W_ERR_CUDA (-2)        /* a CUDA runtime call failed (t2w_last_cuda_error gives the code) */
+#define T2W_ERR_OOM (-3)         /* device allocation failed */
+#define T2W_ERR_TIMEOUT (-4)     /* a kernel's bounded wait gave up (reported by t2w_check) */
+#define T2W_ERR_UNSUPPORTED (-5) /* config outside the kernels' shape set, or no sm_100 device */
+#define T2W_ERR_WORKSPACE (-6)   /* workspace too small */
+
+#define T2W_PREC_BF16 0 /* bf16 weights and activations, fp32 accumulate */
+#define T2W_PREC_FP8 1  /* e4m3 weights (per 1x128 block power-of-two fp32 scales) and per-token-scaled e4m3 activations */
+
+#define T2W_FLAG_GRAPH 1u /* capture the whole solve in a CUDA graph per (layout, buffers) key and replay it */
+
+/* Hyper-parameters (the reference reads them off the estimator module: dit_fast.py:109-114, dit_graph.py:56-60). */
+typedef struct t2w_config {
+  int32_t mel, hidden, depth, heads, head_dim, ffn, steps, freq_dim;
+  float cfg_rate, t_scale, max_period, eps_block, eps_final, eps_qk, eps_conv;
+} t2w_config;
+
+/* Weight slots: the `weights` array of t2w_create holds T2W_W_COUNT global pointers followed by depth * T2W_B_COUNT
+ * per-block pointers (block b at T2W_W_COUNT + b * T2W_B_COUNT).  Every pointer is fp32 device memory in the
+ * reference module's own layout (nn.Linear [out, in], Conv1d [out, in, k]); names are the state-dict paths of
+ * stepaudio2's DiT (estimator.<...>). */
+enum t2w_weight_slot {
+  T2W_W_TEMB_FC1_W = 0, /* t_embedder.mlp.0.weight [H, freq]   */
+  T2W_W_TEMB_FC1_B,     /* t_embedder.mlp.0.bias               */
+  T2W_W_TEMB_FC2_W,     /* t_embedder.mlp.2.weight [H, H]      */
+  T2W_W_TEMB_FC2_B,
+  T2W_W_IN_W,           /* in_proj.weight [H, 4 mel]           */
+  T2W_W_IN_B,
+  T2W_W_FINAL_ADA_W,    /* final_layer.adaLN_modulation.1.weight [2H, H] */
+  T2W_W_FINAL_ADA_B,
+  T2W_W_FINAL_W,        /* final_layer.linear.weight [mel, H]  */
+  T2W_W_FINAL_B,
+  T2W_W_COUNT
+};
+enum t2w_block_slot {
+  T2W_B_ADA_W = 0, /* blocks.i.adaLN_modulation.1.weight [9H, H] */
+  T2W_B_ADA_B,
+  T2W_B_Q_W, T2W_B_Q_B, T2W_B_K_W, T2W_B_K_B, T2W_B_V_W, T2W_B_V_B, /* attn.to_q/to_k/to_v */
+  T2W_B_QN_W, T2W_B_QN_B, T2W_B_KN_W, T2W_B_KN_B,                   /* attn.q_norm / k_norm [head_dim] */
+  T2W_B_PROJ_W, T2W_B_PROJ_B,                                       /* attn.proj */
+  T2W_B_C1_W, T2W_B_C1_B,                                           /* conv.block.1 (Conv1d [H, H, 3]) */
+  T2W_B_CLN_W, T2W_B_CLN_B,                                         /* conv.block.3 (LayerNorm [H]) */
+  T2W_B_C2_W, T2W_B_C2_B,                                           /* conv.block.6 */
+  T2W_B_FC1_W, T2W_B_FC1_B, T2W_B_FC2_W, T2W_B_FC2_B,               /* mlp.fc1 / mlp.fc2 */
+  T2W_B_COUNT
+};
+
+typedef struct t2w_solver t2w_solver;
+
+/* One packed solve: n_streams requests, stream i = P_i prompt frames then T_i chunk frames (L_i = P_i + T_i).  The
+ * token-major inputs concatenate the streams' frames: n_tok = sum L_i rows of `mel` floats.  cond is the prompt mel
+ * over prompt frames and zeros over chunk frames; spk is the post-affine speaker vector.  The CFG uncond rows (zero
+ * mu / spk / cond) are made on the device.  out receives the final x of every frame (the chunk mel is rows
+ * P_i .. L_i - 1 of stream i). */
+typedef struct t2w_batch {
+  int32_t n_streams;
+  const int32_t* prompt_len; /* host [n_streams] */
+  const int32_t* chunk_len;  /* host [n_streams] */
+  const float* x0;           /* device [n_tok, mel] */
+  const float* mu;           /* device [n_tok, mel] */
+  const float* cond;         /* device [n_tok, mel] */
+  const float* spk;          /* device [n_streams, mel] */
+  float* out;                /* device [n_tok, mel] */
+} t2w_batch;
+
+/* Library / device probes. */
+T2W_API int t2w_version(void);
+T2W_API int t2w_device_ok(int device); /* 1 when `device` is an sm_100 GPU the kernels can run on, else 0 */
+T2W_API int t2w_last_cuda_error(void); /* the cudaError_t of the last T2W_ERR_CUDA on this thread */
+
+/* Build a solver on the current device: casts / quantises the weights once into solver-owned memory and computes every
+ * step's adaLN modulations (t_embedder + adaLN_modulation of each block and the final layer) with the time-embedding
+ * kernel.  t_sched: host [2 * steps] fp32 (t, dt) per Euler step as the reference's solver loop produces them
+ * (token2wav_batch.py:669-693), or NULL for the cosine schedule evaluated in double.  `stream` orders the set-up work;
+ * the call synchronises it before returning. */
+T2W_API int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* weights, int32_t n_weights,
+               int32_t precision, void* stream, t2w_solver** out);
+T2W_API int t2w_destroy(t2w_solver* s);
+
+/* Workspace bytes a t2w_solve_packed call with these lengths needs (0 on invalid lengths). */
+T2W_API size_t t2w_workspace_bytes(const t2w_solver* s, int32_t n_streams, const int32_t* prompt_len, const int32_t* chunk_len);
+
+/* The full S-step CFG Euler solve of a packed batch on `stream` (asynchronous). */
+T2W_API int t2w_solve_packed(t2w_solver* s, const t2w_batch* batch, void* workspace, size_t workspace_bytes, uint32_t flags,
+                     void* stream);
+
+/* Synchronise the solver's error word: T2W_OK, or T2W_ERR_TIMEOUT if a kernel gave up on a wait (then cleared). */
+T2W_API int t2w_check(t2w_solver* s);
+
+/* Copy the solver's modulation tables to device memory: mods [steps, depth, 9, H] (order sh_msa, 1+sc_msa, g_msa,
+ * sh_mlp, 1+sc_mlp, g_mlp, sh_conv, 1+sc_conv, g_conv) and final [steps, 2, H] (sh, 1+sc); dts [steps] fp32. */
+T2W_API int t2w_mods(const t2w_solver* s, float* mods, float* final_mods, float* dts, void* stream);
+
+/* Counters: graph replays, graph captures, eager solves. */
+T2W_API int t2w_counts(const t2w_solver* s, int64_t* graph_replays, int64_t* graph_captures, int64_t* eager_solves);
+
+/* ---- single kernels (test entry points; bf16 buffers are passed as void*) ---------------------------------------- */
+
+/* out[r] = bf16(LN(h[r]) * scale1 + shift) (LayerNorm without affine, fp32 math); rows whose pad[r] != 0 are zero. */
+T2W_API int t2w_ln_mod(const float* h, int32_t ld_h, const float* shift, const float* scale1, float eps, int32_t rows,
+               int32_t C, void* out_bf16, int32_t ld_out, const uint8_t* pad, void* stream);
+
+/* out[r] = bf16(Mish(LN_affine(x[r]))) with x bf16; rows whose pad[r] != 0 are zero. */
+T2W_API int t2w_ln_mish(const void* x_bf16, const float* w, const float* b, float eps, int32_t rows, int32_t C,
+                void* out_bf16, const uint8_t* pad, void* stream);
+
+#define T2W_EPI_F32 0   /* out fp32 = acc + bias */
+#define T2W_EPI_BF16 1  /* out bf16 = acc + bias */
+#define T2W_EPI_GELU 2  /* out bf16 = gelu_tanh(acc + bias) */
+#define T2W_EPI_RESID 3 /* resid fp32 += gate * (acc + bias) (in place) */
+#define T2W_EPI_QKV 4   /* out bf16 = [LN_q(q) | LN_k(k) | v] per 64-wide head (q/k affine norms) */
+
+/* C[M, N] = sum_tap A[m + tap_row0 + tap, :K] . W[n, tap*K : (tap+1)*K] then the epilogue.  A bf16 [rows_a, lda],
+ * W bf16 [N, taps*K]; rows outside [0, rows_a) read as zero (causal-conv taps).  M % 128 == 0, K % 64 == 0, N % 16 == 0.
+ * qk: for T2W_EPI_QKV, [qn_w, qn_b, kn_w, kn_b] (head_dim each) and qk_eps; q columns [0, N/3), k [N/3, 2N/3). */
+T2W_API int t2w_gemm(const void* A_bf16, int32_t lda, int32_t rows_a, const void* W_bf16, const float* bias, int32_t M,
+             int32_t N, int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo, float* resid,
+             int32_t ld_resid, const float* gate, const float* const* qk, float qk_eps, void* stream);
+
+/* Varlen attention over packed sequences with the block-causal chunk mask: sequence s has its keys at rows
+ * seq_row[s] .. seq_row[s] + seq_len[s] - 1 of qkv (bf16 [rows, 3 * heads * 64], q | k | v column blocks); a query at
+ * position i attends keys j < (i < prompt_len[s] ? prompt_len[s] : seq_len[s]).  out bf16 [rows, heads * 64].
+ * seq_row / seq_len / prompt_len are host arrays. */
+T2W_API int t2w_attn_varlen(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
+                    const int32_t* seq_len, const int32_t* prompt_len, void* out_bf16, void* stream);
+
+/* x[i] += dt ((1 + w) dphi[row[i]] - w dphi[row[i] + half_rows]) for the n_tok cond tokens (mel floats each); also
+ * writes bf16(x) into hx[row] and hx[row + half_rows] (first mel columns of ld_hx) and, when out != NULL, out[i] = x. */
+T2W_API int t2w_euler_cfg(float* x, const float* dphi, int32_t ld_dphi, const int32_t* tok_row, int32_t n_tok, int32_t mel,
+                  int32_t half_rows, float dt, float w, void* hx_bf16, int32_t ld_hx, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* T2W_B200_H_ */

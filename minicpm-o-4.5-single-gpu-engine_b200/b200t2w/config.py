@@ -1,0 +1,95 @@
+"""The one place the Token2Wav DiT/CFM hyper-parameters live.
+
+The reference reads these off the loaded ``stepaudio2`` estimator module (``engine/runtime/dit_fast.py:109-114,129``;
+``engine/runtime/dit_graph.py:56-60``): depth = ``len(est.blocks)``, heads / head_dim from ``blocks[0].attn``, hidden =
+``in_proj.out_features``, mel = ``in_proj.in_features // 4``, ``cfm.inference_cfg_rate``.  The checkpoint's
+``assets/token2wav`` config that fixes their values is not available here, so the defaults below are the
+reference-config values as published for Step-Audio2 / CosyVoice2 ``flow.yaml`` and are UNVERIFIED against the
+checkpoint.  The oracle, the weight packer and the CUDA kernels all read them from a ``DiTConfig``; a correction is a
+one-line change here.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, replace
+
+
+@dataclass(frozen=True)
+class DiTConfig:
+    mel: int = 80                 # mel channels; in_proj takes [x, mu, spk, cond] = 4 * mel (dit_graph.py:59)
+    hidden: int = 512             # in_proj.out_features (unverified)
+    depth: int = 16               # len(est.blocks) (unverified; consistent with token2wav_batch.py:706's 18 GB figure)
+    heads: int = 8                # blocks[i].attn.num_heads (unverified)
+    head_dim: int = 64            # blocks[i].attn.head_dim (the reference's fused q/k norm requires 64, dit_kernels.py:139)
+    mlp_ratio: float = 4.0        # DiTBlock MLP hidden = mlp_ratio * hidden (unverified)
+    steps: int = 10               # Euler steps (Token2Wav n_timesteps, models/token2wav.py:250)
+    cfg_rate: float = 0.7         # cfm.inference_cfg_rate (unverified)
+    freq_dim: int = 256           # TimestepEmbedder sinusoid size (unverified)
+    t_scale: float = 1000.0       # TimestepEmbedder multiplies t by this before the sinusoid (unverified)
+    max_period: float = 10000.0   # sinusoid max period (unverified)
+    eps_block: float = 1e-6       # norm1/norm2/norm3 (no affine) (unverified)
+    eps_final: float = 1e-6       # final_layer.norm_final (no affine) (unverified)
+    eps_qk: float = 1e-5          # attn.q_norm / attn.k_norm (affine, shared eps: dit_fast.py:134) (unverified)
+    eps_conv: float = 1e-5        # conv.block[3] LayerNorm (affine) (unverified)
+    conv_kernel: int = 3          # CausalConv1d kernel; 2 cached frames (token2wav_batch.py:82-97)
+
+    @property
+    def ffn(self) -> int:
+        return int(self.hidden * self.mlp_ratio)
+
+    @property
+    def in_dim(self) -> int:
+        return 4 * self.mel
+
+    @property
+    def conv_pad(self) -> int:
+        return self.conv_kernel - 1
+
+    @property
+    def sm_scale(self) -> float:
+        return 1.0 / math.sqrt(self.head_dim)  # SDPA default scale (dit_fast.py:365 plans no sm_scale)
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+    def validate_for_kernels(self) -> None:
+        """Shape limits of the sm_100a kernels (the oracle has none)."""
+        if self.head_dim != 64:
+            raise ValueError("the attention and q/k-norm kernels take head_dim == 64")
+        if self.hidden != self.heads * self.head_dim:
+            raise ValueError("hidden must equal heads * head_dim")
+        if self.hidden % 128 or self.ffn % 128:
+            raise ValueError("hidden and the MLP width must be multiples of 128")
+        if self.hidden > 1024:
+            raise ValueError("the row kernels hold one hidden row per warp (hidden <= 1024)")
+        if self.mel > 128 or self.mel % 16:
+            raise ValueError("mel must be a multiple of 16 and at most 128")
+        if self.conv_kernel != 3:
+            raise ValueError("the causal conv kernels take kernel size 3")
+
+
+REFERENCE = DiTConfig()
+"""The reference-config (unverified) used by every benchmark configuration."""
+
+TINY = replace(REFERENCE, hidden=128, depth=2, heads=2, mlp_ratio=4.0)
+"""A small config with the same kernel shapes class (head_dim 64), for fast golden fixtures and unit tests."""
+
+
+def t_schedule(steps: int):
+    """The solver's t recurrence in fp32, as ``BatchedToken2Wav._solve`` runs it (token2wav_batch.py:669-693):
+    ``t_span = 1 - cos(linspace(0, 1, S + 1) * pi / 2)``; ``t`` starts at ``t_span[0]`` and is accumulated as ``t + dt``
+    (not read from ``t_span``), ``dt = t_span[step + 1] - t``.  Returns (ts, dts) as python floats of the fp32 values."""
+    import torch
+
+    t_span = torch.linspace(0, 1, steps + 1, dtype=torch.float32)
+    t_span = 1 - torch.cos(t_span * 0.5 * torch.pi)
+    t, dt = t_span[0].clone(), t_span[1] - t_span[0]
+    ts, dts = [], []
+    for step in range(1, steps + 1):
+        ts.append(float(t))
+        dts.append(float(dt))
+        t = t + dt
+        if step < steps:
+            dt = t_span[step + 1] - t
+    return ts, dts

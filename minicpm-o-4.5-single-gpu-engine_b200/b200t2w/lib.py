@@ -1,0 +1,116 @@
+"""ctypes binding of ``libt2w_b200.so`` (the C ABI declared in ``include/t2w_b200.h``).
+
+There is no fallback: if the library is missing or the device is not an sm_100 GPU, calls raise.  Status codes become
+``T2WError`` exceptions carrying the C status and, for CUDA failures, the CUDA error code.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from .build import INCLUDE, LIB_PATH
+
+T2W_OK = 0
+STATUS = {-1: "invalid argument or shape", -2: "CUDA error", -3: "out of device memory", -4: "kernel wait timed out",
+          -5: "unsupported config or device", -6: "workspace too small"}
+PREC = {"bf16": 0, "fp8": 1}
+FLAG_GRAPH = 1
+EPI = {"f32": 0, "bf16": 1, "gelu": 2, "resid": 3, "qkv": 4}
+W_GLOBAL = ["estimator.t_embedder.mlp.0.weight", "estimator.t_embedder.mlp.0.bias", "estimator.t_embedder.mlp.2.weight",
+            "estimator.t_embedder.mlp.2.bias", "estimator.in_proj.weight", "estimator.in_proj.bias",
+            "estimator.final_layer.adaLN_modulation.1.weight", "estimator.final_layer.adaLN_modulation.1.bias",
+            "estimator.final_layer.linear.weight", "estimator.final_layer.linear.bias"]
+W_BLOCK = ["adaLN_modulation.1.weight", "adaLN_modulation.1.bias", "attn.to_q.weight", "attn.to_q.bias",
+           "attn.to_k.weight", "attn.to_k.bias", "attn.to_v.weight", "attn.to_v.bias", "attn.q_norm.weight",
+           "attn.q_norm.bias", "attn.k_norm.weight", "attn.k_norm.bias", "attn.proj.weight", "attn.proj.bias",
+           "conv.block.1.weight", "conv.block.1.bias", "conv.block.3.weight", "conv.block.3.bias", "conv.block.6.weight",
+           "conv.block.6.bias", "mlp.fc1.weight", "mlp.fc1.bias", "mlp.fc2.weight", "mlp.fc2.bias"]
+
+
+class T2WError(RuntimeError):
+    def __init__(self, fn: str, status: int, cuda: int = 0):
+        msg = f"{fn} failed: {STATUS.get(status, 'unknown')} (status {status}"
+        msg += f", cudaError {cuda})" if status == -2 else ")"
+        super().__init__(msg)
+        self.status, self.cuda = status, cuda
+
+
+class Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("mel", "hidden", "depth", "heads", "head_dim", "ffn", "steps", "freq_dim")] + \
+               [(n, ctypes.c_float) for n in ("cfg_rate", "t_scale", "max_period", "eps_block", "eps_final", "eps_qk", "eps_conv")]
+
+
+class Batch(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_int32), ("prompt_len", ctypes.POINTER(ctypes.c_int32)),
+                ("chunk_len", ctypes.POINTER(ctypes.c_int32)), ("x0", ctypes.c_void_p), ("mu", ctypes.c_void_p),
+                ("cond", ctypes.c_void_p), ("spk", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int32
+_F = ctypes.c_float
+_SIGS = {
+    "t2w_version": ([], ctypes.c_int),
+    "t2w_device_ok": ([ctypes.c_int], ctypes.c_int),
+    "t2w_last_cuda_error": ([], ctypes.c_int),
+    "t2w_create": ([ctypes.POINTER(Config), ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_P), _I, _I, _P,
+                    ctypes.POINTER(_P)], ctypes.c_int),
+    "t2w_destroy": ([_P], ctypes.c_int),
+    "t2w_workspace_bytes": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_size_t),
+    "t2w_solve_packed": ([_P, ctypes.POINTER(Batch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
+    "t2w_check": ([_P], ctypes.c_int),
+    "t2w_mods": ([_P, _P, _P, _P, _P], ctypes.c_int),
+    "t2w_counts": ([_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)],
+                   ctypes.c_int),
+    "t2w_ln_mod": ([_P, _I, _P, _P, _F, _I, _I, _P, _I, _P, _P], ctypes.c_int),
+    "t2w_ln_mish": ([_P, _P, _P, _F, _I, _I, _P, _P, _P], ctypes.c_int),
+    "t2w_gemm": ([_P, _I, _I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, ctypes.POINTER(_P), _F, _P],
+                 ctypes.c_int),
+    "t2w_attn_varlen": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P], ctypes.c_int),
+    "t2w_euler_cfg": ([_P, _P, _I, _P, _I, _I, _I, _F, _F, _P, _I, _P, _P], ctypes.c_int),
+}
+
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Every function the public headers declare."""
+    out = []
+    for f in sorted(os.listdir(INCLUDE)):
+        if f.endswith(".h"):
+            src = open(os.path.join(INCLUDE, f)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            out += re.findall(r"^\s*(?:T2W_API\s+)?(?:size_t|int|void)\s+(t2w_\w+)\s*\(", src, flags=re.M)
+    return out
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load (once) and type the library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        path = path or LIB_PATH
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: build it with b200t2w.build.build()")
+        lib = ctypes.CDLL(path)
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes, fn.restype = args, res
+        _lib = lib
+    return _lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != T2W_OK:
+        raise T2WError(fn, status, load().t2w_last_cuda_error() if status == -2 else 0)
+
+
+def call(fn: str, *args) -> int:
+    rc = getattr(load(), fn)(*args)
+    check(fn, rc)
+    return rc
+
+
+def i32_array(xs) -> ctypes.Array:
+    return (ctypes.c_int32 * len(xs))(*[int(x) for x in xs])

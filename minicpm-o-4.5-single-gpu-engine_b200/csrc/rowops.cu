@@ -1,0 +1,328 @@
+// Memory-bound row kernels of the solve: LayerNorm + adaLN modulation, LayerNorm(affine) + Mish, the CFG / Euler update,
+// input packing, weight conversion, and the once-per-solver time-embedding + adaLN modulation tables.
+// One warp per row, 128-bit loads, warp-shuffle reductions, fp32 math (the reference's Triton kernels also normalise in
+// fp32 and round once to the activation type: engine/runtime/dit_kernels.py:1-60,145-164).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace t2w {
+
+namespace {
+
+constexpr int kRowsPerBlock = 8;  // warps per block
+
+// LN over C = 128 * V values held as V float4 per lane (column 4 (32 i + lane) + e).
+template <int V>
+T2W_DEV void row_stats(const float4 (&x)[V], int C, float eps, float& mean, float& rstd) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) s += (x[i].x + x[i].y) + (x[i].z + x[i].w);
+  mean = warp_sum(s) / (float)C;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float a = x[i].x - mean, b = x[i].y - mean, c = x[i].z - mean, d = x[i].w - mean;
+    ss += (a * a + b * b) + (c * c + d * d);
+  }
+  rstd = rsqrtf(warp_sum(ss) / (float)C + eps);
+}
+
+T2W_DEV void store_bf16x4(__nv_bfloat16* dst, float a, float b, float c, float d) {
+  uint2 u;
+  u.x = pack_bf16x2(a, b);
+  u.y = pack_bf16x2(c, d);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int ldh, const float* __restrict__ shift,
+                                                const float* __restrict__ scale1, float eps, int rows,
+                                                __nv_bfloat16* __restrict__ out, int ldo,
+                                                const uint8_t* __restrict__ pad) {
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int C = 128 * V;
+  __nv_bfloat16* o = out + (size_t)row * ldo;
+  if (pad && pad[row]) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) store_bf16x4(o + 4 * (32 * i + lane), 0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  float4 x[V];
+  const float4* hr = reinterpret_cast<const float4*>(h + (size_t)row * ldh);
+#pragma unroll
+  for (int i = 0; i < V; ++i) x[i] = hr[32 * i + lane];
+  float mean, rstd;
+  row_stats<V>(x, C, eps, mean, rstd);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = 4 * (32 * i + lane);
+    const float4 sc = __ldg(reinterpret_cast<const float4*>(scale1 + c));
+    const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + c));
+    store_bf16x4(o + c, fmaf((x[i].x - mean) * rstd, sc.x, sh.x), fmaf((x[i].y - mean) * rstd, sc.y, sh.y),
+                 fmaf((x[i].z - mean) * rstd, sc.z, sh.z), fmaf((x[i].w - mean) * rstd, sc.w, sh.w));
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) k_ln_mish(const __nv_bfloat16* __restrict__ xin, const float* __restrict__ w,
+                                                 const float* __restrict__ b, float eps, int rows,
+                                                 __nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ pad) {
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int C = 128 * V;
+  __nv_bfloat16* o = out + (size_t)row * C;
+  if (pad && pad[row]) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) store_bf16x4(o + 4 * (32 * i + lane), 0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  float4 x[V];
+  const uint2* xr = reinterpret_cast<const uint2*>(xin + (size_t)row * C);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const uint2 u = xr[32 * i + lane];
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    x[i] = make_float4(a.x, a.y, c.x, c.y);
+  }
+  float mean, rstd;
+  row_stats<V>(x, C, eps, mean, rstd);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = 4 * (32 * i + lane);
+    const float4 ww = __ldg(reinterpret_cast<const float4*>(w + c));
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(b + c));
+    store_bf16x4(o + c, mish(fmaf((x[i].x - mean) * rstd, ww.x, bb.x)), mish(fmaf((x[i].y - mean) * rstd, ww.y, bb.y)),
+                 mish(fmaf((x[i].z - mean) * rstd, ww.z, bb.z)), mish(fmaf((x[i].w - mean) * rstd, ww.w, bb.w)));
+  }
+}
+
+// hx rows: [x | mu | spk | cond] for the cond half, [x | 0 | 0 | 0] for the uncond half (CFG: zeroed conditioning,
+// token2wav_batch.py:672-674).  One thread per (token, mel channel).
+__global__ void k_pack(const float* __restrict__ x0, const float* __restrict__ mu, const float* __restrict__ cond,
+                       const float* __restrict__ spk, const int* __restrict__ tok_row, const int* __restrict__ tok_stream,
+                       int n_tok, int mel, int half_rows, __nv_bfloat16* __restrict__ hx, int ld_hx,
+                       float* __restrict__ x) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)n_tok * mel) return;
+  const int i = (int)(idx / mel), c = (int)(idx - (long long)i * mel);
+  const int r = tok_row[i], s = tok_stream[i];
+  const float xv = x0[idx];
+  x[idx] = xv;
+  __nv_bfloat16* a = hx + (size_t)r * ld_hx;
+  __nv_bfloat16* u = hx + (size_t)(r + half_rows) * ld_hx;
+  const __nv_bfloat16 xb = __float2bfloat16_rn(xv), z = __float2bfloat16_rn(0.f);
+  a[c] = xb;
+  a[mel + c] = __float2bfloat16_rn(mu[idx]);
+  a[2 * mel + c] = __float2bfloat16_rn(spk[(size_t)s * mel + c]);
+  a[3 * mel + c] = __float2bfloat16_rn(cond[idx]);
+  u[c] = xb;
+  u[mel + c] = z;
+  u[2 * mel + c] = z;
+  u[3 * mel + c] = z;
+}
+
+// x += dt ((1 + w) d - w u): the CFG combine and the Euler step in one pass (token2wav_batch.py:689-690).
+__global__ void k_euler(float* __restrict__ x, const float* __restrict__ dphi, int ld_dphi,
+                        const int* __restrict__ tok_row, int n_tok, int mel, int half_rows, float dt, float w,
+                        __nv_bfloat16* __restrict__ hx, int ld_hx, float* __restrict__ out) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)n_tok * mel) return;
+  const int i = (int)(idx / mel), c = (int)(idx - (long long)i * mel);
+  const int r = tok_row[i];
+  const float d = dphi[(size_t)r * ld_dphi + c], u = dphi[(size_t)(r + half_rows) * ld_dphi + c];
+  const float xv = x[idx] + dt * ((1.f + w) * d - w * u);
+  x[idx] = xv;
+  const __nv_bfloat16 xb = __float2bfloat16_rn(xv);
+  if (hx) {
+    hx[(size_t)r * ld_hx + c] = xb;
+    hx[(size_t)(r + half_rows) * ld_hx + c] = xb;
+  }
+  if (out) out[idx] = xv;
+}
+
+__global__ void k_f32_to_bf16(const float* __restrict__ s, __nv_bfloat16* __restrict__ d, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) d[i] = __float2bfloat16_rn(s[i]);
+}
+
+__global__ void k_conv_weight(const float* __restrict__ s, __nv_bfloat16* __restrict__ d, int cout, int cin, int k) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // over dst [cout, k * cin]
+  if (i >= (long long)cout * cin * k) return;
+  const int o = (int)(i / ((long long)k * cin));
+  const int rem = (int)(i - (long long)o * k * cin);
+  const int tap = rem / cin, c = rem - tap * cin;
+  d[i] = __float2bfloat16_rn(s[((size_t)o * cin + c) * k + tap]);
+}
+
+// Time embedding: sinusoid(t * t_scale) -> Linear -> SiLU -> Linear, then SiLU (the adaLN_modulation input).  One block
+// per step, one thread per hidden unit.
+__global__ void k_temb(const float* __restrict__ ts, const float* __restrict__ freqs, int freq_dim, float t_scale,
+                       const float* __restrict__ w1, const float* __restrict__ b1, const float* __restrict__ w2,
+                       const float* __restrict__ b2, int H, float* __restrict__ silu_temb) {
+  extern __shared__ float sm[];
+  float* emb = sm;             // [freq_dim]
+  float* hid = sm + freq_dim;  // [H]
+  const int s = blockIdx.x;
+  const float t = ts[s] * t_scale;
+  const int half = freq_dim / 2;
+  for (int k = threadIdx.x; k < half; k += blockDim.x) {
+    const float a = t * freqs[k];
+    emb[k] = cosf(a);
+    emb[half + k] = sinf(a);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < H; j += blockDim.x) {
+    float acc = b1[j];
+    for (int k = 0; k < freq_dim; ++k) acc = fmaf(w1[(size_t)j * freq_dim + k], emb[k], acc);
+    hid[j] = acc / (1.f + expf(-acc));
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < H; j += blockDim.x) {
+    float acc = b2[j];
+    for (int k = 0; k < H; ++k) acc = fmaf(w2[(size_t)j * H + k], hid[k], acc);
+    silu_temb[(size_t)s * H + j] = acc / (1.f + expf(-acc));
+  }
+}
+
+// Every adaLN output row j of one weight matrix W [R, H] for all steps: out[s, j] = b[j] + W[j] . silu_temb[s]; chunk
+// c = j / H is a scale when (c % 3) == 1 (sh, sc, g per branch; final layer: sh, sc), stored as 1 + scale.  One warp
+// per row (the row is read once for all steps), 128-bit loads.
+template <int MAXS>
+__global__ void k_adaln(const float* __restrict__ W, const float* __restrict__ b, int R, int H, int steps,
+                        const float* __restrict__ silu_temb, float* __restrict__ out, long long step_stride,
+                        int chunk_period) {
+  extern __shared__ float st[];  // [steps, H]
+  for (int i = threadIdx.x; i < steps * H; i += blockDim.x) st[i] = silu_temb[i];
+  __syncthreads();
+  const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (j >= R) return;
+  float acc[MAXS];
+#pragma unroll
+  for (int s = 0; s < MAXS; ++s) acc[s] = 0.f;
+  const float4* wr = reinterpret_cast<const float4*>(W + (size_t)j * H);
+  for (int k4 = lane; k4 < H / 4; k4 += 32) {
+    const float4 wv = __ldg(wr + k4);
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s) {
+      if (s < steps) {
+        const float4 tv = *reinterpret_cast<const float4*>(st + s * H + 4 * k4);
+        acc[s] = fmaf(wv.x, tv.x, fmaf(wv.y, tv.y, fmaf(wv.z, tv.z, fmaf(wv.w, tv.w, acc[s]))));
+      }
+    }
+  }
+  const int c = j / H;
+  const float add = ((c % chunk_period) == 1) ? 1.f : 0.f;
+#pragma unroll
+  for (int s = 0; s < MAXS; ++s) {
+    const float v = warp_sum(acc[s]);
+    if (s < steps && lane == 0) out[s * step_stride + j] = v + b[j] + add;
+  }
+}
+
+int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  return T2W_OK;
+}
+
+unsigned blocks_for(long long n, int per) { return (unsigned)((n + per - 1) / per); }
+
+}  // namespace
+
+int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scale1, float eps, int rows, int C,
+                  __nv_bfloat16* out, int ldo, const uint8_t* pad, cudaStream_t st) {
+  if (rows <= 0) return T2W_OK;
+  if (ldh % 4 || ldo % 4) return T2W_ERR_INVALID;
+  const unsigned g = blocks_for(rows, kRowsPerBlock);
+  switch (C) {
+    case 128: k_ln_mod<1><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
+    case 256: k_ln_mod<2><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
+    case 512: k_ln_mod<4><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
+    case 768: k_ln_mod<6><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
+    case 1024: k_ln_mod<8><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
+    default: return T2W_ERR_INVALID;
+  }
+  return check_launch();
+}
+
+int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C,
+                   __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st) {
+  if (rows <= 0) return T2W_OK;
+  const unsigned g = blocks_for(rows, kRowsPerBlock);
+  switch (C) {
+    case 128: k_ln_mish<1><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
+    case 256: k_ln_mish<2><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
+    case 512: k_ln_mish<4><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
+    case 768: k_ln_mish<6><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
+    case 1024: k_ln_mish<8><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
+    default: return T2W_ERR_INVALID;
+  }
+  return check_launch();
+}
+
+int launch_pack(const float* x0, const float* mu, const float* cond, const float* spk, const int* tok_row,
+                const int* tok_stream, int n_tok, int mel, int half_rows, __nv_bfloat16* hx, int ld_hx, float* x,
+                cudaStream_t st) {
+  const long long n = (long long)n_tok * mel;
+  if (n <= 0) return T2W_OK;
+  k_pack<<<blocks_for(n, 256), 256, 0, st>>>(x0, mu, cond, spk, tok_row, tok_stream, n_tok, mel, half_rows, hx, ld_hx, x);
+  return check_launch();
+}
+
+int launch_euler(float* x, const float* dphi, int ld_dphi, const int* tok_row, int n_tok, int mel, int half_rows,
+                 float dt, float w, __nv_bfloat16* hx, int ld_hx, float* out, cudaStream_t st) {
+  const long long n = (long long)n_tok * mel;
+  if (n <= 0) return T2W_OK;
+  k_euler<<<blocks_for(n, 256), 256, 0, st>>>(x, dphi, ld_dphi, tok_row, n_tok, mel, half_rows, dt, w, hx, ld_hx, out);
+  return check_launch();
+}
+
+int launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, long long n, cudaStream_t st) {
+  if (n <= 0) return T2W_OK;
+  k_f32_to_bf16<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, n);
+  return check_launch();
+}
+
+int launch_conv_weight(const float* src, __nv_bfloat16* dst, int cout, int cin, int k, cudaStream_t st) {
+  const long long n = (long long)cout * cin * k;
+  k_conv_weight<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, cout, cin, k);
+  return check_launch();
+}
+
+int launch_temb_mods(const float* ts, int steps, const float* freqs, int freq_dim, float t_scale, const float* fc1_w,
+                     const float* fc1_b, const float* fc2_w, const float* fc2_b, int H, const float* const* ada_w,
+                     const float* const* ada_b, int depth, const float* fin_w, const float* fin_b, float* silu_temb,
+                     float* mods, float* final_mods, cudaStream_t st) {
+  constexpr int MAXS = 16;
+  if (steps > MAXS || H % 128) return T2W_ERR_UNSUPPORTED;
+  k_temb<<<steps, 512, (freq_dim + H) * sizeof(float), st>>>(ts, freqs, freq_dim, t_scale, fc1_w, fc1_b, fc2_w, fc2_b,
+                                                               H, silu_temb);
+  int rc = check_launch();
+  if (rc) return rc;
+  const size_t sm = (size_t)steps * H * sizeof(float);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_adaln<MAXS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return T2W_ERR_CUDA;
+    }
+  }
+  const int warps = 8;
+  for (int b = 0; b < depth; ++b) {
+    const int R = 9 * H;
+    // mods layout [steps, depth, 9, H]: block b of step s at (s * depth + b) * 9H
+    k_adaln<MAXS><<<blocks_for(R, warps), 32 * warps, sm, st>>>(ada_w[b], ada_b[b], R, H, steps, silu_temb,
+                                                                 mods + (size_t)b * R, (long long)depth * R, 3);
+    if ((rc = check_launch())) return rc;
+  }
+  k_adaln<MAXS><<<blocks_for(2 * H, warps), 32 * warps, sm, st>>>(fin_w, fin_b, 2 * H, H, steps, silu_temb, final_mods,
+                                                                   2LL * H, 2);
+  return check_launch();
+}
+
+}  // namespace t2w

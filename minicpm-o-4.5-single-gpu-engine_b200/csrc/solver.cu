@@ -1,0 +1,704 @@
+// The Token2Wav DiT/CFM solver runtime and the C ABI of libt2w_b200.so.
+//
+// A solver owns its weights (cast to bf16 / re-laid out once at creation, as FastDiT casts them:
+// engine/runtime/dit_fast.py:131-145) and every step's adaLN modulation table (computed once on the device by the
+// time-embedding kernel, as FastDiT._modulations does on the host: dit_fast.py:157-178).  A solve is planned on the
+// host (token rows, pad rows, attention work items), its small index arrays are copied into the caller's workspace,
+// and the S-step CFG Euler loop is enqueued on the caller's stream: per step the in_proj GEMM, per block ten kernels
+// (LN+mod, QKV GEMM with the q/k norms, attention, proj GEMM + gated residual, LN+mod, conv GEMM, LN+Mish, conv GEMM +
+// gated residual, LN+mod, fc1 GEMM + GELU, fc2 GEMM + gated residual; 12 launches), then LN+mod, the final GEMM and the
+// fused CFG/Euler kernel.  With T2W_FLAG_GRAPH the whole solve is captured once per (layout, buffers) key into a CUDA
+// graph and replayed (the reference replays one graph per solve: dit_fast.py:393-422,470).
+//
+// Packed row layout (both CFG halves at fixed offsets, as dit_fast.py:19-23 lays its tokens out): the cond half holds
+// each stream's segment [2 zero rows | L_i frames]; the uncond half repeats it at row offset half_rows.  The two zero
+// rows in front of each segment are the causal convolutions' left padding (the reference's empty conv cache at a
+// prompt setup), so a conv tap is a plain row shift and the im2col matrix never exists.
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace t2w {
+
+static thread_local int g_last_cuda_error = 0;
+void set_cuda_error(cudaError_t e) { g_last_cuda_error = (int)e; }
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
+                  uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || !base || (reinterpret_cast<uintptr_t>(base) & 15) || (pitch_bytes & 15) || box_rows > 256 ||
+      box_cols * (uint32_t)elem_bytes != 128)
+    return false;
+  const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace t2w
+
+using namespace t2w;
+
+namespace {
+
+#define T2W_CUDA(call)                   \
+  do {                                   \
+    cudaError_t e_ = (call);             \
+    if (e_ != cudaSuccess) {             \
+      set_cuda_error(e_);                \
+      return T2W_ERR_CUDA;               \
+    }                                    \
+  } while (0)
+#define T2W_TRY(call)       \
+  do {                      \
+    int rc_ = (call);       \
+    if (rc_) return rc_;    \
+  } while (0)
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct BlockW {
+  __nv_bfloat16 *qkv, *proj, *c1, *c2, *fc1, *fc2;
+  float *b_qkv, *qn_w, *qn_b, *kn_w, *kn_b, *b_proj, *b_c1, *cln_w, *cln_b, *b_c2, *b_fc1, *b_fc2;
+  CUtensorMap tm_qkv, tm_proj, tm_c1, tm_c2, tm_fc1, tm_fc2;
+};
+
+struct Plan {
+  int n_streams = 0, n_tok = 0, half_rows = 0, rows = 0, n_work = 0;
+  std::vector<int> tok_row, tok_stream;
+  std::vector<uint8_t> pad;
+  std::vector<AttnWork> work;
+  uint64_t key = 0;
+};
+
+struct WsLayout {
+  size_t hx, h, a, qkv, o, c1, f, dphi, x, pad, tok_row, tok_stream, work, total;
+};
+
+uint64_t mix(uint64_t h, uint64_t v) {
+  h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+  return h * 0xff51afd7ed558ccdull;
+}
+
+}  // namespace
+
+struct t2w_solver {
+  t2w_config cfg{};
+  int precision = T2W_PREC_BF16;
+  int device = 0;
+  void* arena = nullptr;
+  __nv_bfloat16 *w_in = nullptr, *w_fin = nullptr;
+  float *b_in = nullptr, *b_fin = nullptr;
+  float *mods = nullptr, *final_mods = nullptr, *dts_dev = nullptr;
+  std::vector<float> dts;
+  std::vector<BlockW> blk;
+  CUtensorMap tm_in{}, tm_fin{};
+  int* err = nullptr;
+  std::unordered_map<uint64_t, cudaGraphExec_t> graphs;
+  std::unordered_map<uintptr_t, uint64_t> ws_meta;  // workspace -> plan key of the index arrays it holds
+  int64_t n_replays = 0, n_captures = 0, n_eager = 0;
+};
+
+namespace {
+
+bool valid_cfg(const t2w_config& c) {
+  return c.mel > 0 && c.mel % 16 == 0 && c.mel <= 128 && c.head_dim == 64 && c.heads > 0 &&
+         c.hidden == c.heads * c.head_dim && c.hidden % 128 == 0 && c.hidden <= 1024 && c.ffn % 128 == 0 &&
+         c.depth > 0 && c.steps > 0 && c.steps <= 16 && c.freq_dim > 0 && c.freq_dim % 2 == 0 &&
+         gemm_block_n(3 * c.hidden) && gemm_block_n(c.ffn) && gemm_block_n(c.hidden) && (4 * c.mel) % 64 == 0 &&
+         (c.mel == 80 || gemm_block_n(c.mel));
+}
+
+bool make_plan(const t2w_config& c, int n, const int* P, const int* T, Plan& pl) {
+  if (n <= 0 || !P || !T) return false;
+  pl = Plan();
+  pl.n_streams = n;
+  uint64_t key = mix(0, (uint64_t)n);
+  long long half = 0;
+  for (int i = 0; i < n; ++i) {
+    if (P[i] < 0 || T[i] < 0 || P[i] + T[i] <= 0) return false;
+    half += 2 + P[i] + T[i];
+    pl.n_tok += P[i] + T[i];
+    key = mix(mix(key, (uint64_t)P[i]), (uint64_t)T[i]);
+  }
+  half = (half + 7) / 8 * 8;
+  if (2 * half + 128 > (1ll << 30)) return false;
+  pl.half_rows = (int)half;
+  pl.rows = (int)((2 * half + 127) / 128 * 128);
+  pl.pad.assign(pl.rows, 1);
+  pl.tok_row.resize(pl.n_tok);
+  pl.tok_stream.resize(pl.n_tok);
+  int tok = 0, row = 0;
+  for (int i = 0; i < n; ++i) {
+    const int L = P[i] + T[i];
+    row += 2;
+    for (int t = 0; t < L; ++t) {
+      pl.tok_row[tok] = row + t;
+      pl.tok_stream[tok] = i;
+      pl.pad[row + t] = 0;
+      pl.pad[row + t + half] = 0;
+      ++tok;
+    }
+    for (int hh = 0; hh < 2; ++hh)
+      for (int q = 0; q < L; q += 128) pl.work.push_back(AttnWork{row + hh * (int)half + q, row + hh * (int)half, q, P[i], L});
+    row += L;
+  }
+  pl.n_work = (int)pl.work.size();
+  pl.key = mix(key, (uint64_t)c.hidden);
+  return true;
+}
+
+WsLayout layout(const t2w_config& c, const Plan& pl) {
+  WsLayout w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t R = (size_t)pl.rows, H = (size_t)c.hidden;
+  w.hx = take(R * 4 * c.mel * 2);
+  w.h = take(R * H * 4);
+  w.a = take(R * H * 2);
+  w.qkv = take(R * 3 * H * 2);
+  w.o = take(R * H * 2);
+  w.c1 = take(R * H * 2);
+  w.f = take(R * (size_t)c.ffn * 2);
+  w.dphi = take(R * (size_t)c.mel * 4);
+  w.x = take((size_t)pl.n_tok * c.mel * 4);
+  w.pad = take(R);
+  w.tok_row = take((size_t)pl.n_tok * 4);
+  w.tok_stream = take((size_t)pl.n_tok * 4);
+  w.work = take((size_t)pl.n_work * sizeof(AttnWork));
+  w.total = off;
+  return w;
+}
+
+template <class T>
+T* at(void* base, size_t off) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(base) + off);
+}
+
+bool weight_map(CUtensorMap* m, const void* w, int N, int Ktot) {
+  const int bn = gemm_block_n(N);
+  return bn && make_tmap_2d(m, w, 2, (uint64_t)N, (uint64_t)Ktot, (uint64_t)Ktot * 2, bn, 64);
+}
+
+// Enqueue one whole solve (no host synchronisation, graph-capturable).
+int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, cudaStream_t st) {
+  const t2w_config& c = s->cfg;
+  const WsLayout L = layout(c, pl);
+  const int H = c.hidden, R = pl.rows, mel = c.mel, F = c.ffn;
+  __nv_bfloat16* hx = at<__nv_bfloat16>(ws, L.hx);
+  float* h = at<float>(ws, L.h);
+  __nv_bfloat16* a = at<__nv_bfloat16>(ws, L.a);
+  __nv_bfloat16* qkv = at<__nv_bfloat16>(ws, L.qkv);
+  __nv_bfloat16* o = at<__nv_bfloat16>(ws, L.o);  // attention output, then the first conv's pre-norm output
+  __nv_bfloat16* c1 = at<__nv_bfloat16>(ws, L.c1);
+  __nv_bfloat16* f = at<__nv_bfloat16>(ws, L.f);
+  float* dphi = at<float>(ws, L.dphi);
+  float* x = at<float>(ws, L.x);
+  const uint8_t* pad = at<uint8_t>(ws, L.pad);
+  const int* tok_row = at<int>(ws, L.tok_row);
+  const int* tok_stream = at<int>(ws, L.tok_stream);
+  const AttnWork* work = at<AttnWork>(ws, L.work);
+
+  CUtensorMap tm_hx, tm_a, tm_o, tm_c1, tm_f, tm_qkv;
+  if (!make_tmap_2d(&tm_hx, hx, 2, R, 4 * mel, 4 * mel * 2, 128, 64) || !make_tmap_2d(&tm_a, a, 2, R, H, H * 2, 128, 64) ||
+      !make_tmap_2d(&tm_o, o, 2, R, H, H * 2, 128, 64) || !make_tmap_2d(&tm_c1, c1, 2, R, H, H * 2, 128, 64) ||
+      !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&tm_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 128, 64))
+    return T2W_ERR_INVALID;
+
+  T2W_CUDA(cudaMemsetAsync(hx, 0, (size_t)R * 4 * mel * 2, st));
+  T2W_TRY(launch_pack(b.x0, b.mu, b.cond, b.spk, tok_row, tok_stream, pl.n_tok, mel, pl.half_rows, hx, 4 * mel, x, st));
+
+  GemmArgs g;
+  g.rows_a = R;
+  g.M = R;
+  g.err = s->err;
+  AttnArgs at_args;
+  at_args.qkv = qkv;
+  at_args.rows = R;
+  at_args.heads = c.heads;
+  at_args.work = work;
+  at_args.n_work = pl.n_work;
+  at_args.out = o;
+  at_args.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)c.head_dim));
+  at_args.err = s->err;
+
+  for (int step = 0; step < c.steps; ++step) {
+    g = GemmArgs();
+    g.rows_a = R;
+    g.M = R;
+    g.err = s->err;
+    g.A = hx; g.lda = 4 * mel; g.W = s->w_in; g.bias = s->b_in; g.N = H; g.K = 4 * mel; g.epi = T2W_EPI_F32;
+    g.out = h; g.ldo = H;
+    T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in));
+    for (int bi = 0; bi < c.depth; ++bi) {
+      const BlockW& w = s->blk[bi];
+      const float* M = s->mods + ((size_t)step * c.depth + bi) * 9 * H;
+      const float *sh_a = M, *sc_a = M + H, *g_a = M + 2 * H, *sh_m = M + 3 * H, *sc_m = M + 4 * H, *g_m = M + 5 * H;
+      const float *sh_c = M + 6 * H, *sc_c = M + 7 * H, *g_c = M + 8 * H;
+      // attention branch
+      T2W_TRY(launch_ln_mod(h, H, sh_a, sc_a, c.eps_block, R, H, a, H, nullptr, st));
+      GemmArgs q = GemmArgs();
+      q.rows_a = R; q.M = R; q.err = s->err;
+      q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
+      q.qn_w = w.qn_w; q.qn_b = w.qn_b; q.kn_w = w.kn_w; q.kn_b = w.kn_b; q.qk_eps = c.eps_qk;
+      T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv));
+      T2W_TRY(launch_attn(at_args, st, &tm_qkv));
+      GemmArgs pr = GemmArgs();
+      pr.rows_a = R; pr.M = R; pr.err = s->err;
+      pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_RESID;
+      pr.resid = h; pr.ldr = H; pr.gate = g_a;
+      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj));
+      // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108)
+      T2W_TRY(launch_ln_mod(h, H, sh_c, sc_c, c.eps_block, R, H, a, H, pad, st));
+      GemmArgs k1 = GemmArgs();
+      k1.rows_a = R; k1.M = R; k1.err = s->err;
+      k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
+      k1.epi = T2W_EPI_BF16; k1.out = o; k1.ldo = H;
+      T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1));
+      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, c1, pad, st));
+      GemmArgs k2 = GemmArgs();
+      k2.rows_a = R; k2.M = R; k2.err = s->err;
+      k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
+      k2.epi = T2W_EPI_RESID; k2.resid = h; k2.ldr = H; k2.gate = g_c;
+      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2));
+      // MLP branch
+      T2W_TRY(launch_ln_mod(h, H, sh_m, sc_m, c.eps_block, R, H, a, H, nullptr, st));
+      GemmArgs f1 = GemmArgs();
+      f1.rows_a = R; f1.M = R; f1.err = s->err;
+      f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
+      T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1));
+      GemmArgs f2 = GemmArgs();
+      f2.rows_a = R; f2.M = R; f2.err = s->err;
+      f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_RESID;
+      f2.resid = h; f2.ldr = H; f2.gate = g_m;
+      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2));
+    }
+    const float* FM = s->final_mods + (size_t)step * 2 * H;
+    T2W_TRY(launch_ln_mod(h, H, FM, FM + H, c.eps_final, R, H, a, H, nullptr, st));
+    GemmArgs fin = GemmArgs();
+    fin.rows_a = R; fin.M = R; fin.err = s->err;
+    fin.A = a; fin.lda = H; fin.W = s->w_fin; fin.bias = s->b_fin; fin.N = mel; fin.K = H; fin.epi = T2W_EPI_F32;
+    fin.out = dphi; fin.ldo = mel;
+    T2W_TRY(launch_gemm(fin, st, &tm_a, &s->tm_fin));
+    const bool last = step == c.steps - 1;
+    T2W_TRY(launch_euler(x, dphi, mel, tok_row, pl.n_tok, mel, pl.half_rows, s->dts[step], c.cfg_rate,
+                         last ? nullptr : hx, 4 * mel, last ? b.out : nullptr, st));
+  }
+  return T2W_OK;
+}
+
+int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
+  const WsLayout L = layout(s->cfg, pl);
+  T2W_CUDA(cudaMemcpyAsync(at<uint8_t>(ws, L.pad), pl.pad.data(), pl.pad.size(), cudaMemcpyHostToDevice, st));
+  T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_row), pl.tok_row.data(), pl.tok_row.size() * 4, cudaMemcpyHostToDevice, st));
+  T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_stream), pl.tok_stream.data(), pl.tok_stream.size() * 4,
+                           cudaMemcpyHostToDevice, st));
+  T2W_CUDA(cudaMemcpyAsync(at<AttnWork>(ws, L.work), pl.work.data(), pl.work.size() * sizeof(AttnWork),
+                           cudaMemcpyHostToDevice, st));
+  s->ws_meta[reinterpret_cast<uintptr_t>(ws)] = pl.key;
+  return T2W_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int t2w_version(void) { return 1; }
+
+int t2w_last_cuda_error(void) { return g_last_cuda_error; }
+
+int t2w_device_ok(int device) {
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return 0;
+  return p.major == 10 ? 1 : 0;
+}
+
+int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* weights, int32_t n_weights,
+               int32_t precision, void* stream, t2w_solver** out) {
+  if (!cfg || !weights || !out || !valid_cfg(*cfg)) return T2W_ERR_INVALID;
+  if (precision != T2W_PREC_BF16) return T2W_ERR_UNSUPPORTED;
+  const t2w_config& c = *cfg;
+  if (n_weights != T2W_W_COUNT + c.depth * T2W_B_COUNT) return T2W_ERR_INVALID;
+  for (int i = 0; i < n_weights; ++i)
+    if (!weights[i]) return T2W_ERR_INVALID;
+  int dev = 0;
+  T2W_CUDA(cudaGetDevice(&dev));
+  if (!t2w_device_ok(dev)) return T2W_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int H = c.hidden, F = c.ffn, mel = c.mel, S = c.steps;
+
+  // arena: bf16 matrices, then fp32 vectors and tables
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_in = take((size_t)H * 4 * mel * 2), o_fin = take((size_t)mel * H * 2);
+  const size_t o_bin = take(H * 4), o_bfin = take(mel * 4);
+  const size_t o_mods = take((size_t)S * c.depth * 9 * H * 4), o_fmods = take((size_t)S * 2 * H * 4);
+  const size_t o_dts = take(S * 4), o_ts = take(S * 4), o_freq = take(c.freq_dim * 4), o_st = take((size_t)S * H * 4);
+  const size_t o_err = take(16);
+  std::vector<size_t> ob(c.depth * 18);
+  for (int b = 0; b < c.depth; ++b) {
+    size_t* q = &ob[b * 18];
+    q[0] = take((size_t)3 * H * H * 2);
+    q[1] = take((size_t)H * H * 2);
+    q[2] = take((size_t)H * 3 * H * 2);
+    q[3] = take((size_t)H * 3 * H * 2);
+    q[4] = take((size_t)F * H * 2);
+    q[5] = take((size_t)H * F * 2);
+    q[6] = take(3 * H * 4);
+    q[7] = take(c.head_dim * 4);
+    q[8] = take(c.head_dim * 4);
+    q[9] = take(c.head_dim * 4);
+    q[10] = take(c.head_dim * 4);
+    q[11] = take(H * 4);
+    q[12] = take(H * 4);
+    q[13] = take(H * 4);
+    q[14] = take(H * 4);
+    q[15] = take(H * 4);
+    q[16] = take(F * 4);
+    q[17] = take(H * 4);
+  }
+  t2w_solver* s = new t2w_solver();
+  s->cfg = c;
+  s->precision = precision;
+  s->device = dev;
+  if (cudaMalloc(&s->arena, off) != cudaSuccess) {
+    delete s;
+    return T2W_ERR_OOM;
+  }
+  void* A = s->arena;
+  auto fail = [&](int rc) {
+    cudaFree(s->arena);
+    delete s;
+    return rc;
+  };
+  auto W = [&](int slot) { return weights[slot]; };
+  auto BWp = [&](int b, int slot) { return weights[T2W_W_COUNT + b * T2W_B_COUNT + slot]; };
+  auto copyv = [&](float* dst, const float* src, size_t n) {
+    return cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess;
+  };
+  s->w_in = at<__nv_bfloat16>(A, o_in);
+  s->w_fin = at<__nv_bfloat16>(A, o_fin);
+  s->b_in = at<float>(A, o_bin);
+  s->b_fin = at<float>(A, o_bfin);
+  s->mods = at<float>(A, o_mods);
+  s->final_mods = at<float>(A, o_fmods);
+  s->dts_dev = at<float>(A, o_dts);
+  s->err = at<int>(A, o_err);
+  if (launch_f32_to_bf16(W(T2W_W_IN_W), s->w_in, (long long)H * 4 * mel, st) ||
+      launch_f32_to_bf16(W(T2W_W_FINAL_W), s->w_fin, (long long)mel * H, st) || !copyv(s->b_in, W(T2W_W_IN_B), H) ||
+      !copyv(s->b_fin, W(T2W_W_FINAL_B), mel))
+    return fail(T2W_ERR_CUDA);
+  s->blk.resize(c.depth);
+  std::vector<const float*> ada_w(c.depth), ada_b(c.depth);
+  for (int b = 0; b < c.depth; ++b) {
+    BlockW& w = s->blk[b];
+    const size_t* q = &ob[b * 18];
+    w.qkv = at<__nv_bfloat16>(A, q[0]);
+    w.proj = at<__nv_bfloat16>(A, q[1]);
+    w.c1 = at<__nv_bfloat16>(A, q[2]);
+    w.c2 = at<__nv_bfloat16>(A, q[3]);
+    w.fc1 = at<__nv_bfloat16>(A, q[4]);
+    w.fc2 = at<__nv_bfloat16>(A, q[5]);
+    w.b_qkv = at<float>(A, q[6]);
+    w.qn_w = at<float>(A, q[7]);
+    w.qn_b = at<float>(A, q[8]);
+    w.kn_w = at<float>(A, q[9]);
+    w.kn_b = at<float>(A, q[10]);
+    w.b_proj = at<float>(A, q[11]);
+    w.b_c1 = at<float>(A, q[12]);
+    w.cln_w = at<float>(A, q[13]);
+    w.cln_b = at<float>(A, q[14]);
+    w.b_c2 = at<float>(A, q[15]);
+    w.b_fc1 = at<float>(A, q[16]);
+    w.b_fc2 = at<float>(A, q[17]);
+    const long long HH = (long long)H * H;
+    bool ok = !launch_f32_to_bf16(BWp(b, T2W_B_Q_W), w.qkv, HH, st) &&
+              !launch_f32_to_bf16(BWp(b, T2W_B_K_W), w.qkv + HH, HH, st) &&
+              !launch_f32_to_bf16(BWp(b, T2W_B_V_W), w.qkv + 2 * HH, HH, st) &&
+              !launch_f32_to_bf16(BWp(b, T2W_B_PROJ_W), w.proj, HH, st) &&
+              !launch_conv_weight(BWp(b, T2W_B_C1_W), w.c1, H, H, 3, st) &&
+              !launch_conv_weight(BWp(b, T2W_B_C2_W), w.c2, H, H, 3, st) &&
+              !launch_f32_to_bf16(BWp(b, T2W_B_FC1_W), w.fc1, (long long)F * H, st) &&
+              !launch_f32_to_bf16(BWp(b, T2W_B_FC2_W), w.fc2, (long long)H * F, st) &&
+              copyv(w.b_qkv, BWp(b, T2W_B_Q_B), H) && copyv(w.b_qkv + H, BWp(b, T2W_B_K_B), H) &&
+              copyv(w.b_qkv + 2 * H, BWp(b, T2W_B_V_B), H) && copyv(w.qn_w, BWp(b, T2W_B_QN_W), c.head_dim) &&
+              copyv(w.qn_b, BWp(b, T2W_B_QN_B), c.head_dim) && copyv(w.kn_w, BWp(b, T2W_B_KN_W), c.head_dim) &&
+              copyv(w.kn_b, BWp(b, T2W_B_KN_B), c.head_dim) && copyv(w.b_proj, BWp(b, T2W_B_PROJ_B), H) &&
+              copyv(w.b_c1, BWp(b, T2W_B_C1_B), H) && copyv(w.cln_w, BWp(b, T2W_B_CLN_W), H) &&
+              copyv(w.cln_b, BWp(b, T2W_B_CLN_B), H) && copyv(w.b_c2, BWp(b, T2W_B_C2_B), H) &&
+              copyv(w.b_fc1, BWp(b, T2W_B_FC1_B), F) && copyv(w.b_fc2, BWp(b, T2W_B_FC2_B), H);
+    if (!ok) return fail(T2W_ERR_CUDA);
+    if (!weight_map(&w.tm_qkv, w.qkv, 3 * H, H) || !weight_map(&w.tm_proj, w.proj, H, H) ||
+        !weight_map(&w.tm_c1, w.c1, H, 3 * H) || !weight_map(&w.tm_c2, w.c2, H, 3 * H) ||
+        !weight_map(&w.tm_fc1, w.fc1, F, H) || !weight_map(&w.tm_fc2, w.fc2, H, F))
+      return fail(T2W_ERR_INVALID);
+    ada_w[b] = BWp(b, T2W_B_ADA_W);
+    ada_b[b] = BWp(b, T2W_B_ADA_B);
+  }
+  if (!weight_map(&s->tm_in, s->w_in, H, 4 * mel) || !weight_map(&s->tm_fin, s->w_fin, mel, H)) return fail(T2W_ERR_INVALID);
+
+  // t schedule: the caller's fp32 (t, dt) pairs, else the cosine schedule in double rounded to fp32
+  std::vector<float> ts(S);
+  s->dts.resize(S);
+  if (t_sched) {
+    for (int i = 0; i < S; ++i) {
+      ts[i] = t_sched[2 * i];
+      s->dts[i] = t_sched[2 * i + 1];
+    }
+  } else {
+    std::vector<double> span(S + 1);
+    for (int i = 0; i <= S; ++i) span[i] = 1.0 - std::cos((double)i / S * 0.5 * M_PI);
+    double t = span[0];
+    for (int i = 0; i < S; ++i) {
+      ts[i] = (float)t;
+      s->dts[i] = (float)(span[i + 1] - t);
+      t += span[i + 1] - t;
+    }
+  }
+  const int half = c.freq_dim / 2;
+  std::vector<float> freqs(half);
+  const float lnp = (float)(-std::log((double)c.max_period));
+  for (int k = 0; k < half; ++k) freqs[k] = std::exp(lnp * (float)k / (float)half);
+  float* ts_dev = at<float>(A, o_ts);
+  float* fr_dev = at<float>(A, o_freq);
+  if (cudaMemcpyAsync(ts_dev, ts.data(), S * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(s->dts_dev, s->dts.data(), S * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(fr_dev, freqs.data(), half * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemsetAsync(s->err, 0, 16, st) != cudaSuccess)
+    return fail(T2W_ERR_CUDA);
+  const int rc = launch_temb_mods(ts_dev, S, fr_dev, c.freq_dim, c.t_scale, W(T2W_W_TEMB_FC1_W), W(T2W_W_TEMB_FC1_B),
+                                  W(T2W_W_TEMB_FC2_W), W(T2W_W_TEMB_FC2_B), H, ada_w.data(), ada_b.data(), c.depth,
+                                  W(T2W_W_FINAL_ADA_W), W(T2W_W_FINAL_ADA_B), at<float>(A, o_st), s->mods,
+                                  s->final_mods, st);
+  if (rc) return fail(rc);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return fail(T2W_ERR_CUDA);
+  }
+  *out = s;
+  return T2W_OK;
+}
+
+int t2w_destroy(t2w_solver* s) {
+  if (!s) return T2W_ERR_INVALID;
+  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  cudaFree(s->arena);
+  delete s;
+  return T2W_OK;
+}
+
+size_t t2w_workspace_bytes(const t2w_solver* s, int32_t n, const int32_t* P, const int32_t* T) {
+  if (!s) return 0;
+  Plan pl;
+  if (!make_plan(s->cfg, n, P, T, pl)) return 0;
+  return layout(s->cfg, pl).total;
+}
+
+int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_bytes, uint32_t flags, void* stream) {
+  if (!s || !b || !ws || !b->x0 || !b->mu || !b->cond || !b->spk || !b->out) return T2W_ERR_INVALID;
+  Plan pl;
+  if (!make_plan(s->cfg, b->n_streams, b->prompt_len, b->chunk_len, pl)) return T2W_ERR_INVALID;
+  if (layout(s->cfg, pl).total > ws_bytes) return T2W_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return T2W_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uintptr_t wkey = reinterpret_cast<uintptr_t>(ws);
+  auto it = s->ws_meta.find(wkey);
+  if (it == s->ws_meta.end() || it->second != pl.key) T2W_TRY(upload_meta(s, pl, ws, st));
+  if (!(flags & T2W_FLAG_GRAPH)) {
+    T2W_TRY(enqueue_solve(s, pl, *b, ws, st));
+    ++s->n_eager;
+    return T2W_OK;
+  }
+  uint64_t key = pl.key;
+  for (const void* p : {(const void*)ws, (const void*)b->x0, (const void*)b->mu, (const void*)b->cond,
+                        (const void*)b->spk, (const void*)b->out})
+    key = mix(key, reinterpret_cast<uint64_t>(p));
+  auto g = s->graphs.find(key);
+  if (g == s->graphs.end()) {
+    cudaStreamCaptureStatus cs;
+    T2W_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: use flags = 0
+    T2W_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_solve(s, pl, *b, ws, st);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ec != cudaSuccess) {
+      set_cuda_error(ec);
+      return T2W_ERR_CUDA;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) {
+      set_cuda_error(ei);
+      return T2W_ERR_CUDA;
+    }
+    g = s->graphs.emplace(key, exec).first;
+    ++s->n_captures;
+  }
+  T2W_CUDA(cudaGraphLaunch(g->second, st));
+  ++s->n_replays;
+  return T2W_OK;
+}
+
+int t2w_check(t2w_solver* s) {
+  if (!s) return T2W_ERR_INVALID;
+  int v = 0;
+  T2W_CUDA(cudaMemcpy(&v, s->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    T2W_CUDA(cudaMemset(s->err, 0, sizeof(int)));
+    return v;
+  }
+  return T2W_OK;
+}
+
+int t2w_mods(const t2w_solver* s, float* mods, float* final_mods, float* dts, void* stream) {
+  if (!s) return T2W_ERR_INVALID;
+  const t2w_config& c = s->cfg;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mods) T2W_CUDA(cudaMemcpyAsync(mods, s->mods, (size_t)c.steps * c.depth * 9 * c.hidden * 4, cudaMemcpyDeviceToDevice, st));
+  if (final_mods)
+    T2W_CUDA(cudaMemcpyAsync(final_mods, s->final_mods, (size_t)c.steps * 2 * c.hidden * 4, cudaMemcpyDeviceToDevice, st));
+  if (dts) T2W_CUDA(cudaMemcpyAsync(dts, s->dts_dev, (size_t)c.steps * 4, cudaMemcpyDeviceToDevice, st));
+  return T2W_OK;
+}
+
+int t2w_counts(const t2w_solver* s, int64_t* replays, int64_t* captures, int64_t* eager) {
+  if (!s) return T2W_ERR_INVALID;
+  if (replays) *replays = s->n_replays;
+  if (captures) *captures = s->n_captures;
+  if (eager) *eager = s->n_eager;
+  return T2W_OK;
+}
+
+int t2w_ln_mod(const float* h, int32_t ld_h, const float* shift, const float* scale1, float eps, int32_t rows,
+               int32_t C, void* out, int32_t ld_out, const uint8_t* pad, void* stream) {
+  if (!h || !shift || !scale1 || !out) return T2W_ERR_INVALID;
+  return launch_ln_mod(h, ld_h, shift, scale1, eps, rows, C, static_cast<__nv_bfloat16*>(out), ld_out, pad,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int t2w_ln_mish(const void* x, const float* w, const float* b, float eps, int32_t rows, int32_t C, void* out,
+                const uint8_t* pad, void* stream) {
+  if (!x || !w || !b || !out) return T2W_ERR_INVALID;
+  return launch_ln_mish(static_cast<const __nv_bfloat16*>(x), w, b, eps, rows, C, static_cast<__nv_bfloat16*>(out),
+                        pad, static_cast<cudaStream_t>(stream));
+}
+
+int t2w_gemm(const void* A, int32_t lda, int32_t rows_a, const void* W, const float* bias, int32_t M, int32_t N,
+             int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo, float* resid,
+             int32_t ld_resid, const float* gate, const float* const* qk, float qk_eps, void* stream) {
+  GemmArgs g;
+  g.A = A;
+  g.lda = lda;
+  g.rows_a = rows_a;
+  g.W = W;
+  g.bias = bias;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.taps = taps;
+  g.tap_row0 = tap_row0;
+  g.epi = epi;
+  g.out = out;
+  g.ldo = ldo;
+  g.resid = resid;
+  g.ldr = ld_resid;
+  g.gate = gate;
+  if (qk) {
+    g.qn_w = qk[0];
+    g.qn_b = qk[1];
+    g.kn_w = qk[2];
+    g.kn_b = qk[3];
+  }
+  g.qk_eps = qk_eps;
+  return launch_gemm(g, static_cast<cudaStream_t>(stream));
+}
+
+int t2w_attn_varlen(const void* qkv, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
+                    const int32_t* seq_len, const int32_t* prompt_len, void* out, void* stream) {
+  if (!qkv || !out || !seq_row || !seq_len || !prompt_len || n_seq < 0 || heads <= 0) return T2W_ERR_INVALID;
+  std::vector<AttnWork> work;
+  for (int s = 0; s < n_seq; ++s) {
+    if (seq_len[s] <= 0 || prompt_len[s] < 0 || prompt_len[s] > seq_len[s] || seq_row[s] < 0 ||
+        seq_row[s] + seq_len[s] > rows)
+      return T2W_ERR_INVALID;
+    for (int q = 0; q < seq_len[s]; q += 128)
+      work.push_back(AttnWork{seq_row[s] + q, seq_row[s], q, prompt_len[s], seq_len[s]});
+  }
+  if (work.empty()) return T2W_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  AttnWork* d = nullptr;
+  T2W_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), work.size() * sizeof(AttnWork), st));
+  T2W_CUDA(cudaMemcpyAsync(d, work.data(), work.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st));
+  AttnArgs a;
+  a.qkv = qkv;
+  a.rows = rows;
+  a.heads = heads;
+  a.work = d;
+  a.n_work = (int)work.size();
+  a.out = out;
+  a.scale_log2 = (float)(1.4426950408889634 / 8.0);
+  const int rc = launch_attn(a, st);
+  cudaFreeAsync(d, st);
+  return rc;
+}
+
+int t2w_euler_cfg(float* x, const float* dphi, int32_t ld_dphi, const int32_t* tok_row, int32_t n_tok, int32_t mel,
+                  int32_t half_rows, float dt, float w, void* hx, int32_t ld_hx, float* out, void* stream) {
+  if (!x || !dphi || !tok_row) return T2W_ERR_INVALID;
+  return launch_euler(x, dphi, ld_dphi, tok_row, n_tok, mel, half_rows, dt, w, static_cast<__nv_bfloat16*>(hx), ld_hx,
+                      out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,304 @@
+#!/usr/bin/env python
+"""Benchmark of the Token2Wav DiT/CFM flow-matching solve on B200 (BASELINE.json metric: chunk mel frames/s per full
+CFG ODE solve, with p50 / p95 per-chunk latency).
+
+One "step" is one full S-step CFG Euler solve (one CUDA-graph replay) over one batch of packed ``[prompt | chunk]``
+streams.  Default workload (N = 1): benchmark config 2, 16 streams of a 300-frame prompt + 50-frame chunk, bf16,
+random-init reference-config weights, seeded synthetic inputs.  With ``--gpus N`` (launched by torchrun) every rank is
+an independent replica with its own 16 streams (weak scaling; streams never cross GPUs, so there is no collective on the
+data path, only a gloo barrier and a max over ranks of the device-timed region).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|target|c5|c3] [--impl b200|reference]
+
+``--impl reference`` times the reference's own algorithm on the host cores (the CPU oracle port of the reference
+solver, all threads), one stream of the workload per step, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "minicpm-o-4.5-single-gpu-engine_b200")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+
+from b200t2w.config import REFERENCE, DiTConfig  # noqa: E402
+from b200t2w.workload import C2, C3, C5, TARGET, Workload, make_streams, uniform_streams  # noqa: E402
+
+METRIC = "DiT mel frames/s per full CFG ODE solve"
+UNIT = "mel frames/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-profile", action="store_true")
+    return ap.parse_args()
+
+
+def shard(name: str, rank: int, world: int) -> Workload:
+    """This rank's streams.  c2 / target: a fixed per-GPU batch (weak scaling); c5: 1024 streams split by rank."""
+    if name == "c5":
+        n = C5.streams // world
+        return Workload(f"{C5.name}[rank {rank}/{world}]", C5.seed, C5.lengths[rank * n:(rank + 1) * n])
+    base = {"c2": C2, "target": TARGET, "c3": C3}[name]
+    if world == 1:
+        return base
+    return Workload(f"{base.name}[rank {rank}]", base.seed + 1000 * rank, base.lengths)
+
+
+def flops_per_solve(cfg: DiTConfig, lengths) -> tuple[float, float]:
+    """(GEMM FLOPs, attention FLOPs) of one full CFG solve, from the per-token / per-key formulas of the path:
+    per token per block 2H(10H + 2F) GEMM FLOPs (QKV 3H, proj H, two 3-tap convs 3H each, fc1 / fc2 F), plus in_proj
+    (2 * 4mel * H) and the final linear (2 H mel) per token; attention 4 H per (query, key) pair; tokens count both CFG
+    halves; a packed row (P, T) has P^2 + T (P + T) (query, key) pairs per half."""
+    H, F, Dp, S = cfg.hidden, cfg.ffn, cfg.depth, cfg.steps
+    gemm = attn = 0.0
+    for P, T in lengths:
+        tok = 2 * (P + T)
+        gemm += S * tok * (Dp * 2 * H * (10 * H + 2 * F) + 2 * cfg.in_dim * H + 2 * H * cfg.mel)
+        attn += S * Dp * 4 * H * 2 * (P * P + T * (P + T))
+    return gemm, attn
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.p = None
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                                       "-i", str(index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local_rank])
+        except (ValueError, IndexError):
+            return local_rank
+    return local_rank
+
+
+def cpu_oracle_time(cfg: DiTConfig, streams: list, reps: int, warm: int) -> tuple[list, int]:
+    """Seconds per one-stream solve of the CPU oracle (fp32, all host threads)."""
+    from oracle import dit_oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = dit_oracle.build_model(cfg, seed=0)
+    ts = []
+    for i in range(warm + reps):
+        s = streams[i % len(streams)]
+        t0 = time.perf_counter()
+        dit_oracle.solve_packed(model, s["x0"], s["mu"], s["cond"], s["spk"], s["P"], s["T"])
+        if i >= warm:
+            ts.append(time.perf_counter() - t0)
+    return ts, threads
+
+
+def reference_arm(a, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    wl = shard(a.workload, 0, 1)
+    streams = make_streams(wl, count=min(4, wl.streams))
+    ts, threads = cpu_oracle_time(REFERENCE, streams, a.steps, a.warmup)
+    T = [streams[i % len(streams)]["T"] for i in range(a.steps)]
+    value = sum(T) / sum(ts)
+    sample = f"1 stream of {wl.name} (P={streams[0]['P']}, T={streams[0]['T']}) per step, fp32 CPU oracle port"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": 1000 * statistics.mean(ts), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "streams_per_step": 1, "model": "reference-config DiT (unverified), random init"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main() -> None:
+    a = args_()
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    if a.impl == "reference":
+        reference_arm(a, rank, world)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    from b200t2w.solver import B200Solver, Layout
+    from b200t2w.weights import random_state_dict
+
+    cfg = REFERENCE
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    wl = shard(a.workload, rank, world)
+    streams = make_streams(wl, cfg.mel)
+    layout = Layout(tuple(s["P"] for s in streams), tuple(s["T"] for s in streams))
+    solver = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), device=dev)
+    bufs = solver.static_buffers(layout)
+    host = {k: torch.cat([s[k].t() for s in streams]).contiguous().pin_memory() for k in ("x0", "mu", "cond")}
+    host["spk"] = torch.stack([s["spk"] for s in streams]).contiguous().pin_memory()
+    host_out = torch.empty(layout.n_tok, cfg.mel, dtype=torch.float32).pin_memory()
+    for k in ("x0", "mu", "cond", "spk"):
+        bufs[k].copy_(host[k])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def solve():
+        solver.solve_packed_dev(layout, bufs["x0"], bufs["mu"], bufs["cond"], bufs["spk"], bufs["out"], workspace=bufs["ws"])
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+
+    # ---- device-resident throughput (inputs already in HBM)
+    for _ in range(a.warmup):
+        solve()
+    barrier()
+    clocks = Clocks(physical_index(local))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    for e0, e1 in evs:
+        flush.fill_(1)  # L2 flush between timed solves (outside the timed interval)
+        e0.record(st)
+        solve()
+        e1.record(st)
+    barrier()
+    clk = clocks.stop()
+    solver.check()
+    times = [e0.elapsed_time(e1) for e0, e1 in evs]  # ms
+    total_ms = sum(times)
+
+    # ---- end to end through the public API: pinned host inputs -> device -> solve -> host result
+    h2d = sum(host[k].numel() * 4 for k in ("x0", "mu", "cond", "spk"))
+    d2h = host_out.numel() * 4
+    e2e_t = []
+    for i in range(a.warmup + a.steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for k in ("x0", "mu", "cond", "spk"):
+            bufs[k].copy_(host[k], non_blocking=True)
+        solve()
+        host_out.copy_(bufs["out"], non_blocking=True)
+        e1.record(st)
+        e1.synchronize()
+        if i >= a.warmup:
+            e2e_t.append(e0.elapsed_time(e1))
+    barrier()
+
+    # ---- max over ranks of the device-timed regions
+    red = torch.tensor([total_ms, sum(e2e_t)], dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(red, op=torch.distributed.ReduceOp.MAX)
+    max_ms, max_e2e_ms = float(red[0]), float(red[1])
+    chunk_frames = wl.chunk_frames  # per rank per solve
+    value = world * chunk_frames * a.steps / (max_ms / 1000)
+    e2e_value = world * chunk_frames * a.steps / (max_e2e_ms / 1000)
+
+    prof = solver.profile(layout, bufs) if not a.no_profile else {}
+    gemm_flops, attn_flops = flops_per_solve(cfg, layout_pairs := list(zip(layout.prompt, layout.chunk)))
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
+    launches = sum(c for _, c in prof.values()) if prof else None
+    gemm_ms = sum(ms for k, (ms, _) in prof.items() if k.startswith("gemm")) if prof else None
+    roofline = None
+    if prof:
+        achieved = gemm_flops / (gemm_ms / 1000) / 1e12
+        traffic = None
+        try:
+            traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json"))).get("gemm_bytes_per_solve")
+        except (OSError, ValueError):
+            pass
+        roofline = {"bound": "tensor", "kernel": "k_gemm (all tcgen05 GEMM launches of one solve)", "achieved": achieved,
+                    "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                    "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "fallback",
+                    "traffic": traffic, "gemm_ms_per_solve": gemm_ms, "gemm_tflop_per_solve": gemm_flops / 1e12,
+                    "solve_tflops": (gemm_flops + attn_flops) / (statistics.mean(times) / 1000) / 1e12,
+                    "kernel_ms_per_solve": {k: round(ms, 4) for k, (ms, _) in prof.items()}}
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        sample = make_streams(wl, cfg.mel, count=1)
+        ts, threads = cpu_oracle_time(cfg, sample, reps=2, warm=0)
+        cpu = {"value": sample[0]["T"] / statistics.mean(ts), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"1 stream (P={sample[0]['P']}, T={sample[0]['T']}) of {wl.name}, fp32 CPU oracle, 2 solves"}
+    if rank == 0:
+        srt = sorted(times)
+        lat = {"p50": statistics.median(times), "p95": srt[min(len(srt) - 1, int(round(0.95 * (len(srt) - 1))))]}
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": max_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": wl.name, "streams_per_gpu": wl.streams, "prompt_frames": layout.prompt[0],
+                       "chunk_frames": layout.chunk[0], "chunk_frames_per_solve_per_gpu": chunk_frames,
+                       "packed_frames_per_solve_per_gpu": 2 * wl.packed_frames, "mel": cfg.mel, "euler_steps": cfg.steps,
+                       "cfg": True, "model": "reference-config DiT (H=512, depth 16, 8x64 heads, unverified), random init",
+                       "l2": "flushed between timed solves (256 MiB write, untimed)",
+                       "parallelism": f"replicas x{world} (streams sharded by request, no collectives)"},
+            "latency_ms": lat, "processed_frames_per_s": value * 2 * wl.packed_frames / chunk_frames,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "latency_ms_p50": statistics.median(e2e_t)},
+            "gpu_launches": launches * a.steps if launches else None, "roofline": roofline, "cpu_baseline": cpu,
+            "clocks": clk}), flush=True)
+    solver.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -120,6 +120,29 @@ T2W_API size_t t2w_workspace_bytes(const t2w_solver* s, int32_t n_streams, const
 T2W_API int t2w_solve_packed(t2w_solver* s, const t2w_batch* batch, void* workspace, size_t workspace_bytes, uint32_t flags,
                      void* stream);
 
+/* Kernel classes of t2w_profile_solve. */
+enum t2w_kernel_class {
+  T2W_KC_PACK = 0,   /* input packing (CFG rows) */
+  T2W_KC_GEMM_IN,    /* in_proj GEMM */
+  T2W_KC_LN_MOD,     /* LayerNorm + adaLN modulation (norm1 / norm3 / norm2 / final) */
+  T2W_KC_GEMM_QKV,   /* QKV GEMM with the per-head q / k norms */
+  T2W_KC_ATTN,       /* varlen attention */
+  T2W_KC_GEMM_PROJ,  /* attention output projection + gated residual */
+  T2W_KC_GEMM_CONV1, /* first causal conv (3 taps) */
+  T2W_KC_LN_MISH,    /* conv LayerNorm (affine) + Mish */
+  T2W_KC_GEMM_CONV2, /* second causal conv + gated residual */
+  T2W_KC_GEMM_FC1,   /* MLP fc1 + GELU */
+  T2W_KC_GEMM_FC2,   /* MLP fc2 + gated residual */
+  T2W_KC_GEMM_FINAL, /* final linear */
+  T2W_KC_EULER,      /* CFG combine + Euler step */
+  T2W_KC_COUNT
+};
+
+/* One eager solve with a CUDA event between consecutive launches; ms[c] / launches[c] receive each kernel class's
+ * summed device time and launch count ([T2W_KC_COUNT] each).  Synchronises `stream`. */
+T2W_API int t2w_profile_solve(t2w_solver* s, const t2w_batch* batch, void* workspace, size_t workspace_bytes, void* stream,
+                              float* ms, int32_t* launches);
+
 /* Synchronise the solver's error word: T2W_OK, or T2W_ERR_TIMEOUT if a kernel gave up on a wait (then cleared). */
 T2W_API int t2w_check(t2w_solver* s);
 

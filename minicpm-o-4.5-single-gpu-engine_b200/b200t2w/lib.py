@@ -18,6 +18,8 @@ STATUS = {-1: "invalid argument or shape", -2: "CUDA error", -3: "out of device 
 PREC = {"bf16": 0, "fp8": 1}
 FLAG_GRAPH = 1
 EPI = {"f32": 0, "bf16": 1, "gelu": 2, "resid": 3, "qkv": 4}
+KERNEL_CLASSES = ["pack", "gemm_in", "ln_mod", "gemm_qkv", "attn", "gemm_proj", "gemm_conv1", "ln_mish", "gemm_conv2",
+                  "gemm_fc1", "gemm_fc2", "gemm_final", "euler"]
 W_GLOBAL = ["estimator.t_embedder.mlp.0.weight", "estimator.t_embedder.mlp.0.bias", "estimator.t_embedder.mlp.2.weight",
             "estimator.t_embedder.mlp.2.bias", "estimator.in_proj.weight", "estimator.in_proj.bias",
             "estimator.final_layer.adaLN_modulation.1.weight", "estimator.final_layer.adaLN_modulation.1.bias",
@@ -61,6 +63,8 @@ _SIGS = {
     "t2w_workspace_bytes": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_size_t),
     "t2w_solve_packed": ([_P, ctypes.POINTER(Batch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
     "t2w_check": ([_P], ctypes.c_int),
+    "t2w_profile_solve": ([_P, ctypes.POINTER(Batch), _P, ctypes.c_size_t, _P, ctypes.POINTER(ctypes.c_float),
+                           ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "t2w_mods": ([_P, _P, _P, _P, _P], ctypes.c_int),
     "t2w_counts": ([_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)],
                    ctypes.c_int),

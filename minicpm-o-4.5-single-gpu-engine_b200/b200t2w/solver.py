@@ -152,6 +152,19 @@ class B200Solver:
                ctypes.c_uint32(L.FLAG_GRAPH if graph else 0), ctypes.c_void_p(st.cuda_stream))
         return out
 
+    def profile(self, layout: Layout, bufs: dict | None = None) -> dict:
+        """One eager solve of ``layout`` with CUDA events between launches: {kernel class: (ms, launches)}."""
+        b = bufs if bufs is not None else self.static_buffers(layout)
+        P, T = L.i32_array(layout.prompt), L.i32_array(layout.chunk)
+        batch = L.Batch(layout.n_streams, P, T, b["x0"].data_ptr(), b["mu"].data_ptr(), b["cond"].data_ptr(),
+                        b["spk"].data_ptr(), b["out"].data_ptr())
+        n = len(L.KERNEL_CLASSES)
+        ms, cnt = (ctypes.c_float * n)(), (ctypes.c_int32 * n)()
+        st = torch.cuda.current_stream(self.device)
+        L.call("t2w_profile_solve", self._h, ctypes.byref(batch), ctypes.c_void_p(b["ws"].data_ptr()),
+               ctypes.c_size_t(b["ws"].numel()), ctypes.c_void_p(st.cuda_stream), ms, cnt)
+        return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(L.KERNEL_CLASSES)}
+
     def static_buffers(self, layout: Layout) -> dict:
         """Per-layout static input / output buffers (CUDA-graph replays hit the same pointers)."""
         key = (layout.prompt, layout.chunk)

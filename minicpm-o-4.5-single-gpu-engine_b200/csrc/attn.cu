@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(192, 1) k_attn(const __grid_constant__ CUtenso
     for (int i = 0; i < kD; ++i) o[i] = 0.f;
     uint8_t* prow = sP + r * 128;
     for (int j = 0; j < n_kt; ++j) {
-      if (!mbar_wait(s_full, j & 1, p.err)) break;
+      // warp-uniform: tcgen05.ld below is .sync.aligned
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err))) break;
       tc_fence_after();
       const int kb = j * kTile;
       float mx = -INFINITY;
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(192, 1) k_attn(const __grid_constant__ CUtenso
       const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_use);
       l = l * alpha + rs;
       m = m_new;
-      if (!mbar_wait(o_full, j & 1, p.err)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(o_full, j & 1, p.err))) break;
       tc_fence_after();
       float oj[32];
       tmem_ld32(trow + kOCol, oj);

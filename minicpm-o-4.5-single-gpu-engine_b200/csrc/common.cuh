@@ -147,6 +147,12 @@ T2W_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+T2W_DEV void tmem_ld32p(uint32_t taddr, float* v) {
+  float t[32];
+  tmem_ld32(taddr, t);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = t[i];
+}
 T2W_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(

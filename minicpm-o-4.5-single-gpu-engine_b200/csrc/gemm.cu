@@ -5,8 +5,11 @@
 //   warp 1  : TMEM allocator + single-thread tcgen05.mma issuer (M = 128, N = BN, K = 16 per instruction)
 //   warps 2-5: epilogue; warp w reads TMEM lanes 32 (w % 4) .. +31, so each thread owns one output row
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so a tile's epilogue overlaps the next tile's MMAs.
+// The epilogue stages its output tile in shared memory (128-byte swizzled boxes of 128 rows x 128 bytes) and writes it
+// with asynchronous TMA stores; for the gated residual it first TMA-loads the fp32 residual tile into the same buffer
+// (issued before it waits for the accumulator, so the load overlaps the MMAs).
 // The causal convolutions use taps = 3, tap_row0 = -2: tap t of output row m reads activation row m - 2 + t, so the
-// im2col matrix is never materialised; rows before 0 come back zero from TMA.
+// im2col matrix is never materialised; rows before 0 come back zero from TMA.  No TMA multicast.
 #include <cstdio>
 
 #include "common.cuh"
@@ -18,16 +21,28 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // bf16 elements per 128-byte swizzle row
+constexpr int kMaxSmem = 232448;
+constexpr int kBoxBytes = kBM * 128;  // one staged output box: 128 rows x 128 bytes
 
-template <int BN>
+__host__ __device__ constexpr bool epi_f32_out(int epi) { return epi == T2W_EPI_F32 || epi == T2W_EPI_RESID; }
+
+template <int BN, int EPI, bool TMA_OUT>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int OUT_ELEM = epi_f32_out(EPI) ? 4 : 2;
+  static constexpr int BOX_COLS = 128 / OUT_ELEM;
+  static constexpr int N_BOXES = TMA_OUT ? BN / BOX_COLS : 0;
+  static constexpr int OUT_BYTES = N_BOXES * kBoxBytes;
+  static constexpr int FIXED = 1024 + 256;
+  static constexpr int STAGES_FIT = (kMaxSmem - FIXED - OUT_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + FIXED;
+  static_assert(STAGES >= 2, "not enough shared memory for a 2-stage ring");
   static_assert(B_BYTES % 1024 == 0, "W tile must keep 1024-byte alignment of the swizzle atoms");
+  static_assert(!TMA_OUT || BN % BOX_COLS == 0, "output tile must be whole boxes");
 };
 
 struct DevArgs {
@@ -35,8 +50,6 @@ struct DevArgs {
   const float* bias;
   void* out;
   int ldo;
-  float* resid;
-  int ldr;
   const float* gate;
   const float* qn_w;
   const float* qn_b;
@@ -46,23 +59,23 @@ struct DevArgs {
   int* err;
 };
 
-T2W_DEV void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
-  uint4 u0, u1;
-  u0.x = pack_bf16x2(v[0], v[1]);
-  u0.y = pack_bf16x2(v[2], v[3]);
-  u0.z = pack_bf16x2(v[4], v[5]);
-  u0.w = pack_bf16x2(v[6], v[7]);
-  u1.x = pack_bf16x2(v[8], v[9]);
-  u1.y = pack_bf16x2(v[10], v[11]);
-  u1.z = pack_bf16x2(v[12], v[13]);
-  u1.w = pack_bf16x2(v[14], v[15]);
-  reinterpret_cast<uint4*>(dst)[0] = u0;
-  reinterpret_cast<uint4*>(dst)[1] = u1;
+T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               : "memory");
 }
+T2W_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+T2W_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+T2W_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+T2W_DEV void epi_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-T2W_DEV void add_vec16(float (&v)[16], const float* __restrict__ b) {
+// 16-byte chunk `c` of row `r` inside one staged box (128B swizzle: chunk index XOR row % 8).
+T2W_DEV uint8_t* box_chunk(uint8_t* box, int r, int c) { return box + r * 128 + ((c ^ (r & 7)) << 4); }
+
+T2W_DEV void add_bias(float* v, const float* __restrict__ b, int n) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < n / 4; ++j) {
     const float4 q = __ldg(reinterpret_cast<const float4*>(b) + j);
     v[4 * j + 0] += q.x;
     v[4 * j + 1] += q.y;
@@ -71,99 +84,121 @@ T2W_DEV void add_vec16(float (&v)[16], const float* __restrict__ b) {
   }
 }
 
-template <int BN, int EPI>
-T2W_DEV void epilogue(const DevArgs& p, uint32_t taddr, int row, int n0) {
-  const bool row_ok = row < p.M;
-  if constexpr (EPI == T2W_EPI_QKV) {
-    const int qcols = p.N / 3;
+// Write 64 bf16 values (one row of one bf16 box) into the staging box.
+T2W_DEV void stage_bf16_row(uint8_t* box, int r, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+    u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+    u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+    u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(box_chunk(box, r, c)) = u;
+  }
+}
+
+// Epilogue of one tile into the staging buffer (TMA_OUT) or straight to global memory (BN = 80 final layer).
+template <int BN, int EPI, bool TMA_OUT>
+T2W_DEV void epilogue(const DevArgs& p, uint32_t taddr, int r, int row, int n0, uint8_t* stage) {
+  if constexpr (!TMA_OUT) {
+    static_assert(EPI == T2W_EPI_F32 || EPI == T2W_EPI_BF16, "direct stores: f32 / bf16 only");
 #pragma unroll 1
-    for (int g = 0; g < BN / 64; ++g) {
-      const int c0 = n0 + g * 64;
-      float v[4][16];
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      tmem_ld16(taddr + c, v);
+      if (row >= p.M) continue;
+      add_bias(v, p.bias + n0 + c, 16);
+      if constexpr (EPI == T2W_EPI_F32) {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + n0 + c);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        tmem_ld16(taddr + g * 64 + 16 * j, v[j]);
-        add_vec16(v[j], p.bias + c0 + 16 * j);
+        for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + n0 + c);
+        dst[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        dst[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                            pack_bf16x2(v[14], v[15]));
       }
-      if (c0 < 2 * qcols) {  // q or k head: LayerNorm over the head's 64 values (affine), fp32
-        const int d0 = (c0 % qcols) % 64;  // always 0: heads are 64-aligned inside the q / k blocks
-        const float* nw = (c0 < qcols ? p.qn_w : p.kn_w) + d0;
-        const float* nb = (c0 < qcols ? p.qn_b : p.kn_b) + d0;
-        float s = 0.f;
+    }
+  } else if constexpr (EPI == T2W_EPI_F32 || EPI == T2W_EPI_RESID) {
+#pragma unroll 1
+    for (int b = 0; b < BN / 32; ++b) {
+      float v[32];
+      tmem_ld32(taddr + 32 * b, v);
+      const int col = n0 + 32 * b;
+      add_bias(v, p.bias + col, 32);
+      uint8_t* box = stage + b * kBoxBytes;
+      if constexpr (EPI == T2W_EPI_RESID) {
+        const float* g = p.gate + col;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int c = 0; c < 8; ++c) {
+          float4* q = reinterpret_cast<float4*>(box_chunk(box, r, c));
+          const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + c);
+          float4 h = *q;
+          h.x = fmaf(gg.x, v[4 * c + 0], h.x);
+          h.y = fmaf(gg.y, v[4 * c + 1], h.y);
+          h.z = fmaf(gg.z, v[4 * c + 2], h.z);
+          h.w = fmaf(gg.w, v[4 * c + 3], h.w);
+          *q = h;
+        }
+      } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) s += v[j][i];
-        const float mean = s * (1.f / 64.f);
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float d = v[j][i] - mean;
-            ss += d * d;
-          }
-        const float rstd = rsqrtf(ss * (1.f / 64.f) + p.qk_eps);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[j][i] = (v[j][i] - mean) * rstd * __ldg(nw + 16 * j + i) + __ldg(nb + 16 * j + i);
-      }
-      if (row_ok) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + c0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) store_bf16x16(dst + 16 * j, v[j]);
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(box_chunk(box, r, c)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
       }
     }
   } else {
+    // bf16 outputs: one 64-column box per iteration (one head for the QKV epilogue)
+    const int qcols = p.N / 3;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      const int col = n0 + c;
-      float v[16];
-      tmem_ld16(taddr + c, v);
-      if (!row_ok) continue;
-      add_vec16(v, p.bias + col);
-      if constexpr (EPI == T2W_EPI_F32) {
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + col);
+    for (int b = 0; b < BN / 64; ++b) {
+      float v[64];
+      tmem_ld32p(taddr + 64 * b, v);
+      tmem_ld32p(taddr + 64 * b + 32, v + 32);
+      const int c0 = n0 + 64 * b;
+      add_bias(v, p.bias + c0, 64);
+      if constexpr (EPI == T2W_EPI_QKV) {
+        if (c0 < 2 * qcols) {  // a q or k head: LayerNorm over its 64 values (affine), fp32
+          const float* nw = c0 < qcols ? p.qn_w : p.kn_w;
+          const float* nb = c0 < qcols ? p.qn_b : p.kn_b;
+          float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      } else if constexpr (EPI == T2W_EPI_BF16 || EPI == T2W_EPI_GELU) {
-        if constexpr (EPI == T2W_EPI_GELU) {
+          for (int i = 0; i < 64; ++i) s += v[i];
+          const float mean = s * (1.f / 64.f);
+          float ss = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(v[i]);
+          for (int i = 0; i < 64; ++i) {
+            const float d = v[i] - mean;
+            ss += d * d;
+          }
+          const float rstd = rsqrtf(ss * (1.f / 64.f) + p.qk_eps);
+#pragma unroll
+          for (int i = 0; i < 64; ++i) v[i] = (v[i] - mean) * rstd * __ldg(nw + i) + __ldg(nb + i);
         }
-        store_bf16x16(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + col, v);
-      } else if constexpr (EPI == T2W_EPI_RESID) {
-        float4* r = reinterpret_cast<float4*>(p.resid + (size_t)row * p.ldr + col);
-        const float4* g = reinterpret_cast<const float4*>(p.gate + col);
+      } else if constexpr (EPI == T2W_EPI_GELU) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float4 x = r[j];
-          const float4 gg = __ldg(g + j);
-          x.x = fmaf(gg.x, v[4 * j + 0], x.x);
-          x.y = fmaf(gg.y, v[4 * j + 1], x.y);
-          x.z = fmaf(gg.z, v[4 * j + 2], x.z);
-          x.w = fmaf(gg.w, v[4 * j + 3], x.w);
-          r[j] = x;
-        }
+        for (int i = 0; i < 64; ++i) v[i] = gelu_tanh(v[i]);
       }
+      stage_bf16_row(stage + b * kBoxBytes, r, v);
     }
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool TMA_OUT>
 __global__ void __launch_bounds__(192, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const DevArgs p) {
-  using C = GemmCfg<BN>;
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+           const __grid_constant__ CUtensorMap tmC, const DevArgs p) {
+  using C = GemmCfg<BN, EPI, TMA_OUT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint8_t* sOut = sB + C::STAGES * C::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::OUT_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* res_full = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -175,9 +210,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
+    mbar_init(res_full, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    if constexpr (TMA_OUT) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -243,17 +280,48 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int q = warp & 3;
+    const int r = q * 32 + lane;  // tile row == TMEM lane
+    const bool leader = threadIdx.x == 64;
+    // `ok` stays warp-uniform (tcgen05.ld is .sync.aligned); after a timed-out wait the warp skips all further waits
+    // and work but still reaches every named barrier, so no warp is left waiting at one.
+    bool ok = true;
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
-      if (!mbar_wait(&tfull[acc], (it >> 1) & 1, p.err)) break;
-      tc_fence_after();
       const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-      epilogue<BN, EPI>(p, taddr, m0 + q * 32 + lane, n0);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if constexpr (TMA_OUT) {
+        if (leader) bulk_wait_read0();  // the previous tile's stores have read the staging buffer
+        epi_barrier();
+        if constexpr (EPI == T2W_EPI_RESID) {
+          if (leader && ok) {
+            mbar_expect_tx(res_full, C::OUT_BYTES);
+            for (int b = 0; b < C::N_BOXES; ++b) tma_load_2d(sOut + b * kBoxBytes, &tmC, n0 + b * C::BOX_COLS, m0, res_full);
+          }
+        }
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err));
+      if constexpr (EPI == T2W_EPI_RESID) {
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(res_full, it & 1, p.err));
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+        epilogue<BN, EPI, TMA_OUT>(p, taddr, r, m0 + r, n0, sOut);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
+      if constexpr (TMA_OUT) {
+        fence_proxy_async_smem();
+        epi_barrier();
+        if (leader && ok) {
+          for (int b = 0; b < C::N_BOXES; ++b) tma_store_2d(&tmC, sOut + b * kBoxBytes, n0 + b * C::BOX_COLS, m0);
+          bulk_commit();
+        }
+      }
+    }
+    if constexpr (TMA_OUT) {
+      if (leader) bulk_wait0();
     }
   }
   __syncthreads();
@@ -263,29 +331,47 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int BN, int EPI>
-int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const CUtensorMap* tmW) {
-  using C = GemmCfg<BN>;
+template <int BN, int EPI, bool TMA_OUT>
+int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const WeightMaps* wm,
+                const CUtensorMap* tmC) {
+  const CUtensorMap* tmW = nullptr;
+  if (wm) {
+    tmW = BN == 80 ? (wm->has80 ? &wm->bn80 : nullptr) : BN == 128 ? (wm->has128 ? &wm->bn128 : nullptr)
+                                                                 : (wm->has256 ? &wm->bn256 : nullptr);
+    if (!tmW) return T2W_ERR_INVALID;
+  }
+  using C = GemmCfg<BN, EPI, TMA_OUT>;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<BN, EPI, TMA_OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
     }
     attr_done = true;
   }
-  CUtensorMap ma, mw;
+  CUtensorMap ma, mw, mc;
   if (!tmA) {
-    if (!make_tmap_2d(&ma, a.A, 2, (uint64_t)a.rows_a, (uint64_t)a.K * (a.taps == 1 ? 1 : 1), (uint64_t)a.lda * 2, kBM,
-                      kBK))
-      return T2W_ERR_INVALID;
+    if (!make_tmap_2d(&ma, a.A, 2, (uint64_t)a.rows_a, (uint64_t)a.K, (uint64_t)a.lda * 2, kBM, kBK)) return T2W_ERR_INVALID;
     tmA = &ma;
   }
   if (!tmW) {
     if (!make_tmap_2d(&mw, a.W, 2, (uint64_t)a.N, (uint64_t)a.K * a.taps, (uint64_t)a.K * a.taps * 2, BN, kBK))
       return T2W_ERR_INVALID;
     tmW = &mw;
+  }
+  if (!tmC) {
+    if (TMA_OUT) {
+      const bool f32 = epi_f32_out(EPI);
+      const void* base = EPI == T2W_EPI_RESID ? (const void*)a.resid : a.out;
+      const int ld = EPI == T2W_EPI_RESID ? a.ldr : a.ldo;
+      if (!make_tmap_2d(&mc, base, f32 ? 4 : 2, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)ld * (f32 ? 4 : 2), kBM,
+                        C::BOX_COLS))
+        return T2W_ERR_INVALID;
+    } else {
+      mc = *tmA;  // unused
+    }
+    tmC = &mc;
   }
   DevArgs p;
   p.M = a.M;
@@ -298,8 +384,6 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.bias = a.bias;
   p.out = a.out;
   p.ldo = a.ldo;
-  p.resid = a.resid;
-  p.ldr = a.ldr;
   p.gate = a.gate;
   p.qn_w = a.qn_w;
   p.qn_b = a.qn_b;
@@ -308,7 +392,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.qk_eps = a.qk_eps;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  k_gemm<BN, EPI><<<grid, 192, C::SMEM, st>>>(*tmA, *tmW, p);
+  k_gemm<BN, EPI, TMA_OUT><<<grid, 192, C::SMEM, st>>>(*tmA, *tmW, *tmC, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_cuda_error(e);
@@ -317,47 +401,62 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   return T2W_OK;
 }
 
-template <int BN>
-int dispatch_epi(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const CUtensorMap* tmW) {
-  switch (a.epi) {
-    case T2W_EPI_F32: return launch_impl<BN, T2W_EPI_F32>(a, st, tmA, tmW);
-    case T2W_EPI_BF16: return launch_impl<BN, T2W_EPI_BF16>(a, st, tmA, tmW);
-    case T2W_EPI_GELU: return launch_impl<BN, T2W_EPI_GELU>(a, st, tmA, tmW);
-    case T2W_EPI_RESID: return launch_impl<BN, T2W_EPI_RESID>(a, st, tmA, tmW);
-    case T2W_EPI_QKV:
-      if constexpr (BN % 64 == 0) return launch_impl<BN, T2W_EPI_QKV>(a, st, tmA, tmW);
-      return T2W_ERR_INVALID;
-    default: return T2W_ERR_INVALID;
-  }
-}
-
 }  // namespace
 
-int gemm_block_n(int N) {
-  if (N % 256 == 0) return 256;
-  if (N % 128 == 0) return 128;
-  if (N == 80) return 80;
-  return 0;
+bool gemm_n_supported(int N) { return N == 80 || (N > 0 && N % 128 == 0); }
+
+bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot) {
+  *m = WeightMaps();
+  if (N == 80) return (m->has80 = make_tmap_2d(&m->bn80, W, 2, N, Ktot, (uint64_t)Ktot * 2, 80, kBK));
+  if (N % 128) return false;
+  m->has128 = make_tmap_2d(&m->bn128, W, 2, N, Ktot, (uint64_t)Ktot * 2, 128, kBK);
+  if (N % 256 == 0) m->has256 = make_tmap_2d(&m->bn256, W, 2, N, Ktot, (uint64_t)Ktot * 2, 256, kBK);
+  return m->has128;
 }
 
-int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const CUtensorMap* tmW) {
+// Column tile: 80 only for the 80-wide final layer; fp32 outputs use 128 (the staged fp32 tile must fit beside the
+// ring); otherwise the larger of 128 / 256 unless 128 finishes in fewer whole waves of 128-column work.
+int gemm_block_n_for(int N, int M, int epi) {
+  if (N == 80) return 80;
+  if (N % 128) return 0;
+  if (epi_f32_out(epi) || N % 256) return 128;
+  if (M <= 0) return 256;
+  const long long tiles_m = (M + kBM - 1) / kBM, sms = num_sms();
+  const long long w256 = (tiles_m * (N / 256) + sms - 1) / sms * 2, w128 = (tiles_m * (N / 128) + sms - 1) / sms;
+  return w128 < w256 ? 128 : 256;
+}
+
+int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const WeightMaps* tmW,
+                const CUtensorMap* tmC) {
   if (!a.A || !a.W || !a.bias || a.M <= 0 || a.M % kBM || a.K <= 0 || a.K % kBK || a.taps < 1 || a.rows_a <= 0 ||
       a.lda < a.K || a.lda % 8)
     return T2W_ERR_INVALID;
-  const int bn = gemm_block_n(a.N);
+  const int bn = gemm_block_n_for(a.N, a.M, a.epi);
   if (!bn) return T2W_ERR_INVALID;
   if (a.epi == T2W_EPI_RESID && (!a.resid || !a.gate || a.ldr % 4)) return T2W_ERR_INVALID;
   if (a.epi != T2W_EPI_RESID && (!a.out || a.ldo % 8)) return T2W_ERR_INVALID;
   if (a.epi == T2W_EPI_QKV && (a.N % 3 || (a.N / 3) % 64 || !a.qn_w || !a.qn_b || !a.kn_w || !a.kn_b)) return T2W_ERR_INVALID;
-  switch (bn) {
-    case 256: return dispatch_epi<256>(a, st, tmA, tmW);
-    case 128: return dispatch_epi<128>(a, st, tmA, tmW);
-    case 80:
-      if (a.epi == T2W_EPI_F32) return launch_impl<80, T2W_EPI_F32>(a, st, tmA, tmW);
-      if (a.epi == T2W_EPI_BF16) return launch_impl<80, T2W_EPI_BF16>(a, st, tmA, tmW);
-      return T2W_ERR_INVALID;
+  if (bn == 80) {
+    if (a.epi == T2W_EPI_F32) return launch_impl<80, T2W_EPI_F32, false>(a, st, tmA, tmW, tmC);
+    if (a.epi == T2W_EPI_BF16) return launch_impl<80, T2W_EPI_BF16, false>(a, st, tmA, tmW, tmC);
+    return T2W_ERR_INVALID;
   }
-  return T2W_ERR_INVALID;
+  if (bn == 256) {
+    switch (a.epi) {
+      case T2W_EPI_BF16: return launch_impl<256, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_GELU: return launch_impl<256, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_QKV: return launch_impl<256, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
+      default: return T2W_ERR_INVALID;
+    }
+  }
+  switch (a.epi) {
+    case T2W_EPI_F32: return launch_impl<128, T2W_EPI_F32, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_BF16: return launch_impl<128, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_GELU: return launch_impl<128, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_RESID: return launch_impl<128, T2W_EPI_RESID, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_QKV: return launch_impl<128, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
+    default: return T2W_ERR_INVALID;
+  }
 }
 
 }  // namespace t2w

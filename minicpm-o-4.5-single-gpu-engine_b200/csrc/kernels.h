@@ -36,10 +36,20 @@ struct GemmArgs {
   float qk_eps = 0.f;
   int* err = nullptr;
 };
-// Column tile the launcher picks for N.
-int gemm_block_n(int N);
-// Enqueue C = A W^T (+ epilogue).  tmA / tmW may be prebuilt (nullptr: encoded here).  Returns a T2W status.
-int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA = nullptr, const CUtensorMap* tmW = nullptr);
+// Column tile the launcher picks for an N-wide output of M rows with epilogue `epi` (0: N unsupported).
+int gemm_block_n_for(int N, int M, int epi);
+// Whether some (M, epi) can use an N-wide output at all.
+bool gemm_n_supported(int N);
+// Tensor maps of one weight matrix W [N, Ktot] bf16 for every column tile the launcher may pick.
+struct WeightMaps {
+  CUtensorMap bn80, bn128, bn256;
+  bool has80 = false, has128 = false, has256 = false;
+};
+bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot);
+// Enqueue C = A W^T (+ epilogue).  tmA / W maps / tmC may be prebuilt (nullptr: encoded here; tmC is the output map,
+// or the residual map for T2W_EPI_RESID, with 128-row boxes of 128 bytes).  Returns a T2W status.
+int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA = nullptr, const WeightMaps* wm = nullptr,
+                const CUtensorMap* tmC = nullptr);
 
 // One attention work item: a 128-query tile of one packed sequence.
 struct AttnWork {

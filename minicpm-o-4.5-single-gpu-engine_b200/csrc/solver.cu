@@ -62,7 +62,9 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t r
   if (!fn || !base || (reinterpret_cast<uintptr_t>(base) & 15) || (pitch_bytes & 15) || box_rows > 256 ||
       box_cols * (uint32_t)elem_bytes != 128)
     return false;
-  const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType dt = elem_bytes == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {pitch_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
@@ -97,7 +99,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 struct BlockW {
   __nv_bfloat16 *qkv, *proj, *c1, *c2, *fc1, *fc2;
   float *b_qkv, *qn_w, *qn_b, *kn_w, *kn_b, *b_proj, *b_c1, *cln_w, *cln_b, *b_c2, *b_fc1, *b_fc2;
-  CUtensorMap tm_qkv, tm_proj, tm_c1, tm_c2, tm_fc1, tm_fc2;
+  WeightMaps tm_qkv, tm_proj, tm_c1, tm_c2, tm_fc1, tm_fc2;
 };
 
 struct Plan {
@@ -129,10 +131,12 @@ struct t2w_solver {
   float *mods = nullptr, *final_mods = nullptr, *dts_dev = nullptr;
   std::vector<float> dts;
   std::vector<BlockW> blk;
-  CUtensorMap tm_in{}, tm_fin{};
+  WeightMaps tm_in{}, tm_fin{};
   int* err = nullptr;
+  cudaStream_t cap_stream = nullptr;
   std::unordered_map<uint64_t, cudaGraphExec_t> graphs;
   std::unordered_map<uintptr_t, uint64_t> ws_meta;  // workspace -> plan key of the index arrays it holds
+  std::vector<cudaEvent_t> prof_events;
   int64_t n_replays = 0, n_captures = 0, n_eager = 0;
 };
 
@@ -142,8 +146,8 @@ bool valid_cfg(const t2w_config& c) {
   return c.mel > 0 && c.mel % 16 == 0 && c.mel <= 128 && c.head_dim == 64 && c.heads > 0 &&
          c.hidden == c.heads * c.head_dim && c.hidden % 128 == 0 && c.hidden <= 1024 && c.ffn % 128 == 0 &&
          c.depth > 0 && c.steps > 0 && c.steps <= 16 && c.freq_dim > 0 && c.freq_dim % 2 == 0 &&
-         gemm_block_n(3 * c.hidden) && gemm_block_n(c.ffn) && gemm_block_n(c.hidden) && (4 * c.mel) % 64 == 0 &&
-         (c.mel == 80 || gemm_block_n(c.mel));
+         gemm_n_supported(3 * c.hidden) && gemm_n_supported(c.ffn) && gemm_n_supported(c.hidden) &&
+         (4 * c.mel) % 64 == 0 && (c.mel == 80 || gemm_n_supported(c.mel));
 }
 
 bool make_plan(const t2w_config& c, int n, const int* P, const int* T, Plan& pl) {
@@ -216,13 +220,29 @@ T* at(void* base, size_t off) {
   return reinterpret_cast<T*>(static_cast<uint8_t*>(base) + off);
 }
 
-bool weight_map(CUtensorMap* m, const void* w, int N, int Ktot) {
-  const int bn = gemm_block_n(N);
-  return bn && make_tmap_2d(m, w, 2, (uint64_t)N, (uint64_t)Ktot, (uint64_t)Ktot * 2, bn, 64);
-}
+bool weight_map(WeightMaps* m, const void* w, int N, int Ktot) { return make_weight_maps(m, w, N, Ktot); }
+
+// Optional per-launch timing: an event before every launch (and one after the last) on the solve's stream.
+struct Prof {
+  std::vector<cudaEvent_t>* events = nullptr;
+  std::vector<int> cls;
+  int tick(int c, cudaStream_t st) {
+    if (!events) return T2W_OK;
+    if (events->size() <= cls.size()) {
+      cudaEvent_t e;
+      T2W_CUDA(cudaEventCreate(&e));
+      events->push_back(e);
+    }
+    T2W_CUDA(cudaEventRecord((*events)[cls.size()], st));
+    cls.push_back(c);
+    return T2W_OK;
+  }
+};
 
 // Enqueue one whole solve (no host synchronisation, graph-capturable).
-int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, cudaStream_t st) {
+int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, cudaStream_t st, Prof* prof = nullptr) {
+  Prof none;
+  Prof& P = prof ? *prof : none;
   const t2w_config& c = s->cfg;
   const WsLayout L = layout(c, pl);
   const int H = c.hidden, R = pl.rows, mel = c.mel, F = c.ffn;
@@ -240,13 +260,21 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   const int* tok_stream = at<int>(ws, L.tok_stream);
   const AttnWork* work = at<AttnWork>(ws, L.work);
 
-  CUtensorMap tm_hx, tm_a, tm_o, tm_c1, tm_f, tm_qkv;
+  // bf16 maps serve both as GEMM A operands and as bf16 output maps (128-row boxes of 64 columns); h is fp32 (boxes of
+  // 32 columns) for the in_proj output and the gated residuals.
+  CUtensorMap tm_hx, tm_a, tm_o, tm_c1, tm_f, tm_qkv, tm_h;
   if (!make_tmap_2d(&tm_hx, hx, 2, R, 4 * mel, 4 * mel * 2, 128, 64) || !make_tmap_2d(&tm_a, a, 2, R, H, H * 2, 128, 64) ||
       !make_tmap_2d(&tm_o, o, 2, R, H, H * 2, 128, 64) || !make_tmap_2d(&tm_c1, c1, 2, R, H, H * 2, 128, 64) ||
-      !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&tm_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 128, 64))
+      !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&tm_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 128, 64) ||
+      !make_tmap_2d(&tm_h, h, 4, R, H, H * 4, 128, 32))
     return T2W_ERR_INVALID;
 
   T2W_CUDA(cudaMemsetAsync(hx, 0, (size_t)R * 4 * mel * 2, st));
+  // Attention writes only sequence rows; the pad rows of its output buffer must hold finite values (zero here, later
+  // finite conv outputs), or the proj GEMM carries workspace garbage into pad rows of h, and a NaN there reaches the
+  // masked keys of the next attention, where 0 * NaN poisons the P V product.
+  T2W_CUDA(cudaMemsetAsync(o, 0, (size_t)R * H * 2, st));
+  T2W_TRY(P.tick(T2W_KC_PACK, st));
   T2W_TRY(launch_pack(b.x0, b.mu, b.cond, b.spk, tok_row, tok_stream, pl.n_tok, mel, pl.half_rows, hx, 4 * mel, x, st));
 
   GemmArgs g;
@@ -270,62 +298,77 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     g.err = s->err;
     g.A = hx; g.lda = 4 * mel; g.W = s->w_in; g.bias = s->b_in; g.N = H; g.K = 4 * mel; g.epi = T2W_EPI_F32;
     g.out = h; g.ldo = H;
-    T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in));
+    T2W_TRY(P.tick(T2W_KC_GEMM_IN, st));
+    T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in, &tm_h));
     for (int bi = 0; bi < c.depth; ++bi) {
       const BlockW& w = s->blk[bi];
       const float* M = s->mods + ((size_t)step * c.depth + bi) * 9 * H;
       const float *sh_a = M, *sc_a = M + H, *g_a = M + 2 * H, *sh_m = M + 3 * H, *sc_m = M + 4 * H, *g_m = M + 5 * H;
       const float *sh_c = M + 6 * H, *sc_c = M + 7 * H, *g_c = M + 8 * H;
       // attention branch
+      T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_ln_mod(h, H, sh_a, sc_a, c.eps_block, R, H, a, H, nullptr, st));
       GemmArgs q = GemmArgs();
       q.rows_a = R; q.M = R; q.err = s->err;
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
       q.qn_w = w.qn_w; q.qn_b = w.qn_b; q.kn_w = w.kn_w; q.kn_b = w.kn_b; q.qk_eps = c.eps_qk;
-      T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv));
+      T2W_TRY(P.tick(T2W_KC_GEMM_QKV, st));
+      T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv, &tm_qkv));
+      T2W_TRY(P.tick(T2W_KC_ATTN, st));
       T2W_TRY(launch_attn(at_args, st, &tm_qkv));
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
       pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_RESID;
       pr.resid = h; pr.ldr = H; pr.gate = g_a;
-      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj));
+      T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
+      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &tm_h));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108)
+      T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_ln_mod(h, H, sh_c, sc_c, c.eps_block, R, H, a, H, pad, st));
       GemmArgs k1 = GemmArgs();
       k1.rows_a = R; k1.M = R; k1.err = s->err;
       k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
       k1.epi = T2W_EPI_BF16; k1.out = o; k1.ldo = H;
-      T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1));
+      T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
+      T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &tm_o));
+      T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
       T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, c1, pad, st));
       GemmArgs k2 = GemmArgs();
       k2.rows_a = R; k2.M = R; k2.err = s->err;
       k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
       k2.epi = T2W_EPI_RESID; k2.resid = h; k2.ldr = H; k2.gate = g_c;
-      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2));
+      T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
+      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &tm_h));
       // MLP branch
+      T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_ln_mod(h, H, sh_m, sc_m, c.eps_block, R, H, a, H, nullptr, st));
       GemmArgs f1 = GemmArgs();
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
-      T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1));
+      T2W_TRY(P.tick(T2W_KC_GEMM_FC1, st));
+      T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1, &tm_f));
       GemmArgs f2 = GemmArgs();
       f2.rows_a = R; f2.M = R; f2.err = s->err;
       f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_RESID;
       f2.resid = h; f2.ldr = H; f2.gate = g_m;
-      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2));
+      T2W_TRY(P.tick(T2W_KC_GEMM_FC2, st));
+      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, &tm_h));
     }
     const float* FM = s->final_mods + (size_t)step * 2 * H;
+    T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
     T2W_TRY(launch_ln_mod(h, H, FM, FM + H, c.eps_final, R, H, a, H, nullptr, st));
     GemmArgs fin = GemmArgs();
     fin.rows_a = R; fin.M = R; fin.err = s->err;
     fin.A = a; fin.lda = H; fin.W = s->w_fin; fin.bias = s->b_fin; fin.N = mel; fin.K = H; fin.epi = T2W_EPI_F32;
     fin.out = dphi; fin.ldo = mel;
-    T2W_TRY(launch_gemm(fin, st, &tm_a, &s->tm_fin));
+    T2W_TRY(P.tick(T2W_KC_GEMM_FINAL, st));
+    T2W_TRY(launch_gemm(fin, st, &tm_a, &s->tm_fin, nullptr));
     const bool last = step == c.steps - 1;
+    T2W_TRY(P.tick(T2W_KC_EULER, st));
     T2W_TRY(launch_euler(x, dphi, mel, tok_row, pl.n_tok, mel, pl.half_rows, s->dts[step], c.cfg_rate,
                          last ? nullptr : hx, 4 * mel, last ? b.out : nullptr, st));
   }
-  return T2W_OK;
+  return P.tick(-1, st);  // closing event
 }
 
 int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
@@ -528,6 +571,8 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
 int t2w_destroy(t2w_solver* s) {
   if (!s) return T2W_ERR_INVALID;
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  if (s->cap_stream) cudaStreamDestroy(s->cap_stream);
+  for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
   cudaFree(s->arena);
   delete s;
   return T2W_OK;
@@ -564,10 +609,13 @@ int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_byte
     cudaStreamCaptureStatus cs;
     T2W_CUDA(cudaStreamIsCapturing(st, &cs));
     if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: use flags = 0
-    T2W_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_solve(s, pl, *b, ws, st);
+    // Capture on the solver's own stream (the caller's may be the legacy default stream, which cannot be captured);
+    // capturing executes nothing, and the graph is launched on the caller's stream below.
+    if (!s->cap_stream) T2W_CUDA(cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking));
+    T2W_CUDA(cudaStreamBeginCapture(s->cap_stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_solve(s, pl, *b, ws, s->cap_stream);
     cudaGraph_t graph = nullptr;
-    const cudaError_t ec = cudaStreamEndCapture(st, &graph);
+    const cudaError_t ec = cudaStreamEndCapture(s->cap_stream, &graph);
     if (rc) {
       if (graph) cudaGraphDestroy(graph);
       return rc;
@@ -588,6 +636,36 @@ int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_byte
   }
   T2W_CUDA(cudaGraphLaunch(g->second, st));
   ++s->n_replays;
+  return T2W_OK;
+}
+
+int t2w_profile_solve(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_bytes, void* stream, float* ms,
+                      int32_t* launches) {
+  if (!s || !b || !ws || !ms || !launches || !b->x0 || !b->mu || !b->cond || !b->spk || !b->out) return T2W_ERR_INVALID;
+  Plan pl;
+  if (!make_plan(s->cfg, b->n_streams, b->prompt_len, b->chunk_len, pl)) return T2W_ERR_INVALID;
+  if (layout(s->cfg, pl).total > ws_bytes || (reinterpret_cast<uintptr_t>(ws) & 255)) return T2W_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto it = s->ws_meta.find(reinterpret_cast<uintptr_t>(ws));
+  if (it == s->ws_meta.end() || it->second != pl.key) T2W_TRY(upload_meta(s, pl, ws, st));
+  Prof prof;
+  prof.events = &s->prof_events;
+  T2W_TRY(enqueue_solve(s, pl, *b, ws, st, &prof));
+  T2W_CUDA(cudaStreamSynchronize(st));
+  for (int c = 0; c < T2W_KC_COUNT; ++c) {
+    ms[c] = 0.f;
+    launches[c] = 0;
+  }
+  for (size_t i = 0; i + 1 < prof.cls.size(); ++i) {
+    float t = 0.f;
+    T2W_CUDA(cudaEventElapsedTime(&t, s->prof_events[i], s->prof_events[i + 1]));
+    const int c = prof.cls[i];
+    if (c >= 0 && c < T2W_KC_COUNT) {
+      ms[c] += t;
+      launches[c] += 1;
+    }
+  }
+  ++s->n_eager;
   return T2W_OK;
 }
 

@@ -10,7 +10,8 @@
  *   t2w_solve_packed      FastDiT.solve               engine/runtime/dit_fast.py:432-495, and
  *                         BatchedToken2Wav._solve     engine/runtime/token2wav_batch.py:632-702 (CFG Euler solve)
  *   t2w_mods              FastDiT._modulations        engine/runtime/dit_fast.py:157-178
- *   t2w_ln_mod            ln_mod / add_ln_mod         engine/runtime/dit_kernels.py:13-60
+ *   t2w_ln_mod            ln_mod                      engine/runtime/dit_kernels.py:13-32
+ *   t2w_add_ln_mod        add_ln_mod                  engine/runtime/dit_kernels.py:35-60
  *   t2w_ln_mish           ln_mish                     engine/runtime/dit_kernels.py:145-164
  *   t2w_gemm              F.linear calls of the block engine/runtime/dit_fast.py:283-301 (cuBLAS in the reference)
  *   t2w_attn_varlen       BatchPrefillWithPagedKVCacheWrapper.run  engine/runtime/dit_fast.py:291,347-367
@@ -159,22 +160,28 @@ T2W_API int t2w_counts(const t2w_solver* s, int64_t* graph_replays, int64_t* gra
 T2W_API int t2w_ln_mod(const float* h, int32_t ld_h, const float* shift, const float* scale1, float eps, int32_t rows,
                int32_t C, void* out_bf16, int32_t ld_out, const uint8_t* pad, void* stream);
 
+/* h[r] += g * y[r] (y bf16 [rows, C], fp32 math, h updated in place; skipped when y is NULL), then
+ * out[r] = bf16(LN(h[r]) * scale1 + shift); rows whose pad[r] != 0 get zero output.  Replaces add_ln_mod
+ * (dit_kernels.py:35-60), with the residual kept in fp32. */
+T2W_API int t2w_add_ln_mod(float* h, const void* y_bf16, const float* g, const float* shift, const float* scale1, float eps,
+                           int32_t rows, int32_t C, void* out_bf16, const uint8_t* pad, void* stream);
+
 /* out[r] = bf16(Mish(LN_affine(x[r]))) with x bf16; rows whose pad[r] != 0 are zero. */
 T2W_API int t2w_ln_mish(const void* x_bf16, const float* w, const float* b, float eps, int32_t rows, int32_t C,
                 void* out_bf16, const uint8_t* pad, void* stream);
 
-#define T2W_EPI_F32 0   /* out fp32 = acc + bias */
-#define T2W_EPI_BF16 1  /* out bf16 = acc + bias */
-#define T2W_EPI_GELU 2  /* out bf16 = gelu_tanh(acc + bias) */
-#define T2W_EPI_RESID 3 /* resid fp32 += gate * (acc + bias) (in place) */
-#define T2W_EPI_QKV 4   /* out bf16 = [LN_q(q) | LN_k(k) | v] per 64-wide head (q/k affine norms) */
+#define T2W_EPI_F32 0  /* out fp32 = acc + bias */
+#define T2W_EPI_BF16 1 /* out bf16 = acc + bias */
+#define T2W_EPI_GELU 2 /* out bf16 = gelu_tanh(acc + bias) */
+#define T2W_EPI_QKV 4  /* out bf16 = [LN_q(q) | LN_k(k) | v] per 64-wide head (q/k affine norms) */
 
 /* C[M, N] = sum_tap A[m + tap_row0 + tap, :K] . W[n, tap*K : (tap+1)*K] then the epilogue.  A bf16 [rows_a, lda],
- * W bf16 [N, taps*K]; rows outside [0, rows_a) read as zero (causal-conv taps).  M % 128 == 0, K % 64 == 0, N % 16 == 0.
- * qk: for T2W_EPI_QKV, [qn_w, qn_b, kn_w, kn_b] (head_dim each) and qk_eps; q columns [0, N/3), k [N/3, 2N/3). */
+ * W bf16 [N, taps*K]; rows outside [0, rows_a) read as zero (causal-conv taps).  M % 128 == 0, K % 64 == 0,
+ * N % 128 == 0 or N == 80.  qk: for T2W_EPI_QKV, [qn_w, qn_b, kn_w, kn_b] (head_dim each) and qk_eps; q columns
+ * [0, N/3), k [N/3, 2N/3).  The gated residual of proj / conv2 / fc2 is applied by t2w_add_ln_mod. */
 T2W_API int t2w_gemm(const void* A_bf16, int32_t lda, int32_t rows_a, const void* W_bf16, const float* bias, int32_t M,
-             int32_t N, int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo, float* resid,
-             int32_t ld_resid, const float* gate, const float* const* qk, float qk_eps, void* stream);
+                     int32_t N, int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo,
+                     const float* const* qk, float qk_eps, void* stream);
 
 /* Varlen attention over packed sequences with the block-causal chunk mask: sequence s has its keys at rows
  * seq_row[s] .. seq_row[s] + seq_len[s] - 1 of qkv (bf16 [rows, 3 * heads * 64], q | k | v column blocks); a query at

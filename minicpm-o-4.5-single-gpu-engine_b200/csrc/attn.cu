@@ -1,16 +1,22 @@
 // Varlen attention over packed [prompt | chunk] sequences, head_dim 64, on tcgen05 tensor cores.
 //
-// One CTA per (128-query tile, head).  Mask (the reference's streaming form, packed): a query at position i of its
-// sequence attends keys j < lim(i), lim = P for prompt queries (i < P), L for chunk queries.  The reference solves the
-// prompt alone and then the chunk against the prompt's cached keys (engine/runtime/token2wav_batch.py:632-702,
-// FlashInfer non-causal prefill over [new, cache] slots: engine/runtime/dit_fast.py:347-367); attention depends only on
-// the key set, so both give the same rows.
+// Mask (the reference's streaming form, packed): a query at position i of its sequence attends keys j < lim(i),
+// lim = P for prompt queries (i < P), L for chunk queries.  The reference solves the prompt alone and then the chunk
+// against the prompt's cached keys (engine/runtime/token2wav_batch.py:632-702, FlashInfer non-causal prefill over
+// [new, cache] slots: engine/runtime/dit_fast.py:347-367); attention depends only on the key set, so both give the
+// same rows.
 //
-// Warps: 0 = TMA (Q once, K/V tiles of 128 keys, 2 stages), 1 = MMA issuer, 2-5 = softmax / output, one query row per
-// thread (TMEM lane).  Per key tile j: S = Q K^T (M 128, N 128, K 64) into TMEM; the row's thread reads S, updates its
-// running max / sum, writes P = exp(S - m) as bf16 into shared memory (K-major, 128B swizzle), then O_j = P V (M 128,
-// N 64, K 128, V read MN-major straight from its TMA tile) into TMEM; the thread folds O_j into its fp32 register
-// accumulator with the running rescale.  No TMA multicast.
+// Persistent CTAs (one per SM), two independent pipelines per CTA.  A work item is (128-query tile, head); pipeline p
+// of CTA c takes items p + 2 (c + k * grid).  Warps: 0 = TMA producer for both pipelines, 1 = TMEM allocator and MMA
+// issuer for both (each a polling loop over the two pipelines' barriers), 2-5 = softmax of pipeline 0, 6-9 = softmax of
+// pipeline 1 (one query row per thread = TMEM lane).  Per key tile j of 128 keys:
+//   S = Q K^T (M 128, N 128, K 64) into the pipeline's TMEM S region;
+//   the row's thread loads its 128 scores, updates the running max (log2 domain) and, when that max rises by more than
+//   8 (or on the first tile), rescales its O row in TMEM; it writes P = 2^(S c - m) as bf16 pairs back into the S
+//   columns (tcgen05.st), so the P V product reads A straight from TMEM;
+//   O += P V (M 128, N 64, K 128, V MN-major from its TMA tile) accumulates in the pipeline's TMEM O region.
+// Tensor-core ops of one issuing thread run in issue order, so S_{j+1} never overwrites P_j before P_j V_j has read it.
+// No TMA multicast.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -21,57 +27,94 @@ namespace {
 constexpr int kTile = 128;
 constexpr int kD = 64;
 constexpr int kTileBytes = kTile * kD * 2;  // 16 KB: 128 rows x 128 bytes
-constexpr int kSCol = 0, kOCol = 128, kTmemCols = 256;
-constexpr int kSmem = kTileBytes * (1 + 2 + 2 + 2) + 1024 + 256;  // Q, K x2, V x2, P (2 swizzle atoms)
+constexpr int kStages = 2;
+constexpr int kPipeBytes = kTileBytes * (1 + 2 * kStages);  // Q + K/V ring
+constexpr int kSmem = 2 * kPipeBytes + 1024 + 512;
+constexpr int kTmemCols = 512;  // per pipeline: S/P 128 columns at 256 p, O 64 columns at 256 p + 128
+constexpr float kRescaleThreshold = 8.f;
 
 struct DevArgs {
   const AttnWork* work;
-  int heads;
+  int n_items, heads;
   __nv_bfloat16* out;
   int ldo;
   float scale_log2;
   int* err;
 };
 
-__global__ void __launch_bounds__(192, 1) k_attn(const __grid_constant__ CUtensorMap tm, const DevArgs p) {
+struct PipeBars {
+  uint64_t q_full, q_free, kv_full[kStages], kv_empty[kStages], s_full, p_full, o_done, o_free;
+};
+
+T2W_DEV void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+T2W_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// O (+)= P V with P from TMEM (A operand, K-major: 2 bf16 keys per 32-bit column) and V from shared memory.
+T2W_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+T2W_DEV int item_tiles(const AttnWork& w) {
+  const int kmax = (w.q_pos + kTile > w.P) ? w.L : w.P;  // any chunk query in the tile sees every key
+  return (kmax + kTile - 1) / kTile;
+}
+
+// Per-pipeline progress of the producer and of the MMA issuer (each a polling state machine).
+struct ProdState {
+  int k = 0, item = -1, j = 0, n_kt = 0, stage = 0;
+  uint32_t phase = 0;
+  bool need_q = true, done = false;
+  AttnWork w{};
+  int h = 0;
+};
+struct MmaState {
+  int k = 0, item = -1, j = 0, n_kt = 0, stage = 0, tiles = 0;
+  uint32_t phase = 0;
+  int st = 0;  // 0 wait Q, 1 wait K/V, 2 wait P, 3 done
+  bool done = false;
+};
+
+__global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtensorMap tm, const DevArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTileBytes;      // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;  // 2 stages
-  uint8_t* sP = sV + 2 * kTileBytes;  // keys 0..63 | keys 64..127
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTileBytes);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_full = bars + 8;
-  uint64_t* o_free = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
-
-  const AttnWork w = p.work[blockIdx.x];
-  const int h = blockIdx.y;
-  const int H = p.heads * kD;
-  const int kmax = (w.q_pos + kTile > w.P) ? w.L : w.P;  // any chunk query in the tile sees every key
-  const int n_kt = (kmax + kTile - 1) / kTile;
+  PipeBars* bars = reinterpret_cast<PipeBars*>(smem + 2 * kPipeBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = p.heads * kD;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int q = 0; q < 2; ++q) {
+      PipeBars& b = bars[q];
+      mbar_init(&b.q_full, 1);
+      mbar_init(&b.q_free, 1);
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(&b.kv_full[s], 1);
+        mbar_init(&b.kv_empty[s], 1);
+      }
+      mbar_init(&b.s_full, 1);
+      mbar_init(&b.p_full, 4);
+      mbar_init(&b.o_done, 1);
+      mbar_init(&b.o_free, 4);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     fence_mbar_init();
     tma_prefetch_desc(&tm);
   }
+  pdl_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -79,133 +122,238 @@ __global__ void __launch_bounds__(192, 1) k_attn(const __grid_constant__ CUtenso
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch();
   const uint32_t tmem = *tmem_slot;
+  const int stride = 2 * gridDim.x;
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tm, h * kD, w.q_row, q_full);
-      for (int j = 0; j < n_kt; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1u, p.err)) break;
-        mbar_expect_tx(&kv_full[s], 2 * kTileBytes);
-        tma_load_2d(sK + s * kTileBytes, &tm, H + h * kD, w.k_row + j * kTile, &kv_full[s]);
-        tma_load_2d(sV + s * kTileBytes, &tm, 2 * H + h * kD, w.k_row + j * kTile, &kv_full[s]);
+      ProdState ps[2];
+      unsigned long long idle_since = globaltimer();
+      bool abort = false;
+      while (!(ps[0].done && ps[1].done) && !abort) {
+        bool progressed = false;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          ProdState& s = ps[q];
+          if (s.done) continue;
+          PipeBars& b = bars[q];
+          uint8_t* base = smem + q * kPipeBytes;
+          if (s.need_q) {
+            const int item = q + 2 * blockIdx.x + s.k * stride;
+            if (item >= p.n_items) {
+              s.done = true;
+              progressed = true;
+              continue;
+            }
+            // the previous item's last S MMA has read the Q buffer
+            if (!mbar_test(smem_u32(&b.q_free), ((s.k & 1) ^ 1u))) continue;
+            s.item = item;
+            s.w = p.work[item / p.heads];
+            s.h = item % p.heads;
+            s.n_kt = item_tiles(s.w);
+            s.j = 0;
+            mbar_expect_tx(&b.q_full, kTileBytes);
+            tma_load_2d(base, &tm, s.h * kD, s.w.q_row, &b.q_full);
+            s.need_q = false;
+            progressed = true;
+          } else {
+            if (!mbar_test(smem_u32(&b.kv_empty[s.stage]), s.phase ^ 1u)) continue;
+            uint8_t* kv = base + kTileBytes + s.stage * 2 * kTileBytes;
+            mbar_expect_tx(&b.kv_full[s.stage], 2 * kTileBytes);
+            tma_load_2d(kv, &tm, H + s.h * kD, s.w.k_row + s.j * kTile, &b.kv_full[s.stage]);
+            tma_load_2d(kv + kTileBytes, &tm, 2 * H + s.h * kD, s.w.k_row + s.j * kTile, &b.kv_full[s.stage]);
+            if (++s.stage == kStages) {
+              s.stage = 0;
+              s.phase ^= 1u;
+            }
+            if (++s.j == s.n_kt) {
+              s.need_q = true;
+              ++s.k;
+            }
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle_since = globaltimer();
+        } else if (globaltimer() - idle_since > kWaitLimitNs) {
+          atomicExch(p.err, T2W_ERR_TIMEOUT);
+          abort = true;
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_bf16(kTile, kTile);
       constexpr uint32_t idesc_pv = idesc_bf16(kTile, kD, /*b_mn_major=*/true);
-      bool ok = mbar_wait(q_full, 0, p.err);
-      const uint32_t q0 = smem_u32(sQ), p0 = smem_u32(sP);
-      for (int j = 0; j < n_kt && ok; ++j) {
-        const int s = j & 1;
-        if (!(ok = mbar_wait(&kv_full[s], (j >> 1) & 1, p.err))) break;
-        if (j > 0 && !(ok = mbar_wait(s_free, (j - 1) & 1, p.err))) break;
-        tc_fence_after();
-        const uint32_t k0 = smem_u32(sK + s * kTileBytes), v0 = smem_u32(sV + s * kTileBytes);
+      MmaState ms[2];
+      unsigned long long idle_since = globaltimer();
+      bool abort = false;
+      while (!(ms[0].done && ms[1].done) && !abort) {
+        bool progressed = false;
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k)
-          umma_f16(tmem + kSCol, sdesc_sw128(q0 + 32 * k, 1024, 16), sdesc_sw128(k0 + 32 * k, 1024, 16), idesc_qk,
-                   k ? 1u : 0u);
-        umma_commit(s_full);
-        if (!(ok = mbar_wait(p_full, j & 1, p.err))) break;
-        if (j > 0 && !(ok = mbar_wait(o_free, (j - 1) & 1, p.err))) break;
-        tc_fence_after();
+        for (int q = 0; q < 2; ++q) {
+          MmaState& s = ms[q];
+          if (s.done) continue;
+          PipeBars& b = bars[q];
+          uint8_t* base = smem + q * kPipeBytes;
+          const uint32_t sreg = tmem + 256 * q, oreg = sreg + 128;
+          if (s.st == 0) {  // wait for this item's Q
+            const int item = q + 2 * blockIdx.x + s.k * stride;
+            if (item >= p.n_items) {
+              s.done = true;
+              progressed = true;
+              continue;
+            }
+            if (!mbar_test(smem_u32(&b.q_full), s.k & 1)) continue;
+            s.item = item;
+            s.n_kt = item_tiles(p.work[item / p.heads]);
+            s.j = 0;
+            s.st = 1;
+            progressed = true;
+          } else if (s.st == 1) {  // S_j = Q K_j^T
+            if (!mbar_test(smem_u32(&b.kv_full[s.stage]), s.phase)) continue;
+            tc_fence_after();
+            const uint32_t q0 = smem_u32(base), k0 = smem_u32(base + kTileBytes + s.stage * 2 * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < kTile / 16; ++k) {
-          // A = P (K-major): 16 keys at byte 32 (k % 4) of swizzle atom k / 4.  B = V (MN-major): 16 key rows.
-          umma_f16(tmem + kOCol, sdesc_sw128(p0 + (k >> 2) * kTileBytes + 32 * (k & 3), 1024, 16),
-                   sdesc_sw128(v0 + k * 16 * 128, 1024, 8192), idesc_pv, k ? 1u : 0u);
+            for (int k = 0; k < kD / 16; ++k)
+              umma_f16(sreg, sdesc_sw128(q0 + 32 * k, 1024, 16), sdesc_sw128(k0 + 32 * k, 1024, 16), idesc_qk, k ? 1u : 0u);
+            umma_commit(&b.s_full);
+            if (s.j == s.n_kt - 1) umma_commit(&b.q_free);
+            s.st = 2;
+            progressed = true;
+          } else {  // O += P_j V_j once the softmax has written P_j (and, for j = 0, read the previous item's O)
+            if (!mbar_test(smem_u32(&b.p_full), s.tiles & 1)) continue;
+            if (s.j == 0 && s.k > 0 && !mbar_test(smem_u32(&b.o_free), (s.k - 1) & 1)) continue;
+            tc_fence_after();
+            const uint32_t v0 = smem_u32(base + kTileBytes + s.stage * 2 * kTileBytes + kTileBytes);
+#pragma unroll
+            for (int k = 0; k < kTile / 16; ++k)
+              umma_f16_ts(oreg, sreg + 8 * k, sdesc_sw128(v0 + k * 16 * 128, 1024, 8192), idesc_pv,
+                          (s.j > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&b.o_done);
+            umma_commit(&b.kv_empty[s.stage]);
+            ++s.tiles;
+            if (++s.stage == kStages) {
+              s.stage = 0;
+              s.phase ^= 1u;
+            }
+            if (++s.j == s.n_kt) {
+              ++s.k;
+              s.st = 0;
+            } else {
+              s.st = 1;
+            }
+            progressed = true;
+          }
         }
-        umma_commit(o_full);
-        umma_commit(&kv_empty[s]);
+        if (progressed) {
+          idle_since = globaltimer();
+        } else if (globaltimer() - idle_since > kWaitLimitNs) {
+          atomicExch(p.err, T2W_ERR_TIMEOUT);
+          abort = true;
+        }
       }
     }
   } else {
-    const int qw = warp & 3;
-    const int r = qw * 32 + lane;  // query row of the tile == TMEM lane
-    const int pos = w.q_pos + r;
-    const int lim = pos < w.P ? w.P : (pos < w.L ? w.L : 0);
-    const uint32_t trow = tmem + ((uint32_t)(qw * 32) << 16);
-    float m = -INFINITY, l = 0.f;
-    float o[kD];
+    const int q = (warp - 2) >> 2;  // pipeline
+    const int qw = warp & 3;        // TMEM lane quarter
+    const int r = qw * 32 + lane;   // query row of the tile
+    PipeBars& b = bars[q];
+    const uint32_t lanes = (uint32_t)(qw * 32) << 16;
+    const uint32_t sreg = tmem + 256 * q + lanes, oreg = tmem + 256 * q + 128 + lanes;
+    int tiles = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int item = q + 2 * blockIdx.x + k * stride;
+      if (item >= p.n_items) break;
+      const AttnWork w = p.work[item / p.heads];
+      const int h = item % p.heads;
+      const int n_kt = item_tiles(w);
+      const int pos = w.q_pos + r;
+      const int lim = pos < w.P ? w.P : (pos < w.L ? w.L : 0);
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_kt; ++j, ++tiles) {
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.s_full, tiles & 1, p.err)))) break;
+        // P_{j-1} V_{j-1} was issued before S_j, so it is complete too; waiting keeps o_done's phases in step
+        if (j > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done, (tiles - 1) & 1, p.err)))) break;
+        tc_fence_after();
+        // pass 1: the row max over valid keys (32 scores live at a time)
+        const int kb = j * kTile;
+        float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kD; ++i) o[i] = 0.f;
-    uint8_t* prow = sP + r * 128;
-    for (int j = 0; j < n_kt; ++j) {
-      // warp-uniform: tcgen05.ld below is .sync.aligned
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err))) break;
-      tc_fence_after();
-      const int kb = j * kTile;
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(trow + kSCol + 32 * c, v);
+        for (int c = 0; c < 4; ++c) {
+          float sv[32];
+          tmem_ld32(sreg + 32 * c, sv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (kb + 32 * c + i < lim) mx = fmaxf(mx, v[i]);
-      }
-      const float m_new = fmaxf(m, mx * p.scale_log2);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(trow + kSCol + 32 * c, v);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k0 = kb + 32 * c + 2 * i;
-          const float e0 = (k0 < lim) ? exp2f(v[2 * i] * p.scale_log2 - m_use) : 0.f;
-          const float e1 = (k0 + 1 < lim) ? exp2f(v[2 * i + 1] * p.scale_log2 - m_use) : 0.f;
-          rs += e0 + e1;
-          pk[i] = pack_bf16x2(e0, e1);
+          for (int i = 0; i < 32; ++i)
+            if (kb + 32 * c + i < lim) mx = fmaxf(mx, sv[i]);
         }
-        // keys 32c .. 32c + 31 = four 16-byte chunks of the row, in atom (32c / 64), swizzled by row % 8
-        uint8_t* atom = prow + (c >> 1) * kTileBytes;
+        mx *= p.scale_log2;
+        // raise the reference max only when it grows by more than the threshold (p <= 2^8 fits bf16 comfortably)
+        const bool raise = mx > m + kRescaleThreshold;
+        const float m_new = raise ? mx : m;
+        if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          const float f = raise ? exp2f(m - m_new) : 1.f;
+          l *= f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int chunk = ((c & 1) * 4 + u) ^ (r & 7);
-          *reinterpret_cast<uint4*>(atom + chunk * 16) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          for (int c = 0; c < 2; ++c) {
+            float o[32];
+            tmem_ld32(oreg + 32 * c, o);
+            uint32_t u[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * f);
+            tmem_st32(oreg + 32 * c, u);
+          }
         }
+        m = m_new;
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        // pass 2: P = 2^(S c - m) as bf16 pairs, written back over the S columns it came from
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float sv[64];
+          tmem_ld32p(sreg + 64 * c, sv);
+          tmem_ld32p(sreg + 64 * c + 32, sv + 32);
+          uint32_t u[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int kk = kb + 64 * c + 2 * i;
+            const float e0 = (kk < lim) ? exp2_approx(fmaf(sv[2 * i], p.scale_log2, -m_use)) : 0.f;
+            const float e1 = (kk + 1 < lim) ? exp2_approx(fmaf(sv[2 * i + 1], p.scale_log2, -m_use)) : 0.f;
+            rs += e0 + e1;
+            u[i] = pack_bf16x2(e0, e1);
+          }
+          tmem_st32(sreg + 32 * c, u);
+        }
+        l += rs;
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b.p_full);
       }
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);
-        mbar_arrive(p_full);
-      }
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_use);
-      l = l * alpha + rs;
-      m = m_new;
-      if (!__all_sync(0xffffffffu, mbar_wait(o_full, j & 1, p.err))) break;
+      if (!ok) break;
+      // the item's last P V
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done, (tiles - 1) & 1, p.err)))) break;
       tc_fence_after();
-      float oj[32];
-      tmem_ld32(trow + kOCol, oj);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], alpha, oj[i]);
-      tmem_ld32(trow + kOCol + 32, oj);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[32 + i] = fmaf(o[32 + i], alpha, oj[i]);
+      float o[kD];
+      tmem_ld32p(oreg, o);
+      tmem_ld32p(oreg + 32, o + 32);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);
-    }
-    if (lim > 0) {
-      const float inv = 1.f / l;
-      __nv_bfloat16* dst = p.out + (size_t)(w.q_row + r) * p.ldo + h * kD;
+      if (lane == 0) mbar_arrive(&b.o_free);
+      if (lim > 0) {
+        const float inv = 1.f / l;
+        __nv_bfloat16* dst = p.out + (size_t)(w.q_row + r) * p.ldo + h * kD;
 #pragma unroll
-      for (int u = 0; u < kD / 8; ++u) {
-        uint4 q;
-        q.x = pack_bf16x2(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
-        q.y = pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
-        q.z = pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
-        q.w = pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
-        reinterpret_cast<uint4*>(dst)[u] = q;
+        for (int u = 0; u < kD / 8; ++u) {
+          uint4 v;
+          v.x = pack_bf16x2(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
+          v.y = pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
+          v.z = pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
+          v.w = pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
+          reinterpret_cast<uint4*>(dst)[u] = v;
+        }
       }
     }
   }
@@ -236,10 +384,11 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm) {
     if (!make_tmap_2d(&m, a.qkv, 2, (uint64_t)a.rows, cols, cols * 2, kTile, kD)) return T2W_ERR_INVALID;
     tm = &m;
   }
-  DevArgs p{a.work, a.heads, reinterpret_cast<__nv_bfloat16*>(a.out), a.heads * kD, a.scale_log2, a.err};
-  dim3 grid(a.n_work, a.heads);
-  k_attn<<<grid, 192, kSmem, st>>>(*tm, p);
-  cudaError_t e = cudaGetLastError();
+  const int n_items = a.n_work * a.heads;
+  DevArgs p{a.work, n_items, a.heads, reinterpret_cast<__nv_bfloat16*>(a.out), a.heads * kD, a.scale_log2, a.err};
+  int grid = (n_items + 1) / 2;
+  if (grid > num_sms()) grid = num_sms();
+  cudaError_t e = launch_k(k_attn, dim3(grid), dim3(320), kSmem, st, *tm, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;

@@ -48,6 +48,18 @@ T2W_DEV bool mbar_try_wait(uint32_t addr, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe of a phase (for loops that poll several barriers: try_wait may suspend the thread for a while).
+T2W_DEV bool mbar_test(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Wait for the phase of parity `parity` to complete; false (and the error word set) after kWaitLimitNs.
 T2W_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   const uint32_t a = smem_u32(bar);
@@ -167,11 +179,25 @@ T2W_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream serialization: it may start while its predecessor
+// drains.  pdl_wait() blocks until the predecessor grid has completed and its memory is visible; each kernel calls it
+// before touching activations and before allocating TMEM (so an early CTA never holds TMEM its predecessor needs).
+// pdl_launch() then lets the successor start launching.
+T2W_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+T2W_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- small math
 T2W_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+// 2^x with the hardware approximation (ex2.approx, flush-to-zero); used for softmax weights rounded to bf16 afterwards.
+T2W_DEV float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 T2W_DEV float tanh_approx(float x) {
   float y;

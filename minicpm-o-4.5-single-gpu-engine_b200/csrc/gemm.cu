@@ -3,11 +3,12 @@
 // One persistent CTA per SM, 6 warps:
 //   warp 0  : TMA producer (one elected lane), STAGES-deep ring of A [128 x 64] and W [BN x 64] bf16 tiles, 128B swizzle
 //   warp 1  : TMEM allocator + single-thread tcgen05.mma issuer (M = 128, N = BN, K = 16 per instruction)
-//   warps 2-5: epilogue; warp w reads TMEM lanes 32 (w % 4) .. +31, so each thread owns one output row
+//   warps 2-9: epilogue in two halves of four warps; warp w reads TMEM lanes 32 (w % 4) .. +31, so each thread owns one
+//              output row, and half (w - 2) / 4 takes every other 128-byte output box of the tile
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so a tile's epilogue overlaps the next tile's MMAs.
-// The epilogue stages its output tile in shared memory (128-byte swizzled boxes of 128 rows x 128 bytes) and writes it
-// with asynchronous TMA stores; for the gated residual it first TMA-loads the fp32 residual tile into the same buffer
-// (issued before it waits for the accumulator, so the load overlaps the MMAs).
+// Each epilogue half stages its boxes (128 rows x 128 bytes, 128B swizzle) in its own shared-memory slot and writes them
+// with asynchronous TMA stores issued by the half's leader thread.  Two warps per SM sub-partition keep the TMEM loads
+// and the epilogue math of one box overlapped with the other's.
 // The causal convolutions use taps = 3, tap_row0 = -2: tap t of output row m reads activation row m - 2 + t, so the
 // im2col matrix is never materialised; rows before 0 come back zero from TMA.  No TMA multicast.
 #include <cstdio>
@@ -24,7 +25,7 @@ constexpr int kBK = 64;  // bf16 elements per 128-byte swizzle row
 constexpr int kMaxSmem = 232448;
 constexpr int kBoxBytes = kBM * 128;  // one staged output box: 128 rows x 128 bytes
 
-__host__ __device__ constexpr bool epi_f32_out(int epi) { return epi == T2W_EPI_F32 || epi == T2W_EPI_RESID; }
+__host__ __device__ constexpr bool epi_f32_out(int epi) { return epi == T2W_EPI_F32; }
 
 template <int BN, int EPI, bool TMA_OUT>
 struct GemmCfg {
@@ -34,15 +35,16 @@ struct GemmCfg {
   static constexpr int OUT_ELEM = epi_f32_out(EPI) ? 4 : 2;
   static constexpr int BOX_COLS = 128 / OUT_ELEM;
   static constexpr int N_BOXES = TMA_OUT ? BN / BOX_COLS : 0;
-  static constexpr int OUT_BYTES = N_BOXES * kBoxBytes;
+  static constexpr int OUT_BYTES = TMA_OUT ? 2 * kBoxBytes : 0;  // one staging slot per epilogue half
   static constexpr int FIXED = 1024 + 256;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - OUT_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + FIXED;
+  static constexpr int THREADS = 320;
   static_assert(STAGES >= 2, "not enough shared memory for a 2-stage ring");
   static_assert(B_BYTES % 1024 == 0, "W tile must keep 1024-byte alignment of the swizzle atoms");
-  static_assert(!TMA_OUT || BN % BOX_COLS == 0, "output tile must be whole boxes");
+  static_assert(!TMA_OUT || (BN % BOX_COLS == 0 && N_BOXES % 2 == 0), "output tile must be an even number of boxes");
 };
 
 struct DevArgs {
@@ -50,7 +52,6 @@ struct DevArgs {
   const float* bias;
   void* out;
   int ldo;
-  const float* gate;
   const float* qn_w;
   const float* qn_b;
   const float* kn_w;
@@ -68,7 +69,8 @@ T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, i
 T2W_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 T2W_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 T2W_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-T2W_DEV void epi_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of one epilogue half (ids 1 and 2, 128 threads each).
+T2W_DEV void epi_barrier(int half) { asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory"); }
 
 // 16-byte chunk `c` of row `r` inside one staged box (128B swizzle: chunk index XOR row % 8).
 T2W_DEV uint8_t* box_chunk(uint8_t* box, int r, int c) { return box + r * 128 + ((c ^ (r & 7)) << 4); }
@@ -97,94 +99,82 @@ T2W_DEV void stage_bf16_row(uint8_t* box, int r, const float* v) {
   }
 }
 
-// Epilogue of one tile into the staging buffer (TMA_OUT) or straight to global memory (BN = 80 final layer).
-template <int BN, int EPI, bool TMA_OUT>
-T2W_DEV void epilogue(const DevArgs& p, uint32_t taddr, int r, int row, int n0, uint8_t* stage) {
-  if constexpr (!TMA_OUT) {
-    static_assert(EPI == T2W_EPI_F32 || EPI == T2W_EPI_BF16, "direct stores: f32 / bf16 only");
+// Direct-store epilogue of one tile (BN = 80 final layer: no staging).
+template <int BN, int EPI>
+T2W_DEV void epilogue_direct(const DevArgs& p, uint32_t taddr, int row, int n0) {
+  static_assert(EPI == T2W_EPI_F32 || EPI == T2W_EPI_BF16, "direct stores: f32 / bf16 only");
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      tmem_ld16(taddr + c, v);
-      if (row >= p.M) continue;
-      add_bias(v, p.bias + n0 + c, 16);
-      if constexpr (EPI == T2W_EPI_F32) {
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + n0 + c);
+  for (int c = 0; c < BN; c += 16) {
+    float v[16];
+    tmem_ld16(taddr + c, v);
+    if (row >= p.M) continue;
+    add_bias(v, p.bias + n0 + c, 16);
+    if constexpr (EPI == T2W_EPI_F32) {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + n0 + c);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      } else {
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + n0 + c);
-        dst[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-        dst[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
-                            pack_bf16x2(v[14], v[15]));
-      }
-    }
-  } else if constexpr (EPI == T2W_EPI_F32 || EPI == T2W_EPI_RESID) {
-#pragma unroll 1
-    for (int b = 0; b < BN / 32; ++b) {
-      float v[32];
-      tmem_ld32(taddr + 32 * b, v);
-      const int col = n0 + 32 * b;
-      add_bias(v, p.bias + col, 32);
-      uint8_t* box = stage + b * kBoxBytes;
-      if constexpr (EPI == T2W_EPI_RESID) {
-        const float* g = p.gate + col;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float4* q = reinterpret_cast<float4*>(box_chunk(box, r, c));
-          const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + c);
-          float4 h = *q;
-          h.x = fmaf(gg.x, v[4 * c + 0], h.x);
-          h.y = fmaf(gg.y, v[4 * c + 1], h.y);
-          h.z = fmaf(gg.z, v[4 * c + 2], h.z);
-          h.w = fmaf(gg.w, v[4 * c + 3], h.w);
-          *q = h;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<float4*>(box_chunk(box, r, c)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-      }
-    }
-  } else {
-    // bf16 outputs: one 64-column box per iteration (one head for the QKV epilogue)
-    const int qcols = p.N / 3;
-#pragma unroll 1
-    for (int b = 0; b < BN / 64; ++b) {
-      float v[64];
-      tmem_ld32p(taddr + 64 * b, v);
-      tmem_ld32p(taddr + 64 * b + 32, v + 32);
-      const int c0 = n0 + 64 * b;
-      add_bias(v, p.bias + c0, 64);
-      if constexpr (EPI == T2W_EPI_QKV) {
-        if (c0 < 2 * qcols) {  // a q or k head: LayerNorm over its 64 values (affine), fp32
-          const float* nw = c0 < qcols ? p.qn_w : p.kn_w;
-          const float* nb = c0 < qcols ? p.qn_b : p.kn_b;
-          float s = 0.f;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) s += v[i];
-          const float mean = s * (1.f / 64.f);
-          float ss = 0.f;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float d = v[i] - mean;
-            ss += d * d;
-          }
-          const float rstd = rsqrtf(ss * (1.f / 64.f) + p.qk_eps);
-#pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = (v[i] - mean) * rstd * __ldg(nw + i) + __ldg(nb + i);
-        }
-      } else if constexpr (EPI == T2W_EPI_GELU) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = gelu_tanh(v[i]);
-      }
-      stage_bf16_row(stage + b * kBoxBytes, r, v);
+      for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + n0 + c);
+      dst[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+      dst[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                          pack_bf16x2(v[14], v[15]));
     }
   }
 }
 
+// Box b of a tile (BOX_COLS output columns of this thread's row r) into its staging box.
+template <int EPI, int BOX_COLS>
+T2W_DEV void epilogue_box(const DevArgs& p, uint32_t taddr, int r, int n0, int b, uint8_t* box) {
+  if constexpr (EPI == T2W_EPI_F32) {
+    float v[32];
+    tmem_ld32(taddr + 32 * b, v);
+    add_bias(v, p.bias + n0 + 32 * b, 32);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(box_chunk(box, r, c)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  } else {
+    // bf16 outputs: a 64-column box (one head for the QKV epilogue)
+    const int c0 = n0 + 64 * b;
+    float v[64];
+    tmem_ld32p(taddr + 64 * b, v);
+    tmem_ld32p(taddr + 64 * b + 32, v + 32);
+    add_bias(v, p.bias + c0, 64);
+    if constexpr (EPI == T2W_EPI_QKV) {
+      const int qcols = p.N / 3;
+      if (c0 < 2 * qcols) {  // a q or k head: LayerNorm over its 64 values (affine), fp32
+        const float* nw = c0 < qcols ? p.qn_w : p.kn_w;
+        const float* nb = c0 < qcols ? p.qn_b : p.kn_b;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s += v[i];
+        const float mean = s * (1.f / 64.f);
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float d = v[i] - mean;
+          ss += d * d;
+        }
+        const float rstd = rsqrtf(ss * (1.f / 64.f) + p.qk_eps);
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) {
+          const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw + i));
+          const float4 b4 = __ldg(reinterpret_cast<const float4*>(nb + i));
+          v[i + 0] = fmaf((v[i + 0] - mean) * rstd, w4.x, b4.x);
+          v[i + 1] = fmaf((v[i + 1] - mean) * rstd, w4.y, b4.y);
+          v[i + 2] = fmaf((v[i + 2] - mean) * rstd, w4.z, b4.z);
+          v[i + 3] = fmaf((v[i + 3] - mean) * rstd, w4.w, b4.w);
+        }
+      }
+    } else if constexpr (EPI == T2W_EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) v[i] = gelu_tanh(v[i]);
+    }
+    stage_bf16_row(box, r, v);
+  }
+}
+
 template <int BN, int EPI, bool TMA_OUT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
            const __grid_constant__ CUtensorMap tmC, const DevArgs p) {
   using C = GemmCfg<BN, EPI, TMA_OUT>;
@@ -197,8 +187,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* res_full = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -208,14 +197,14 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], 8);  // one arrival per epilogue warp
     }
-    mbar_init(res_full, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
     if constexpr (TMA_OUT) tma_prefetch_desc(&tmC);
   }
+  pdl_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
@@ -223,6 +212,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch();
   const uint32_t tmem = *tmem_slot;
 
   const int kb_per_tap = p.K / kBK;
@@ -280,8 +270,10 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = q * 32 + lane;  // tile row == TMEM lane
-    const bool leader = threadIdx.x == 64;
+    const bool leader = lane == 0 && q == 2;  // warps 2 and 6: store issuers of the two halves
+    uint8_t* slot = sOut + half * kBoxBytes;
     // `ok` stays warp-uniform (tcgen05.ld is .sync.aligned); after a timed-out wait the warp skips all further waits
     // and work but still reaches every named barrier, so no warp is left waiting at one.
     bool ok = true;
@@ -289,35 +281,30 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
-      if constexpr (TMA_OUT) {
-        if (leader) bulk_wait_read0();  // the previous tile's stores have read the staging buffer
-        epi_barrier();
-        if constexpr (EPI == T2W_EPI_RESID) {
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err));
+      if (ok) tc_fence_after();
+      if constexpr (!TMA_OUT) {
+        if (ok && half == 0) epilogue_direct<BN, EPI>(p, taddr, m0 + r, n0);
+      } else {
+#pragma unroll 1
+        for (int b = half; b < C::N_BOXES; b += 2) {
+          // this half's previous store has finished reading its slot
+          if (leader) bulk_wait_read0();
+          epi_barrier(half);
+          if (ok) epilogue_box<EPI, C::BOX_COLS>(p, taddr, r, n0, b, slot);
+          fence_proxy_async_smem();
+          epi_barrier(half);
           if (leader && ok) {
-            mbar_expect_tx(res_full, C::OUT_BYTES);
-            for (int b = 0; b < C::N_BOXES; ++b) tma_load_2d(sOut + b * kBoxBytes, &tmC, n0 + b * C::BOX_COLS, m0, res_full);
+            tma_store_2d(&tmC, slot, n0 + b * C::BOX_COLS, m0);
+            bulk_commit();
           }
         }
       }
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err));
-      if constexpr (EPI == T2W_EPI_RESID) {
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(res_full, it & 1, p.err));
-      }
-      if (ok) {
-        tc_fence_after();
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-        epilogue<BN, EPI, TMA_OUT>(p, taddr, r, m0 + r, n0, sOut);
+      if (ok) {  // every TMEM column this warp reads of the accumulator has been read
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
-      }
-      if constexpr (TMA_OUT) {
-        fence_proxy_async_smem();
-        epi_barrier();
-        if (leader && ok) {
-          for (int b = 0; b < C::N_BOXES; ++b) tma_store_2d(&tmC, sOut + b * kBoxBytes, n0 + b * C::BOX_COLS, m0);
-          bulk_commit();
-        }
       }
     }
     if constexpr (TMA_OUT) {
@@ -363,9 +350,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   if (!tmC) {
     if (TMA_OUT) {
       const bool f32 = epi_f32_out(EPI);
-      const void* base = EPI == T2W_EPI_RESID ? (const void*)a.resid : a.out;
-      const int ld = EPI == T2W_EPI_RESID ? a.ldr : a.ldo;
-      if (!make_tmap_2d(&mc, base, f32 ? 4 : 2, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)ld * (f32 ? 4 : 2), kBM,
+      if (!make_tmap_2d(&mc, a.out, f32 ? 4 : 2, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)a.ldo * (f32 ? 4 : 2), kBM,
                         C::BOX_COLS))
         return T2W_ERR_INVALID;
     } else {
@@ -384,7 +369,6 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.bias = a.bias;
   p.out = a.out;
   p.ldo = a.ldo;
-  p.gate = a.gate;
   p.qn_w = a.qn_w;
   p.qn_b = a.qn_b;
   p.kn_w = a.kn_w;
@@ -392,8 +376,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.qk_eps = a.qk_eps;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  k_gemm<BN, EPI, TMA_OUT><<<grid, 192, C::SMEM, st>>>(*tmA, *tmW, *tmC, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(k_gemm<BN, EPI, TMA_OUT>, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tmA, *tmW, *tmC, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -414,27 +397,25 @@ bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot) {
   return m->has128;
 }
 
-// Column tile: 80 only for the 80-wide final layer; fp32 outputs use 128 (the staged fp32 tile must fit beside the
-// ring); otherwise the larger of 128 / 256 unless 128 finishes in fewer whole waves of 128-column work.
+// Column tile: 80 for the 80-wide final layer, else 256 (a 128 x 128 tile needs operand bytes from shared memory
+// faster than the SM delivers them beside the TMA writes; 128 x 256 runs the tensor core at its rate), 128 only when N
+// is not a multiple of 256.
 int gemm_block_n_for(int N, int M, int epi) {
+  (void)M;
+  (void)epi;
   if (N == 80) return 80;
-  if (N % 128) return 0;
-  if (epi_f32_out(epi) || N % 256) return 128;
-  if (M <= 0) return 256;
-  const long long tiles_m = (M + kBM - 1) / kBM, sms = num_sms();
-  const long long w256 = (tiles_m * (N / 256) + sms - 1) / sms * 2, w128 = (tiles_m * (N / 128) + sms - 1) / sms;
-  return w128 < w256 ? 128 : 256;
+  if (N % 256 == 0) return 256;
+  if (N % 128 == 0) return 128;
+  return 0;
 }
 
 int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const WeightMaps* tmW,
                 const CUtensorMap* tmC) {
-  if (!a.A || !a.W || !a.bias || a.M <= 0 || a.M % kBM || a.K <= 0 || a.K % kBK || a.taps < 1 || a.rows_a <= 0 ||
-      a.lda < a.K || a.lda % 8)
+  if (!a.A || !a.W || !a.bias || !a.out || a.M <= 0 || a.M % kBM || a.K <= 0 || a.K % kBK || a.taps < 1 ||
+      a.rows_a <= 0 || a.lda < a.K || a.lda % 8 || a.ldo % 8)
     return T2W_ERR_INVALID;
   const int bn = gemm_block_n_for(a.N, a.M, a.epi);
   if (!bn) return T2W_ERR_INVALID;
-  if (a.epi == T2W_EPI_RESID && (!a.resid || !a.gate || a.ldr % 4)) return T2W_ERR_INVALID;
-  if (a.epi != T2W_EPI_RESID && (!a.out || a.ldo % 8)) return T2W_ERR_INVALID;
   if (a.epi == T2W_EPI_QKV && (a.N % 3 || (a.N / 3) % 64 || !a.qn_w || !a.qn_b || !a.kn_w || !a.kn_b)) return T2W_ERR_INVALID;
   if (bn == 80) {
     if (a.epi == T2W_EPI_F32) return launch_impl<80, T2W_EPI_F32, false>(a, st, tmA, tmW, tmC);
@@ -443,6 +424,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   }
   if (bn == 256) {
     switch (a.epi) {
+      case T2W_EPI_F32: return launch_impl<256, T2W_EPI_F32, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_BF16: return launch_impl<256, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_GELU: return launch_impl<256, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_QKV: return launch_impl<256, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
@@ -453,7 +435,6 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
     case T2W_EPI_F32: return launch_impl<128, T2W_EPI_F32, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_BF16: return launch_impl<128, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_GELU: return launch_impl<128, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
-    case T2W_EPI_RESID: return launch_impl<128, T2W_EPI_RESID, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_QKV: return launch_impl<128, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
     default: return T2W_ERR_INVALID;
   }

@@ -11,6 +11,24 @@ namespace t2w {
 // Thread-local last CUDA error for t2w_last_cuda_error().
 void set_cuda_error(cudaError_t e);
 int num_sms();
+// Whether kernels are launched with programmatic dependent launch (default on; T2W_PDL=0 turns it off).
+bool pdl_enabled();
+
+// Launch `kernel` on `st`, with programmatic stream serialization when enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // TMA tensor map of a row-major 2D bf16 / fp8 matrix [rows, cols] with row pitch `pitch_bytes`, box
 // [box_rows, box_cols] (box_cols * elem_bytes == 128: one 128-byte swizzle span), 128-byte swizzle, zero OOB fill.
@@ -26,9 +44,6 @@ struct GemmArgs {
   int epi = 0;
   void* out = nullptr;
   int ldo = 0;
-  float* resid = nullptr;
-  int ldr = 0;
-  const float* gate = nullptr;
   const float* qn_w = nullptr;
   const float* qn_b = nullptr;
   const float* kn_w = nullptr;
@@ -46,8 +61,8 @@ struct WeightMaps {
   bool has80 = false, has128 = false, has256 = false;
 };
 bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot);
-// Enqueue C = A W^T (+ epilogue).  tmA / W maps / tmC may be prebuilt (nullptr: encoded here; tmC is the output map,
-// or the residual map for T2W_EPI_RESID, with 128-row boxes of 128 bytes).  Returns a T2W status.
+// Enqueue C = A W^T (+ epilogue).  tmA / W maps / tmC may be prebuilt (nullptr: encoded here; tmC is the output map
+// with 128-row boxes of 128 bytes).  Returns a T2W status.
 int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA = nullptr, const WeightMaps* wm = nullptr,
                 const CUtensorMap* tmC = nullptr);
 
@@ -72,6 +87,9 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm = null
 // Row kernels.
 int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scale1, float eps, int rows, int C,
                   __nv_bfloat16* out, int ldo, const uint8_t* pad, cudaStream_t st);
+// h += g * y (fp32, in place; skipped when y == nullptr), then out = bf16(LN(h) * scale1 + shift), pad rows zero.
+int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
+                      int rows, int C, __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st);
 int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C,
                    __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st);
 int launch_pack(const float* x0, const float* mu, const float* cond, const float* spk, const int* tok_row,

@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int
                                                 const float* __restrict__ scale1, float eps, int rows,
                                                 __nv_bfloat16* __restrict__ out, int ldo,
                                                 const uint8_t* __restrict__ pad) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   constexpr int C = 128 * V;
@@ -64,10 +66,61 @@ __global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int
   }
 }
 
+// h += g * y (the gated residual of the preceding GEMM's bf16 output y, fp32, stored back), then out = LN(h) * scale1 +
+// shift (dit_kernels.py:35-60's add_ln_mod, with the residual kept in fp32).  y == nullptr: plain LN + modulation.
+template <int V>
+__global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const __nv_bfloat16* __restrict__ y,
+                                                    const float* __restrict__ g, const float* __restrict__ shift,
+                                                    const float* __restrict__ scale1, float eps, int rows,
+                                                    __nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ pad) {
+  pdl_wait();
+  pdl_launch();
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int C = 128 * V;
+  float4 x[V];
+  float4* hr = reinterpret_cast<float4*>(h + (size_t)row * C);
+#pragma unroll
+  for (int i = 0; i < V; ++i) x[i] = hr[32 * i + lane];
+  if (y) {
+    const uint2* yr = reinterpret_cast<const uint2*>(y + (size_t)row * C);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const uint2 u = yr[32 * i + lane];
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 32 * i + lane);
+      x[i].x = fmaf(gg.x, a.x, x[i].x);
+      x[i].y = fmaf(gg.y, a.y, x[i].y);
+      x[i].z = fmaf(gg.z, c.x, x[i].z);
+      x[i].w = fmaf(gg.w, c.y, x[i].w);
+      hr[32 * i + lane] = x[i];
+    }
+  }
+  __nv_bfloat16* o = out + (size_t)row * C;
+  if (pad && pad[row]) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) store_bf16x4(o + 4 * (32 * i + lane), 0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  float mean, rstd;
+  row_stats<V>(x, C, eps, mean, rstd);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = 4 * (32 * i + lane);
+    const float4 sc = __ldg(reinterpret_cast<const float4*>(scale1 + c));
+    const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + c));
+    store_bf16x4(o + c, fmaf((x[i].x - mean) * rstd, sc.x, sh.x), fmaf((x[i].y - mean) * rstd, sc.y, sh.y),
+                 fmaf((x[i].z - mean) * rstd, sc.z, sh.z), fmaf((x[i].w - mean) * rstd, sc.w, sh.w));
+  }
+}
+
 template <int V>
 __global__ void __launch_bounds__(256) k_ln_mish(const __nv_bfloat16* __restrict__ xin, const float* __restrict__ w,
                                                  const float* __restrict__ b, float eps, int rows,
                                                  __nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ pad) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   constexpr int C = 128 * V;
@@ -104,6 +157,8 @@ __global__ void k_pack(const float* __restrict__ x0, const float* __restrict__ m
                        const float* __restrict__ spk, const int* __restrict__ tok_row, const int* __restrict__ tok_stream,
                        int n_tok, int mel, int half_rows, __nv_bfloat16* __restrict__ hx, int ld_hx,
                        float* __restrict__ x) {
+  pdl_wait();
+  pdl_launch();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)n_tok * mel) return;
   const int i = (int)(idx / mel), c = (int)(idx - (long long)i * mel);
@@ -127,6 +182,8 @@ __global__ void k_pack(const float* __restrict__ x0, const float* __restrict__ m
 __global__ void k_euler(float* __restrict__ x, const float* __restrict__ dphi, int ld_dphi,
                         const int* __restrict__ tok_row, int n_tok, int mel, int half_rows, float dt, float w,
                         __nv_bfloat16* __restrict__ hx, int ld_hx, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)n_tok * mel) return;
   const int i = (int)(idx / mel), c = (int)(idx - (long long)i * mel);
@@ -143,11 +200,15 @@ __global__ void k_euler(float* __restrict__ x, const float* __restrict__ dphi, i
 }
 
 __global__ void k_f32_to_bf16(const float* __restrict__ s, __nv_bfloat16* __restrict__ d, long long n) {
+  pdl_wait();
+  pdl_launch();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) d[i] = __float2bfloat16_rn(s[i]);
 }
 
 __global__ void k_conv_weight(const float* __restrict__ s, __nv_bfloat16* __restrict__ d, int cout, int cin, int k) {
+  pdl_wait();
+  pdl_launch();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // over dst [cout, k * cin]
   if (i >= (long long)cout * cin * k) return;
   const int o = (int)(i / ((long long)k * cin));
@@ -161,6 +222,8 @@ __global__ void k_conv_weight(const float* __restrict__ s, __nv_bfloat16* __rest
 __global__ void k_temb(const float* __restrict__ ts, const float* __restrict__ freqs, int freq_dim, float t_scale,
                        const float* __restrict__ w1, const float* __restrict__ b1, const float* __restrict__ w2,
                        const float* __restrict__ b2, int H, float* __restrict__ silu_temb) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ float sm[];
   float* emb = sm;             // [freq_dim]
   float* hid = sm + freq_dim;  // [H]
@@ -193,6 +256,8 @@ template <int MAXS>
 __global__ void k_adaln(const float* __restrict__ W, const float* __restrict__ b, int R, int H, int steps,
                         const float* __restrict__ silu_temb, float* __restrict__ out, long long step_stride,
                         int chunk_period) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ float st[];  // [steps, H]
   for (int i = threadIdx.x; i < steps * H; i += blockDim.x) st[i] = silu_temb[i];
   __syncthreads();
@@ -221,8 +286,14 @@ __global__ void k_adaln(const float* __restrict__ W, const float* __restrict__ b
   }
 }
 
+thread_local cudaError_t t_launch_err = cudaSuccess;
+void check_err(cudaError_t e) {
+  if (e != cudaSuccess) t_launch_err = e;
+}
+// Status of the launches since the last check (a launch error, else any pending CUDA error).
 int check_launch() {
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = t_launch_err != cudaSuccess ? t_launch_err : cudaGetLastError();
+  t_launch_err = cudaSuccess;
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -240,11 +311,27 @@ int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scal
   if (ldh % 4 || ldo % 4) return T2W_ERR_INVALID;
   const unsigned g = blocks_for(rows, kRowsPerBlock);
   switch (C) {
-    case 128: k_ln_mod<1><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
-    case 256: k_ln_mod<2><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
-    case 512: k_ln_mod<4><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
-    case 768: k_ln_mod<6><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
-    case 1024: k_ln_mod<8><<<g, 256, 0, st>>>(h, ldh, shift, scale1, eps, rows, out, ldo, pad); break;
+    case 128: check_err(launch_k(k_ln_mod<1>, dim3(g), dim3(256), 0, st, h, ldh, shift, scale1, eps, rows, out, ldo, pad)); break;
+    case 256: check_err(launch_k(k_ln_mod<2>, dim3(g), dim3(256), 0, st, h, ldh, shift, scale1, eps, rows, out, ldo, pad)); break;
+    case 512: check_err(launch_k(k_ln_mod<4>, dim3(g), dim3(256), 0, st, h, ldh, shift, scale1, eps, rows, out, ldo, pad)); break;
+    case 768: check_err(launch_k(k_ln_mod<6>, dim3(g), dim3(256), 0, st, h, ldh, shift, scale1, eps, rows, out, ldo, pad)); break;
+    case 1024: check_err(launch_k(k_ln_mod<8>, dim3(g), dim3(256), 0, st, h, ldh, shift, scale1, eps, rows, out, ldo, pad)); break;
+    default: return T2W_ERR_INVALID;
+  }
+  return check_launch();
+}
+
+int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
+                      int rows, int C, __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st) {
+  if (rows <= 0) return T2W_OK;
+  if (y && !g) return T2W_ERR_INVALID;
+  const unsigned gr = blocks_for(rows, kRowsPerBlock);
+  switch (C) {
+    case 128: check_err(launch_k(k_add_ln_mod<1>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
+    case 256: check_err(launch_k(k_add_ln_mod<2>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
+    case 512: check_err(launch_k(k_add_ln_mod<4>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
+    case 768: check_err(launch_k(k_add_ln_mod<6>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
+    case 1024: check_err(launch_k(k_add_ln_mod<8>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
     default: return T2W_ERR_INVALID;
   }
   return check_launch();
@@ -255,11 +342,11 @@ int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float
   if (rows <= 0) return T2W_OK;
   const unsigned g = blocks_for(rows, kRowsPerBlock);
   switch (C) {
-    case 128: k_ln_mish<1><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
-    case 256: k_ln_mish<2><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
-    case 512: k_ln_mish<4><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
-    case 768: k_ln_mish<6><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
-    case 1024: k_ln_mish<8><<<g, 256, 0, st>>>(x, w, b, eps, rows, out, pad); break;
+    case 128: check_err(launch_k(k_ln_mish<1>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
+    case 256: check_err(launch_k(k_ln_mish<2>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
+    case 512: check_err(launch_k(k_ln_mish<4>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
+    case 768: check_err(launch_k(k_ln_mish<6>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
+    case 1024: check_err(launch_k(k_ln_mish<8>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
     default: return T2W_ERR_INVALID;
   }
   return check_launch();
@@ -270,7 +357,8 @@ int launch_pack(const float* x0, const float* mu, const float* cond, const float
                 cudaStream_t st) {
   const long long n = (long long)n_tok * mel;
   if (n <= 0) return T2W_OK;
-  k_pack<<<blocks_for(n, 256), 256, 0, st>>>(x0, mu, cond, spk, tok_row, tok_stream, n_tok, mel, half_rows, hx, ld_hx, x);
+  check_err(launch_k(k_pack, dim3(blocks_for(n, 256)), dim3(256), 0, st, x0, mu, cond, spk, tok_row, tok_stream, n_tok, mel,
+                     half_rows, hx, ld_hx, x));
   return check_launch();
 }
 
@@ -278,19 +366,20 @@ int launch_euler(float* x, const float* dphi, int ld_dphi, const int* tok_row, i
                  float dt, float w, __nv_bfloat16* hx, int ld_hx, float* out, cudaStream_t st) {
   const long long n = (long long)n_tok * mel;
   if (n <= 0) return T2W_OK;
-  k_euler<<<blocks_for(n, 256), 256, 0, st>>>(x, dphi, ld_dphi, tok_row, n_tok, mel, half_rows, dt, w, hx, ld_hx, out);
+  check_err(launch_k(k_euler, dim3(blocks_for(n, 256)), dim3(256), 0, st, x, dphi, ld_dphi, tok_row, n_tok, mel, half_rows,
+                     dt, w, hx, ld_hx, out));
   return check_launch();
 }
 
 int launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, long long n, cudaStream_t st) {
   if (n <= 0) return T2W_OK;
-  k_f32_to_bf16<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, n);
+  check_err(launch_k(k_f32_to_bf16, dim3(blocks_for(n, 256)), dim3(256), 0, st, src, dst, n));
   return check_launch();
 }
 
 int launch_conv_weight(const float* src, __nv_bfloat16* dst, int cout, int cin, int k, cudaStream_t st) {
   const long long n = (long long)cout * cin * k;
-  k_conv_weight<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, cout, cin, k);
+  check_err(launch_k(k_conv_weight, dim3(blocks_for(n, 256)), dim3(256), 0, st, src, dst, cout, cin, k));
   return check_launch();
 }
 
@@ -300,8 +389,8 @@ int launch_temb_mods(const float* ts, int steps, const float* freqs, int freq_di
                      float* mods, float* final_mods, cudaStream_t st) {
   constexpr int MAXS = 16;
   if (steps > MAXS || H % 128) return T2W_ERR_UNSUPPORTED;
-  k_temb<<<steps, 512, (freq_dim + H) * sizeof(float), st>>>(ts, freqs, freq_dim, t_scale, fc1_w, fc1_b, fc2_w, fc2_b,
-                                                               H, silu_temb);
+  check_err(launch_k(k_temb, dim3(steps), dim3(512), (freq_dim + H) * sizeof(float), st, ts, freqs, freq_dim, t_scale,
+                     fc1_w, fc1_b, fc2_w, fc2_b, H, silu_temb));
   int rc = check_launch();
   if (rc) return rc;
   const size_t sm = (size_t)steps * H * sizeof(float);
@@ -316,12 +405,12 @@ int launch_temb_mods(const float* ts, int steps, const float* freqs, int freq_di
   for (int b = 0; b < depth; ++b) {
     const int R = 9 * H;
     // mods layout [steps, depth, 9, H]: block b of step s at (s * depth + b) * 9H
-    k_adaln<MAXS><<<blocks_for(R, warps), 32 * warps, sm, st>>>(ada_w[b], ada_b[b], R, H, steps, silu_temb,
-                                                                 mods + (size_t)b * R, (long long)depth * R, 3);
+    check_err(launch_k(k_adaln<MAXS>, dim3(blocks_for(R, warps)), dim3(32 * warps), sm, st, ada_w[b], ada_b[b], R, H,
+                       steps, silu_temb, mods + (size_t)b * R, (long long)depth * R, 3));
     if ((rc = check_launch())) return rc;
   }
-  k_adaln<MAXS><<<blocks_for(2 * H, warps), 32 * warps, sm, st>>>(fin_w, fin_b, 2 * H, H, steps, silu_temb, final_mods,
-                                                                   2LL * H, 2);
+  check_err(launch_k(k_adaln<MAXS>, dim3(blocks_for(2 * H, warps)), dim3(32 * warps), sm, st, fin_w, fin_b, 2 * H, H, steps,
+                     silu_temb, final_mods, 2LL * H, 2));
   return check_launch();
 }
 

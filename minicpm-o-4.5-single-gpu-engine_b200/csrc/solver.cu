@@ -15,6 +15,7 @@
 // rows in front of each segment are the causal convolutions' left padding (the reference's empty conv cache at a
 // prompt setup), so a conv tap is a plain row shift and the im2col matrix never exists.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -37,6 +38,15 @@ int num_sms() {
     if (n <= 0) n = 148;
   }
   return n;
+}
+
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("T2W_PDL");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -111,7 +121,7 @@ struct Plan {
 };
 
 struct WsLayout {
-  size_t hx, h, a, qkv, o, c1, f, dphi, x, pad, tok_row, tok_stream, work, total;
+  size_t hx, h, a, qkv, o, y, c1, f, dphi, x, pad, tok_row, tok_stream, work, total;
 };
 
 uint64_t mix(uint64_t h, uint64_t v) {
@@ -203,6 +213,7 @@ WsLayout layout(const t2w_config& c, const Plan& pl) {
   w.a = take(R * H * 2);
   w.qkv = take(R * 3 * H * 2);
   w.o = take(R * H * 2);
+  w.y = take(R * H * 2);
   w.c1 = take(R * H * 2);
   w.f = take(R * (size_t)c.ffn * 2);
   w.dphi = take(R * (size_t)c.mel * 4);
@@ -251,6 +262,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   __nv_bfloat16* a = at<__nv_bfloat16>(ws, L.a);
   __nv_bfloat16* qkv = at<__nv_bfloat16>(ws, L.qkv);
   __nv_bfloat16* o = at<__nv_bfloat16>(ws, L.o);  // attention output, then the first conv's pre-norm output
+  __nv_bfloat16* y = at<__nv_bfloat16>(ws, L.y);  // proj / conv2 / fc2 output, added into h by the next norm
   __nv_bfloat16* c1 = at<__nv_bfloat16>(ws, L.c1);
   __nv_bfloat16* f = at<__nv_bfloat16>(ws, L.f);
   float* dphi = at<float>(ws, L.dphi);
@@ -262,8 +274,9 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
 
   // bf16 maps serve both as GEMM A operands and as bf16 output maps (128-row boxes of 64 columns); h is fp32 (boxes of
   // 32 columns) for the in_proj output and the gated residuals.
-  CUtensorMap tm_hx, tm_a, tm_o, tm_c1, tm_f, tm_qkv, tm_h;
+  CUtensorMap tm_hx, tm_a, tm_o, tm_y, tm_c1, tm_f, tm_qkv, tm_h;
   if (!make_tmap_2d(&tm_hx, hx, 2, R, 4 * mel, 4 * mel * 2, 128, 64) || !make_tmap_2d(&tm_a, a, 2, R, H, H * 2, 128, 64) ||
+      !make_tmap_2d(&tm_y, y, 2, R, H, H * 2, 128, 64) ||
       !make_tmap_2d(&tm_o, o, 2, R, H, H * 2, 128, 64) || !make_tmap_2d(&tm_c1, c1, 2, R, H, H * 2, 128, 64) ||
       !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&tm_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 128, 64) ||
       !make_tmap_2d(&tm_h, h, 4, R, H, H * 4, 128, 32))
@@ -300,6 +313,11 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     g.out = h; g.ldo = H;
     T2W_TRY(P.tick(T2W_KC_GEMM_IN, st));
     T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in, &tm_h));
+    // The gated residual of each branch (h += g * y) is applied by the norm that follows it (add_ln_mod), as the
+    // reference's fused_residual path does (dit_fast.py:306-344); the MLP's pending (g, y) is added by the next block's
+    // first norm or by the final layer's norm.
+    const float* pend_g = nullptr;
+    const __nv_bfloat16* pend_y = nullptr;
     for (int bi = 0; bi < c.depth; ++bi) {
       const BlockW& w = s->blk[bi];
       const float* M = s->mods + ((size_t)step * c.depth + bi) * 9 * H;
@@ -307,7 +325,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       const float *sh_c = M + 6 * H, *sc_c = M + 7 * H, *g_c = M + 8 * H;
       // attention branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_ln_mod(h, H, sh_a, sc_a, c.eps_block, R, H, a, H, nullptr, st));
+      T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, a, nullptr, st));
       GemmArgs q = GemmArgs();
       q.rows_a = R; q.M = R; q.err = s->err;
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
@@ -318,13 +336,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_attn(at_args, st, &tm_qkv));
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
-      pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_RESID;
-      pr.resid = h; pr.ldr = H; pr.gate = g_a;
+      pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_BF16; pr.out = y; pr.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
-      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &tm_h));
-      // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108)
+      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &tm_y));
+      // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_ln_mod(h, H, sh_c, sc_c, c.eps_block, R, H, a, H, pad, st));
+      T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, a, pad, st));
       GemmArgs k1 = GemmArgs();
       k1.rows_a = R; k1.M = R; k1.err = s->err;
       k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
@@ -336,12 +353,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       GemmArgs k2 = GemmArgs();
       k2.rows_a = R; k2.M = R; k2.err = s->err;
       k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
-      k2.epi = T2W_EPI_RESID; k2.resid = h; k2.ldr = H; k2.gate = g_c;
+      k2.epi = T2W_EPI_BF16; k2.out = y; k2.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
-      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &tm_h));
+      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &tm_y));
       // MLP branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_ln_mod(h, H, sh_m, sc_m, c.eps_block, R, H, a, H, nullptr, st));
+      T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, a, nullptr, st));
       GemmArgs f1 = GemmArgs();
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
@@ -349,14 +366,15 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1, &tm_f));
       GemmArgs f2 = GemmArgs();
       f2.rows_a = R; f2.M = R; f2.err = s->err;
-      f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_RESID;
-      f2.resid = h; f2.ldr = H; f2.gate = g_m;
+      f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_BF16; f2.out = y; f2.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_FC2, st));
-      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, &tm_h));
+      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, &tm_y));
+      pend_g = g_m;
+      pend_y = y;
     }
     const float* FM = s->final_mods + (size_t)step * 2 * H;
     T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-    T2W_TRY(launch_ln_mod(h, H, FM, FM + H, c.eps_final, R, H, a, H, nullptr, st));
+    T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, FM, FM + H, c.eps_final, R, H, a, nullptr, st));
     GemmArgs fin = GemmArgs();
     fin.rows_a = R; fin.M = R; fin.err = s->err;
     fin.A = a; fin.lda = H; fin.W = s->w_fin; fin.bias = s->b_fin; fin.N = mel; fin.K = H; fin.epi = T2W_EPI_F32;
@@ -706,6 +724,13 @@ int t2w_ln_mod(const float* h, int32_t ld_h, const float* shift, const float* sc
                        static_cast<cudaStream_t>(stream));
 }
 
+int t2w_add_ln_mod(float* h, const void* y, const float* g, const float* shift, const float* scale1, float eps, int32_t rows,
+                   int32_t C, void* out, const uint8_t* pad, void* stream) {
+  if (!h || !shift || !scale1 || !out) return T2W_ERR_INVALID;
+  return launch_add_ln_mod(h, static_cast<const __nv_bfloat16*>(y), g, shift, scale1, eps, rows, C,
+                           static_cast<__nv_bfloat16*>(out), pad, static_cast<cudaStream_t>(stream));
+}
+
 int t2w_ln_mish(const void* x, const float* w, const float* b, float eps, int32_t rows, int32_t C, void* out,
                 const uint8_t* pad, void* stream) {
   if (!x || !w || !b || !out) return T2W_ERR_INVALID;
@@ -714,8 +739,8 @@ int t2w_ln_mish(const void* x, const float* w, const float* b, float eps, int32_
 }
 
 int t2w_gemm(const void* A, int32_t lda, int32_t rows_a, const void* W, const float* bias, int32_t M, int32_t N,
-             int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo, float* resid,
-             int32_t ld_resid, const float* gate, const float* const* qk, float qk_eps, void* stream) {
+             int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo, const float* const* qk,
+             float qk_eps, void* stream) {
   GemmArgs g;
   g.A = A;
   g.lda = lda;
@@ -730,9 +755,6 @@ int t2w_gemm(const void* A, int32_t lda, int32_t rows_a, const void* W, const fl
   g.epi = epi;
   g.out = out;
   g.ldo = ldo;
-  g.resid = resid;
-  g.ldr = ld_resid;
-  g.gate = gate;
   if (qk) {
     g.qn_w = qk[0];
     g.qn_b = qk[1];

@@ -33,10 +33,10 @@ def _dev():
     torch.manual_seed(0)
 
 
-def gemm(A, W, bias, M, N, K, epi, out=None, ldo=0, taps=1, tap_row0=0, resid=None, gate=None, qk=None, qk_eps=1e-5):
+def gemm(A, W, bias, M, N, K, epi, out=None, ldo=0, taps=1, tap_row0=0, qk=None, qk_eps=1e-5):
     qk_arr = (ctypes.c_void_p * 4)(*[t.data_ptr() for t in qk]) if qk is not None else None
     L.call("t2w_gemm", P(A), A.shape[1], A.shape[0], P(W), P(bias), M, N, K, taps, tap_row0, L.EPI[epi], P(out), ldo,
-           P(resid), resid.shape[1] if resid is not None else 0, P(gate), qk_arr, ctypes.c_float(qk_eps), S())
+           qk_arr, ctypes.c_float(qk_eps), S())
     torch.cuda.synchronize()
 
 
@@ -58,6 +58,25 @@ def test_ln_mod(C, rows):
     assert (out[pad.bool()] == 0).all()
 
 
+@pytest.mark.parametrize("with_y", [True, False])
+def test_add_ln_mod(with_y):
+    rows, C = 333, 512
+    h = torch.randn(rows, C, device="cuda") * 2
+    y = rand_bf16(rows, C) if with_y else None
+    g = torch.randn(C, device="cuda")
+    sh, sc = torch.randn(C, device="cuda"), 1 + 0.3 * torch.randn(C, device="cuda")
+    pad = torch.zeros(rows, dtype=torch.uint8, device="cuda")
+    pad[5::40] = 1
+    out = torch.empty(rows, C, device="cuda", dtype=torch.bfloat16)
+    h_ref = h + g * y.float() if with_y else h.clone()
+    L.call("t2w_add_ln_mod", P(h), P(y), P(g), P(sh), P(sc), ctypes.c_float(1e-6), rows, C, P(out), P(pad), S())
+    torch.cuda.synchronize()
+    assert rel(h, h_ref) < 1e-6
+    ref = F.layer_norm(h_ref, (C,), eps=1e-6) * sc + sh
+    ref[pad.bool()] = 0
+    assert rel(out, ref) < 5e-3 and (out[pad.bool()] == 0).all()
+
+
 def test_ln_mish():
     rows, C = 257, 512
     x = rand_bf16(rows, C, scale=2.0)
@@ -72,7 +91,7 @@ def test_ln_mish():
     assert rel(out, ref) < 5e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (384, 512, 512), (256, 80, 512), (256, 384, 128)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (384, 512, 512), (256, 80, 512), (256, 384, 128), (1280, 2048, 192)])
 def test_gemm_f32(M, N, K):
     A, W, b = rand_bf16(M, K), rand_bf16(N, K, scale=0.05), torch.randn(N, device="cuda")
     out = torch.zeros(M, N, device="cuda")
@@ -81,8 +100,8 @@ def test_gemm_f32(M, N, K):
     assert rel(out, ref) < 1e-5, rel(out, ref)
 
 
-def test_gemm_bf16_and_gelu():
-    M, N, K = 384, 2048, 512
+@pytest.mark.parametrize("M,N,K", [(384, 2048, 512), (512, 384, 2048)])
+def test_gemm_bf16_and_gelu(M, N, K):
     A, W, b = rand_bf16(M, K), rand_bf16(N, K, scale=0.05), torch.randn(N, device="cuda") * 0.1
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     gemm(A, W, b, M, N, K, "bf16", out, N)
@@ -90,16 +109,6 @@ def test_gemm_bf16_and_gelu():
     assert rel(out, ref) < 5e-3
     gemm(A, W, b, M, N, K, "gelu", out, N)
     assert rel(out, F.gelu(ref, approximate="tanh")) < 5e-3
-
-
-def test_gemm_gated_residual():
-    M, N, K = 256, 512, 2048
-    A, W, b = rand_bf16(M, K), rand_bf16(N, K, scale=0.02), torch.randn(N, device="cuda") * 0.1
-    h = torch.randn(M, N, device="cuda")
-    g = torch.randn(N, device="cuda")
-    ref = h + g * (A.float() @ W.float().t() + b)
-    gemm(A, W, b, M, N, K, "resid", resid=h, gate=g)
-    assert rel(h, ref) < 1e-5
 
 
 @pytest.mark.parametrize("H", [512, 128])

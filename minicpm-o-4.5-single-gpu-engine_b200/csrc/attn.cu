@@ -59,6 +59,16 @@ T2W_DEV void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
 }
 T2W_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 64 columns, no wait (the caller waits once for several loads).
+T2W_DEV void tmem_ld64_nowait(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+T2W_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // O (+)= P V with P from TMEM (A operand, K-major: 2 bf16 keys per 32-bit column) and V from shared memory.
 T2W_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -129,7 +139,8 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
   if (warp == 0) {
     if (lane == 0) {
       ProdState ps[2];
-      unsigned long long idle_since = globaltimer();
+      long long idle_since = clock64();
+      uint32_t polls = 0;
       bool abort = false;
       while (!(ps[0].done && ps[1].done) && !abort) {
         bool progressed = false;
@@ -175,8 +186,8 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
           }
         }
         if (progressed) {
-          idle_since = globaltimer();
-        } else if (globaltimer() - idle_since > kWaitLimitNs) {
+          idle_since = clock64();
+        } else if ((++polls & 255u) == 0 && clock64() - idle_since > kWaitLimitCycles) {
           atomicExch(p.err, T2W_ERR_TIMEOUT);
           abort = true;
         }
@@ -187,7 +198,8 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
       constexpr uint32_t idesc_qk = idesc_bf16(kTile, kTile);
       constexpr uint32_t idesc_pv = idesc_bf16(kTile, kD, /*b_mn_major=*/true);
       MmaState ms[2];
-      unsigned long long idle_since = globaltimer();
+      long long idle_since = clock64();
+      uint32_t polls = 0;
       bool abort = false;
       while (!(ms[0].done && ms[1].done) && !abort) {
         bool progressed = false;
@@ -248,8 +260,8 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
           }
         }
         if (progressed) {
-          idle_since = globaltimer();
-        } else if (globaltimer() - idle_since > kWaitLimitNs) {
+          idle_since = clock64();
+        } else if ((++polls & 255u) == 0 && clock64() - idle_since > kWaitLimitCycles) {
           atomicExch(p.err, T2W_ERR_TIMEOUT);
           abort = true;
         }
@@ -278,53 +290,62 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
         // P_{j-1} V_{j-1} was issued before S_j, so it is complete too; waiting keeps o_done's phases in step
         if (j > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done, (tiles - 1) & 1, p.err)))) break;
         tc_fence_after();
-        // pass 1: the row max over valid keys (32 scores live at a time)
+        // all 128 scores of the row in one TMEM round trip
+        uint32_t sr[128];
+        tmem_ld64_nowait(sreg, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
+        tmem_ld64_nowait(sreg + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+        tmem_ld_wait();
         const int kb = j * kTile;
+        // rows whose 128 keys of this tile are all valid skip the mask (every prompt row before the prompt's last
+        // tile, every chunk row before the sequence's last tile)
+        const bool full = __all_sync(0xffffffffu, kb + kTile <= lim);
         float mx = -INFINITY;
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float sv[32];
-          tmem_ld32(sreg + 32 * c, sv);
+          for (int i = 0; i < kTile; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])));
+        } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (kb + 32 * c + i < lim) mx = fmaxf(mx, sv[i]);
+          for (int i = 0; i < kTile; ++i)
+            if (kb + i < lim) mx = fmaxf(mx, __uint_as_float(sr[i]));
         }
         mx *= p.scale_log2;
         // raise the reference max only when it grows by more than the threshold (p <= 2^8 fits bf16 comfortably)
         const bool raise = mx > m + kRescaleThreshold;
-        const float m_new = raise ? mx : m;
+        const float m_old = m;
+        m = raise ? mx : m;
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        // P = 2^(S c - m) as bf16 pairs, written back over the S columns (each pair replaces two consumed scores)
+        const float2 c2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_use, -m_use);
+        float2 rs2 = make_float2(0.f, 0.f);
+        uint32_t u[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float2 a = fma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), c2, nm2);
+          float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
+          if (!full) {
+            const int kk = kb + 2 * i;
+            e.x = (kk < lim) ? e.x : 0.f;
+            e.y = (kk + 1 < lim) ? e.y : 0.f;
+          }
+          rs2 = add2(rs2, e);
+          u[i] = pack_bf16x2(e.x, e.y);
+        }
+        const float rs = rs2.x + rs2.y;
+        tmem_st32(sreg, *reinterpret_cast<const uint32_t(*)[32]>(&u[0]));
+        tmem_st32(sreg + 32, *reinterpret_cast<const uint32_t(*)[32]>(&u[32]));
+        // O holds P_{<j} V_{<j} relative to the old reference max: rescale it (rare) before P_j V_j is issued
         if (j > 0 && __any_sync(0xffffffffu, raise)) {
-          const float f = raise ? exp2f(m - m_new) : 1.f;
+          const float f = raise ? exp2_approx(m_old - m) : 1.f;
           l *= f;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             float o[32];
             tmem_ld32(oreg + 32 * c, o);
-            uint32_t u[32];
+            uint32_t ou[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * f);
-            tmem_st32(oreg + 32 * c, u);
+            for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(o[i] * f);
+            tmem_st32(oreg + 32 * c, ou);
           }
-        }
-        m = m_new;
-        const float m_use = (m == -INFINITY) ? 0.f : m;
-        // pass 2: P = 2^(S c - m) as bf16 pairs, written back over the S columns it came from
-        float rs = 0.f;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float sv[64];
-          tmem_ld32p(sreg + 64 * c, sv);
-          tmem_ld32p(sreg + 64 * c + 32, sv + 32);
-          uint32_t u[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int kk = kb + 64 * c + 2 * i;
-            const float e0 = (kk < lim) ? exp2_approx(fmaf(sv[2 * i], p.scale_log2, -m_use)) : 0.f;
-            const float e1 = (kk + 1 < lim) ? exp2_approx(fmaf(sv[2 * i + 1], p.scale_log2, -m_use)) : 0.f;
-            rs += e0 + e1;
-            u[i] = pack_bf16x2(e0, e1);
-          }
-          tmem_st32(sreg + 32 * c, u);
         }
         l += rs;
         tmem_st_wait();

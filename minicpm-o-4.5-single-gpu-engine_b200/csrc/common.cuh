@@ -17,6 +17,9 @@ namespace t2w {
 // Every spin-wait in this library gives up after this long, records T2W_ERR_TIMEOUT in the caller's error word and
 // lets the kernel run to its end (TMEM is still released), so a lost arrival never hangs the GPU.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// The same limit in SM clock cycles, for polling loops that read the cheap SM-local clock instead of %globaltimer
+// (about 2 s at the B200's 1.965 GHz maximum clock; longer at lower clocks).
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 T2W_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -193,6 +196,26 @@ T2W_DEV float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// Packed fp32 pair arithmetic (sm_100): one instruction for two lanes of work.
+T2W_DEV float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+T2W_DEV float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // 2^x with the hardware approximation (ex2.approx, flush-to-zero); used for softmax weights rounded to bf16 afterwards.
 T2W_DEV float exp2_approx(float x) {
   float y;

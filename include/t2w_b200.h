@@ -190,6 +190,17 @@ T2W_API int t2w_gemm(const void* A_bf16, int32_t lda, int32_t rows_a, const void
 T2W_API int t2w_attn_varlen(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
                     const int32_t* seq_len, const int32_t* prompt_len, void* out_bf16, void* stream);
 
+/* t2w_attn_varlen for callers that cannot allocate device memory when they call in (a runtime that has reserved the
+ * whole GPU for its own pool, or a plugin running where the CUDA allocator must not be called).  No counterpart in the
+ * reference.  Same arguments, same results; the per-call work list (one entry per 128-query tile) lives in a fixed
+ * device array of this library instead of a per-call allocation: at most 8192 tiles per call (160 KB, held on every GPU
+ * that loads the library until exit); more returns T2W_ERR_INVALID.  The first call on a device looks up that array's
+ * device address, so make it before any stream capture.  All calls share the array: calls whose GPU work overlaps (two
+ * streams, two threads) race on it and must be serialised by the caller. */
+T2W_API int t2w_attn_varlen_noalloc(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq,
+                                    const int32_t* seq_row, const int32_t* seq_len, const int32_t* prompt_len,
+                                    void* out_bf16, void* stream);
+
 /* x[i] += dt ((1 + w) dphi[row[i]] - w dphi[row[i] + half_rows]) for the n_tok cond tokens (mel floats each); also
  * writes bf16(x) into hx[row] and hx[row + half_rows] (first mel columns of ld_hx) and, when out != NULL, out[i] = x. */
 T2W_API int t2w_euler_cfg(float* x, const float* dphi, int32_t ld_dphi, const int32_t* tok_row, int32_t n_tok, int32_t mel,

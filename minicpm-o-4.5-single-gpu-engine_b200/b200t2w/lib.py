@@ -73,6 +73,8 @@ _SIGS = {
     "t2w_ln_mish": ([_P, _P, _P, _F, _I, _I, _P, _P, _P], ctypes.c_int),
     "t2w_gemm": ([_P, _I, _I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, ctypes.POINTER(_P), _F, _P], ctypes.c_int),
     "t2w_attn_varlen": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P], ctypes.c_int),
+    "t2w_attn_varlen_noalloc": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P],
+                                ctypes.c_int),
     "t2w_euler_cfg": ([_P, _P, _I, _P, _I, _I, _I, _F, _F, _P, _I, _P, _P], ctypes.c_int),
 }
 

@@ -17,6 +17,9 @@
 //   O += P V (M 128, N 64, K 128, V MN-major from its TMA tile) accumulates in the pipeline's TMEM O region.
 // Tensor-core ops of one issuing thread run in issue order, so S_{j+1} never overwrites P_j before P_j V_j has read it.
 // No TMA multicast.
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -418,3 +421,74 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm) {
 }
 
 }  // namespace t2w
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Allocation-free attention entry point.
+//
+// Some callers cannot allocate device memory at the moment they call in: a serving runtime that reserves every byte
+// of the GPU up front for its own pool (a cudaMalloc there fails or breaks its memory accounting), or a plugin that is
+// invoked inside a host framework's region where calling the CUDA allocator is not permitted.  t2w_attn_varlen needs a
+// small device-side work list (one entry per 128-query tile), which it allocates per call; this variant keeps that
+// list in a fixed file-scope device array instead.  The array is reserved in every GPU that loads this library and is
+// held until the process exits.
+namespace {
+
+constexpr int kNoAllocMaxWork = 8192;  // query tiles (of 128 rows) per call: 8192 x 20 B = 160 KB per GPU
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) t2w::AttnWork g_noalloc_work[kNoAllocMaxWork];
+
+std::mutex g_noalloc_mu;
+t2w::AttnWork* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+}  // namespace
+
+extern "C" int t2w_attn_varlen_noalloc(const void* qkv, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
+                                       const int32_t* seq_len, const int32_t* prompt_len, void* out, void* stream) {
+  using namespace t2w;
+  if (!qkv || !out || !seq_row || !seq_len || !prompt_len || n_seq < 0 || heads <= 0) return T2W_ERR_INVALID;
+  std::vector<AttnWork> work;
+  for (int s = 0; s < n_seq; ++s) {
+    if (seq_len[s] <= 0 || prompt_len[s] < 0 || prompt_len[s] > seq_len[s] || seq_row[s] < 0 ||
+        seq_row[s] + seq_len[s] > rows)
+      return T2W_ERR_INVALID;
+    for (int q = 0; q < seq_len[s]; q += 128) work.push_back(AttnWork{seq_row[s] + q, seq_row[s], q, prompt_len[s], seq_len[s]});
+  }
+  if (work.size() > (size_t)kNoAllocMaxWork) return T2W_ERR_INVALID;  // beyond the fixed scratch array
+  if (work.empty()) return T2W_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    if (e != cudaSuccess) set_cuda_error(e);
+    return e != cudaSuccess ? T2W_ERR_CUDA : T2W_ERR_UNSUPPORTED;
+  }
+  AttnWork* scratch = nullptr;
+  {
+    // once per device, with that device current: the array's device address (its host-side name is only a stand-in)
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_noalloc_work);
+      if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return T2W_ERR_CUDA;
+      }
+      g_noalloc_ptr[dev] = static_cast<AttnWork*>(ptr);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  e = cudaMemcpyAsync(scratch, work.data(), work.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  AttnArgs a;
+  a.qkv = qkv;
+  a.rows = rows;
+  a.heads = heads;
+  a.work = scratch;
+  a.n_work = (int)work.size();
+  a.out = out;
+  a.scale_log2 = (float)(1.4426950408889634 / 8.0);
+  return launch_attn(a, st);
+}

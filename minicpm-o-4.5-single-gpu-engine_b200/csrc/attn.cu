@@ -7,16 +7,18 @@
 // same rows.
 //
 // Persistent CTAs (one per SM), two independent pipelines per CTA.  A work item is (128-query tile, head); pipeline p
-// of CTA c takes items p + 2 (c + k * grid).  Warps: 0 = TMA producer for both pipelines, 1 = TMEM allocator and MMA
-// issuer for both (each a polling loop over the two pipelines' barriers), 2-5 = softmax of pipeline 0, 6-9 = softmax of
-// pipeline 1 (one query row per thread = TMEM lane).  Per key tile j of 128 keys:
-//   S = Q K^T (M 128, N 128, K 64) into the pipeline's TMEM S region;
-//   the row's thread loads its 128 scores, updates the running max (log2 domain) and, when that max rises by more than
-//   8 (or on the first tile), rescales its O row in TMEM; it writes P = 2^(S c - m) as bf16 pairs back into the S
-//   columns (tcgen05.st), so the P V product reads A straight from TMEM;
-//   O += P V (M 128, N 64, K 128, V MN-major from its TMA tile) accumulates in the pipeline's TMEM O region.
-// Tensor-core ops of one issuing thread run in issue order, so S_{j+1} never overwrites P_j before P_j V_j has read it.
-// No TMA multicast.
+// of CTA c takes items p + 2 (c + k * grid).  Warps: 0 / 1 = TMA producers of pipelines 0 / 1, 2 / 3 = MMA issuers of
+// pipelines 0 / 1 (warp 2 also allocates TMEM), 4-7 = softmax of pipeline 0, 8-11 = softmax of pipeline 1 (one query
+// row per thread = TMEM lane).  Each control thread serves one pipeline with blocking waits in a fixed order.  Keys go
+// in tiles of 64; per tile t of a pipeline:
+//   S_t = Q K_t^T (M 128, N 64, K 64) into S buffer t % 2 of the pipeline's TMEM;
+//   the row's thread loads its 64 scores, keeps a running max (log2 domain) that it raises only when the tile's max
+//   exceeds it by more than 8 (then it rescales its O row in TMEM), and writes P = 2^(S c - m) as bf16 pairs back over
+//   the scores (tcgen05.st), so the P V product reads its A operand straight from TMEM;
+//   O += P_t V_t (M 128, N 64, K 64, V MN-major from its TMA tile) accumulates in the pipeline's TMEM O region.
+// With two S buffers the issuer computes S_{t+1} (and S_{t+2} once P_t V_t is issued) while the softmax works on tile
+// t, so the softmax warps run from tile to tile without waiting on the tensor core.  Tensor-core ops of one issuing
+// thread run in issue order, so S_{t+2} never overwrites P_t before P_t V_t has read it.  No TMA multicast.
 #include <mutex>
 #include <vector>
 
@@ -27,13 +29,20 @@ namespace t2w {
 
 namespace {
 
-constexpr int kTile = 128;
+constexpr int kQTile = 128;                    // queries per item
+constexpr int kKTile = 64;                     // keys per S tile
 constexpr int kD = 64;
-constexpr int kTileBytes = kTile * kD * 2;  // 16 KB: 128 rows x 128 bytes
-constexpr int kStages = 2;
-constexpr int kPipeBytes = kTileBytes * (1 + 2 * kStages);  // Q + K/V ring
-constexpr int kSmem = 2 * kPipeBytes + 1024 + 512;
-constexpr int kTmemCols = 512;  // per pipeline: S/P 128 columns at 256 p, O 64 columns at 256 p + 128
+constexpr int kQBytes = kQTile * kD * 2;       // 16 KB
+constexpr int kKVBytes = kKTile * kD * 2;      // 8 KB each for K and V
+constexpr int kStages = 4;                     // K/V ring per pipeline
+constexpr int kPipeBytes = kQBytes + kStages * 2 * kKVBytes;  // 80 KB
+constexpr int kMaxCtaItems = 512;  // items per CTA staged in shared memory (the grid grows to keep within it)
+struct ItemEntry {
+  AttnWork w;
+  int h, n_kt;
+};
+constexpr int kSmem = 2 * kPipeBytes + 1024 + 512 + kMaxCtaItems * (int)sizeof(ItemEntry);
+constexpr int kTmemCols = 512;  // pipeline p: S/P buffers at 192 p + {0, 64}, O at 192 p + 128
 constexpr float kRescaleThreshold = 8.f;
 
 struct DevArgs {
@@ -46,7 +55,7 @@ struct DevArgs {
 };
 
 struct PipeBars {
-  uint64_t q_full, q_free, kv_full[kStages], kv_empty[kStages], s_full, p_full, o_done, o_free;
+  uint64_t q_full, q_free, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2], o_done[2], o_free;
 };
 
 T2W_DEV void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
@@ -62,16 +71,6 @@ T2W_DEV void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
 }
 T2W_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 32 lanes x 64 columns, no wait (the caller waits once for several loads).
-T2W_DEV void tmem_ld64_nowait(uint32_t taddr, uint32_t (&r)[64]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr)
-      : "memory");
-}
-T2W_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 // O (+)= P V with P from TMEM (A operand, K-major: 2 bf16 keys per 32-bit column) and V from shared memory.
 T2W_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -83,32 +82,22 @@ T2W_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint3
 }
 
 T2W_DEV int item_tiles(const AttnWork& w) {
-  const int kmax = (w.q_pos + kTile > w.P) ? w.L : w.P;  // any chunk query in the tile sees every key
-  return (kmax + kTile - 1) / kTile;
+  const int kmax = (w.q_pos + kQTile > w.P) ? w.L : w.P;  // any chunk query in the tile sees every key
+  return (kmax + kKTile - 1) / kKTile;
 }
 
-// Per-pipeline progress of the producer and of the MMA issuer (each a polling state machine).
-struct ProdState {
-  int k = 0, item = -1, j = 0, n_kt = 0, stage = 0;
-  uint32_t phase = 0;
-  bool need_q = true, done = false;
-  AttnWork w{};
-  int h = 0;
-};
-struct MmaState {
-  int k = 0, item = -1, j = 0, n_kt = 0, stage = 0, tiles = 0;
-  uint32_t phase = 0;
-  int st = 0;  // 0 wait Q, 1 wait K/V, 2 wait P, 3 done
-  bool done = false;
-};
-
-__global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtensorMap tm, const DevArgs p) {
+__global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtensorMap tm_q,
+                                                 const __grid_constant__ CUtensorMap tm_kv, const DevArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   PipeBars* bars = reinterpret_cast<PipeBars*>(smem + 2 * kPipeBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+  ItemEntry* items = reinterpret_cast<ItemEntry*>(smem + 2 * kPipeBytes + 512);  // local item 2 k + q of pipeline q
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = p.heads * kD;
+  const int stride = 2 * gridDim.x;
+  // this CTA's items: global item q + 2 (blockIdx.x + k grid) is local item 2 k + q
+  const int n_local = (p.n_items > 2 * (int)blockIdx.x) ? ((p.n_items - 2 * (int)blockIdx.x + stride - 1) / stride) * 2 : 0;
 
   if (threadIdx.x == 0) {
     for (int q = 0; q < 2; ++q) {
@@ -119,210 +108,170 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
         mbar_init(&b.kv_full[s], 1);
         mbar_init(&b.kv_empty[s], 1);
       }
-      mbar_init(&b.s_full, 1);
-      mbar_init(&b.p_full, 4);
-      mbar_init(&b.o_done, 1);
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&b.s_full[s], 1);
+        mbar_init(&b.p_full[s], 4);
+        mbar_init(&b.o_done[s], 1);
+      }
       mbar_init(&b.o_free, 4);
     }
     fence_mbar_init();
-    tma_prefetch_desc(&tm);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_kv);
   }
   pdl_wait();
-  if (warp == 1) {
+  if (warp == 2) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
+  }
+  for (int i = threadIdx.x; i < n_local && i < kMaxCtaItems; i += blockDim.x) {
+    const int item = (i & 1) + 2 * blockIdx.x + (i >> 1) * stride;
+    if (item < p.n_items) {
+      ItemEntry e;
+      e.w = p.work[item / p.heads];
+      e.h = item % p.heads;
+      e.n_kt = item_tiles(e.w);
+      items[i] = e;
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   pdl_launch();
   const uint32_t tmem = *tmem_slot;
-  const int stride = 2 * gridDim.x;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      ProdState ps[2];
-      long long idle_since = clock64();
-      uint32_t polls = 0;
-      bool abort = false;
-      while (!(ps[0].done && ps[1].done) && !abort) {
-        bool progressed = false;
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          ProdState& s = ps[q];
-          if (s.done) continue;
-          PipeBars& b = bars[q];
-          uint8_t* base = smem + q * kPipeBytes;
-          if (s.need_q) {
-            const int item = q + 2 * blockIdx.x + s.k * stride;
-            if (item >= p.n_items) {
-              s.done = true;
-              progressed = true;
-              continue;
-            }
-            // the previous item's last S MMA has read the Q buffer
-            if (!mbar_test(smem_u32(&b.q_free), ((s.k & 1) ^ 1u))) continue;
-            s.item = item;
-            s.w = p.work[item / p.heads];
-            s.h = item % p.heads;
-            s.n_kt = item_tiles(s.w);
-            s.j = 0;
-            mbar_expect_tx(&b.q_full, kTileBytes);
-            tma_load_2d(base, &tm, s.h * kD, s.w.q_row, &b.q_full);
-            s.need_q = false;
-            progressed = true;
-          } else {
-            if (!mbar_test(smem_u32(&b.kv_empty[s.stage]), s.phase ^ 1u)) continue;
-            uint8_t* kv = base + kTileBytes + s.stage * 2 * kTileBytes;
-            mbar_expect_tx(&b.kv_full[s.stage], 2 * kTileBytes);
-            tma_load_2d(kv, &tm, H + s.h * kD, s.w.k_row + s.j * kTile, &b.kv_full[s.stage]);
-            tma_load_2d(kv + kTileBytes, &tm, 2 * H + s.h * kD, s.w.k_row + s.j * kTile, &b.kv_full[s.stage]);
-            if (++s.stage == kStages) {
-              s.stage = 0;
-              s.phase ^= 1u;
-            }
-            if (++s.j == s.n_kt) {
-              s.need_q = true;
-              ++s.k;
-            }
-            progressed = true;
-          }
-        }
-        if (progressed) {
-          idle_since = clock64();
-        } else if ((++polls & 255u) == 0 && clock64() - idle_since > kWaitLimitCycles) {
-          atomicExch(p.err, T2W_ERR_TIMEOUT);
-          abort = true;
+  if (warp < 2) {
+    if (lane == 0) {  // TMA producer of pipeline q
+      const int q = warp;
+      PipeBars& b = bars[q];
+      uint8_t* base = smem + q * kPipeBytes;
+      int t = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        if (q + 2 * (int)blockIdx.x + k * stride >= p.n_items) break;
+        const ItemEntry e = items[2 * k + q];
+        // the previous item's last S MMA has read the Q buffer
+        if (!(ok = mbar_wait(&b.q_free, (k & 1) ^ 1u, p.err))) break;
+        mbar_expect_tx(&b.q_full, kQBytes);
+        tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+        for (int j = 0; j < e.n_kt; ++j, ++t) {
+          const int st = t % kStages;
+          if (!(ok = mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err))) break;
+          uint8_t* kv = base + kQBytes + st * 2 * kKVBytes;
+          mbar_expect_tx(&b.kv_full[st], 2 * kKVBytes);
+          tma_load_2d(kv, &tm_kv, H + e.h * kD, e.w.k_row + j * kKTile, &b.kv_full[st]);
+          tma_load_2d(kv + kKVBytes, &tm_kv, 2 * H + e.h * kD, e.w.k_row + j * kKTile, &b.kv_full[st]);
         }
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_bf16(kTile, kTile);
-      constexpr uint32_t idesc_pv = idesc_bf16(kTile, kD, /*b_mn_major=*/true);
-      MmaState ms[2];
-      long long idle_since = clock64();
-      uint32_t polls = 0;
-      bool abort = false;
-      while (!(ms[0].done && ms[1].done) && !abort) {
-        bool progressed = false;
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          MmaState& s = ms[q];
-          if (s.done) continue;
-          PipeBars& b = bars[q];
-          uint8_t* base = smem + q * kPipeBytes;
-          const uint32_t sreg = tmem + 256 * q, oreg = sreg + 128;
-          if (s.st == 0) {  // wait for this item's Q
-            const int item = q + 2 * blockIdx.x + s.k * stride;
-            if (item >= p.n_items) {
-              s.done = true;
-              progressed = true;
-              continue;
-            }
-            if (!mbar_test(smem_u32(&b.q_full), s.k & 1)) continue;
-            s.item = item;
-            s.n_kt = item_tiles(p.work[item / p.heads]);
-            s.j = 0;
-            s.st = 1;
-            progressed = true;
-          } else if (s.st == 1) {  // S_j = Q K_j^T
-            if (!mbar_test(smem_u32(&b.kv_full[s.stage]), s.phase)) continue;
-            tc_fence_after();
-            const uint32_t q0 = smem_u32(base), k0 = smem_u32(base + kTileBytes + s.stage * 2 * kTileBytes);
-#pragma unroll
-            for (int k = 0; k < kD / 16; ++k)
-              umma_f16(sreg, sdesc_sw128(q0 + 32 * k, 1024, 16), sdesc_sw128(k0 + 32 * k, 1024, 16), idesc_qk, k ? 1u : 0u);
-            umma_commit(&b.s_full);
-            if (s.j == s.n_kt - 1) umma_commit(&b.q_free);
-            s.st = 2;
-            progressed = true;
-          } else {  // O += P_j V_j once the softmax has written P_j (and, for j = 0, read the previous item's O)
-            if (!mbar_test(smem_u32(&b.p_full), s.tiles & 1)) continue;
-            if (s.j == 0 && s.k > 0 && !mbar_test(smem_u32(&b.o_free), (s.k - 1) & 1)) continue;
-            tc_fence_after();
-            const uint32_t v0 = smem_u32(base + kTileBytes + s.stage * 2 * kTileBytes + kTileBytes);
-#pragma unroll
-            for (int k = 0; k < kTile / 16; ++k)
-              umma_f16_ts(oreg, sreg + 8 * k, sdesc_sw128(v0 + k * 16 * 128, 1024, 8192), idesc_pv,
-                          (s.j > 0 || k > 0) ? 1u : 0u);
-            umma_commit(&b.o_done);
-            umma_commit(&b.kv_empty[s.stage]);
-            ++s.tiles;
-            if (++s.stage == kStages) {
-              s.stage = 0;
-              s.phase ^= 1u;
-            }
-            if (++s.j == s.n_kt) {
-              ++s.k;
-              s.st = 0;
-            } else {
-              s.st = 1;
-            }
-            progressed = true;
-          }
-        }
-        if (progressed) {
-          idle_since = clock64();
-        } else if ((++polls & 255u) == 0 && clock64() - idle_since > kWaitLimitCycles) {
-          atomicExch(p.err, T2W_ERR_TIMEOUT);
-          abort = true;
-        }
+  } else if (warp < 4) {
+    if (lane == 0) {  // MMA issuer of pipeline q: S_0, S_1, then P_t V_t followed by S_{t+2}
+      const int q = warp - 2;
+      PipeBars& b = bars[q];
+      uint8_t* base = smem + q * kPipeBytes;
+      const uint32_t preg = tmem + 192 * q;
+      constexpr uint32_t idesc_qk = idesc_bf16(kQTile, kKTile);
+      constexpr uint32_t idesc_pv = idesc_bf16(kQTile, kD, /*b_mn_major=*/true);
+      int n_items_q = 0, total = 0;
+      for (int k = 0; q + 2 * (int)blockIdx.x + k * stride < p.n_items; ++k) {
+        ++n_items_q;
+        total += items[2 * k + q].n_kt;
       }
+      // S side cursor: item ks, tile js of it, global tile ts; P V side: item kp, tile jp, global tile tp
+      int ks = 0, js = 0, ts = 0, kp = 0, jp = 0;
+      bool ok = true;
+      auto issue_s = [&]() -> bool {
+        if (js == 0 && !mbar_wait(&b.q_full, ks & 1, p.err)) return false;
+        if (!mbar_wait(&b.kv_full[ts % kStages], (ts / kStages) & 1, p.err)) return false;
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(base), k0 = smem_u32(base + kQBytes + (ts % kStages) * 2 * kKVBytes);
+        const uint32_t sbuf = preg + 64 * (ts & 1);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          umma_f16(sbuf, sdesc_sw128(q0 + 32 * kk, 1024, 16), sdesc_sw128(k0 + 32 * kk, 1024, 16), idesc_qk, kk ? 1u : 0u);
+        umma_commit(&b.s_full[ts & 1]);
+        ++ts;
+        if (++js == items[2 * ks + q].n_kt) {
+          umma_commit(&b.q_free);
+          js = 0;
+          ++ks;
+        }
+        return true;
+      };
+      for (int i = 0; i < 2 && ts < total && ok; ++i) ok = issue_s();
+      for (int tp = 0; tp < total && ok; ++tp) {
+        if (!(ok = mbar_wait(&b.p_full[tp & 1], (tp >> 1) & 1, p.err))) break;
+        // an item's first P V overwrites O: the softmax has read the previous item's O
+        if (jp == 0 && kp > 0 && !(ok = mbar_wait(&b.o_free, (kp - 1) & 1, p.err))) break;
+        tc_fence_after();
+        const int st = tp % kStages;
+        const uint32_t v0 = smem_u32(base + kQBytes + st * 2 * kKVBytes + kKVBytes);
+        const uint32_t pbuf = preg + 64 * (tp & 1), oreg = preg + 128;
+#pragma unroll
+        for (int kk = 0; kk < kKTile / 16; ++kk)
+          umma_f16_ts(oreg, pbuf + 8 * kk, sdesc_sw128(v0 + kk * 16 * 128, 1024, 8192), idesc_pv,
+                      (jp > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&b.o_done[tp & 1]);
+        umma_commit(&b.kv_empty[st]);
+        if (++jp == items[2 * kp + q].n_kt) {
+          jp = 0;
+          ++kp;
+        }
+        if (ts < total) ok = issue_s();
+      }
+      (void)n_items_q;
     }
   } else {
-    const int q = (warp - 2) >> 2;  // pipeline
+    const int q = (warp - 4) >> 2;  // pipeline
     const int qw = warp & 3;        // TMEM lane quarter
     const int r = qw * 32 + lane;   // query row of the tile
     PipeBars& b = bars[q];
     const uint32_t lanes = (uint32_t)(qw * 32) << 16;
-    const uint32_t sreg = tmem + 256 * q + lanes, oreg = tmem + 256 * q + 128 + lanes;
-    int tiles = 0;
+    const uint32_t preg = tmem + 192 * q + lanes, oreg = preg + 128;
+    int t = 0;  // global tile counter of this pipeline
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int item = q + 2 * blockIdx.x + k * stride;
       if (item >= p.n_items) break;
-      const AttnWork w = p.work[item / p.heads];
-      const int h = item % p.heads;
-      const int n_kt = item_tiles(w);
+      const AttnWork w = items[2 * k + q].w;
+      const int h = items[2 * k + q].h;
+      const int n_kt = items[2 * k + q].n_kt;
       const int pos = w.q_pos + r;
       const int lim = pos < w.P ? w.P : (pos < w.L ? w.L : 0);
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < n_kt; ++j, ++tiles) {
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.s_full, tiles & 1, p.err)))) break;
-        // P_{j-1} V_{j-1} was issued before S_j, so it is complete too; waiting keeps o_done's phases in step
-        if (j > 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done, (tiles - 1) & 1, p.err)))) break;
+      for (int j = 0; j < n_kt; ++j, ++t) {
+        // warp-uniform: tcgen05.ld / st below are .sync.aligned
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.s_full[t & 1], (t >> 1) & 1, p.err)))) break;
         tc_fence_after();
-        // all 128 scores of the row in one TMEM round trip
-        uint32_t sr[128];
-        tmem_ld64_nowait(sreg, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
-        tmem_ld64_nowait(sreg + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+        const uint32_t sbuf = preg + 64 * (t & 1);
+        uint32_t sr[64];
+        tmem_ld64_nowait(sbuf, sr);
         tmem_ld_wait();
-        const int kb = j * kTile;
-        // rows whose 128 keys of this tile are all valid skip the mask (every prompt row before the prompt's last
-        // tile, every chunk row before the sequence's last tile)
-        const bool full = __all_sync(0xffffffffu, kb + kTile <= lim);
-        float mx = -INFINITY;
+        const int kb = j * kKTile;
+        // rows whose 64 keys of this tile are all valid skip the mask
+        const bool full = __all_sync(0xffffffffu, kb + kKTile <= lim);
+        // row max over valid keys: four independent partial maxima (short dependency chains)
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (full) {
 #pragma unroll
-          for (int i = 0; i < kTile; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])));
+          for (int i = 0; i < kKTile; ++i) mq[i & 3] = fmaxf(mq[i & 3], __uint_as_float(sr[i]));
         } else {
 #pragma unroll
-          for (int i = 0; i < kTile; ++i)
-            if (kb + i < lim) mx = fmaxf(mx, __uint_as_float(sr[i]));
+          for (int i = 0; i < kKTile; ++i)
+            if (kb + i < lim) mq[i & 3] = fmaxf(mq[i & 3], __uint_as_float(sr[i]));
         }
-        mx *= p.scale_log2;
+        float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
         // raise the reference max only when it grows by more than the threshold (p <= 2^8 fits bf16 comfortably)
         const bool raise = mx > m + kRescaleThreshold;
         const float m_old = m;
         m = raise ? mx : m;
         const float m_use = (m == -INFINITY) ? 0.f : m;
-        // P = 2^(S c - m) as bf16 pairs, written back over the S columns (each pair replaces two consumed scores)
+        // P = 2^(S c - m) as bf16 pairs, written back over the scores
         const float2 c2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_use, -m_use);
-        float2 rs2 = make_float2(0.f, 0.f);
-        uint32_t u[64];
+        float2 rsq[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        uint32_t u[32];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 32; ++i) {
           const float2 a = fma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), c2, nm2);
           float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
           if (!full) {
@@ -330,14 +279,16 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
             e.x = (kk < lim) ? e.x : 0.f;
             e.y = (kk + 1 < lim) ? e.y : 0.f;
           }
-          rs2 = add2(rs2, e);
+          rsq[i & 3] = add2(rsq[i & 3], e);
           u[i] = pack_bf16x2(e.x, e.y);
         }
-        const float rs = rs2.x + rs2.y;
-        tmem_st32(sreg, *reinterpret_cast<const uint32_t(*)[32]>(&u[0]));
-        tmem_st32(sreg + 32, *reinterpret_cast<const uint32_t(*)[32]>(&u[32]));
-        // O holds P_{<j} V_{<j} relative to the old reference max: rescale it (rare) before P_j V_j is issued
+        tmem_st32(sbuf, u);
+        // O holds P_{<j} V_{<j} relative to the old reference max: rescale it (rare) once P_{j-1} V_{j-1} is done.
+        // S_t's completion implies every tensor op issued before it, so the skipped waits of o_done never fall two
+        // phases behind.
         if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.err)))) break;
+          tc_fence_after();
           const float f = raise ? exp2_approx(m_old - m) : 1.f;
           l *= f;
 #pragma unroll
@@ -350,15 +301,16 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
             tmem_st32(oreg + 32 * c, ou);
           }
         }
-        l += rs;
+        const float2 rs2 = add2(add2(rsq[0], rsq[1]), add2(rsq[2], rsq[3]));
+        l += rs2.x + rs2.y;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&b.p_full);
+        if (lane == 0) mbar_arrive(&b.p_full[t & 1]);
       }
       if (!ok) break;
-      // the item's last P V
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done, (tiles - 1) & 1, p.err)))) break;
+      // the item's last P V (tile t - 1)
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.err)))) break;
       tc_fence_after();
       float o[kD];
       tmem_ld32p(oreg, o);
@@ -382,7 +334,7 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
     }
   }
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -390,7 +342,13 @@ __global__ void __launch_bounds__(320, 1) k_attn(const __grid_constant__ CUtenso
 
 }  // namespace
 
-int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm) {
+bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int rows, int heads) {
+  const uint64_t cols = 3ull * heads * kD;
+  return make_tmap_2d(tm_q, qkv, 2, (uint64_t)rows, cols, cols * 2, kQTile, kD) &&
+         make_tmap_2d(tm_kv, qkv, 2, (uint64_t)rows, cols, cols * 2, kKTile, kD);
+}
+
+int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
   if (!a.qkv || !a.work || !a.out || a.rows <= 0 || a.heads <= 0 || a.n_work < 0) return T2W_ERR_INVALID;
   if (a.n_work == 0) return T2W_OK;
   static bool attr_done = false;
@@ -402,17 +360,20 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm) {
     }
     attr_done = true;
   }
-  CUtensorMap m;
-  if (!tm) {
-    const uint64_t cols = 3ull * a.heads * kD;
-    if (!make_tmap_2d(&m, a.qkv, 2, (uint64_t)a.rows, cols, cols * 2, kTile, kD)) return T2W_ERR_INVALID;
-    tm = &m;
+  CUtensorMap mq, mkv;
+  if (!tm_q || !tm_kv) {
+    if (!make_attn_tmaps(&mq, &mkv, a.qkv, a.rows, a.heads)) return T2W_ERR_INVALID;
+    tm_q = &mq;
+    tm_kv = &mkv;
   }
   const int n_items = a.n_work * a.heads;
   DevArgs p{a.work, n_items, a.heads, reinterpret_cast<__nv_bfloat16*>(a.out), a.heads * kD, a.scale_log2, a.err};
   int grid = (n_items + 1) / 2;
   if (grid > num_sms()) grid = num_sms();
-  cudaError_t e = launch_k(k_attn, dim3(grid), dim3(320), kSmem, st, *tm, p);
+  // each CTA stages at most kMaxCtaItems items in shared memory
+  const int min_grid = (n_items + kMaxCtaItems - 1) / kMaxCtaItems;
+  if (grid < min_grid) grid = min_grid;
+  cudaError_t e = launch_k(k_attn, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;

@@ -82,7 +82,9 @@ struct AttnArgs {
   float scale_log2 = 0.f;
   int* err = nullptr;
 };
-int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm = nullptr);
+// Tensor maps of the attention kernel over a qkv buffer: 128-row query boxes and 64-row key / value boxes.
+bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int rows, int heads);
+int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q = nullptr, const CUtensorMap* tm_kv = nullptr);
 
 // Row kernels.
 int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scale1, float eps, int rows, int C,

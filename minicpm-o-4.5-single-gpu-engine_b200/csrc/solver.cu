@@ -281,6 +281,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&tm_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 128, 64) ||
       !make_tmap_2d(&tm_h, h, 4, R, H, H * 4, 128, 32))
     return T2W_ERR_INVALID;
+  CUtensorMap tm_att_q, tm_att_kv;
+  if (!make_attn_tmaps(&tm_att_q, &tm_att_kv, qkv, R, c.heads)) return T2W_ERR_INVALID;
 
   T2W_CUDA(cudaMemsetAsync(hx, 0, (size_t)R * 4 * mel * 2, st));
   // Attention writes only sequence rows; the pad rows of its output buffer must hold finite values (zero here, later
@@ -333,7 +335,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(P.tick(T2W_KC_GEMM_QKV, st));
       T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv, &tm_qkv));
       T2W_TRY(P.tick(T2W_KC_ATTN, st));
-      T2W_TRY(launch_attn(at_args, st, &tm_qkv));
+      T2W_TRY(launch_attn(at_args, st, &tm_att_q, &tm_att_kv));
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
       pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_BF16; pr.out = y; pr.ldo = H;

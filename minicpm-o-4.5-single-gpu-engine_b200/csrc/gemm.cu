@@ -1,14 +1,14 @@
 // tcgen05 / TMEM GEMM for the DiT projections: C[M, N] = sum_tap A[m + tap_row0 + tap, :] . W[n, tap-block]^T.
 //
-// One persistent CTA per SM, 6 warps:
+// One persistent CTA per SM, 10 warps:
 //   warp 0  : TMA producer (one elected lane), STAGES-deep ring of A [128 x 64] and W [BN x 64] bf16 tiles, 128B swizzle
 //   warp 1  : TMEM allocator + single-thread tcgen05.mma issuer (M = 128, N = BN, K = 16 per instruction)
-//   warps 2-9: epilogue in two halves of four warps; warp w reads TMEM lanes 32 (w % 4) .. +31, so each thread owns one
-//              output row, and half (w - 2) / 4 takes every other 128-byte output box of the tile
-// The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so a tile's epilogue overlaps the next tile's MMAs.
-// Each epilogue half stages its boxes (128 rows x 128 bytes, 128B swizzle) in its own shared-memory slot and writes them
-// with asynchronous TMA stores issued by the half's leader thread.  Two warps per SM sub-partition keep the TMEM loads
-// and the epilogue math of one box overlapped with the other's.
+//   warps 2-9: epilogue; warp w reads TMEM lanes 32 (w % 4) .. +31 (one output row per thread) and takes every other
+//              128-byte output box of the tile, half (w - 2) / 4 the even or the odd ones
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so a tile's epilogue overlaps the next tile's MMAs,
+// and each warp hands its accumulator columns back as soon as its last TMEM load of the tile has landed.  Every
+// epilogue warp stages its 32 rows x 128 bytes of a box (128B swizzle) in a shared-memory slot of its own and writes
+// them with an asynchronous TMA store from its lane 0, so the eight warps never wait for one another.
 // The causal convolutions use taps = 3, tap_row0 = -2: tap t of output row m reads activation row m - 2 + t, so the
 // im2col matrix is never materialised; rows before 0 come back zero from TMA.  No TMA multicast.
 #include <cstdio>
@@ -23,7 +23,9 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // bf16 elements per 128-byte swizzle row
 constexpr int kMaxSmem = 232448;
-constexpr int kBoxBytes = kBM * 128;  // one staged output box: 128 rows x 128 bytes
+constexpr int kStRows = 32;                // rows of one TMA store: one epilogue warp's TMEM lane quarter
+constexpr int kSlotBytes = kStRows * 128;  // one warp's staging slot: 32 rows x 128 bytes
+constexpr int kEpiWarps = 8;
 
 __host__ __device__ constexpr bool epi_f32_out(int epi) { return epi == T2W_EPI_F32; }
 
@@ -35,7 +37,7 @@ struct GemmCfg {
   static constexpr int OUT_ELEM = epi_f32_out(EPI) ? 4 : 2;
   static constexpr int BOX_COLS = 128 / OUT_ELEM;
   static constexpr int N_BOXES = TMA_OUT ? BN / BOX_COLS : 0;
-  static constexpr int OUT_BYTES = TMA_OUT ? 2 * kBoxBytes : 0;  // one staging slot per epilogue half
+  static constexpr int OUT_BYTES = TMA_OUT ? kEpiWarps * kSlotBytes : 0;  // one staging slot per epilogue warp
   static constexpr int FIXED = 1024 + 256;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - OUT_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
@@ -69,35 +71,9 @@ T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, i
 T2W_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 T2W_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 T2W_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// Named barrier of one epilogue half (ids 1 and 2, 128 threads each).
-T2W_DEV void epi_barrier(int half) { asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory"); }
 
-// 16-byte chunk `c` of row `r` inside one staged box (128B swizzle: chunk index XOR row % 8).
+// 16-byte chunk `c` of row `r` inside one staged slot (128B swizzle: chunk index XOR row % 8).
 T2W_DEV uint8_t* box_chunk(uint8_t* box, int r, int c) { return box + r * 128 + ((c ^ (r & 7)) << 4); }
-
-T2W_DEV void add_bias(float* v, const float* __restrict__ b, int n) {
-#pragma unroll
-  for (int j = 0; j < n / 4; ++j) {
-    const float4 q = __ldg(reinterpret_cast<const float4*>(b) + j);
-    v[4 * j + 0] += q.x;
-    v[4 * j + 1] += q.y;
-    v[4 * j + 2] += q.z;
-    v[4 * j + 3] += q.w;
-  }
-}
-
-// Write 64 bf16 values (one row of one bf16 box) into the staging box.
-T2W_DEV void stage_bf16_row(uint8_t* box, int r, const float* v) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 u;
-    u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
-    u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
-    u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
-    u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
-    *reinterpret_cast<uint4*>(box_chunk(box, r, c)) = u;
-  }
-}
 
 // Direct-store epilogue of one tile (BN = 80 final layer: no staging).
 template <int BN, int EPI>
@@ -108,7 +84,9 @@ T2W_DEV void epilogue_direct(const DevArgs& p, uint32_t taddr, int row, int n0) 
     float v[16];
     tmem_ld16(taddr + c, v);
     if (row >= p.M) continue;
-    add_bias(v, p.bias + n0 + c, 16);
+    const float* b = p.bias + n0 + c;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] += __ldg(b + j);
     if constexpr (EPI == T2W_EPI_F32) {
       float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + n0 + c);
 #pragma unroll
@@ -122,54 +100,50 @@ T2W_DEV void epilogue_direct(const DevArgs& p, uint32_t taddr, int row, int n0) 
   }
 }
 
-// Box b of a tile (BOX_COLS output columns of this thread's row r) into its staging box.
-template <int EPI, int BOX_COLS>
-T2W_DEV void epilogue_box(const DevArgs& p, uint32_t taddr, int r, int n0, int b, uint8_t* box) {
+T2W_DEV float2 u2f2(uint32_t a, uint32_t b) { return make_float2(__uint_as_float(a), __uint_as_float(b)); }
+T2W_DEV float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+
+// Epilogue math of box b for this thread's row: `raw` holds the box's accumulator columns (32 fp32 columns, or 64 for
+// bf16 outputs); on return it holds the 32 words staged for the box (fp32 values, or bf16 pairs).
+template <int EPI>
+T2W_DEV void epilogue_math(const DevArgs& p, int n0, int b, uint32_t (&raw)[64]) {
   if constexpr (EPI == T2W_EPI_F32) {
-    float v[32];
-    tmem_ld32(taddr + 32 * b, v);
-    add_bias(v, p.bias + n0 + 32 * b, 32);
+    const float* bias = p.bias + n0 + 32 * b;
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-      *reinterpret_cast<float4*>(box_chunk(box, r, c)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) + __ldg(bias + i));
   } else {
-    // bf16 outputs: a 64-column box (one head for the QKV epilogue)
     const int c0 = n0 + 64 * b;
-    float v[64];
-    tmem_ld32p(taddr + 64 * b, v);
-    tmem_ld32p(taddr + 64 * b + 32, v + 32);
-    add_bias(v, p.bias + c0, 64);
+    float2 v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = add2(u2f2(raw[2 * i], raw[2 * i + 1]), ldg2(p.bias + c0 + 2 * i));
     if constexpr (EPI == T2W_EPI_QKV) {
       const int qcols = p.N / 3;
-      if (c0 < 2 * qcols) {  // a q or k head: LayerNorm over its 64 values (affine), fp32
+      if (c0 < 2 * qcols) {  // a q or k head: LayerNorm over its 64 values (affine), fp32, two passes
         const float* nw = c0 < qcols ? p.qn_w : p.kn_w;
         const float* nb = c0 < qcols ? p.qn_b : p.kn_b;
-        float s = 0.f;
+        float2 s[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-        for (int i = 0; i < 64; ++i) s += v[i];
-        const float mean = s * (1.f / 64.f);
-        float ss = 0.f;
+        for (int i = 4; i < 32; ++i) s[i & 3] = add2(s[i & 3], v[i]);
+        const float2 s2 = add2(add2(s[0], s[1]), add2(s[2], s[3]));
+        const float mean = (s2.x + s2.y) * (1.f / 64.f);
+        const float2 nm = make_float2(-mean, -mean);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float d = v[i] - mean;
-          ss += d * d;
-        }
-        const float rstd = rsqrtf(ss * (1.f / 64.f) + p.qk_eps);
+        for (int i = 0; i < 32; ++i) v[i] = add2(v[i], nm);
+        float2 q[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int i = 0; i < 64; i += 4) {
-          const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw + i));
-          const float4 b4 = __ldg(reinterpret_cast<const float4*>(nb + i));
-          v[i + 0] = fmaf((v[i + 0] - mean) * rstd, w4.x, b4.x);
-          v[i + 1] = fmaf((v[i + 1] - mean) * rstd, w4.y, b4.y);
-          v[i + 2] = fmaf((v[i + 2] - mean) * rstd, w4.z, b4.z);
-          v[i + 3] = fmaf((v[i + 3] - mean) * rstd, w4.w, b4.w);
-        }
+        for (int i = 0; i < 32; ++i) q[i & 3] = fma2(v[i], v[i], q[i & 3]);
+        const float2 q2 = add2(add2(q[0], q[1]), add2(q[2], q[3]));
+        const float rstd = rsqrtf((q2.x + q2.y) * (1.f / 64.f) + p.qk_eps);
+        const float2 rs = make_float2(rstd, rstd), zero = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = fma2(fma2(v[i], rs, zero), ldg2(nw + 2 * i), ldg2(nb + 2 * i));
       }
     } else if constexpr (EPI == T2W_EPI_GELU) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] = gelu_tanh(v[i]);
+      for (int i = 0; i < 32; ++i) v[i] = make_float2(gelu_tanh(v[i].x), gelu_tanh(v[i].y));
     }
-    stage_bf16_row(box, r, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) raw[i] = pack_bf16x2(v[i].x, v[i].y);
   }
 }
 
@@ -271,44 +245,57 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int r = q * 32 + lane;  // tile row == TMEM lane
-    const bool leader = lane == 0 && q == 2;  // warps 2 and 6: store issuers of the two halves
-    uint8_t* slot = sOut + half * kBoxBytes;
-    // `ok` stays warp-uniform (tcgen05.ld is .sync.aligned); after a timed-out wait the warp skips all further waits
-    // and work but still reaches every named barrier, so no warp is left waiting at one.
-    bool ok = true;
+    uint8_t* slot = sOut + (warp - 2) * kSlotBytes;
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err));
-      if (ok) tc_fence_after();
+      // warp-uniform (tcgen05.ld is .sync.aligned); after a timed-out wait the warp stops
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) break;
+      tc_fence_after();
       if constexpr (!TMA_OUT) {
-        if (ok && half == 0) epilogue_direct<BN, EPI>(p, taddr, m0 + r, n0);
+        if (half == 0) epilogue_direct<BN, EPI>(p, taddr, m0 + q * 32 + lane, n0);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
       } else {
 #pragma unroll 1
         for (int b = half; b < C::N_BOXES; b += 2) {
-          // this half's previous store has finished reading its slot
-          if (leader) bulk_wait_read0();
-          epi_barrier(half);
-          if (ok) epilogue_box<EPI, C::BOX_COLS>(p, taddr, r, n0, b, slot);
+          uint32_t raw[64];
+          if constexpr (epi_f32_out(EPI)) {
+            float f[32];
+            tmem_ld32(taddr + 32 * b, f);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(f[i]);
+          } else {
+            tmem_ld64_nowait(taddr + 64 * b, raw);
+            tmem_ld_wait();
+          }
+          if (b + 2 >= C::N_BOXES) {  // this warp's last TMEM load of the accumulator has landed
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+          epilogue_math<EPI>(p, n0, b, raw);
+          // this warp's previous store has finished reading the slot
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(box_chunk(slot, lane, c)) =
+                make_uint4(raw[4 * c], raw[4 * c + 1], raw[4 * c + 2], raw[4 * c + 3]);
           fence_proxy_async_smem();
-          epi_barrier(half);
-          if (leader && ok) {
-            tma_store_2d(&tmC, slot, n0 + b * C::BOX_COLS, m0);
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, slot, n0 + b * C::BOX_COLS, m0 + q * kStRows);
             bulk_commit();
           }
         }
       }
-      if (ok) {  // every TMEM column this warp reads of the accumulator has been read
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
-      }
     }
     if constexpr (TMA_OUT) {
-      if (leader) bulk_wait0();
+      if (lane == 0) bulk_wait0();
     }
   }
   __syncthreads();
@@ -350,7 +337,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   if (!tmC) {
     if (TMA_OUT) {
       const bool f32 = epi_f32_out(EPI);
-      if (!make_tmap_2d(&mc, a.out, f32 ? 4 : 2, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)a.ldo * (f32 ? 4 : 2), kBM,
+      if (!make_tmap_2d(&mc, a.out, f32 ? 4 : 2, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)a.ldo * (f32 ? 4 : 2), kStRows,
                         C::BOX_COLS))
         return T2W_ERR_INVALID;
     } else {

@@ -272,14 +272,16 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   const int* tok_stream = at<int>(ws, L.tok_stream);
   const AttnWork* work = at<AttnWork>(ws, L.work);
 
-  // bf16 maps serve both as GEMM A operands and as bf16 output maps (128-row boxes of 64 columns); h is fp32 (boxes of
-  // 32 columns) for the in_proj output and the gated residuals.
-  CUtensorMap tm_hx, tm_a, tm_o, tm_y, tm_c1, tm_f, tm_qkv, tm_h;
+  // Operand maps (128-row boxes of 64 bf16 columns) and output maps of the GEMM epilogues (32-row boxes, one epilogue
+  // warp's rows: 64 bf16 or 32 fp32 columns).
+  CUtensorMap tm_hx, tm_a, tm_o, tm_c1, tm_f;
+  CUtensorMap st_o, st_y, st_c1, st_f, st_qkv, st_h;
   if (!make_tmap_2d(&tm_hx, hx, 2, R, 4 * mel, 4 * mel * 2, 128, 64) || !make_tmap_2d(&tm_a, a, 2, R, H, H * 2, 128, 64) ||
-      !make_tmap_2d(&tm_y, y, 2, R, H, H * 2, 128, 64) ||
       !make_tmap_2d(&tm_o, o, 2, R, H, H * 2, 128, 64) || !make_tmap_2d(&tm_c1, c1, 2, R, H, H * 2, 128, 64) ||
-      !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&tm_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 128, 64) ||
-      !make_tmap_2d(&tm_h, h, 4, R, H, H * 4, 128, 32))
+      !make_tmap_2d(&tm_f, f, 2, R, F, F * 2, 128, 64) || !make_tmap_2d(&st_o, o, 2, R, H, H * 2, 32, 64) ||
+      !make_tmap_2d(&st_y, y, 2, R, H, H * 2, 32, 64) || !make_tmap_2d(&st_c1, c1, 2, R, H, H * 2, 32, 64) ||
+      !make_tmap_2d(&st_f, f, 2, R, F, F * 2, 32, 64) || !make_tmap_2d(&st_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 32, 64) ||
+      !make_tmap_2d(&st_h, h, 4, R, H, H * 4, 32, 32))
     return T2W_ERR_INVALID;
   CUtensorMap tm_att_q, tm_att_kv;
   if (!make_attn_tmaps(&tm_att_q, &tm_att_kv, qkv, R, c.heads)) return T2W_ERR_INVALID;
@@ -314,7 +316,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     g.A = hx; g.lda = 4 * mel; g.W = s->w_in; g.bias = s->b_in; g.N = H; g.K = 4 * mel; g.epi = T2W_EPI_F32;
     g.out = h; g.ldo = H;
     T2W_TRY(P.tick(T2W_KC_GEMM_IN, st));
-    T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in, &tm_h));
+    T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in, &st_h));
     // The gated residual of each branch (h += g * y) is applied by the norm that follows it (add_ln_mod), as the
     // reference's fused_residual path does (dit_fast.py:306-344); the MLP's pending (g, y) is added by the next block's
     // first norm or by the final layer's norm.
@@ -333,14 +335,14 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
       q.qn_w = w.qn_w; q.qn_b = w.qn_b; q.kn_w = w.kn_w; q.kn_b = w.kn_b; q.qk_eps = c.eps_qk;
       T2W_TRY(P.tick(T2W_KC_GEMM_QKV, st));
-      T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv, &tm_qkv));
+      T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv, &st_qkv));
       T2W_TRY(P.tick(T2W_KC_ATTN, st));
       T2W_TRY(launch_attn(at_args, st, &tm_att_q, &tm_att_kv));
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
       pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_BF16; pr.out = y; pr.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
-      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &tm_y));
+      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_y));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, a, pad, st));
@@ -349,7 +351,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
       k1.epi = T2W_EPI_BF16; k1.out = o; k1.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
-      T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &tm_o));
+      T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &st_o));
       T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
       T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, c1, pad, st));
       GemmArgs k2 = GemmArgs();
@@ -357,7 +359,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
       k2.epi = T2W_EPI_BF16; k2.out = y; k2.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
-      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &tm_y));
+      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &st_y));
       // MLP branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, a, nullptr, st));
@@ -365,12 +367,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
       T2W_TRY(P.tick(T2W_KC_GEMM_FC1, st));
-      T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1, &tm_f));
+      T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1, &st_f));
       GemmArgs f2 = GemmArgs();
       f2.rows_a = R; f2.M = R; f2.err = s->err;
       f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_BF16; f2.out = y; f2.ldo = H;
       T2W_TRY(P.tick(T2W_KC_GEMM_FC2, st));
-      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, &tm_y));
+      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, &st_y));
       pend_g = g_m;
       pend_y = y;
     }

@@ -144,6 +144,51 @@ def test_gemm_causal_conv_taps():
     assert rel(out, conv) < 1e-5
 
 
+@pytest.mark.parametrize("M,N,K,taps,epi", [
+    (11264, 512, 320, 1, "f32"),    # the solve's in_proj at config 2: 176 tiles on 148 SMs (a partial second wave)
+    (11264, 512, 512, 3, "bf16"),   # causal conv: 24 k blocks per tile
+    (11264, 512, 2048, 1, "bf16"),  # fc2
+    (2560, 2048, 512, 1, "gelu"),   # 160 tiles
+    (6400, 384, 256, 1, "bf16"),    # 128-column tiles: 150 tiles
+    (11264, 1536, 512, 1, "qkv"),   # 528 tiles: 3-4 tiles per CTA through both TMEM accumulators
+])
+def test_gemm_full_size(M, N, K, taps, epi):
+    """The solve's GEMM shapes at config-2 size (11264 packed rows) and tile counts that are not a multiple of the SM
+    count, checked whole and per 128-row block (a wrong tile shows up as one bad block)."""
+    A = rand_bf16(M, K)
+    W, b = rand_bf16(N, taps * K, scale=0.03), torch.randn(N, device="cuda") * 0.1
+    f32 = epi == "f32"
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32 if f32 else torch.bfloat16)
+    qk = None
+    if epi == "qkv":
+        qk = [1 + 0.1 * torch.randn(64, device="cuda"), 0.1 * torch.randn(64, device="cuda"),
+              1 + 0.1 * torch.randn(64, device="cuda"), 0.1 * torch.randn(64, device="cuda")]
+    outs = []
+    for _ in range(2):  # two launches: bitwise identical (no atomics or order-dependent sums)
+        out.fill_(float("nan"))
+        gemm(A, W, b, M, N, K, epi, out, N, taps=taps, tap_row0=-2 if taps == 3 else 0, qk=qk)
+        outs.append(out.clone())
+    assert torch.equal(outs[0], outs[1])
+    if taps == 3:
+        Ap = torch.cat([torch.zeros(2, K, device="cuda"), A.float()])
+        ref = torch.cat([Ap[0:M], Ap[1:M + 1], Ap[2:M + 2]], dim=1) @ W.float().t() + b
+    else:
+        ref = A.float() @ W.float().t() + b
+    if epi == "gelu":
+        ref = F.gelu(ref, approximate="tanh")
+    elif epi == "qkv":
+        H = N // 3
+        q, k, v = ref.split(H, dim=1)
+        q = F.layer_norm(q.reshape(M, -1, 64), (64,), qk[0], qk[1], eps=1e-5).reshape(M, H)
+        k = F.layer_norm(k.reshape(M, -1, 64), (64,), qk[2], qk[3], eps=1e-5).reshape(M, H)
+        ref = torch.cat([q, k, v], dim=1)
+    assert torch.isfinite(out).all()
+    e = rel(out, ref)
+    assert e < (1e-5 if f32 else 5e-3), e
+    blk = (out.float() - ref).view(M // 128, 128, N).norm(dim=(1, 2)) / ref.view(M // 128, 128, N).norm(dim=(1, 2))
+    assert float(blk.max()) < (1e-4 if f32 else 1e-2), float(blk.max())
+
+
 def _attn_ref(qkv, seqs, heads):
     H = heads * 64
     out = torch.zeros(qkv.shape[0], H, device="cuda")

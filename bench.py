@@ -8,7 +8,10 @@ random-init reference-config weights, seeded synthetic inputs.  With ``--gpus N`
 an independent replica with its own 16 streams (weak scaling; streams never cross GPUs, so there is no collective on the
 data path, only a gloo barrier and a max over ranks of the device-timed region).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|target|c5|c3] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|target|c5|c3|c4] [--impl b200|reference]
+
+``--workload c4`` is benchmark config 4: config 2's shapes at 128 streams on the FP8 path (e4m3 block projections with
+power-of-two block scales; bf16 in_proj, attention and final layer).
 
 ``--impl reference`` times the reference's own algorithm on the host cores (the CPU oracle port of the reference
 solver, all threads), one stream of the workload per step, on rank 0 only.
@@ -34,7 +37,7 @@ for p in (ROOT, PKG):
 import torch  # noqa: E402
 
 from b200t2w.config import REFERENCE, DiTConfig  # noqa: E402
-from b200t2w.workload import C2, C3, C5, TARGET, Workload, make_streams, uniform_streams  # noqa: E402
+from b200t2w.workload import C2, C3, C4, C5, TARGET, Workload, make_streams, uniform_streams  # noqa: E402
 
 METRIC = "DiT mel frames/s per full CFG ODE solve"
 UNIT = "mel frames/s"
@@ -47,7 +50,7 @@ def args_():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
     return ap.parse_args()
@@ -58,7 +61,7 @@ def shard(name: str, rank: int, world: int) -> Workload:
     if name == "c5":
         n = C5.streams // world
         return Workload(f"{C5.name}[rank {rank}/{world}]", C5.seed, C5.lengths[rank * n:(rank + 1) * n])
-    base = {"c2": C2, "target": TARGET, "c3": C3}[name]
+    base = {"c2": C2, "target": TARGET, "c3": C3, "c4": C4}[name]
     if world == 1:
         return base
     return Workload(f"{base.name}[rank {rank}]", base.seed + 1000 * rank, base.lengths)
@@ -184,7 +187,8 @@ def main() -> None:
     wl = shard(a.workload, rank, world)
     streams = make_streams(wl, cfg.mel)
     layout = Layout(tuple(s["P"] for s in streams), tuple(s["T"] for s in streams))
-    solver = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), device=dev)
+    fp8 = a.workload == "c4"
+    solver = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), precision="fp8" if fp8 else "bf16", device=dev)
     bufs = solver.static_buffers(layout)
     host = {k: torch.cat([s[k].t() for s in streams]).contiguous().pin_memory() for k in ("x0", "mu", "cond")}
     host["spk"] = torch.stack([s["spk"] for s in streams]).contiguous().pin_memory()
@@ -254,6 +258,10 @@ def main() -> None:
     except OSError:
         pass
     peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
+    peak_src = "MEASURED_PEAKS.json bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "fallback"
+    if fp8:  # no measured e4m3 peak: twice the measured bf16 figure (the dense e4m3 / bf16 ratio of the part)
+        peak_tf *= 2
+        peak_src = "2 x " + peak_src + " (no measured e4m3 peak)"
     launches = sum(c for _, c in prof.values()) if prof else None
     gemm_ms = sum(ms for k, (ms, _) in prof.items() if k.startswith("gemm")) if prof else None
     roofline = None
@@ -265,8 +273,7 @@ def main() -> None:
         except (OSError, ValueError):
             pass
         roofline = {"bound": "tensor", "kernel": "k_gemm (all tcgen05 GEMM launches of one solve)", "achieved": achieved,
-                    "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                    "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "fallback",
+                    "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf, "peak_source": peak_src,
                     "traffic": traffic, "gemm_ms_per_solve": gemm_ms, "gemm_tflop_per_solve": gemm_flops / 1e12,
                     "solve_tflops": (gemm_flops + attn_flops) / (statistics.mean(times) / 1000) / 1e12,
                     "kernel_ms_per_solve": {k: round(ms, 4) for k, (ms, _) in prof.items()}}
@@ -282,11 +289,12 @@ def main() -> None:
         print(json.dumps({
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": max_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
+            "dtype": "e4m3 (block projections) + bf16" if fp8 else "bf16", "data": "synthetic",
             "config": {"workload": wl.name, "streams_per_gpu": wl.streams, "prompt_frames": layout.prompt[0],
                        "chunk_frames": layout.chunk[0], "chunk_frames_per_solve_per_gpu": chunk_frames,
                        "packed_frames_per_solve_per_gpu": 2 * wl.packed_frames, "mel": cfg.mel, "euler_steps": cfg.steps,
                        "cfg": True, "model": "reference-config DiT (H=512, depth 16, 8x64 heads, unverified), random init",
+                       "precision": "fp8" if fp8 else "bf16",
                        "l2": "flushed between timed solves (256 MiB write, untimed)",
                        "parallelism": f"replicas x{world} (streams sharded by request, no collectives)"},
             "latency_ms": lat, "processed_frames_per_s": value * 2 * wl.packed_frames / chunk_frames,

@@ -42,7 +42,8 @@ extern "C" {
 #define T2W_ERR_WORKSPACE (-6)   /* workspace too small */
 
 #define T2W_PREC_BF16 0 /* bf16 weights and activations, fp32 accumulate */
-#define T2W_PREC_FP8 1  /* e4m3 weights (per 1x128 block power-of-two fp32 scales) and per-token-scaled e4m3 activations */
+#define T2W_PREC_FP8 1  /* e4m3 weights (power-of-two scale per 1x128 block) and e4m3 activations (power-of-two scale per
+                         * row and 32-column block) in the block projections; bf16 in_proj, final layer, attention */
 
 #define T2W_FLAG_GRAPH 1u /* capture the whole solve in a CUDA graph per (layout, buffers) key and replay it */
 
@@ -174,6 +175,7 @@ T2W_API int t2w_ln_mish(const void* x_bf16, const float* w, const float* b, floa
 #define T2W_EPI_BF16 1 /* out bf16 = acc + bias */
 #define T2W_EPI_GELU 2 /* out bf16 = gelu_tanh(acc + bias) */
 #define T2W_EPI_QKV 4  /* out bf16 = [LN_q(q) | LN_k(k) | v] per 64-wide head (q/k affine norms) */
+#define T2W_EPI_GELU_FP8 8 /* t2w_gemm_e4m3 only: out e4m3 = gelu_tanh(acc + bias) with its scale atoms */
 
 /* C[M, N] = sum_tap A[m + tap_row0 + tap, :K] . W[n, tap*K : (tap+1)*K] then the epilogue.  A bf16 [rows_a, lda],
  * W bf16 [N, taps*K]; rows outside [0, rows_a) read as zero (causal-conv taps).  M % 128 == 0, K % 64 == 0,
@@ -200,6 +202,44 @@ T2W_API int t2w_attn_varlen(const void* qkv_bf16, int32_t rows, int32_t heads, i
 T2W_API int t2w_attn_varlen_noalloc(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq,
                                     const int32_t* seq_row, const int32_t* seq_len, const int32_t* prompt_len,
                                     void* out_bf16, void* stream);
+
+/* ---- FP8 (e4m3) path: values in e4m3 with one power-of-two (UE8M0) scale per row and 32-column block.
+ * The scales of a [rows, C] matrix are stored as "atoms": one 512-byte atom per (128-row tile, 128-column block),
+ * atom (r / 128) * (C / 128) + j / 4 holding row r's scale of block j at byte (r % 32) * 16 + (r % 128 / 32) * 4 + j % 4
+ * (the layout the tensor core's scale-factor copy reads).  A "row-shifted layout" d stores row r at position r + d;
+ * the causal conv's GEMM reads layouts d = 0, 1, 2, which the producing kernel writes together (n_layouts = 3,
+ * layout d at sf + d * layout_bytes).  The reference quantises its FP8 linears with per-output-row weight scales and
+ * per-token activation scales (engine/runtime/fp8.py:15-40); these entry points use per-block power-of-two scales,
+ * which the block-scaled MMA applies inside the K loop. */
+
+/* Bytes of one layout of scale atoms for a [rows, C] e4m3 matrix (C % 128 == 0). */
+T2W_API size_t t2w_e4m3_sf_bytes(int32_t rows, int32_t C);
+/* bf16 [rows, C] -> e4m3 [rows, C] + scale atoms (per 1 x 32 block; C = 128, 512, 1536 or 2048). */
+T2W_API int t2w_quant_e4m3(const void* x_bf16, int32_t rows, int32_t C, void* out_e4m3, uint8_t* sf, int32_t n_layouts,
+                           int64_t layout_bytes, void* stream);
+/* fp32 weight [N, Kt] -> e4m3 [N, Kt] + one power-of-two scale per 1 x 128 block, as atoms [Kt / 128][N / 128][512]
+ * (the weight layout t2w_gemm_e4m3 reads; N, Kt multiples of 128). */
+T2W_API int t2w_quant_weight_e4m3(const float* w, int32_t N, int32_t Kt, void* w_e4m3, uint8_t* sf, void* stream);
+/* t2w_add_ln_mod / t2w_ln_mish with e4m3 output and its scale atoms (n_layouts 1-3). */
+T2W_API int t2w_add_ln_mod_e4m3(float* h, const void* y_bf16, const float* g, const float* shift, const float* scale1,
+                                float eps, int32_t rows, int32_t C, void* out_e4m3, uint8_t* sf, int32_t n_layouts,
+                                int64_t layout_bytes, const uint8_t* pad, void* stream);
+T2W_API int t2w_ln_mish_e4m3(const void* x_bf16, const float* w, const float* b, float eps, int32_t rows, int32_t C,
+                             void* out_e4m3, uint8_t* sf, int32_t n_layouts, int64_t layout_bytes, const uint8_t* pad,
+                             void* stream);
+/* t2w_attn_varlen with e4m3 output [rows, heads * 64] and its scale atoms (layout 0). */
+T2W_API int t2w_attn_varlen_e4m3(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
+                                 const int32_t* seq_len, const int32_t* prompt_len, void* out_e4m3, uint8_t* sf,
+                                 void* stream);
+/* Block-scaled FP8 GEMM: C[M, N] = sum_tap dequant(A8)[m + tap_row0 + tap, :K] . dequant(W8)[n, tap*K : (tap+1)*K]^T
+ * then the epilogue (T2W_EPI_BF16, T2W_EPI_QKV: bf16 out [M, ldo]; T2W_EPI_GELU_FP8: e4m3 out + out_sf atoms).
+ * A8 e4m3 [rows_a, lda bytes] with scale atoms sfa in sfa_layouts row-shifted layouts (tap t reads layout
+ * -(tap_row0 + t)); W8 and sfw from t2w_quant_weight_e4m3.  M % 128 == 0, N % 256 == 0, K % 128 == 0; fp32
+ * accumulation in TMEM.  Replaces the reference's fp8_linear (engine/runtime/fp8.py:27-36). */
+T2W_API int t2w_gemm_e4m3(const void* A8, int32_t lda, int32_t rows_a, const uint8_t* sfa, int32_t sfa_layouts,
+                          int64_t sfa_layout_bytes, const void* W8, const uint8_t* sfw, const float* bias, int32_t M,
+                          int32_t N, int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo,
+                          uint8_t* out_sf, const float* const* qk, float qk_eps, void* stream);
 
 /* x[i] += dt ((1 + w) dphi[row[i]] - w dphi[row[i] + half_rows]) for the n_tok cond tokens (mel floats each); also
  * writes bf16(x) into hx[row] and hx[row + half_rows] (first mel columns of ld_hx) and, when out != NULL, out[i] = x. */

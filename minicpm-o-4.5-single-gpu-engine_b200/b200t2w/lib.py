@@ -17,7 +17,7 @@ STATUS = {-1: "invalid argument or shape", -2: "CUDA error", -3: "out of device 
           -5: "unsupported config or device", -6: "workspace too small"}
 PREC = {"bf16": 0, "fp8": 1}
 FLAG_GRAPH = 1
-EPI = {"f32": 0, "bf16": 1, "gelu": 2, "qkv": 4}
+EPI = {"f32": 0, "bf16": 1, "gelu": 2, "qkv": 4, "gelu_fp8": 8}
 KERNEL_CLASSES = ["pack", "gemm_in", "ln_mod", "gemm_qkv", "attn", "gemm_proj", "gemm_conv1", "ln_mish", "gemm_conv2",
                   "gemm_fc1", "gemm_fc2", "gemm_final", "euler"]
 W_GLOBAL = ["estimator.t_embedder.mlp.0.weight", "estimator.t_embedder.mlp.0.bias", "estimator.t_embedder.mlp.2.weight",
@@ -76,6 +76,15 @@ _SIGS = {
     "t2w_attn_varlen_noalloc": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P],
                                 ctypes.c_int),
     "t2w_euler_cfg": ([_P, _P, _I, _P, _I, _I, _I, _F, _F, _P, _I, _P, _P], ctypes.c_int),
+    "t2w_e4m3_sf_bytes": ([_I, _I], ctypes.c_size_t),
+    "t2w_quant_e4m3": ([_P, _I, _I, _P, _P, _I, ctypes.c_int64, _P], ctypes.c_int),
+    "t2w_quant_weight_e4m3": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
+    "t2w_add_ln_mod_e4m3": ([_P, _P, _P, _P, _P, _F, _I, _I, _P, _P, _I, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "t2w_ln_mish_e4m3": ([_P, _P, _P, _F, _I, _I, _P, _P, _I, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "t2w_attn_varlen_e4m3": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P, _P],
+                             ctypes.c_int),
+    "t2w_gemm_e4m3": ([_P, _I, _I, _P, _I, ctypes.c_int64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P,
+                       ctypes.POINTER(_P), _F, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -48,7 +48,8 @@ constexpr float kRescaleThreshold = 8.f;
 struct DevArgs {
   const AttnWork* work;
   int n_items, heads;
-  __nv_bfloat16* out;
+  void* out;        // bf16, or e4m3 with out_sf (the FP8 path's proj input)
+  uint8_t* out_sf;  // e4m3 output: UE8M0 scale atoms (one byte per row and 32-column block, sf_offset layout)
   int ldo;
   float scale_log2;
   int* err;
@@ -86,6 +87,7 @@ T2W_DEV int item_tiles(const AttnWork& w) {
   return (kmax + kKTile - 1) / kKTile;
 }
 
+template <bool E4M3>
 __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtensorMap tm_q,
                                                  const __grid_constant__ CUtensorMap tm_kv, const DevArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -320,15 +322,41 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       if (lane == 0) mbar_arrive(&b.o_free);
       if (lim > 0) {
         const float inv = 1.f / l;
-        __nv_bfloat16* dst = p.out + (size_t)(w.q_row + r) * p.ldo + h * kD;
+        const int row = w.q_row + r;
+        if constexpr (E4M3) {
+          // two 32-column blocks per head, each with its own power-of-two scale
+          uint8_t* dst = static_cast<uint8_t*>(p.out) + (size_t)row * p.ldo + h * kD;
+          uint32_t eb[2];
 #pragma unroll
-        for (int u = 0; u < kD / 8; ++u) {
-          uint4 v;
-          v.x = pack_bf16x2(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
-          v.y = pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
-          v.z = pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
-          v.w = pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
-          reinterpret_cast<uint4*>(dst)[u] = v;
+          for (int hb = 0; hb < 2; ++hb) {
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * hb + i]));
+            eb[hb] = ue8m0_for_amax(amax * inv);
+            const float f = inv * ue8m0_inv(eb[hb]);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float* q = o + 32 * hb + 16 * u;
+              uint4 v;
+              v.x = e4m3x4(q[0] * f, q[1] * f, q[2] * f, q[3] * f);
+              v.y = e4m3x4(q[4] * f, q[5] * f, q[6] * f, q[7] * f);
+              v.z = e4m3x4(q[8] * f, q[9] * f, q[10] * f, q[11] * f);
+              v.w = e4m3x4(q[12] * f, q[13] * f, q[14] * f, q[15] * f);
+              reinterpret_cast<uint4*>(dst)[2 * hb + u] = v;
+            }
+          }
+          *reinterpret_cast<uint16_t*>(p.out_sf + sf_offset(row, 2 * h, p.ldo)) = (uint16_t)(eb[0] | (eb[1] << 8));
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + h * kD;
+#pragma unroll
+          for (int u = 0; u < kD / 8; ++u) {
+            uint4 v;
+            v.x = pack_bf16x2(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
+            v.y = pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
+            v.z = pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
+            v.w = pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
+            reinterpret_cast<uint4*>(dst)[u] = v;
+          }
         }
       }
     }
@@ -348,12 +376,13 @@ bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int
          make_tmap_2d(tm_kv, qkv, 2, (uint64_t)rows, cols, cols * 2, kKTile, kD);
 }
 
-int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
-  if (!a.qkv || !a.work || !a.out || a.rows <= 0 || a.heads <= 0 || a.n_work < 0) return T2W_ERR_INVALID;
-  if (a.n_work == 0) return T2W_OK;
+namespace {
+
+template <bool E4M3>
+int launch_attn_impl(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_attn<E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
@@ -367,18 +396,27 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, con
     tm_kv = &mkv;
   }
   const int n_items = a.n_work * a.heads;
-  DevArgs p{a.work, n_items, a.heads, reinterpret_cast<__nv_bfloat16*>(a.out), a.heads * kD, a.scale_log2, a.err};
+  DevArgs p{a.work, n_items, a.heads, a.out, a.out_sf, a.heads * kD, a.scale_log2, a.err};
   int grid = (n_items + 1) / 2;
   if (grid > num_sms()) grid = num_sms();
   // each CTA stages at most kMaxCtaItems items in shared memory
   const int min_grid = (n_items + kMaxCtaItems - 1) / kMaxCtaItems;
   if (grid < min_grid) grid = min_grid;
-  cudaError_t e = launch_k(k_attn, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
+  cudaError_t e = launch_k(k_attn<E4M3>, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
   }
   return T2W_OK;
+}
+
+}  // namespace
+
+int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
+  if (!a.qkv || !a.work || !a.out || a.rows <= 0 || a.heads <= 0 || a.n_work < 0) return T2W_ERR_INVALID;
+  if (a.out_sf && (reinterpret_cast<uintptr_t>(a.out_sf) & 1)) return T2W_ERR_INVALID;
+  if (a.n_work == 0) return T2W_OK;
+  return a.out_sf ? launch_attn_impl<true>(a, st, tm_q, tm_kv) : launch_attn_impl<false>(a, st, tm_q, tm_kv);
 }
 
 }  // namespace t2w

@@ -88,6 +88,13 @@ T2W_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, u
 T2W_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16), completing on `bar`.
+T2W_DEV void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 // Generic-proxy shared-memory writes made visible to the async proxy (tensor core operand reads).
 T2W_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -121,6 +128,24 @@ T2W_DEV void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t i
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= (A * 2^sfA) * (B * 2^sfB)^T with e4m3 operands and UE8M0 scales per row and 32-element K block
+// (kind::mxf8f6f4, one scale vector per instruction of K = 32).  The scales sit in TMEM at sfa / sfb; the byte of the
+// 32-bit TMEM word that each instruction reads is the scale-factor id of `idesc`.
+T2W_DEV void umma_mxf8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa_tmem,
+                       uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.scale_vec::1X [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+// Shared memory -> TMEM copy of a 32-row x 16-byte tile, replicated into all four lane quarters (the layout of a
+// scale-factor atom: row m % 32 of 128 rows in lane m % 32, byte 4 (m / 32) + k-block).
+T2W_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
 T2W_DEV void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -132,6 +157,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major 
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
+// Instruction descriptor, kind::mxf8f6f4 with block scaling: D fp32, A/B e4m3 (format 0), K-major, UE8M0 scales
+// (bit 23), scale-factor ids (the byte of the TMEM scale word) for A in bits 29-30 and for B in bits 4-5.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int M, int N, uint32_t sf_id) {
+  return ((sf_id & 3u) << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(M >> 4) << 24) | ((sf_id & 3u) << 29);
+}
 // Instruction descriptor, kind::f8f6f4: D fp32, A/B e4m3 (format 0), K-major.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -142,6 +173,13 @@ __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
 T2W_DEV uint64_t sdesc_sw128(uint32_t saddr, uint32_t sbo_bytes, uint32_t lbo_bytes) {
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Shared-memory matrix descriptor without swizzle (8-row x 16-byte core matrices); used for the 32 x 16-byte
+// scale-factor atoms, where both strides are the 128-byte pitch of consecutive core matrices.
+T2W_DEV uint64_t sdesc_noswz(uint32_t saddr, uint32_t sbo_bytes, uint32_t lbo_bytes) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
 // 32 lanes x 32 consecutive 32-bit columns; the wait is inside the same asm block so no use of the registers can be
@@ -249,6 +287,33 @@ T2W_DEV float mish(float y) {
   const float n = e * (e + 2.f);
   return y * __fdividef(n, n + 2.f);
 }
+// ---------------------------------------------------------------- e4m3 with power-of-two (UE8M0) block scales
+// The UE8M0 byte e of a block whose largest magnitude is amax: the smallest power of two 2^(e - 127) with
+// amax / 2^(e - 127) <= 448 (the e4m3 maximum); an all-zero block gets e = 127 (scale 1).  With amax = m 2^E,
+// m in [1, 2): e - 127 = E - 8 + (m > 1.75).
+T2W_DEV uint32_t ue8m0_for_amax(float amax) {
+  const uint32_t u = __float_as_uint(amax);
+  if (u == 0u) return 127u;
+  int s = (int)(u >> 23) - 127 - 8 + ((u & 0x7fffffu) > 0x600000u ? 1 : 0);
+  s = s < -127 ? -127 : (s > 127 ? 127 : s);
+  return (uint32_t)(s + 127);
+}
+// 2^(127 - e): the factor that maps a block with scale byte e into [-448, 448] (e <= 253).
+T2W_DEV float ue8m0_inv(uint32_t e) { return __uint_as_float((254u - e) << 23); }
+// Two fp32 values -> two e4m3 bytes (round to nearest even, saturating): lo in bits 0-7, hi in bits 8-15.
+T2W_DEV uint32_t e4m3x2(float lo, float hi) {
+  unsigned short v;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(v) : "f"(hi), "f"(lo));
+  return v;
+}
+T2W_DEV uint32_t e4m3x4(float a, float b, float c, float d) { return e4m3x2(a, b) | (e4m3x2(c, d) << 16); }
+// Byte offset of (row, 32-column block j) inside the scale-factor atoms of a [rows, C] e4m3 matrix: one 512-byte atom
+// per (128-row tile, 128-column block), row r of the tile at (r % 32) * 16 + (r / 32) * 4, block j at byte j % 4.
+T2W_DEV uint32_t sf_offset(int row, int j, int C) {
+  const int r = row & 127;
+  return (uint32_t)(((row >> 7) * (C >> 7) + (j >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (j & 3));
+}
+
 T2W_DEV uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -34,6 +34,9 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
 // [box_rows, box_cols] (box_cols * elem_bytes == 128: one 128-byte swizzle span), 128-byte swizzle, zero OOB fill.
 bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
                   uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols);
+// The same with a 32-, 64- or 128-byte swizzle (box_cols * elem_bytes == swizzle_bytes).
+bool make_tmap_2d_ex(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
+                     uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
 
 struct GemmArgs {
   const void* A = nullptr;  // bf16 [rows_a, lda]
@@ -66,6 +69,38 @@ bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot);
 int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA = nullptr, const WeightMaps* wm = nullptr,
                 const CUtensorMap* tmC = nullptr);
 
+// Block-scaled FP8 GEMM (gemm8.cu): A8 e4m3 [rows_a, lda bytes] with UE8M0 scale atoms per (128-row tile, 128-column
+// block) in `sfa_layouts` row-shifted layouts (layout d at sfa + d * sfa_layout; the causal conv needs d = 0, 1, 2),
+// W8 e4m3 [N, taps * K] with atoms [taps * K / 128][N / 128][512].  Epilogues T2W_EPI_BF16, T2W_EPI_QKV (bf16 out)
+// and T2W_EPI_GELU_FP8 (e4m3 out with its scale atoms in out_sf, layout 0).
+struct Gemm8Args {
+  const void* A8 = nullptr;
+  int lda = 0, rows_a = 0;
+  const uint8_t* sfa = nullptr;
+  long long sfa_layout = 0;
+  int sfa_layouts = 1;
+  const void* W8 = nullptr;
+  const uint8_t* sfw = nullptr;
+  const float* bias = nullptr;
+  int M = 0, N = 0, K = 0, taps = 1, tap_row0 = 0;
+  int epi = 0;
+  void* out = nullptr;
+  int ldo = 0;  // elements of the output type
+  uint8_t* out_sf = nullptr;
+  const float* qn_w = nullptr;
+  const float* qn_b = nullptr;
+  const float* kn_w = nullptr;
+  const float* kn_b = nullptr;
+  float qk_eps = 0.f;
+  int* err = nullptr;
+};
+// Bytes of one layout of scale atoms for a [rows, cols] e4m3 matrix.
+size_t gemm8_sf_bytes(int rows, int cols);
+// tmA / tmW / tmC may be prebuilt (A: 128 x 128-byte boxes; W: 256 x 128; C: 32-row boxes of 64 bf16 columns with
+// 128-byte swizzle, or of 64 e4m3 columns with 64-byte swizzle).
+int launch_gemm8(const Gemm8Args& a, cudaStream_t st, const CUtensorMap* tmA = nullptr, const CUtensorMap* tmW = nullptr,
+                 const CUtensorMap* tmC = nullptr);
+
 // One attention work item: a 128-query tile of one packed sequence.
 struct AttnWork {
   int q_row;   // buffer row of the tile's first query
@@ -78,7 +113,8 @@ struct AttnArgs {
   int rows = 0, heads = 0;
   const AttnWork* work = nullptr;  // device [n_work]
   int n_work = 0;
-  void* out = nullptr;  // bf16 [rows, heads * 64]
+  void* out = nullptr;  // bf16 [rows, heads * 64], or e4m3 when out_sf is set
+  uint8_t* out_sf = nullptr;  // e4m3 output: its UE8M0 scale atoms (layout 0)
   float scale_log2 = 0.f;
   int* err = nullptr;
 };
@@ -89,11 +125,31 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q = nu
 // Row kernels.
 int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scale1, float eps, int rows, int C,
                   __nv_bfloat16* out, int ldo, const uint8_t* pad, cudaStream_t st);
-// h += g * y (fp32, in place; skipped when y == nullptr), then out = bf16(LN(h) * scale1 + shift), pad rows zero.
+// Output of a row kernel: bf16 [rows, C], or e4m3 [rows, C] with UE8M0 scale atoms per (row, 32-column block) written
+// in n_layouts row-shifted layouts (layout d at sf + d * layout_bytes holds row x at position x + d: d = 0 for a plain
+// GEMM operand, d = 0, 1, 2 for the causal conv's taps).
+struct RowOut {
+  void* out = nullptr;
+  uint8_t* sf = nullptr;
+  int n_layouts = 1;
+  long long layout_bytes = 0;
+};
+inline RowOut row_out_bf16(__nv_bfloat16* p) {
+  RowOut o;
+  o.out = p;
+  return o;
+}
+// h += g * y (fp32, in place; skipped when y == nullptr), then out = LN(h) * scale1 + shift, pad rows zero.
 int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
-                      int rows, int C, __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st);
-int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C,
-                   __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st);
+                      int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st);
+int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C, const RowOut& o,
+                   const uint8_t* pad, cudaStream_t st);
+// bf16 [rows, C] -> e4m3 + scale atoms (C = 128, 512, 1536 or 2048).
+int launch_quant_rows(const __nv_bfloat16* x, int rows, int C, const RowOut& o, cudaStream_t st);
+// fp32 W [N, Kt] -> e4m3 + per-1x128-block scale atoms [Kt / 128][N / 128][512].
+int launch_quant_weight(const float* w, int N, int Kt, uint8_t* w8, uint8_t* sf, cudaStream_t st);
+// Conv1d weight [out, in, k] fp32 -> fp32 [out, k * in], tap-major (the FP8 path quantises this layout).
+int launch_conv_weight_f32(const float* src, float* dst, int cout, int cin, int k, cudaStream_t st);
 int launch_pack(const float* x0, const float* mu, const float* cond, const float* spk, const int* tok_row,
                 const int* tok_stream, int n_tok, int mel, int half_rows, __nv_bfloat16* hx, int ld_hx, float* x,
                 cudaStream_t st);

@@ -34,6 +34,36 @@ T2W_DEV void store_bf16x4(__nv_bfloat16* dst, float a, float b, float c, float d
   *reinterpret_cast<uint2*>(dst) = u;
 }
 
+// One normalised row (V float4 per lane, column 4 (32 i + lane) + e) to bf16, or to e4m3 with one power-of-two scale
+// per 32-column block (a block spans 8 lanes): the e4m3 bytes go to o.out and the four scale bytes of each 128-column
+// group to the row's atoms in every row-shifted layout (lane d writes layout d).
+template <int V, bool E4M3>
+T2W_DEV void store_row(const RowOut& o, int row, const float4 (&y)[V]) {
+  const int lane = threadIdx.x & 31;
+  constexpr int C = 128 * V;
+  if constexpr (!E4M3) {
+    __nv_bfloat16* d = static_cast<__nv_bfloat16*>(o.out) + (size_t)row * C;
+#pragma unroll
+    for (int i = 0; i < V; ++i) store_bf16x4(d + 4 * (32 * i + lane), y[i].x, y[i].y, y[i].z, y[i].w);
+  } else {
+    uint8_t* d = static_cast<uint8_t*>(o.out) + (size_t)row * C;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float a = fmaxf(fmaxf(fabsf(y[i].x), fabsf(y[i].y)), fmaxf(fabsf(y[i].z), fabsf(y[i].w)));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+      const uint32_t e = ue8m0_for_amax(a);
+      const float inv = ue8m0_inv(e);
+      *reinterpret_cast<uint32_t*>(d + 4 * (32 * i + lane)) = e4m3x4(y[i].x * inv, y[i].y * inv, y[i].z * inv, y[i].w * inv);
+      const uint32_t word = __shfl_sync(0xffffffffu, e, 0) | (__shfl_sync(0xffffffffu, e, 8) << 8) |
+                            (__shfl_sync(0xffffffffu, e, 16) << 16) | (__shfl_sync(0xffffffffu, e, 24) << 24);
+      if (lane < o.n_layouts)
+        *reinterpret_cast<uint32_t*>(o.sf + lane * o.layout_bytes + sf_offset(row + lane, 4 * i, C)) = word;
+    }
+  }
+}
+
 template <int V>
 __global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int ldh, const float* __restrict__ shift,
                                                 const float* __restrict__ scale1, float eps, int rows,
@@ -68,11 +98,11 @@ __global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int
 
 // h += g * y (the gated residual of the preceding GEMM's bf16 output y, fp32, stored back), then out = LN(h) * scale1 +
 // shift (dit_kernels.py:35-60's add_ln_mod, with the residual kept in fp32).  y == nullptr: plain LN + modulation.
-template <int V>
+template <int V, bool E4M3>
 __global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const __nv_bfloat16* __restrict__ y,
                                                     const float* __restrict__ g, const float* __restrict__ shift,
-                                                    const float* __restrict__ scale1, float eps, int rows,
-                                                    __nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ pad) {
+                                                    const float* __restrict__ scale1, float eps, int rows, const RowOut o,
+                                                    const uint8_t* __restrict__ pad) {
   pdl_wait();
   pdl_launch();
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -97,10 +127,10 @@ __global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const
       hr[32 * i + lane] = x[i];
     }
   }
-  __nv_bfloat16* o = out + (size_t)row * C;
   if (pad && pad[row]) {
 #pragma unroll
-    for (int i = 0; i < V; ++i) store_bf16x4(o + 4 * (32 * i + lane), 0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < V; ++i) x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    store_row<V, E4M3>(o, row, x);
     return;
   }
   float mean, rstd;
@@ -110,27 +140,28 @@ __global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const
     const int c = 4 * (32 * i + lane);
     const float4 sc = __ldg(reinterpret_cast<const float4*>(scale1 + c));
     const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + c));
-    store_bf16x4(o + c, fmaf((x[i].x - mean) * rstd, sc.x, sh.x), fmaf((x[i].y - mean) * rstd, sc.y, sh.y),
-                 fmaf((x[i].z - mean) * rstd, sc.z, sh.z), fmaf((x[i].w - mean) * rstd, sc.w, sh.w));
+    x[i] = make_float4(fmaf((x[i].x - mean) * rstd, sc.x, sh.x), fmaf((x[i].y - mean) * rstd, sc.y, sh.y),
+                       fmaf((x[i].z - mean) * rstd, sc.z, sh.z), fmaf((x[i].w - mean) * rstd, sc.w, sh.w));
   }
+  store_row<V, E4M3>(o, row, x);
 }
 
-template <int V>
+template <int V, bool E4M3>
 __global__ void __launch_bounds__(256) k_ln_mish(const __nv_bfloat16* __restrict__ xin, const float* __restrict__ w,
-                                                 const float* __restrict__ b, float eps, int rows,
-                                                 __nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ pad) {
+                                                 const float* __restrict__ b, float eps, int rows, const RowOut o,
+                                                 const uint8_t* __restrict__ pad) {
   pdl_wait();
   pdl_launch();
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   constexpr int C = 128 * V;
-  __nv_bfloat16* o = out + (size_t)row * C;
+  float4 x[V];
   if (pad && pad[row]) {
 #pragma unroll
-    for (int i = 0; i < V; ++i) store_bf16x4(o + 4 * (32 * i + lane), 0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < V; ++i) x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    store_row<V, E4M3>(o, row, x);
     return;
   }
-  float4 x[V];
   const uint2* xr = reinterpret_cast<const uint2*>(xin + (size_t)row * C);
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -146,8 +177,52 @@ __global__ void __launch_bounds__(256) k_ln_mish(const __nv_bfloat16* __restrict
     const int c = 4 * (32 * i + lane);
     const float4 ww = __ldg(reinterpret_cast<const float4*>(w + c));
     const float4 bb = __ldg(reinterpret_cast<const float4*>(b + c));
-    store_bf16x4(o + c, mish(fmaf((x[i].x - mean) * rstd, ww.x, bb.x)), mish(fmaf((x[i].y - mean) * rstd, ww.y, bb.y)),
-                 mish(fmaf((x[i].z - mean) * rstd, ww.z, bb.z)), mish(fmaf((x[i].w - mean) * rstd, ww.w, bb.w)));
+    x[i] = make_float4(mish(fmaf((x[i].x - mean) * rstd, ww.x, bb.x)), mish(fmaf((x[i].y - mean) * rstd, ww.y, bb.y)),
+                       mish(fmaf((x[i].z - mean) * rstd, ww.z, bb.z)), mish(fmaf((x[i].w - mean) * rstd, ww.w, bb.w)));
+  }
+  store_row<V, E4M3>(o, row, x);
+}
+
+// bf16 [rows, C] -> e4m3 with per-(row, 32-column block) power-of-two scales (the activation quantiser of the FP8
+// path's test entry point; inside the solve the producing kernels quantise their own outputs).
+template <int V>
+__global__ void __launch_bounds__(256) k_quant_rows(const __nv_bfloat16* __restrict__ xin, int rows, const RowOut o) {
+  pdl_wait();
+  pdl_launch();
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int C = 128 * V;
+  float4 x[V];
+  const uint2* xr = reinterpret_cast<const uint2*>(xin + (size_t)row * C);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const uint2 u = xr[32 * i + lane];
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    x[i] = make_float4(a.x, a.y, c.x, c.y);
+  }
+  store_row<V, true>(o, row, x);
+}
+
+// Weight W [N, Kt] fp32 -> e4m3 with one power-of-two scale per 1 x 128 block, the scale repeated over the block's
+// four 32-column scale slots of the atoms [Kt / 128][N / 128][512].  One warp per (row, 128-column block).
+__global__ void __launch_bounds__(256) k_quant_weight(const float* __restrict__ w, int N, int Kt, uint8_t* __restrict__ w8,
+                                                      uint8_t* __restrict__ sf) {
+  const int item = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int kblocks = Kt / 128;
+  if (item >= N * kblocks) return;
+  const int n = item / kblocks, kb = item - n * kblocks;
+  const float4 v = __ldg(reinterpret_cast<const float4*>(w + (size_t)n * Kt + 128 * kb) + lane);
+  float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, m));
+  const uint32_t e = ue8m0_for_amax(a);
+  const float inv = ue8m0_inv(e);
+  *reinterpret_cast<uint32_t*>(w8 + (size_t)n * Kt + 128 * kb + 4 * lane) = e4m3x4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+  if (lane == 0) {
+    const int r = n & 127;
+    *reinterpret_cast<uint32_t*>(sf + ((size_t)kb * (N / 128) + n / 128) * 512 + (r & 31) * 16 + (r >> 5) * 4) =
+        e * 0x01010101u;
   }
 }
 
@@ -206,7 +281,8 @@ __global__ void k_f32_to_bf16(const float* __restrict__ s, __nv_bfloat16* __rest
   if (i < n) d[i] = __float2bfloat16_rn(s[i]);
 }
 
-__global__ void k_conv_weight(const float* __restrict__ s, __nv_bfloat16* __restrict__ d, int cout, int cin, int k) {
+template <class T>
+__global__ void k_conv_weight(const float* __restrict__ s, T* __restrict__ d, int cout, int cin, int k) {
   pdl_wait();
   pdl_launch();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // over dst [cout, k * cin]
@@ -214,7 +290,11 @@ __global__ void k_conv_weight(const float* __restrict__ s, __nv_bfloat16* __rest
   const int o = (int)(i / ((long long)k * cin));
   const int rem = (int)(i - (long long)o * k * cin);
   const int tap = rem / cin, c = rem - tap * cin;
-  d[i] = __float2bfloat16_rn(s[((size_t)o * cin + c) * k + tap]);
+  const float v = s[((size_t)o * cin + c) * k + tap];
+  if constexpr (sizeof(T) == 2)
+    d[i] = __float2bfloat16_rn(v);
+  else
+    d[i] = v;
 }
 
 // Time embedding: sinusoid(t * t_scale) -> Linear -> SiLU -> Linear, then SiLU (the adaLN_modulation input).  One block
@@ -321,34 +401,80 @@ int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scal
   return check_launch();
 }
 
-int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
-                      int rows, int C, __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st) {
-  if (rows <= 0) return T2W_OK;
-  if (y && !g) return T2W_ERR_INVALID;
+namespace {
+
+template <bool E4M3>
+int add_ln_mod_impl(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
+                    int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st) {
   const unsigned gr = blocks_for(rows, kRowsPerBlock);
   switch (C) {
-    case 128: check_err(launch_k(k_add_ln_mod<1>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
-    case 256: check_err(launch_k(k_add_ln_mod<2>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
-    case 512: check_err(launch_k(k_add_ln_mod<4>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
-    case 768: check_err(launch_k(k_add_ln_mod<6>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
-    case 1024: check_err(launch_k(k_add_ln_mod<8>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, out, pad)); break;
+    case 128: check_err(launch_k(k_add_ln_mod<1, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
+    case 256: check_err(launch_k(k_add_ln_mod<2, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
+    case 512: check_err(launch_k(k_add_ln_mod<4, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
+    case 768: check_err(launch_k(k_add_ln_mod<6, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
+    case 1024: check_err(launch_k(k_add_ln_mod<8, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
     default: return T2W_ERR_INVALID;
   }
   return check_launch();
 }
 
-int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C,
-                   __nv_bfloat16* out, const uint8_t* pad, cudaStream_t st) {
-  if (rows <= 0) return T2W_OK;
+template <bool E4M3>
+int ln_mish_impl(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C, const RowOut& o,
+                 const uint8_t* pad, cudaStream_t st) {
   const unsigned g = blocks_for(rows, kRowsPerBlock);
   switch (C) {
-    case 128: check_err(launch_k(k_ln_mish<1>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
-    case 256: check_err(launch_k(k_ln_mish<2>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
-    case 512: check_err(launch_k(k_ln_mish<4>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
-    case 768: check_err(launch_k(k_ln_mish<6>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
-    case 1024: check_err(launch_k(k_ln_mish<8>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, out, pad)); break;
+    case 128: check_err(launch_k(k_ln_mish<1, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
+    case 256: check_err(launch_k(k_ln_mish<2, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
+    case 512: check_err(launch_k(k_ln_mish<4, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
+    case 768: check_err(launch_k(k_ln_mish<6, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
+    case 1024: check_err(launch_k(k_ln_mish<8, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
     default: return T2W_ERR_INVALID;
   }
+  return check_launch();
+}
+
+bool row_out_ok(const RowOut& o) {
+  if (!o.out) return false;
+  if (!o.sf) return true;
+  return o.n_layouts >= 1 && o.n_layouts <= 3 && (o.n_layouts == 1 || o.layout_bytes % 16 == 0) &&
+         (reinterpret_cast<uintptr_t>(o.sf) & 3) == 0;
+}
+
+}  // namespace
+
+int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
+                      int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st) {
+  if (rows <= 0) return T2W_OK;
+  if ((y && !g) || !row_out_ok(o)) return T2W_ERR_INVALID;
+  return o.sf ? add_ln_mod_impl<true>(h, y, g, shift, scale1, eps, rows, C, o, pad, st)
+              : add_ln_mod_impl<false>(h, y, g, shift, scale1, eps, rows, C, o, pad, st);
+}
+
+int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C, const RowOut& o,
+                   const uint8_t* pad, cudaStream_t st) {
+  if (rows <= 0) return T2W_OK;
+  if (!row_out_ok(o)) return T2W_ERR_INVALID;
+  return o.sf ? ln_mish_impl<true>(x, w, b, eps, rows, C, o, pad, st) : ln_mish_impl<false>(x, w, b, eps, rows, C, o, pad, st);
+}
+
+int launch_quant_rows(const __nv_bfloat16* x, int rows, int C, const RowOut& o, cudaStream_t st) {
+  if (rows <= 0) return T2W_OK;
+  if (!o.sf || !row_out_ok(o)) return T2W_ERR_INVALID;
+  const unsigned g = blocks_for(rows, kRowsPerBlock);
+  switch (C) {
+    case 128: check_err(launch_k(k_quant_rows<1>, dim3(g), dim3(256), 0, st, x, rows, o)); break;
+    case 512: check_err(launch_k(k_quant_rows<4>, dim3(g), dim3(256), 0, st, x, rows, o)); break;
+    case 1536: check_err(launch_k(k_quant_rows<12>, dim3(g), dim3(256), 0, st, x, rows, o)); break;
+    case 2048: check_err(launch_k(k_quant_rows<16>, dim3(g), dim3(256), 0, st, x, rows, o)); break;
+    default: return T2W_ERR_INVALID;
+  }
+  return check_launch();
+}
+
+int launch_quant_weight(const float* w, int N, int Kt, uint8_t* w8, uint8_t* sf, cudaStream_t st) {
+  if (N <= 0 || N % 128 || Kt <= 0 || Kt % 128 || !w || !w8 || !sf) return T2W_ERR_INVALID;
+  const unsigned g = blocks_for(N * (Kt / 128), kRowsPerBlock);
+  check_err(launch_k(k_quant_weight, dim3(g), dim3(256), 0, st, w, N, Kt, w8, sf));
   return check_launch();
 }
 
@@ -379,7 +505,13 @@ int launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, long long n, cudaSt
 
 int launch_conv_weight(const float* src, __nv_bfloat16* dst, int cout, int cin, int k, cudaStream_t st) {
   const long long n = (long long)cout * cin * k;
-  check_err(launch_k(k_conv_weight, dim3(blocks_for(n, 256)), dim3(256), 0, st, src, dst, cout, cin, k));
+  check_err(launch_k(k_conv_weight<__nv_bfloat16>, dim3(blocks_for(n, 256)), dim3(256), 0, st, src, dst, cout, cin, k));
+  return check_launch();
+}
+
+int launch_conv_weight_f32(const float* src, float* dst, int cout, int cin, int k, cudaStream_t st) {
+  const long long n = (long long)cout * cin * k;
+  check_err(launch_k(k_conv_weight<float>, dim3(blocks_for(n, 256)), dim3(256), 0, st, src, dst, cout, cin, k));
   return check_launch();
 }
 

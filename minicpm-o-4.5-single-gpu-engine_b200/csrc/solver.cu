@@ -14,6 +14,7 @@
 // each stream's segment [2 zero rows | L_i frames]; the uncond half repeats it at row offset half_rows.  The two zero
 // rows in front of each segment are the causal convolutions' left padding (the reference's empty conv cache at a
 // prompt setup), so a conv tap is a plain row shift and the im2col matrix never exists.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -66,22 +67,31 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
-                  uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols) {
+bool make_tmap_2d_ex(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
+                     uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols, int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || !base || (reinterpret_cast<uintptr_t>(base) & 15) || (pitch_bytes & 15) || box_rows > 256 ||
-      box_cols * (uint32_t)elem_bytes != 128)
+      box_cols * (uint32_t)elem_bytes != (uint32_t)swizzle_bytes)
     return false;
   const CUtensorMapDataType dt = elem_bytes == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                    : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (sw == CU_TENSOR_MAP_SWIZZLE_NONE) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {pitch_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t es[2] = {1, 1};
-  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
+                  uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols) {
+  return make_tmap_2d_ex(map, base, elem_bytes, rows, cols, pitch_bytes, box_rows, box_cols, 128);
 }
 
 }  // namespace t2w
@@ -107,10 +117,16 @@ namespace {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct BlockW {
-  __nv_bfloat16 *qkv, *proj, *c1, *c2, *fc1, *fc2;
+  // bf16 path
+  __nv_bfloat16 *qkv = nullptr, *proj = nullptr, *c1 = nullptr, *c2 = nullptr, *fc1 = nullptr, *fc2 = nullptr;
   float *b_qkv, *qn_w, *qn_b, *kn_w, *kn_b, *b_proj, *b_c1, *cln_w, *cln_b, *b_c2, *b_fc1, *b_fc2;
   WeightMaps tm_qkv, tm_proj, tm_c1, tm_c2, tm_fc1, tm_fc2;
+  // FP8 path: e4m3 matrices (same [N, Kt] layouts) with their per-1x128-block scale atoms, and 256-row TMA maps
+  uint8_t* w8[6] = {};
+  uint8_t* sf8[6] = {};
+  CUtensorMap t8[6];
 };
+enum { W8_QKV, W8_PROJ, W8_C1, W8_C2, W8_FC1, W8_FC2 };
 
 struct Plan {
   int n_streams = 0, n_tok = 0, half_rows = 0, rows = 0, n_work = 0;
@@ -121,7 +137,10 @@ struct Plan {
 };
 
 struct WsLayout {
-  size_t hx, h, a, qkv, o, y, c1, f, dphi, x, pad, tok_row, tok_stream, work, total;
+  size_t hx, h, a, qkv, o, y, c1, f, dphi, x, pad, tok_row, tok_stream, work;
+  // FP8 path: e4m3 activations and their scale atoms (sf_h: bytes of one layout for a [rows + 128, hidden] matrix)
+  size_t a8, sfa, o8, sfo, c18, sfc1, f8, sff, sf_h, sf_f;
+  size_t total;
 };
 
 uint64_t mix(uint64_t h, uint64_t v) {
@@ -199,7 +218,7 @@ bool make_plan(const t2w_config& c, int n, const int* P, const int* T, Plan& pl)
   return true;
 }
 
-WsLayout layout(const t2w_config& c, const Plan& pl) {
+WsLayout layout(const t2w_config& c, const Plan& pl, bool fp8) {
   WsLayout w{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -222,6 +241,19 @@ WsLayout layout(const t2w_config& c, const Plan& pl) {
   w.tok_row = take((size_t)pl.n_tok * 4);
   w.tok_stream = take((size_t)pl.n_tok * 4);
   w.work = take((size_t)pl.n_work * sizeof(AttnWork));
+  if (fp8) {
+    // the row-shifted scale layouts hold rows up to rows + 1: one spare row tile
+    w.sf_h = align256(gemm8_sf_bytes(pl.rows + 128, c.hidden));
+    w.sf_f = align256(gemm8_sf_bytes(pl.rows + 128, c.ffn));
+    w.a8 = take(R * H);
+    w.sfa = take(3 * w.sf_h);
+    w.o8 = take(R * H);
+    w.sfo = take(w.sf_h);
+    w.c18 = take(R * H);
+    w.sfc1 = take(3 * w.sf_h);
+    w.f8 = take(R * (size_t)c.ffn);
+    w.sff = take(w.sf_f);
+  }
   w.total = off;
   return w;
 }
@@ -255,7 +287,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   Prof none;
   Prof& P = prof ? *prof : none;
   const t2w_config& c = s->cfg;
-  const WsLayout L = layout(c, pl);
+  const WsLayout L = layout(c, pl, s->precision == T2W_PREC_FP8);
   const int H = c.hidden, R = pl.rows, mel = c.mel, F = c.ffn;
   __nv_bfloat16* hx = at<__nv_bfloat16>(ws, L.hx);
   float* h = at<float>(ws, L.h);
@@ -285,6 +317,64 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     return T2W_ERR_INVALID;
   CUtensorMap tm_att_q, tm_att_kv;
   if (!make_attn_tmaps(&tm_att_q, &tm_att_kv, qkv, R, c.heads)) return T2W_ERR_INVALID;
+  const bool fp8 = s->precision == T2W_PREC_FP8;
+  uint8_t *a8 = nullptr, *sfa = nullptr, *o8 = nullptr, *sfo = nullptr, *c18 = nullptr, *sfc1 = nullptr, *f8 = nullptr,
+          *sff = nullptr;
+  CUtensorMap t8_a, t8_o, t8_c1, t8_f, st8_f;
+  if (fp8) {
+    a8 = at<uint8_t>(ws, L.a8);
+    sfa = at<uint8_t>(ws, L.sfa);
+    o8 = at<uint8_t>(ws, L.o8);
+    sfo = at<uint8_t>(ws, L.sfo);
+    c18 = at<uint8_t>(ws, L.c18);
+    sfc1 = at<uint8_t>(ws, L.sfc1);
+    f8 = at<uint8_t>(ws, L.f8);
+    sff = at<uint8_t>(ws, L.sff);
+    if (!make_tmap_2d(&t8_a, a8, 1, R, H, H, 128, 128) || !make_tmap_2d(&t8_o, o8, 1, R, H, H, 128, 128) ||
+        !make_tmap_2d(&t8_c1, c18, 1, R, H, H, 128, 128) || !make_tmap_2d(&t8_f, f8, 1, R, F, F, 128, 128) ||
+        !make_tmap_2d_ex(&st8_f, f8, 1, R, F, F, 32, 64, 64))
+      return T2W_ERR_INVALID;
+    // scale bytes 127 (= 1) wherever no kernel writes (rows before 0 of the shifted layouts, pad rows of o8)
+    T2W_CUDA(cudaMemsetAsync(sfa, 127, 3 * L.sf_h, st));
+    T2W_CUDA(cudaMemsetAsync(sfc1, 127, 3 * L.sf_h, st));
+    T2W_CUDA(cudaMemsetAsync(sfo, 127, L.sf_h, st));
+    T2W_CUDA(cudaMemsetAsync(o8, 0, (size_t)R * H, st));
+  }
+  RowOut out_a = row_out_bf16(a), out_c1 = row_out_bf16(c1);
+  if (fp8) {
+    out_a.out = a8;
+    out_a.sf = sfa;
+    out_a.n_layouts = 3;
+    out_a.layout_bytes = (long long)L.sf_h;
+    out_c1.out = c18;
+    out_c1.sf = sfc1;
+    out_c1.n_layouts = 3;
+    out_c1.layout_bytes = (long long)L.sf_h;
+  }
+  // an FP8 GEMM of the block: A8 with its atoms, W8 of block weight `wi`
+  auto g8 = [&](const BlockW& w, int wi, const uint8_t* A8, const uint8_t* sf, int layouts, int N, int K, int taps,
+                int epi, void* out, int ldo, const float* bias) {
+    Gemm8Args a;
+    a.A8 = A8;
+    a.lda = K;
+    a.rows_a = R;
+    a.sfa = sf;
+    a.sfa_layout = (long long)L.sf_h;
+    a.sfa_layouts = layouts;
+    a.W8 = w.w8[wi];
+    a.sfw = w.sf8[wi];
+    a.bias = bias;
+    a.M = R;
+    a.N = N;
+    a.K = K;
+    a.taps = taps;
+    a.tap_row0 = taps == 3 ? -2 : 0;
+    a.epi = epi;
+    a.out = out;
+    a.ldo = ldo;
+    a.err = s->err;
+    return a;
+  };
 
   T2W_CUDA(cudaMemsetAsync(hx, 0, (size_t)R * 4 * mel * 2, st));
   // Attention writes only sequence rows; the pad rows of its output buffer must hold finite values (zero here, later
@@ -327,9 +417,51 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       const float* M = s->mods + ((size_t)step * c.depth + bi) * 9 * H;
       const float *sh_a = M, *sc_a = M + H, *g_a = M + 2 * H, *sh_m = M + 3 * H, *sc_m = M + 4 * H, *g_m = M + 5 * H;
       const float *sh_c = M + 6 * H, *sc_c = M + 7 * H, *g_c = M + 8 * H;
+      if (fp8) {
+        // attention branch
+        T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
+        T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, out_a, nullptr, st));
+        Gemm8Args q = g8(w, W8_QKV, a8, sfa, 3, 3 * H, H, 1, T2W_EPI_QKV, qkv, 3 * H, w.b_qkv);
+        q.qn_w = w.qn_w; q.qn_b = w.qn_b; q.kn_w = w.kn_w; q.kn_b = w.kn_b; q.qk_eps = c.eps_qk;
+        T2W_TRY(P.tick(T2W_KC_GEMM_QKV, st));
+        T2W_TRY(launch_gemm8(q, st, &t8_a, &w.t8[W8_QKV], &st_qkv));
+        AttnArgs at8 = at_args;
+        at8.out = o8;
+        at8.out_sf = sfo;
+        T2W_TRY(P.tick(T2W_KC_ATTN, st));
+        T2W_TRY(launch_attn(at8, st, &tm_att_q, &tm_att_kv));
+        T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
+        T2W_TRY(launch_gemm8(g8(w, W8_PROJ, o8, sfo, 1, H, H, 1, T2W_EPI_BF16, y, H, w.b_proj), st, &t8_o,
+                             &w.t8[W8_PROJ], &st_y));
+        // causal conv branch
+        T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
+        T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, out_a, pad, st));
+        T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
+        T2W_TRY(launch_gemm8(g8(w, W8_C1, a8, sfa, 3, H, H, 3, T2W_EPI_BF16, o, H, w.b_c1), st, &t8_a, &w.t8[W8_C1],
+                             &st_o));
+        T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
+        T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, out_c1, pad, st));
+        T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
+        T2W_TRY(launch_gemm8(g8(w, W8_C2, c18, sfc1, 3, H, H, 3, T2W_EPI_BF16, y, H, w.b_c2), st, &t8_c1,
+                             &w.t8[W8_C2], &st_y));
+        // MLP branch: fc1's epilogue quantises GELU's output for fc2
+        T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
+        T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, out_a, nullptr, st));
+        Gemm8Args f1 = g8(w, W8_FC1, a8, sfa, 3, F, H, 1, T2W_EPI_GELU_FP8, f8, F, w.b_fc1);
+        f1.out_sf = sff;
+        T2W_TRY(P.tick(T2W_KC_GEMM_FC1, st));
+        T2W_TRY(launch_gemm8(f1, st, &t8_a, &w.t8[W8_FC1], &st8_f));
+        Gemm8Args f2 = g8(w, W8_FC2, f8, sff, 1, H, F, 1, T2W_EPI_BF16, y, H, w.b_fc2);
+        f2.sfa_layout = (long long)L.sf_f;
+        T2W_TRY(P.tick(T2W_KC_GEMM_FC2, st));
+        T2W_TRY(launch_gemm8(f2, st, &t8_f, &w.t8[W8_FC2], &st_y));
+        pend_g = g_m;
+        pend_y = y;
+        continue;
+      }
       // attention branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, a, nullptr, st));
+      T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, row_out_bf16(a), nullptr, st));
       GemmArgs q = GemmArgs();
       q.rows_a = R; q.M = R; q.err = s->err;
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
@@ -345,7 +477,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_y));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, a, pad, st));
+      T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st));
       GemmArgs k1 = GemmArgs();
       k1.rows_a = R; k1.M = R; k1.err = s->err;
       k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
@@ -353,7 +485,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
       T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &st_o));
       T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
-      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, c1, pad, st));
+      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, row_out_bf16(c1), pad, st));
       GemmArgs k2 = GemmArgs();
       k2.rows_a = R; k2.M = R; k2.err = s->err;
       k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
@@ -362,7 +494,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &st_y));
       // MLP branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, a, nullptr, st));
+      T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, row_out_bf16(a), nullptr, st));
       GemmArgs f1 = GemmArgs();
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
@@ -378,7 +510,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     }
     const float* FM = s->final_mods + (size_t)step * 2 * H;
     T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-    T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, FM, FM + H, c.eps_final, R, H, a, nullptr, st));
+    T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, FM, FM + H, c.eps_final, R, H, row_out_bf16(a), nullptr, st));
     GemmArgs fin = GemmArgs();
     fin.rows_a = R; fin.M = R; fin.err = s->err;
     fin.A = a; fin.lda = H; fin.W = s->w_fin; fin.bias = s->b_fin; fin.N = mel; fin.K = H; fin.epi = T2W_EPI_F32;
@@ -394,7 +526,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
 }
 
 int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
-  const WsLayout L = layout(s->cfg, pl);
+  const WsLayout L = layout(s->cfg, pl, s->precision == T2W_PREC_FP8);
   T2W_CUDA(cudaMemcpyAsync(at<uint8_t>(ws, L.pad), pl.pad.data(), pl.pad.size(), cudaMemcpyHostToDevice, st));
   T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_row), pl.tok_row.data(), pl.tok_row.size() * 4, cudaMemcpyHostToDevice, st));
   T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_stream), pl.tok_stream.data(), pl.tok_stream.size() * 4,
@@ -403,6 +535,37 @@ int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
                            cudaMemcpyHostToDevice, st));
   s->ws_meta[reinterpret_cast<uintptr_t>(ws)] = pl.key;
   return T2W_OK;
+}
+
+// Varlen attention with a per-call device work list (one entry per 128-query tile of each sequence).
+int attn_varlen_alloc(const void* qkv, int rows, int heads, int n_seq, const int32_t* seq_row, const int32_t* seq_len,
+                      const int32_t* prompt_len, void* out, uint8_t* out_sf, void* stream) {
+  if (!qkv || !out || !seq_row || !seq_len || !prompt_len || n_seq < 0 || heads <= 0) return T2W_ERR_INVALID;
+  std::vector<AttnWork> work;
+  for (int s = 0; s < n_seq; ++s) {
+    if (seq_len[s] <= 0 || prompt_len[s] < 0 || prompt_len[s] > seq_len[s] || seq_row[s] < 0 ||
+        seq_row[s] + seq_len[s] > rows)
+      return T2W_ERR_INVALID;
+    for (int q = 0; q < seq_len[s]; q += 128)
+      work.push_back(AttnWork{seq_row[s] + q, seq_row[s], q, prompt_len[s], seq_len[s]});
+  }
+  if (work.empty()) return T2W_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  AttnWork* d = nullptr;
+  T2W_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), work.size() * sizeof(AttnWork), st));
+  T2W_CUDA(cudaMemcpyAsync(d, work.data(), work.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st));
+  AttnArgs a;
+  a.qkv = qkv;
+  a.rows = rows;
+  a.heads = heads;
+  a.work = d;
+  a.n_work = (int)work.size();
+  a.out = out;
+  a.out_sf = out_sf;
+  a.scale_log2 = (float)(1.4426950408889634 / 8.0);
+  const int rc = launch_attn(a, st);
+  cudaFreeAsync(d, st);
+  return rc;
 }
 
 }  // namespace
@@ -422,8 +585,11 @@ int t2w_device_ok(int device) {
 int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* weights, int32_t n_weights,
                int32_t precision, void* stream, t2w_solver** out) {
   if (!cfg || !weights || !out || !valid_cfg(*cfg)) return T2W_ERR_INVALID;
-  if (precision != T2W_PREC_BF16) return T2W_ERR_UNSUPPORTED;
   const t2w_config& c = *cfg;
+  const bool fp8 = precision == T2W_PREC_FP8;
+  if (precision != T2W_PREC_BF16 && !fp8) return T2W_ERR_INVALID;
+  // the FP8 GEMM tiles N by 256 and K by 128
+  if (fp8 && (c.hidden % 256 || c.ffn % 256 || c.hidden % 128)) return T2W_ERR_UNSUPPORTED;
   if (n_weights != T2W_W_COUNT + c.depth * T2W_B_COUNT) return T2W_ERR_INVALID;
   for (int i = 0; i < n_weights; ++i)
     if (!weights[i]) return T2W_ERR_INVALID;
@@ -445,15 +611,14 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
   const size_t o_mods = take((size_t)S * c.depth * 9 * H * 4), o_fmods = take((size_t)S * 2 * H * 4);
   const size_t o_dts = take(S * 4), o_ts = take(S * 4), o_freq = take(c.freq_dim * 4), o_st = take((size_t)S * H * 4);
   const size_t o_err = take(16);
-  std::vector<size_t> ob(c.depth * 18);
+  // per block: the six matrices (bf16, or e4m3 plus per-1x128-block scale atoms), then the vectors
+  const size_t eb = fp8 ? 1 : 2;
+  const int mat_n[6] = {3 * H, H, H, H, F, H}, mat_k[6] = {H, H, 3 * H, 3 * H, H, F};
+  std::vector<size_t> ob(c.depth * 24);
   for (int b = 0; b < c.depth; ++b) {
-    size_t* q = &ob[b * 18];
-    q[0] = take((size_t)3 * H * H * 2);
-    q[1] = take((size_t)H * H * 2);
-    q[2] = take((size_t)H * 3 * H * 2);
-    q[3] = take((size_t)H * 3 * H * 2);
-    q[4] = take((size_t)F * H * 2);
-    q[5] = take((size_t)H * F * 2);
+    size_t* q = &ob[b * 24];
+    for (int i = 0; i < 6; ++i) q[i] = take((size_t)mat_n[i] * mat_k[i] * eb);
+    for (int i = 0; i < 6; ++i) q[18 + i] = take(fp8 ? gemm8_sf_bytes(mat_n[i], mat_k[i]) : 0);
     q[6] = take(3 * H * 4);
     q[7] = take(c.head_dim * 4);
     q[8] = take(c.head_dim * 4);
@@ -500,15 +665,17 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
     return fail(T2W_ERR_CUDA);
   s->blk.resize(c.depth);
   std::vector<const float*> ada_w(c.depth), ada_b(c.depth);
+  // FP8: fp32 staging of one weight matrix in the layout that is quantised ([N, Kt], conv taps tap-major)
+  float* tmp = nullptr;
+  if (fp8 && cudaMalloc(reinterpret_cast<void**>(&tmp), (size_t)std::max(3 * H * H, F * H) * 4) != cudaSuccess)
+    return fail(T2W_ERR_OOM);
+  auto fail2 = [&](int rc) {
+    if (tmp) cudaFree(tmp);
+    return fail(rc);
+  };
   for (int b = 0; b < c.depth; ++b) {
     BlockW& w = s->blk[b];
-    const size_t* q = &ob[b * 18];
-    w.qkv = at<__nv_bfloat16>(A, q[0]);
-    w.proj = at<__nv_bfloat16>(A, q[1]);
-    w.c1 = at<__nv_bfloat16>(A, q[2]);
-    w.c2 = at<__nv_bfloat16>(A, q[3]);
-    w.fc1 = at<__nv_bfloat16>(A, q[4]);
-    w.fc2 = at<__nv_bfloat16>(A, q[5]);
+    const size_t* q = &ob[b * 24];
     w.b_qkv = at<float>(A, q[6]);
     w.qn_w = at<float>(A, q[7]);
     w.qn_b = at<float>(A, q[8]);
@@ -522,30 +689,57 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
     w.b_fc1 = at<float>(A, q[16]);
     w.b_fc2 = at<float>(A, q[17]);
     const long long HH = (long long)H * H;
-    bool ok = !launch_f32_to_bf16(BWp(b, T2W_B_Q_W), w.qkv, HH, st) &&
-              !launch_f32_to_bf16(BWp(b, T2W_B_K_W), w.qkv + HH, HH, st) &&
-              !launch_f32_to_bf16(BWp(b, T2W_B_V_W), w.qkv + 2 * HH, HH, st) &&
-              !launch_f32_to_bf16(BWp(b, T2W_B_PROJ_W), w.proj, HH, st) &&
-              !launch_conv_weight(BWp(b, T2W_B_C1_W), w.c1, H, H, 3, st) &&
-              !launch_conv_weight(BWp(b, T2W_B_C2_W), w.c2, H, H, 3, st) &&
-              !launch_f32_to_bf16(BWp(b, T2W_B_FC1_W), w.fc1, (long long)F * H, st) &&
-              !launch_f32_to_bf16(BWp(b, T2W_B_FC2_W), w.fc2, (long long)H * F, st) &&
-              copyv(w.b_qkv, BWp(b, T2W_B_Q_B), H) && copyv(w.b_qkv + H, BWp(b, T2W_B_K_B), H) &&
+    bool ok = copyv(w.b_qkv, BWp(b, T2W_B_Q_B), H) && copyv(w.b_qkv + H, BWp(b, T2W_B_K_B), H) &&
               copyv(w.b_qkv + 2 * H, BWp(b, T2W_B_V_B), H) && copyv(w.qn_w, BWp(b, T2W_B_QN_W), c.head_dim) &&
               copyv(w.qn_b, BWp(b, T2W_B_QN_B), c.head_dim) && copyv(w.kn_w, BWp(b, T2W_B_KN_W), c.head_dim) &&
               copyv(w.kn_b, BWp(b, T2W_B_KN_B), c.head_dim) && copyv(w.b_proj, BWp(b, T2W_B_PROJ_B), H) &&
               copyv(w.b_c1, BWp(b, T2W_B_C1_B), H) && copyv(w.cln_w, BWp(b, T2W_B_CLN_W), H) &&
               copyv(w.cln_b, BWp(b, T2W_B_CLN_B), H) && copyv(w.b_c2, BWp(b, T2W_B_C2_B), H) &&
               copyv(w.b_fc1, BWp(b, T2W_B_FC1_B), F) && copyv(w.b_fc2, BWp(b, T2W_B_FC2_B), H);
-    if (!ok) return fail(T2W_ERR_CUDA);
-    if (!weight_map(&w.tm_qkv, w.qkv, 3 * H, H) || !weight_map(&w.tm_proj, w.proj, H, H) ||
-        !weight_map(&w.tm_c1, w.c1, H, 3 * H) || !weight_map(&w.tm_c2, w.c2, H, 3 * H) ||
-        !weight_map(&w.tm_fc1, w.fc1, F, H) || !weight_map(&w.tm_fc2, w.fc2, H, F))
-      return fail(T2W_ERR_INVALID);
+    if (!ok) return fail2(T2W_ERR_CUDA);
+    if (fp8) {
+      for (int i = 0; i < 6; ++i) {
+        w.w8[i] = at<uint8_t>(A, q[i]);
+        w.sf8[i] = at<uint8_t>(A, q[18 + i]);
+      }
+      ok = copyv(tmp, BWp(b, T2W_B_Q_W), HH) && copyv(tmp + HH, BWp(b, T2W_B_K_W), HH) &&
+           copyv(tmp + 2 * HH, BWp(b, T2W_B_V_W), HH) &&
+           !launch_quant_weight(tmp, 3 * H, H, w.w8[W8_QKV], w.sf8[W8_QKV], st) &&
+           !launch_quant_weight(BWp(b, T2W_B_PROJ_W), H, H, w.w8[W8_PROJ], w.sf8[W8_PROJ], st) &&
+           !launch_conv_weight_f32(BWp(b, T2W_B_C1_W), tmp, H, H, 3, st) &&
+           !launch_quant_weight(tmp, H, 3 * H, w.w8[W8_C1], w.sf8[W8_C1], st) &&
+           !launch_conv_weight_f32(BWp(b, T2W_B_C2_W), tmp, H, H, 3, st) &&
+           !launch_quant_weight(tmp, H, 3 * H, w.w8[W8_C2], w.sf8[W8_C2], st) &&
+           !launch_quant_weight(BWp(b, T2W_B_FC1_W), F, H, w.w8[W8_FC1], w.sf8[W8_FC1], st) &&
+           !launch_quant_weight(BWp(b, T2W_B_FC2_W), H, F, w.w8[W8_FC2], w.sf8[W8_FC2], st);
+      if (!ok) return fail2(T2W_ERR_CUDA);
+      for (int i = 0; i < 6; ++i)
+        if (!make_tmap_2d(&w.t8[i], w.w8[i], 1, mat_n[i], mat_k[i], mat_k[i], 256, 128)) return fail2(T2W_ERR_INVALID);
+    } else {
+      w.qkv = at<__nv_bfloat16>(A, q[0]);
+      w.proj = at<__nv_bfloat16>(A, q[1]);
+      w.c1 = at<__nv_bfloat16>(A, q[2]);
+      w.c2 = at<__nv_bfloat16>(A, q[3]);
+      w.fc1 = at<__nv_bfloat16>(A, q[4]);
+      w.fc2 = at<__nv_bfloat16>(A, q[5]);
+      ok = !launch_f32_to_bf16(BWp(b, T2W_B_Q_W), w.qkv, HH, st) &&
+           !launch_f32_to_bf16(BWp(b, T2W_B_K_W), w.qkv + HH, HH, st) &&
+           !launch_f32_to_bf16(BWp(b, T2W_B_V_W), w.qkv + 2 * HH, HH, st) &&
+           !launch_f32_to_bf16(BWp(b, T2W_B_PROJ_W), w.proj, HH, st) &&
+           !launch_conv_weight(BWp(b, T2W_B_C1_W), w.c1, H, H, 3, st) &&
+           !launch_conv_weight(BWp(b, T2W_B_C2_W), w.c2, H, H, 3, st) &&
+           !launch_f32_to_bf16(BWp(b, T2W_B_FC1_W), w.fc1, (long long)F * H, st) &&
+           !launch_f32_to_bf16(BWp(b, T2W_B_FC2_W), w.fc2, (long long)H * F, st);
+      if (!ok) return fail2(T2W_ERR_CUDA);
+      if (!weight_map(&w.tm_qkv, w.qkv, 3 * H, H) || !weight_map(&w.tm_proj, w.proj, H, H) ||
+          !weight_map(&w.tm_c1, w.c1, H, 3 * H) || !weight_map(&w.tm_c2, w.c2, H, 3 * H) ||
+          !weight_map(&w.tm_fc1, w.fc1, F, H) || !weight_map(&w.tm_fc2, w.fc2, H, F))
+        return fail2(T2W_ERR_INVALID);
+    }
     ada_w[b] = BWp(b, T2W_B_ADA_W);
     ada_b[b] = BWp(b, T2W_B_ADA_B);
   }
-  if (!weight_map(&s->tm_in, s->w_in, H, 4 * mel) || !weight_map(&s->tm_fin, s->w_fin, mel, H)) return fail(T2W_ERR_INVALID);
+  if (!weight_map(&s->tm_in, s->w_in, H, 4 * mel) || !weight_map(&s->tm_fin, s->w_fin, mel, H)) return fail2(T2W_ERR_INVALID);
 
   // t schedule: the caller's fp32 (t, dt) pairs, else the cosine schedule in double rounded to fp32
   std::vector<float> ts(S);
@@ -575,17 +769,18 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
       cudaMemcpyAsync(s->dts_dev, s->dts.data(), S * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
       cudaMemcpyAsync(fr_dev, freqs.data(), half * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
       cudaMemsetAsync(s->err, 0, 16, st) != cudaSuccess)
-    return fail(T2W_ERR_CUDA);
+    return fail2(T2W_ERR_CUDA);
   const int rc = launch_temb_mods(ts_dev, S, fr_dev, c.freq_dim, c.t_scale, W(T2W_W_TEMB_FC1_W), W(T2W_W_TEMB_FC1_B),
                                   W(T2W_W_TEMB_FC2_W), W(T2W_W_TEMB_FC2_B), H, ada_w.data(), ada_b.data(), c.depth,
                                   W(T2W_W_FINAL_ADA_W), W(T2W_W_FINAL_ADA_B), at<float>(A, o_st), s->mods,
                                   s->final_mods, st);
-  if (rc) return fail(rc);
+  if (rc) return fail2(rc);
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     set_cuda_error(e);
-    return fail(T2W_ERR_CUDA);
+    return fail2(T2W_ERR_CUDA);
   }
+  if (tmp) cudaFree(tmp);
   *out = s;
   return T2W_OK;
 }
@@ -604,14 +799,14 @@ size_t t2w_workspace_bytes(const t2w_solver* s, int32_t n, const int32_t* P, con
   if (!s) return 0;
   Plan pl;
   if (!make_plan(s->cfg, n, P, T, pl)) return 0;
-  return layout(s->cfg, pl).total;
+  return layout(s->cfg, pl, s->precision == T2W_PREC_FP8).total;
 }
 
 int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_bytes, uint32_t flags, void* stream) {
   if (!s || !b || !ws || !b->x0 || !b->mu || !b->cond || !b->spk || !b->out) return T2W_ERR_INVALID;
   Plan pl;
   if (!make_plan(s->cfg, b->n_streams, b->prompt_len, b->chunk_len, pl)) return T2W_ERR_INVALID;
-  if (layout(s->cfg, pl).total > ws_bytes) return T2W_ERR_WORKSPACE;
+  if (layout(s->cfg, pl, s->precision == T2W_PREC_FP8).total > ws_bytes) return T2W_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(ws) & 255) return T2W_ERR_INVALID;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uintptr_t wkey = reinterpret_cast<uintptr_t>(ws);
@@ -666,7 +861,8 @@ int t2w_profile_solve(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_byt
   if (!s || !b || !ws || !ms || !launches || !b->x0 || !b->mu || !b->cond || !b->spk || !b->out) return T2W_ERR_INVALID;
   Plan pl;
   if (!make_plan(s->cfg, b->n_streams, b->prompt_len, b->chunk_len, pl)) return T2W_ERR_INVALID;
-  if (layout(s->cfg, pl).total > ws_bytes || (reinterpret_cast<uintptr_t>(ws) & 255)) return T2W_ERR_WORKSPACE;
+  if (layout(s->cfg, pl, s->precision == T2W_PREC_FP8).total > ws_bytes || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return T2W_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto it = s->ws_meta.find(reinterpret_cast<uintptr_t>(ws));
   if (it == s->ws_meta.end() || it->second != pl.key) T2W_TRY(upload_meta(s, pl, ws, st));
@@ -732,14 +928,92 @@ int t2w_add_ln_mod(float* h, const void* y, const float* g, const float* shift, 
                    int32_t C, void* out, const uint8_t* pad, void* stream) {
   if (!h || !shift || !scale1 || !out) return T2W_ERR_INVALID;
   return launch_add_ln_mod(h, static_cast<const __nv_bfloat16*>(y), g, shift, scale1, eps, rows, C,
-                           static_cast<__nv_bfloat16*>(out), pad, static_cast<cudaStream_t>(stream));
+                           row_out_bf16(static_cast<__nv_bfloat16*>(out)), pad, static_cast<cudaStream_t>(stream));
 }
 
 int t2w_ln_mish(const void* x, const float* w, const float* b, float eps, int32_t rows, int32_t C, void* out,
                 const uint8_t* pad, void* stream) {
   if (!x || !w || !b || !out) return T2W_ERR_INVALID;
-  return launch_ln_mish(static_cast<const __nv_bfloat16*>(x), w, b, eps, rows, C, static_cast<__nv_bfloat16*>(out),
-                        pad, static_cast<cudaStream_t>(stream));
+  return launch_ln_mish(static_cast<const __nv_bfloat16*>(x), w, b, eps, rows, C,
+                        row_out_bf16(static_cast<__nv_bfloat16*>(out)), pad, static_cast<cudaStream_t>(stream));
+}
+
+size_t t2w_e4m3_sf_bytes(int32_t rows, int32_t C) {
+  if (rows <= 0 || C <= 0 || C % 128) return 0;
+  return gemm8_sf_bytes(rows, C);
+}
+
+int t2w_quant_e4m3(const void* x, int32_t rows, int32_t C, void* out, uint8_t* sf, int32_t n_layouts, int64_t layout_bytes,
+                   void* stream) {
+  if (!x || !out || !sf) return T2W_ERR_INVALID;
+  RowOut o;
+  o.out = out;
+  o.sf = sf;
+  o.n_layouts = n_layouts;
+  o.layout_bytes = layout_bytes;
+  return launch_quant_rows(static_cast<const __nv_bfloat16*>(x), rows, C, o, static_cast<cudaStream_t>(stream));
+}
+
+int t2w_quant_weight_e4m3(const float* w, int32_t N, int32_t Kt, void* w8, uint8_t* sf, void* stream) {
+  return launch_quant_weight(w, N, Kt, static_cast<uint8_t*>(w8), sf, static_cast<cudaStream_t>(stream));
+}
+
+int t2w_add_ln_mod_e4m3(float* h, const void* y, const float* g, const float* shift, const float* scale1, float eps,
+                        int32_t rows, int32_t C, void* out, uint8_t* sf, int32_t n_layouts, int64_t layout_bytes,
+                        const uint8_t* pad, void* stream) {
+  if (!h || !shift || !scale1 || !out || !sf) return T2W_ERR_INVALID;
+  RowOut o;
+  o.out = out;
+  o.sf = sf;
+  o.n_layouts = n_layouts;
+  o.layout_bytes = layout_bytes;
+  return launch_add_ln_mod(h, static_cast<const __nv_bfloat16*>(y), g, shift, scale1, eps, rows, C, o, pad,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int t2w_ln_mish_e4m3(const void* x, const float* w, const float* b, float eps, int32_t rows, int32_t C, void* out,
+                     uint8_t* sf, int32_t n_layouts, int64_t layout_bytes, const uint8_t* pad, void* stream) {
+  if (!x || !w || !b || !out || !sf) return T2W_ERR_INVALID;
+  RowOut o;
+  o.out = out;
+  o.sf = sf;
+  o.n_layouts = n_layouts;
+  o.layout_bytes = layout_bytes;
+  return launch_ln_mish(static_cast<const __nv_bfloat16*>(x), w, b, eps, rows, C, o, pad,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int t2w_gemm_e4m3(const void* A8, int32_t lda, int32_t rows_a, const uint8_t* sfa, int32_t sfa_layouts,
+                  int64_t sfa_layout_bytes, const void* W8, const uint8_t* sfw, const float* bias, int32_t M, int32_t N,
+                  int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo, uint8_t* out_sf,
+                  const float* const* qk, float qk_eps, void* stream) {
+  Gemm8Args g;
+  g.A8 = A8;
+  g.lda = lda;
+  g.rows_a = rows_a;
+  g.sfa = sfa;
+  g.sfa_layouts = sfa_layouts;
+  g.sfa_layout = sfa_layout_bytes;
+  g.W8 = W8;
+  g.sfw = sfw;
+  g.bias = bias;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.taps = taps;
+  g.tap_row0 = tap_row0;
+  g.epi = epi;
+  g.out = out;
+  g.ldo = ldo;
+  g.out_sf = out_sf;
+  if (qk) {
+    g.qn_w = qk[0];
+    g.qn_b = qk[1];
+    g.kn_w = qk[2];
+    g.kn_b = qk[3];
+  }
+  g.qk_eps = qk_eps;
+  return launch_gemm8(g, static_cast<cudaStream_t>(stream));
 }
 
 int t2w_gemm(const void* A, int32_t lda, int32_t rows_a, const void* W, const float* bias, int32_t M, int32_t N,
@@ -771,31 +1045,13 @@ int t2w_gemm(const void* A, int32_t lda, int32_t rows_a, const void* W, const fl
 
 int t2w_attn_varlen(const void* qkv, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
                     const int32_t* seq_len, const int32_t* prompt_len, void* out, void* stream) {
-  if (!qkv || !out || !seq_row || !seq_len || !prompt_len || n_seq < 0 || heads <= 0) return T2W_ERR_INVALID;
-  std::vector<AttnWork> work;
-  for (int s = 0; s < n_seq; ++s) {
-    if (seq_len[s] <= 0 || prompt_len[s] < 0 || prompt_len[s] > seq_len[s] || seq_row[s] < 0 ||
-        seq_row[s] + seq_len[s] > rows)
-      return T2W_ERR_INVALID;
-    for (int q = 0; q < seq_len[s]; q += 128)
-      work.push_back(AttnWork{seq_row[s] + q, seq_row[s], q, prompt_len[s], seq_len[s]});
-  }
-  if (work.empty()) return T2W_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  AttnWork* d = nullptr;
-  T2W_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), work.size() * sizeof(AttnWork), st));
-  T2W_CUDA(cudaMemcpyAsync(d, work.data(), work.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st));
-  AttnArgs a;
-  a.qkv = qkv;
-  a.rows = rows;
-  a.heads = heads;
-  a.work = d;
-  a.n_work = (int)work.size();
-  a.out = out;
-  a.scale_log2 = (float)(1.4426950408889634 / 8.0);
-  const int rc = launch_attn(a, st);
-  cudaFreeAsync(d, st);
-  return rc;
+  return attn_varlen_alloc(qkv, rows, heads, n_seq, seq_row, seq_len, prompt_len, out, nullptr, stream);
+}
+
+int t2w_attn_varlen_e4m3(const void* qkv, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
+                         const int32_t* seq_len, const int32_t* prompt_len, void* out, uint8_t* sf, void* stream) {
+  if (!sf) return T2W_ERR_INVALID;
+  return attn_varlen_alloc(qkv, rows, heads, n_seq, seq_row, seq_len, prompt_len, out, sf, stream);
 }
 
 int t2w_euler_cfg(float* x, const float* dphi, int32_t ld_dphi, const int32_t* tok_row, int32_t n_tok, int32_t mel,

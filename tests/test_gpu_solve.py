@@ -121,3 +121,37 @@ def test_workspace_and_bad_shapes_raise(tiny):
     with pytest.raises(T2WError):
         s.solve_packed_dev(lay, z, z, z, torch.zeros(1, TINY.mel, device="cuda"), z,
                            workspace=torch.empty(256, dtype=torch.uint8, device="cuda"))
+
+
+TOL_FP8 = 3e-2
+
+
+def test_fp8_small_config_vs_oracle():
+    """The FP8 path (e4m3 block projections) end to end on a small config whose projections tile by 256."""
+    from b200t2w.config import DiTConfig
+
+    cfg = DiTConfig(hidden=256, depth=2, heads=4)
+    m = dit_oracle.build_model(cfg, seed=0)
+    s = B200Solver(cfg, state_dict_from_module(m), precision="fp8")
+    streams = make_streams(Workload("fp8s", 7, ((60, 20), (33, 17), (130, 40))), cfg.mel)
+    outs = s.solve_streams(streams)
+    s.check()
+    for st, o in zip(streams, outs):
+        ref = dit_oracle.solve_packed(m, st["x0"], st["mu"], st["cond"], st["spk"], st["P"], st["T"])
+        e = rel(o, ref)
+        print(f"fp8 small (P={st['P']}, T={st['T']}): rel-L2 {e:.3e} max-abs {maxabs(o, ref):.3e}")
+        assert e < TOL_FP8
+
+
+def test_fp8_c1_full_size_vs_golden(ref, golden_dir):
+    """Reference config on the FP8 path against the reference driver's fp32 chunk mel."""
+    m, _ = ref
+    s = B200Solver(REFERENCE, state_dict_from_module(m), precision="fp8")
+    rec = torch.load(os.path.join(golden_dir, "c1_reference.pt"))
+    st = make_streams(C1)[0]
+    out = s.solve_streams([st])[0]
+    s.check()
+    g = rec["streams"][0]
+    e = rel(out[:, st["P"]:], g["ref_chunk_mel"])
+    print(f"C1 FP8 chunk mel rel-L2 {e:.3e} max-abs {maxabs(out[:, st['P']:], g['ref_chunk_mel']):.3e}")
+    assert e < TOL_FP8

@@ -12,7 +12,10 @@ Two halves:
    (``engine/runtime/token2wav_batch.py:82-110,781-810``; ``engine/runtime/dit_fast.py:107-178``), so the reference's
    own driver (``BatchedToken2Wav._solve`` / ``_estimator_temb`` / ``_block_chunk`` / ``_conv_block_chunk``) runs
    unmodified on them; ``tests/golden/make_golden.py`` does exactly that to pin this oracle.
-2. ``solve_packed``: the CFG Euler solve of packed ``[prompt | chunk]`` rows.  The reference solves the prompt alone
+2. ``solve_packed``: the CFG Euler solve of packed ``[prompt | chunk]`` rows.  ``solve_window``: the steady-state form,
+   one window of a stream against its estimator caches (keys ``[new, cache]``, two cached conv frames, the cache
+   trimmed to the prompt's frames plus the last 100 after every kept window), as ``BatchedToken2Wav._solve`` and
+   ``_flow_finish`` do it (``token2wav_batch.py:33-39,388-395,632-702``).  The reference solves the prompt alone
    first (``Flow.setup_cache``: all prompt frames attend each other, conv caches start at zero,
    ``token2wav_batch.py:551-553``) and then the chunk against the prompt's cached keys and conv frames of the same
    (step, block) (``token2wav_batch.py:632-702``).  The DiT has no positional encoding (``dit_fast.py:5-6``), so one
@@ -267,6 +270,88 @@ def solve_streams(model: CFM, streams: list[dict], threads: int | None = None) -
     if threads:
         torch.set_num_threads(threads)
     return [solve_packed(model, s["x0"], s["mu"], s["cond"], s["spk"], s["P"], s["T"]) for s in streams]
+
+
+TRIM_SUFFIX = 100
+
+
+class StreamCache:
+    """One request's estimator caches in the reference's layout (both CFG rows): ``att`` [S, depth, 2, heads, L,
+    2 * head_dim] (K then V on the last dim, keys in ``[new, cache]`` order) and ``cnn`` [S, depth, 2, 2H, 2] (the two
+    frames before the next window of each conv's input); ``keep`` is the trim length (the prompt's mel frames)."""
+
+    def __init__(self, cfg: DiTConfig, keep: int = 0):
+        self.att = torch.zeros(cfg.steps, cfg.depth, 2, cfg.heads, 0, 2 * cfg.head_dim)
+        self.cnn = torch.zeros(cfg.steps, cfg.depth, 2, 2 * cfg.hidden, 2)
+        self.keep = keep
+
+    @property
+    def length(self) -> int:
+        return self.att.shape[4]
+
+
+def trim(att: torch.Tensor, keep: int) -> torch.Tensor:
+    """The reference's cache trim (``token2wav_batch.py:36-39``): over ``keep + 100`` keys, keep the first ``keep`` and
+    the last 100."""
+    L = att.shape[4]
+    if L > keep + TRIM_SUFFIX:
+        return torch.cat([att[:, :, :, :, :keep], att[:, :, :, :, L - TRIM_SUFFIX:]], dim=4)
+    return att
+
+
+def _conv_cached(conv: nn.Conv1d, x: torch.Tensor, cache: torch.Tensor):
+    """A causal conv over ``[cached frames | window]``; returns (output [b, C, T], new cache = the last k - 1 frames)."""
+    full = torch.cat([cache, x], dim=2)
+    k1 = conv.kernel_size[0] - 1
+    return F.conv1d(full, conv.weight, conv.bias), full[:, :, full.shape[2] - k1:]
+
+
+@torch.inference_mode()
+def solve_window(model: CFM, cache: StreamCache, x0, mu, spk, cond=None, keep_cache: bool = True) -> torch.Tensor:
+    """One window of ``T`` frames of one stream: the CFG Euler solve against the stream's caches.
+
+    x0, mu, cond: [mel, T] fp32 (cond None: zeros); spk: [mel].  Returns the window's mel [mel, T].  With
+    ``keep_cache`` the caches become the window's new ones (keys ``[new, old]`` trimmed as the reference trims them,
+    conv caches the last two input frames of each conv); otherwise (a final flush) they are left unchanged.  The
+    caller takes x0 from the flow's fixed noise at the stream's cache length, as the reference does
+    (``token2wav_batch.py:668``)."""
+    est = model.estimator
+    cfg = est.cfg
+    w = float(model.inference_cfg_rate)
+    H, T = cfg.hidden, x0.shape[1]
+    x = x0.float()[None]
+    mu_in = torch.stack([mu, torch.zeros_like(mu)]).float()
+    spk_in = torch.stack([spk, torch.zeros_like(spk)]).float()
+    c_in = torch.zeros_like(mu_in) if cond is None else torch.stack([cond, torch.zeros_like(cond)]).float()
+    new_att, new_cnn = [], []
+    ts, dts = t_schedule(cfg.steps)
+    for step, (t, dt) in enumerate(zip(ts, dts)):
+        temb = est.t_embedder(torch.full((2,), t, dtype=torch.float32)).unsqueeze(1)
+        xx = x.expand(2, -1, -1)
+        h = est.in_proj(torch.cat([xx, mu_in, spk_in[:, :, None].expand(-1, -1, T), c_in], dim=1).transpose(1, 2))
+        att_s, cnn_s = [], []
+        for b, blk in enumerate(est.blocks):
+            sh_a, sc_a, g_a, sh_m, sc_m, g_m, sh_c, sc_c, g_c = blk.adaLN_modulation(temb).chunk(9, dim=-1)
+            y, na = blk.attn.forward_chunk(modulate(blk.norm1(h), sh_a, sc_a), cache.att[step, b])
+            h = h + g_a * y
+            att_s.append(na)
+            cb = blk.conv.block
+            c1, c2 = cache.cnn[step, b].split(H, dim=1)
+            a = modulate(blk.norm3(h), sh_c, sc_c).transpose(1, 2)
+            y, n1 = _conv_cached(cb[1], a, c1)
+            y = cb[4](cb[3](y.transpose(1, 2))).transpose(1, 2)
+            y, n2 = _conv_cached(cb[6], y, c2)
+            h = h + g_c * y.transpose(1, 2)
+            cnn_s.append(torch.cat([n1, n2], dim=1))
+            h = h + g_m * blk.mlp(modulate(blk.norm2(h), sh_m, sc_m))
+        v = est.final_layer(h, temb).transpose(1, 2)
+        x = x + torch.tensor(dt, dtype=torch.float32) * ((1.0 + w) * v[0:1] - w * v[1:2])
+        new_att.append(torch.stack(att_s))
+        new_cnn.append(torch.stack(cnn_s))
+    if keep_cache:
+        cache.att = trim(torch.stack(new_att), cache.keep)
+        cache.cnn = torch.stack(new_cnn)
+    return x[0].float()
 
 
 def state_dict_np(model: CFM) -> dict:

@@ -16,6 +16,12 @@ What it does, per fixture stream ``(P, T)``:
 3. Runs the oracle's packed solve ``solve_packed`` over ``[prompt | chunk]`` and asserts both agree (fp32, CPU).
 4. Writes ``tests/golden/*.pt``: the reference driver's outputs (prompt and chunk mel), the inputs' and weights'
    digests, and for the tiny config the inputs themselves.
+
+``steady_tiny.pt`` pins the steady-state form: per stream, the prompt setup and then a run of windows through the
+reference's ``_solve`` with ``keep_cache`` (and, for a final flush, without), trimming the estimator's key cache after
+every kept window with the reference's own ``_trim`` (``token2wav_batch.py:36-39``, as ``_flow_finish`` does with the
+prompt's mel frames as ``keep``).  The windows are long enough for the trim to evict keys.  The oracle's
+``solve_window`` is checked against it.
 """
 
 from __future__ import annotations
@@ -106,6 +112,57 @@ def make(cfg, workload: Workload, name: str, keep_inputs: bool) -> None:
     torch.save(rec, os.path.join(HERE, f"{name}.pt"))
 
 
+def reference_windows(model, P: int, windows: list, seed: int) -> dict:
+    """One stream through the reference driver: setup over the prompt, then ``windows`` = [(T, keep_cache), ...]."""
+    from engine.models.token2wav import StreamState
+    from engine.runtime.token2wav_batch import BatchedToken2Wav, _trim
+
+    cfg = model.estimator.cfg
+    g = torch.Generator().manual_seed(seed)
+    bt = BatchedToken2Wav.__new__(BatchedToken2Wav)
+    bt.flow = SimpleNamespace(decoder=model)
+    bt.t2w = SimpleNamespace(n_timesteps=cfg.steps)
+    bt.graphs = bt.euler = None
+    st = StreamState(prompt=None, flow_cache={
+        "estimator_cnn_cache": torch.zeros(cfg.steps, cfg.depth, 2, 2 * cfg.hidden, 2),
+        "estimator_att_cache": torch.zeros(cfg.steps, cfg.depth, 2, cfg.heads, 0, 2 * cfg.head_dim)}, hift_cache={})
+    spk = torch.randn(cfg.mel, generator=g)
+    out = {"P": P, "spk": spk, "windows": []}
+    for wi, (T, keep) in enumerate([(P, True)] + list(windows)):
+        mu = torch.randn(cfg.mel, T, generator=g)
+        cond = torch.randn(cfg.mel, T, generator=g) if wi == 0 else None
+        o = st.flow_cache["estimator_att_cache"].shape[4]
+        x0 = model.rand_noise[0, :, o:o + T].clone()
+        with torch.inference_mode():
+            mel = bt._solve([st], mu[None].contiguous(), spk[None], cond=None if cond is None else cond[None].contiguous(),
+                            keep_cache=keep)[0]
+            if keep:
+                st.flow_cache["estimator_att_cache"] = _trim(st.flow_cache["estimator_att_cache"], P, 4)
+        out["windows"].append({"T": T, "keep": keep, "offset": o, "x0": x0, "mu": mu, "cond": cond, "ref_mel": mel.clone(),
+                               "cache_len_after": st.flow_cache["estimator_att_cache"].shape[4]})
+    return out
+
+
+def make_steady() -> None:
+    cfg = TINY
+    model = dit_oracle.build_model(cfg, seed=0, noise_frames=2048)
+    plans = [(20, [(12, True), (30, True), (41, True), (7, True), (25, False)], 11),
+             (9, [(5, True), (1, True), (33, True), (40, True), (50, True), (2, False)], 12),
+             (64, [(50, True), (50, True), (3, True)], 13)]
+    rec = {"config": cfg.to_dict(), "weights_digest": weights_digest(model), "streams": []}
+    for P, windows, seed in plans:
+        s = reference_windows(model, P, windows, seed)
+        cache = dit_oracle.StreamCache(cfg, keep=P)
+        for w in s["windows"]:
+            mel = dit_oracle.solve_window(model, cache, w["x0"], w["mu"], s["spk"], w["cond"], keep_cache=w["keep"])
+            e = rel(mel, w["ref_mel"])
+            print(f"steady P={P} T={w['T']} keep={w['keep']} offset={w['offset']} cache after={w['cache_len_after']}: "
+                  f"oracle vs reference rel-L2 {e:.2e}")
+            assert e < 1e-5 and cache.length == w["cache_len_after"], (e, cache.length)
+        rec["streams"].append(s)
+    torch.save(rec, os.path.join(HERE, "steady_tiny.pt"))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("T2W_REFERENCE", "/root/reference"))
@@ -115,6 +172,7 @@ def main() -> None:
     install_shim()
     torch.set_num_threads(os.cpu_count() or 1)
     make(TINY, Workload("tiny_ragged", 7, ((24, 10), (17, 13), (3, 1), (1, 6))), "tiny_ragged", keep_inputs=True)
+    make_steady()
     if not a.skip_full:
         make(REFERENCE, C1, "c1_reference", keep_inputs=False)
 

@@ -41,6 +41,26 @@ def test_oracle_c1_full_size_matches_reference_driver(golden_dir):
     _check_fixture(os.path.join(golden_dir, "c1_reference.pt"), REFERENCE, lambda rec: make_streams(C1))
 
 
+def test_oracle_steady_windows_match_reference_driver(golden_dir):
+    """Steady state: the prompt setup then runs of windows against the caches, with the reference's trim (first P plus
+    the last 100 keys) and final flushes that leave the caches untouched."""
+    rec = torch.load(os.path.join(golden_dir, "steady_tiny.pt"))
+    assert DiTConfig(**rec["config"]) == TINY
+    model = dit_oracle.build_model(TINY, seed=0, noise_frames=2048)
+    assert weights_digest(model) == rec["weights_digest"]
+    trimmed = False
+    for s in rec["streams"]:
+        cache = dit_oracle.StreamCache(TINY, keep=s["P"])
+        for w in s["windows"]:
+            assert torch.equal(w["x0"], model.rand_noise[0, :, cache.length:cache.length + w["T"]])
+            before = cache.length
+            mel = dit_oracle.solve_window(model, cache, w["x0"], w["mu"], s["spk"], w["cond"], keep_cache=w["keep"])
+            assert rel(mel, w["ref_mel"]) < 1e-5
+            assert cache.length == w["cache_len_after"]
+            trimmed |= w["keep"] and cache.length < before + w["T"]
+    assert trimmed, "the fixture must exercise the trim"
+
+
 def test_block_causal_mask():
     m = dit_oracle.block_causal_mask(3, 2)
     assert m.shape == (5, 5)

@@ -122,6 +122,44 @@ T2W_API size_t t2w_workspace_bytes(const t2w_solver* s, int32_t n_streams, const
 T2W_API int t2w_solve_packed(t2w_solver* s, const t2w_batch* batch, void* workspace, size_t workspace_bytes, uint32_t flags,
                      void* stream);
 
+/* ---- Steady-state (slot-pool) solve: the production form of the same estimator (FastDiT.solve,
+ * engine/runtime/dit_fast.py:432-495).  Every cached key frame of a CFG row is one slot of a pool holding K and V of
+ * each (step, block); a call solves one window of T_i frames per request against each CFG row's key list (its cached
+ * slots followed by the window's new slots, which the call fills), and each CFG row's two cached conv frames per
+ * (step, block, conv) sit in a conv-cache row slot.  Slot allocation, the [new, cache] order and the trim to the
+ * prompt's frames + 100 stay with the caller (host bookkeeping, as the reference's SlotPool / FastCache). */
+typedef struct t2w_slots t2w_slots;
+
+typedef struct t2w_slot_batch {
+  int32_t n_streams;       /* requests n */
+  const int32_t* chunk_len; /* host [n] window frames T_i > 0 */
+  const int32_t* kv_len;    /* host [2n] keys of CFG row r (cond rows 0..n-1, then uncond rows): cached + T_i new */
+  const int32_t* kv_idx;    /* host: the 2n key lists (pool slots) concatenated; each ends with its T_i new slots */
+  const int32_t* cnn_rd;    /* host [2n] conv-cache row slot each CFG row reads */
+  const int32_t* cnn_wr;    /* host [2n] row slot that receives its new conv frames (== rd keeps them) */
+  const float* x0;          /* device [sum T, mel] (the flow's fixed noise at each request's cache length) */
+  const float* mu;          /* device [sum T, mel] */
+  const float* cond;        /* device [sum T, mel] or NULL (zeros) */
+  const float* spk;         /* device [n, mel] */
+  float* out;               /* device [sum T, mel]: each window's mel, token-major */
+} t2w_slot_batch;
+
+/* Pools for n_slots key slots and n_rowslots conv-cache row slots on the current device (zeroed):
+ * steps * depth * (n_slots * 4 * hidden + n_rowslots * 8 * hidden) bytes. */
+T2W_API int t2w_slots_create(const t2w_solver* s, int32_t n_slots, int32_t n_rowslots, t2w_slots** out);
+T2W_API int t2w_slots_destroy(t2w_slots* p);
+/* K / V of every (step, block): slot src[i] -> dst[i] (host arrays; FastDiT.clone, dit_fast.py:204-216). */
+T2W_API int t2w_slots_copy(t2w_slots* p, const int32_t* src, const int32_t* dst, int32_t n, void* stream);
+/* Conv caches of every (step, block): row slot src -> dst, or zeros into dst when src < 0 (FastDiT.new_cache). */
+T2W_API int t2w_slots_copy_row(t2w_slots* p, int32_t src, int32_t dst, void* stream);
+/* Workspace bytes of a t2w_solve_slots call (0 on an invalid batch). */
+T2W_API size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_slot_batch* b);
+/* The S-step CFG Euler solve of one window per request against the pools (bf16 path).  Attention gathers each CFG
+ * row's key list from the pool; the causal convs read the row's cached frames in front of its window.  Asynchronous
+ * on `stream`; the host arrays are read before the call returns.  flags: reserved (0). */
+T2W_API int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* workspace, size_t workspace_bytes,
+                            uint32_t flags, void* stream);
+
 /* Kernel classes of t2w_profile_solve. */
 enum t2w_kernel_class {
   T2W_KC_PACK = 0,   /* input packing (CFG rows) */

@@ -4,7 +4,8 @@ solver interface.  The arithmetic lives in ``libt2w_b200.so`` (hand-written sm_1
 
 from .config import REFERENCE, TINY, DiTConfig, t_schedule  # noqa: F401
 
-__all__ = ["DiTConfig", "REFERENCE", "TINY", "t_schedule", "B200Solver", "Layout", "state_dict_from_module"]
+__all__ = ["DiTConfig", "REFERENCE", "TINY", "t_schedule", "B200Solver", "Layout", "state_dict_from_module",
+           "B200FastDiT", "FastCache"]
 
 
 def __getattr__(name):
@@ -12,4 +13,8 @@ def __getattr__(name):
         from . import solver
 
         return getattr(solver, name)
+    if name in ("B200FastDiT", "FastCache"):
+        from . import fastdit
+
+        return getattr(fastdit, name)
     raise AttributeError(name)

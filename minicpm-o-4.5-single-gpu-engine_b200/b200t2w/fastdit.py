@@ -1,0 +1,189 @@
+"""Steady-state Token2Wav solve on B200: the drop-in for the reference's ``FastDiT`` (engine/runtime/dit_fast.py).
+
+The reference keeps every CFG row's cached key frames in a slot pool (FlashInfer paged K/V, page size 1) and its two
+conv-cache frames per (step, block) in a row-slot pool; a call solves one window per request against those caches,
+appends the window's keys (``[new, cache]`` order) and trims the cache to the prompt's frames plus the last 100
+(``dit_fast.py:58-97,432-495``, ``token2wav_batch.py:33-39``).  ``B200FastDiT`` keeps that host bookkeeping (slot ids,
+the reference's key order, the trim) in Python, as the reference does, and runs the solve in the CUDA library
+(``t2w_solve_slots``): pools on the device, attention gathering each row's key list, conv caches filled in front of
+each window.  Method names and argument meaning follow ``FastDiT``: ``new_cache``, ``release``, ``clone``, ``solve``,
+``counts``, ``pool.in_use()``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import lib as L
+from .solver import B200Solver
+
+TRIM_SUFFIX = 100
+
+
+class SlotIds:
+    """Host free list of pool slot ids (the reference's ``SlotPool`` bookkeeping, ``dit_fast.py:58-78``)."""
+
+    def __init__(self, n: int):
+        self.n = n
+        self.free = list(range(n - 1, -1, -1))
+
+    def alloc(self, k: int) -> list:
+        if k > len(self.free):
+            raise RuntimeError(f"Token2Wav cache pool exhausted ({k} slots wanted, {len(self.free)} free of {self.n})")
+        out = self.free[len(self.free) - k:][::-1] if k else []
+        del self.free[len(self.free) - k:]
+        return out
+
+    def release(self, ids: list) -> None:
+        self.free.extend(ids)
+
+    def in_use(self) -> int:
+        return self.n - len(self.free)
+
+
+@dataclass
+class FastRow:
+    """One CFG row's caches: key slots in the reference's tensor order and its conv-cache row slot."""
+    order: list = field(default_factory=list)
+    cnn: int = -1
+
+
+@dataclass
+class FastCache:
+    """A request's estimator caches (conditional and unconditional rows) and its trim length (prompt mel frames)."""
+    rows: tuple
+    keep: int = 0
+
+    @property
+    def length(self) -> int:
+        return len(self.rows[0].order)
+
+
+class B200FastDiT:
+    """``FastDiT`` on the B200 kernels.
+
+    ``solver``: a bf16 ``B200Solver`` (weights, modulation tables).  ``noise``: the flow's fixed noise [mel, frames]
+    (``cfm.rand_noise[0]``), read at each request's cache length.  ``n_slots``: key slots (each holds K and V of every
+    (step, block) of one frame: steps * depth * 4 * hidden bytes).  ``max_streams``: concurrent requests (two
+    conv-cache row slots each)."""
+
+    def __init__(self, solver: B200Solver, noise: torch.Tensor, n_slots: int = 32768, max_streams: int = 96):
+        if solver.precision != "bf16":
+            raise ValueError("the slot-pool solve runs the bf16 path")
+        self.solver, self.cfg, self.device = solver, solver.cfg, solver.device
+        self.noise = noise.detach().to(self.device, torch.float32).contiguous()
+        self._lib = L.load()
+        n_rs = 2 * max_streams + 1  # + one scratch row slot: the write target of rows that keep nothing
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            L.call("t2w_slots_create", solver._h, n_slots, n_rs, ctypes.byref(h))
+        self._p = h
+        self.pool = SlotIds(n_slots)
+        self.cnn_free = list(range(n_rs - 1, 0, -1))
+        self.cnn_scratch = 0
+        self._ws = None
+        self.counts = {"graph": 0, "eager": 0}
+
+    def close(self) -> None:
+        if getattr(self, "_p", None) is not None and self._p.value:
+            self._lib.t2w_slots_destroy(self._p)
+            self._p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    # --- caches -------------------------------------------------------------------------------------------------------
+    def new_cache(self) -> FastCache:
+        if len(self.cnn_free) < 2:
+            raise RuntimeError("Token2Wav conv-cache row slots exhausted")
+        rows = (FastRow(cnn=self.cnn_free.pop()), FastRow(cnn=self.cnn_free.pop()))
+        for r in rows:
+            L.call("t2w_slots_copy_row", self._p, -1, r.cnn, self._stream())
+        return FastCache(rows)
+
+    def release(self, c: FastCache) -> None:
+        for r in c.rows:
+            self.pool.release(r.order)
+            r.order = []
+            if r.cnn >= 0:
+                self.cnn_free.append(r.cnn)
+                r.cnn = -1
+
+    def clone(self, c: FastCache) -> FastCache:
+        """An independent copy (new slots holding the same keys and values, copied conv caches)."""
+        out = self.new_cache()
+        out.keep = c.keep
+        for src, dst in zip(c.rows, out.rows):
+            L.call("t2w_slots_copy_row", self._p, src.cnn, dst.cnn, self._stream())
+            dst.order = self.pool.alloc(len(src.order))
+            if src.order:
+                L.call("t2w_slots_copy", self._p, L.i32_array(src.order), L.i32_array(dst.order), len(src.order),
+                       self._stream())
+        return out
+
+    # --- solve --------------------------------------------------------------------------------------------------------
+    @torch.inference_mode()
+    def solve(self, caches: list, mu: list, spks: torch.Tensor, cond: list | None, keep: list) -> list:
+        """One window per request (``FastDiT.solve``): ``mu[i]`` [mel, T_i], ``spks`` [n, mel] (after the affine
+        layer), ``cond[i]`` [mel, T_i] or None (zeros; ``cond`` None: zeros for all).  Requests with ``keep[i]`` keep
+        the window's keys and conv caches, trimmed as the reference trims them; the others (final flushes) leave their
+        caches untouched.  Returns each request's mel [mel, T_i] fp32."""
+        n = len(caches)
+        mel = self.cfg.mel
+        Ts = [int(m.shape[1]) for m in mu]
+        lens = [c.length for c in caches]
+        rows = [c.rows[0] for c in caches] + [c.rows[1] for c in caches]
+        new = [self.pool.alloc(t) for t in Ts + Ts]
+        kv_len, kv_idx, rd, wr = [], [], [], []
+        for r in range(2 * n):
+            i = r % n
+            lst = rows[r].order + new[r]  # attention depends on the key set; the window's slots go last
+            kv_len.append(len(lst))
+            kv_idx += lst
+            rd.append(rows[r].cnn)
+            wr.append(rows[r].cnn if keep[i] else self.cnn_scratch)
+        dev = self.device
+        x0 = torch.cat([self.noise[:, o:o + t].t() for o, t in zip(lens, Ts)]).contiguous()
+        mu_t = torch.cat([m.t() for m in mu]).to(dev, torch.float32).contiguous()
+        cond_t = None
+        if cond is not None:
+            cond_t = torch.cat([(c.t() if c is not None else torch.zeros(t, mel)).to(dev, torch.float32)
+                                for c, t in zip(cond, Ts)]).contiguous()
+        spk = spks.to(dev, torch.float32).contiguous()
+        out = torch.empty(sum(Ts), mel, device=dev)
+        P = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
+        arrs = [L.i32_array(a) for a in (Ts, kv_len, kv_idx, rd, wr)]  # alive until the call returns
+        ip = [ctypes.cast(a, ctypes.POINTER(ctypes.c_int32)) for a in arrs]
+        b = L.SlotBatch(n, *ip, P(x0), P(mu_t), P(cond_t), P(spk), P(out))
+        need = int(self._lib.t2w_slot_workspace_bytes(self.solver._h, self._p, ctypes.byref(b)))
+        if not need:
+            raise L.T2WError("t2w_slot_workspace_bytes", -1)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        L.call("t2w_solve_slots", self.solver._h, self._p, ctypes.byref(b), P(self._ws), need, 0, self._stream())
+        self.counts["eager"] += 1
+        # the reference's cache order and trim (dit_fast.py:482-490)
+        for i, c in enumerate(caches):
+            for r, nw in ((rows[i], new[i]), (rows[n + i], new[n + i])):
+                if keep[i]:
+                    order = nw + r.order
+                    if len(order) > c.keep + TRIM_SUFFIX:
+                        self.pool.release(order[c.keep:len(order) - TRIM_SUFFIX])
+                        order = order[:c.keep] + order[len(order) - TRIM_SUFFIX:]
+                    r.order = order
+                else:
+                    self.pool.release(nw)
+        res, o = [], 0
+        for t in Ts:
+            res.append(out[o:o + t].t().float())
+            o += t
+        return res

@@ -50,6 +50,12 @@ class Batch(ctypes.Structure):
                 ("cond", ctypes.c_void_p), ("spk", ctypes.c_void_p), ("out", ctypes.c_void_p)]
 
 
+class SlotBatch(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_int32)] + \
+               [(n, ctypes.POINTER(ctypes.c_int32)) for n in ("chunk_len", "kv_len", "kv_idx", "cnn_rd", "cnn_wr")] + \
+               [(n, ctypes.c_void_p) for n in ("x0", "mu", "cond", "spk", "out")]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _F = ctypes.c_float
@@ -76,6 +82,12 @@ _SIGS = {
     "t2w_attn_varlen_noalloc": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P],
                                 ctypes.c_int),
     "t2w_euler_cfg": ([_P, _P, _I, _P, _I, _I, _I, _F, _F, _P, _I, _P, _P], ctypes.c_int),
+    "t2w_slots_create": ([_P, _I, _I, ctypes.POINTER(_P)], ctypes.c_int),
+    "t2w_slots_destroy": ([_P], ctypes.c_int),
+    "t2w_slots_copy": ([_P, ctypes.POINTER(_I), ctypes.POINTER(_I), _I, _P], ctypes.c_int),
+    "t2w_slots_copy_row": ([_P, _I, _I, _P], ctypes.c_int),
+    "t2w_slot_workspace_bytes": ([_P, _P, ctypes.POINTER(SlotBatch)], ctypes.c_size_t),
+    "t2w_solve_slots": ([_P, _P, ctypes.POINTER(SlotBatch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
     "t2w_e4m3_sf_bytes": ([_I, _I], ctypes.c_size_t),
     "t2w_quant_e4m3": ([_P, _I, _I, _P, _P, _I, ctypes.c_int64, _P], ctypes.c_int),
     "t2w_quant_weight_e4m3": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),

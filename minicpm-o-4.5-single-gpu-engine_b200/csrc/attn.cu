@@ -53,7 +53,21 @@ struct DevArgs {
   int ldo;
   float scale_log2;
   int* err;
+  // gathered keys (slot-pool form): key j of an item is row kv_idx[w.k_row + j] of the pool, K at column h * 64 and V
+  // at column heads * 64 + h * 64 of a row of pool_ld bf16
+  const __nv_bfloat16* pool;
+  const int* kv_idx;
+  int pool_ld;
 };
+
+// 16-byte global -> shared copy (zero-filled when src_bytes == 0) and the arrival of this thread's outstanding copies
+// on an mbarrier (counted against the barrier's expected arrivals).
+T2W_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+T2W_DEV void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 struct PipeBars {
   uint64_t q_full, q_free, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2], o_done[2], o_free;
@@ -82,12 +96,15 @@ T2W_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint3
       : "memory");
 }
 
+// Key tiles of an item.  Packed form: prompt queries see P keys, chunk queries L.  Gathered form (GATHER): the
+// window's P queries each see all L keys of the row's list.
+template <bool GATHER>
 T2W_DEV int item_tiles(const AttnWork& w) {
-  const int kmax = (w.q_pos + kQTile > w.P) ? w.L : w.P;  // any chunk query in the tile sees every key
+  const int kmax = GATHER ? w.L : ((w.q_pos + kQTile > w.P) ? w.L : w.P);  // any chunk query in the tile sees every key
   return (kmax + kKTile - 1) / kKTile;
 }
 
-template <bool E4M3>
+template <bool E4M3, bool GATHER>
 __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtensorMap tm_q,
                                                  const __grid_constant__ CUtensorMap tm_kv, const DevArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -107,7 +124,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       mbar_init(&b.q_full, 1);
       mbar_init(&b.q_free, 1);
       for (int s = 0; s < kStages; ++s) {
-        mbar_init(&b.kv_full[s], 1);
+        mbar_init(&b.kv_full[s], GATHER ? 32 : 1);  // gathered: one cp.async arrival per producer lane
         mbar_init(&b.kv_empty[s], 1);
       }
       for (int s = 0; s < 2; ++s) {
@@ -132,7 +149,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       ItemEntry e;
       e.w = p.work[item / p.heads];
       e.h = item % p.heads;
-      e.n_kt = item_tiles(e.w);
+      e.n_kt = item_tiles<GATHER>(e.w);
       items[i] = e;
     }
   }
@@ -143,26 +160,69 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 2) {
-    if (lane == 0) {  // TMA producer of pipeline q
-      const int q = warp;
-      PipeBars& b = bars[q];
-      uint8_t* base = smem + q * kPipeBytes;
+    const int q = warp;
+    PipeBars& b = bars[q];
+    uint8_t* base = smem + q * kPipeBytes;
+    if constexpr (!GATHER) {
+      if (lane == 0) {  // TMA producer of pipeline q
+        int t = 0;
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+          if (q + 2 * (int)blockIdx.x + k * stride >= p.n_items) break;
+          const ItemEntry e = items[2 * k + q];
+          // the previous item's last S MMA has read the Q buffer
+          if (!(ok = mbar_wait(&b.q_free, (k & 1) ^ 1u, p.err))) break;
+          mbar_expect_tx(&b.q_full, kQBytes);
+          tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+          for (int j = 0; j < e.n_kt; ++j, ++t) {
+            const int st = t % kStages;
+            if (!(ok = mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err))) break;
+            uint8_t* kv = base + kQBytes + st * 2 * kKVBytes;
+            mbar_expect_tx(&b.kv_full[st], 2 * kKVBytes);
+            tma_load_2d(kv, &tm_kv, H + e.h * kD, e.w.k_row + j * kKTile, &b.kv_full[st]);
+            tma_load_2d(kv + kKVBytes, &tm_kv, 2 * H + e.h * kD, e.w.k_row + j * kKTile, &b.kv_full[st]);
+          }
+        }
+      }
+    } else {
+      // gathered K / V: the whole warp copies each 64-key tile from the slot pool with 16-byte cp.async, placing rows
+      // in the 128-byte-swizzled layout the TMA tiles have (chunk c of row r at chunk c ^ (r % 8)); keys past the
+      // row's list are zero-filled
       int t = 0;
       bool ok = true;
       for (int k = 0; ok; ++k) {
         if (q + 2 * (int)blockIdx.x + k * stride >= p.n_items) break;
         const ItemEntry e = items[2 * k + q];
-        // the previous item's last S MMA has read the Q buffer
-        if (!(ok = mbar_wait(&b.q_free, (k & 1) ^ 1u, p.err))) break;
-        mbar_expect_tx(&b.q_full, kQBytes);
-        tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+        if (lane == 0) {
+          if ((ok = mbar_wait(&b.q_free, (k & 1) ^ 1u, p.err))) {
+            mbar_expect_tx(&b.q_full, kQBytes);
+            tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+          }
+        }
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        const __nv_bfloat16* kcol = p.pool + e.h * kD;
+        const __nv_bfloat16* vcol = p.pool + H + e.h * kD;
         for (int j = 0; j < e.n_kt; ++j, ++t) {
           const int st = t % kStages;
-          if (!(ok = mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err))) break;
-          uint8_t* kv = base + kQBytes + st * 2 * kKVBytes;
-          mbar_expect_tx(&b.kv_full[st], 2 * kKVBytes);
-          tma_load_2d(kv, &tm_kv, H + e.h * kD, e.w.k_row + j * kKTile, &b.kv_full[st]);
-          tma_load_2d(kv + kKVBytes, &tm_kv, 2 * H + e.h * kD, e.w.k_row + j * kKTile, &b.kv_full[st]);
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err)))) break;
+          const uint32_t ks = smem_u32(base + kQBytes + st * 2 * kKVBytes), vs = ks + kKVBytes;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int r = lane + 32 * half;
+            const int key = j * kKTile + r;
+            const bool valid = key < e.w.L;
+            const size_t slot = valid ? (size_t)__ldg(p.kv_idx + e.w.k_row + key) : 0;
+            const __nv_bfloat16* ksrc = kcol + slot * p.pool_ld;
+            const __nv_bfloat16* vsrc = vcol + slot * p.pool_ld;
+            const uint32_t nb = valid ? 16u : 0u;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint32_t off = r * 128 + ((c ^ (r & 7)) << 4);
+              cp_async16(ks + off, ksrc + 8 * c, nb);
+              cp_async16(vs + off, vsrc + 8 * c, nb);
+            }
+          }
+          cp_async_arrive_noinc(&b.kv_full[st]);
         }
       }
     }
@@ -185,6 +245,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       auto issue_s = [&]() -> bool {
         if (js == 0 && !mbar_wait(&b.q_full, ks & 1, p.err)) return false;
         if (!mbar_wait(&b.kv_full[ts % kStages], (ts / kStages) & 1, p.err)) return false;
+        if constexpr (GATHER) fence_proxy_async_smem();  // cp.async wrote the tile through the generic proxy
         tc_fence_after();
         const uint32_t q0 = smem_u32(base), k0 = smem_u32(base + kQBytes + (ts % kStages) * 2 * kKVBytes);
         const uint32_t sbuf = preg + 64 * (ts & 1);
@@ -239,7 +300,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       const int h = items[2 * k + q].h;
       const int n_kt = items[2 * k + q].n_kt;
       const int pos = w.q_pos + r;
-      const int lim = pos < w.P ? w.P : (pos < w.L ? w.L : 0);
+      const int lim = GATHER ? (pos < w.P ? w.L : 0) : (pos < w.P ? w.P : (pos < w.L ? w.L : 0));
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_kt; ++j, ++t) {
         // warp-uniform: tcgen05.ld / st below are .sync.aligned
@@ -378,11 +439,11 @@ bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int
 
 namespace {
 
-template <bool E4M3>
+template <bool E4M3, bool GATHER>
 int launch_attn_impl(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn<E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_attn<E4M3, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
@@ -396,13 +457,13 @@ int launch_attn_impl(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q
     tm_kv = &mkv;
   }
   const int n_items = a.n_work * a.heads;
-  DevArgs p{a.work, n_items, a.heads, a.out, a.out_sf, a.heads * kD, a.scale_log2, a.err};
+  DevArgs p{a.work, n_items, a.heads, a.out, a.out_sf, a.heads * kD, a.scale_log2, a.err, a.pool, a.kv_idx, a.pool_ld};
   int grid = (n_items + 1) / 2;
   if (grid > num_sms()) grid = num_sms();
   // each CTA stages at most kMaxCtaItems items in shared memory
   const int min_grid = (n_items + kMaxCtaItems - 1) / kMaxCtaItems;
   if (grid < min_grid) grid = min_grid;
-  cudaError_t e = launch_k(k_attn<E4M3>, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
+  cudaError_t e = launch_k(k_attn<E4M3, GATHER>, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -416,7 +477,13 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, con
   if (!a.qkv || !a.work || !a.out || a.rows <= 0 || a.heads <= 0 || a.n_work < 0) return T2W_ERR_INVALID;
   if (a.out_sf && (reinterpret_cast<uintptr_t>(a.out_sf) & 1)) return T2W_ERR_INVALID;
   if (a.n_work == 0) return T2W_OK;
-  return a.out_sf ? launch_attn_impl<true>(a, st, tm_q, tm_kv) : launch_attn_impl<false>(a, st, tm_q, tm_kv);
+  if (a.pool) {  // gathered keys from the slot pool (bf16 output only)
+    if (a.out_sf || !a.kv_idx || a.pool_ld < 2 * a.heads * kD || a.pool_ld % 8 ||
+        (reinterpret_cast<uintptr_t>(a.pool) & 15))
+      return T2W_ERR_INVALID;
+    return launch_attn_impl<false, true>(a, st, tm_q, tm_kv);
+  }
+  return a.out_sf ? launch_attn_impl<true, false>(a, st, tm_q, tm_kv) : launch_attn_impl<false, false>(a, st, tm_q, tm_kv);
 }
 
 }  // namespace t2w

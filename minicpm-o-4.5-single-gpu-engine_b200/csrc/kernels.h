@@ -101,7 +101,8 @@ size_t gemm8_sf_bytes(int rows, int cols);
 int launch_gemm8(const Gemm8Args& a, cudaStream_t st, const CUtensorMap* tmA = nullptr, const CUtensorMap* tmW = nullptr,
                  const CUtensorMap* tmC = nullptr);
 
-// One attention work item: a 128-query tile of one packed sequence.
+// One attention work item: a 128-query tile of one packed sequence (gathered form: k_row is the offset of the row's
+// key list in kv_idx, P its window's query count, L its key count).
 struct AttnWork {
   int q_row;   // buffer row of the tile's first query
   int k_row;   // buffer row of the sequence's first key
@@ -116,11 +117,31 @@ struct AttnArgs {
   void* out = nullptr;  // bf16 [rows, heads * 64], or e4m3 when out_sf is set
   uint8_t* out_sf = nullptr;  // e4m3 output: its UE8M0 scale atoms (layout 0)
   float scale_log2 = 0.f;
+  // Gathered keys (slot-pool form; pool != nullptr): work item keys j = pool rows kv_idx[k_row + j], K at column
+  // h * 64 and V at heads * 64 + h * 64 of rows of pool_ld bf16; the item's P queries (from q_pos) see all L keys.
+  const __nv_bfloat16* pool = nullptr;
+  const int* kv_idx = nullptr;
+  int pool_ld = 0;
   int* err = nullptr;
 };
 // Tensor maps of the attention kernel over a qkv buffer: 128-row query boxes and 64-row key / value boxes.
 bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int rows, int heads);
 int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q = nullptr, const CUtensorMap* tm_kv = nullptr);
+
+// Slot-pool (steady-state) kernels, slots.cu.  A conv row: a CFG row's window starts at buffer row seg_row (its two
+// cache rows sit just before it), has T frames, reads conv-cache row slot rd and writes rd's new frames to wr.
+struct ConvRow {
+  int seg_row, T, rd, wr;
+};
+int launch_kv_scatter(const __nv_bfloat16* qkv, int H, const int* tok_qrow, const int* tok_slot, int n,
+                      __nv_bfloat16* pool, cudaStream_t st);
+// cpool: this (step, block)'s conv pool at the conv's frames of row slot 0; slot_ld: elements between row slots.
+int launch_conv_cache(__nv_bfloat16* buf, int H, const ConvRow* rows, int n, __nv_bfloat16* cpool, long long slot_ld,
+                      cudaStream_t st);
+int launch_slot_copy(__nv_bfloat16* pool, int pool_ld, long long sb_ld, int n_sb, const int* src, const int* dst, int n,
+                     cudaStream_t st);
+int launch_rowslot_copy(__nv_bfloat16* cpool, long long slot_ld, long long sb_ld, int n_sb, int src, int dst,
+                        cudaStream_t st);
 
 // Row kernels.
 int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scale1, float eps, int rows, int C,

@@ -246,7 +246,7 @@ __global__ void k_pack(const float* __restrict__ x0, const float* __restrict__ m
   a[c] = xb;
   a[mel + c] = __float2bfloat16_rn(mu[idx]);
   a[2 * mel + c] = __float2bfloat16_rn(spk[(size_t)s * mel + c]);
-  a[3 * mel + c] = __float2bfloat16_rn(cond[idx]);
+  a[3 * mel + c] = __float2bfloat16_rn(cond ? cond[idx] : 0.f);  // no condition: zeros
   u[c] = xb;
   u[mel + c] = z;
   u[2 * mel + c] = z;

@@ -134,12 +134,18 @@ struct Plan {
   std::vector<uint8_t> pad;
   std::vector<AttnWork> work;
   uint64_t key = 0;
+  // slot-pool (steady-state) solves only: gathered attention key lists, conv rows, and the new keys' (row, slot)
+  bool slots = false;
+  std::vector<int> kv_idx, tok_qrow, tok_slot;
+  std::vector<ConvRow> conv_rows;
 };
 
 struct WsLayout {
   size_t hx, h, a, qkv, o, y, c1, f, dphi, x, pad, tok_row, tok_stream, work;
   // FP8 path: e4m3 activations and their scale atoms (sf_h: bytes of one layout for a [rows + 128, hidden] matrix)
   size_t a8, sfa, o8, sfo, c18, sfc1, f8, sff, sf_h, sf_f;
+  // slot-pool solves: device copies of the plan's key lists, conv rows and new-key scatter lists
+  size_t kv_idx, conv_rows, tok_qrow, tok_slot;
   size_t total;
 };
 
@@ -167,6 +173,17 @@ struct t2w_solver {
   std::unordered_map<uintptr_t, uint64_t> ws_meta;  // workspace -> plan key of the index arrays it holds
   std::vector<cudaEvent_t> prof_events;
   int64_t n_replays = 0, n_captures = 0, n_eager = 0;
+};
+
+// Device pools of the steady-state solve (one per solver and device): K/V slots per (step, block) and conv-cache row
+// slots per (step, block).
+struct t2w_slots {
+  int device = 0, n_slots = 0, n_rowslots = 0, n_sb = 0, H = 0;
+  __nv_bfloat16* kv = nullptr;   // [n_sb][n_slots][2 H]
+  __nv_bfloat16* cnn = nullptr;  // [n_sb][n_rowslots][2 convs][2 frames][H]
+  long long kv_sb() const { return (long long)n_slots * 2 * H; }
+  long long cnn_slot() const { return 4ll * H; }
+  long long cnn_sb() const { return (long long)n_rowslots * 4 * H; }
 };
 
 namespace {
@@ -218,6 +235,49 @@ bool make_plan(const t2w_config& c, int n, const int* P, const int* T, Plan& pl)
   return true;
 }
 
+// Steady-state plan: one window of T[i] frames per request against its cached keys.  Rows as the packed plan with no
+// prompt part: per CFG half, per request [2 conv-cache rows | T[i] window rows].  CFG row r (cond rows 0..n-1, then
+// uncond rows) attends the kv_len[r] pool slots of its list (its cached keys, then its T[i] new slots, which the QKV
+// output is scattered into) and reads / writes conv-cache row slots rd[r] / wr[r].
+bool make_plan_slots(const t2w_config& c, int n, const int* T, const int* kv_len, const int* kv_idx, const int* rd,
+                     const int* wr, int n_slots, int n_rowslots, Plan& pl) {
+  if (n <= 0 || !T || !kv_len || !kv_idx || !rd || !wr) return false;
+  std::vector<int> P0(n, 0);
+  for (int i = 0; i < n; ++i)
+    if (T[i] <= 0) return false;
+  if (!make_plan(c, n, P0.data(), T, pl)) return false;
+  pl.slots = true;
+  pl.work.clear();
+  long long off = 0;
+  std::vector<long long> kv_off(2 * n);
+  for (int r = 0; r < 2 * n; ++r) {
+    const int i = r % n;
+    if (kv_len[r] < T[i] || rd[r] < 0 || rd[r] >= n_rowslots || wr[r] < 0 || wr[r] >= n_rowslots) return false;
+    kv_off[r] = off;
+    off += kv_len[r];
+  }
+  if (off > (1ll << 30)) return false;
+  pl.kv_idx.assign(kv_idx, kv_idx + off);
+  for (long long j = 0; j < off; ++j)
+    if (pl.kv_idx[j] < 0 || pl.kv_idx[j] >= n_slots) return false;
+  int row = 0;
+  for (int i = 0; i < n; ++i) {
+    row += 2;
+    for (int hh = 0; hh < 2; ++hh) {
+      const int r = hh * n + i, seg = row + hh * pl.half_rows;
+      for (int q = 0; q < T[i]; q += 128) pl.work.push_back(AttnWork{seg + q, (int)kv_off[r], q, T[i], kv_len[r]});
+      pl.conv_rows.push_back(ConvRow{seg, T[i], rd[r], wr[r]});
+      for (int t = 0; t < T[i]; ++t) {
+        pl.tok_qrow.push_back(seg + t);
+        pl.tok_slot.push_back(pl.kv_idx[kv_off[r] + kv_len[r] - T[i] + t]);
+      }
+    }
+    row += T[i];
+  }
+  pl.n_work = (int)pl.work.size();
+  return true;
+}
+
 WsLayout layout(const t2w_config& c, const Plan& pl, bool fp8) {
   WsLayout w{};
   size_t off = 0;
@@ -241,6 +301,12 @@ WsLayout layout(const t2w_config& c, const Plan& pl, bool fp8) {
   w.tok_row = take((size_t)pl.n_tok * 4);
   w.tok_stream = take((size_t)pl.n_tok * 4);
   w.work = take((size_t)pl.n_work * sizeof(AttnWork));
+  if (pl.slots) {
+    w.kv_idx = take(pl.kv_idx.size() * 4);
+    w.conv_rows = take(pl.conv_rows.size() * sizeof(ConvRow));
+    w.tok_qrow = take(pl.tok_qrow.size() * 4);
+    w.tok_slot = take(pl.tok_slot.size() * 4);
+  }
   if (fp8) {
     // the row-shifted scale layouts hold rows up to rows + 1: one spare row tile
     w.sf_h = align256(gemm8_sf_bytes(pl.rows + 128, c.hidden));
@@ -283,7 +349,8 @@ struct Prof {
 };
 
 // Enqueue one whole solve (no host synchronisation, graph-capturable).
-int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, cudaStream_t st, Prof* prof = nullptr) {
+int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, cudaStream_t st, Prof* prof = nullptr,
+                  const t2w_slots* sp = nullptr) {
   Prof none;
   Prof& P = prof ? *prof : none;
   const t2w_config& c = s->cfg;
@@ -318,6 +385,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   CUtensorMap tm_att_q, tm_att_kv;
   if (!make_attn_tmaps(&tm_att_q, &tm_att_kv, qkv, R, c.heads)) return T2W_ERR_INVALID;
   const bool fp8 = s->precision == T2W_PREC_FP8;
+  if (pl.slots && (!sp || fp8)) return T2W_ERR_UNSUPPORTED;  // the slot-pool solve runs the bf16 path
+  const int* kv_idx_d = pl.slots ? at<int>(ws, L.kv_idx) : nullptr;
+  const ConvRow* conv_rows_d = pl.slots ? at<ConvRow>(ws, L.conv_rows) : nullptr;
+  const int* tok_qrow_d = pl.slots ? at<int>(ws, L.tok_qrow) : nullptr;
+  const int* tok_slot_d = pl.slots ? at<int>(ws, L.tok_slot) : nullptr;
+  const int n_conv_rows = (int)pl.conv_rows.size(), n_new = (int)pl.tok_slot.size();
   uint8_t *a8 = nullptr, *sfa = nullptr, *o8 = nullptr, *sfo = nullptr, *c18 = nullptr, *sfc1 = nullptr, *f8 = nullptr,
           *sff = nullptr;
   CUtensorMap t8_a, t8_o, t8_c1, t8_f, st8_f;
@@ -468,8 +541,17 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       q.qn_w = w.qn_w; q.qn_b = w.qn_b; q.kn_w = w.kn_w; q.kn_b = w.kn_b; q.qk_eps = c.eps_qk;
       T2W_TRY(P.tick(T2W_KC_GEMM_QKV, st));
       T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv, &st_qkv));
+      const int sb = step * c.depth + bi;
+      AttnArgs at_use = at_args;
+      if (pl.slots) {  // the window's new keys into their slots; attention gathers every row's key list
+        __nv_bfloat16* kvp = sp->kv + sb * sp->kv_sb();
+        T2W_TRY(launch_kv_scatter(qkv, H, tok_qrow_d, tok_slot_d, n_new, kvp, st));
+        at_use.pool = kvp;
+        at_use.kv_idx = kv_idx_d;
+        at_use.pool_ld = 2 * H;
+      }
       T2W_TRY(P.tick(T2W_KC_ATTN, st));
-      T2W_TRY(launch_attn(at_args, st, &tm_att_q, &tm_att_kv));
+      T2W_TRY(launch_attn(at_use, st, &tm_att_q, &tm_att_kv));
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
       pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_BF16; pr.out = y; pr.ldo = H;
@@ -478,6 +560,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st));
+      if (pl.slots)  // cached conv-input frames in front of each window, and the window's last two saved
+        T2W_TRY(launch_conv_cache(a, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb(), sp->cnn_slot(), st));
       GemmArgs k1 = GemmArgs();
       k1.rows_a = R; k1.M = R; k1.err = s->err;
       k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
@@ -486,6 +570,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &st_o));
       T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
       T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, row_out_bf16(c1), pad, st));
+      if (pl.slots)
+        T2W_TRY(launch_conv_cache(c1, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb() + 2 * H, sp->cnn_slot(), st));
       GemmArgs k2 = GemmArgs();
       k2.rows_a = R; k2.M = R; k2.err = s->err;
       k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
@@ -533,6 +619,15 @@ int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
                            cudaMemcpyHostToDevice, st));
   T2W_CUDA(cudaMemcpyAsync(at<AttnWork>(ws, L.work), pl.work.data(), pl.work.size() * sizeof(AttnWork),
                            cudaMemcpyHostToDevice, st));
+  if (pl.slots) {
+    T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.kv_idx), pl.kv_idx.data(), pl.kv_idx.size() * 4, cudaMemcpyHostToDevice, st));
+    T2W_CUDA(cudaMemcpyAsync(at<ConvRow>(ws, L.conv_rows), pl.conv_rows.data(), pl.conv_rows.size() * sizeof(ConvRow),
+                             cudaMemcpyHostToDevice, st));
+    T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_qrow), pl.tok_qrow.data(), pl.tok_qrow.size() * 4, cudaMemcpyHostToDevice, st));
+    T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_slot), pl.tok_slot.data(), pl.tok_slot.size() * 4, cudaMemcpyHostToDevice, st));
+    s->ws_meta.erase(reinterpret_cast<uintptr_t>(ws));  // slot lists change every call: nothing to reuse
+    return T2W_OK;
+  }
   s->ws_meta[reinterpret_cast<uintptr_t>(ws)] = pl.key;
   return T2W_OK;
 }
@@ -914,6 +1009,99 @@ int t2w_counts(const t2w_solver* s, int64_t* replays, int64_t* captures, int64_t
   if (replays) *replays = s->n_replays;
   if (captures) *captures = s->n_captures;
   if (eager) *eager = s->n_eager;
+  return T2W_OK;
+}
+
+int t2w_slots_create(const t2w_solver* s, int32_t n_slots, int32_t n_rowslots, t2w_slots** out) {
+  if (!s || !out || n_slots <= 0 || n_rowslots <= 0) return T2W_ERR_INVALID;
+  t2w_slots* p = new t2w_slots();
+  T2W_CUDA(cudaGetDevice(&p->device));
+  p->n_slots = n_slots;
+  p->n_rowslots = n_rowslots;
+  p->n_sb = s->cfg.steps * s->cfg.depth;
+  p->H = s->cfg.hidden;
+  const size_t kv_bytes = (size_t)p->n_sb * p->kv_sb() * 2, cnn_bytes = (size_t)p->n_sb * p->cnn_sb() * 2;
+  if (cudaMalloc(reinterpret_cast<void**>(&p->kv), kv_bytes) != cudaSuccess) {
+    delete p;
+    return T2W_ERR_OOM;
+  }
+  if (cudaMalloc(reinterpret_cast<void**>(&p->cnn), cnn_bytes) != cudaSuccess) {
+    cudaFree(p->kv);
+    delete p;
+    return T2W_ERR_OOM;
+  }
+  // finite contents everywhere (slots are read only through key lists, but a zero pool keeps stray reads harmless)
+  if (cudaMemset(p->kv, 0, kv_bytes) != cudaSuccess || cudaMemset(p->cnn, 0, cnn_bytes) != cudaSuccess) {
+    cudaFree(p->kv);
+    cudaFree(p->cnn);
+    delete p;
+    return T2W_ERR_CUDA;
+  }
+  *out = p;
+  return T2W_OK;
+}
+
+int t2w_slots_destroy(t2w_slots* p) {
+  if (!p) return T2W_ERR_INVALID;
+  cudaFree(p->kv);
+  cudaFree(p->cnn);
+  delete p;
+  return T2W_OK;
+}
+
+int t2w_slots_copy(t2w_slots* p, const int32_t* src, const int32_t* dst, int32_t n, void* stream) {
+  if (!p || n < 0 || (n > 0 && (!src || !dst))) return T2W_ERR_INVALID;
+  if (n == 0) return T2W_OK;
+  for (int i = 0; i < n; ++i)
+    if (src[i] < 0 || src[i] >= p->n_slots || dst[i] < 0 || dst[i] >= p->n_slots) return T2W_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* d = nullptr;
+  T2W_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * (size_t)n * 4, st));
+  T2W_CUDA(cudaMemcpyAsync(d, src, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+  T2W_CUDA(cudaMemcpyAsync(d + n, dst, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+  const int rc = launch_slot_copy(p->kv, 2 * p->H, p->kv_sb(), p->n_sb, d, d + n, n, st);
+  cudaFreeAsync(d, st);
+  return rc;
+}
+
+int t2w_slots_copy_row(t2w_slots* p, int32_t src, int32_t dst, void* stream) {
+  if (!p || src >= p->n_rowslots || dst < 0 || dst >= p->n_rowslots) return T2W_ERR_INVALID;
+  return launch_rowslot_copy(p->cnn, p->cnn_slot(), p->cnn_sb(), p->n_sb, src < 0 ? -1 : src, dst,
+                             static_cast<cudaStream_t>(stream));
+}
+
+size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_slot_batch* b) {
+  if (!s || !p || !b) return 0;
+  Plan pl;
+  if (!make_plan_slots(s->cfg, b->n_streams, b->chunk_len, b->kv_len, b->kv_idx, b->cnn_rd, b->cnn_wr, p->n_slots,
+                       p->n_rowslots, pl))
+    return 0;
+  return layout(s->cfg, pl, false).total;
+}
+
+int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* ws, size_t ws_bytes, uint32_t flags,
+                    void* stream) {
+  (void)flags;
+  if (!s || !p || !b || !ws || !b->x0 || !b->mu || !b->spk || !b->out) return T2W_ERR_INVALID;
+  if (s->precision != T2W_PREC_BF16) return T2W_ERR_UNSUPPORTED;
+  Plan pl;
+  if (!make_plan_slots(s->cfg, b->n_streams, b->chunk_len, b->kv_len, b->kv_idx, b->cnn_rd, b->cnn_wr, p->n_slots,
+                       p->n_rowslots, pl))
+    return T2W_ERR_INVALID;
+  if (layout(s->cfg, pl, false).total > ws_bytes) return T2W_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return T2W_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  T2W_TRY(upload_meta(s, pl, ws, st));
+  // the window solve is the packed solve's body with P = 0 rows: every row a window
+  t2w_batch pb{};
+  pb.n_streams = b->n_streams;
+  pb.x0 = b->x0;
+  pb.mu = b->mu;
+  pb.cond = b->cond;
+  pb.spk = b->spk;
+  pb.out = b->out;
+  T2W_TRY(enqueue_solve(s, pl, pb, ws, st, nullptr, p));
+  ++s->n_eager;
   return T2W_OK;
 }
 

@@ -10,6 +10,10 @@ data path, only a gloo barrier and a max over ranks of the device-timed region).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|target|c5|c3|c4] [--impl b200|reference]
 
+``--workload steady`` times the steady-state form (the reference's ``FastDiT.solve``): 64 streams with 300-frame
+prompts already set up, one 50-frame window per stream per call against the slot-pool caches (trimmed to the prompt
+plus the last 100 keys, as the reference trims them); a step is one such call, timed through the public API.
+
 ``--workload c4`` is benchmark config 4: config 2's shapes at 128 streams on the FP8 path (e4m3 block projections with
 power-of-two block scales; bf16 in_proj, attention and final layer).
 
@@ -50,7 +54,7 @@ def args_():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3", "c4"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3", "c4", "steady"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
     return ap.parse_args()
@@ -61,7 +65,7 @@ def shard(name: str, rank: int, world: int) -> Workload:
     if name == "c5":
         n = C5.streams // world
         return Workload(f"{C5.name}[rank {rank}/{world}]", C5.seed, C5.lengths[rank * n:(rank + 1) * n])
-    base = {"c2": C2, "target": TARGET, "c3": C3, "c4": C4}[name]
+    base = {"c2": C2, "target": TARGET, "c3": C3, "c4": C4, "steady": C2}[name]
     if world == 1:
         return base
     return Workload(f"{base.name}[rank {rank}]", base.seed + 1000 * rank, base.lengths)
@@ -164,6 +168,73 @@ def reference_arm(a, rank: int, world: int) -> None:
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
+def steady_arm(a, rank: int, world: int) -> None:
+    """Steady-state windows through ``B200FastDiT`` (one process per GPU, each with its own 64 streams)."""
+    from b200t2w.fastdit import B200FastDiT
+    from b200t2w.solver import B200Solver
+    from b200t2w.weights import random_state_dict
+
+    cfg = REFERENCE
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, P, T = 64, 300, 50
+    g = torch.Generator().manual_seed(11 + rank)
+    noise = torch.randn(cfg.mel, 8192, generator=g)
+    solver = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), device=dev)
+    fd = B200FastDiT(solver, noise, n_slots=2 * n * (P + 100 + T + 8), max_streams=n)
+    spk = torch.randn(n, cfg.mel, generator=g)
+    caches = [fd.new_cache() for _ in range(n)]
+    for c in caches:
+        c.keep = P
+    for i0 in range(0, n, 16):  # prompt setups, 16 per call
+        cs = caches[i0:i0 + 16]
+        fd.solve(cs, [torch.randn(cfg.mel, P, generator=g) for _ in cs], spk[i0:i0 + 16],
+                 [torch.randn(cfg.mel, P, generator=g) for _ in cs], [True] * len(cs))
+    mus = [[torch.randn(cfg.mel, T, generator=g).to(dev) for _ in range(n)] for _ in range(4)]
+    spk_d = spk.to(dev)
+
+    def step(k):
+        return fd.solve(caches, mus[k % 4], spk_d, None, [True] * n)
+
+    for k in range(max(a.warmup, 3)):  # caches reach the trimmed steady length (P + 100)
+        step(k)
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    times = []
+    for k in range(a.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        out = step(k)
+        e1.record(st)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    solver.check()
+    frames = n * T
+    red = torch.tensor([sum(times)], dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(red, op=torch.distributed.ReduceOp.MAX)
+    value = world * frames * a.steps / (float(red[0]) / 1000)
+    # per stream per window: S [2T (Dp 36 H^2 + 800 H) + Dp 4H 2T (keys)], keys = cache (P + 100) + T
+    keys = caches[0].length
+    flop = n * cfg.steps * (2 * T * (cfg.depth * 2 * cfg.hidden * (10 * cfg.hidden + 2 * cfg.ffn) + 800 * cfg.hidden)
+                            + cfg.depth * 4 * cfg.hidden * 2 * T * keys)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "DiT mel frames/s, steady-state windows (slot-pool solve)", "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": statistics.mean(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"steady_{n}x{T} (P={P} cached, keys per row {keys})", "streams_per_gpu": n,
+                       "window_frames": T, "prompt_frames": P, "model": "reference-config DiT (unverified), random init",
+                       "timing": "CUDA events around each public-API call (host planning and uploads inside)"},
+            "latency_ms": {"p50": statistics.median(times)}, "tflops": flop / (statistics.mean(times) / 1000) / 1e12,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": n * T * cfg.mel * 4,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+    del out
+    fd.close()
+    solver.close()
+
+
 def main() -> None:
     a = args_()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
@@ -175,6 +246,12 @@ def main() -> None:
     if a.impl == "reference":
         reference_arm(a, rank, world)
         if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if a.workload == "steady":
+        steady_arm(a, rank, world)
+        if world > 1:
+            torch.distributed.barrier()
             torch.distributed.destroy_process_group()
         return
 

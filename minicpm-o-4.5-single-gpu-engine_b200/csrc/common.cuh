@@ -287,6 +287,31 @@ T2W_DEV float mish(float y) {
   const float n = e * (e + 2.f);
   return y * __fdividef(n, n + 2.f);
 }
+// ---------------------------------------------------------------- cross-CTA flags (gpu scope)
+T2W_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+T2W_DEV void red_release_add_gpu(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Async-proxy (TMA) global writes ordered before this thread's later generic-proxy operations.
+T2W_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// Bounded wait until *f >= target; false (and T2W_ERR_TIMEOUT in err) after kWaitLimitNs.
+T2W_DEV bool wait_counter(const int* f, int target, int* err) {
+  if (ld_acquire_gpu(f) >= target) return true;
+  const unsigned long long t0 = globaltimer();
+  while (ld_acquire_gpu(f) < target) {
+    __nanosleep(128);
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      if (err) atomicExch(err, T2W_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- e4m3 with power-of-two (UE8M0) block scales
 // The UE8M0 byte e of a block whose largest magnitude is amax: the smallest power of two 2^(e - 127) with
 // amax / 2^(e - 127) <= 448 (the e4m3 maximum); an all-zero block gets e = 127 (scale 1).  With amax = m 2^E,

@@ -60,6 +60,7 @@ struct DevArgs {
   const float* kn_b;
   float qk_eps;
   int* err;
+  int* done_flags;  // per 128-row block: +1 from each epilogue warp once its stores of a tile are complete
 };
 
 T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -292,6 +293,12 @@ __global__ void __launch_bounds__(320, 1)
             bulk_commit();
           }
         }
+        if (p.done_flags && lane == 0) {  // publish: this warp's rows of the tile are in global memory
+          bulk_wait0();
+          fence_proxy_async_global();
+          __threadfence();
+          red_release_add_gpu(p.done_flags + m0 / kBM, 1);
+        }
       }
     }
     if constexpr (TMA_OUT) {
@@ -362,6 +369,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.kn_b = a.kn_b;
   p.qk_eps = a.qk_eps;
   p.err = a.err;
+  p.done_flags = TMA_OUT ? a.done_flags : nullptr;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   cudaError_t e = launch_k(k_gemm<BN, EPI, TMA_OUT>, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tmA, *tmW, *tmC, p);
   if (e != cudaSuccess) {

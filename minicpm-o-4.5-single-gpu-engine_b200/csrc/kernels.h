@@ -53,6 +53,9 @@ struct GemmArgs {
   const float* kn_b = nullptr;
   float qk_eps = 0.f;
   int* err = nullptr;
+  // Completion counters, one per 128-row block: each epilogue warp adds 1 once its stores of a tile are complete
+  // (8 per tile; a block is done at 8 * N / BN).  Lets the row kernel that follows start early (RowWait).
+  int* done_flags = nullptr;
 };
 // Column tile the launcher picks for an N-wide output of M rows with epilogue `epi` (0: N unsupported).
 int gemm_block_n_for(int N, int M, int epi);
@@ -160,11 +163,19 @@ inline RowOut row_out_bf16(__nv_bfloat16* p) {
   o.out = p;
   return o;
 }
+// A row kernel that follows a GEMM with done_flags: instead of waiting for the GEMM's whole grid (programmatic launch)
+// each warp waits until its row's 128-row block reached `target` (bounded; T2W_ERR_TIMEOUT into err), so the rows of
+// finished tiles are normalised on SMs the GEMM's last partial wave leaves idle.  flags == nullptr: plain ordering.
+struct RowWait {
+  const int* flags = nullptr;
+  int target = 0;
+  int* err = nullptr;
+};
 // h += g * y (fp32, in place; skipped when y == nullptr), then out = LN(h) * scale1 + shift, pad rows zero.
 int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
-                      int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st);
+                      int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st, const RowWait& wt = RowWait());
 int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C, const RowOut& o,
-                   const uint8_t* pad, cudaStream_t st);
+                   const uint8_t* pad, cudaStream_t st, const RowWait& wt = RowWait());
 // bf16 [rows, C] -> e4m3 + scale atoms (C = 128, 512, 1536 or 2048).
 int launch_quant_rows(const __nv_bfloat16* x, int rows, int C, const RowOut& o, cudaStream_t st);
 // fp32 W [N, Kt] -> e4m3 + per-1x128-block scale atoms [Kt / 128][N / 128][512].

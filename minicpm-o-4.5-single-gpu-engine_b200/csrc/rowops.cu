@@ -98,15 +98,25 @@ __global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int
 
 // h += g * y (the gated residual of the preceding GEMM's bf16 output y, fp32, stored back), then out = LN(h) * scale1 +
 // shift (dit_kernels.py:35-60's add_ln_mod, with the residual kept in fp32).  y == nullptr: plain LN + modulation.
+// Whether this warp's row may be read: plain programmatic ordering, or its 128-row block's GEMM tiles are complete.
+T2W_DEV bool row_ready(const RowWait& wt, int row) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = wait_counter(wt.flags + (row >> 7), wt.target, wt.err);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 template <int V, bool E4M3>
 __global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const __nv_bfloat16* __restrict__ y,
                                                     const float* __restrict__ g, const float* __restrict__ shift,
                                                     const float* __restrict__ scale1, float eps, int rows, const RowOut o,
-                                                    const uint8_t* __restrict__ pad) {
-  pdl_wait();
-  pdl_launch();
+                                                    const uint8_t* __restrict__ pad, const RowWait wt) {
+  // With flags the row's own GEMM tiles are awaited below instead of the whole grid.  The successor is not let in early
+  // (no launch_dependents): a persistent GEMM launched early would hold whole SMs idle in its own wait while this
+  // kernel's blocks still need them.
+  if (!wt.flags) pdl_wait();
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
+  if (wt.flags && !row_ready(wt, row)) return;
   constexpr int C = 128 * V;
   float4 x[V];
   float4* hr = reinterpret_cast<float4*>(h + (size_t)row * C);
@@ -116,7 +126,7 @@ __global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const
     const uint2* yr = reinterpret_cast<const uint2*>(y + (size_t)row * C);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      const uint2 u = yr[32 * i + lane];
+      const uint2 u = __ldcg(yr + 32 * i + lane);  // L2: the GEMM may have written it after this SM cached lines
       const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
       const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
       const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 32 * i + lane);
@@ -149,11 +159,11 @@ __global__ void __launch_bounds__(256) k_add_ln_mod(float* __restrict__ h, const
 template <int V, bool E4M3>
 __global__ void __launch_bounds__(256) k_ln_mish(const __nv_bfloat16* __restrict__ xin, const float* __restrict__ w,
                                                  const float* __restrict__ b, float eps, int rows, const RowOut o,
-                                                 const uint8_t* __restrict__ pad) {
-  pdl_wait();
-  pdl_launch();
+                                                 const uint8_t* __restrict__ pad, const RowWait wt) {
+  if (!wt.flags) pdl_wait();  // no launch_dependents: see k_add_ln_mod
   const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
+  if (wt.flags && !row_ready(wt, row)) return;
   constexpr int C = 128 * V;
   float4 x[V];
   if (pad && pad[row]) {
@@ -165,7 +175,7 @@ __global__ void __launch_bounds__(256) k_ln_mish(const __nv_bfloat16* __restrict
   const uint2* xr = reinterpret_cast<const uint2*>(xin + (size_t)row * C);
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    const uint2 u = xr[32 * i + lane];
+    const uint2 u = __ldcg(xr + 32 * i + lane);
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
     const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
     x[i] = make_float4(a.x, a.y, c.x, c.y);
@@ -405,14 +415,14 @@ namespace {
 
 template <bool E4M3>
 int add_ln_mod_impl(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
-                    int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st) {
+                    int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st, const RowWait& wt) {
   const unsigned gr = blocks_for(rows, kRowsPerBlock);
   switch (C) {
-    case 128: check_err(launch_k(k_add_ln_mod<1, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
-    case 256: check_err(launch_k(k_add_ln_mod<2, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
-    case 512: check_err(launch_k(k_add_ln_mod<4, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
-    case 768: check_err(launch_k(k_add_ln_mod<6, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
-    case 1024: check_err(launch_k(k_add_ln_mod<8, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad)); break;
+    case 128: check_err(launch_k(k_add_ln_mod<1, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad, wt)); break;
+    case 256: check_err(launch_k(k_add_ln_mod<2, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad, wt)); break;
+    case 512: check_err(launch_k(k_add_ln_mod<4, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad, wt)); break;
+    case 768: check_err(launch_k(k_add_ln_mod<6, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad, wt)); break;
+    case 1024: check_err(launch_k(k_add_ln_mod<8, E4M3>, dim3(gr), dim3(256), 0, st, h, y, g, shift, scale1, eps, rows, o, pad, wt)); break;
     default: return T2W_ERR_INVALID;
   }
   return check_launch();
@@ -420,14 +430,14 @@ int add_ln_mod_impl(float* h, const __nv_bfloat16* y, const float* g, const floa
 
 template <bool E4M3>
 int ln_mish_impl(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C, const RowOut& o,
-                 const uint8_t* pad, cudaStream_t st) {
+                 const uint8_t* pad, cudaStream_t st, const RowWait& wt) {
   const unsigned g = blocks_for(rows, kRowsPerBlock);
   switch (C) {
-    case 128: check_err(launch_k(k_ln_mish<1, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
-    case 256: check_err(launch_k(k_ln_mish<2, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
-    case 512: check_err(launch_k(k_ln_mish<4, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
-    case 768: check_err(launch_k(k_ln_mish<6, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
-    case 1024: check_err(launch_k(k_ln_mish<8, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad)); break;
+    case 128: check_err(launch_k(k_ln_mish<1, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad, wt)); break;
+    case 256: check_err(launch_k(k_ln_mish<2, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad, wt)); break;
+    case 512: check_err(launch_k(k_ln_mish<4, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad, wt)); break;
+    case 768: check_err(launch_k(k_ln_mish<6, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad, wt)); break;
+    case 1024: check_err(launch_k(k_ln_mish<8, E4M3>, dim3(g), dim3(256), 0, st, x, w, b, eps, rows, o, pad, wt)); break;
     default: return T2W_ERR_INVALID;
   }
   return check_launch();
@@ -443,18 +453,19 @@ bool row_out_ok(const RowOut& o) {
 }  // namespace
 
 int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
-                      int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st) {
+                      int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st, const RowWait& wt) {
   if (rows <= 0) return T2W_OK;
-  if ((y && !g) || !row_out_ok(o)) return T2W_ERR_INVALID;
-  return o.sf ? add_ln_mod_impl<true>(h, y, g, shift, scale1, eps, rows, C, o, pad, st)
-              : add_ln_mod_impl<false>(h, y, g, shift, scale1, eps, rows, C, o, pad, st);
+  if ((y && !g) || !row_out_ok(o) || (wt.flags && !y)) return T2W_ERR_INVALID;
+  return o.sf ? add_ln_mod_impl<true>(h, y, g, shift, scale1, eps, rows, C, o, pad, st, wt)
+              : add_ln_mod_impl<false>(h, y, g, shift, scale1, eps, rows, C, o, pad, st, wt);
 }
 
 int launch_ln_mish(const __nv_bfloat16* x, const float* w, const float* b, float eps, int rows, int C, const RowOut& o,
-                   const uint8_t* pad, cudaStream_t st) {
+                   const uint8_t* pad, cudaStream_t st, const RowWait& wt) {
   if (rows <= 0) return T2W_OK;
   if (!row_out_ok(o)) return T2W_ERR_INVALID;
-  return o.sf ? ln_mish_impl<true>(x, w, b, eps, rows, C, o, pad, st) : ln_mish_impl<false>(x, w, b, eps, rows, C, o, pad, st);
+  return o.sf ? ln_mish_impl<true>(x, w, b, eps, rows, C, o, pad, st, wt)
+              : ln_mish_impl<false>(x, w, b, eps, rows, C, o, pad, st, wt);
 }
 
 int launch_quant_rows(const __nv_bfloat16* x, int rows, int C, const RowOut& o, cudaStream_t st) {

@@ -146,6 +146,8 @@ struct WsLayout {
   size_t a8, sfa, o8, sfo, c18, sfc1, f8, sff, sf_h, sf_f;
   // slot-pool solves: device copies of the plan's key lists, conv rows and new-key scatter lists
   size_t kv_idx, conv_rows, tok_qrow, tok_slot;
+  // completion counters of the GEMMs whose following row kernel starts early: [step][block][4][rows / 128]
+  size_t done;
   size_t total;
 };
 
@@ -301,6 +303,7 @@ WsLayout layout(const t2w_config& c, const Plan& pl, bool fp8) {
   w.tok_row = take((size_t)pl.n_tok * 4);
   w.tok_stream = take((size_t)pl.n_tok * 4);
   w.work = take((size_t)pl.n_work * sizeof(AttnWork));
+  w.done = take((size_t)c.steps * c.depth * 4 * (pl.rows / 128) * sizeof(int));
   if (pl.slots) {
     w.kv_idx = take(pl.kv_idx.size() * 4);
     w.conv_rows = take(pl.conv_rows.size() * sizeof(ConvRow));
@@ -454,6 +457,11 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   // finite conv outputs), or the proj GEMM carries workspace garbage into pad rows of h, and a NaN there reaches the
   // masked keys of the next attention, where 0 * NaN poisons the P V product.
   T2W_CUDA(cudaMemsetAsync(o, 0, (size_t)R * H * 2, st));
+  int* done_all = at<int>(ws, L.done);
+  const int mblocks = R / 128;
+  T2W_CUDA(cudaMemsetAsync(done_all, 0, (size_t)c.steps * c.depth * 4 * mblocks * sizeof(int), st));
+  // the N = H GEMMs (proj, conv1, conv2, fc2) publish per-block completion; the row kernel after each waits per block
+  const int done_target = 8 * (H / gemm_block_n_for(H, R, T2W_EPI_BF16));
   T2W_TRY(P.tick(T2W_KC_PACK, st));
   T2W_TRY(launch_pack(b.x0, b.mu, b.cond, b.spk, tok_row, tok_stream, pl.n_tok, mel, pl.half_rows, hx, 4 * mel, x, st));
 
@@ -485,11 +493,20 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     // first norm or by the final layer's norm.
     const float* pend_g = nullptr;
     const __nv_bfloat16* pend_y = nullptr;
+    int* pend_done = nullptr;
     for (int bi = 0; bi < c.depth; ++bi) {
       const BlockW& w = s->blk[bi];
       const float* M = s->mods + ((size_t)step * c.depth + bi) * 9 * H;
       const float *sh_a = M, *sc_a = M + H, *g_a = M + 2 * H, *sh_m = M + 3 * H, *sc_m = M + 4 * H, *g_m = M + 5 * H;
       const float *sh_c = M + 6 * H, *sc_c = M + 7 * H, *g_c = M + 8 * H;
+      int* dn = done_all + ((size_t)step * c.depth + bi) * 4 * mblocks;  // proj, conv1, conv2, fc2
+      auto waits = [&](int* f) {
+        RowWait r;
+        r.flags = f;
+        r.target = done_target;
+        r.err = s->err;
+        return r;
+      };
       if (fp8) {
         // attention branch
         T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
@@ -530,11 +547,13 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
         T2W_TRY(launch_gemm8(f2, st, &t8_f, &w.t8[W8_FC2], &st_y));
         pend_g = g_m;
         pend_y = y;
+        pend_done = nullptr;
         continue;
       }
       // attention branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, row_out_bf16(a), nullptr, st));
+      T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, row_out_bf16(a), nullptr, st,
+                                waits(pend_done)));
       GemmArgs q = GemmArgs();
       q.rows_a = R; q.M = R; q.err = s->err;
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
@@ -555,32 +574,36 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
       pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_BF16; pr.out = y; pr.ldo = H;
+      pr.done_flags = dn;
       T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
       T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_y));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st));
+      T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st, waits(dn)));
       if (pl.slots)  // cached conv-input frames in front of each window, and the window's last two saved
         T2W_TRY(launch_conv_cache(a, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb(), sp->cnn_slot(), st));
       GemmArgs k1 = GemmArgs();
       k1.rows_a = R; k1.M = R; k1.err = s->err;
       k1.A = a; k1.lda = H; k1.W = w.c1; k1.bias = w.b_c1; k1.N = H; k1.K = H; k1.taps = 3; k1.tap_row0 = -2;
       k1.epi = T2W_EPI_BF16; k1.out = o; k1.ldo = H;
+      k1.done_flags = dn + mblocks;
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
       T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &st_o));
       T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
-      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, row_out_bf16(c1), pad, st));
+      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, row_out_bf16(c1), pad, st, waits(dn + mblocks)));
       if (pl.slots)
         T2W_TRY(launch_conv_cache(c1, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb() + 2 * H, sp->cnn_slot(), st));
       GemmArgs k2 = GemmArgs();
       k2.rows_a = R; k2.M = R; k2.err = s->err;
       k2.A = c1; k2.lda = H; k2.W = w.c2; k2.bias = w.b_c2; k2.N = H; k2.K = H; k2.taps = 3; k2.tap_row0 = -2;
       k2.epi = T2W_EPI_BF16; k2.out = y; k2.ldo = H;
+      k2.done_flags = dn + 2 * mblocks;
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
       T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, &st_y));
       // MLP branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, row_out_bf16(a), nullptr, st));
+      T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, row_out_bf16(a), nullptr, st,
+                                waits(dn + 2 * mblocks)));
       GemmArgs f1 = GemmArgs();
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
@@ -589,14 +612,20 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       GemmArgs f2 = GemmArgs();
       f2.rows_a = R; f2.M = R; f2.err = s->err;
       f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_BF16; f2.out = y; f2.ldo = H;
+      f2.done_flags = dn + 3 * mblocks;
       T2W_TRY(P.tick(T2W_KC_GEMM_FC2, st));
       T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, &st_y));
       pend_g = g_m;
       pend_y = y;
+      pend_done = dn + 3 * mblocks;
     }
     const float* FM = s->final_mods + (size_t)step * 2 * H;
     T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-    T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, FM, FM + H, c.eps_final, R, H, row_out_bf16(a), nullptr, st));
+    RowWait fw;
+    fw.flags = pend_done;
+    fw.target = done_target;
+    fw.err = s->err;
+    T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, FM, FM + H, c.eps_final, R, H, row_out_bf16(a), nullptr, st, fw));
     GemmArgs fin = GemmArgs();
     fin.rows_a = R; fin.M = R; fin.err = s->err;
     fin.A = a; fin.lda = H; fin.W = s->w_fin; fin.bias = s->b_fin; fin.N = mel; fin.K = H; fin.epi = T2W_EPI_F32;

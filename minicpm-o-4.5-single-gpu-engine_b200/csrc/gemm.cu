@@ -12,6 +12,7 @@
 // The causal convolutions use taps = 3, tap_row0 = -2: tap t of output row m reads activation row m - 2 + t, so the
 // im2col matrix is never materialised; rows before 0 come back zero from TMA.  No TMA multicast.
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -312,6 +313,225 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+
+// ---------------------------------------------------------------- CTA-pair variant (tcgen05 cta_group::2)
+// A cluster of two CTAs on neighbouring SMs computes a 256 x 256 tile: CTA r of the pair loads rows 128 r .. + 127 of
+// the tile's A and rows 128 r .. + 127 of its 256 W rows, and one M = 256 MMA issued by CTA 0 reads both CTAs' shared
+// memory and accumulates each CTA's 128 output rows in that CTA's TMEM.  Per CTA and K block the operand bytes drop
+// from 48 KB (128 x 256 single-CTA tile) to 32 KB for the same tensor work, which is what bounds the long-K GEMMs
+// (their operands stream from L2).  Protocol (the CTA pair shares barrier offsets):
+//   full[s]   CTA 0 only: arrive + expect the stage's bytes of both CTAs; both CTAs' TMA loads complete on it;
+//   empty[s]  both CTAs: CTA 0's MMA commit arrives on the pair's empty[s] once the stage is consumed;
+//   tfull[a]  both CTAs: CTA 0's commit after a tile's last MMA;
+//   tempty[a] CTA 0 only: 16 arrivals (8 epilogue warps per CTA) once both CTAs hold the accumulator in registers.
+// Both CTAs allocate TMEM with cta_group::2 from the same warp and free it after a cluster barrier.  No multicast load.
+constexpr int kPairStages = 6;
+constexpr int kPairABytes = kBM * kBK * 2, kPairBBytes = 128 * kBK * 2;
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr int kPairSmem = kPairStages * kPairStageBytes + kEpiWarps * kSlotBytes + 1024 + 256;
+
+T2W_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of `smem_addr`'s counterpart in CTA `rank` of the cluster.
+T2W_DEV uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+T2W_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+T2W_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory that completes on an mbarrier of either CTA of the pair.
+T2W_DEV void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y, uint32_t mbar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster_addr)
+      : "memory");
+}
+T2W_DEV void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar`'s counterparts in both CTAs of the pair once this thread's issued MMAs have completed.
+T2W_DEV void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"((unsigned short)3)
+               : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(320, 1)
+    k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                const __grid_constant__ CUtensorMap tmC, const DevArgs p) {
+  constexpr int BN = 256;
+  constexpr int BOX_COLS = epi_f32_out(EPI) ? 32 : 64;
+  constexpr int N_BOXES = BN / BOX_COLS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPairStages * kPairABytes;
+  uint8_t* sOut = sB + kPairStages * kPairBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kEpiWarps * kSlotBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmC);
+  }
+  pdl_wait();
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
+  tc_fence_after();
+  pdl_launch();
+  const uint32_t tmem = *tmem_slot;
+
+  const int kb_per_tap = p.K / kBK;
+  const int num_kb = kb_per_tap * p.taps;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer of this CTA's half of every stage
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += n_pairs) {
+        const int m0 = (tile / p.tiles_n) * (2 * kBM) + (int)rank * kBM, n0 = (tile % p.tiles_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          const int tap = kb / kb_per_tap, kk = (kb - tap * kb_per_tap) * kBK;
+          tma_load_2d_pair(sA + stage * kPairABytes, &tmA, kk, m0 + p.tap_row0 + tap, fb);
+          tma_load_2d_pair(sB + stage * kPairBBytes, &tmW, tap * p.K + kk, n0 + (int)rank * 128, fb);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {  // the pair's MMA issuer
+      constexpr uint32_t idesc = idesc_bf16(2 * kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += n_pairs, ++it) {
+        const int acc = it & 1;
+        if (!(ok = mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1u, p.err))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, p.err))) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * kPairABytes), b0 = smem_u32(sB + stage * kPairBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16_pair(d, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
+                          (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(&empty[stage]);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit_pair(&tfull[acc]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* slot = sOut + (warp - 2) * kSlotBytes;
+    int it = 0;
+    for (int tile = pair; tile < p.num_tiles; tile += n_pairs, ++it) {
+      const int acc = it & 1;
+      const int m0 = (tile / p.tiles_n) * (2 * kBM) + (int)rank * kBM, n0 = (tile % p.tiles_n) * BN;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int b = half; b < N_BOXES; b += 2) {
+        uint32_t raw[64];
+        if constexpr (epi_f32_out(EPI)) {
+          float f[32];
+          tmem_ld32(taddr + 32 * b, f);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(f[i]);
+        } else {
+          tmem_ld64_nowait(taddr + 64 * b, raw);
+          tmem_ld_wait();
+        }
+        if (b + 2 >= N_BOXES) {  // this warp's last TMEM load of the accumulator: release it to the pair's issuer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[acc]), 0));
+        }
+        epilogue_math<EPI>(p, n0, b, raw);
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(box_chunk(slot, lane, c)) =
+              make_uint4(raw[4 * c], raw[4 * c + 1], raw[4 * c + 2], raw[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, slot, n0 + b * BOX_COLS, m0 + q * kStRows);
+          bulk_commit();
+        }
+      }
+      if (p.done_flags && lane == 0 && m0 < p.M) {  // (CTA 1 of a pair past M when M % 256 == 128 stores nothing)
+        bulk_wait0();
+        fence_proxy_async_global();
+        __threadfence();
+        red_release_add_gpu(p.done_flags + m0 / kBM, 1);
+      }
+    }
+    if (lane == 0) bulk_wait0();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the pair's MMAs and TMEM loads are done in both CTAs
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
 template <int BN, int EPI, bool TMA_OUT>
 int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const WeightMaps* wm,
                 const CUtensorMap* tmC) {
@@ -379,6 +599,111 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   return T2W_OK;
 }
 
+
+// CTA-pair launch (cluster of 2): 256 x 256 tiles, grid of at most the pairs that can be resident at once.
+template <int EPI>
+int launch_pair_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const WeightMaps* wm,
+                     const CUtensorMap* tmC) {
+  static int max_pairs = -1;
+  if (max_pairs < 0) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_pair<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return T2W_ERR_CUDA;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(320);
+    cfg.dynamicSmemBytes = kPairSmem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, k_gemm_pair<EPI>, &cfg);
+    if (e != cudaSuccess || n <= 0) {
+      set_cuda_error(e);
+      return T2W_ERR_CUDA;
+    }
+    max_pairs = n;
+  }
+  const CUtensorMap* tmW = (wm && wm->has128) ? &wm->bn128 : nullptr;
+  CUtensorMap ma, mw, mc;
+  if (!tmA) {
+    if (!make_tmap_2d(&ma, a.A, 2, (uint64_t)a.rows_a, (uint64_t)a.K, (uint64_t)a.lda * 2, kBM, kBK)) return T2W_ERR_INVALID;
+    tmA = &ma;
+  }
+  if (!tmW) {
+    if (!make_tmap_2d(&mw, a.W, 2, (uint64_t)a.N, (uint64_t)a.K * a.taps, (uint64_t)a.K * a.taps * 2, 128, kBK))
+      return T2W_ERR_INVALID;
+    tmW = &mw;
+  }
+  if (!tmC) {
+    const bool f32 = epi_f32_out(EPI);
+    if (!make_tmap_2d(&mc, a.out, f32 ? 4 : 2, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)a.ldo * (f32 ? 4 : 2), kStRows,
+                      f32 ? 32 : 64))
+      return T2W_ERR_INVALID;
+    tmC = &mc;
+  }
+  DevArgs p;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.taps = a.taps;
+  p.tap_row0 = a.tap_row0;
+  p.tiles_n = a.N / 256;
+  p.num_tiles = ((a.M + 2 * kBM - 1) / (2 * kBM)) * p.tiles_n;
+  p.bias = a.bias;
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.qn_w = a.qn_w;
+  p.qn_b = a.qn_b;
+  p.kn_w = a.kn_w;
+  p.kn_b = a.kn_b;
+  p.qk_eps = a.qk_eps;
+  p.err = a.err;
+  p.done_flags = a.done_flags;
+  const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(320);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_pair<EPI>, *tmA, *tmW, *tmC, p);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  return T2W_OK;
+}
+
+// Which 256-column GEMMs run on CTA pairs.  Measured on B200 (bf16, N = 512): the pair kernel wins on long K once
+// there are several rounds of tiles (M = 44800: 3-tap conv 51.1 vs 54.5 us, K = 2048 75 vs 80 us), and loses on
+// short K and on one-and-a-bit rounds (M = 11264), where the epilogue or the partial last round bounds the time.
+// T2W_GEMM_PAIR=0 / =1 overrides the rule (never / always).
+bool use_pair(const GemmArgs& a) {
+  static int v = -2;
+  if (v == -2) {
+    const char* e = getenv("T2W_GEMM_PAIR");
+    v = (e && e[0] == '0') ? 0 : (e && e[0] == '1') ? 1 : -1;
+  }
+  if (v >= 0) return v == 1;
+  const long long pair_tiles = (long long)((a.M + 255) / 256) * (a.N / 256);
+  return a.K * a.taps >= 1536 && pair_tiles >= 3ll * (num_sms() / 2);
+}
+
 }  // namespace
 
 bool gemm_n_supported(int N) { return N == 80 || (N > 0 && N % 128 == 0); }
@@ -416,6 +741,15 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
     if (a.epi == T2W_EPI_F32) return launch_impl<80, T2W_EPI_F32, false>(a, st, tmA, tmW, tmC);
     if (a.epi == T2W_EPI_BF16) return launch_impl<80, T2W_EPI_BF16, false>(a, st, tmA, tmW, tmC);
     return T2W_ERR_INVALID;
+  }
+  if (bn == 256 && use_pair(a)) {
+    switch (a.epi) {
+      case T2W_EPI_F32: return launch_pair_impl<T2W_EPI_F32>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_BF16: return launch_pair_impl<T2W_EPI_BF16>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_GELU: return launch_pair_impl<T2W_EPI_GELU>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_QKV: return launch_pair_impl<T2W_EPI_QKV>(a, st, tmA, tmW, tmC);
+      default: return T2W_ERR_INVALID;
+    }
   }
   if (bn == 256) {
     switch (a.epi) {

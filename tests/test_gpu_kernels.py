@@ -151,6 +151,8 @@ def test_gemm_causal_conv_taps():
     (2560, 2048, 512, 1, "gelu"),   # 160 tiles
     (6400, 384, 256, 1, "bf16"),    # 128-column tiles: 150 tiles
     (11264, 1536, 512, 1, "qkv"),   # 528 tiles: 3-4 tiles per CTA through both TMEM accumulators
+    (45056, 512, 512, 3, "bf16"),   # long K with many rounds: the CTA-pair (cta_group::2) 256 x 256 kernel
+    (45184, 512, 2048, 1, "bf16"),  # CTA pairs with M % 256 == 128 (the last pair's second CTA has no rows)
 ])
 def test_gemm_full_size(M, N, K, taps, epi):
     """The solve's GEMM shapes at config-2 size (11264 packed rows) and tile counts that are not a multiple of the SM

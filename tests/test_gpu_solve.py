@@ -12,7 +12,7 @@ import torch
 
 from b200t2w.config import REFERENCE, TINY
 from b200t2w.solver import B200Solver, Layout, state_dict_from_module
-from b200t2w.workload import C1, C2, C3, Workload, make_streams
+from b200t2w.workload import C1, C2, C3, TARGET, Workload, make_streams
 from oracle import dit_oracle
 
 pytestmark = pytest.mark.gpu
@@ -96,7 +96,7 @@ def test_c1_full_size_vs_golden(ref, golden_dir):
     assert e < TOL_BF16
 
 
-@pytest.mark.parametrize("wl,sample", [(C2, (0, 15)), (C3, (0, 37))])
+@pytest.mark.parametrize("wl,sample", [(C2, (0, 15)), (C3, (0, 37)), (TARGET, (0, 63))])
 def test_batch_streams_vs_oracle(ref, wl, sample):
     m, s = ref
     streams = make_streams(wl)

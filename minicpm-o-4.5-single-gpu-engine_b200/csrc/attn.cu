@@ -311,19 +311,24 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         tmem_ld64_nowait(sbuf, sr);
         tmem_ld_wait();
         const int kb = j * kKTile;
-        // rows whose 64 keys of this tile are all valid skip the mask
-        const bool full = __all_sync(0xffffffffu, kb + kKTile <= lim);
-        // row max over valid keys: four independent partial maxima (short dependency chains)
-        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (full) {
-#pragma unroll
-          for (int i = 0; i < kKTile; ++i) mq[i & 3] = fmaxf(mq[i & 3], __uint_as_float(sr[i]));
-        } else {
+        // keys at or past the row's limit score -inf: they add nothing to the max and 2^-inf = 0 to P (warps whose
+        // rows see all 64 keys of the tile skip this)
+        if (!__all_sync(0xffffffffu, kb + kKTile <= lim)) {
 #pragma unroll
           for (int i = 0; i < kKTile; ++i)
-            if (kb + i < lim) mq[i & 3] = fmaxf(mq[i & 3], __uint_as_float(sr[i]));
+            if (kb + i >= lim) sr[i] = __float_as_uint(-INFINITY);
         }
-        float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
+        // row max: three-input maxima in four independent chains
+        float mq[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          mq[c] = fmax3(__uint_as_float(sr[16 * c]), __uint_as_float(sr[16 * c + 1]), __uint_as_float(sr[16 * c + 2]));
+#pragma unroll
+          for (int i = 3; i < 15; i += 2)
+            mq[c] = fmax3(mq[c], __uint_as_float(sr[16 * c + i]), __uint_as_float(sr[16 * c + i + 1]));
+          mq[c] = fmaxf(mq[c], __uint_as_float(sr[16 * c + 15]));
+        }
+        float mx = fmax3(fmaxf(mq[0], mq[1]), mq[2], mq[3]) * p.scale_log2;
         // raise the reference max only when it grows by more than the threshold (p <= 2^8 fits bf16 comfortably)
         const bool raise = mx > m + kRescaleThreshold;
         const float m_old = m;
@@ -335,14 +340,9 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         uint32_t u[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float2 a = fma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), c2, nm2);
-          float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
-          if (!full) {
-            const int kk = kb + 2 * i;
-            e.x = (kk < lim) ? e.x : 0.f;
-            e.y = (kk + 1 < lim) ? e.y : 0.f;
-          }
-          rsq[i & 3] = add2(rsq[i & 3], e);
+          const float2 a = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), c2, nm2);
+          const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
+          rsq[i & 3] = __fadd2_rn(rsq[i & 3], e);
           u[i] = pack_bf16x2(e.x, e.y);
         }
         tmem_st32(sbuf, u);
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
             tmem_st32(oreg + 32 * c, ou);
           }
         }
-        const float2 rs2 = add2(add2(rsq[0], rsq[1]), add2(rsq[2], rsq[3]));
+        const float2 rs2 = __fadd2_rn(__fadd2_rn(rsq[0], rsq[1]), __fadd2_rn(rsq[2], rsq[3]));
         l += rs2.x + rs2.y;
         tmem_st_wait();
         tc_fence_before();

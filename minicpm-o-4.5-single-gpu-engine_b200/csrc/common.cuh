@@ -263,6 +263,12 @@ T2W_DEV float2 add2(float2 a, float2 b) {
   return d;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+T2W_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 // 2^x with the hardware approximation (ex2.approx, flush-to-zero); used for softmax weights rounded to bf16 afterwards.
 T2W_DEV float exp2_approx(float x) {
   float y;

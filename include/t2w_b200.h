@@ -156,7 +156,10 @@ T2W_API int t2w_slots_copy_row(t2w_slots* p, int32_t src, int32_t dst, void* str
 T2W_API size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_slot_batch* b);
 /* The S-step CFG Euler solve of one window per request against the pools (bf16 path).  Attention gathers each CFG
  * row's key list from the pool; the causal convs read the row's cached frames in front of its window.  Asynchronous
- * on `stream`; the host arrays are read before the call returns.  flags: reserved (0). */
+ * on `stream`; the host arrays are read before the call returns (they are uploaded into the workspace on `stream`).
+ * flags T2W_FLAG_GRAPH: replay a CUDA graph per (sizes of the call's lists, workspace, input / output and pool
+ * buffers), captured the second time such a key is seen (the reference's FastDiT.capture, dit_fast.py:347-428);
+ * keep the input / output buffers fixed between calls (copy into static buffers) so the key repeats. */
 T2W_API int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* workspace, size_t workspace_bytes,
                             uint32_t flags, void* stream);
 

@@ -7,7 +7,9 @@ appends the window's keys (``[new, cache]`` order) and trims the cache to the pr
 the reference's key order, the trim) in Python, as the reference does, and runs the solve in the CUDA library
 (``t2w_solve_slots``): pools on the device, attention gathering each row's key list, conv caches filled in front of
 each window.  Method names and argument meaning follow ``FastDiT``: ``new_cache``, ``release``, ``clone``, ``solve``,
-``counts``, ``pool.in_use()``.
+``counts``, ``pool.in_use()``.  With ``use_graphs`` the solve replays a CUDA graph per call structure (sizes of the
+window and key lists), as ``FastDiT.capture`` does per bucket (``dit_fast.py:347-428``): inputs are copied into
+static buffers first (``dit_fast.py:463-469``), and a structure is captured the second time it is seen.
 """
 
 from __future__ import annotations
@@ -70,7 +72,8 @@ class B200FastDiT:
     (step, block) of one frame: steps * depth * 4 * hidden bytes).  ``max_streams``: concurrent requests (two
     conv-cache row slots each)."""
 
-    def __init__(self, solver: B200Solver, noise: torch.Tensor, n_slots: int = 32768, max_streams: int = 96):
+    def __init__(self, solver: B200Solver, noise: torch.Tensor, n_slots: int = 32768, max_streams: int = 96,
+                 use_graphs: bool = True):
         if solver.precision != "bf16":
             raise ValueError("the slot-pool solve runs the bf16 path")
         self.solver, self.cfg, self.device = solver, solver.cfg, solver.device
@@ -85,6 +88,8 @@ class B200FastDiT:
         self.cnn_free = list(range(n_rs - 1, 0, -1))
         self.cnn_scratch = 0
         self._ws = None
+        self.use_graphs = use_graphs
+        self._static = {}  # (tokens, requests, has cond) -> static input / output buffers of the graph path
         self.counts = {"graph": 0, "eager": 0}
 
     def close(self) -> None:
@@ -152,25 +157,35 @@ class B200FastDiT:
             rd.append(rows[r].cnn)
             wr.append(rows[r].cnn if keep[i] else self.cnn_scratch)
         dev = self.device
-        x0 = torch.cat([self.noise[:, o:o + t].t() for o, t in zip(lens, Ts)]).contiguous()
-        mu_t = torch.cat([m.t() for m in mu]).to(dev, torch.float32).contiguous()
-        cond_t = None
+        n_tok = sum(Ts)
+        key = (n_tok, n, cond is not None)
+        bufs = self._static.get(key)
+        if bufs is None:
+            z = lambda *sh: torch.zeros(*sh, dtype=torch.float32, device=dev)  # noqa: E731
+            bufs = {"x0": z(n_tok, mel), "mu": z(n_tok, mel), "cond": z(n_tok, mel) if cond is not None else None,
+                    "spk": z(n, mel), "out": z(n_tok, mel)}
+            self._static[key] = bufs
+        torch.cat([self.noise[:, o:o + t].t() for o, t in zip(lens, Ts)], out=bufs["x0"])
+        # inputs in pinned host memory are copied without stalling the host (pageable ones copy synchronously)
+        torch.cat([m.t().to(dev, torch.float32, non_blocking=True) for m in mu], out=bufs["mu"])
         if cond is not None:
-            cond_t = torch.cat([(c.t() if c is not None else torch.zeros(t, mel)).to(dev, torch.float32)
-                                for c, t in zip(cond, Ts)]).contiguous()
-        spk = spks.to(dev, torch.float32).contiguous()
-        out = torch.empty(sum(Ts), mel, device=dev)
+            torch.cat([(c.t() if c is not None else torch.zeros(t, mel)).to(dev, torch.float32, non_blocking=True)
+                       for c, t in zip(cond, Ts)], out=bufs["cond"])
+        bufs["spk"].copy_(spks.to(dev, torch.float32, non_blocking=True))
+        out = bufs["out"]
         P = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
         arrs = [L.i32_array(a) for a in (Ts, kv_len, kv_idx, rd, wr)]  # alive until the call returns
         ip = [ctypes.cast(a, ctypes.POINTER(ctypes.c_int32)) for a in arrs]
-        b = L.SlotBatch(n, *ip, P(x0), P(mu_t), P(cond_t), P(spk), P(out))
+        b = L.SlotBatch(n, *ip, P(bufs["x0"]), P(bufs["mu"]), P(bufs["cond"]), P(bufs["spk"]), P(out))
         need = int(self._lib.t2w_slot_workspace_bytes(self.solver._h, self._p, ctypes.byref(b)))
         if not need:
             raise L.T2WError("t2w_slot_workspace_bytes", -1)
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=dev)
-        L.call("t2w_solve_slots", self.solver._h, self._p, ctypes.byref(b), P(self._ws), need, 0, self._stream())
-        self.counts["eager"] += 1
+        before = self.solver.counts()["graph"]
+        L.call("t2w_solve_slots", self.solver._h, self._p, ctypes.byref(b), P(self._ws), self._ws.numel(),
+               L.FLAG_GRAPH if self.use_graphs else 0, self._stream())
+        self.counts["graph" if self.solver.counts()["graph"] > before else "eager"] += 1
         # the reference's cache order and trim (dit_fast.py:482-490)
         for i, c in enumerate(caches):
             for r, nw in ((rows[i], new[i]), (rows[n + i], new[n + i])):
@@ -184,6 +199,6 @@ class B200FastDiT:
                     self.pool.release(nw)
         res, o = [], 0
         for t in Ts:
-            res.append(out[o:o + t].t().float())
+            res.append(out[o:o + t].t().clone())  # the static buffer is rewritten by the next call
             o += t
         return res

@@ -172,6 +172,7 @@ struct t2w_solver {
   int* err = nullptr;
   cudaStream_t cap_stream = nullptr;
   std::unordered_map<uint64_t, cudaGraphExec_t> graphs;
+  std::unordered_map<uint64_t, int> slot_seen;  // slot-solve graph keys seen so far (captured on the second call)
   std::unordered_map<uintptr_t, uint64_t> ws_meta;  // workspace -> plan key of the index arrays it holds
   std::vector<cudaEvent_t> prof_events;
   int64_t n_replays = 0, n_captures = 0, n_eager = 0;
@@ -661,6 +662,51 @@ int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
   return T2W_OK;
 }
 
+// Launch the solve graph cached under `key` on `st`, capturing `enqueue` into it first if there is none.  The capture
+// runs on the solver's own stream (the caller's may be the legacy default stream, which cannot be captured); capturing
+// executes nothing.  At most kMaxGraphs graphs are kept: past that, the stream is synchronised and one is dropped.
+constexpr size_t kMaxGraphs = 64;
+template <class F>
+int replay(t2w_solver* s, uint64_t key, cudaStream_t st, F&& enqueue) {
+  auto g = s->graphs.find(key);
+  if (g == s->graphs.end()) {
+    cudaStreamCaptureStatus cs;
+    T2W_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: use flags = 0
+    if (s->graphs.size() >= kMaxGraphs) {
+      T2W_CUDA(cudaStreamSynchronize(st));
+      auto victim = s->graphs.begin();
+      cudaGraphExecDestroy(victim->second);
+      s->graphs.erase(victim);
+    }
+    if (!s->cap_stream) T2W_CUDA(cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking));
+    T2W_CUDA(cudaStreamBeginCapture(s->cap_stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue(s->cap_stream);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(s->cap_stream, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ec != cudaSuccess) {
+      set_cuda_error(ec);
+      return T2W_ERR_CUDA;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) {
+      set_cuda_error(ei);
+      return T2W_ERR_CUDA;
+    }
+    g = s->graphs.emplace(key, exec).first;
+    ++s->n_captures;
+  }
+  T2W_CUDA(cudaGraphLaunch(g->second, st));
+  ++s->n_replays;
+  return T2W_OK;
+}
+
 // Varlen attention with a per-call device work list (one entry per 128-query tile of each sequence).
 int attn_varlen_alloc(const void* qkv, int rows, int heads, int n_seq, const int32_t* seq_row, const int32_t* seq_len,
                       const int32_t* prompt_len, void* out, uint8_t* out_sf, void* stream) {
@@ -945,39 +991,7 @@ int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_byte
   for (const void* p : {(const void*)ws, (const void*)b->x0, (const void*)b->mu, (const void*)b->cond,
                         (const void*)b->spk, (const void*)b->out})
     key = mix(key, reinterpret_cast<uint64_t>(p));
-  auto g = s->graphs.find(key);
-  if (g == s->graphs.end()) {
-    cudaStreamCaptureStatus cs;
-    T2W_CUDA(cudaStreamIsCapturing(st, &cs));
-    if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: use flags = 0
-    // Capture on the solver's own stream (the caller's may be the legacy default stream, which cannot be captured);
-    // capturing executes nothing, and the graph is launched on the caller's stream below.
-    if (!s->cap_stream) T2W_CUDA(cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking));
-    T2W_CUDA(cudaStreamBeginCapture(s->cap_stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_solve(s, pl, *b, ws, s->cap_stream);
-    cudaGraph_t graph = nullptr;
-    const cudaError_t ec = cudaStreamEndCapture(s->cap_stream, &graph);
-    if (rc) {
-      if (graph) cudaGraphDestroy(graph);
-      return rc;
-    }
-    if (ec != cudaSuccess) {
-      set_cuda_error(ec);
-      return T2W_ERR_CUDA;
-    }
-    cudaGraphExec_t exec = nullptr;
-    const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (ei != cudaSuccess) {
-      set_cuda_error(ei);
-      return T2W_ERR_CUDA;
-    }
-    g = s->graphs.emplace(key, exec).first;
-    ++s->n_captures;
-  }
-  T2W_CUDA(cudaGraphLaunch(g->second, st));
-  ++s->n_replays;
-  return T2W_OK;
+  return replay(s, key, st, [&](cudaStream_t cs) { return enqueue_solve(s, pl, *b, ws, cs); });
 }
 
 int t2w_profile_solve(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_bytes, void* stream, float* ms,
@@ -1110,7 +1124,6 @@ size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t
 
 int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* ws, size_t ws_bytes, uint32_t flags,
                     void* stream) {
-  (void)flags;
   if (!s || !p || !b || !ws || !b->x0 || !b->mu || !b->spk || !b->out) return T2W_ERR_INVALID;
   if (s->precision != T2W_PREC_BF16) return T2W_ERR_UNSUPPORTED;
   Plan pl;
@@ -1129,6 +1142,20 @@ int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* 
   pb.cond = b->cond;
   pb.spk = b->spk;
   pb.out = b->out;
+  // The launches depend on the plan's sizes and the buffers only: the slot lists, conv rows and work list are read
+  // from the workspace, where upload_meta has just put this call's.  A graph per such key, captured the second time
+  // the key is seen (a key met once, as while caches still grow towards their trimmed length, runs eagerly).
+  uint64_t key = 0x510750175107ull;
+  for (long long v : {(long long)pl.n_streams, (long long)pl.n_tok, (long long)pl.half_rows, (long long)pl.rows,
+                      (long long)pl.n_work, (long long)pl.kv_idx.size(), (long long)pl.conv_rows.size(),
+                      (long long)pl.tok_slot.size()})
+    key = mix(key, (uint64_t)v);
+  for (const void* q : {(const void*)ws, (const void*)b->x0, (const void*)b->mu, (const void*)b->cond,
+                        (const void*)b->spk, (const void*)b->out, (const void*)p->kv, (const void*)p->cnn})
+    key = mix(key, reinterpret_cast<uint64_t>(q));
+  if (s->slot_seen.size() > 4096) s->slot_seen.clear();
+  if ((flags & T2W_FLAG_GRAPH) && (s->graphs.count(key) || ++s->slot_seen[key] >= 2))
+    return replay(s, key, st, [&](cudaStream_t cs) { return enqueue_solve(s, pl, pb, ws, cs, nullptr, p); });
   T2W_TRY(enqueue_solve(s, pl, pb, ws, st, nullptr, p));
   ++s->n_eager;
   return T2W_OK;

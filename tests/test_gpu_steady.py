@@ -105,3 +105,31 @@ def test_steady_reference_config_vs_oracle():
             e = rel(out[(i, k)], w["ref_mel"])
             print(f"reference config stream {i} window {k}: rel-L2 {e:.3e}")
             assert e < TOL_BF16
+
+
+def test_steady_graph_replay_equals_eager():
+    """use_graphs: once the windows reach the trimmed steady length the call structure repeats, its graph is captured
+    on the second sight and replayed; every window's mel equals the eager solve's bit for bit."""
+    m = dit_oracle.build_model(TINY, seed=0, noise_frames=4096)
+    solver = B200Solver(TINY, state_dict_from_module(m))
+    fds = {g: B200FastDiT(solver, m.rand_noise[0], n_slots=4096, max_streams=4, use_graphs=g) for g in (False, True)}
+    gen = torch.Generator().manual_seed(9)
+    mel, n, P, T = TINY.mel, 3, 40, 32  # caches trimmed to P + 100 keys from the fifth window on
+    spk = torch.randn(n, mel, generator=gen)
+    windows = [([torch.randn(mel, P, generator=gen) for _ in range(n)], [torch.randn(mel, P, generator=gen) for _ in range(n)])]
+    windows += [([torch.randn(mel, T, generator=gen) for _ in range(n)], None) for _ in range(10)]
+    outs = {}
+    for g, fd in fds.items():
+        caches = [fd.new_cache() for _ in range(n)]
+        for c in caches:
+            c.keep = P
+        outs[g] = [fd.solve(caches, mu, spk, cond, [True] * n) for mu, cond in windows]
+        fd.solver.check()
+        for c in caches:
+            fd.release(c)
+        assert fd.pool.in_use() == 0
+    assert fds[False].counts["graph"] == 0
+    assert fds[True].counts["graph"] >= 3, fds[True].counts
+    for wa, wb in zip(outs[False], outs[True]):
+        for a, b in zip(wa, wb):
+            assert torch.equal(a, b)

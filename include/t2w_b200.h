@@ -152,6 +152,12 @@ T2W_API int t2w_slots_destroy(t2w_slots* p);
 T2W_API int t2w_slots_copy(t2w_slots* p, const int32_t* src, const int32_t* dst, int32_t n, void* stream);
 /* Conv caches of every (step, block): row slot src -> dst, or zeros into dst when src < 0 (FastDiT.new_cache). */
 T2W_API int t2w_slots_copy_row(t2w_slots* p, int32_t src, int32_t dst, void* stream);
+/* The pools' device memory and geometry, for callers that move caches in and out of slots themselves (the module-level
+ * forward_chunk(..., cnn_cache, att_cache) adapter, token2wav_batch.py:643-644): kv bf16 [n_sb][n_slots][2 hidden]
+ * (slot s of (step, block) sb: K of head h at columns h*64 .. +63, V at hidden + h*64 .. +63), cnn bf16
+ * [n_sb][n_rowslots][2 convs][2 frames, oldest first][hidden], n_sb = steps * depth with sb = step * depth + block. */
+T2W_API int t2w_slots_pools(const t2w_slots* p, void** kv, void** cnn, int32_t* n_sb, int32_t* n_slots,
+                            int32_t* n_rowslots, int32_t* hidden);
 /* Workspace bytes of a t2w_solve_slots call (0 on an invalid batch). */
 T2W_API size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_slot_batch* b);
 /* The S-step CFG Euler solve of one window per request against the pools (bf16 path).  Attention gathers each CFG

@@ -64,6 +64,14 @@ class FastCache:
         return len(self.rows[0].order)
 
 
+class _DeviceArray:
+    """A device buffer handed to torch through the CUDA array interface (no copy; the owner keeps it alive)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "strides": None, "version": 2}
+
+
 class B200FastDiT:
     """``FastDiT`` on the B200 kernels.
 
@@ -135,9 +143,96 @@ class B200FastDiT:
                        self._stream())
         return out
 
+    # --- caches as tensors (the module-level forward_chunk adapter) ---------------------------------------------------
+    def pools(self) -> tuple:
+        """The slot pools as torch views (no copy): K/V [steps * depth, n_slots, 2H] (K heads, then V heads) and conv
+        caches [steps * depth, n_rowslots, 2 convs, 2 frames (oldest first), H], bf16."""
+        if getattr(self, "_pool_views", None) is None:
+            kv, cn = ctypes.c_void_p(), ctypes.c_void_p()
+            n_sb, n_slots, n_rs, H = (ctypes.c_int32() for _ in range(4))
+            L.call("t2w_slots_pools", self._p, ctypes.byref(kv), ctypes.byref(cn), ctypes.byref(n_sb),
+                   ctypes.byref(n_slots), ctypes.byref(n_rs), ctypes.byref(H))
+            with torch.cuda.device(self.device):
+                k = torch.as_tensor(_DeviceArray(kv.value, (n_sb.value, n_slots.value, 2 * H.value), "<i2"),
+                                    device=self.device).view(torch.bfloat16)
+                c = torch.as_tensor(_DeviceArray(cn.value, (n_sb.value, n_rs.value, 2, 2, H.value), "<i2"),
+                                    device=self.device).view(torch.bfloat16)
+            self._pool_views = (k, c)
+        return self._pool_views
+
+    def load_cache(self, att: torch.Tensor, cnn: torch.Tensor, keep: int = 0) -> FastCache:
+        """A cache holding the reference's tensors (``token2wav_batch.py:643-644``): ``att`` [steps, depth, 2, heads,
+        L, 2 * 64] (K then V of each head, keys in the reference's order), ``cnn`` [steps, depth, 2, 2H, 2] (each
+        conv's last two input frames, conv 1 then conv 2).  Values are stored in bf16."""
+        c = self.cfg
+        S, D, H, nh = c.steps, c.depth, c.hidden, c.heads
+        Lk = int(att.shape[4])
+        if tuple(att.shape) != (S, D, 2, nh, Lk, 2 * c.head_dim) or tuple(cnn.shape) != (S, D, 2, 2 * H, 2):
+            raise ValueError(f"caches: expected att [{S}, {D}, 2, {nh}, L, {2 * c.head_dim}] and cnn [{S}, {D}, 2, "
+                             f"{2 * H}, 2], got {tuple(att.shape)} and {tuple(cnn.shape)}")
+        kv, cn = self.pools()
+        fc = self.new_cache()
+        fc.keep = keep
+        a = att.to(self.device, torch.bfloat16)
+        cc = cnn.to(self.device, torch.bfloat16)
+        for half, row in enumerate(fc.rows):
+            row.order = self.pool.alloc(Lk)
+            if Lk:
+                x = a[:, :, half]  # [S, D, heads, L, 128]
+                k = x[..., :c.head_dim].permute(0, 1, 3, 2, 4).reshape(S * D, Lk, H)
+                v = x[..., c.head_dim:].permute(0, 1, 3, 2, 4).reshape(S * D, Lk, H)
+                kv[:, torch.tensor(row.order, device=self.device)] = torch.cat([k, v], dim=2)
+            cn[:, row.cnn] = cc[:, :, half].reshape(S * D, 2, H, 2).permute(0, 1, 3, 2)
+        return fc
+
+    def export_cache(self, fc: FastCache, dtype=torch.float32) -> tuple:
+        """``fc``'s caches as the reference's tensors ``(att, cnn)`` (layouts of ``load_cache``)."""
+        c = self.cfg
+        S, D, H, nh, hd = c.steps, c.depth, c.hidden, c.heads, c.head_dim
+        kv, cn = self.pools()
+        Lk = fc.length
+        att = torch.empty(S, D, 2, nh, Lk, 2 * hd, dtype=dtype, device=self.device)
+        cnn = torch.empty(S, D, 2, 2 * H, 2, dtype=dtype, device=self.device)
+        for half, row in enumerate(fc.rows):
+            if Lk:
+                x = kv[:, torch.tensor(row.order, device=self.device)]  # [S * D, L, 2H]
+                k = x[..., :H].reshape(S, D, Lk, nh, hd).permute(0, 1, 3, 2, 4)
+                v = x[..., H:].reshape(S, D, Lk, nh, hd).permute(0, 1, 3, 2, 4)
+                att[:, :, half] = torch.cat([k, v], dim=-1).to(dtype)
+            cnn[:, :, half] = cn[:, row.cnn].permute(0, 1, 3, 2).reshape(S, D, 2 * H, 2).to(dtype)
+        return att, cnn
+
+    @torch.inference_mode()
+    def forward_chunk(self, mu, spks, cond, n_timesteps: int = 10, temperature: float = 1.0, cnn_cache=None,
+                      att_cache=None):
+        """``CausalConditionalCFM.forward_chunk(mu, spks, cond, n_timesteps, temperature, cnn_cache, att_cache)`` for
+        one request (``tools/spike/t2w_profile.py:63-64``): ``mu`` / ``cond`` [1, mel, T], ``spks`` [1, mel] (after
+        the affine layer), caches as in ``load_cache`` (None: empty).  The noise is the flow's fixed noise at the
+        cache length, times ``temperature``.  Returns ``(mel [1, mel, T] fp32, new_cnn, new_att)`` with the new keys
+        in front of the old ones and nothing trimmed (the caller trims, as the reference's callers do); caches come
+        back in ``att_cache``'s dtype (fp32 when None)."""
+        c = self.cfg
+        if n_timesteps != c.steps:
+            raise ValueError(f"solver built for {c.steps} steps, asked for {n_timesteps}")
+        T = int(mu.shape[2])
+        dtype = att_cache.dtype if att_cache is not None else torch.float32
+        if att_cache is None:
+            att_cache = torch.zeros(c.steps, c.depth, 2, c.heads, 0, 2 * c.head_dim)
+        if cnn_cache is None:
+            cnn_cache = torch.zeros(c.steps, c.depth, 2, 2 * c.hidden, 2)
+        fc = self.load_cache(att_cache, cnn_cache, keep=int(att_cache.shape[4]) + T)  # nothing to trim
+        try:
+            mel = self.solve([fc], [mu[0]], spks.reshape(1, -1), [cond[0]] if cond is not None else None, [True],
+                             temperature=temperature)[0]
+            new_att, new_cnn = self.export_cache(fc, dtype)
+        finally:
+            self.release(fc)
+        return mel[None], new_cnn, new_att
+
     # --- solve --------------------------------------------------------------------------------------------------------
     @torch.inference_mode()
-    def solve(self, caches: list, mu: list, spks: torch.Tensor, cond: list | None, keep: list) -> list:
+    def solve(self, caches: list, mu: list, spks: torch.Tensor, cond: list | None, keep: list,
+              temperature: float = 1.0) -> list:
         """One window per request (``FastDiT.solve``): ``mu[i]`` [mel, T_i], ``spks`` [n, mel] (after the affine
         layer), ``cond[i]`` [mel, T_i] or None (zeros; ``cond`` None: zeros for all).  Requests with ``keep[i]`` keep
         the window's keys and conv caches, trimmed as the reference trims them; the others (final flushes) leave their
@@ -166,6 +261,8 @@ class B200FastDiT:
                     "spk": z(n, mel), "out": z(n_tok, mel)}
             self._static[key] = bufs
         torch.cat([self.noise[:, o:o + t].t() for o, t in zip(lens, Ts)], out=bufs["x0"])
+        if temperature != 1.0:  # the fixed noise scaled as CausalConditionalCFM.forward_chunk scales it
+            bufs["x0"].mul_(temperature)
         # inputs in pinned host memory are copied without stalling the host (pageable ones copy synchronously)
         torch.cat([m.t().to(dev, torch.float32, non_blocking=True) for m in mu], out=bufs["mu"])
         if cond is not None:

@@ -86,6 +86,8 @@ _SIGS = {
     "t2w_slots_destroy": ([_P], ctypes.c_int),
     "t2w_slots_copy": ([_P, ctypes.POINTER(_I), ctypes.POINTER(_I), _I, _P], ctypes.c_int),
     "t2w_slots_copy_row": ([_P, _I, _I, _P], ctypes.c_int),
+    "t2w_slots_pools": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                         ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_slot_workspace_bytes": ([_P, _P, ctypes.POINTER(SlotBatch)], ctypes.c_size_t),
     "t2w_solve_slots": ([_P, _P, ctypes.POINTER(SlotBatch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
     "t2w_e4m3_sf_bytes": ([_I, _I], ctypes.c_size_t),

@@ -1113,6 +1113,18 @@ int t2w_slots_copy_row(t2w_slots* p, int32_t src, int32_t dst, void* stream) {
                              static_cast<cudaStream_t>(stream));
 }
 
+int t2w_slots_pools(const t2w_slots* p, void** kv, void** cnn, int32_t* n_sb, int32_t* n_slots, int32_t* n_rowslots,
+                    int32_t* hidden) {
+  if (!p || !kv || !cnn || !n_sb || !n_slots || !n_rowslots || !hidden) return T2W_ERR_INVALID;
+  *kv = p->kv;
+  *cnn = p->cnn;
+  *n_sb = p->n_sb;
+  *n_slots = p->n_slots;
+  *n_rowslots = p->n_rowslots;
+  *hidden = p->H;
+  return T2W_OK;
+}
+
 size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_slot_batch* b) {
   if (!s || !p || !b) return 0;
   Plan pl;

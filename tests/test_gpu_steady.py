@@ -133,3 +133,29 @@ def test_steady_graph_replay_equals_eager():
     for wa, wb in zip(outs[False], outs[True]):
         for a, b in zip(wa, wb):
             assert torch.equal(a, b)
+
+
+def test_forward_chunk_with_caches_vs_oracle():
+    """The reference's module-level forward_chunk(mu, spks, cond, n_timesteps, temperature, cnn_cache, att_cache): a
+    prompt window with empty caches, then chunk windows fed the caches the previous call returned, against the
+    oracle's window solve: the mel, the new attention cache (keys [new, old], nothing trimmed) and the conv cache
+    within the bf16 tolerance; the slots are all returned."""
+    m = dit_oracle.build_model(TINY, seed=0, noise_frames=2048)
+    fd = B200FastDiT(B200Solver(TINY, state_dict_from_module(m)), m.rand_noise[0], n_slots=1024, max_streams=2)
+    gen = torch.Generator().manual_seed(21)
+    mel = TINY.mel
+    spk = torch.randn(1, mel, generator=gen)
+    cache = dit_oracle.StreamCache(TINY, keep=10 ** 6)
+    att = cnn = None
+    for j, (T, temp) in enumerate(((40, 1.0), (24, 1.0), (24, 0.7))):
+        mu = torch.randn(1, mel, T, generator=gen)
+        cond = torch.randn(1, mel, T, generator=gen) if j == 0 else None
+        out, cnn, att = fd.forward_chunk(mu, spk, cond, TINY.steps, temp, cnn, att)
+        x0 = m.rand_noise[0, :, cache.length:cache.length + T] * temp
+        ref = dit_oracle.solve_window(m, cache, x0, mu[0], spk[0], cond[0] if cond is not None else None)
+        assert out.shape == (1, mel, T) and out.dtype == torch.float32
+        assert att.shape == cache.att.shape and cnn.shape == cache.cnn.shape
+        e = (rel(out[0], ref), rel(att, cache.att), rel(cnn, cache.cnn))
+        print(f"window {j} (T={T}, temperature {temp}): rel-L2 mel {e[0]:.2e}, att cache {e[1]:.2e}, cnn cache {e[2]:.2e}")
+        assert max(e) < TOL_BF16, e
+    assert fd.pool.in_use() == 0

@@ -302,6 +302,25 @@ T2W_DEV int ld_acquire_gpu(const int* p) {
 T2W_DEV void red_release_add_gpu(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// L2 eviction priority for data a later kernel reads again (an access policy for .L2::cache_hint loads and stores;
+// no device setting is changed): lines touched with it are evicted after the normal ones.
+T2W_DEV uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+T2W_DEV float4 ld_f4_l2hint(const float4* a, uint64_t policy) {
+  float4 v;
+  asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(a), "l"(policy));
+  return v;
+}
+T2W_DEV void st_f4_l2hint(float4* a, float4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(a), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w), "l"(policy)
+               : "memory");
+}
 // Async-proxy (TMA) global writes ordered before this thread's later generic-proxy operations.
 T2W_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 // Bounded wait until *f >= target; false (and T2W_ERR_TIMEOUT in err) after kWaitLimitNs.

@@ -57,6 +57,9 @@ def args_():
     ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3", "c4", "steady"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="also record one graph-replayed solve with torch.profiler (CUPTI) and report each kernel "
+                         "position's share of the solve's span (the time by which it extends the critical path)")
     return ap.parse_args()
 
 
@@ -69,6 +72,57 @@ def shard(name: str, rank: int, world: int) -> Workload:
     if world == 1:
         return base
     return Workload(f"{base.name}[rank {rank}]", base.seed + 1000 * rank, base.lengths)
+
+
+def timeline_from_events(evs: list) -> dict:
+    """Per-position time of one solve from its kernels' (name, GPU start us, GPU end us).  Kernels are named by their
+    place in a DiT block: a GEMM by its epilogue (k_gemm<BN, EPI, ...>: EPI 0 in_proj, 2 fc1 with GELU, 4 QKV,
+    BN 80 the final linear) or, for the plain bf16 ones, by the kernel before it (attention -> proj, add_ln_mod ->
+    conv1, ln_mish -> conv2, fc1 -> fc2); a LayerNorm kernel by the GEMM it follows.  "exposed" is the time by which a
+    kernel extends the end of the solve so far, so the exposed times add up to the solve's span (kernels overlap
+    through programmatic dependent launch and early starts on completion counters)."""
+    import re
+
+    evs = sorted(evs, key=lambda e: e[1])
+    if not evs:
+        return {}
+    names = []
+    for n, _, _ in evs:
+        m = re.search(r"k_gemm\w*<(\d+), (\d+)", n)
+        if m:
+            bn, epi = int(m.group(1)), int(m.group(2))
+            prev = names[-1].split(" after ")[0] if names else ""
+            nm = ("final" if bn == 80 else "in_proj" if epi == 0 else "fc1" if epi == 2 else "qkv" if epi == 4
+                  else {"attn": "proj", "ln_mish": "conv2", "fc1": "fc2"}.get(prev, "conv1"))
+        elif "k_add_ln_mod" in n or "k_ln_mish" in n:
+            nm = ("add_ln_mod" if "add_ln_mod" in n else "ln_mish") + (f" after {names[-1]}" if names else "")
+        else:
+            m = re.search(r"k_(\w+)", n)
+            nm = m.group(1) if m else "other"
+            nm = "attn" if nm.startswith("attn") else nm
+        names.append(nm)
+    exposed, busy, last = {}, {}, evs[0][1]
+    for (_, s0, e0), nm in zip(evs, names):
+        busy[nm] = busy.get(nm, 0.0) + (e0 - s0)
+        if e0 > last:
+            exposed[nm] = exposed.get(nm, 0.0) + (e0 - last)
+            last = e0
+    return {"solve_ms": round((evs[-1][2] - evs[0][1]) / 1000, 3), "kernels": len(evs),
+            "exposed_ms": {k: round(v / 1000, 3) for k, v in sorted(exposed.items(), key=lambda x: -x[1])},
+            "kernel_ms": {k: round(v / 1000, 3) for k, v in sorted(busy.items(), key=lambda x: -x[1])}}
+
+
+def timeline(solve) -> dict:
+    """One solve under torch.profiler with CUDA activities only (CUPTI records the kernels inside the CUDA graph with
+    their GPU start and end): ``timeline_from_events`` of it."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as pr:
+        solve()
+        torch.cuda.synchronize()
+    return timeline_from_events([(e.name, e.time_range.start, e.time_range.end) for e in pr.events()
+                                 if e.device_type.name == "CUDA"])
 
 
 def flops_per_solve(cfg: DiTConfig, lengths) -> tuple[float, float]:
@@ -344,6 +398,7 @@ def main() -> None:
     e2e_value = world * chunk_frames * a.steps / (max_e2e_ms / 1000)
 
     prof = solver.profile(layout, bufs) if not a.no_profile else {}
+    tl = timeline(solve) if a.timeline and rank == 0 else None
     gemm_flops, attn_flops = flops_per_solve(cfg, layout_pairs := list(zip(layout.prompt, layout.chunk)))
     peaks = {}
     try:
@@ -394,7 +449,7 @@ def main() -> None:
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "latency_ms_p50": statistics.median(e2e_t)},
             "gpu_launches": launches * a.steps if launches else None, "roofline": roofline, "cpu_baseline": cpu,
-            "clocks": clk}), flush=True)
+            "clocks": clk, **({"timeline": tl} if tl else {})}), flush=True)
     solver.close()
     if world > 1:
         torch.distributed.barrier()

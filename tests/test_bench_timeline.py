@@ -1,0 +1,44 @@
+"""CPU: bench.py's per-position timeline of a solve (names kernels by their place in a DiT block and attributes the
+solve's span to the kernels that extend it), on a hand-made event list shaped like one block."""
+
+import importlib.util
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def load_bench():
+    spec = importlib.util.spec_from_file_location("bench_for_test", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    argv = sys.argv
+    try:
+        sys.argv = ["bench.py"]
+        spec.loader.exec_module(mod)
+    finally:
+        sys.argv = argv
+    return mod
+
+
+def g(bn, epi):
+    return f"void t2w::(anonymous namespace)::k_gemm<{bn}, {epi}, true>(CUtensorMap_st, CUtensorMap_st, DevArgs)"
+
+
+def test_timeline_names_and_exposed_span():
+    b = load_bench()
+    row = "void t2w::(anonymous namespace)::k_add_ln_mod<4, false>(float*, ...)"
+    mish = "void t2w::(anonymous namespace)::k_ln_mish<4, false>(...)"
+    attn = "void t2w::(anonymous namespace)::k_attn<false, false>(...)"
+    # one block: qkv, attn, proj, aln, conv1, ln_mish, conv2, aln, fc1, fc2, aln (overlapping starts)
+    seq = [(g(256, 4), 0, 20), (attn, 15, 45), (g(256, 1), 40, 60), (row, 55, 70), (g(256, 1), 69, 95),
+           (mish, 90, 99), (g(256, 1), 98, 125), (row, 120, 130), (g(256, 2), 129, 155), (g(256, 1), 154, 185),
+           (row, 180, 190)]
+    t = b.timeline_from_events(seq)
+    assert t["kernels"] == 11
+    assert abs(t["solve_ms"] - 0.190) < 1e-9
+    assert abs(sum(t["exposed_ms"].values()) - t["solve_ms"]) < 1e-6
+    assert set(t["exposed_ms"]) == {"qkv", "attn", "proj", "add_ln_mod after proj", "conv1", "ln_mish after conv1",
+                                    "conv2", "add_ln_mod after conv2", "fc1", "fc2", "add_ln_mod after fc2"}
+    assert abs(t["exposed_ms"]["attn"] - 0.025) < 1e-9  # ends 25 us after QKV
+    assert abs(t["kernel_ms"]["proj"] - 0.020) < 1e-9
+    assert b.timeline_from_events([]) == {}

@@ -88,9 +88,10 @@ def timeline_from_events(evs: list) -> dict:
         return {}
     names = []
     for n, _, _ in evs:
-        m = re.search(r"k_gemm\w*<(\d+), (\d+)", n)
-        if m:
-            bn, epi = int(m.group(1)), int(m.group(2))
+        m = re.search(r"k_gemm<(\d+), (\d+)", n)
+        mp = re.search(r"k_gemm(?:_pair|8)<(\d+)>", n)  # the CTA-pair and FP8 GEMMs: k_gemm_pair<EPI>, k_gemm8<EPI>
+        if m or mp:
+            bn, epi = (int(m.group(1)), int(m.group(2))) if m else (256, int(mp.group(1)))
             prev = names[-1].split(" after ")[0] if names else ""
             nm = ("final" if bn == 80 else "in_proj" if epi == 0 else "fc1" if epi == 2 else "qkv" if epi == 4
                   else {"attn": "proj", "ln_mish": "conv2", "fc1": "fc2"}.get(prev, "conv1"))

@@ -42,3 +42,8 @@ def test_timeline_names_and_exposed_span():
     assert abs(t["exposed_ms"]["attn"] - 0.025) < 1e-9  # ends 25 us after QKV
     assert abs(t["kernel_ms"]["proj"] - 0.020) < 1e-9
     assert b.timeline_from_events([]) == {}
+    # the CTA-pair and FP8 GEMMs carry only their epilogue as a template argument
+    pair = "void t2w::(anonymous namespace)::k_gemm_pair<1>(CUtensorMap_st, CUtensorMap_st, CUtensorMap_st, DevArgs)"
+    fp8 = "void t2w::(anonymous namespace)::k_gemm8<2>(...)"
+    t = b.timeline_from_events([(attn, 0, 10), (pair, 5, 20), (fp8, 19, 30)])
+    assert list(t["kernel_ms"]) == ["proj", "fc1", "attn"] or set(t["kernel_ms"]) == {"attn", "proj", "fc1"}

@@ -46,4 +46,4 @@ def test_timeline_names_and_exposed_span():
     pair = "void t2w::(anonymous namespace)::k_gemm_pair<1>(CUtensorMap_st, CUtensorMap_st, CUtensorMap_st, DevArgs)"
     fp8 = "void t2w::(anonymous namespace)::k_gemm8<2>(...)"
     t = b.timeline_from_events([(attn, 0, 10), (pair, 5, 20), (fp8, 19, 30)])
-    assert list(t["kernel_ms"]) == ["proj", "fc1", "attn"] or set(t["kernel_ms"]) == {"attn", "proj", "fc1"}
+    assert set(t["kernel_ms"]) == {"attn", "proj", "fc1"}

@@ -76,6 +76,36 @@ TINY = replace(REFERENCE, hidden=128, depth=2, heads=2, mlp_ratio=4.0)
 """A small config with the same kernel shapes class (head_dim 64), for fast golden fixtures and unit tests."""
 
 
+def config_from_module(cfm, steps: int | None = None, base: DiTConfig = REFERENCE) -> DiTConfig:
+    """The ``DiTConfig`` of a loaded ``CausalConditionalCFM``-like module, read off its attributes as the reference's
+    ``FastDiT`` reads them (``engine/runtime/dit_fast.py:107-145``): depth = ``len(est.blocks)``; heads / head_dim from
+    ``blocks[0].attn``; hidden = ``in_proj.out_features``; mel = ``in_proj.in_features // 4``; the MLP width from
+    ``blocks[0].mlp.fc1``; the eps of ``norm1``, ``norm_final``, ``attn.q_norm`` and ``conv.block[3]``; the conv
+    kernel from ``conv.block[1]``; the sinusoid size from ``t_embedder.mlp[0]``; ``cfm.inference_cfg_rate``.  The
+    sinusoid's ``t_scale`` and ``max_period`` are not module attributes and come from ``base``.  Raises ValueError
+    when the module contradicts itself (q_norm / k_norm eps, norm1 / norm2 / norm3 eps, mel vs ``out_channels``)."""
+    est = cfm.estimator
+    b0 = est.blocks[0]
+    a = b0.attn
+    hidden = int(est.in_proj.out_features)
+    mel = int(est.in_proj.in_features) // 4
+    if int(est.in_proj.in_features) != 4 * mel:
+        raise ValueError("in_proj.in_features must be 4 * mel ([x, mu, spk, cond])")
+    if int(getattr(est, "out_channels", mel)) != mel:
+        raise ValueError("estimator.out_channels must equal in_proj.in_features // 4")
+    if a.q_norm.eps != a.k_norm.eps:
+        raise ValueError("attn.q_norm and attn.k_norm must share one eps")
+    if not (b0.norm1.eps == b0.norm2.eps == b0.norm3.eps):
+        raise ValueError("norm1 / norm2 / norm3 must share one eps")
+    ffn = int(b0.mlp.fc1.out_features)
+    return replace(
+        base, mel=mel, hidden=hidden, depth=len(est.blocks), heads=int(a.num_heads), head_dim=int(a.head_dim),
+        mlp_ratio=ffn / hidden, steps=int(steps) if steps is not None else base.steps,
+        cfg_rate=float(cfm.inference_cfg_rate), freq_dim=int(est.t_embedder.mlp[0].in_features),
+        eps_block=float(b0.norm1.eps), eps_final=float(est.final_layer.norm_final.eps), eps_qk=float(a.q_norm.eps),
+        eps_conv=float(b0.conv.block[3].eps), conv_kernel=int(b0.conv.block[1].kernel_size[0]))
+
+
 def t_schedule(steps: int):
     """The solver's t recurrence in fp32, as ``BatchedToken2Wav._solve`` runs it (token2wav_batch.py:669-693):
     ``t_span = 1 - cos(linspace(0, 1, S + 1) * pi / 2)``; ``t`` starts at ``t_span[0]`` and is accumulated as ``t + dt``

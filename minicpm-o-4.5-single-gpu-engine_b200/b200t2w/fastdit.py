@@ -99,6 +99,34 @@ class B200FastDiT:
         self.use_graphs = use_graphs
         self._static = {}  # (tokens, requests, has cond) -> static input / output buffers of the graph path
         self.counts = {"graph": 0, "eager": 0}
+        self.scratch = 0  # pool slots reserved for pad rows: none (pad rows never reach the pool here)
+
+    @classmethod
+    def from_cfm(cls, cfm, steps: int, n_slots: int = 32768, max_streams: int = 96, device="cuda",
+                 use_graphs: bool = False, setup_tokens: int = 0, fused_residual: bool = False,
+                 fused_conv: bool = False) -> "B200FastDiT":
+        """Built as the reference builds ``FastDiT(cfm, steps, ...)`` (``engine/runtime/dit_fast.py:99-146``): the
+        config read off ``cfm.estimator`` (``config_from_module``), the weights packed to bf16 from the module's own
+        parameters, the fixed noise ``cfm.rand_noise[0]``.  ``setup_tokens``, ``fused_residual`` and ``fused_conv``
+        select graph-bucket padding and kernel fusions inside the reference's solve; this solve has no row buckets and
+        always runs its fused residual / norm / conv-gather kernels, so they are accepted and change nothing (the
+        reference's own check that ``fused_conv`` needs ``fused_residual`` is kept)."""
+        from .config import config_from_module
+        from .solver import state_dict_from_module
+
+        if fused_conv and not fused_residual:
+            raise ValueError("fused_conv is a fused_residual option")
+        if int(setup_tokens) < 0:
+            raise ValueError("setup_tokens must be >= 0")
+        cfg = config_from_module(cfm, steps=steps)
+        solver = B200Solver(cfg, state_dict_from_module(cfm), precision="bf16", device=device)
+        return cls(solver, cfm.rand_noise[0], n_slots=n_slots, max_streams=max_streams, use_graphs=use_graphs)
+
+    def capture_all(self, row_buckets=None) -> int:
+        """The reference captures one graph per row bucket up front (``dit_fast.py:347-428``).  Here a graph is keyed
+        by the call's exact structure and captured the second time that structure is solved, so nothing is captured
+        ahead; returns 0 (graphs captured now)."""
+        return 0
 
     def close(self) -> None:
         if getattr(self, "_p", None) is not None and self._p.value:

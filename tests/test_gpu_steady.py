@@ -159,3 +159,26 @@ def test_forward_chunk_with_caches_vs_oracle():
         print(f"window {j} (T={T}, temperature {temp}): rel-L2 mel {e[0]:.2e}, att cache {e[1]:.2e}, cnn cache {e[2]:.2e}")
         assert max(e) < TOL_BF16, e
     assert fd.pool.in_use() == 0
+
+
+def test_from_cfm_vs_reference_driver(golden_dir):
+    """Built the reference's way, ``FastDiT(cfm, steps, n_slots, max_streams, device, use_graphs, ...)``: the same
+    windows as the reference driver within the bf16 tolerance, and the attributes its worker reads
+    (``pool.in_use() - scratch``, ``cnn_free``, ``counts``, ``capture_all()``)."""
+    rec = torch.load(os.path.join(golden_dir, "steady_tiny.pt"))
+    m = dit_oracle.build_model(TINY, seed=0, noise_frames=2048)
+    fd = B200FastDiT.from_cfm(m, TINY.steps, n_slots=4096, max_streams=8, device="cuda", use_graphs=True,
+                              setup_tokens=64, fused_residual=True, fused_conv=True)
+    assert fd.cfg == TINY and fd.capture_all() == 0
+    free0 = len(fd.cnn_free)
+    out, caches = run_interleaved(fd, rec["streams"])
+    for i, s in enumerate(rec["streams"]):
+        for k, w in enumerate(s["windows"]):
+            e = rel(out[(i, k)], w["ref_mel"])
+            assert e < TOL_BF16, (i, k, e)
+    assert fd.pool.in_use() - fd.scratch == 2 * sum(c.length for c in caches)
+    assert len(fd.cnn_free) == free0 - 2 * len(caches)
+    assert fd.counts["graph"] + fd.counts["eager"] == max(len(s["windows"]) for s in rec["streams"])
+    for c in caches:
+        fd.release(c)
+    assert fd.pool.in_use() == 0 and len(fd.cnn_free) == free0

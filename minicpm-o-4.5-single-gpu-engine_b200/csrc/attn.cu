@@ -44,6 +44,13 @@ struct ItemEntry {
 constexpr int kSmem = 2 * kPipeBytes + 1024 + 512 + kMaxCtaItems * (int)sizeof(ItemEntry);
 constexpr int kTmemCols = 512;  // pipeline p: S/P buffers at 192 p + {0, 64}, O at 192 p + 128
 constexpr float kRescaleThreshold = 8.f;
+// The two pipelines of a CTA take consecutive heads of the same query tiles, so left alone they run the same phases at
+// the same moments and contend for the same issue slots and special-function units.  Pipeline 1's softmax starts this
+// many cycles after its first S tile is ready (about one tile's softmax), and the offset persists because the
+// pipelines' items have equal lengths.  Measured on the config-2 solve (16 x 350 frames, 160 launches): attention
+// 4.19 -> 3.78 ms per solve; 0.7K / 1.4K / 2.1K / 2.8K / 3.5K / 5.6K cycles gave 4.10 / 4.04 / 3.78 / 3.81 / 3.91 /
+// 4.03 ms.
+constexpr long long kPipeStagger = 2400;
 
 struct DevArgs {
   const AttnWork* work;
@@ -305,6 +312,11 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       for (int j = 0; j < n_kt; ++j, ++t) {
         // warp-uniform: tcgen05.ld / st below are .sync.aligned
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.s_full[t & 1], (t >> 1) & 1, p.err)))) break;
+        if (t == 0 && q == 1) {  // offset pipeline 1 from pipeline 0 (bounded spin)
+          const long long t0 = clock64();
+          while (clock64() - t0 < kPipeStagger) {
+          }
+        }
         tc_fence_after();
         const uint32_t sbuf = preg + 64 * (t & 1);
         uint32_t sr[64];

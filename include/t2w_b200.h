@@ -221,13 +221,16 @@ T2W_API int t2w_ln_mish(const void* x_bf16, const float* w, const float* b, floa
 #define T2W_EPI_F32 0  /* out fp32 = acc + bias */
 #define T2W_EPI_BF16 1 /* out bf16 = acc + bias */
 #define T2W_EPI_GELU 2 /* out bf16 = gelu_tanh(acc + bias) */
+#define T2W_EPI_RESID 3 /* out fp32 += gate * (acc + bias), in place: the gated residual (gate: N floats, qk[0]) */
 #define T2W_EPI_QKV 4  /* out bf16 = [LN_q(q) | LN_k(k) | v] per 64-wide head (q/k affine norms) */
 #define T2W_EPI_GELU_FP8 8 /* t2w_gemm_e4m3 only: out e4m3 = gelu_tanh(acc + bias) with its scale atoms */
 
 /* C[M, N] = sum_tap A[m + tap_row0 + tap, :K] . W[n, tap*K : (tap+1)*K] then the epilogue.  A bf16 [rows_a, lda],
  * W bf16 [N, taps*K]; rows outside [0, rows_a) read as zero (causal-conv taps).  M % 128 == 0, K % 64 == 0,
  * N % 128 == 0 or N == 80.  qk: for T2W_EPI_QKV, [qn_w, qn_b, kn_w, kn_b] (head_dim each) and qk_eps; q columns
- * [0, N/3), k [N/3, 2N/3).  The gated residual of proj / conv2 / fc2 is applied by t2w_add_ln_mod. */
+ * [0, N/3), k [N/3, 2N/3).  qk: for T2W_EPI_RESID, qk[0] is the gate (N floats); out, gate and bias 16-byte aligned.
+ * The solve applies the gated residual of proj with T2W_EPI_RESID; those of conv2 / fc2 are added from their bf16
+ * outputs by t2w_add_ln_mod. */
 T2W_API int t2w_gemm(const void* A_bf16, int32_t lda, int32_t rows_a, const void* W_bf16, const float* bias, int32_t M,
                      int32_t N, int32_t K, int32_t taps, int32_t tap_row0, int32_t epi, void* out, int32_t ldo,
                      const float* const* qk, float qk_eps, void* stream);

@@ -17,7 +17,7 @@ STATUS = {-1: "invalid argument or shape", -2: "CUDA error", -3: "out of device 
           -5: "unsupported config or device", -6: "workspace too small"}
 PREC = {"bf16": 0, "fp8": 1}
 FLAG_GRAPH = 1
-EPI = {"f32": 0, "bf16": 1, "gelu": 2, "qkv": 4, "gelu_fp8": 8}
+EPI = {"f32": 0, "bf16": 1, "gelu": 2, "resid": 3, "qkv": 4, "gelu_fp8": 8}
 KERNEL_CLASSES = ["pack", "gemm_in", "ln_mod", "gemm_qkv", "attn", "gemm_proj", "gemm_conv1", "ln_mish", "gemm_conv2",
                   "gemm_fc1", "gemm_fc2", "gemm_final", "euler"]
 W_GLOBAL = ["estimator.t_embedder.mlp.0.weight", "estimator.t_embedder.mlp.0.bias", "estimator.t_embedder.mlp.2.weight",

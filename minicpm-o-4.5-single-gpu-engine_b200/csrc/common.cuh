@@ -309,9 +309,11 @@ T2W_DEV uint64_t l2_policy_evict_last() {
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+// L2 only (.cg): the rows read this way are rewritten by other SMs between two reads (the residual stream, updated by
+// GEMM epilogues and read by the norms after them), so no SM may serve them from its own L1.
 T2W_DEV float4 ld_f4_l2hint(const float4* a, uint64_t policy) {
   float4 v;
-  asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+  asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "l"(a), "l"(policy));
   return v;

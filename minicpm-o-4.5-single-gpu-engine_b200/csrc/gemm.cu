@@ -28,7 +28,7 @@ constexpr int kStRows = 32;                // rows of one TMA store: one epilogu
 constexpr int kSlotBytes = kStRows * 128;  // one warp's staging slot: 32 rows x 128 bytes
 constexpr int kEpiWarps = 8;
 
-__host__ __device__ constexpr bool epi_f32_out(int epi) { return epi == T2W_EPI_F32; }
+__host__ __device__ constexpr bool epi_f32_out(int epi) { return epi == T2W_EPI_F32 || epi == T2W_EPI_RESID; }
 
 template <int BN, int EPI, bool TMA_OUT>
 struct GemmCfg {
@@ -62,6 +62,7 @@ struct DevArgs {
   float qk_eps;
   int* err;
   int* done_flags;  // per 128-row block: +1 from each epilogue warp once its stores of a tile are complete
+  const float* gate;  // T2W_EPI_RESID: per-column gate of the residual update
 };
 
 T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -69,6 +70,14 @@ T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, i
                    reinterpret_cast<uint64_t>(map)),
                "r"(x), "r"(y), "r"(smem_u32(smem_src))
                : "memory");
+}
+// out[box] += smem box (fp32 add performed in L2), evict-last: the residual stream it updates stays resident.
+T2W_DEV void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::
+          "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(smem_u32(smem_src)), "l"(policy)
+      : "memory");
 }
 T2W_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 T2W_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -113,6 +122,17 @@ T2W_DEV void epilogue_math(const DevArgs& p, int n0, int b, uint32_t (&raw)[64])
     const float* bias = p.bias + n0 + 32 * b;
 #pragma unroll
     for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) + __ldg(bias + i));
+  } else if constexpr (EPI == T2W_EPI_RESID) {  // the update gate * (acc + bias); the TMA reduce adds it to out
+    const float4* bias = reinterpret_cast<const float4*>(p.bias + n0 + 32 * b);
+    const float4* gate = reinterpret_cast<const float4*>(p.gate + n0 + 32 * b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 bb = __ldg(bias + j), gg = __ldg(gate + j);
+      raw[4 * j] = __float_as_uint(gg.x * (__uint_as_float(raw[4 * j]) + bb.x));
+      raw[4 * j + 1] = __float_as_uint(gg.y * (__uint_as_float(raw[4 * j + 1]) + bb.y));
+      raw[4 * j + 2] = __float_as_uint(gg.z * (__uint_as_float(raw[4 * j + 2]) + bb.z));
+      raw[4 * j + 3] = __float_as_uint(gg.w * (__uint_as_float(raw[4 * j + 3]) + bb.w));
+    }
   } else {
     const int c0 = n0 + 64 * b;
     float2 v[32];
@@ -290,7 +310,10 @@ __global__ void __launch_bounds__(320, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, slot, n0 + b * C::BOX_COLS, m0 + q * kStRows);
+            if constexpr (EPI == T2W_EPI_RESID)
+              tma_reduce_add_2d(&tmC, slot, n0 + b * C::BOX_COLS, m0 + q * kStRows, l2_policy_evict_last());
+            else
+              tma_store_2d(&tmC, slot, n0 + b * C::BOX_COLS, m0 + q * kStRows);
             bulk_commit();
           }
         }
@@ -510,7 +533,10 @@ __global__ void __launch_bounds__(320, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, slot, n0 + b * BOX_COLS, m0 + q * kStRows);
+          if constexpr (EPI == T2W_EPI_RESID)
+            tma_reduce_add_2d(&tmC, slot, n0 + b * BOX_COLS, m0 + q * kStRows, l2_policy_evict_last());
+          else
+            tma_store_2d(&tmC, slot, n0 + b * BOX_COLS, m0 + q * kStRows);
           bulk_commit();
         }
       }
@@ -590,6 +616,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.qk_eps = a.qk_eps;
   p.err = a.err;
   p.done_flags = TMA_OUT ? a.done_flags : nullptr;
+  p.gate = a.gate;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   cudaError_t e = launch_k(k_gemm<BN, EPI, TMA_OUT>, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tmA, *tmW, *tmC, p);
   if (e != cudaSuccess) {
@@ -666,6 +693,7 @@ int launch_pair_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA,
   p.qk_eps = a.qk_eps;
   p.err = a.err;
   p.done_flags = a.done_flags;
+  p.gate = a.gate;
   const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
@@ -737,6 +765,9 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   const int bn = gemm_block_n_for(a.N, a.M, a.epi);
   if (!bn) return T2W_ERR_INVALID;
   if (a.epi == T2W_EPI_QKV && (a.N % 3 || (a.N / 3) % 64 || !a.qn_w || !a.qn_b || !a.kn_w || !a.kn_b)) return T2W_ERR_INVALID;
+  if (a.epi == T2W_EPI_RESID && (!a.gate || (reinterpret_cast<uintptr_t>(a.out) & 15) ||
+                                 (reinterpret_cast<uintptr_t>(a.gate) & 15) || (reinterpret_cast<uintptr_t>(a.bias) & 15)))
+    return T2W_ERR_INVALID;
   if (bn == 80) {
     if (a.epi == T2W_EPI_F32) return launch_impl<80, T2W_EPI_F32, false>(a, st, tmA, tmW, tmC);
     if (a.epi == T2W_EPI_BF16) return launch_impl<80, T2W_EPI_BF16, false>(a, st, tmA, tmW, tmC);
@@ -748,6 +779,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
       case T2W_EPI_BF16: return launch_pair_impl<T2W_EPI_BF16>(a, st, tmA, tmW, tmC);
       case T2W_EPI_GELU: return launch_pair_impl<T2W_EPI_GELU>(a, st, tmA, tmW, tmC);
       case T2W_EPI_QKV: return launch_pair_impl<T2W_EPI_QKV>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_RESID: return launch_pair_impl<T2W_EPI_RESID>(a, st, tmA, tmW, tmC);
       default: return T2W_ERR_INVALID;
     }
   }
@@ -757,6 +789,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
       case T2W_EPI_BF16: return launch_impl<256, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_GELU: return launch_impl<256, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_QKV: return launch_impl<256, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_RESID: return launch_impl<256, T2W_EPI_RESID, true>(a, st, tmA, tmW, tmC);
       default: return T2W_ERR_INVALID;
     }
   }
@@ -765,6 +798,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
     case T2W_EPI_BF16: return launch_impl<128, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_GELU: return launch_impl<128, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_QKV: return launch_impl<128, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_RESID: return launch_impl<128, T2W_EPI_RESID, true>(a, st, tmA, tmW, tmC);
     default: return T2W_ERR_INVALID;
   }
 }

@@ -56,6 +56,7 @@ struct GemmArgs {
   // Completion counters, one per 128-row block: each epilogue warp adds 1 once its stores of a tile are complete
   // (8 per tile; a block is done at 8 * N / BN).  Lets the row kernel that follows start early (RowWait).
   int* done_flags = nullptr;
+  const float* gate = nullptr;  // T2W_EPI_RESID: out (fp32) += gate[n] * (acc + bias[n]), N floats
 };
 // Column tile the launcher picks for an N-wide output of M rows with epilogue `epi` (0: N unsupported).
 int gemm_block_n_for(int N, int M, int epi);

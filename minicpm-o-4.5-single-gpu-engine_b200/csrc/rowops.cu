@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(256) k_ln_mod(const float* __restrict__ h, int
 }
 
 // h += g * y (the gated residual of the preceding GEMM's bf16 output y, fp32, stored back), then out = LN(h) * scale1 +
-// shift (dit_kernels.py:35-60's add_ln_mod, with the residual kept in fp32).  y == nullptr: plain LN + modulation.
+// shift (dit_kernels.py:35-60's add_ln_mod, with the residual kept in fp32).  y == nullptr: plain LN + modulation (the
+// bf16 solve, whose GEMM epilogues update h themselves; with flags, the rows wait for that GEMM's tiles).
 // Whether this warp's row may be read: plain programmatic ordering, or its 128-row block's GEMM tiles are complete.
 T2W_DEV bool row_ready(const RowWait& wt, int row) {
   bool ok = true;
@@ -458,7 +459,7 @@ bool row_out_ok(const RowOut& o) {
 int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,
                       int rows, int C, const RowOut& o, const uint8_t* pad, cudaStream_t st, const RowWait& wt) {
   if (rows <= 0) return T2W_OK;
-  if ((y && !g) || !row_out_ok(o) || (wt.flags && !y)) return T2W_ERR_INVALID;
+  if ((y && !g) || !row_out_ok(o)) return T2W_ERR_INVALID;
   return o.sf ? add_ln_mod_impl<true>(h, y, g, shift, scale1, eps, rows, C, o, pad, st, wt)
               : add_ln_mod_impl<false>(h, y, g, shift, scale1, eps, rows, C, o, pad, st, wt);
 }

@@ -491,7 +491,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     T2W_TRY(launch_gemm(g, st, &tm_hx, &s->tm_in, &st_h));
     // The gated residual of each branch (h += g * y) is applied by the norm that follows it (add_ln_mod), as the
     // reference's fused_residual path does (dit_fast.py:306-344); the MLP's pending (g, y) is added by the next block's
-    // first norm or by the final layer's norm.
+    // first norm or by the final layer's norm.  bf16 path, attention branch: the proj GEMM's epilogue adds
+    // g * (acc + bias) to h itself (T2W_EPI_RESID, a TMA reduce-add in L2) and the norm after it reads h alone.  proj
+    // has K = 512, so its second round of tiles is short and that norm sat on the critical path (measured at config 2:
+    // norm 1.32 -> 0.48 ms, proj 2.14 -> 2.82 ms per solve).  After conv2 and fc2 (K = 1536 / 2048) the norm of the
+    // early row blocks hides under the GEMM's last round, while the fp32 reduce lengthens the last tile's epilogue:
+    // there the same change cost 0.2 ms each, so they keep the bf16 output.
     const float* pend_g = nullptr;
     const __nv_bfloat16* pend_y = nullptr;
     int* pend_done = nullptr;
@@ -574,13 +579,14 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_attn(at_use, st, &tm_att_q, &tm_att_kv));
       GemmArgs pr = GemmArgs();
       pr.rows_a = R; pr.M = R; pr.err = s->err;
-      pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_BF16; pr.out = y; pr.ldo = H;
+      pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_RESID; pr.out = h; pr.ldo = H;
+      pr.gate = g_a;
       pr.done_flags = dn;
       T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
-      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_y));
+      T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_h));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st, waits(dn)));
+      T2W_TRY(launch_add_ln_mod(h, nullptr, nullptr, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st, waits(dn)));
       if (pl.slots)  // cached conv-input frames in front of each window, and the window's last two saved
         T2W_TRY(launch_conv_cache(a, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb(), sp->cnn_slot(), st));
       GemmArgs k1 = GemmArgs();
@@ -1289,12 +1295,13 @@ int t2w_gemm(const void* A, int32_t lda, int32_t rows_a, const void* W, const fl
   g.epi = epi;
   g.out = out;
   g.ldo = ldo;
-  if (qk) {
+  if (qk && epi == T2W_EPI_QKV) {
     g.qn_w = qk[0];
     g.qn_b = qk[1];
     g.kn_w = qk[2];
     g.kn_b = qk[3];
   }
+  if (qk && epi == T2W_EPI_RESID) g.gate = qk[0];
   g.qk_eps = qk_eps;
   return launch_gemm(g, static_cast<cudaStream_t>(stream));
 }

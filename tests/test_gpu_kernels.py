@@ -191,6 +191,52 @@ def test_gemm_full_size(M, N, K, taps, epi):
     assert float(blk.max()) < (1e-4 if f32 else 1e-2), float(blk.max())
 
 
+@pytest.mark.parametrize("M,N,K,taps", [
+    (384, 512, 512, 1),      # one partial round
+    (11264, 512, 512, 1),    # proj at config 2: 176 tiles on 148 SMs
+    (11264, 512, 512, 3),    # conv2 (causal taps) at config 2
+    (11264, 512, 2048, 1),   # fc2 at config 2
+    (512, 384, 256, 1),      # 128-column tiles
+    (45184, 512, 2048, 1),   # CTA pairs, M % 256 == 128 (the last pair's second CTA has no rows)
+])
+def test_gemm_gated_residual(M, N, K, taps):
+    """T2W_EPI_RESID: h += gate * (A W^T + bias) in place in fp32 (the solve's proj / conv2 / fc2 epilogue), checked
+    whole and per 128-row block, with a row stride wider than N; two launches from the same h are bitwise equal."""
+    A = rand_bf16(M, K)
+    W, b = rand_bf16(N, taps * K, scale=0.03), torch.randn(N, device="cuda") * 0.1
+    gate = torch.randn(N, device="cuda")
+    ldo = N + 128
+    h0 = torch.randn(M, ldo, device="cuda") * 2
+    outs = []
+    for _ in range(2):
+        h = h0.clone()
+        gemm(A, W, b, M, N, K, "resid", h, ldo, taps=taps, tap_row0=-2 if taps == 3 else 0, qk=[gate])
+        outs.append(h)
+    assert torch.equal(outs[0], outs[1])
+    h = outs[0]
+    if taps == 3:
+        Ap = torch.cat([torch.zeros(2, K, device="cuda"), A.float()])
+        y = torch.cat([Ap[0:M], Ap[1:M + 1], Ap[2:M + 2]], dim=1) @ W.float().t() + b
+    else:
+        y = A.float() @ W.float().t() + b
+    ref = h0.clone()
+    ref[:, :N] += gate * y
+    assert torch.equal(h[:, N:], h0[:, N:])  # columns past N untouched
+    e = rel(h[:, :N] - h0[:, :N], ref[:, :N] - h0[:, :N])  # error relative to the update itself
+    assert e < 1e-5, e
+    d = (h[:, :N] - ref[:, :N]).view(M // 128, 128, N).norm(dim=(1, 2))
+    assert float((d / (gate * y).view(M // 128, 128, N).norm(dim=(1, 2))).max()) < 1e-4
+
+
+def test_gemm_gated_residual_rejects_bad_args():
+    A, W, b = rand_bf16(128, 64), rand_bf16(256, 64), torch.zeros(256, device="cuda")
+    h = torch.zeros(128, 256, device="cuda")
+    qk_arr = None
+    rc = L.load().t2w_gemm(P(A), 64, 128, P(W), P(b), 128, 256, 64, 1, 0, L.EPI["resid"], P(h), 256, qk_arr,
+                           ctypes.c_float(0.0), S())
+    assert rc == -1  # T2W_ERR_INVALID: no gate
+
+
 def _attn_ref(qkv, seqs, heads):
     H = heads * 64
     out = torch.zeros(qkv.shape[0], H, device="cuda")

@@ -300,6 +300,67 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
     const uint32_t preg = tmem + 192 * q + lanes, oreg = preg + 128;
     int t = 0;  // global tile counter of this pipeline
     bool ok = true;
+    // The previous item's output, finished during the next item's first tile: its last P V has completed by then, so
+    // the O read does not wait on the tensor core (O is read before that item's first P V overwrites it: o_free).
+    struct Pending {
+      AttnWork w;
+      int h, lim, t_last;
+      float l;
+    } pend;
+    bool have_pend = false;
+    auto finish = [&](const Pending& pd) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&b.o_done[pd.t_last & 1], (pd.t_last >> 1) & 1, p.err))) return false;
+      tc_fence_after();
+      float o[kD];
+      tmem_ld32p(oreg, o);
+      tmem_ld32p(oreg + 32, o + 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.o_free);
+      const AttnWork& w = pd.w;
+      const int h = pd.h, lim = pd.lim;
+      const float l = pd.l;
+      if (lim > 0) {
+        const float inv = 1.f / l;
+        const int row = w.q_row + r;
+        if constexpr (E4M3) {
+          // two 32-column blocks per head, each with its own power-of-two scale
+          uint8_t* dst = static_cast<uint8_t*>(p.out) + (size_t)row * p.ldo + h * kD;
+          uint32_t eb[2];
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * hb + i]));
+            eb[hb] = ue8m0_for_amax(amax * inv);
+            const float f = inv * ue8m0_inv(eb[hb]);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float* q = o + 32 * hb + 16 * u;
+              uint4 v;
+              v.x = e4m3x4(q[0] * f, q[1] * f, q[2] * f, q[3] * f);
+              v.y = e4m3x4(q[4] * f, q[5] * f, q[6] * f, q[7] * f);
+              v.z = e4m3x4(q[8] * f, q[9] * f, q[10] * f, q[11] * f);
+              v.w = e4m3x4(q[12] * f, q[13] * f, q[14] * f, q[15] * f);
+              reinterpret_cast<uint4*>(dst)[2 * hb + u] = v;
+            }
+          }
+          *reinterpret_cast<uint16_t*>(p.out_sf + sf_offset(row, 2 * h, p.ldo)) = (uint16_t)(eb[0] | (eb[1] << 8));
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + h * kD;
+#pragma unroll
+          for (int u = 0; u < kD / 8; ++u) {
+            uint4 v;
+            v.x = pack_bf16x2(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
+            v.y = pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
+            v.z = pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
+            v.w = pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
+            reinterpret_cast<uint4*>(dst)[u] = v;
+          }
+        }
+      }
+      return true;
+    };
     for (int k = 0; ok; ++k) {
       const int item = q + 2 * blockIdx.x + k * stride;
       if (item >= p.n_items) break;
@@ -379,60 +440,23 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         const float2 rs2 = __fadd2_rn(__fadd2_rn(rsq[0], rsq[1]), __fadd2_rn(rsq[2], rsq[3]));
         l += rs2.x + rs2.y;
         tmem_st_wait();
+        if (j == 0 && have_pend) {  // the previous item's output (before this tile's P V can overwrite O)
+          if (!(ok = finish(pend))) break;
+          have_pend = false;
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&b.p_full[t & 1]);
       }
       if (!ok) break;
-      // the item's last P V (tile t - 1)
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.err)))) break;
-      tc_fence_after();
-      float o[kD];
-      tmem_ld32p(oreg, o);
-      tmem_ld32p(oreg + 32, o + 32);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&b.o_free);
-      if (lim > 0) {
-        const float inv = 1.f / l;
-        const int row = w.q_row + r;
-        if constexpr (E4M3) {
-          // two 32-column blocks per head, each with its own power-of-two scale
-          uint8_t* dst = static_cast<uint8_t*>(p.out) + (size_t)row * p.ldo + h * kD;
-          uint32_t eb[2];
-#pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            float amax = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * hb + i]));
-            eb[hb] = ue8m0_for_amax(amax * inv);
-            const float f = inv * ue8m0_inv(eb[hb]);
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const float* q = o + 32 * hb + 16 * u;
-              uint4 v;
-              v.x = e4m3x4(q[0] * f, q[1] * f, q[2] * f, q[3] * f);
-              v.y = e4m3x4(q[4] * f, q[5] * f, q[6] * f, q[7] * f);
-              v.z = e4m3x4(q[8] * f, q[9] * f, q[10] * f, q[11] * f);
-              v.w = e4m3x4(q[12] * f, q[13] * f, q[14] * f, q[15] * f);
-              reinterpret_cast<uint4*>(dst)[2 * hb + u] = v;
-            }
-          }
-          *reinterpret_cast<uint16_t*>(p.out_sf + sf_offset(row, 2 * h, p.ldo)) = (uint16_t)(eb[0] | (eb[1] << 8));
-        } else {
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + h * kD;
-#pragma unroll
-          for (int u = 0; u < kD / 8; ++u) {
-            uint4 v;
-            v.x = pack_bf16x2(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
-            v.y = pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
-            v.z = pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
-            v.w = pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
-            reinterpret_cast<uint4*>(dst)[u] = v;
-          }
-        }
-      }
+      pend.w = w;
+      pend.h = h;
+      pend.lim = lim;
+      pend.t_last = t - 1;
+      pend.l = l;
+      have_pend = true;
     }
+    if (ok && have_pend) finish(pend);
   }
   __syncthreads();
   if (warp == 2) {

@@ -65,6 +65,8 @@ struct DevArgs {
   const __nv_bfloat16* pool;
   const int* kv_idx;
   int pool_ld;
+  const void* pf;  // L2 prefetch of the next GEMM's weights, 64 KB per CTA
+  unsigned pf_bytes;
 };
 
 // 16-byte global -> shared copy (zero-filled when src_bytes == 0) and the arrival of this thread's outstanding copies
@@ -145,6 +147,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_kv);
   }
+  if (threadIdx.x == 0) prefetch_l2_piece(p.pf, p.pf_bytes, blockIdx.x);
   pdl_wait();
   if (warp == 2) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -493,7 +496,8 @@ int launch_attn_impl(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q
     tm_kv = &mkv;
   }
   const int n_items = a.n_work * a.heads;
-  DevArgs p{a.work, n_items, a.heads, a.out, a.out_sf, a.heads * kD, a.scale_log2, a.err, a.pool, a.kv_idx, a.pool_ld};
+  DevArgs p{a.work,    n_items,  a.heads, a.out,  a.out_sf, a.heads * kD, a.scale_log2,
+            a.err,     a.pool,   a.kv_idx, a.pool_ld, a.pf, a.pf_bytes};
   int grid = (n_items + 1) / 2;
   if (grid > num_sms()) grid = num_sms();
   // each CTA stages at most kMaxCtaItems items in shared memory

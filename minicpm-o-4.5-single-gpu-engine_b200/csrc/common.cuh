@@ -237,6 +237,20 @@ T2W_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 T2W_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 T2W_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---------------------------------------------------------------- L2 prefetch
+// Bring piece `piece` (64 KB) of [p, p + bytes) into L2: the weights of a GEMM that follows, HBM-resident (all blocks'
+// weights together exceed L2) and read by every CTA of that GEMM's first round.  Each block of the issuing kernel
+// takes one piece.
+constexpr unsigned kPrefetchPiece = 64u << 10;
+T2W_DEV void prefetch_l2_piece(const void* p, unsigned bytes, int piece) {
+  const unsigned off = (unsigned)piece * kPrefetchPiece;
+  if (p && off < bytes) {
+    const unsigned n = bytes - off < kPrefetchPiece ? bytes - off : kPrefetchPiece;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(p) + off), "r"(n & ~15u)
+                 : "memory");
+  }
+}
+
 // ---------------------------------------------------------------- small math
 T2W_DEV float warp_sum(float v) {
 #pragma unroll

@@ -63,6 +63,8 @@ struct DevArgs {
   int* err;
   int* done_flags;  // per 128-row block: +1 from each epilogue warp once its stores of a tile are complete
   const float* gate;  // T2W_EPI_RESID: per-column gate of the residual update
+  const void* pf;     // L2 prefetch of the next GEMM's weights (see GemmArgs)
+  unsigned pf_bytes;
 };
 
 T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -221,6 +223,7 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
+        if (tile + (int)gridDim.x >= p.num_tiles) prefetch_l2_piece(p.pf, p.pf_bytes, blockIdx.x);  // last tile
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
@@ -617,6 +620,8 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.err = a.err;
   p.done_flags = TMA_OUT ? a.done_flags : nullptr;
   p.gate = a.gate;
+  p.pf = a.pf;
+  p.pf_bytes = a.pf_bytes;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   cudaError_t e = launch_k(k_gemm<BN, EPI, TMA_OUT>, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tmA, *tmW, *tmC, p);
   if (e != cudaSuccess) {
@@ -694,6 +699,8 @@ int launch_pair_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA,
   p.err = a.err;
   p.done_flags = a.done_flags;
   p.gate = a.gate;
+  p.pf = nullptr;  // (the pair kernel issues no prefetch)
+  p.pf_bytes = 0;
   const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);

@@ -56,6 +56,9 @@ struct GemmArgs {
   // Completion counters, one per 128-row block: each epilogue warp adds 1 once its stores of a tile are complete
   // (8 per tile; a block is done at 8 * N / BN).  Lets the row kernel that follows start early (RowWait).
   int* done_flags = nullptr;
+  // L2 prefetch of the next GEMM's weights, issued by each CTA as its producer starts its last tile (64 KB per CTA)
+  const void* pf = nullptr;
+  unsigned pf_bytes = 0;
   const float* gate = nullptr;  // T2W_EPI_RESID: out (fp32) += gate[n] * (acc + bias[n]), N floats
 };
 // Column tile the launcher picks for an N-wide output of M rows with epilogue `epi` (0: N unsupported).
@@ -127,6 +130,8 @@ struct AttnArgs {
   const int* kv_idx = nullptr;
   int pool_ld = 0;
   int* err = nullptr;
+  const void* pf = nullptr;  // L2 prefetch of the next GEMM's weights (64 KB per CTA of the first CTAs)
+  unsigned pf_bytes = 0;
 };
 // Tensor maps of the attention kernel over a qkv buffer: 128-row query boxes and 64-row key / value boxes.
 bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int rows, int heads);
@@ -171,6 +176,11 @@ struct RowWait {
   const int* flags = nullptr;
   int target = 0;
   int* err = nullptr;
+  // L2 prefetch of the next GEMM's weights, issued as the kernel starts (64 KB per block of the first blocks)
+  const void* pf = nullptr;
+  unsigned pf_bytes = 0;
+  const void* pf2 = nullptr;
+  unsigned pf2_bytes = 0;
 };
 // h += g * y (fp32, in place; skipped when y == nullptr), then out = LN(h) * scale1 + shift, pad rows zero.
 int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,

@@ -506,22 +506,33 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       const float *sh_a = M, *sc_a = M + H, *g_a = M + 2 * H, *sh_m = M + 3 * H, *sc_m = M + 4 * H, *g_m = M + 5 * H;
       const float *sh_c = M + 6 * H, *sc_c = M + 7 * H, *g_c = M + 8 * H;
       int* dn = done_all + ((size_t)step * c.depth + bi) * 4 * mblocks;  // proj, conv1, conv2, fc2
-      auto waits = [&](int* f) {
+      // each norm kernel prefetches the weights of the GEMM after it into L2 (HBM-resident: all blocks' weights exceed
+      // L2); attention prefetches proj's, and fc1 fc2's as its CTAs start their last tile
+      auto waits = [&](int* f, const void* pf = nullptr, size_t pf_bytes = 0, const void* pf2 = nullptr,
+                       size_t pf2_bytes = 0) {
         RowWait r;
         r.flags = f;
         r.target = done_target;
         r.err = s->err;
+        r.pf = pf;
+        r.pf_bytes = (unsigned)pf_bytes;
+        r.pf2 = pf2;
+        r.pf2_bytes = (unsigned)pf2_bytes;
         return r;
       };
+      const size_t wb_hh = (size_t)H * H * 2, wb_conv = 3 * wb_hh, wb_qkv = 3 * wb_hh, wb_mlp = (size_t)F * H * 2;
       if (fp8) {
         // attention branch
         T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-        T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, out_a, nullptr, st));
+        T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, out_a, nullptr, st,
+                                  waits(nullptr, w.w8[W8_QKV], (size_t)3 * H * H)));
         Gemm8Args q = g8(w, W8_QKV, a8, sfa, 3, 3 * H, H, 1, T2W_EPI_QKV, qkv, 3 * H, w.b_qkv);
         q.qn_w = w.qn_w; q.qn_b = w.qn_b; q.kn_w = w.kn_w; q.kn_b = w.kn_b; q.qk_eps = c.eps_qk;
         T2W_TRY(P.tick(T2W_KC_GEMM_QKV, st));
         T2W_TRY(launch_gemm8(q, st, &t8_a, &w.t8[W8_QKV], &st_qkv));
         AttnArgs at8 = at_args;
+        at8.pf = w.w8[W8_PROJ];
+        at8.pf_bytes = (unsigned)((size_t)H * H);
         at8.out = o8;
         at8.out_sf = sfo;
         T2W_TRY(P.tick(T2W_KC_ATTN, st));
@@ -531,18 +542,21 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
                              &w.t8[W8_PROJ], &st_y));
         // causal conv branch
         T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-        T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, out_a, pad, st));
+        T2W_TRY(launch_add_ln_mod(h, y, g_a, sh_c, sc_c, c.eps_block, R, H, out_a, pad, st,
+                                  waits(nullptr, w.w8[W8_C1], (size_t)3 * H * H)));
         T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
         T2W_TRY(launch_gemm8(g8(w, W8_C1, a8, sfa, 3, H, H, 3, T2W_EPI_BF16, o, H, w.b_c1), st, &t8_a, &w.t8[W8_C1],
                              &st_o));
         T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
-        T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, out_c1, pad, st));
+        T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, out_c1, pad, st,
+                               waits(nullptr, w.w8[W8_C2], (size_t)3 * H * H)));
         T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
         T2W_TRY(launch_gemm8(g8(w, W8_C2, c18, sfc1, 3, H, H, 3, T2W_EPI_BF16, y, H, w.b_c2), st, &t8_c1,
                              &w.t8[W8_C2], &st_y));
         // MLP branch: fc1's epilogue quantises GELU's output for fc2
         T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-        T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, out_a, nullptr, st));
+        T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, out_a, nullptr, st,
+                                  waits(nullptr, w.w8[W8_FC1], (size_t)F * H)));
         Gemm8Args f1 = g8(w, W8_FC1, a8, sfa, 3, F, H, 1, T2W_EPI_GELU_FP8, f8, F, w.b_fc1);
         f1.out_sf = sff;
         T2W_TRY(P.tick(T2W_KC_GEMM_FC1, st));
@@ -559,7 +573,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       // attention branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, row_out_bf16(a), nullptr, st,
-                                waits(pend_done)));
+                                waits(pend_done, w.qkv, wb_qkv)));
       GemmArgs q = GemmArgs();
       q.rows_a = R; q.M = R; q.err = s->err;
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
@@ -568,6 +582,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_gemm(q, st, &tm_a, &w.tm_qkv, &st_qkv));
       const int sb = step * c.depth + bi;
       AttnArgs at_use = at_args;
+      at_use.pf = w.proj;
+      at_use.pf_bytes = (unsigned)wb_hh;
       if (pl.slots) {  // the window's new keys into their slots; attention gathers every row's key list
         __nv_bfloat16* kvp = sp->kv + sb * sp->kv_sb();
         T2W_TRY(launch_kv_scatter(qkv, H, tok_qrow_d, tok_slot_d, n_new, kvp, st));
@@ -586,7 +602,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_h));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, nullptr, nullptr, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st, waits(dn)));
+      T2W_TRY(launch_add_ln_mod(h, nullptr, nullptr, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st,
+                                waits(dn, w.c1, wb_conv)));
       if (pl.slots)  // cached conv-input frames in front of each window, and the window's last two saved
         T2W_TRY(launch_conv_cache(a, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb(), sp->cnn_slot(), st));
       GemmArgs k1 = GemmArgs();
@@ -597,7 +614,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV1, st));
       T2W_TRY(launch_gemm(k1, st, &tm_a, &w.tm_c1, &st_o));
       T2W_TRY(P.tick(T2W_KC_LN_MISH, st));
-      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, row_out_bf16(c1), pad, st, waits(dn + mblocks)));
+      T2W_TRY(launch_ln_mish(o, w.cln_w, w.cln_b, c.eps_conv, R, H, row_out_bf16(c1), pad, st,
+                             waits(dn + mblocks, w.c2, wb_conv)));
       if (pl.slots)
         T2W_TRY(launch_conv_cache(c1, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb() + 2 * H, sp->cnn_slot(), st));
       GemmArgs k2 = GemmArgs();
@@ -610,10 +628,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       // MLP branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, y, g_c, sh_m, sc_m, c.eps_block, R, H, row_out_bf16(a), nullptr, st,
-                                waits(dn + 2 * mblocks)));
+                                waits(dn + 2 * mblocks, w.fc1, wb_mlp)));
       GemmArgs f1 = GemmArgs();
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
+      f1.pf = w.fc2;
+      f1.pf_bytes = (unsigned)wb_mlp;
       T2W_TRY(P.tick(T2W_KC_GEMM_FC1, st));
       T2W_TRY(launch_gemm(f1, st, &tm_a, &w.tm_fc1, &st_f));
       GemmArgs f2 = GemmArgs();

@@ -92,7 +92,8 @@ def timeline_from_events(evs: list) -> dict:
         mp = re.search(r"k_gemm(?:_pair|8)<(\d+)>", n)  # the CTA-pair and FP8 GEMMs: k_gemm_pair<EPI>, k_gemm8<EPI>
         if m or mp:
             bn, epi = (int(m.group(1)), int(m.group(2))) if m else (256, int(mp.group(1)))
-            prev = names[-1].split(" after ")[0] if names else ""
+            # the kernel before it, skipping the slot-pool solve's cache-scatter kernels
+            prev = next((x.split(" after ")[0] for x in reversed(names) if x not in ("conv_cache", "kv_scatter")), "")
             nm = ("final" if bn == 80 else "in_proj" if epi == 0 else "fc1" if epi == 2 else "qkv" if epi == 4
                   else {"attn": "proj", "ln_mish": "conv2", "fc1": "fc2"}.get(prev, "conv1"))
         elif "k_add_ln_mod" in n or "k_ln_mish" in n:
@@ -280,6 +281,7 @@ def steady_arm(a, rank: int, world: int) -> None:
         l1.synchronize()
         lat.append(l0.elapsed_time(l1))
     solver.check()
+    tl = timeline(lambda: step(0)) if a.timeline and rank == 0 else None
     frames = n * T
     red = torch.tensor([sum(times)], dtype=torch.float64)
     if world > 1:
@@ -301,7 +303,7 @@ def steady_arm(a, rank: int, world: int) -> None:
                        "solve_calls": dict(fd.counts)},
             "latency_ms": {"p50": statistics.median(lat)}, "tflops": flop / (statistics.mean(times) / 1000) / 1e12,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": n * T * cfg.mel * 4,
-                    "d2h_bytes_per_step": n * T * cfg.mel * 4}}), flush=True)
+                    "d2h_bytes_per_step": n * T * cfg.mel * 4}, **({"timeline": tl} if tl else {})}), flush=True)
     fd.close()
     solver.close()
 

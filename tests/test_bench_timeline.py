@@ -47,3 +47,19 @@ def test_timeline_names_and_exposed_span():
     fp8 = "void t2w::(anonymous namespace)::k_gemm8<2>(...)"
     t = b.timeline_from_events([(attn, 0, 10), (pair, 5, 20), (fp8, 19, 30)])
     assert set(t["kernel_ms"]) == {"attn", "proj", "fc1"}
+
+
+def test_timeline_slot_solve_scatter_kernels():
+    """The slot-pool solve puts k_kv_scatter after QKV and k_conv_cache after the norms before each conv: the GEMMs
+    after them keep their block positions (conv2 after ln_mish, not conv1)."""
+    b = load_bench()
+    row = "void t2w::(anonymous namespace)::k_add_ln_mod<4, false>(float*, ...)"
+    mish = "void t2w::(anonymous namespace)::k_ln_mish<4, false>(...)"
+    attn = "void t2w::(anonymous namespace)::k_attn<false, true>(...)"
+    scat = "void t2w::(anonymous namespace)::k_kv_scatter(...)"
+    cc = "void t2w::(anonymous namespace)::k_conv_cache(...)"
+    seq = [(g(256, 4), 0, 10), (scat, 10, 11), (attn, 11, 20), (g(256, 3), 20, 30), (row, 29, 32), (cc, 32, 33),
+           (g(256, 1), 33, 40), (mish, 39, 42), (cc, 42, 43), (g(256, 1), 43, 50)]
+    t = b.timeline_from_events(seq)
+    assert set(t["kernel_ms"]) == {"qkv", "kv_scatter", "attn", "proj", "add_ln_mod after proj", "conv_cache",
+                                   "conv1", "ln_mish after conv1", "conv2"}

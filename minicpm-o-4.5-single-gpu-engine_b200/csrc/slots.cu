@@ -16,6 +16,25 @@ namespace {
 
 constexpr int kWarps = 8;
 
+// A warp copies n16 16-byte chunks: all of a lane's loads are issued before its stores (up to 8 per lane in flight;
+// a plain loop keeps one load-store round trip per chunk).
+T2W_DEV void warp_copy16(uint4* __restrict__ dst, const uint4* __restrict__ src, int n16, int lane) {
+  constexpr int kMax = 8;
+  for (int c0 = 0; c0 < n16; c0 += 32 * kMax) {
+    uint4 v[kMax];
+#pragma unroll
+    for (int j = 0; j < kMax; ++j) {
+      const int c = c0 + 32 * j + lane;
+      if (c < n16) v[j] = src[c];
+    }
+#pragma unroll
+    for (int j = 0; j < kMax; ++j) {
+      const int c = c0 + 32 * j + lane;
+      if (c < n16) dst[c] = v[j];
+    }
+  }
+}
+
 // One warp per new token: its K and V (2 H bf16 of the QKV output row) into its pool slot.
 __global__ void __launch_bounds__(256) k_kv_scatter(const __nv_bfloat16* __restrict__ qkv, int ld_qkv, int H,
                                                     const int* __restrict__ tok_qrow, const int* __restrict__ tok_slot,
@@ -26,7 +45,7 @@ __global__ void __launch_bounds__(256) k_kv_scatter(const __nv_bfloat16* __restr
   if (i >= n) return;
   const uint4* src = reinterpret_cast<const uint4*>(qkv + (size_t)tok_qrow[i] * ld_qkv + H);
   uint4* dst = reinterpret_cast<uint4*>(pool + (size_t)tok_slot[i] * pool_ld);
-  for (int c = lane; c < 2 * H / 8; c += 32) dst[c] = src[c];
+  warp_copy16(dst, src, 2 * H / 8, lane);
 }
 
 // One warp per CFG row: cached frames -> the two rows before its window in `buf`; then the last two rows of
@@ -42,10 +61,10 @@ __global__ void __launch_bounds__(256) k_conv_cache(__nv_bfloat16* __restrict__ 
   const uint4* rd = reinterpret_cast<const uint4*>(cpool + (size_t)r.rd * slot_ld);
   uint4* wr = reinterpret_cast<uint4*>(cpool + (size_t)r.wr * slot_ld);
   uint4* b0 = reinterpret_cast<uint4*>(buf + (size_t)(r.seg_row - 2) * H);
-  for (int c = lane; c < 2 * n16; c += 32) b0[c] = rd[c];  // frames 0, 1 -> rows seg_row - 2, seg_row - 1
+  warp_copy16(b0, rd, 2 * n16, lane);  // frames 0, 1 -> rows seg_row - 2, seg_row - 1
   __syncwarp();
   const uint4* last = reinterpret_cast<const uint4*>(buf + (size_t)(r.seg_row - 2 + r.T) * H);
-  for (int c = lane; c < 2 * n16; c += 32) wr[c] = last[c];
+  warp_copy16(wr, last, 2 * n16, lane);
 }
 
 // K / V of every (step, block): slot src[i] -> slot dst[i].  One warp per (sb, pair).

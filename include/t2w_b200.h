@@ -110,7 +110,9 @@ T2W_API int t2w_last_cuda_error(void); /* the cudaError_t of the last T2W_ERR_CU
  * step's adaLN modulations (t_embedder + adaLN_modulation of each block and the final layer) with the time-embedding
  * kernel.  t_sched: host [2 * steps] fp32 (t, dt) per Euler step as the reference's solver loop produces them
  * (token2wav_batch.py:669-693), or NULL for the cosine schedule evaluated in double.  `stream` orders the set-up work;
- * the call synchronises it before returning. */
+ * the call synchronises it before returning.  Every later call that takes the solver (or a slot pool made from it)
+ * runs on this device whatever device is current, and leaves the caller's current device as it found it; the
+ * pointers and stream passed to those calls must belong to this device. */
 T2W_API int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* weights, int32_t n_weights,
                int32_t precision, void* stream, t2w_solver** out);
 T2W_API int t2w_destroy(t2w_solver* s);
@@ -144,7 +146,7 @@ typedef struct t2w_slot_batch {
   float* out;               /* device [sum T, mel]: each window's mel, token-major */
 } t2w_slot_batch;
 
-/* Pools for n_slots key slots and n_rowslots conv-cache row slots on the current device (zeroed):
+/* Pools for n_slots key slots and n_rowslots conv-cache row slots on the solver's device (zeroed):
  * steps * depth * (n_slots * 4 * hidden + n_rowslots * 8 * hidden) bytes. */
 T2W_API int t2w_slots_create(const t2w_solver* s, int32_t n_slots, int32_t n_rowslots, t2w_slots** out);
 T2W_API int t2w_slots_destroy(t2w_slots* p);

@@ -480,14 +480,13 @@ namespace {
 
 template <bool E4M3, bool GATHER>
 int launch_attn_impl(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn<E4M3, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  static std::atomic<uint64_t> attr_done{0};
+  {
+    const cudaError_t e = smem_attr_once(k_attn<E4M3, GATHER>, kSmem, attr_done);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
     }
-    attr_done = true;
   }
   CUtensorMap mq, mkv;
   if (!tm_q || !tm_kv) {

@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/t2w_b200.h"
 
 #define T2W_DEV __device__ __forceinline__
@@ -236,6 +238,21 @@ T2W_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // pdl_launch() then lets the successor start launching.
 T2W_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 T2W_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------- launch attributes
+// A kernel's MaxDynamicSharedMemorySize attribute belongs to the device it was set on: a process that drives several
+// GPUs must set it on each.  `done` keeps one bit per device ordinal (devices from 64 on set it at every launch).
+template <class K>
+inline cudaError_t smem_attr_once(K* kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // ---------------------------------------------------------------- L2 prefetch
 // Bring piece `piece` (64 KB) of [p, p + bytes) into L2: the weights of a GEMM that follows, HBM-resident (all blocks'

@@ -571,14 +571,13 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
     if (!tmW) return T2W_ERR_INVALID;
   }
   using C = GemmCfg<BN, EPI, TMA_OUT>;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm<BN, EPI, TMA_OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  static std::atomic<uint64_t> attr_done{0};
+  {
+    const cudaError_t e = smem_attr_once(k_gemm<BN, EPI, TMA_OUT>, C::SMEM, attr_done);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
     }
-    attr_done = true;
   }
   CUtensorMap ma, mw, mc;
   if (!tmA) {
@@ -636,13 +635,17 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
 template <int EPI>
 int launch_pair_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, const WeightMaps* wm,
                      const CUtensorMap* tmC) {
-  static int max_pairs = -1;
-  if (max_pairs < 0) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_pair<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+  static std::atomic<uint64_t> attr_done{0};
+  {
+    const cudaError_t e = smem_attr_once(k_gemm_pair<EPI>, kPairSmem, attr_done);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
     }
+  }
+  static int max_pairs = -1;  // clusters resident at once (the same on every B200)
+  if (max_pairs < 0) {
+    cudaError_t e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2);
     cfg.blockDim = dim3(320);

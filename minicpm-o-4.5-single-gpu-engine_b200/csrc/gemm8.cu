@@ -287,14 +287,13 @@ __global__ void __launch_bounds__(320, 1)
 template <int EPI>
 int launch8_impl(const Gemm8Args& a, cudaStream_t st, const CUtensorMap* tmA, const CUtensorMap* tmW,
                  const CUtensorMap* tmC) {
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm8<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  static std::atomic<uint64_t> attr_done{0};
+  {
+    const cudaError_t e = smem_attr_once(k_gemm8<EPI>, kSmem, attr_done);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
     }
-    attr_done = true;
   }
   CUtensorMap ma, mw, mc;
   if (!tmA) {

@@ -691,6 +691,31 @@ int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
 // Launch the solve graph cached under `key` on `st`, capturing `enqueue` into it first if there is none.  The capture
 // runs on the solver's own stream (the caller's may be the legacy default stream, which cannot be captured); capturing
 // executes nothing.  At most kMaxGraphs graphs are kept: past that, the stream is synchronised and one is dropped.
+// The solver's (or slot pool's) device is made current for the duration of a call and the caller's restored after it:
+// its memory, streams and graphs belong to that device, and a caller that drives several GPUs from one thread may have
+// another one current.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) {
+      ok = false;
+      return;
+    }
+    if (cur != dev) {
+      ok = cudaSetDevice(dev) == cudaSuccess;
+      prev = cur;
+    }
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+#define T2W_ON_DEVICE(dev)              \
+  DeviceGuard t2w_device_guard_(dev);   \
+  if (!t2w_device_guard_.ok) return T2W_ERR_CUDA
+
 constexpr size_t kMaxGraphs = 64;
 template <class F>
 int replay(t2w_solver* s, uint64_t key, cudaStream_t st, F&& enqueue) {
@@ -983,6 +1008,7 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
 
 int t2w_destroy(t2w_solver* s) {
   if (!s) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
   if (s->cap_stream) cudaStreamDestroy(s->cap_stream);
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
@@ -1000,6 +1026,7 @@ size_t t2w_workspace_bytes(const t2w_solver* s, int32_t n, const int32_t* P, con
 
 int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_bytes, uint32_t flags, void* stream) {
   if (!s || !b || !ws || !b->x0 || !b->mu || !b->cond || !b->spk || !b->out) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   Plan pl;
   if (!make_plan(s->cfg, b->n_streams, b->prompt_len, b->chunk_len, pl)) return T2W_ERR_INVALID;
   if (layout(s->cfg, pl, s->precision == T2W_PREC_FP8).total > ws_bytes) return T2W_ERR_WORKSPACE;
@@ -1023,6 +1050,7 @@ int t2w_solve_packed(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_byte
 int t2w_profile_solve(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_bytes, void* stream, float* ms,
                       int32_t* launches) {
   if (!s || !b || !ws || !ms || !launches || !b->x0 || !b->mu || !b->cond || !b->spk || !b->out) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   Plan pl;
   if (!make_plan(s->cfg, b->n_streams, b->prompt_len, b->chunk_len, pl)) return T2W_ERR_INVALID;
   if (layout(s->cfg, pl, s->precision == T2W_PREC_FP8).total > ws_bytes || (reinterpret_cast<uintptr_t>(ws) & 255))
@@ -1053,6 +1081,7 @@ int t2w_profile_solve(t2w_solver* s, const t2w_batch* b, void* ws, size_t ws_byt
 
 int t2w_check(t2w_solver* s) {
   if (!s) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   int v = 0;
   T2W_CUDA(cudaMemcpy(&v, s->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (v) {
@@ -1064,6 +1093,7 @@ int t2w_check(t2w_solver* s) {
 
 int t2w_mods(const t2w_solver* s, float* mods, float* final_mods, float* dts, void* stream) {
   if (!s) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   const t2w_config& c = s->cfg;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (mods) T2W_CUDA(cudaMemcpyAsync(mods, s->mods, (size_t)c.steps * c.depth * 9 * c.hidden * 4, cudaMemcpyDeviceToDevice, st));
@@ -1083,8 +1113,9 @@ int t2w_counts(const t2w_solver* s, int64_t* replays, int64_t* captures, int64_t
 
 int t2w_slots_create(const t2w_solver* s, int32_t n_slots, int32_t n_rowslots, t2w_slots** out) {
   if (!s || !out || n_slots <= 0 || n_rowslots <= 0) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   t2w_slots* p = new t2w_slots();
-  T2W_CUDA(cudaGetDevice(&p->device));
+  p->device = s->device;
   p->n_slots = n_slots;
   p->n_rowslots = n_rowslots;
   p->n_sb = s->cfg.steps * s->cfg.depth;
@@ -1112,6 +1143,7 @@ int t2w_slots_create(const t2w_solver* s, int32_t n_slots, int32_t n_rowslots, t
 
 int t2w_slots_destroy(t2w_slots* p) {
   if (!p) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(p->device);
   cudaFree(p->kv);
   cudaFree(p->cnn);
   delete p;
@@ -1121,6 +1153,7 @@ int t2w_slots_destroy(t2w_slots* p) {
 int t2w_slots_copy(t2w_slots* p, const int32_t* src, const int32_t* dst, int32_t n, void* stream) {
   if (!p || n < 0 || (n > 0 && (!src || !dst))) return T2W_ERR_INVALID;
   if (n == 0) return T2W_OK;
+  T2W_ON_DEVICE(p->device);
   for (int i = 0; i < n; ++i)
     if (src[i] < 0 || src[i] >= p->n_slots || dst[i] < 0 || dst[i] >= p->n_slots) return T2W_ERR_INVALID;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1135,6 +1168,7 @@ int t2w_slots_copy(t2w_slots* p, const int32_t* src, const int32_t* dst, int32_t
 
 int t2w_slots_copy_row(t2w_slots* p, int32_t src, int32_t dst, void* stream) {
   if (!p || src >= p->n_rowslots || dst < 0 || dst >= p->n_rowslots) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(p->device);
   return launch_rowslot_copy(p->cnn, p->cnn_slot(), p->cnn_sb(), p->n_sb, src < 0 ? -1 : src, dst,
                              static_cast<cudaStream_t>(stream));
 }
@@ -1164,6 +1198,8 @@ int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* 
                     void* stream) {
   if (!s || !p || !b || !ws || !b->x0 || !b->mu || !b->spk || !b->out) return T2W_ERR_INVALID;
   if (s->precision != T2W_PREC_BF16) return T2W_ERR_UNSUPPORTED;
+  if (p->device != s->device) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
   Plan pl;
   if (!make_plan_slots(s->cfg, b->n_streams, b->chunk_len, b->kv_len, b->kv_idx, b->cnn_rd, b->cnn_wr, p->n_slots,
                        p->n_rowslots, pl))

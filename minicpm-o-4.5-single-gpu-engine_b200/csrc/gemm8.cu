@@ -54,6 +54,8 @@ struct DevArgs {
   const float* kn_b;
   float qk_eps;
   int* err;
+  const void* pf;  // L2 prefetch of the next GEMM's weights (see Gemm8Args)
+  unsigned pf_bytes;
 };
 
 T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * kBN;
+        if (tile + (int)gridDim.x >= p.num_tiles) prefetch_l2_piece(p.pf, p.pf_bytes, blockIdx.x);  // last tile
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
           mbar_expect_tx(&full[stage], kABytes + kBBytes + kSfABytes + kSfBBytes);
@@ -334,6 +337,8 @@ int launch8_impl(const Gemm8Args& a, cudaStream_t st, const CUtensorMap* tmA, co
   p.kn_b = a.kn_b;
   p.qk_eps = a.qk_eps;
   p.err = a.err;
+  p.pf = a.pf;
+  p.pf_bytes = a.pf_bytes;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   cudaError_t e = launch_k(k_gemm8<EPI>, dim3(grid), dim3(320), kSmem, st, *tmA, *tmW, *tmC, p);
   if (e != cudaSuccess) {

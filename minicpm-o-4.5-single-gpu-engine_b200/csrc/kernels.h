@@ -100,6 +100,9 @@ struct Gemm8Args {
   const float* kn_b = nullptr;
   float qk_eps = 0.f;
   int* err = nullptr;
+  // L2 prefetch of the next GEMM's weights, issued by each CTA as its producer starts its last tile (64 KB per CTA)
+  const void* pf = nullptr;
+  unsigned pf_bytes = 0;
 };
 // Bytes of one layout of scale atoms for a [rows, cols] e4m3 matrix.
 size_t gemm8_sf_bytes(int rows, int cols);

@@ -559,6 +559,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
                                   waits(nullptr, w.w8[W8_FC1], (size_t)F * H)));
         Gemm8Args f1 = g8(w, W8_FC1, a8, sfa, 3, F, H, 1, T2W_EPI_GELU_FP8, f8, F, w.b_fc1);
         f1.out_sf = sff;
+        f1.pf = w.w8[W8_FC2];  // fc2's e4m3 weights, as fc1's CTAs start their last tile
+        f1.pf_bytes = (unsigned)((size_t)F * H);
         T2W_TRY(P.tick(T2W_KC_GEMM_FC1, st));
         T2W_TRY(launch_gemm8(f1, st, &t8_a, &w.t8[W8_FC1], &st8_f));
         Gemm8Args f2 = g8(w, W8_FC2, f8, sff, 1, H, F, 1, T2W_EPI_BF16, y, H, w.b_fc2);

@@ -212,7 +212,16 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         const __nv_bfloat16* kcol = p.pool + e.h * kD;
         const __nv_bfloat16* vcol = p.pool + H + e.h * kD;
+        // the slot indices of the next tile's keys are loaded while this tile's copies are issued, so the index
+        // load's latency is off the producer's path after an item's first tile
+        auto slot_of = [&](int key) { return key < e.w.L ? __ldg(p.kv_idx + e.w.k_row + key) : 0; };
+        int nxt[2] = {slot_of(lane), slot_of(lane + 32)};
         for (int j = 0; j < e.n_kt; ++j, ++t) {
+          const int cur[2] = {nxt[0], nxt[1]};
+          if (j + 1 < e.n_kt) {
+            nxt[0] = slot_of((j + 1) * kKTile + lane);
+            nxt[1] = slot_of((j + 1) * kKTile + lane + 32);
+          }
           const int st = t % kStages;
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err)))) break;
           const uint32_t ks = smem_u32(base + kQBytes + st * 2 * kKVBytes), vs = ks + kKVBytes;
@@ -221,7 +230,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
             const int r = lane + 32 * half;
             const int key = j * kKTile + r;
             const bool valid = key < e.w.L;
-            const size_t slot = valid ? (size_t)__ldg(p.kv_idx + e.w.k_row + key) : 0;
+            const size_t slot = (size_t)cur[half];
             const __nv_bfloat16* ksrc = kcol + slot * p.pool_ld;
             const __nv_bfloat16* vsrc = vcol + slot * p.pool_ld;
             const uint32_t nb = valid ? 16u : 0u;

@@ -200,9 +200,18 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       // row's list are zero-filled
       int t = 0;
       bool ok = true;
+      // The slot indices of the next tile's keys (the next item's first tile after an item's last) are loaded while
+      // this tile's copies are issued, so the index load's latency is off the producer's path.
+      auto slot_of = [&](const AttnWork& w, int key) { return key < w.L ? __ldg(p.kv_idx + w.k_row + key) : 0; };
+      int nxt[2] = {0, 0};
+      if (q + 2 * (int)blockIdx.x < p.n_items) {
+        nxt[0] = slot_of(items[q].w, lane);
+        nxt[1] = slot_of(items[q].w, lane + 32);
+      }
       for (int k = 0; ok; ++k) {
         if (q + 2 * (int)blockIdx.x + k * stride >= p.n_items) break;
         const ItemEntry e = items[2 * k + q];
+        const bool has_next_item = q + 2 * (int)blockIdx.x + (k + 1) * stride < p.n_items;
         if (lane == 0) {
           if ((ok = mbar_wait(&b.q_free, (k & 1) ^ 1u, p.err))) {
             mbar_expect_tx(&b.q_full, kQBytes);
@@ -212,15 +221,15 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         const __nv_bfloat16* kcol = p.pool + e.h * kD;
         const __nv_bfloat16* vcol = p.pool + H + e.h * kD;
-        // the slot indices of the next tile's keys are loaded while this tile's copies are issued, so the index
-        // load's latency is off the producer's path after an item's first tile
-        auto slot_of = [&](int key) { return key < e.w.L ? __ldg(p.kv_idx + e.w.k_row + key) : 0; };
-        int nxt[2] = {slot_of(lane), slot_of(lane + 32)};
         for (int j = 0; j < e.n_kt; ++j, ++t) {
           const int cur[2] = {nxt[0], nxt[1]};
           if (j + 1 < e.n_kt) {
-            nxt[0] = slot_of((j + 1) * kKTile + lane);
-            nxt[1] = slot_of((j + 1) * kKTile + lane + 32);
+            nxt[0] = slot_of(e.w, (j + 1) * kKTile + lane);
+            nxt[1] = slot_of(e.w, (j + 1) * kKTile + lane + 32);
+          } else if (has_next_item) {
+            const AttnWork& wn = items[2 * (k + 1) + q].w;
+            nxt[0] = slot_of(wn, lane);
+            nxt[1] = slot_of(wn, lane + 32);
           }
           const int st = t % kStages;
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err)))) break;

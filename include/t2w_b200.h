@@ -240,7 +240,8 @@ T2W_API int t2w_gemm(const void* A_bf16, int32_t lda, int32_t rows_a, const void
 /* Varlen attention over packed sequences with the block-causal chunk mask: sequence s has its keys at rows
  * seq_row[s] .. seq_row[s] + seq_len[s] - 1 of qkv (bf16 [rows, 3 * heads * 64], q | k | v column blocks); a query at
  * position i attends keys j < (i < prompt_len[s] ? prompt_len[s] : seq_len[s]).  out bf16 [rows, heads * 64].
- * seq_row / seq_len / prompt_len are host arrays. */
+ * seq_row / seq_len / prompt_len are host arrays.  The per-call work list is uploaded from host memory that lives only
+ * for the call, so a stream under capture is refused (T2W_ERR_INVALID, nothing enqueued). */
 T2W_API int t2w_attn_varlen(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq, const int32_t* seq_row,
                     const int32_t* seq_len, const int32_t* prompt_len, void* out_bf16, void* stream);
 
@@ -249,8 +250,10 @@ T2W_API int t2w_attn_varlen(const void* qkv_bf16, int32_t rows, int32_t heads, i
  * reference.  Same arguments, same results; the per-call work list (one entry per 128-query tile) lives in a fixed
  * device array of this library instead of a per-call allocation: at most 8192 tiles per call (160 KB, held on every GPU
  * that loads the library until exit); more returns T2W_ERR_INVALID.  The first call on a device looks up that array's
- * device address, so make it before any stream capture.  All calls share the array: calls whose GPU work overlaps (two
- * streams, two threads) race on it and must be serialised by the caller. */
+ * device address.  Like t2w_attn_varlen, it uploads the work list from host memory that lives only for the call, so no
+ * call may be made on a stream under capture: such a call returns T2W_ERR_INVALID and enqueues nothing.  All calls
+ * share the array: calls whose GPU work overlaps (two streams, two threads) race on it and must be serialised by the
+ * caller. */
 T2W_API int t2w_attn_varlen_noalloc(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_seq,
                                     const int32_t* seq_row, const int32_t* seq_len, const int32_t* prompt_len,
                                     void* out_bf16, void* stream);

@@ -572,14 +572,24 @@ extern "C" int t2w_attn_varlen_noalloc(const void* qkv, int32_t rows, int32_t he
   std::vector<AttnWork> work;
   for (int s = 0; s < n_seq; ++s) {
     if (seq_len[s] <= 0 || prompt_len[s] < 0 || prompt_len[s] > seq_len[s] || seq_row[s] < 0 ||
-        seq_row[s] + seq_len[s] > rows)
+        (int64_t)seq_row[s] + seq_len[s] > rows)
       return T2W_ERR_INVALID;
     for (int q = 0; q < seq_len[s]; q += 128) work.push_back(AttnWork{seq_row[s] + q, seq_row[s], q, prompt_len[s], seq_len[s]});
   }
   if (work.size() > (size_t)kNoAllocMaxWork) return T2W_ERR_INVALID;  // beyond the fixed scratch array
   if (work.empty()) return T2W_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The work list is copied from a host vector that dies when this call returns: a capture would record a copy from
+  // freed host memory, so a capturing stream is refused (nothing is enqueued and the capture stays valid).
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cs);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
     if (e != cudaSuccess) set_cuda_error(e);
     return e != cudaSuccess ? T2W_ERR_CUDA : T2W_ERR_UNSUPPORTED;
@@ -599,7 +609,6 @@ extern "C" int t2w_attn_varlen_noalloc(const void* qkv, int32_t rows, int32_t he
     }
     scratch = g_noalloc_ptr[dev];
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   e = cudaMemcpyAsync(scratch, work.data(), work.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) {
     set_cuda_error(e);

@@ -171,7 +171,13 @@ struct t2w_solver {
   WeightMaps tm_in{}, tm_fin{};
   int* err = nullptr;
   cudaStream_t cap_stream = nullptr;
-  std::unordered_map<uint64_t, cudaGraphExec_t> graphs;
+  // cached solve graphs: the executable and an event recorded after its latest launch (an evicted graph may still be
+  // running on another caller stream; its event is waited on before the executable is destroyed)
+  struct CachedGraph {
+    cudaGraphExec_t exec = nullptr;
+    cudaEvent_t done = nullptr;
+  };
+  std::unordered_map<uint64_t, CachedGraph> graphs;
   std::unordered_map<uint64_t, int> slot_seen;  // slot-solve graph keys seen so far (captured on the second call)
   std::unordered_map<uintptr_t, uint64_t> ws_meta;  // workspace -> plan key of the index arrays it holds
   std::vector<cudaEvent_t> prof_events;
@@ -692,7 +698,7 @@ int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
 
 // Launch the solve graph cached under `key` on `st`, capturing `enqueue` into it first if there is none.  The capture
 // runs on the solver's own stream (the caller's may be the legacy default stream, which cannot be captured); capturing
-// executes nothing.  At most kMaxGraphs graphs are kept: past that, the stream is synchronised and one is dropped.
+// executes nothing.  At most kMaxGraphs graphs are kept: past that, one is dropped once its latest launch has finished.
 // The solver's (or slot pool's) device is made current for the duration of a call and the caller's restored after it:
 // its memory, streams and graphs belong to that device, and a caller that drives several GPUs from one thread may have
 // another one current.
@@ -726,10 +732,11 @@ int replay(t2w_solver* s, uint64_t key, cudaStream_t st, F&& enqueue) {
     cudaStreamCaptureStatus cs;
     T2W_CUDA(cudaStreamIsCapturing(st, &cs));
     if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: use flags = 0
-    if (s->graphs.size() >= kMaxGraphs) {
-      T2W_CUDA(cudaStreamSynchronize(st));
+    if (s->graphs.size() >= kMaxGraphs) {  // drop one, once its latest launch (on whichever stream) has finished
       auto victim = s->graphs.begin();
-      cudaGraphExecDestroy(victim->second);
+      T2W_CUDA(cudaEventSynchronize(victim->second.done));
+      cudaGraphExecDestroy(victim->second.exec);
+      cudaEventDestroy(victim->second.done);
       s->graphs.erase(victim);
     }
     if (!s->cap_stream) T2W_CUDA(cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking));
@@ -745,17 +752,24 @@ int replay(t2w_solver* s, uint64_t key, cudaStream_t st, F&& enqueue) {
       set_cuda_error(ec);
       return T2W_ERR_CUDA;
     }
-    cudaGraphExec_t exec = nullptr;
-    const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+    t2w_solver::CachedGraph cg;
+    const cudaError_t ei = cudaGraphInstantiate(&cg.exec, graph, 0);
     cudaGraphDestroy(graph);
     if (ei != cudaSuccess) {
       set_cuda_error(ei);
       return T2W_ERR_CUDA;
     }
-    g = s->graphs.emplace(key, exec).first;
+    const cudaError_t ee = cudaEventCreateWithFlags(&cg.done, cudaEventDisableTiming);
+    if (ee != cudaSuccess) {
+      cudaGraphExecDestroy(cg.exec);
+      set_cuda_error(ee);
+      return T2W_ERR_CUDA;
+    }
+    g = s->graphs.emplace(key, cg).first;
     ++s->n_captures;
   }
-  T2W_CUDA(cudaGraphLaunch(g->second, st));
+  T2W_CUDA(cudaGraphLaunch(g->second.exec, st));
+  T2W_CUDA(cudaEventRecord(g->second.done, st));
   ++s->n_replays;
   return T2W_OK;
 }
@@ -767,13 +781,17 @@ int attn_varlen_alloc(const void* qkv, int rows, int heads, int n_seq, const int
   std::vector<AttnWork> work;
   for (int s = 0; s < n_seq; ++s) {
     if (seq_len[s] <= 0 || prompt_len[s] < 0 || prompt_len[s] > seq_len[s] || seq_row[s] < 0 ||
-        seq_row[s] + seq_len[s] > rows)
+        (int64_t)seq_row[s] + seq_len[s] > rows)
       return T2W_ERR_INVALID;
     for (int q = 0; q < seq_len[s]; q += 128)
       work.push_back(AttnWork{seq_row[s] + q, seq_row[s], q, prompt_len[s], seq_len[s]});
   }
   if (work.empty()) return T2W_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the work list is copied from a host vector that dies with this call: a capturing stream is refused
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  T2W_CUDA(cudaStreamIsCapturing(st, &cs));
+  if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;
   AttnWork* d = nullptr;
   T2W_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), work.size() * sizeof(AttnWork), st));
   T2W_CUDA(cudaMemcpyAsync(d, work.data(), work.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st));
@@ -1011,7 +1029,10 @@ int t2w_create(const t2w_config* cfg, const float* t_sched, const float* const* 
 int t2w_destroy(t2w_solver* s) {
   if (!s) return T2W_ERR_INVALID;
   T2W_ON_DEVICE(s->device);
-  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : s->graphs) {
+    cudaGraphExecDestroy(kv.second.exec);
+    cudaEventDestroy(kv.second.done);
+  }
   if (s->cap_stream) cudaStreamDestroy(s->cap_stream);
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
   cudaFree(s->arena);

@@ -54,3 +54,12 @@ def test_weight_names_exist_in_the_estimator_layout():
 def test_error_status_is_an_exception():
     e = L.T2WError("t2w_solve_packed", -6)
     assert "workspace" in str(e) and e.status == -6
+
+
+def test_varlen_attention_rejects_overflowing_rows_without_a_gpu():
+    """A sequence whose end (seq_row + seq_len) passes INT32_MAX is refused by the size check, which is computed in
+    64 bits and comes before any CUDA call (no device is touched; the pointers are never read)."""
+    for fn in ("t2w_attn_varlen", "t2w_attn_varlen_noalloc"):
+        rc = getattr(L.load(), fn)(ctypes.c_void_p(16), 1000, 1, 1, L.i32_array([2**31 - 10]), L.i32_array([100]),
+                                   L.i32_array([100]), ctypes.c_void_p(16), None)
+        assert rc == -1, (fn, rc)

@@ -12,7 +12,7 @@ import torch
 
 from b200t2w.config import REFERENCE, TINY
 from b200t2w.solver import B200Solver, Layout, state_dict_from_module
-from b200t2w.workload import C1, C2, C3, TARGET, Workload, make_streams
+from b200t2w.workload import C1, C2, C3, C4, TARGET, Workload, make_streams
 from oracle import dit_oracle
 
 pytestmark = pytest.mark.gpu
@@ -96,7 +96,11 @@ def test_c1_full_size_vs_golden(ref, golden_dir):
     assert e < TOL_BF16
 
 
-@pytest.mark.parametrize("wl,sample", [(C2, (0, 15)), (C3, (0, 37)), (TARGET, (0, 63))])
+# Config 3's sample covers its ragged extremes: stream 25 is the shortest packed row (P=100, T=41), stream 58 the
+# longest (P=492, T=91), stream 40 the shortest chunk (P=419, T=26), stream 9 the longest chunk (T=99), stream 24 a
+# middle row (P=314, T=69), plus streams 0 and 37.  Those rows exercise the block-causal mask's partial 64-key tiles
+# at both ends of the prompt / chunk boundary and the conv pads between short and long neighbours.
+@pytest.mark.parametrize("wl,sample", [(C2, (0, 15)), (C3, (0, 9, 24, 25, 37, 40, 58)), (TARGET, (0, 63))])
 def test_batch_streams_vs_oracle(ref, wl, sample):
     m, s = ref
     streams = make_streams(wl)
@@ -106,7 +110,8 @@ def test_batch_streams_vs_oracle(ref, wl, sample):
         st = streams[i]
         o = dit_oracle.solve_packed(m, st["x0"], st["mu"], st["cond"], st["spk"], st["P"], st["T"])
         e = rel(outs[i][:, st["P"]:], o[:, st["P"]:])
-        print(f"{wl.name} stream {i} (P={st['P']}, T={st['T']}): chunk rel-L2 {e:.3e}")
+        print(f"{wl.name} stream {i} (P={st['P']}, T={st['T']}): chunk rel-L2 {e:.3e} "
+              f"max-abs {maxabs(outs[i][:, st['P']:], o[:, st['P']:]):.3e}")
         assert e < TOL_BF16
 
 
@@ -155,3 +160,22 @@ def test_fp8_c1_full_size_vs_golden(ref, golden_dir):
     e = rel(out[:, st["P"]:], g["ref_chunk_mel"])
     print(f"C1 FP8 chunk mel rel-L2 {e:.3e} max-abs {maxabs(out[:, st['P']:], g['ref_chunk_mel']):.3e}")
     assert e < TOL_FP8
+
+
+def test_fp8_c4_full_shape_vs_oracle(ref):
+    """Config 4 at its real shape: 128 streams of (300 + 50) frames solved as one batch on the FP8 path (2 x 45,056
+    packed rows, so the large-M tile schedule of the e4m3 GEMMs runs), streams 0, 63 and 127 against the fp32 oracle
+    at the FP8 tolerance."""
+    m, _ = ref
+    s = B200Solver(REFERENCE, state_dict_from_module(m), precision="fp8")
+    streams = make_streams(C4)
+    assert len(streams) == 128
+    outs = s.solve_streams(streams)
+    s.check()
+    for i in (0, 63, 127):
+        st = streams[i]
+        o = dit_oracle.solve_packed(m, st["x0"], st["mu"], st["cond"], st["spk"], st["P"], st["T"])
+        e = rel(outs[i][:, st["P"]:], o[:, st["P"]:])
+        print(f"{C4.name} stream {i}: FP8 chunk rel-L2 {e:.3e} max-abs {maxabs(outs[i][:, st['P']:], o[:, st['P']:]):.3e}")
+        assert e < TOL_FP8
+    s.close()

@@ -62,3 +62,25 @@ def test_noalloc_rejects_more_tiles_than_its_array():
         L.call("t2w_attn_varlen_noalloc", _ptr(qkv), rows, heads, len(seqs), L.i32_array(r), L.i32_array(Ls),
                L.i32_array(Ps), _ptr(qkv), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert e.value.status == -1
+
+
+def test_noalloc_refuses_a_capturing_stream():
+    """The work list is copied from host memory that lives only for the call, so a stream under capture is refused
+    with T2W_ERR_INVALID; nothing is enqueued and the capture stays valid."""
+    rows, heads = 256, 2
+    qkv = torch.zeros(rows, 3 * heads * 64, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(rows, heads * 64, device="cuda", dtype=torch.bfloat16)
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(side):
+        graph.capture_begin()
+        try:
+            rc = L.load().t2w_attn_varlen_noalloc(_ptr(qkv), rows, heads, 1, L.i32_array([0]), L.i32_array([200]),
+                                                  L.i32_array([150]), _ptr(out), ctypes.c_void_p(side.cuda_stream))
+            out.add_(0)  # the capture is still usable after the refusal
+        finally:
+            graph.capture_end()
+    assert rc == -1
+    graph.replay()
+    torch.cuda.synchronize()

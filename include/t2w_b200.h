@@ -40,6 +40,7 @@ extern "C" {
 #define T2W_ERR_TIMEOUT (-4)     /* a kernel's bounded wait gave up (reported by t2w_check) */
 #define T2W_ERR_UNSUPPORTED (-5) /* config outside the kernels' shape set, or no sm_100 device */
 #define T2W_ERR_WORKSPACE (-6)   /* workspace too small */
+#define T2W_ERR_EXHAUSTED (-7)   /* the slot pool, the conv-cache row slots or the cache handles are used up */
 
 #define T2W_PREC_BF16 0 /* bf16 weights and activations, fp32 accumulate */
 #define T2W_PREC_FP8 1  /* e4m3 weights (power-of-two scale per 1x128 block) and e4m3 activations (power-of-two scale per
@@ -170,6 +171,61 @@ T2W_API size_t t2w_slot_workspace_bytes(const t2w_solver* s, const t2w_slots* p,
  * keep the input / output buffers fixed between calls (copy into static buffers) so the key repeats. */
 T2W_API int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* workspace, size_t workspace_bytes,
                             uint32_t flags, void* stream);
+
+/* ---- Stream caches kept by the library (replaces the reference's Python SlotPool / FastCache bookkeeping,
+ * engine/runtime/dit_fast.py:58-97,181-216, and the order / trim after a solve, dit_fast.py:480-490).  A cache is an
+ * int32 handle into a registry of the slot pools; per CFG row (0 conditional, 1 unconditional) it holds its key slots
+ * in the reference's tensor order (each kept window's keys in front of the older ones) and one conv-cache row slot.
+ * After a kept window the order is cut to its first `keep` entries plus its last 100 (token2wav_batch.py:33-39).
+ * Slots are handed out by the library; a stale or unknown handle is T2W_ERR_INVALID.  Calls on one t2w_slots are
+ * serialised by the library's lock; the GPU work they enqueue is ordered by the caller's stream (slots returned by one
+ * call may be written by the next call on the same stream). */
+typedef struct t2w_cache_info {
+  int32_t length;     /* cached keys per CFG row */
+  int32_t keep;       /* trim length */
+  int32_t rowslot[2]; /* conv-cache row slot of each CFG row */
+} t2w_cache_info;
+
+/* A new empty cache (FastDiT.new_cache, dit_fast.py:181-189): its two conv-cache row slots are zeroed on `stream`.
+ * T2W_ERR_EXHAUSTED when no row slots are left. */
+T2W_API int t2w_cache_new(t2w_slots* p, int32_t keep, void* stream, int32_t* handle);
+/* Return a cache's key and row slots (FastDiT.release, dit_fast.py:189-195); the handle is retired. */
+T2W_API int t2w_cache_release(t2w_slots* p, int32_t handle);
+/* An independent copy: new slots holding the same keys and values and a copy of the conv caches, enqueued on
+ * `stream` (FastDiT.clone, dit_fast.py:204-216). */
+T2W_API int t2w_cache_clone(t2w_slots* p, int32_t handle, void* stream, int32_t* out);
+T2W_API int t2w_cache_get(const t2w_slots* p, int32_t handle, t2w_cache_info* info);
+T2W_API int t2w_cache_set_keep(t2w_slots* p, int32_t handle, int32_t keep);
+/* The key slots of CFG row `half` in the reference's order (cap entries at most; returns T2W_ERR_INVALID if fewer). */
+T2W_API int t2w_cache_keys(const t2w_slots* p, int32_t handle, int32_t half, int32_t* slots, int32_t cap);
+/* Give an EMPTY cache n key slots per CFG row as its order (row 0's ids to slots[0 .. n), row 1's to slots[n .. 2n)),
+ * for callers that write keys into those slots themselves (the module-level forward_chunk adapter). */
+T2W_API int t2w_cache_reserve(t2w_slots* p, int32_t handle, int32_t n, int32_t* slots);
+/* Pool usage: key slots handed out, conv-cache row slots still free, live cache handles. */
+T2W_API int t2w_slots_usage(const t2w_slots* p, int32_t* keys_in_use, int32_t* rowslots_free, int32_t* caches);
+
+/* One window per request against the library-kept caches: the steady-state solve with the host bookkeeping done
+ * natively.  x0 of request i is temperature * noise[:, L_i : L_i + T_i] (the flow's fixed noise read at the cache
+ * length L_i, as FastDiT.solve reads cfm.rand_noise, dit_fast.py:448-449), gathered on the device.  Requests whose
+ * keep[i] != 0 keep the window's keys (in front of their order, then trimmed) and conv caches; the others (final
+ * flushes) leave their caches as they were. */
+typedef struct t2w_cached_batch {
+  int32_t n_streams;
+  const int32_t* handle;    /* host [n] cache handles, pairwise distinct */
+  const int32_t* chunk_len; /* host [n] window frames T_i > 0 */
+  const uint8_t* keep;      /* host [n] */
+  const float* noise;       /* device [mel, noise_frames] */
+  int32_t noise_frames;
+  float temperature;
+  const float* mu;          /* device [sum T, mel] */
+  const float* cond;        /* device [sum T, mel] or NULL (zeros) */
+  const float* spk;         /* device [n, mel] */
+  float* out;               /* device [sum T, mel] */
+} t2w_cached_batch;
+T2W_API size_t t2w_cached_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_cached_batch* b);
+/* Asynchronous on `stream`; the caches' records are updated before the call returns.  flags as t2w_solve_slots. */
+T2W_API int t2w_solve_cached(t2w_solver* s, t2w_slots* p, const t2w_cached_batch* b, void* workspace,
+                             size_t workspace_bytes, uint32_t flags, void* stream);
 
 /* Kernel classes of t2w_profile_solve. */
 enum t2w_kernel_class {

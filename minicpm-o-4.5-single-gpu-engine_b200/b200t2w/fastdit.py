@@ -3,65 +3,96 @@
 The reference keeps every CFG row's cached key frames in a slot pool (FlashInfer paged K/V, page size 1) and its two
 conv-cache frames per (step, block) in a row-slot pool; a call solves one window per request against those caches,
 appends the window's keys (``[new, cache]`` order) and trims the cache to the prompt's frames plus the last 100
-(``dit_fast.py:58-97,432-495``, ``token2wav_batch.py:33-39``).  ``B200FastDiT`` keeps that host bookkeeping (slot ids,
-the reference's key order, the trim) in Python, as the reference does, and runs the solve in the CUDA library
-(``t2w_solve_slots``): pools on the device, attention gathering each row's key list, conv caches filled in front of
-each window.  Method names and argument meaning follow ``FastDiT``: ``new_cache``, ``release``, ``clone``, ``solve``,
-``counts``, ``pool.in_use()``.  With ``use_graphs`` the solve replays a CUDA graph per call structure (sizes of the
-window and key lists), as ``FastDiT.capture`` does per bucket (``dit_fast.py:347-428``): inputs are copied into
-static buffers first (``dit_fast.py:463-469``), and a structure is captured the second time it is seen.
+(``dit_fast.py:58-97,432-495``, ``token2wav_batch.py:33-39``).  Here the pools, the caches' key orders, slot allocation
+and the trim all live in the CUDA library (``t2w_cache_*``, ``t2w_solve_cached``): a ``FastCache`` is a handle, and a
+call hands the library the handles, window lengths and inputs; the library builds every CFG row's key list, gathers
+x0 from the flow's fixed noise at each cache length, runs the solve (attention gathering each row's key list, conv
+caches filled in front of each window) and updates the orders.  Method names and argument meaning follow ``FastDiT``:
+``new_cache``, ``release``, ``clone``, ``solve``, ``counts``, ``pool.in_use()``, ``cnn_free``.  With ``use_graphs`` the
+solve replays a CUDA graph per call structure (sizes of the window and key lists), as ``FastDiT.capture`` does per
+bucket (``dit_fast.py:347-428``): inputs are copied into static buffers first (``dit_fast.py:463-469``), and a
+structure is captured the second time it is seen.
 """
 
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass, field
 
 import torch
 
 from . import lib as L
 from .solver import B200Solver
 
-TRIM_SUFFIX = 100
+TRIM_SUFFIX = 100  # keys kept after the first ``keep`` (the library applies the trim)
+_WORKSPACE_TOO_SMALL = -6
 
 
-class SlotIds:
-    """Host free list of pool slot ids (the reference's ``SlotPool`` bookkeeping, ``dit_fast.py:58-78``)."""
-
-    def __init__(self, n: int):
-        self.n = n
-        self.free = list(range(n - 1, -1, -1))
-
-    def alloc(self, k: int) -> list:
-        if k > len(self.free):
-            raise RuntimeError(f"Token2Wav cache pool exhausted ({k} slots wanted, {len(self.free)} free of {self.n})")
-        out = self.free[len(self.free) - k:][::-1] if k else []
-        del self.free[len(self.free) - k:]
-        return out
-
-    def release(self, ids: list) -> None:
-        self.free.extend(ids)
-
-    def in_use(self) -> int:
-        return self.n - len(self.free)
-
-
-@dataclass
-class FastRow:
-    """One CFG row's caches: key slots in the reference's tensor order and its conv-cache row slot."""
-    order: list = field(default_factory=list)
-    cnn: int = -1
-
-
-@dataclass
 class FastCache:
-    """A request's estimator caches (conditional and unconditional rows) and its trim length (prompt mel frames)."""
-    rows: tuple
-    keep: int = 0
+    """A request's estimator caches (both CFG rows), held by the library: a handle plus the two attributes the engine
+    reads and sets, ``length`` (cached keys per CFG row) and ``keep`` (the trim length: the prompt's mel frames)."""
+
+    __slots__ = ("_fd", "handle")
+
+    def __init__(self, fd: "B200FastDiT", handle: int):
+        self._fd, self.handle = fd, handle
+
+    def _info(self) -> L.CacheInfo:
+        info = L.CacheInfo()
+        L.call("t2w_cache_get", self._fd._p, self.handle, ctypes.byref(info))
+        return info
 
     @property
     def length(self) -> int:
-        return len(self.rows[0].order)
+        return self._info().length if self.handle >= 0 else 0
+
+    @property
+    def keep(self) -> int:
+        return self._info().keep if self.handle >= 0 else 0
+
+    @keep.setter
+    def keep(self, v: int) -> None:
+        L.call("t2w_cache_set_keep", self._fd._p, self.handle, int(v))
+
+
+class _PoolUsage:
+    """``pool.in_use()``: key slots handed out (both CFG rows count)."""
+
+    def __init__(self, fd: "B200FastDiT"):
+        self._fd = fd
+
+    def in_use(self) -> int:
+        return self._fd._usage()[0]
+
+
+class _FreeRowSlots:
+    """``len(cnn_free)``: conv-cache row slots still free (two per new cache)."""
+
+    def __init__(self, fd: "B200FastDiT"):
+        self._fd = fd
+
+    def __len__(self) -> int:
+        return self._fd._usage()[1]
+
+
+class _HostStaging:
+    """Pinned host mirrors of one static input buffer: a window's host tensors are concatenated into a mirror and moved
+    by one asynchronous copy.  Two mirrors alternate; a mirror is rewritten once the copy that last read it is done."""
+
+    def __init__(self, like: torch.Tensor):
+        self.bufs = [torch.empty(like.shape, dtype=like.dtype).pin_memory() for _ in range(2)]
+        self.events = [None, None]
+        self.next = 0
+
+    def copy(self, dst: torch.Tensor, src_host: torch.Tensor, stream) -> None:
+        k = self.next
+        self.next ^= 1
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        self.bufs[k].copy_(src_host)
+        dst.copy_(self.bufs[k], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.events[k] = ev
 
 
 class _DeviceArray:
@@ -92,12 +123,12 @@ class B200FastDiT:
         with torch.cuda.device(self.device):
             L.call("t2w_slots_create", solver._h, n_slots, n_rs, ctypes.byref(h))
         self._p = h
-        self.pool = SlotIds(n_slots)
-        self.cnn_free = list(range(n_rs - 1, 0, -1))
-        self.cnn_scratch = 0
+        self.pool = _PoolUsage(self)
+        self.cnn_free = _FreeRowSlots(self)
         self._ws = None
         self.use_graphs = use_graphs
         self._static = {}  # (tokens, requests, has cond) -> static input / output buffers of the graph path
+        self._staging = {}
         self.counts = {"graph": 0, "eager": 0}
         self.scratch = 0  # pool slots reserved for pad rows: none (pad rows never reach the pool here)
 
@@ -142,34 +173,33 @@ class B200FastDiT:
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
+    def _usage(self) -> tuple:
+        used, free, live = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        L.call("t2w_slots_usage", self._p, ctypes.byref(used), ctypes.byref(free), ctypes.byref(live))
+        return used.value, free.value, live.value
+
     # --- caches -------------------------------------------------------------------------------------------------------
     def new_cache(self) -> FastCache:
-        if len(self.cnn_free) < 2:
-            raise RuntimeError("Token2Wav conv-cache row slots exhausted")
-        rows = (FastRow(cnn=self.cnn_free.pop()), FastRow(cnn=self.cnn_free.pop()))
-        for r in rows:
-            L.call("t2w_slots_copy_row", self._p, -1, r.cnn, self._stream())
-        return FastCache(rows)
+        h = ctypes.c_int32()
+        L.call("t2w_cache_new", self._p, 0, self._stream(), ctypes.byref(h))
+        return FastCache(self, h.value)
 
     def release(self, c: FastCache) -> None:
-        for r in c.rows:
-            self.pool.release(r.order)
-            r.order = []
-            if r.cnn >= 0:
-                self.cnn_free.append(r.cnn)
-                r.cnn = -1
+        if c.handle >= 0:
+            L.call("t2w_cache_release", self._p, c.handle)
+            c.handle = -1
 
     def clone(self, c: FastCache) -> FastCache:
         """An independent copy (new slots holding the same keys and values, copied conv caches)."""
-        out = self.new_cache()
-        out.keep = c.keep
-        for src, dst in zip(c.rows, out.rows):
-            L.call("t2w_slots_copy_row", self._p, src.cnn, dst.cnn, self._stream())
-            dst.order = self.pool.alloc(len(src.order))
-            if src.order:
-                L.call("t2w_slots_copy", self._p, L.i32_array(src.order), L.i32_array(dst.order), len(src.order),
-                       self._stream())
-        return out
+        h = ctypes.c_int32()
+        L.call("t2w_cache_clone", self._p, c.handle, self._stream(), ctypes.byref(h))
+        return FastCache(self, h.value)
+
+    def _keys(self, c: FastCache, half: int) -> list:
+        n = c.length
+        arr = (ctypes.c_int32 * max(n, 1))()
+        L.call("t2w_cache_keys", self._p, c.handle, half, arr, n)
+        return list(arr[:n])
 
     # --- caches as tensors (the module-level forward_chunk adapter) ---------------------------------------------------
     def pools(self) -> tuple:
@@ -201,16 +231,19 @@ class B200FastDiT:
         kv, cn = self.pools()
         fc = self.new_cache()
         fc.keep = keep
+        slots = (ctypes.c_int32 * max(2 * Lk, 1))()
+        L.call("t2w_cache_reserve", self._p, fc.handle, Lk, slots)
+        rowslots = fc._info().rowslot
         a = att.to(self.device, torch.bfloat16)
         cc = cnn.to(self.device, torch.bfloat16)
-        for half, row in enumerate(fc.rows):
-            row.order = self.pool.alloc(Lk)
+        for half in range(2):
             if Lk:
                 x = a[:, :, half]  # [S, D, heads, L, 128]
                 k = x[..., :c.head_dim].permute(0, 1, 3, 2, 4).reshape(S * D, Lk, H)
                 v = x[..., c.head_dim:].permute(0, 1, 3, 2, 4).reshape(S * D, Lk, H)
-                kv[:, torch.tensor(row.order, device=self.device)] = torch.cat([k, v], dim=2)
-            cn[:, row.cnn] = cc[:, :, half].reshape(S * D, 2, H, 2).permute(0, 1, 3, 2)
+                idx = torch.tensor(list(slots[half * Lk:(half + 1) * Lk]), device=self.device)
+                kv[:, idx] = torch.cat([k, v], dim=2)
+            cn[:, rowslots[half]] = cc[:, :, half].reshape(S * D, 2, H, 2).permute(0, 1, 3, 2)
         return fc
 
     def export_cache(self, fc: FastCache, dtype=torch.float32) -> tuple:
@@ -221,13 +254,14 @@ class B200FastDiT:
         Lk = fc.length
         att = torch.empty(S, D, 2, nh, Lk, 2 * hd, dtype=dtype, device=self.device)
         cnn = torch.empty(S, D, 2, 2 * H, 2, dtype=dtype, device=self.device)
-        for half, row in enumerate(fc.rows):
+        rowslots = fc._info().rowslot
+        for half in range(2):
             if Lk:
-                x = kv[:, torch.tensor(row.order, device=self.device)]  # [S * D, L, 2H]
+                x = kv[:, torch.tensor(self._keys(fc, half), device=self.device)]  # [S * D, L, 2H]
                 k = x[..., :H].reshape(S, D, Lk, nh, hd).permute(0, 1, 3, 2, 4)
                 v = x[..., H:].reshape(S, D, Lk, nh, hd).permute(0, 1, 3, 2, 4)
                 att[:, :, half] = torch.cat([k, v], dim=-1).to(dtype)
-            cnn[:, :, half] = cn[:, row.cnn].permute(0, 1, 3, 2).reshape(S, D, 2 * H, 2).to(dtype)
+            cnn[:, :, half] = cn[:, rowslots[half]].permute(0, 1, 3, 2).reshape(S, D, 2 * H, 2).to(dtype)
         return att, cnn
 
     @torch.inference_mode()
@@ -258,72 +292,67 @@ class B200FastDiT:
         return mel[None], new_cnn, new_att
 
     # --- solve --------------------------------------------------------------------------------------------------------
+    def _stage(self, key, name: str, dst: torch.Tensor, parts: list) -> None:
+        """Concatenate ``parts`` ([T_i, mel] views, host or device) into the static device buffer ``dst``: on the
+        device with one kernel when every part is there, else on the host into a pinned mirror and one copy."""
+        if all(t.device == self.device for t in parts):
+            torch.cat([t.to(torch.float32) for t in parts], out=dst)
+            return
+        host = torch.cat([t.detach().to("cpu", torch.float32) for t in parts])
+        st = self._staging.get((key, name))
+        if st is None:
+            st = self._staging[(key, name)] = _HostStaging(dst)
+        st.copy(dst, host, torch.cuda.current_stream(self.device))
+
     @torch.inference_mode()
     def solve(self, caches: list, mu: list, spks: torch.Tensor, cond: list | None, keep: list,
               temperature: float = 1.0) -> list:
         """One window per request (``FastDiT.solve``): ``mu[i]`` [mel, T_i], ``spks`` [n, mel] (after the affine
         layer), ``cond[i]`` [mel, T_i] or None (zeros; ``cond`` None: zeros for all).  Requests with ``keep[i]`` keep
         the window's keys and conv caches, trimmed as the reference trims them; the others (final flushes) leave their
-        caches untouched.  Returns each request's mel [mel, T_i] fp32."""
+        caches untouched.  Returns each request's mel [mel, T_i] fp32 (views of one fresh tensor, as the reference
+        returns views of its output)."""
         n = len(caches)
         mel = self.cfg.mel
         Ts = [int(m.shape[1]) for m in mu]
-        lens = [c.length for c in caches]
-        rows = [c.rows[0] for c in caches] + [c.rows[1] for c in caches]
-        new = [self.pool.alloc(t) for t in Ts + Ts]
-        kv_len, kv_idx, rd, wr = [], [], [], []
-        for r in range(2 * n):
-            i = r % n
-            lst = rows[r].order + new[r]  # attention depends on the key set; the window's slots go last
-            kv_len.append(len(lst))
-            kv_idx += lst
-            rd.append(rows[r].cnn)
-            wr.append(rows[r].cnn if keep[i] else self.cnn_scratch)
         dev = self.device
         n_tok = sum(Ts)
         key = (n_tok, n, cond is not None)
         bufs = self._static.get(key)
         if bufs is None:
             z = lambda *sh: torch.zeros(*sh, dtype=torch.float32, device=dev)  # noqa: E731
-            bufs = {"x0": z(n_tok, mel), "mu": z(n_tok, mel), "cond": z(n_tok, mel) if cond is not None else None,
-                    "spk": z(n, mel), "out": z(n_tok, mel)}
+            bufs = {"mu": z(n_tok, mel), "cond": z(n_tok, mel) if cond is not None else None, "spk": z(n, mel),
+                    "out": z(n_tok, mel)}
             self._static[key] = bufs
-        torch.cat([self.noise[:, o:o + t].t() for o, t in zip(lens, Ts)], out=bufs["x0"])
-        if temperature != 1.0:  # the fixed noise scaled as CausalConditionalCFM.forward_chunk scales it
-            bufs["x0"].mul_(temperature)
-        # inputs in pinned host memory are copied without stalling the host (pageable ones copy synchronously)
-        torch.cat([m.t().to(dev, torch.float32, non_blocking=True) for m in mu], out=bufs["mu"])
+        self._stage(key, "mu", bufs["mu"], [m.t() for m in mu])
         if cond is not None:
-            torch.cat([(c.t() if c is not None else torch.zeros(t, mel)).to(dev, torch.float32, non_blocking=True)
-                       for c, t in zip(cond, Ts)], out=bufs["cond"])
-        bufs["spk"].copy_(spks.to(dev, torch.float32, non_blocking=True))
-        out = bufs["out"]
+            self._stage(key, "cond", bufs["cond"],
+                        [c.t() if c is not None else torch.zeros(t, mel, device=mu[i].device) for i, (c, t)
+                         in enumerate(zip(cond, Ts))])
+        self._stage(key, "spk", bufs["spk"], [spks.reshape(n, mel)])
         P = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
-        arrs = [L.i32_array(a) for a in (Ts, kv_len, kv_idx, rd, wr)]  # alive until the call returns
-        ip = [ctypes.cast(a, ctypes.POINTER(ctypes.c_int32)) for a in arrs]
-        b = L.SlotBatch(n, *ip, P(bufs["x0"]), P(bufs["mu"]), P(bufs["cond"]), P(bufs["spk"]), P(out))
-        need = int(self._lib.t2w_slot_workspace_bytes(self.solver._h, self._p, ctypes.byref(b)))
-        if not need:
-            raise L.T2WError("t2w_slot_workspace_bytes", -1)
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        handles = L.i32_array([c.handle for c in caches])
+        tl = L.i32_array(Ts)
+        kp = (ctypes.c_uint8 * n)(*[1 if k else 0 for k in keep])
+        b = L.CachedBatch(n, handles, tl, kp, P(self.noise), int(self.noise.shape[1]), float(temperature), P(bufs["mu"]),
+                          P(bufs["cond"]), P(bufs["spk"]), P(bufs["out"]))
         before = self.solver.counts()["graph"]
-        L.call("t2w_solve_slots", self.solver._h, self._p, ctypes.byref(b), P(self._ws), self._ws.numel(),
-               L.FLAG_GRAPH if self.use_graphs else 0, self._stream())
+        flags = L.FLAG_GRAPH if self.use_graphs else 0
+        for _ in range(2):
+            ws = self._ws if self._ws is not None else torch.empty(256, dtype=torch.uint8, device=dev)
+            rc = self._lib.t2w_solve_cached(self.solver._h, self._p, ctypes.byref(b), P(ws), ws.numel(), flags,
+                                            self._stream())
+            if rc != _WORKSPACE_TOO_SMALL:
+                break
+            need = int(self._lib.t2w_cached_workspace_bytes(self.solver._h, self._p, ctypes.byref(b)))
+            if not need:
+                raise L.T2WError("t2w_cached_workspace_bytes", -1)
+            self._ws = torch.empty(need + need // 4, dtype=torch.uint8, device=dev)
+        L.check("t2w_solve_cached", rc)
         self.counts["graph" if self.solver.counts()["graph"] > before else "eager"] += 1
-        # the reference's cache order and trim (dit_fast.py:482-490)
-        for i, c in enumerate(caches):
-            for r, nw in ((rows[i], new[i]), (rows[n + i], new[n + i])):
-                if keep[i]:
-                    order = nw + r.order
-                    if len(order) > c.keep + TRIM_SUFFIX:
-                        self.pool.release(order[c.keep:len(order) - TRIM_SUFFIX])
-                        order = order[:c.keep] + order[len(order) - TRIM_SUFFIX:]
-                    r.order = order
-                else:
-                    self.pool.release(nw)
+        out = bufs["out"].clone()  # the static buffer is rewritten by the next call
         res, o = [], 0
         for t in Ts:
-            res.append(out[o:o + t].t().clone())  # the static buffer is rewritten by the next call
+            res.append(out[o:o + t].t())
             o += t
         return res

@@ -14,7 +14,8 @@ from .build import INCLUDE, LIB_PATH
 
 T2W_OK = 0
 STATUS = {-1: "invalid argument or shape", -2: "CUDA error", -3: "out of device memory", -4: "kernel wait timed out",
-          -5: "unsupported config or device", -6: "workspace too small"}
+          -5: "unsupported config or device", -6: "workspace too small",
+          -7: "Token2Wav cache pool exhausted (key slots, conv-cache row slots or cache handles)"}
 PREC = {"bf16": 0, "fp8": 1}
 FLAG_GRAPH = 1
 EPI = {"f32": 0, "bf16": 1, "gelu": 2, "resid": 3, "qkv": 4, "gelu_fp8": 8}
@@ -56,6 +57,17 @@ class SlotBatch(ctypes.Structure):
                [(n, ctypes.c_void_p) for n in ("x0", "mu", "cond", "spk", "out")]
 
 
+class CacheInfo(ctypes.Structure):
+    _fields_ = [("length", ctypes.c_int32), ("keep", ctypes.c_int32), ("rowslot", ctypes.c_int32 * 2)]
+
+
+class CachedBatch(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_int32), ("handle", ctypes.POINTER(ctypes.c_int32)),
+                ("chunk_len", ctypes.POINTER(ctypes.c_int32)), ("keep", ctypes.POINTER(ctypes.c_uint8)),
+                ("noise", ctypes.c_void_p), ("noise_frames", ctypes.c_int32), ("temperature", ctypes.c_float),
+                ("mu", ctypes.c_void_p), ("cond", ctypes.c_void_p), ("spk", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _F = ctypes.c_float
@@ -90,6 +102,16 @@ _SIGS = {
                          ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_slot_workspace_bytes": ([_P, _P, ctypes.POINTER(SlotBatch)], ctypes.c_size_t),
     "t2w_solve_slots": ([_P, _P, ctypes.POINTER(SlotBatch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
+    "t2w_cache_new": ([_P, _I, _P, ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_cache_release": ([_P, _I], ctypes.c_int),
+    "t2w_cache_clone": ([_P, _I, _P, ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_cache_get": ([_P, _I, ctypes.POINTER(CacheInfo)], ctypes.c_int),
+    "t2w_cache_set_keep": ([_P, _I, _I], ctypes.c_int),
+    "t2w_cache_keys": ([_P, _I, _I, ctypes.POINTER(_I), _I], ctypes.c_int),
+    "t2w_cache_reserve": ([_P, _I, _I, ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_slots_usage": ([_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_cached_workspace_bytes": ([_P, _P, ctypes.POINTER(CachedBatch)], ctypes.c_size_t),
+    "t2w_solve_cached": ([_P, _P, ctypes.POINTER(CachedBatch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
     "t2w_e4m3_sf_bytes": ([_I, _I], ctypes.c_size_t),
     "t2w_quant_e4m3": ([_P, _I, _I, _P, _P, _I, ctypes.c_int64, _P], ctypes.c_int),
     "t2w_quant_weight_e4m3": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),

@@ -154,6 +154,9 @@ int launch_slot_copy(__nv_bfloat16* pool, int pool_ld, long long sb_ld, int n_sb
                      cudaStream_t st);
 int launch_rowslot_copy(__nv_bfloat16* cpool, long long slot_ld, long long sb_ld, int n_sb, int src, int dst,
                         cudaStream_t st);
+// x0[i][c] = temp * noise[c * frames + col[i]] for n tokens (token-major [n, mel] fp32).
+int launch_noise_x0(const float* noise, int frames, int mel, const int* col, int n, float temp, float* x0,
+                    cudaStream_t st);
 
 // Row kernels.
 int launch_ln_mod(const float* h, int ldh, const float* shift, const float* scale1, float eps, int rows, int C,

@@ -89,7 +89,32 @@ __global__ void __launch_bounds__(256) k_rowslot_copy(__nv_bfloat16* __restrict_
   for (int c = threadIdx.x; c < slot_ld / 8; c += blockDim.x) d[c] = s ? s[c] : make_uint4(0, 0, 0, 0);
 }
 
+// x0 of a solve over library-kept caches: token i's channel c = temp * noise[c][col[i]] (the flow's fixed noise,
+// [mel, frames], read at each request's cache length).  One thread per (token, channel), token-major output.
+__global__ void __launch_bounds__(256) k_noise_x0(const float* __restrict__ noise, int frames, int mel,
+                                                  const int* __restrict__ col, int n, float temp, float* __restrict__ x0) {
+  pdl_wait();
+  pdl_launch();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)n * mel) return;
+  const int tok = (int)(i / mel), c = (int)(i - (long long)tok * mel);
+  x0[i] = temp * noise[(size_t)c * frames + col[tok]];
+}
+
 }  // namespace
+
+int launch_noise_x0(const float* noise, int frames, int mel, const int* col, int n, float temp, float* x0,
+                    cudaStream_t st) {
+  if (n <= 0) return T2W_OK;
+  const long long items = (long long)n * mel;
+  cudaError_t e = launch_k(k_noise_x0, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, st, noise, frames, mel, col,
+                           n, temp, x0);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  return T2W_OK;
+}
 
 int launch_kv_scatter(const __nv_bfloat16* qkv, int H, const int* tok_qrow, const int* tok_slot, int n,
                       __nv_bfloat16* pool, cudaStream_t st) {

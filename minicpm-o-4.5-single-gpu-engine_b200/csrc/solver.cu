@@ -22,6 +22,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "cache_registry.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -138,6 +139,16 @@ struct Plan {
   bool slots = false;
   std::vector<int> kv_idx, tok_qrow, tok_slot;
   std::vector<ConvRow> conv_rows;
+  // solves over library-kept caches: x0 gathered on the device from the flow's noise at column tok_col[token]
+  bool gather = false;
+  std::vector<int> tok_col;
+};
+
+// The flow's fixed noise a gathered x0 is read from ([mel, frames] fp32) and its temperature.
+struct NoiseSrc {
+  const float* noise = nullptr;
+  int frames = 0;
+  float temperature = 1.f;
 };
 
 struct WsLayout {
@@ -146,6 +157,10 @@ struct WsLayout {
   size_t a8, sfa, o8, sfo, c18, sfc1, f8, sff, sf_h, sf_f;
   // slot-pool solves: device copies of the plan's key lists, conv rows and new-key scatter lists
   size_t kv_idx, conv_rows, tok_qrow, tok_slot;
+  // solves over library-kept caches: the gathered x0 [n_tok, mel] and each token's noise column
+  size_t x0g, tok_col;
+  // the block of index arrays uploaded per plan (pad .. tok_col)
+  size_t meta, meta_bytes;
   // completion counters of the GEMMs whose following row kernel starts early: [step][block][4][rows / 128]
   size_t done;
   size_t total;
@@ -182,12 +197,25 @@ struct t2w_solver {
   std::unordered_map<uintptr_t, uint64_t> ws_meta;  // workspace -> plan key of the index arrays it holds
   std::vector<cudaEvent_t> prof_events;
   int64_t n_replays = 0, n_captures = 0, n_eager = 0;
+  // pinned host images of the plans' index arrays, rotated between uploads
+  static constexpr int kStaging = 4;
+  struct Staging {
+    void* host = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+    bool used = false;
+  };
+  Staging staging[kStaging];
+  int staging_next = 0;
 };
 
 // Device pools of the steady-state solve (one per solver and device): K/V slots per (step, block) and conv-cache row
 // slots per (step, block).
 struct t2w_slots {
   int device = 0, n_slots = 0, n_rowslots = 0, n_sb = 0, H = 0;
+  // the caches kept by the library (handles, key orders, slot allocation) and the lock its entry points take
+  t2w::CacheRegistry reg;
+  std::mutex mu;
   __nv_bfloat16* kv = nullptr;   // [n_sb][n_slots][2 H]
   __nv_bfloat16* cnn = nullptr;  // [n_sb][n_rowslots][2 convs][2 frames][H]
   long long kv_sb() const { return (long long)n_slots * 2 * H; }
@@ -306,17 +334,28 @@ WsLayout layout(const t2w_config& c, const Plan& pl, bool fp8) {
   w.f = take(R * (size_t)c.ffn * 2);
   w.dphi = take(R * (size_t)c.mel * 4);
   w.x = take((size_t)pl.n_tok * c.mel * 4);
-  w.pad = take(R);
-  w.tok_row = take((size_t)pl.n_tok * 4);
-  w.tok_stream = take((size_t)pl.n_tok * 4);
-  w.work = take((size_t)pl.n_work * sizeof(AttnWork));
   w.done = take((size_t)c.steps * c.depth * 4 * (pl.rows / 128) * sizeof(int));
+  if (pl.gather) w.x0g = take((size_t)pl.n_tok * c.mel * 4);
+  // the plan's index arrays, packed in one block (16-byte aligned entries) that one host-to-device copy fills
+  w.meta = off;
+  auto put = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 15) & ~size_t(15);
+    return o;
+  };
+  w.pad = put(R);
+  w.tok_row = put((size_t)pl.n_tok * 4);
+  w.tok_stream = put((size_t)pl.n_tok * 4);
+  w.work = put((size_t)pl.n_work * sizeof(AttnWork));
   if (pl.slots) {
-    w.kv_idx = take(pl.kv_idx.size() * 4);
-    w.conv_rows = take(pl.conv_rows.size() * sizeof(ConvRow));
-    w.tok_qrow = take(pl.tok_qrow.size() * 4);
-    w.tok_slot = take(pl.tok_slot.size() * 4);
+    w.kv_idx = put(pl.kv_idx.size() * 4);
+    w.conv_rows = put(pl.conv_rows.size() * sizeof(ConvRow));
+    w.tok_qrow = put(pl.tok_qrow.size() * 4);
+    w.tok_slot = put(pl.tok_slot.size() * 4);
   }
+  if (pl.gather) w.tok_col = put(pl.tok_col.size() * 4);
+  w.meta_bytes = off - w.meta;
+  off = align256(off);
   if (fp8) {
     // the row-shifted scale layouts hold rows up to rows + 1: one spare row tile
     w.sf_h = align256(gemm8_sf_bytes(pl.rows + 128, c.hidden));
@@ -360,7 +399,7 @@ struct Prof {
 
 // Enqueue one whole solve (no host synchronisation, graph-capturable).
 int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, cudaStream_t st, Prof* prof = nullptr,
-                  const t2w_slots* sp = nullptr) {
+                  const t2w_slots* sp = nullptr, const NoiseSrc* nsrc = nullptr) {
   Prof none;
   Prof& P = prof ? *prof : none;
   const t2w_config& c = s->cfg;
@@ -470,6 +509,11 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   // the N = H GEMMs (proj, conv1, conv2, fc2) publish per-block completion; the row kernel after each waits per block
   const int done_target = 8 * (H / gemm_block_n_for(H, R, T2W_EPI_BF16));
   T2W_TRY(P.tick(T2W_KC_PACK, st));
+  if (pl.gather) {  // x0 from the flow's noise at each request's cache length, into the workspace (b.x0 points there)
+    if (!nsrc || b.x0 != at<float>(ws, L.x0g)) return T2W_ERR_INVALID;
+    T2W_TRY(launch_noise_x0(nsrc->noise, nsrc->frames, mel, at<int>(ws, L.tok_col), pl.n_tok, nsrc->temperature,
+                            at<float>(ws, L.x0g), st));
+  }
   T2W_TRY(launch_pack(b.x0, b.mu, b.cond, b.spk, tok_row, tok_stream, pl.n_tok, mel, pl.half_rows, hx, 4 * mel, x, st));
 
   GemmArgs g;
@@ -675,20 +719,42 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   return P.tick(-1, st);  // closing event
 }
 
+// Copy the plan's index arrays into the workspace: their image is assembled in a pinned host staging buffer and moved
+// by one asynchronous copy (a copy from pageable memory would first synchronise the stream, stalling the host on the
+// previous solve).  Staging buffers rotate; one is rewritten only after the copy that last read it has completed.
 int upload_meta(t2w_solver* s, const Plan& pl, void* ws, cudaStream_t st) {
   const WsLayout L = layout(s->cfg, pl, s->precision == T2W_PREC_FP8);
-  T2W_CUDA(cudaMemcpyAsync(at<uint8_t>(ws, L.pad), pl.pad.data(), pl.pad.size(), cudaMemcpyHostToDevice, st));
-  T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_row), pl.tok_row.data(), pl.tok_row.size() * 4, cudaMemcpyHostToDevice, st));
-  T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_stream), pl.tok_stream.data(), pl.tok_stream.size() * 4,
-                           cudaMemcpyHostToDevice, st));
-  T2W_CUDA(cudaMemcpyAsync(at<AttnWork>(ws, L.work), pl.work.data(), pl.work.size() * sizeof(AttnWork),
-                           cudaMemcpyHostToDevice, st));
+  t2w_solver::Staging& sg = s->staging[s->staging_next];
+  s->staging_next = (s->staging_next + 1) % t2w_solver::kStaging;
+  if (sg.used) T2W_CUDA(cudaEventSynchronize(sg.done));
+  if (sg.cap < L.meta_bytes) {
+    if (sg.host) cudaFreeHost(sg.host);
+    sg.host = nullptr;
+    sg.cap = 0;
+    const size_t cap = std::max<size_t>(L.meta_bytes + L.meta_bytes / 4, 1 << 16);
+    T2W_CUDA(cudaMallocHost(&sg.host, cap));
+    sg.cap = cap;
+  }
+  if (!sg.done) T2W_CUDA(cudaEventCreateWithFlags(&sg.done, cudaEventDisableTiming));
+  uint8_t* img = static_cast<uint8_t*>(sg.host);
+  auto put = [&](size_t off, const void* src, size_t bytes) {
+    if (bytes) std::memcpy(img + (off - L.meta), src, bytes);
+  };
+  put(L.pad, pl.pad.data(), pl.pad.size());
+  put(L.tok_row, pl.tok_row.data(), pl.tok_row.size() * 4);
+  put(L.tok_stream, pl.tok_stream.data(), pl.tok_stream.size() * 4);
+  put(L.work, pl.work.data(), pl.work.size() * sizeof(AttnWork));
   if (pl.slots) {
-    T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.kv_idx), pl.kv_idx.data(), pl.kv_idx.size() * 4, cudaMemcpyHostToDevice, st));
-    T2W_CUDA(cudaMemcpyAsync(at<ConvRow>(ws, L.conv_rows), pl.conv_rows.data(), pl.conv_rows.size() * sizeof(ConvRow),
-                             cudaMemcpyHostToDevice, st));
-    T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_qrow), pl.tok_qrow.data(), pl.tok_qrow.size() * 4, cudaMemcpyHostToDevice, st));
-    T2W_CUDA(cudaMemcpyAsync(at<int>(ws, L.tok_slot), pl.tok_slot.data(), pl.tok_slot.size() * 4, cudaMemcpyHostToDevice, st));
+    put(L.kv_idx, pl.kv_idx.data(), pl.kv_idx.size() * 4);
+    put(L.conv_rows, pl.conv_rows.data(), pl.conv_rows.size() * sizeof(ConvRow));
+    put(L.tok_qrow, pl.tok_qrow.data(), pl.tok_qrow.size() * 4);
+    put(L.tok_slot, pl.tok_slot.data(), pl.tok_slot.size() * 4);
+  }
+  if (pl.gather) put(L.tok_col, pl.tok_col.data(), pl.tok_col.size() * 4);
+  T2W_CUDA(cudaMemcpyAsync(at<uint8_t>(ws, L.meta), img, L.meta_bytes, cudaMemcpyHostToDevice, st));
+  T2W_CUDA(cudaEventRecord(sg.done, st));
+  sg.used = true;
+  if (pl.slots) {
     s->ws_meta.erase(reinterpret_cast<uintptr_t>(ws));  // slot lists change every call: nothing to reuse
     return T2W_OK;
   }
@@ -807,6 +873,88 @@ int attn_varlen_alloc(const void* qkv, int rows, int heads, int n_seq, const int
   const int rc = launch_attn(a, st);
   cudaFreeAsync(d, st);
   return rc;
+}
+
+// Enqueue a planned slot-pool solve (eager, or a CUDA graph per launch structure).  The launches depend on the plan's
+// sizes and the buffers only: the slot lists, conv rows, work list (and, for gathered x0, the noise columns) are read
+// from the workspace, where upload_meta has just put this call's.  A graph per such key, captured the second time the
+// key is seen (a key met once, as while caches still grow towards their trimmed length, runs eagerly).
+int run_slot_plan(t2w_solver* s, t2w_slots* p, const Plan& pl, const t2w_batch& pb, void* ws, uint32_t flags,
+                  cudaStream_t st, const NoiseSrc* nsrc) {
+  T2W_TRY(upload_meta(s, pl, ws, st));
+  uint64_t key = 0x510750175107ull;
+  for (long long v : {(long long)pl.n_streams, (long long)pl.n_tok, (long long)pl.half_rows, (long long)pl.rows,
+                      (long long)pl.n_work, (long long)pl.kv_idx.size(), (long long)pl.conv_rows.size(),
+                      (long long)pl.tok_slot.size(), (long long)pl.gather})
+    key = mix(key, (uint64_t)v);
+  for (const void* q : {(const void*)ws, (const void*)pb.x0, (const void*)pb.mu, (const void*)pb.cond,
+                        (const void*)pb.spk, (const void*)pb.out, (const void*)p->kv, (const void*)p->cnn})
+    key = mix(key, reinterpret_cast<uint64_t>(q));
+  if (nsrc) {  // the noise buffer and temperature are baked into the gather launch
+    uint32_t tb = 0;
+    std::memcpy(&tb, &nsrc->temperature, 4);
+    key = mix(mix(mix(key, reinterpret_cast<uint64_t>(nsrc->noise)), (uint64_t)nsrc->frames), tb);
+  }
+  if (s->slot_seen.size() > 4096) s->slot_seen.clear();
+  if ((flags & T2W_FLAG_GRAPH) && (s->graphs.count(key) || ++s->slot_seen[key] >= 2))
+    return replay(s, key, st, [&](cudaStream_t cs) { return enqueue_solve(s, pl, pb, ws, cs, nullptr, p, nsrc); });
+  T2W_TRY(enqueue_solve(s, pl, pb, ws, st, nullptr, p, nsrc));
+  ++s->n_eager;
+  return T2W_OK;
+}
+
+// The key lists, conv rows and noise columns of a window solve over library-kept caches (records already checked).
+// fresh holds 2 * sum T new slots: request i's CFG row h takes T_i of them at fresh_off[h * n + i].
+bool plan_cached(const t2w_config& c, const t2w_slots* p, int n, const int32_t* T, const uint8_t* keep,
+                 const std::vector<CacheRecord*>& recs, const std::vector<int32_t>& fresh, Plan& pl) {
+  std::vector<int> kv_len(2 * n), rd(2 * n), wr(2 * n);
+  std::vector<int> kv_idx;
+  size_t total = 0;
+  for (int r = 0; r < 2 * n; ++r) total += recs[r % n]->keys[r / n].size() + (size_t)T[r % n];
+  kv_idx.reserve(total);
+  size_t fo = 0;
+  std::vector<size_t> fresh_off(2 * n);
+  for (int h = 0; h < 2; ++h)
+    for (int i = 0; i < n; ++i) {
+      fresh_off[h * n + i] = fo;
+      fo += (size_t)T[i];
+    }
+  for (int r = 0; r < 2 * n; ++r) {
+    const int i = r % n, h = r / n;
+    const std::vector<int32_t>& k = recs[i]->keys[h];
+    kv_idx.insert(kv_idx.end(), k.begin(), k.end());  // cached keys, then the window's new slots
+    kv_idx.insert(kv_idx.end(), fresh.begin() + fresh_off[r], fresh.begin() + fresh_off[r] + T[i]);
+    kv_len[r] = (int)k.size() + T[i];
+    rd[r] = recs[i]->rowslot[h];
+    wr[r] = keep[i] ? rd[r] : 0;  // row slot 0: scratch target of rows that keep nothing
+  }
+  if (!make_plan_slots(c, n, T, kv_len.data(), kv_idx.data(), rd.data(), wr.data(), p->n_slots, p->n_rowslots, pl))
+    return false;
+  pl.gather = true;
+  pl.tok_col.clear();
+  pl.tok_col.reserve(pl.n_tok);
+  for (int i = 0; i < n; ++i)
+    for (int t = 0; t < T[i]; ++t) pl.tok_col.push_back((int)recs[i]->keys[0].size() + t);
+  return true;
+}
+
+// Records of a cached batch: every handle live and used once, every window inside the noise.
+int cached_records(t2w_slots* p, const t2w_cached_batch* b, std::vector<CacheRecord*>& recs, long long* new_slots) {
+  const int n = b->n_streams;
+  if (n <= 0 || !b->handle || !b->chunk_len || !b->keep || b->noise_frames <= 0) return T2W_ERR_INVALID;
+  std::vector<int32_t> ids(b->handle, b->handle + n);
+  std::sort(ids.begin(), ids.end());
+  if (std::adjacent_find(ids.begin(), ids.end()) != ids.end()) return T2W_ERR_INVALID;
+  recs.resize(n);
+  long long need = 0;
+  for (int i = 0; i < n; ++i) {
+    recs[i] = p->reg.find(b->handle[i]);
+    if (!recs[i] || b->chunk_len[i] <= 0) return T2W_ERR_INVALID;
+    if ((long long)recs[i]->keys[0].size() + b->chunk_len[i] > b->noise_frames) return T2W_ERR_INVALID;
+    need += 2ll * b->chunk_len[i];
+  }
+  *new_slots = need;
+  return T2W_OK;
 }
 
 }  // namespace
@@ -1035,6 +1183,13 @@ int t2w_destroy(t2w_solver* s) {
   }
   if (s->cap_stream) cudaStreamDestroy(s->cap_stream);
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
+  for (auto& sg : s->staging) {
+    if (sg.done) {
+      cudaEventSynchronize(sg.done);
+      cudaEventDestroy(sg.done);
+    }
+    if (sg.host) cudaFreeHost(sg.host);
+  }
   cudaFree(s->arena);
   delete s;
   return T2W_OK;
@@ -1143,6 +1298,7 @@ int t2w_slots_create(const t2w_solver* s, int32_t n_slots, int32_t n_rowslots, t
   p->n_rowslots = n_rowslots;
   p->n_sb = s->cfg.steps * s->cfg.depth;
   p->H = s->cfg.hidden;
+  p->reg.init(n_slots, n_rowslots);
   const size_t kv_bytes = (size_t)p->n_sb * p->kv_sb() * 2, cnn_bytes = (size_t)p->n_sb * p->cnn_sb() * 2;
   if (cudaMalloc(reinterpret_cast<void**>(&p->kv), kv_bytes) != cudaSuccess) {
     delete p;
@@ -1229,8 +1385,6 @@ int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* 
     return T2W_ERR_INVALID;
   if (layout(s->cfg, pl, false).total > ws_bytes) return T2W_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(ws) & 255) return T2W_ERR_INVALID;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  T2W_TRY(upload_meta(s, pl, ws, st));
   // the window solve is the packed solve's body with P = 0 rows: every row a window
   t2w_batch pb{};
   pb.n_streams = b->n_streams;
@@ -1239,22 +1393,198 @@ int t2w_solve_slots(t2w_solver* s, t2w_slots* p, const t2w_slot_batch* b, void* 
   pb.cond = b->cond;
   pb.spk = b->spk;
   pb.out = b->out;
-  // The launches depend on the plan's sizes and the buffers only: the slot lists, conv rows and work list are read
-  // from the workspace, where upload_meta has just put this call's.  A graph per such key, captured the second time
-  // the key is seen (a key met once, as while caches still grow towards their trimmed length, runs eagerly).
-  uint64_t key = 0x510750175107ull;
-  for (long long v : {(long long)pl.n_streams, (long long)pl.n_tok, (long long)pl.half_rows, (long long)pl.rows,
-                      (long long)pl.n_work, (long long)pl.kv_idx.size(), (long long)pl.conv_rows.size(),
-                      (long long)pl.tok_slot.size()})
-    key = mix(key, (uint64_t)v);
-  for (const void* q : {(const void*)ws, (const void*)b->x0, (const void*)b->mu, (const void*)b->cond,
-                        (const void*)b->spk, (const void*)b->out, (const void*)p->kv, (const void*)p->cnn})
-    key = mix(key, reinterpret_cast<uint64_t>(q));
-  if (s->slot_seen.size() > 4096) s->slot_seen.clear();
-  if ((flags & T2W_FLAG_GRAPH) && (s->graphs.count(key) || ++s->slot_seen[key] >= 2))
-    return replay(s, key, st, [&](cudaStream_t cs) { return enqueue_solve(s, pl, pb, ws, cs, nullptr, p); });
-  T2W_TRY(enqueue_solve(s, pl, pb, ws, st, nullptr, p));
-  ++s->n_eager;
+  return run_slot_plan(s, p, pl, pb, ws, flags, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+// ---- caches kept by the library -----------------------------------------------------------------------------------
+
+int t2w_cache_new(t2w_slots* p, int32_t keep, void* stream, int32_t* handle) {
+  if (!p || !handle) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(p->device);
+  std::lock_guard<std::mutex> lock(p->mu);
+  const int32_t id = p->reg.open();
+  if (id < 0) return T2W_ERR_EXHAUSTED;
+  CacheRecord* r = p->reg.find(id);
+  r->keep = keep;
+  for (int h = 0; h < 2; ++h) {
+    const int rc = launch_rowslot_copy(p->cnn, p->cnn_slot(), p->cnn_sb(), p->n_sb, -1, r->rowslot[h],
+                                       static_cast<cudaStream_t>(stream));
+    if (rc) {
+      p->reg.close(id);
+      return rc;
+    }
+  }
+  *handle = id;
+  return T2W_OK;
+}
+
+int t2w_cache_release(t2w_slots* p, int32_t handle) {
+  if (!p) return T2W_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(p->mu);
+  if (!p->reg.find(handle)) return T2W_ERR_INVALID;
+  p->reg.close(handle);
+  return T2W_OK;
+}
+
+int t2w_cache_clone(t2w_slots* p, int32_t handle, void* stream, int32_t* out) {
+  if (!p || !out) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(p->device);
+  std::lock_guard<std::mutex> lock(p->mu);
+  if (!p->reg.find(handle)) return T2W_ERR_INVALID;
+  const int32_t id = p->reg.open();  // may grow the record table: look both records up afterwards
+  if (id < 0) return T2W_ERR_EXHAUSTED;
+  CacheRecord* src = p->reg.find(handle);
+  CacheRecord* dst = p->reg.find(id);
+  dst->keep = src->keep;
+  const int n = (int)src->keys[0].size();
+  std::vector<int32_t> ids(2 * (size_t)n);
+  if (!p->reg.slots.take(2 * n, ids.data())) {
+    p->reg.close(id);
+    return T2W_ERR_EXHAUSTED;
+  }
+  dst->keys[0].assign(ids.begin(), ids.begin() + n);
+  dst->keys[1].assign(ids.begin() + n, ids.end());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = T2W_OK;
+  for (int h = 0; h < 2 && !rc; ++h)
+    rc = launch_rowslot_copy(p->cnn, p->cnn_slot(), p->cnn_sb(), p->n_sb, src->rowslot[h], dst->rowslot[h], st);
+  if (!rc && n > 0) {
+    std::vector<int32_t> from(src->keys[0]);
+    from.insert(from.end(), src->keys[1].begin(), src->keys[1].end());
+    int* d = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d), 4 * (size_t)n * 4, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d, from.data(), 2 * (size_t)n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d + 2 * n, ids.data(), 2 * (size_t)n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) rc = launch_slot_copy(p->kv, 2 * p->H, p->kv_sb(), p->n_sb, d, d + 2 * n, 2 * n, st);
+    if (d) cudaFreeAsync(d, st);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      rc = T2W_ERR_CUDA;
+    }
+    // the host index vectors above are pageable: the copies complete before cudaMemcpyAsync returns
+  }
+  if (rc) {
+    p->reg.close(id);
+    return rc;
+  }
+  *out = id;
+  return T2W_OK;
+}
+
+int t2w_cache_get(const t2w_slots* p, int32_t handle, t2w_cache_info* info) {
+  if (!p || !info) return T2W_ERR_INVALID;
+  t2w_slots* q = const_cast<t2w_slots*>(p);
+  std::lock_guard<std::mutex> lock(q->mu);
+  const CacheRecord* r = q->reg.find(handle);
+  if (!r) return T2W_ERR_INVALID;
+  info->length = (int32_t)r->keys[0].size();
+  info->keep = r->keep;
+  info->rowslot[0] = r->rowslot[0];
+  info->rowslot[1] = r->rowslot[1];
+  return T2W_OK;
+}
+
+int t2w_cache_set_keep(t2w_slots* p, int32_t handle, int32_t keep) {
+  if (!p) return T2W_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(p->mu);
+  CacheRecord* r = p->reg.find(handle);
+  if (!r) return T2W_ERR_INVALID;
+  r->keep = keep;
+  return T2W_OK;
+}
+
+int t2w_cache_keys(const t2w_slots* p, int32_t handle, int32_t half, int32_t* slots, int32_t cap) {
+  if (!p || (half != 0 && half != 1) || cap < 0 || (cap > 0 && !slots)) return T2W_ERR_INVALID;
+  t2w_slots* q = const_cast<t2w_slots*>(p);
+  std::lock_guard<std::mutex> lock(q->mu);
+  const CacheRecord* r = q->reg.find(handle);
+  if (!r || (size_t)cap < r->keys[half].size()) return T2W_ERR_INVALID;
+  std::copy(r->keys[half].begin(), r->keys[half].end(), slots);
+  return T2W_OK;
+}
+
+int t2w_cache_reserve(t2w_slots* p, int32_t handle, int32_t n, int32_t* slots) {
+  if (!p || n < 0 || (n > 0 && !slots)) return T2W_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(p->mu);
+  CacheRecord* r = p->reg.find(handle);
+  if (!r || !r->keys[0].empty() || !r->keys[1].empty()) return T2W_ERR_INVALID;
+  if (n == 0) return T2W_OK;
+  if (!p->reg.slots.take(2 * n, slots)) return T2W_ERR_EXHAUSTED;
+  r->keys[0].assign(slots, slots + n);
+  r->keys[1].assign(slots + n, slots + 2 * n);
+  return T2W_OK;
+}
+
+int t2w_slots_usage(const t2w_slots* p, int32_t* keys_in_use, int32_t* rowslots_free, int32_t* caches) {
+  if (!p) return T2W_ERR_INVALID;
+  t2w_slots* q = const_cast<t2w_slots*>(p);
+  std::lock_guard<std::mutex> lock(q->mu);
+  if (keys_in_use) *keys_in_use = q->reg.slots.used();
+  if (rowslots_free) *rowslots_free = q->reg.rows.available();
+  if (caches) *caches = q->reg.live();
+  return T2W_OK;
+}
+
+size_t t2w_cached_workspace_bytes(const t2w_solver* s, const t2w_slots* p, const t2w_cached_batch* b) {
+  if (!s || !p || !b) return 0;
+  t2w_slots* q = const_cast<t2w_slots*>(p);
+  std::lock_guard<std::mutex> lock(q->mu);
+  std::vector<CacheRecord*> recs;
+  long long need = 0;
+  if (cached_records(q, b, recs, &need) != T2W_OK) return 0;
+  std::vector<int32_t> fresh((size_t)need, 0);  // sizes only: slot 0 stands in for every new slot
+  Plan pl;
+  if (!plan_cached(s->cfg, q, b->n_streams, b->chunk_len, b->keep, recs, fresh, pl)) return 0;
+  return layout(s->cfg, pl, false).total;
+}
+
+int t2w_solve_cached(t2w_solver* s, t2w_slots* p, const t2w_cached_batch* b, void* ws, size_t ws_bytes, uint32_t flags,
+                     void* stream) {
+  if (!s || !p || !b || !ws || !b->noise || !b->mu || !b->spk || !b->out) return T2W_ERR_INVALID;
+  if (s->precision != T2W_PREC_BF16) return T2W_ERR_UNSUPPORTED;
+  if (p->device != s->device) return T2W_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return T2W_ERR_INVALID;
+  T2W_ON_DEVICE(s->device);
+  std::lock_guard<std::mutex> lock(p->mu);
+  std::vector<CacheRecord*> recs;
+  long long need = 0;
+  T2W_TRY(cached_records(p, b, recs, &need));
+  if (need > p->reg.slots.available()) return T2W_ERR_EXHAUSTED;
+  std::vector<int32_t> fresh((size_t)need);
+  p->reg.slots.take((int)need, fresh.data());
+  auto undo = [&](int rc) {
+    p->reg.slots.give(fresh.data(), fresh.size());
+    return rc;
+  };
+  const int n = b->n_streams;
+  Plan pl;
+  if (!plan_cached(s->cfg, p, n, b->chunk_len, b->keep, recs, fresh, pl)) return undo(T2W_ERR_INVALID);
+  const WsLayout L = layout(s->cfg, pl, false);
+  if (L.total > ws_bytes) return undo(T2W_ERR_WORKSPACE);
+  t2w_batch pb{};
+  pb.n_streams = n;
+  pb.x0 = at<float>(ws, L.x0g);
+  pb.mu = b->mu;
+  pb.cond = b->cond;
+  pb.spk = b->spk;
+  pb.out = b->out;
+  NoiseSrc ns;
+  ns.noise = b->noise;
+  ns.frames = b->noise_frames;
+  ns.temperature = b->temperature;
+  const int rc = run_slot_plan(s, p, pl, pb, ws, flags, static_cast<cudaStream_t>(stream), &ns);
+  if (rc) return undo(rc);
+  // the reference's order and trim (dit_fast.py:480-490); final flushes hand their window's slots straight back
+  size_t fo = 0;
+  for (int h = 0; h < 2; ++h)
+    for (int i = 0; i < n; ++i) {
+      const int T = b->chunk_len[i];
+      if (b->keep[i])
+        p->reg.commit_window(*recs[i], h, fresh.data() + fo, T);
+      else
+        p->reg.slots.give(fresh.data() + fo, (size_t)T);
+      fo += (size_t)T;
+    }
   return T2W_OK;
 }
 

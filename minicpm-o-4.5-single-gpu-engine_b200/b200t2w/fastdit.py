@@ -21,6 +21,7 @@ import ctypes
 import torch
 
 from . import lib as L
+from . import ops as O
 from .solver import B200Solver
 
 TRIM_SUFFIX = 100  # keys kept after the first ``keep`` (the library applies the trim)
@@ -119,10 +120,9 @@ class B200FastDiT:
         self.noise = noise.detach().to(self.device, torch.float32).contiguous()
         self._lib = L.load()
         n_rs = 2 * max_streams + 1  # + one scratch row slot: the write target of rows that keep nothing
-        h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
-            L.call("t2w_slots_create", solver._h, n_slots, n_rs, ctypes.byref(h))
-        self._p = h
+            self._pid = int(O.call("slots_create", solver._hid, n_slots, n_rs))
+        self._p = ctypes.c_void_p(self._pid)
         self.pool = _PoolUsage(self)
         self.cnn_free = _FreeRowSlots(self)
         self._ws = None
@@ -161,7 +161,7 @@ class B200FastDiT:
 
     def close(self) -> None:
         if getattr(self, "_p", None) is not None and self._p.value:
-            self._lib.t2w_slots_destroy(self._p)
+            O.call("slots_destroy", self._pid)
             self._p = None
 
     def __del__(self):
@@ -330,25 +330,23 @@ class B200FastDiT:
                         [c.t() if c is not None else torch.zeros(t, mel, device=mu[i].device) for i, (c, t)
                          in enumerate(zip(cond, Ts))])
         self._stage(key, "spk", bufs["spk"], [spks.reshape(n, mel)])
-        P = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
-        handles = L.i32_array([c.handle for c in caches])
-        tl = L.i32_array(Ts)
-        kp = (ctypes.c_uint8 * n)(*[1 if k else 0 for k in keep])
-        b = L.CachedBatch(n, handles, tl, kp, P(self.noise), int(self.noise.shape[1]), float(temperature), P(bufs["mu"]),
-                          P(bufs["cond"]), P(bufs["spk"]), P(bufs["out"]))
+        handles = [c.handle for c in caches]
+        kp = [1 if k else 0 for k in keep]
         before = self.solver.counts()["graph"]
-        flags = L.FLAG_GRAPH if self.use_graphs else 0
-        for _ in range(2):
-            ws = self._ws if self._ws is not None else torch.empty(256, dtype=torch.uint8, device=dev)
-            rc = self._lib.t2w_solve_cached(self.solver._h, self._p, ctypes.byref(b), P(ws), ws.numel(), flags,
-                                            self._stream())
-            if rc != _WORKSPACE_TOO_SMALL:
-                break
-            need = int(self._lib.t2w_cached_workspace_bytes(self.solver._h, self._p, ctypes.byref(b)))
+        if self._ws is None:
+            self._ws = torch.empty(256, dtype=torch.uint8, device=dev)
+        args = (self.solver._hid, self._pid, handles, Ts, kp, self.noise, float(temperature), bufs["mu"], bufs["cond"],
+                bufs["spk"], bufs["out"])
+        try:
+            O.call("solve_cached", *args, self._ws, bool(self.use_graphs))
+        except L.T2WError as e:
+            if e.status != _WORKSPACE_TOO_SMALL:
+                raise
+            need = int(O.call("cached_workspace_bytes", *args[:6]))
             if not need:
-                raise L.T2WError("t2w_cached_workspace_bytes", -1)
+                raise L.T2WError("t2w_cached_workspace_bytes", -1) from e
             self._ws = torch.empty(need + need // 4, dtype=torch.uint8, device=dev)
-        L.check("t2w_solve_cached", rc)
+            O.call("solve_cached", *args, self._ws, bool(self.use_graphs))
         self.counts["graph" if self.solver.counts()["graph"] > before else "eager"] += 1
         out = bufs["out"].clone()  # the static buffer is rewritten by the next call
         res, o = [], 0

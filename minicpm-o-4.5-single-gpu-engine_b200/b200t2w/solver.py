@@ -15,6 +15,7 @@ from dataclasses import dataclass
 import torch
 
 from . import lib as L
+from . import ops as O
 from .config import DiTConfig, t_schedule
 
 
@@ -71,23 +72,19 @@ class B200Solver:
             raise KeyError(f"weights missing {len(missing)} entries, e.g. {missing[:3]}")
         with torch.cuda.device(self.device):
             dev_w = [weights[n].detach().to(self.device, torch.float32).contiguous() for n in names]
-            ptrs = (ctypes.c_void_p * len(dev_w))(*[t.data_ptr() for t in dev_w])
             ts, dts = t_schedule(cfg.steps)
-            sched = (ctypes.c_float * (2 * cfg.steps))(*[v for pair in zip(ts, dts) for v in pair])
-            c = L.Config(cfg.mel, cfg.hidden, cfg.depth, cfg.heads, cfg.head_dim, cfg.ffn, cfg.steps, cfg.freq_dim,
-                         cfg.cfg_rate, cfg.t_scale, cfg.max_period, cfg.eps_block, cfg.eps_final, cfg.eps_qk, cfg.eps_conv)
-            h = ctypes.c_void_p()
-            stream = torch.cuda.current_stream(self.device).cuda_stream
-            L.call("t2w_create", ctypes.byref(c), sched, ptrs, len(dev_w), L.PREC[precision], ctypes.c_void_p(stream),
-                   ctypes.byref(h))
+            cfg_i = [cfg.mel, cfg.hidden, cfg.depth, cfg.heads, cfg.head_dim, cfg.ffn, cfg.steps, cfg.freq_dim]
+            cfg_f = [cfg.cfg_rate, cfg.t_scale, cfg.max_period, cfg.eps_block, cfg.eps_final, cfg.eps_qk, cfg.eps_conv]
+            hid = O.call("create", cfg_i, cfg_f, [v for pair in zip(ts, dts) for v in pair], dev_w, L.PREC[precision])
             del dev_w
-        self._h = h
+        self._hid = int(hid)  # the solver handle as the torch ops take it
+        self._h = ctypes.c_void_p(self._hid)  # and as the ctypes binding takes it
         self._ws: dict = {}
         self._bufs: dict = {}
 
     def close(self) -> None:
         if getattr(self, "_h", None) is not None and self._h.value:
-            self._lib.t2w_destroy(self._h)
+            O.call("destroy", self._hid)
             self._h = None
 
     def __del__(self):
@@ -118,7 +115,7 @@ class B200Solver:
 
     # ------------------------------------------------------------------------------------------------ packed solve
     def workspace_bytes(self, layout: Layout) -> int:
-        n = self._lib.t2w_workspace_bytes(self._h, layout.n_streams, L.i32_array(layout.prompt), L.i32_array(layout.chunk))
+        n = O.call("workspace_bytes", self._hid, list(layout.prompt), list(layout.chunk))
         if not n:
             raise L.T2WError("t2w_workspace_bytes", -1)
         return int(n)
@@ -145,11 +142,10 @@ class B200Solver:
                 raise ValueError(f"{name}: expected contiguous fp32 {shape} on {self.device}, got {tuple(t.shape)} "
                                  f"{t.dtype} on {t.device}")
         ws = workspace if workspace is not None else self.workspace(layout, key=(layout.prompt, layout.chunk))
-        P, T = L.i32_array(layout.prompt), L.i32_array(layout.chunk)
-        b = L.Batch(layout.n_streams, P, T, x0.data_ptr(), mu.data_ptr(), cond.data_ptr(), spk.data_ptr(), out.data_ptr())
         st = stream if stream is not None else torch.cuda.current_stream(self.device)
-        L.call("t2w_solve_packed", self._h, ctypes.byref(b), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
-               ctypes.c_uint32(L.FLAG_GRAPH if graph else 0), ctypes.c_void_p(st.cuda_stream))
+        with torch.cuda.stream(st):  # the op enqueues on the current stream of the tensors' device
+            O.call("solve_packed", self._hid, list(layout.prompt), list(layout.chunk), x0, mu, cond, spk, out, ws,
+                   bool(graph))
         return out
 
     def profile(self, layout: Layout, bufs: dict | None = None) -> dict:

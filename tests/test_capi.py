@@ -63,3 +63,28 @@ def test_varlen_attention_rejects_overflowing_rows_without_a_gpu():
         rc = getattr(L.load(), fn)(ctypes.c_void_p(16), 1000, 1, 1, L.i32_array([2**31 - 10]), L.i32_array([100]),
                                    L.i32_array([100]), ctypes.c_void_p(16), None)
         assert rc == -1, (fn, rc)
+
+
+def test_torch_ops_are_registered():
+    """The torch custom-op shim builds, loads without a GPU, and registers every op over the C ABI."""
+    from b200t2w import ops
+    from b200t2w.build import build_ops
+
+    ns = ops.load(build_ops())
+    for name in ops.OPS:
+        assert hasattr(ns, name), name
+    schema = str(ns.solve_packed.default._schema)
+    assert schema.startswith("b200t2w::solve_packed(int solver, int[] prompt_len, int[] chunk_len"), schema
+    assert "Tensor(a!) out" in schema
+
+
+def test_torch_op_error_is_a_t2w_error_without_a_gpu():
+    """A failing op's status crosses torch's dispatcher as an exception (the shim shares torch's C++ runtime) and
+    comes back as ``T2WError``: destroying a null solver is refused before any CUDA call."""
+    import pytest
+
+    from b200t2w import ops
+
+    with pytest.raises(L.T2WError) as e:
+        ops.call("destroy", 0)
+    assert e.value.status == -1

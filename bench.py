@@ -1,24 +1,33 @@
 #!/usr/bin/env python
 """Benchmark of the Token2Wav DiT/CFM flow-matching solve on B200 (BASELINE.json metric: chunk mel frames/s per full
-CFG ODE solve, with p50 / p95 per-chunk latency).
+CFG ODE solve at 1/2/4/8 GPUs, with p50 / p95 per-chunk latency).
 
-One "step" is one full S-step CFG Euler solve (one CUDA-graph replay) over one batch of packed ``[prompt | chunk]``
-streams.  Default workload (N = 1): benchmark config 2, 16 streams of a 300-frame prompt + 50-frame chunk, bf16,
-random-init reference-config weights, seeded synthetic inputs.  With ``--gpus N`` (launched by torchrun) every rank is
-an independent replica with its own 16 streams (weak scaling; streams never cross GPUs, so there is no collective on the
-data path, only a gloo barrier and a max over ranks of the device-timed region).
+Default workload: benchmark config 5 — 1024 independent streams, each a 300-frame prompt + 50-frame chunk (seed 3),
+sharded by stream across the N ranks by the product's own scheduler (``b200t2w.scheduler.shard_streams``, contiguous),
+one process per GPU, no collective on the data path (only a gloo barrier and a max over ranks of the device-timed
+region).  Total work is fixed as N grows: strong scaling.  Each rank solves its shard in batches of ``--batch`` streams
+(64: the north star's target shape, 64 x (300 + 50), bf16), one CUDA-graph-replayed full 10-step CFG solve per batch,
+back to back.  One "step" = the whole job: every stream's chunk solved once.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|target|c5|c3|c4] [--impl b200|reference]
+    value          = 1024 x 50 chunk mel frames / (max over ranks of the step's device time)
+    latency_ms     = per-chunk latency: a chunk's solve ends with its batch, so each chunk's latency is the time from
+                     the step's start to its batch's end; p50 / p95 over all chunks of all timed steps and ranks
+    e2e            = the same job through the public API (``B200Solver.solve_streams`` on per-stream host tensors:
+                     host -> device copies of every input and a device -> host read of every chunk mel inside the
+                     timed region)
+    roofline       = the bf16 GEMMs of one batch solve (FLOPs from the path's formula / their event-timed time in an
+                     eager profiling solve) against MEASURED_PEAKS.json bf16_tflops_sustained
+    subrecords     = (N = 1, rank 0) config 2, config 3, config 4 (FP8), the steady-state form at 32 and 64 windows,
+                     each with its own ms, frames/s and GEMM fraction
+    reference_gpu  = (N = 1) the reference's own GPU PyTorch path on this GPU (``BatchedToken2Wav._solve``, fp16,
+                     run by ``bench.py --impl reference --reference-gpu`` in a child process), with the speed-up of this
+                     build at the target shape and at config 2
 
-``--workload steady`` times the steady-state form (the reference's ``FastDiT.solve``): 64 streams with 300-frame
-prompts already set up, one 50-frame window per stream per call against the slot-pool caches (trimmed to the prompt
-plus the last 100 keys, as the reference trims them); a step is one such call, timed through the public API.
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5|c2|target|c3|c4|steady] [--impl b200|reference]
 
-``--workload c4`` is benchmark config 4: config 2's shapes at 128 streams on the FP8 path (e4m3 block projections with
-power-of-two block scales; bf16 in_proj, attention and final layer).
-
-``--impl reference`` times the reference's own algorithm on the host cores (the CPU oracle port of the reference
-solver, all threads), one stream of the workload per step, on rank 0 only.
+``--impl reference`` times the reference's algorithm on the host cores (the fp32 CPU oracle port of the reference
+solver on all threads), one stream of the workload per step, on rank 0 only.  ``--impl reference --reference-gpu``
+prints the reference GPU path's timings instead (used by the default arm).
 """
 
 from __future__ import annotations
@@ -41,7 +50,7 @@ for p in (ROOT, PKG):
 import torch  # noqa: E402
 
 from b200t2w.config import REFERENCE, DiTConfig  # noqa: E402
-from b200t2w.workload import C2, C3, C4, C5, TARGET, Workload, make_streams, uniform_streams  # noqa: E402
+from b200t2w.workload import C2, C3, C4, C5, TARGET, Workload, make_streams  # noqa: E402
 
 METRIC = "DiT mel frames/s per full CFG ODE solve"
 UNIT = "mel frames/s"
@@ -51,27 +60,34 @@ L2_FLUSH_BYTES = 256 << 20
 def args_():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "target", "c5", "c3", "c4", "steady"])
+    ap.add_argument("--workload", default="c5", choices=["c5", "c2", "target", "c3", "c4", "steady"])
+    ap.add_argument("--batch", type=int, default=64, help="streams per solve on a rank (c5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true")
+    ap.add_argument("--reference-gpu", action="store_true",
+                    help="with --impl reference: time the reference's GPU PyTorch path and print its record")
+    ap.add_argument("--reference-fastdit", action="store_true",
+                    help="with --reference-gpu: also time the reference's FastDiT (FlashInfer + Triton + cuBLAS)")
     ap.add_argument("--timeline", action="store_true",
                     help="also record one graph-replayed solve with torch.profiler (CUPTI) and report each kernel "
                          "position's share of the solve's span (the time by which it extends the critical path)")
     return ap.parse_args()
 
 
-def shard(name: str, rank: int, world: int) -> Workload:
-    """This rank's streams.  c2 / target: a fixed per-GPU batch (weak scaling); c5: 1024 streams split by rank."""
+def rank_streams(name: str, rank: int, world: int) -> tuple[Workload, list]:
+    """This rank's workload and stream indices.  c5: the 1024 streams split by the product's scheduler (contiguous
+    blocks, strong scaling); the fixed-size configs: every rank runs the whole config (replicas, weak scaling)."""
+    from b200t2w.scheduler import shard_streams
+
     if name == "c5":
-        n = C5.streams // world
-        return Workload(f"{C5.name}[rank {rank}/{world}]", C5.seed, C5.lengths[rank * n:(rank + 1) * n])
-    base = {"c2": C2, "target": TARGET, "c3": C3, "c4": C4, "steady": C2}[name]
-    if world == 1:
-        return base
-    return Workload(f"{base.name}[rank {rank}]", base.seed + 1000 * rank, base.lengths)
+        return C5, shard_streams(list(C5.lengths), world, contiguous=True)[rank]
+    wl = {"c2": C2, "target": TARGET, "c3": C3, "c4": C4, "steady": C2}[name]
+    return wl, list(range(wl.streams))
 
 
 def timeline_from_events(evs: list) -> dict:
@@ -207,9 +223,11 @@ def cpu_oracle_time(cfg: DiTConfig, streams: list, reps: int, warm: int) -> tupl
 
 
 def reference_arm(a, rank: int, world: int) -> None:
+    """The reference's solver algorithm on the host cores (the fp32 CPU oracle port), one stream of the workload per
+    step, rank 0 only; the other ranks exit without work."""
     if rank != 0:
         return
-    wl = shard(a.workload, 0, 1)
+    wl, _ = rank_streams(a.workload, 0, 1)
     streams = make_streams(wl, count=min(4, wl.streams))
     ts, threads = cpu_oracle_time(REFERENCE, streams, a.steps, a.warmup)
     T = [streams[i % len(streams)]["T"] for i in range(a.steps)]
@@ -217,25 +235,160 @@ def reference_arm(a, rank: int, world: int) -> None:
     sample = f"1 stream of {wl.name} (P={streams[0]['P']}, T={streams[0]['T']}) per step, fp32 CPU oracle port"
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": 1000 * statistics.mean(ts), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "warmup": a.warmup, "ms_per_step": 1000 * statistics.mean(ts), "higher_is_better": True,
+        "scaling": "strong" if a.workload == "c5" else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
         "config": {"workload": wl.name, "streams_per_step": 1, "model": "reference-config DiT (unverified), random init"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
-def steady_arm(a, rank: int, world: int) -> None:
-    """Steady-state windows through ``B200FastDiT`` (one process per GPU, each with its own 64 streams)."""
+def _reference_modules():
+    """The reference checkout installed in baseline/_ref (its engine package) plus the one symbol its solver imports
+    from the absent stepaudio2 package (``decoder_dit.modulate``), and the restated estimator modules it drives."""
+    import types
+
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "engine")):
+        raise RuntimeError("baseline/_ref is not installed")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from oracle import dit_oracle
+
+    names = ["stepaudio2", "stepaudio2.cosyvoice2", "stepaudio2.cosyvoice2.flow", "stepaudio2.cosyvoice2.flow.decoder_dit"]
+    for n in names:
+        sys.modules.setdefault(n, types.ModuleType(n))
+    sys.modules["stepaudio2.cosyvoice2.flow.decoder_dit"].modulate = dit_oracle.modulate
+    return dit_oracle
+
+
+def reference_gpu_eager(wl: Workload, steps: int, warm: int, dev) -> dict:
+    """The reference's own GPU PyTorch path, ``BatchedToken2Wav._solve`` (engine/runtime/token2wav_batch.py:632-702),
+    unmodified, on this GPU in fp16 (the reference's FP16 flow): the prompt setup of every stream (prompt mel as the
+    condition, empty caches) then its chunk against the caches it left, over the whole batch at once — the two-stage
+    form of one full 10-step CFG solve of a chunk with its prompt.  Event-timed per two-stage solve."""
+    from types import SimpleNamespace
+
+    dit_oracle = _reference_modules()
+    from engine.models.token2wav import StreamState
+    from engine.runtime.token2wav_batch import BatchedToken2Wav
+
+    cfg = REFERENCE
+    P, T = wl.lengths[0]
+    assert all(x == (P, T) for x in wl.lengths)
+    n = wl.streams
+    model = dit_oracle.build_model(cfg, seed=0, noise_frames=P + T + 8).to(dev).half()
+    bt = BatchedToken2Wav.__new__(BatchedToken2Wav)
+    bt.flow = SimpleNamespace(decoder=model)
+    bt.t2w = SimpleNamespace(n_timesteps=cfg.steps)
+    bt.graphs = bt.euler = None
+    ss = make_streams(wl, cfg.mel)
+    h = lambda k, a, b: torch.stack([s[k][:, a:b] for s in ss]).to(dev, torch.float16).contiguous()  # noqa: E731
+    mu_p, mu_c, cond_p = h("mu", 0, P), h("mu", P, P + T), h("cond", 0, P)
+    spk = torch.stack([s["spk"] for s in ss]).to(dev, torch.float16)
+
+    def solve():
+        sts = [StreamState(prompt=None, hift_cache={}, flow_cache={
+            "estimator_cnn_cache": torch.zeros(cfg.steps, cfg.depth, 2, 2 * cfg.hidden, 2, device=dev, dtype=torch.float16),
+            "estimator_att_cache": torch.zeros(cfg.steps, cfg.depth, 2, cfg.heads, 0, 2 * cfg.head_dim, device=dev,
+                                               dtype=torch.float16)}) for _ in range(n)]
+        bt._solve(sts, mu_p, spk, cond=cond_p, keep_cache=True)
+        return bt._solve(sts, mu_c, spk, cond=None, keep_cache=True)
+
+    st = torch.cuda.current_stream(dev)
+    with torch.inference_mode():
+        for _ in range(warm):
+            solve()
+        torch.cuda.synchronize(dev)
+        ms = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            solve()
+            e1.record(st)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+    m = statistics.median(ms)
+    return {"path": "BatchedToken2Wav._solve (engine/runtime/token2wav_batch.py:632-702), eager, fp16, two-stage "
+                    "(prompt setup then chunk)", "workload": wl.name, "streams": n, "ms_per_solve": m,
+            "chunk_frames_per_s": n * T / (m / 1000), "timed_solves": steps}
+
+
+def reference_gpu_fastdit(wl: Workload, steps: int, warm: int, dev) -> dict:
+    """The reference's production form, ``FastDiT.solve`` (engine/runtime/dit_fast.py:432-495: FlashInfer paged
+    prefill, Triton norm kernels, cuBLAS linears, CUDA graphs per row bucket), fp16: every stream's prompt setup then
+    its chunk window, timed as one two-stage solve, and the chunk window alone (the steady-state call)."""
+    dit_oracle = _reference_modules()
+    from engine.runtime.dit_fast import FastDiT
+
+    cfg = REFERENCE
+    P, T = wl.lengths[0]
+    n = wl.streams
+    model = dit_oracle.build_model(cfg, seed=0, noise_frames=P + T + 8).to(dev).half()
+    fd = FastDiT(model, cfg.steps, n_slots=2 * n * (P + T + 8), max_streams=max(96, n), device=dev, use_graphs=True,
+                 fused_residual=True, fused_conv=True)
+    ss = make_streams(wl, cfg.mel)
+    mu_p = [s["mu"][:, :P].to(dev, torch.float16) for s in ss]
+    mu_c = [s["mu"][:, P:].to(dev, torch.float16) for s in ss]
+    cond_p = [s["cond"][:, :P].to(dev, torch.float16) for s in ss]
+    spk = torch.stack([s["spk"] for s in ss]).to(dev, torch.float16)
+    st = torch.cuda.current_stream(dev)
+    two, win = [], []
+    with torch.inference_mode():
+        for i in range(warm + steps):
+            caches = [fd.new_cache() for _ in range(n)]
+            for c in caches:
+                c.keep = P
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(st)
+            fd.solve(caches, mu_p, spk, cond_p, [True] * n)
+            e1.record(st)
+            fd.solve(caches, mu_c, spk, None, [True] * n)
+            e2.record(st)
+            e2.synchronize()
+            if i >= warm:
+                two.append(e0.elapsed_time(e2))
+                win.append(e1.elapsed_time(e2))
+            for c in caches:
+                fd.release(c)
+    m, mw = statistics.median(two), statistics.median(win)
+    return {"path": "FastDiT.solve (engine/runtime/dit_fast.py:432-495), FlashInfer + Triton + cuBLAS, fp16, graphs",
+            "workload": wl.name, "streams": n, "ms_per_solve": m, "chunk_frames_per_s": n * T / (m / 1000),
+            "window_ms": mw, "window_frames_per_s": n * T / (mw / 1000), "timed_solves": steps,
+            "graph_calls": dict(fd.counts)}
+
+
+def reference_gpu_arm(a) -> None:
+    """``--impl reference --reference-gpu``: one JSON record of the reference's GPU PyTorch path at the target shape
+    and at config 2 (a child process of the default arm; nothing of this build's library is loaded here)."""
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    rec = {"impl": "reference_gpu", "gpu": torch.cuda.get_device_name(dev)}
+    for name, wl in (("target", TARGET), ("c2", C2)):
+        try:
+            rec[name] = reference_gpu_eager(wl, steps=3, warm=1, dev=dev)
+        except Exception as e:  # reported, not raised: the default arm's own numbers stand without it
+            rec[name] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+        if a.reference_fastdit:
+            try:
+                rec[name + "_fastdit"] = reference_gpu_fastdit(wl, steps=3, warm=2, dev=dev)
+            except Exception as e:
+                rec[name + "_fastdit"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    print(json.dumps(rec), flush=True)
+
+
+def steady_record(cfg: DiTConfig, dev, n: int, steps: int, warmup: int, seed: int, timeline_on: bool = False) -> dict:
+    """Steady-state windows through ``B200FastDiT`` (the reference's ``FastDiT.solve`` form): ``n`` streams with
+    300-frame prompts set up, then one 50-frame window per stream per call against the slot-pool caches (trimmed to the
+    prompt plus the last 100 keys).  Window inputs sit in pinned host memory and each call's mel is read back to pinned
+    host memory, inside the timed region.  Throughput: calls back to back (a call's host work overlaps the previous
+    call's GPU work); latency: one call at a time."""
     from b200t2w.fastdit import B200FastDiT
     from b200t2w.solver import B200Solver
     from b200t2w.weights import random_state_dict
 
-    cfg = REFERENCE
-    local = int(os.environ.get("LOCAL_RANK", 0))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    n, P, T = 64, 300, 50
-    g = torch.Generator().manual_seed(11 + rank)
+    P, T = 300, 50
+    g = torch.Generator().manual_seed(seed)
     noise = torch.randn(cfg.mel, 8192, generator=g)
     solver = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), device=dev)
     fd = B200FastDiT(solver, noise, n_slots=2 * n * (P + 100 + T + 8), max_streams=n)
@@ -247,7 +400,6 @@ def steady_arm(a, rank: int, world: int) -> None:
         cs = caches[i0:i0 + 16]
         fd.solve(cs, [torch.randn(cfg.mel, P, generator=g) for _ in cs], spk[i0:i0 + 16],
                  [torch.randn(cfg.mel, P, generator=g) for _ in cs], [True] * len(cs))
-    # window inputs in pinned host memory (copied in by each call), each call's mel read back to pinned host memory
     mus = [[torch.randn(cfg.mel, T, generator=g).pin_memory() for _ in range(n)] for _ in range(4)]
     spk_d = spk.to(dev)
     host_out = torch.empty(n, cfg.mel, T).pin_memory()
@@ -258,22 +410,19 @@ def steady_arm(a, rank: int, world: int) -> None:
 
     # caches reach the trimmed steady length (P + 100) after three windows; the steady structure's CUDA graph is
     # captured on its second call, so two more warm-up windows keep the capture out of the timed region
-    for k in range(max(a.warmup, 3) + 2):
+    for k in range(max(warmup, 3) + 2):
         step(k)
     torch.cuda.synchronize(dev)
     st = torch.cuda.current_stream(dev)
-    # throughput: calls back to back, as a serving loop issues them (a call's host planning overlaps the previous
-    # call's GPU work); one event pair around the K calls
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for k in range(a.steps):
+    for k in range(steps):
         step(k)
     e1.record(st)
     e1.synchronize()
-    times = [e0.elapsed_time(e1) / a.steps] * a.steps
-    # latency: one call at a time, host planning inside
+    ms = e0.elapsed_time(e1) / steps
     lat = []
-    for k in range(min(a.steps, 5)):
+    for k in range(min(steps, 5)):
         l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0.record(st)
         step(k)
@@ -281,52 +430,82 @@ def steady_arm(a, rank: int, world: int) -> None:
         l1.synchronize()
         lat.append(l0.elapsed_time(l1))
     solver.check()
-    tl = timeline(lambda: step(0)) if a.timeline and rank == 0 else None
-    frames = n * T
-    red = torch.tensor([sum(times)], dtype=torch.float64)
-    if world > 1:
-        torch.distributed.all_reduce(red, op=torch.distributed.ReduceOp.MAX)
-    value = world * frames * a.steps / (float(red[0]) / 1000)
-    # per stream per window: S [2T (Dp 36 H^2 + 800 H) + Dp 4H 2T (keys)], keys = cache (P + 100) + T
+    tl = timeline(lambda: step(0)) if timeline_on else None
     keys = caches[0].length
+    # per stream per window: S [2T (Dp 36 H^2 + 800 H) + Dp 4H 2T (keys)], keys = cache (P + 100) + T
     flop = n * cfg.steps * (2 * T * (cfg.depth * 2 * cfg.hidden * (10 * cfg.hidden + 2 * cfg.ffn) + 800 * cfg.hidden)
                             + cfg.depth * 4 * cfg.hidden * 2 * T * keys)
-    if rank == 0:
-        print(json.dumps({
-            "metric": "DiT mel frames/s, steady-state windows (slot-pool solve)", "value": value, "unit": UNIT,
-            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": statistics.mean(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"steady_{n}x{T} (P={P} cached, keys per row {keys})", "streams_per_gpu": n,
-                       "window_frames": T, "prompt_frames": P, "model": "reference-config DiT (unverified), random init",
-                       "timing": "CUDA events around K back-to-back public-API calls (host planning, the pinned "
-                                 "host -> device input copies and the device -> host mel read-back inside)",
-                       "solve_calls": dict(fd.counts)},
-            "latency_ms": {"p50": statistics.median(lat)}, "tflops": flop / (statistics.mean(times) / 1000) / 1e12,
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": n * T * cfg.mel * 4,
-                    "d2h_bytes_per_step": n * T * cfg.mel * 4}, **({"timeline": tl} if tl else {})}), flush=True)
+    rec = {"workload": f"steady_{n}x{T} (P={P} cached, keys per row {keys})", "streams": n, "ms_per_call": ms,
+           "chunk_frames_per_s": n * T / (ms / 1000), "latency_ms_p50": statistics.median(lat),
+           "tflops": flop / (ms / 1000) / 1e12, "solve_calls": dict(fd.counts),
+           "h2d_bytes_per_call": n * T * cfg.mel * 4, "d2h_bytes_per_call": n * T * cfg.mel * 4}
+    if tl:
+        rec["timeline"] = tl
     fd.close()
     solver.close()
+    return rec
 
 
-def main() -> None:
-    a = args_()
-    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
-    local = int(os.environ.get("LOCAL_RANK", 0))
-    if world > 1:
-        import torch.distributed as dist
+def packed_record(solver, wl: Workload, steps: int, warm: int, flush: torch.Tensor, peak_tf: float) -> dict:
+    """One packed workload as a sub-record: device-resident inputs, ``steps`` graph-replayed solves with L2 flushed
+    between them (median event time), and the GEMM fraction from one eager profiling solve."""
+    from b200t2w.solver import Layout
 
-        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
-    if a.impl == "reference":
-        reference_arm(a, rank, world)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-    if a.workload == "steady":
-        steady_arm(a, rank, world)
-        if world > 1:
-            torch.distributed.barrier()
-            torch.distributed.destroy_process_group()
-        return
+    dev = solver.device
+    streams = make_streams(wl, solver.cfg.mel)
+    layout = Layout(tuple(x["P"] for x in streams), tuple(x["T"] for x in streams))
+    b = solver.static_buffers(layout)
+    for k in ("x0", "mu", "cond"):
+        b[k].copy_(torch.cat([x[k].t() for x in streams]))
+    b["spk"].copy_(torch.stack([x["spk"] for x in streams]))
+    st = torch.cuda.current_stream(dev)
+
+    def solve():
+        solver.solve_packed_dev(layout, b["x0"], b["mu"], b["cond"], b["spk"], b["out"], workspace=b["ws"])
+
+    for _ in range(warm):
+        solve()
+    ms = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        solve()
+        e1.record(st)
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    solver.check()
+    prof = solver.profile(layout, b)
+    gemm_flops, attn_flops = flops_per_solve(solver.cfg, list(zip(layout.prompt, layout.chunk)))
+    gemm_ms = sum(v for k, (v, _) in prof.items() if k.startswith("gemm"))
+    m = statistics.median(ms)
+    return {"workload": wl.name, "precision": solver.precision, "streams": wl.streams, "ms_per_solve": m,
+            "chunk_frames_per_s": wl.chunk_frames / (m / 1000), "gemm_tflops": gemm_flops / (gemm_ms / 1000) / 1e12,
+            "gemm_frac": gemm_flops / (gemm_ms / 1000) / 1e12 / peak_tf, "gemm_ms_per_solve": gemm_ms,
+            "attn_ms_per_solve": prof["attn"][0], "solve_tflops": (gemm_flops + attn_flops) / (m / 1000) / 1e12,
+            "launches_per_solve": sum(c for _, c in prof.values())}
+
+
+def reference_gpu_child(a) -> dict:
+    """Run ``bench.py --impl reference --reference-gpu`` as a child process (this process never loads the reference
+    or its restated modules) and return its record."""
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--reference-gpu"]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env={**os.environ, "WORLD_SIZE": "1",
+                                                                                  "RANK": "0"})
+        lines = [x for x in r.stdout.strip().splitlines() if x.startswith("{")]
+        if r.returncode or not lines:
+            return {"unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout)[-300:]}"}
+        return json.loads(lines[-1])
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "timed out after 900 s"}
+
+
+def packed_job(a, rank: int, world: int, local: int) -> None:
+    """The default arm: this rank's streams in batches of ``--batch`` (one graph-replayed solve each), timed as one
+    whole-job step; then the same job end to end through the public API; then (N = 1, rank 0) the sub-records, the
+    CPU baseline and the reference GPU path."""
+    import torch.distributed as dist
 
     from b200t2w.solver import B200Solver, Layout
     from b200t2w.weights import random_state_dict
@@ -334,129 +513,232 @@ def main() -> None:
     cfg = REFERENCE
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    wl = shard(a.workload, rank, world)
-    streams = make_streams(wl, cfg.mel)
-    layout = Layout(tuple(s["P"] for s in streams), tuple(s["T"] for s in streams))
+    wl, idx = rank_streams(a.workload, rank, world)
     fp8 = a.workload == "c4"
+    batch = a.batch if a.workload == "c5" else max(len(idx), 1)
+    streams = make_streams(wl, cfg.mel, first=idx[0], count=len(idx)) if idx else []
+    assert [x["index"] for x in streams] == idx
+    groups = [streams[i:i + batch] for i in range(0, len(streams), batch)]
     solver = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), precision="fp8" if fp8 else "bf16", device=dev)
-    bufs = solver.static_buffers(layout)
-    host = {k: torch.cat([s[k].t() for s in streams]).contiguous().pin_memory() for k in ("x0", "mu", "cond")}
-    host["spk"] = torch.stack([s["spk"] for s in streams]).contiguous().pin_memory()
-    host_out = torch.empty(layout.n_tok, cfg.mel, dtype=torch.float32).pin_memory()
-    for k in ("x0", "mu", "cond", "spk"):
-        bufs[k].copy_(host[k])
+    jobs = []
+    for g in groups:  # device-resident inputs: one buffer set (and graph) per batch
+        layout = Layout(tuple(x["P"] for x in g), tuple(x["T"] for x in g))
+        b = {k: torch.cat([x[k].t() for x in g]).to(dev).contiguous() for k in ("x0", "mu", "cond")}
+        b["spk"] = torch.stack([x["spk"] for x in g]).to(dev)
+        b["out"] = torch.empty_like(b["x0"])
+        b["ws"] = solver.workspace(layout, key=(layout.prompt, layout.chunk))
+        jobs.append((layout, b))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream(dev)
-
-    def solve():
-        solver.solve_packed_dev(layout, bufs["x0"], bufs["mu"], bufs["cond"], bufs["spk"], bufs["out"], workspace=bufs["ws"])
 
     def barrier():
         torch.cuda.synchronize(dev)
         if world > 1:
-            torch.distributed.barrier()
+            dist.barrier()
 
-    # ---- device-resident throughput (inputs already in HBM)
+    def step(evs=None):
+        for j, (layout, b) in enumerate(jobs):
+            solver.solve_packed_dev(layout, b["x0"], b["mu"], b["cond"], b["spk"], b["out"], workspace=b["ws"])
+            if evs is not None:
+                evs[j + 1].record(st)
+
+    # ---- device-resident throughput and per-chunk latency (inputs already in HBM)
     for _ in range(a.warmup):
-        solve()
+        step()
     barrier()
     clocks = Clocks(physical_index(local))
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
-    for e0, e1 in evs:
-        flush.fill_(1)  # L2 flush between timed solves (outside the timed interval)
-        e0.record(st)
-        solve()
-        e1.record(st)
+    recs = []
+    for _ in range(a.steps):
+        flush.fill_(1)  # L2 flush between timed steps (outside the timed interval)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(jobs) + 1)]
+        evs[0].record(st)
+        step(evs)
+        recs.append(evs)
     barrier()
     clk = clocks.stop()
     solver.check()
-    times = [e0.elapsed_time(e1) for e0, e1 in evs]  # ms
-    total_ms = sum(times)
+    step_ms = [e[0].elapsed_time(e[-1]) if len(e) > 1 else 0.0 for e in recs]
+    lat = [e[0].elapsed_time(e[j + 1]) for e in recs for j, g in enumerate(groups) for _ in g]  # one per chunk
+    batch_ms = [e[j].elapsed_time(e[j + 1]) for e in recs for j in range(len(jobs))]
 
-    # ---- end to end through the public API: pinned host inputs -> device -> solve -> host result
-    h2d = sum(host[k].numel() * 4 for k in ("x0", "mu", "cond", "spk"))
+    # ---- end to end through the public API: per-stream host tensors -> solve_streams -> chunk mels on the host
+    host_out = torch.empty(cfg.mel, sum(x["T"] for x in streams), dtype=torch.float32).pin_memory()
+    h2d = sum(4 * (3 * x["x0"].numel() + x["spk"].numel()) for x in streams)
     d2h = host_out.numel() * 4
-    e2e_t = []
-    for i in range(a.warmup + a.steps):
+    e2e_ms = []
+    for i in range(1 + a.steps):
         flush.fill_(1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        for k in ("x0", "mu", "cond", "spk"):
-            bufs[k].copy_(host[k], non_blocking=True)
-        solve()
-        host_out.copy_(bufs["out"], non_blocking=True)
+        o = 0
+        for g in groups:
+            outs = solver.solve_streams(g)
+            chunk = torch.cat([y[:, x["P"]:] for x, y in zip(g, outs)], dim=1)
+            host_out[:, o:o + chunk.shape[1]].copy_(chunk, non_blocking=True)
+            o += chunk.shape[1]
         e1.record(st)
         e1.synchronize()
-        if i >= a.warmup:
-            e2e_t.append(e0.elapsed_time(e1))
+        if i >= 1:
+            e2e_ms.append(e0.elapsed_time(e1))
     barrier()
 
-    # ---- max over ranks of the device-timed regions
-    red = torch.tensor([total_ms, sum(e2e_t)], dtype=torch.float64)
+    # ---- max over ranks of the device-timed regions; every chunk's latency to rank 0
+    red = torch.tensor([sum(step_ms), sum(e2e_ms)], dtype=torch.float64)
+    all_lat = [lat]
     if world > 1:
-        torch.distributed.all_reduce(red, op=torch.distributed.ReduceOp.MAX)
-    max_ms, max_e2e_ms = float(red[0]), float(red[1])
-    chunk_frames = wl.chunk_frames  # per rank per solve
-    value = world * chunk_frames * a.steps / (max_ms / 1000)
-    e2e_value = world * chunk_frames * a.steps / (max_e2e_ms / 1000)
+        dist.all_reduce(red, op=dist.ReduceOp.MAX)
+        all_lat = [None] * world
+        dist.all_gather_object(all_lat, lat)
+    max_ms, max_e2e = float(red[0]), float(red[1])
+    frames = sum(t for _, t in wl.lengths) if a.workload == "c5" else world * wl.chunk_frames
+    value = frames * a.steps / (max_ms / 1000)
+    e2e_value = frames * a.steps / (max_e2e / 1000)
 
-    prof = solver.profile(layout, bufs) if not a.no_profile else {}
-    tl = timeline(solve) if a.timeline and rank == 0 else None
-    gemm_flops, attn_flops = flops_per_solve(cfg, layout_pairs := list(zip(layout.prompt, layout.chunk)))
+    roofline = prof = None
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except OSError:
         pass
     peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
-    peak_src = "MEASURED_PEAKS.json bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "fallback"
+    peak_src = ("MEASURED_PEAKS.json bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks
+                else "fallback 1400 TFLOP/s")
     if fp8:  # no measured e4m3 peak: twice the measured bf16 figure (the dense e4m3 / bf16 ratio of the part)
-        peak_tf *= 2
-        peak_src = "2 x " + peak_src + " (no measured e4m3 peak)"
-    launches = sum(c for _, c in prof.values()) if prof else None
-    gemm_ms = sum(ms for k, (ms, _) in prof.items() if k.startswith("gemm")) if prof else None
-    roofline = None
-    if prof:
+        peak_tf, peak_src = 2 * peak_tf, "2 x " + peak_src + " (no measured e4m3 peak)"
+    if not a.no_profile and jobs:
+        layout, b = jobs[0]
+        prof = solver.profile(layout, b)
+        gemm_flops, attn_flops = flops_per_solve(cfg, list(zip(layout.prompt, layout.chunk)))
+        gemm_ms = sum(v for k, (v, _) in prof.items() if k.startswith("gemm"))
         achieved = gemm_flops / (gemm_ms / 1000) / 1e12
-        traffic = None
-        try:
-            traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json"))).get("gemm_bytes_per_solve")
-        except (OSError, ValueError):
-            pass
-        roofline = {"bound": "tensor", "kernel": "k_gemm (all tcgen05 GEMM launches of one solve)", "achieved": achieved,
-                    "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf, "peak_source": peak_src,
-                    "traffic": traffic, "gemm_ms_per_solve": gemm_ms, "gemm_tflop_per_solve": gemm_flops / 1e12,
-                    "solve_tflops": (gemm_flops + attn_flops) / (statistics.mean(times) / 1000) / 1e12,
-                    "kernel_ms_per_solve": {k: round(ms, 4) for k, (ms, _) in prof.items()}}
-    cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        sample = make_streams(wl, cfg.mel, count=1)
-        ts, threads = cpu_oracle_time(cfg, sample, reps=2, warm=0)
-        cpu = {"value": sample[0]["T"] / statistics.mean(ts), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"1 stream (P={sample[0]['P']}, T={sample[0]['T']}) of {wl.name}, fp32 CPU oracle, 2 solves"}
-    if rank == 0:
-        srt = sorted(times)
-        lat = {"p50": statistics.median(times), "p95": srt[min(len(srt) - 1, int(round(0.95 * (len(srt) - 1))))]}
-        print(json.dumps({
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": max_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3 (block projections) + bf16" if fp8 else "bf16", "data": "synthetic",
-            "config": {"workload": wl.name, "streams_per_gpu": wl.streams, "prompt_frames": layout.prompt[0],
-                       "chunk_frames": layout.chunk[0], "chunk_frames_per_solve_per_gpu": chunk_frames,
-                       "packed_frames_per_solve_per_gpu": 2 * wl.packed_frames, "mel": cfg.mel, "euler_steps": cfg.steps,
-                       "cfg": True, "model": "reference-config DiT (H=512, depth 16, 8x64 heads, unverified), random init",
-                       "precision": "fp8" if fp8 else "bf16",
-                       "l2": "flushed between timed solves (256 MiB write, untimed)",
-                       "parallelism": f"replicas x{world} (streams sharded by request, no collectives)"},
-            "latency_ms": lat, "processed_frames_per_s": value * 2 * wl.packed_frames / chunk_frames,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "latency_ms_p50": statistics.median(e2e_t)},
-            "gpu_launches": launches * a.steps if launches else None, "roofline": roofline, "cpu_baseline": cpu,
-            "clocks": clk, **({"timeline": tl} if tl else {})}), flush=True)
+        roofline = {"bound": "tensor", "kernel": "k_gemm (all tcgen05 GEMM launches of one batch solve)",
+                    "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                    "peak_source": peak_src, "traffic": None,
+                    "traffic_note": "not captured in this run: per-kernel DRAM bytes come from ncu (profiles/)",
+                    "units": f"one solve of {len(layout.prompt)} streams "
+                             f"({layout.prompt[0]} + {layout.chunk[0]} frames)",
+                    "gemm_tflop_per_solve": gemm_flops / 1e12, "gemm_ms_per_solve": gemm_ms,
+                    "solve_tflops": (gemm_flops + attn_flops) / (statistics.median(batch_ms) / 1000) / 1e12,
+                    "kernel_ms_per_solve": {k: round(v, 4) for k, (v, _) in prof.items()}}
+    tl = None
+    if a.timeline and rank == 0 and jobs:
+        layout, b = jobs[0]
+        tl = timeline(lambda: solver.solve_packed_dev(layout, b["x0"], b["mu"], b["cond"], b["spk"], b["out"],
+                                                      workspace=b["ws"]))
+    sub, cpu, ref_gpu = {}, None, None
+    if rank == 0 and world == 1:
+        if not a.no_subrecords:
+            if a.workload != "c2":
+                sub["c2"] = packed_record(solver, C2, 5, 2, flush, peak_tf)
+            sub["c3"] = packed_record(solver, C3, 3, 1, flush, peak_tf)
+            if a.workload == "c5":
+                sub["target"] = {"workload": TARGET.name, "streams": TARGET.streams,
+                                 "ms_per_solve": statistics.median(batch_ms),
+                                 "chunk_frames_per_s": TARGET.chunk_frames / (statistics.median(batch_ms) / 1000),
+                                 "gemm_frac": roofline["frac"] if roofline else None,
+                                 "note": "the c5 job's batches are the target shape (64 x (300 + 50))"}
+        if not a.no_cpu_baseline:
+            sample = make_streams(wl, cfg.mel, count=1)
+            ts, threads = cpu_oracle_time(cfg, sample, reps=2, warm=0)
+            cpu = {"value": sample[0]["T"] / statistics.mean(ts), "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"1 stream (P={sample[0]['P']}, T={sample[0]['T']}) of {wl.name}, fp32 CPU oracle, "
+                             "2 solves"}
+    launches = sum(c for _, c in prof.values()) * len(jobs) * a.steps if prof else None
+    solver_precision = solver.precision
     solver.close()
+    del jobs
+    if rank == 0 and world == 1 and not a.no_subrecords:
+        torch.cuda.empty_cache()
+        fp8s = B200Solver(cfg, random_state_dict(cfg, seed=0, device=dev), precision="fp8", device=dev)
+        sub["c4_fp8"] = packed_record(fp8s, C4, 3, 1, flush, 2 * peaks.get("bf16_tflops_sustained", 1400.0))
+        fp8s.close()
+        torch.cuda.empty_cache()
+        for n in (32, 64):
+            sub[f"steady_{n}"] = steady_record(cfg, dev, n, steps=10, warmup=3, seed=11)
+            torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not a.no_reference_gpu:
+        torch.cuda.empty_cache()
+        ref_gpu = reference_gpu_child(a)
+        ours = {"target": sub.get("target", {}).get("ms_per_solve"), "c2": (sub.get("c2") or {}).get("ms_per_solve")}
+        if a.workload == "c2":
+            ours["c2"] = statistics.median(batch_ms)
+        for k, v in ours.items():
+            r = (ref_gpu.get(k) or {}).get("ms_per_solve")
+            if v and r:
+                ref_gpu.setdefault("speedup", {})[k] = r / v
+            rf = (ref_gpu.get(k + "_fastdit") or {}).get("ms_per_solve")
+            if v and rf:
+                ref_gpu.setdefault("speedup_vs_fastdit", {})[k] = rf / v
+    if rank == 0:
+        flat = sorted(x for r in all_lat for x in r)
+        pct = lambda q: flat[min(len(flat) - 1, int(round(q * (len(flat) - 1))))] if flat else None  # noqa: E731
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": max_ms / a.steps, "higher_is_better": True,
+            "scaling": "strong" if a.workload == "c5" else "weak", "vs_baseline": None,
+            "dtype": "e4m3 (block projections) + bf16" if solver_precision == "fp8" else "bf16", "data": "synthetic",
+            "config": {"workload": wl.name, "streams_total": len(wl.lengths) if a.workload == "c5" else world * wl.streams,
+                       "streams_per_gpu": len(idx), "batch_streams": batch, "prompt_frames": wl.lengths[0][0],
+                       "chunk_frames": wl.lengths[0][1], "chunk_frames_per_step": frames, "mel": cfg.mel,
+                       "euler_steps": cfg.steps, "cfg": True,
+                       "model": "reference-config DiT (H=512, depth 16, 8x64 heads, unverified), random init",
+                       "precision": solver_precision,
+                       "sharding": "b200t2w.scheduler.shard_streams (contiguous), one process per GPU, no collectives"
+                       if a.workload == "c5" else f"replicas x{world}",
+                       "l2": "flushed between timed steps (256 MiB write, untimed); each step's inputs and working set "
+                             "exceed L2"},
+            "latency_ms": {"p50": pct(0.5), "p95": pct(0.95), "per": "chunk (its batch's end - the step's start)",
+                           "batch_solve_ms_p50": statistics.median(batch_ms)},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "B200Solver.solve_streams on per-stream host tensors, chunk mels read back to pinned host"},
+            "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk}
+        if sub:
+            line["subrecords"] = sub
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
+        if tl:
+            line["timeline"] = tl
+        print(json.dumps(line), flush=True)
     if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+        dist.barrier()
+
+
+def main() -> None:
+    a = args_()
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if a.impl == "reference" and a.reference_gpu:
+        reference_gpu_arm(a)
+        return
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    try:
+        if a.impl == "reference":
+            reference_arm(a, rank, world)
+        elif a.workload == "steady":
+            torch.cuda.set_device(local)
+            rec = steady_record(REFERENCE, torch.device("cuda", local), 64, a.steps, a.warmup, seed=11 + rank,
+                                timeline_on=a.timeline and rank == 0)
+            red = torch.tensor([rec["ms_per_call"]], dtype=torch.float64)
+            if world > 1:
+                torch.distributed.all_reduce(red, op=torch.distributed.ReduceOp.MAX)
+            if rank == 0:
+                value = world * rec["streams"] * 50 / (float(red[0]) / 1000)
+                print(json.dumps({
+                    "metric": "DiT mel frames/s, steady-state windows (slot-pool solve)", "value": value, "unit": UNIT,
+                    "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": float(red[0]),
+                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                    "data": "synthetic", "config": {"workload": rec["workload"], "streams_per_gpu": rec["streams"]},
+                    "latency_ms": {"p50": rec["latency_ms_p50"]}, "tflops": rec["tflops"],
+                    "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": rec["h2d_bytes_per_call"],
+                            "d2h_bytes_per_step": rec["d2h_bytes_per_call"]}, "steady": rec}), flush=True)
+        else:
+            packed_job(a, rank, world, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":

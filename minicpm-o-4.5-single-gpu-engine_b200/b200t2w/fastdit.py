@@ -23,6 +23,7 @@ import torch
 from . import lib as L
 from . import ops as O
 from .solver import B200Solver
+from .staging import HostStaging
 
 TRIM_SUFFIX = 100  # keys kept after the first ``keep`` (the library applies the trim)
 _WORKSPACE_TOO_SMALL = -6
@@ -73,27 +74,6 @@ class _FreeRowSlots:
 
     def __len__(self) -> int:
         return self._fd._usage()[1]
-
-
-class _HostStaging:
-    """Pinned host mirrors of one static input buffer: a window's host tensors are concatenated into a mirror and moved
-    by one asynchronous copy.  Two mirrors alternate; a mirror is rewritten once the copy that last read it is done."""
-
-    def __init__(self, like: torch.Tensor):
-        self.bufs = [torch.empty(like.shape, dtype=like.dtype).pin_memory() for _ in range(2)]
-        self.events = [None, None]
-        self.next = 0
-
-    def copy(self, dst: torch.Tensor, src_host: torch.Tensor, stream) -> None:
-        k = self.next
-        self.next ^= 1
-        if self.events[k] is not None:
-            self.events[k].synchronize()
-        self.bufs[k].copy_(src_host)
-        dst.copy_(self.bufs[k], non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record(stream)
-        self.events[k] = ev
 
 
 class _DeviceArray:
@@ -301,7 +281,7 @@ class B200FastDiT:
         host = torch.cat([t.detach().to("cpu", torch.float32) for t in parts])
         st = self._staging.get((key, name))
         if st is None:
-            st = self._staging[(key, name)] = _HostStaging(dst)
+            st = self._staging[(key, name)] = HostStaging(dst)
         st.copy(dst, host, torch.cuda.current_stream(self.device))
 
     @torch.inference_mode()

@@ -17,6 +17,7 @@ import torch
 from . import lib as L
 from . import ops as O
 from .config import DiTConfig, t_schedule
+from .staging import HostStaging
 
 
 def state_dict_from_module(cfm) -> dict:
@@ -81,6 +82,7 @@ class B200Solver:
         self._h = ctypes.c_void_p(self._hid)  # and as the ctypes binding takes it
         self._ws: dict = {}
         self._bufs: dict = {}
+        self._staging: dict = {}
 
     def close(self) -> None:
         if getattr(self, "_h", None) is not None and self._h.value:
@@ -174,15 +176,31 @@ class B200Solver:
         return b
 
     def solve_streams(self, streams: list, graph: bool = True) -> list:
-        """Solve packed streams (dicts with x0 / mu / cond [mel, L], spk [mel], P, T; any device) and return each
-        stream's final x [mel, L] fp32 on the solver's device (the chunk mel is ``[:, P:]``)."""
+        """Solve packed streams (dicts with x0 / mu / cond [mel, L], spk [mel], P, T; host or device tensors) and return
+        each stream's final x [mel, L] fp32 on the solver's device (the chunk mel is ``[:, P:]``; views of one fresh
+        tensor).  Host inputs are gathered into pinned mirrors of the static buffers and moved by one asynchronous copy
+        per input, so the host can prepare the next call while this one runs."""
         layout = Layout(tuple(int(s["P"]) for s in streams), tuple(int(s["T"]) for s in streams))
         b = self.static_buffers(layout)
-        for k in ("x0", "mu", "cond"):
-            b[k].copy_(torch.cat([s[k].t() for s in streams]).to(self.device, torch.float32))
-        b["spk"].copy_(torch.stack([s["spk"] for s in streams]).to(self.device, torch.float32))
+        st = torch.cuda.current_stream(self.device)
+        key = (layout.prompt, layout.chunk)
+        for k in ("x0", "mu", "cond", "spk"):
+            parts = [s[k] if k == "spk" else s[k].t() for s in streams]
+            if all(p.device == self.device for p in parts):
+                if k == "spk":
+                    torch.stack([p.to(torch.float32) for p in parts], out=b[k])
+                else:
+                    torch.cat([p.to(torch.float32) for p in parts], out=b[k])
+                continue
+            host = torch.stack([p.to("cpu", torch.float32) for p in parts]) if k == "spk" else \
+                torch.cat([p.to("cpu", torch.float32) for p in parts])
+            stg = self._staging.get((key, k))
+            if stg is None:
+                stg = self._staging[(key, k)] = HostStaging(b[k])
+            stg.copy(b[k], host, st)
         self.solve_packed_dev(layout, b["x0"], b["mu"], b["cond"], b["spk"], b["out"], workspace=b["ws"], graph=graph)
-        return [b["out"][o:o + n].t().clone() for o, n in zip(layout.offsets(), layout.lengths)]
+        out = b["out"].clone()  # the static buffer is rewritten by the next call
+        return [out[o:o + n].t() for o, n in zip(layout.offsets(), layout.lengths)]
 
     # ------------------------------------------------------------------------------------------------ reference API
     def forward_chunk(self, mu, spks, cond, n_timesteps: int = 10, temperature: float = 1.0, x0=None, prompt_len: int = 0):

@@ -63,3 +63,14 @@ def test_timeline_slot_solve_scatter_kernels():
     t = b.timeline_from_events(seq)
     assert set(t["kernel_ms"]) == {"qkv", "kv_scatter", "attn", "proj", "add_ln_mod after proj", "conv_cache",
                                    "conv1", "ln_mish after conv1", "conv2"}
+
+
+def test_c5_ranks_partition_the_1024_streams_through_the_scheduler():
+    """bench.py's default job: config 5's 1024 streams split by the product's scheduler, contiguous and equal per rank,
+    every stream on exactly one rank at N = 1, 2, 4, 8 (strong scaling)."""
+    for world in (1, 2, 4, 8):
+        bench = load_bench()
+        parts = [bench.rank_streams("c5", r, world)[1] for r in range(world)]
+        assert sorted(i for p in parts for i in p) == list(range(1024))
+        assert all(len(p) == 1024 // world for p in parts)
+        assert all(p == list(range(p[0], p[0] + len(p))) for p in parts)

@@ -489,7 +489,7 @@ def packed_record(solver, wl: Workload, steps: int, warm: int, flush: torch.Tens
 def reference_gpu_child(a) -> dict:
     """Run ``bench.py --impl reference --reference-gpu`` as a child process (this process never loads the reference
     or its restated modules) and return its record."""
-    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--reference-gpu"]
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--reference-gpu", "--reference-fastdit"]
     try:
         r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env={**os.environ, "WORLD_SIZE": "1",
                                                                                   "RANK": "0"})

@@ -253,6 +253,13 @@ T2W_API int t2w_profile_solve(t2w_solver* s, const t2w_batch* batch, void* works
 /* Synchronise the solver's error word: T2W_OK, or T2W_ERR_TIMEOUT if a kernel gave up on a wait (then cleared). */
 T2W_API int t2w_check(t2w_solver* s);
 
+/* Test entry point of the bounded waits (no reference counterpart; the reference's analogue is failure isolation,
+ * engine/runtime/t2w_worker.py:546-553): launches the row kernel in its early-start mode on 256 scratch rows whose
+ * 128-row block counter nothing publishes, with the wait limited to limit_ns (1e5 .. 2e9).  Every warp gives up after
+ * the limit and records T2W_ERR_TIMEOUT in the solver's error word, then returns; t2w_check reports and clears it.
+ * Asynchronous on `stream`; the solver stays usable. */
+T2W_API int t2w_test_wait_timeout(t2w_solver* s, int64_t limit_ns, void* stream);
+
 /* Copy the solver's modulation tables to device memory: mods [steps, depth, 9, H] (order sh_msa, 1+sc_msa, g_msa,
  * sh_mlp, 1+sc_mlp, g_mlp, sh_conv, 1+sc_conv, g_conv) and final [steps, 2, H] (sh, 1+sc); dts [steps] fp32. */
 T2W_API int t2w_mods(const t2w_solver* s, float* mods, float* final_mods, float* dts, void* stream);

@@ -81,6 +81,7 @@ _SIGS = {
     "t2w_workspace_bytes": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_size_t),
     "t2w_solve_packed": ([_P, ctypes.POINTER(Batch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
     "t2w_check": ([_P], ctypes.c_int),
+    "t2w_test_wait_timeout": ([_P, ctypes.c_int64, _P], ctypes.c_int),
     "t2w_profile_solve": ([_P, ctypes.POINTER(Batch), _P, ctypes.c_size_t, _P, ctypes.POINTER(ctypes.c_float),
                            ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "t2w_mods": ([_P, _P, _P, _P, _P], ctypes.c_int),

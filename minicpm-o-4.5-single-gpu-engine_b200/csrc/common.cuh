@@ -356,13 +356,14 @@ T2W_DEV void st_f4_l2hint(float4* a, float4 v, uint64_t policy) {
 }
 // Async-proxy (TMA) global writes ordered before this thread's later generic-proxy operations.
 T2W_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
-// Bounded wait until *f >= target; false (and T2W_ERR_TIMEOUT in err) after kWaitLimitNs.
-T2W_DEV bool wait_counter(const int* f, int target, int* err) {
+// Bounded wait until *f >= target; false (and T2W_ERR_TIMEOUT in err) after limit_ns (0: kWaitLimitNs).
+T2W_DEV bool wait_counter(const int* f, int target, int* err, unsigned long long limit_ns = 0) {
   if (ld_acquire_gpu(f) >= target) return true;
+  const unsigned long long limit = limit_ns ? limit_ns : kWaitLimitNs;
   const unsigned long long t0 = globaltimer();
   while (ld_acquire_gpu(f) < target) {
     __nanosleep(128);
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       if (err) atomicExch(err, T2W_ERR_TIMEOUT);
       return false;
     }

@@ -187,6 +187,8 @@ struct RowWait {
   unsigned pf_bytes = 0;
   const void* pf2 = nullptr;
   unsigned pf2_bytes = 0;
+  // the wait's limit in ns (0: the library's 2 s); a shorter one lets a test make a wait run out quickly
+  unsigned long long limit_ns = 0;
 };
 // h += g * y (fp32, in place; skipped when y == nullptr), then out = LN(h) * scale1 + shift, pad rows zero.
 int launch_add_ln_mod(float* h, const __nv_bfloat16* y, const float* g, const float* shift, const float* scale1, float eps,

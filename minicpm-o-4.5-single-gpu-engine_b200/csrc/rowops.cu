@@ -111,7 +111,7 @@ T2W_DEV void prefetch_next_weights(const RowWait& wt) {
 
 T2W_DEV bool row_ready(const RowWait& wt, int row) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = wait_counter(wt.flags + (row >> 7), wt.target, wt.err);
+  if ((threadIdx.x & 31) == 0) ok = wait_counter(wt.flags + (row >> 7), wt.target, wt.err, wt.limit_ns);
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 

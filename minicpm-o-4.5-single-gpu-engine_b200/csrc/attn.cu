@@ -390,6 +390,10 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       const int n_kt = items[2 * k + q].n_kt;
       const int pos = w.q_pos + r;
       const int lim = GATHER ? (pos < w.P ? w.L : 0) : (pos < w.P ? w.P : (pos < w.L ? w.L : 0));
+      // A warp whose 32 query rows all lie past the item's queries (a 50-frame window fills 50 rows of the 128-row
+      // tile; a sequence's last tile is partial) computes no softmax: its rows' P and O are never stored, so whatever
+      // the TMEM holds there only reaches those rows' discarded outputs.  It still takes part in every barrier.
+      const bool idle = __all_sync(0xffffffffu, lim == 0);
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_kt; ++j, ++t) {
         // warp-uniform: tcgen05.ld / st below are .sync.aligned
@@ -401,6 +405,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         }
         tc_fence_after();
         const uint32_t sbuf = preg + 64 * (t & 1);
+        if (!idle) {
         uint32_t sr[64];
         tmem_ld64_nowait(sbuf, sr);
         tmem_ld_wait();
@@ -461,6 +466,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         const float2 rs2 = __fadd2_rn(__fadd2_rn(rsq[0], rsq[1]), __fadd2_rn(rsq[2], rsq[3]));
         l += rs2.x + rs2.y;
         tmem_st_wait();
+        }
         if (j == 0 && have_pend) {  // the previous item's output (before this tile's P V can overwrite O)
           if (!(ok = finish(pend))) break;
           have_pend = false;

@@ -364,11 +364,15 @@ def reference_gpu_arm(a) -> None:
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     rec = {"impl": "reference_gpu", "gpu": torch.cuda.get_device_name(dev)}
-    for name, wl in (("target", TARGET), ("c2", C2)):
-        try:
-            rec[name] = reference_gpu_eager(wl, steps=3, warm=1, dev=dev)
-        except Exception as e:  # reported, not raised: the default arm's own numbers stand without it
-            rec[name] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    # the reference's decode calls carry at most 32 streams (BatchedToken2Wav.max_flow_streams, token2wav_batch.py:196):
+    # its graph-replayed window solve is timed at that size too, beside this build's 32-window steady call
+    w32 = Workload("ref_w32_32x(300+50)", 1, C2.lengths[:1] * 32)
+    for name, wl in (("target", TARGET), ("c2", C2), ("w32", w32)):
+        if name != "w32":
+            try:
+                rec[name] = reference_gpu_eager(wl, steps=3, warm=1, dev=dev)
+            except Exception as e:  # reported, not raised: the default arm's own numbers stand without it
+                rec[name] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
         if a.reference_fastdit:
             try:
                 rec[name + "_fastdit"] = reference_gpu_fastdit(wl, steps=3, warm=2, dev=dev)
@@ -660,6 +664,10 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
         torch.cuda.empty_cache()
         ref_gpu = reference_gpu_child(a)
         ours = {"target": sub.get("target", {}).get("ms_per_solve"), "c2": (sub.get("c2") or {}).get("ms_per_solve")}
+        w_ours = (sub.get("steady_32") or {}).get("ms_per_call")
+        w_ref = (ref_gpu.get("w32_fastdit") or {}).get("window_ms")
+        if w_ours and w_ref:  # steady-state windows, 32 per call: FastDiT's graph-replayed window vs this build's call
+            ref_gpu["steady_32_speedup_vs_fastdit_window"] = w_ref / w_ours
         if a.workload == "c2":
             ours["c2"] = statistics.median(batch_ms)
         for k, v in ours.items():

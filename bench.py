@@ -566,20 +566,20 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
     batch_ms = [e[j].elapsed_time(e[j + 1]) for e in recs for j in range(len(jobs))]
 
     # ---- end to end through the public API: per-stream host tensors -> solve_streams -> chunk mels on the host
-    host_out = torch.empty(cfg.mel, sum(x["T"] for x in streams), dtype=torch.float32).pin_memory()
+    # one contiguous pinned block per batch: an asynchronous device -> host copy into a strided slice would be staged
+    # synchronously and hold the host until the batch's solve is done
+    host_out = [torch.empty(cfg.mel, sum(x["T"] for x in g), dtype=torch.float32).pin_memory() for g in groups]
     h2d = sum(4 * (3 * x["x0"].numel() + x["spk"].numel()) for x in streams)
-    d2h = host_out.numel() * 4
+    d2h = sum(t.numel() * 4 for t in host_out)
     e2e_ms = []
     for i in range(1 + a.steps):
         flush.fill_(1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        o = 0
-        for g in groups:
+        for gi, g in enumerate(groups):
             outs = solver.solve_streams(g)
             chunk = torch.cat([y[:, x["P"]:] for x, y in zip(g, outs)], dim=1)
-            host_out[:, o:o + chunk.shape[1]].copy_(chunk, non_blocking=True)
-            o += chunk.shape[1]
+            host_out[gi].copy_(chunk, non_blocking=True)
         e1.record(st)
         e1.synchronize()
         if i >= 1:

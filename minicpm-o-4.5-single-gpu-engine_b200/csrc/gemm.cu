@@ -65,7 +65,6 @@ struct DevArgs {
   const float* gate;  // T2W_EPI_RESID: per-column gate of the residual update
   const void* pf;     // L2 prefetch of the next GEMM's weights (see GemmArgs)
   unsigned pf_bytes;
-  int k_splits;  // work units per output tile (split along K; T2W_EPI_RESID only)
 };
 
 T2W_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
@@ -120,7 +119,7 @@ T2W_DEV float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2
 // Epilogue math of box b for this thread's row: `raw` holds the box's accumulator columns (32 fp32 columns, or 64 for
 // bf16 outputs); on return it holds the 32 words staged for the box (fp32 values, or bf16 pairs).
 template <int EPI>
-T2W_DEV void epilogue_math(const DevArgs& p, int n0, int b, uint32_t (&raw)[64], bool bias_on = true) {
+T2W_DEV void epilogue_math(const DevArgs& p, int n0, int b, uint32_t (&raw)[64]) {
   if constexpr (EPI == T2W_EPI_F32) {
     const float* bias = p.bias + n0 + 32 * b;
 #pragma unroll
@@ -130,7 +129,7 @@ T2W_DEV void epilogue_math(const DevArgs& p, int n0, int b, uint32_t (&raw)[64],
     const float4* gate = reinterpret_cast<const float4*>(p.gate + n0 + 32 * b);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float4 bb = bias_on ? __ldg(bias + j) : make_float4(0.f, 0.f, 0.f, 0.f), gg = __ldg(gate + j);
+      const float4 bb = __ldg(bias + j), gg = __ldg(gate + j);
       raw[4 * j] = __float_as_uint(gg.x * (__uint_as_float(raw[4 * j]) + bb.x));
       raw[4 * j + 1] = __float_as_uint(gg.y * (__uint_as_float(raw[4 * j + 1]) + bb.y));
       raw[4 * j + 2] = __float_as_uint(gg.z * (__uint_as_float(raw[4 * j + 2]) + bb.z));
@@ -223,11 +222,9 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int ks = tile % p.k_splits, ot = tile / p.k_splits;
-        const int m0 = (ot / p.tiles_n) * kBM, n0 = (ot % p.tiles_n) * BN;
+        const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
         if (tile + (int)gridDim.x >= p.num_tiles) prefetch_l2_piece(p.pf, p.pf_bytes, blockIdx.x);  // last tile
-        const int kb0 = ks * num_kb / p.k_splits, kb1 = (ks + 1) * num_kb / p.k_splits;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
           const int tap = kb / kb_per_tap, kk = (kb - tap * kb_per_tap) * kBK;
@@ -252,16 +249,14 @@ __global__ void __launch_bounds__(320, 1)
         if (!(ok = mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1u, p.err))) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
-        const int ks = tile % p.k_splits;
-        const int kb0 = ks * num_kb / p.k_splits, kb1 = (ks + 1) * num_kb / p.k_splits;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb) {
           if (!(ok = mbar_wait(&full[stage], phase, p.err))) break;
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES), b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             umma_f16(d, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
-                     (kb != kb0 || k != 0) ? 1u : 0u);
+                     (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -279,8 +274,7 @@ __global__ void __launch_bounds__(320, 1)
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
-      const int ks = tile % p.k_splits, ot = tile / p.k_splits;
-      const int m0 = (ot / p.tiles_n) * kBM, n0 = (ot % p.tiles_n) * BN;
+      const int m0 = (tile / p.tiles_n) * kBM, n0 = (tile % p.tiles_n) * BN;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
       // warp-uniform (tcgen05.ld is .sync.aligned); after a timed-out wait the warp stops
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) break;
@@ -308,7 +302,7 @@ __global__ void __launch_bounds__(320, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
           }
-          epilogue_math<EPI>(p, n0, b, raw, ks == 0);
+          epilogue_math<EPI>(p, n0, b, raw);
           // this warp's previous store has finished reading the slot
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
@@ -613,8 +607,7 @@ int launch_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
   p.taps = a.taps;
   p.tap_row0 = a.tap_row0;
   p.tiles_n = a.N / BN;
-  p.k_splits = a.k_splits;
-  p.num_tiles = (a.M / kBM) * p.tiles_n * p.k_splits;
+  p.num_tiles = (a.M / kBM) * p.tiles_n;
   p.bias = a.bias;
   p.out = a.out;
   p.ldo = a.ldo;
@@ -697,7 +690,6 @@ int launch_pair_impl(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA,
   p.taps = a.taps;
   p.tap_row0 = a.tap_row0;
   p.tiles_n = a.N / 256;
-  p.k_splits = 1;
   p.num_tiles = ((a.M + 2 * kBM - 1) / (2 * kBM)) * p.tiles_n;
   p.bias = a.bias;
   p.out = a.out;
@@ -763,21 +755,6 @@ bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot) {
   return m->has128;
 }
 
-int gemm_k_splits(int tiles, int k_blocks) {
-  const int sms = num_sms();
-  int best = 1;
-  double best_t = (double)((tiles + sms - 1) / sms);
-  for (int s = 2; s <= 4; ++s) {
-    if (k_blocks / s < 8) break;
-    const double t = (double)((tiles * s + sms - 1) / sms) / s;
-    if (t < best_t - 0.05) {
-      best_t = t;
-      best = s;
-    }
-  }
-  return best;
-}
-
 // Column tile: 80 for the 80-wide final layer, else 256 (a 128 x 128 tile needs operand bytes from shared memory
 // faster than the SM delivers them beside the TMA writes; 128 x 256 runs the tensor core at its rate), 128 only when N
 // is not a multiple of 256.
@@ -806,9 +783,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
     if (a.epi == T2W_EPI_BF16) return launch_impl<80, T2W_EPI_BF16, false>(a, st, tmA, tmW, tmC);
     return T2W_ERR_INVALID;
   }
-  if (a.k_splits < 1 || (a.k_splits > 1 && (a.epi != T2W_EPI_RESID || a.K * a.taps / kBK < a.k_splits)))
-    return T2W_ERR_INVALID;
-  if (bn == 256 && a.k_splits == 1 && use_pair(a)) {
+  if (bn == 256 && use_pair(a)) {
     switch (a.epi) {
       case T2W_EPI_F32: return launch_pair_impl<T2W_EPI_F32>(a, st, tmA, tmW, tmC);
       case T2W_EPI_BF16: return launch_pair_impl<T2W_EPI_BF16>(a, st, tmA, tmW, tmC);

@@ -60,13 +60,7 @@ struct GemmArgs {
   const void* pf = nullptr;
   unsigned pf_bytes = 0;
   const float* gate = nullptr;  // T2W_EPI_RESID: out (fp32) += gate[n] * (acc + bias[n]), N floats
-  // T2W_EPI_RESID only: each output tile's K range split over this many CTAs, every part adding its gated partial sum
-  // into out (the bias with the first part), so a GEMM with too few tiles for the SMs gets more work units
-  int k_splits = 1;
 };
-// K splits that minimise the rounds of work units (tiles x splits over the SMs, per split) for a gated-residual GEMM,
-// keeping at least 8 K blocks of 64 per part; 1 when splitting does not help.
-int gemm_k_splits(int tiles, int k_blocks);
 // Column tile the launcher picks for an N-wide output of M rows with epilogue `epi` (0: N unsupported).
 int gemm_block_n_for(int N, int M, int epi);
 // Whether some (M, epi) can use an N-wide output at all.

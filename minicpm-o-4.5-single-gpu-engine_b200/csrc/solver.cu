@@ -508,13 +508,6 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
   T2W_CUDA(cudaMemsetAsync(done_all, 0, (size_t)c.steps * c.depth * 4 * mblocks * sizeof(int), st));
   // the N = H GEMMs (proj, conv1, conv2, fc2) publish per-block completion; the row kernel after each waits per block
   const int done_target = 8 * (H / gemm_block_n_for(H, R, T2W_EPI_BF16));
-  // K splits of the gated-residual GEMMs (N = H): too few 128 x 256 tiles for the SMs (config 2: 176 on 148 SMs, the
-  // steady state's 104) get split work units, each adding its partial sum into h; conv2 / fc2 then add their gated
-  // residual in the epilogue as proj does
-  const int h_tiles = mblocks * (H / gemm_block_n_for(H, R, T2W_EPI_RESID));
-  const int split_proj = gemm_k_splits(h_tiles, H / 64);
-  const int split_conv2 = gemm_k_splits(h_tiles, 3 * H / 64);
-  const int split_fc2 = gemm_k_splits(h_tiles, F / 64);
   T2W_TRY(P.tick(T2W_KC_PACK, st));
   if (pl.gather) {  // x0 from the flow's noise at each request's cache length, into the workspace (b.x0 points there)
     if (!nsrc || b.x0 != at<float>(ws, L.x0g)) return T2W_ERR_INVALID;
@@ -557,7 +550,6 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
     const float* pend_g = nullptr;
     const __nv_bfloat16* pend_y = nullptr;
     int* pend_done = nullptr;
-    int pend_splits = 1;
     for (int bi = 0; bi < c.depth; ++bi) {
       const BlockW& w = s->blk[bi];
       const float* M = s->mods + ((size_t)step * c.depth + bi) * 9 * H;
@@ -567,10 +559,10 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       // each norm kernel prefetches the weights of the GEMM after it into L2 (HBM-resident: all blocks' weights exceed
       // L2); attention prefetches proj's, and fc1 fc2's as its CTAs start their last tile
       auto waits = [&](int* f, const void* pf = nullptr, size_t pf_bytes = 0, const void* pf2 = nullptr,
-                       size_t pf2_bytes = 0, int splits = 1) {
+                       size_t pf2_bytes = 0) {
         RowWait r;
         r.flags = f;
-        r.target = done_target * splits;
+        r.target = done_target;
         r.err = s->err;
         r.pf = pf;
         r.pf_bytes = (unsigned)pf_bytes;
@@ -633,7 +625,7 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       // attention branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, sh_a, sc_a, c.eps_block, R, H, row_out_bf16(a), nullptr, st,
-                                waits(pend_done, w.qkv, wb_qkv, nullptr, 0, pend_splits)));
+                                waits(pend_done, w.qkv, wb_qkv)));
       GemmArgs q = GemmArgs();
       q.rows_a = R; q.M = R; q.err = s->err;
       q.A = a; q.lda = H; q.W = w.qkv; q.bias = w.b_qkv; q.N = 3 * H; q.K = H; q.epi = T2W_EPI_QKV; q.out = qkv; q.ldo = 3 * H;
@@ -658,13 +650,12 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       pr.A = o; pr.lda = H; pr.W = w.proj; pr.bias = w.b_proj; pr.N = H; pr.K = H; pr.epi = T2W_EPI_RESID; pr.out = h; pr.ldo = H;
       pr.gate = g_a;
       pr.done_flags = dn;
-      pr.k_splits = split_proj;
       T2W_TRY(P.tick(T2W_KC_GEMM_PROJ, st));
       T2W_TRY(launch_gemm(pr, st, &tm_o, &w.tm_proj, &st_h));
       // causal conv branch (norm3 / conv modulations: token2wav_batch.py:107-108); pad rows of its input are zero
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
       T2W_TRY(launch_add_ln_mod(h, nullptr, nullptr, sh_c, sc_c, c.eps_block, R, H, row_out_bf16(a), pad, st,
-                                waits(dn, w.c1, wb_conv, nullptr, 0, split_proj)));
+                                waits(dn, w.c1, wb_conv)));
       if (pl.slots)  // cached conv-input frames in front of each window, and the window's last two saved
         T2W_TRY(launch_conv_cache(a, H, conv_rows_d, n_conv_rows, sp->cnn + sb * sp->cnn_sb(), sp->cnn_slot(), st));
       GemmArgs k1 = GemmArgs();
@@ -688,18 +679,16 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       // after each reads h alone instead of h and y and writing h back: at the target shape (64 x (300 + 50), 704 tiles
       // per N = 512 GEMM) the solve went 109.5 -> 106.4 ms; at config 2 (176 tiles) the longer fp32 epilogue of the
       // last round costs more than the norm saves (29.1 -> 29.5 ms), so below three rounds of tiles they keep bf16 y.
-      const bool big = (long long)mblocks * (H / 256) >= 3ll * num_sms();
-      const bool ra2 = big || split_conv2 > 1, ra4 = big || split_fc2 > 1;
-      if (ra2) {
-        k2.epi = T2W_EPI_RESID; k2.out = h; k2.gate = g_c; k2.k_splits = split_conv2;
+      const bool ra = (long long)mblocks * (H / 256) >= 3ll * num_sms();
+      if (ra) {
+        k2.epi = T2W_EPI_RESID; k2.out = h; k2.gate = g_c;
       }
       T2W_TRY(P.tick(T2W_KC_GEMM_CONV2, st));
-      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, ra2 ? &st_h : &st_y));
+      T2W_TRY(launch_gemm(k2, st, &tm_c1, &w.tm_c2, ra ? &st_h : &st_y));
       // MLP branch
       T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
-      T2W_TRY(launch_add_ln_mod(h, ra2 ? nullptr : y, ra2 ? nullptr : g_c, sh_m, sc_m, c.eps_block, R, H,
-                                row_out_bf16(a), nullptr, st,
-                                waits(dn + 2 * mblocks, w.fc1, wb_mlp, nullptr, 0, ra2 ? split_conv2 : 1)));
+      T2W_TRY(launch_add_ln_mod(h, ra ? nullptr : y, ra ? nullptr : g_c, sh_m, sc_m, c.eps_block, R, H,
+                                row_out_bf16(a), nullptr, st, waits(dn + 2 * mblocks, w.fc1, wb_mlp)));
       GemmArgs f1 = GemmArgs();
       f1.rows_a = R; f1.M = R; f1.err = s->err;
       f1.A = a; f1.lda = H; f1.W = w.fc1; f1.bias = w.b_fc1; f1.N = F; f1.K = H; f1.epi = T2W_EPI_GELU; f1.out = f; f1.ldo = F;
@@ -711,21 +700,20 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       f2.rows_a = R; f2.M = R; f2.err = s->err;
       f2.A = f; f2.lda = F; f2.W = w.fc2; f2.bias = w.b_fc2; f2.N = H; f2.K = F; f2.epi = T2W_EPI_BF16; f2.out = y; f2.ldo = H;
       f2.done_flags = dn + 3 * mblocks;
-      if (ra4) {
-        f2.epi = T2W_EPI_RESID; f2.out = h; f2.gate = g_m; f2.k_splits = split_fc2;
+      if (ra) {
+        f2.epi = T2W_EPI_RESID; f2.out = h; f2.gate = g_m;
       }
       T2W_TRY(P.tick(T2W_KC_GEMM_FC2, st));
-      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, ra4 ? &st_h : &st_y));
-      pend_g = ra4 ? nullptr : g_m;
-      pend_y = ra4 ? nullptr : y;
+      T2W_TRY(launch_gemm(f2, st, &tm_f, &w.tm_fc2, ra ? &st_h : &st_y));
+      pend_g = ra ? nullptr : g_m;
+      pend_y = ra ? nullptr : y;
       pend_done = dn + 3 * mblocks;
-      pend_splits = ra4 ? split_fc2 : 1;
     }
     const float* FM = s->final_mods + (size_t)step * 2 * H;
     T2W_TRY(P.tick(T2W_KC_LN_MOD, st));
     RowWait fw;
     fw.flags = pend_done;
-    fw.target = done_target * pend_splits;
+    fw.target = done_target;
     fw.err = s->err;
     T2W_TRY(launch_add_ln_mod(h, pend_y, pend_g, FM, FM + H, c.eps_final, R, H, row_out_bf16(a), nullptr, st, fw));
     GemmArgs fin = GemmArgs();

@@ -64,7 +64,7 @@ def args_():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="c5", choices=["c5", "c2", "target", "c3", "c4", "steady"])
-    ap.add_argument("--batch", type=int, default=64, help="streams per solve on a rank (c5)")
+    ap.add_argument("--batch", type=int, default=64, help="streams per solve on a rank (c5) / windows per call (steady)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true")
@@ -727,7 +727,7 @@ def main() -> None:
             reference_arm(a, rank, world)
         elif a.workload == "steady":
             torch.cuda.set_device(local)
-            rec = steady_record(REFERENCE, torch.device("cuda", local), 64, a.steps, a.warmup, seed=11 + rank,
+            rec = steady_record(REFERENCE, torch.device("cuda", local), a.batch, a.steps, a.warmup, seed=11 + rank,
                                 timeline_on=a.timeline and rank == 0)
             red = torch.tensor([rec["ms_per_call"]], dtype=torch.float64)
             if world > 1:

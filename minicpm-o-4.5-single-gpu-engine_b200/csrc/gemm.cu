@@ -756,13 +756,24 @@ bool make_weight_maps(WeightMaps* m, const void* W, int N, int Ktot) {
 }
 
 // Column tile: 80 for the 80-wide final layer, else 256 (a 128 x 128 tile needs operand bytes from shared memory
-// faster than the SM delivers them beside the TMA writes; 128 x 256 runs the tensor core at its rate), 128 only when N
-// is not a multiple of 256.
+// faster than the SM delivers them beside the TMA writes; 128 x 256 runs the tensor core at its rate), 128 when N is
+// not a multiple of 256 or when 256-column tiles would fill at most half the SMs.  T2W_GEMM_BN=128 / =256 overrides
+// the rule for multiples of 256.
 int gemm_block_n_for(int N, int M, int epi) {
-  (void)M;
   (void)epi;
+  static int force = -2;
+  if (force == -2) {
+    const char* e = getenv("T2W_GEMM_BN");
+    force = (e && atoi(e) == 128) ? 128 : (e && atoi(e) == 256) ? 256 : 0;
+  }
   if (N == 80) return 80;
-  if (N % 256 == 0) return 256;
+  if (N % 256 == 0) {
+    if (force) return force;
+    // With few 128-row blocks the 128 x 256 tiles leave most SMs idle; 128-column tiles double the CTAs at the cost
+    // of the tensor core's rate on each (their operands arrive from shared memory more slowly per FLOP).
+    const long long tiles = (long long)((M + kBM - 1) / kBM) * (N / 256);
+    return 2 * tiles <= num_sms() ? 128 : 256;
+  }
   if (N % 128 == 0) return 128;
   return 0;
 }

@@ -123,3 +123,59 @@ def t_schedule(steps: int):
         if step < steps:
             dt = t_span[step + 1] - t
     return ts, dts
+
+
+@dataclass(frozen=True)
+class EncoderConfig:
+    """The flow encoder's hyper-parameters (``UpsampleConformerEncoderV2`` of ``stepaudio2``; the reference reads them
+    off the module: ``len(enc.encoders)``, ``len(enc.up_encoders)``, ``enc.up_layer.stride``,
+    ``enc.pre_lookahead_layer.pre_lookahead_len``, the attention cache's heads and ``2 * d_k``,
+    ``engine/runtime/token2wav_batch.py:408-418``).  The values are the published CosyVoice2 / Step-Audio2 ``flow.yaml``
+    encoder (512 wide, 8 heads, 2048-wide swish feed-forward, 6 + 4 conformer blocks without conv module or macaron,
+    ESPnet relative positions, linear input layer, pre-norm) and are UNVERIFIED against the checkpoint."""
+    vocab: int = 6561             # flow.input_embedding rows (speech tokens, unverified)
+    hidden: int = 512             # encoder output_size and input_size (unverified)
+    heads: int = 8                # attention heads (unverified)
+    head_dim: int = 64            # d_k; the attention cache holds [k | v] = 2 d_k per frame
+    ffn: int = 2048               # linear_units (unverified)
+    blocks1: int = 6              # len(enc.encoders) (unverified)
+    blocks2: int = 4              # len(enc.up_encoders) (unverified)
+    stride: int = 2               # enc.up_layer.stride: two mel frames per token
+    lookahead: int = 3            # enc.pre_lookahead_layer.pre_lookahead_len (engine/token2wav_chunker.py:20)
+    mel: int = 80                 # encoder_proj output (the DiT's mu channels)
+    spk_dim: int = 192            # spk_embed_affine_layer input (CAMPPlus embedding, unverified)
+    eps_layer: float = 1e-12      # norm_mha / norm_ff of each conformer layer (unverified)
+    eps_embed: float = 1e-5       # embed / up_embed LayerNorm (unverified)
+    eps_after: float = 1e-5       # after_norm (unverified)
+    leaky_slope: float = 0.01     # pre-lookahead conv1 activation (F.leaky_relu default)
+    max_period: float = 10000.0   # relative positional encoding sinusoid base
+
+    @property
+    def conv1_kernel(self) -> int:
+        return self.lookahead + 1
+
+    @property
+    def up_kernel(self) -> int:
+        return 2 * self.stride + 1
+
+    @property
+    def cnn_cache(self) -> int:
+        """Frames of the conv cache: 2 of the pre-lookahead conv2, 2 * stride of the upsampling conv."""
+        return 2 + 2 * self.stride
+
+    def validate_for_kernels(self) -> None:
+        if self.head_dim != 64 or self.hidden != self.heads * self.head_dim:
+            raise ValueError("the attention kernel takes head_dim == 64 and hidden == heads * 64")
+        if self.hidden % 128 or self.ffn % 128 or self.hidden > 1024:
+            raise ValueError("hidden and ffn must be multiples of 128, hidden <= 1024")
+        if self.mel != 80:
+            raise ValueError("encoder_proj runs on the 80-column GEMM tile")
+        if self.stride != 2 or self.lookahead != 3:
+            raise ValueError("the conv kernels take stride 2 and a 3-frame lookahead")
+
+
+ENCODER = EncoderConfig()
+"""The reference-config (unverified) flow encoder."""
+
+ENCODER_TINY = replace(ENCODER, hidden=128, heads=2, ffn=256, blocks1=2, blocks2=2, spk_dim=32)
+"""A small encoder with the same kernel shape class, for fast golden fixtures."""

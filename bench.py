@@ -63,7 +63,7 @@ def args_():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="c5", choices=["c5", "c2", "target", "c3", "c4", "steady"])
+    ap.add_argument("--workload", default="c5", choices=["c5", "c2", "target", "c3", "c4", "steady", "encoder"])
     ap.add_argument("--batch", type=int, default=64, help="streams per solve on a rank (c5) / windows per call (steady)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
@@ -450,6 +450,88 @@ def steady_record(cfg: DiTConfig, dev, n: int, steps: int, warmup: int, seed: in
     return rec
 
 
+def encoder_flops(ecfg, T: int, K1: int, K2: int) -> float:
+    """Algorithmic FLOPs of one flow-encoder window of T token frames (first stack: T queries over K1 keys; second
+    stack: 2T over K2): per frame and layer 2H(5H + 2F) for [q + u | q + v | k | v], linear_out, w_1, w_2; per
+    (query, key) 6H for (q + u) k, (q + v) P(r) and P V; the embed linear and the 4- and 3-tap pre-lookahead convs
+    over the T + 3 / T frames; the 5-tap up conv, up embed and encoder_proj over the 2T upsampled frames."""
+    H, F = ecfg.hidden, ecfg.ffn
+    layer = 2 * H * (5 * H + 2 * F)
+    s1 = ecfg.blocks1 * (T * layer + 6 * H * T * K1)
+    s2 = ecfg.blocks2 * (2 * T * layer + 6 * H * 2 * T * K2)
+    convs = (T + 3) * 2 * H * H + T * 2 * H * H * (4 + 3) + 2 * T * (2 * H * H * 5 + 2 * H * H + 2 * H * ecfg.mel)
+    return float(s1 + s2 + convs)
+
+
+def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, seed: int, peak_tf: float,
+                   cpu: bool = True) -> dict:
+    """The flow encoder (row f3: speech tokens -> mu) at the reference config, random init: ``n`` streams set up with
+    ``prompt_tokens``-token prompts in one call (the batched prompt setup), then steady windows of 25 tokens + 3
+    look-ahead tokens, one per stream per call, once the caches have reached their trimmed length.  Window tokens are
+    copied from pinned host memory and every call's mu is read back to pinned host memory inside the timed region
+    (device events around the calls, back to back).  The fp32 CPU oracle times one stream's window beside it."""
+    from b200t2w.config import ENCODER
+    from b200t2w.encoder import B200FlowEncoder
+    from oracle import encoder_oracle as eo
+
+    g = torch.Generator().manual_seed(seed)
+    flow = eo.build_flow(ENCODER, seed=0)
+    enc = B200FlowEncoder.from_flow(flow, device=dev, max_frames=2048, n_slots1=n * 512, n_slots2=n * 1024,
+                                    n_streams=n)
+    prompts = [torch.randint(0, ENCODER.vocab, (prompt_tokens,), generator=g) for _ in range(n)]
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    handles, _ = enc.setup(prompts)
+    e1.record(st)
+    e1.synchronize()
+    setup_ms = e0.elapsed_time(e1)
+    W, T = 28, 25
+    wins = [[torch.randint(0, ENCODER.vocab, (W,), generator=g).tolist() for _ in range(n)] for _ in range(4)]
+    host_out = torch.empty(n * 2 * T, ENCODER.mel).pin_memory()
+    out = torch.empty(n * 2 * T, ENCODER.mel, device=dev)
+
+    def call(k):
+        enc.encode_packed(handles, wins[k % 4], [False] * n, out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    for k in range(max(warmup, 4)):  # caches reach the trimmed length (keep + 100) after a few windows
+        call(k)
+    torch.cuda.synchronize(dev)
+    k1, k2, keep = enc.stream_info(handles[0])
+    e0.record(st)
+    for k in range(steps):
+        call(k)
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    enc.check()
+    flop = n * encoder_flops(ENCODER, T, k1 + T, k2 + 2 * T)
+    rec = {"workload": f"flow encoder, {n} streams, steady windows of {W} tokens ({T} + 3 look-ahead) after "
+                       f"{prompt_tokens}-token prompts (keys per stream: stack 1 {k1} + {T}, stack 2 {k2} + {2 * T})",
+           "ms_per_call": ms, "mu_frames_per_s": n * 2 * T / (ms / 1000), "tflops": flop / (ms / 1000) / 1e12,
+           "frac_of_bf16_peak": flop / (ms / 1000) / 1e12 / peak_tf,
+           "setup_ms": setup_ms, "setup_mu_frames_per_s": n * 2 * prompt_tokens / (setup_ms / 1000),
+           "h2d_bytes_per_call": n * W * 4, "d2h_bytes_per_call": n * 2 * T * ENCODER.mel * 4,
+           "note": "setup_ms is the first call (includes its workspace allocation)"}
+    if cpu:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        _, s = eo.encode_prompt(flow, prompts[0])
+        ts = []
+        for k in range(5):
+            t0 = time.perf_counter()
+            eo.encode_window(flow, s, torch.tensor(wins[k % 4][0]), False)
+            ts.append(time.perf_counter() - t0)
+        cpu_s = statistics.median(ts[2:])
+        rec["cpu_baseline"] = {"value": 2 * T / cpu_s, "unit": "mu frames/s", "cores": threads, "kind": "port",
+                               "sample": "1 stream's steady window, fp32 CPU oracle (median of 3 after 2 warm-up)"}
+    for h in handles:
+        enc.release(h)
+    enc.close()
+    return rec
+
+
 def packed_record(solver, wl: Workload, steps: int, warm: int, flush: torch.Tensor, peak_tf: float) -> dict:
     """One packed workload as a sub-record: device-resident inputs, ``steps`` graph-replayed solves with L2 flushed
     between them (median event time), and the GEMM fraction from one eager profiling solve."""
@@ -660,6 +742,8 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
         for n in (32, 64):
             sub[f"steady_{n}"] = steady_record(cfg, dev, n, steps=10, warmup=3, seed=11)
             torch.cuda.empty_cache()
+        sub["encoder_64"] = encoder_record(dev, 64, 150, steps=10, warmup=4, seed=12, peak_tf=peak_tf)
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not a.no_reference_gpu:
         torch.cuda.empty_cache()
         ref_gpu = reference_gpu_child(a)
@@ -725,6 +809,18 @@ def main() -> None:
     try:
         if a.impl == "reference":
             reference_arm(a, rank, world)
+        elif a.workload == "encoder":
+            torch.cuda.set_device(local)
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+                os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+            rec = encoder_record(torch.device("cuda", local), a.batch, 150, a.steps, a.warmup, seed=12 + rank,
+                                 peak_tf=peaks.get("bf16_tflops_sustained", 1400.0), cpu=not a.no_cpu_baseline)
+            if rank == 0:
+                print(json.dumps({"metric": "flow encoder mu frames/s (steady windows)", "value": rec["mu_frames_per_s"],
+                                  "unit": "mu frames/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+                                  "ms_per_step": rec["ms_per_call"], "higher_is_better": True, "dtype": "bf16",
+                                  "data": "synthetic", "config": {"workload": rec["workload"]}, "encoder": rec}),
+                      flush=True)
         elif a.workload == "steady":
             torch.cuda.set_device(local)
             rec = steady_record(REFERENCE, torch.device("cuda", local), a.batch, a.steps, a.warmup, seed=11 + rank,

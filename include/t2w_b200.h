@@ -288,6 +288,8 @@ T2W_API int t2w_ln_mish(const void* x_bf16, const float* w, const float* b, floa
 #define T2W_EPI_GELU 2 /* out bf16 = gelu_tanh(acc + bias) */
 #define T2W_EPI_RESID 3 /* out fp32 += gate * (acc + bias), in place: the gated residual (gate: N floats, qk[0]) */
 #define T2W_EPI_QKV 4  /* out bf16 = [LN_q(q) | LN_k(k) | v] per 64-wide head (q/k affine norms) */
+#define T2W_EPI_SILU 5 /* out bf16 = silu(acc + bias): the flow encoder's swish feed-forward */
+#define T2W_EPI_LEAKY 6 /* out bf16 = leaky_relu(acc + bias) with slope qk_eps: the pre-lookahead conv1 */
 #define T2W_EPI_GELU_FP8 8 /* t2w_gemm_e4m3 only: out e4m3 = gelu_tanh(acc + bias) with its scale atoms */
 
 /* C[M, N] = sum_tap A[m + tap_row0 + tap, :K] . W[n, tap*K : (tap+1)*K] then the epilogue.  A bf16 [rows_a, lda],
@@ -363,6 +365,117 @@ T2W_API int t2w_gemm_e4m3(const void* A8, int32_t lda, int32_t rows_a, const uin
  * writes bf16(x) into hx[row] and hx[row + half_rows] (first mel columns of ld_hx) and, when out != NULL, out[i] = x. */
 T2W_API int t2w_euler_cfg(float* x, const float* dphi, int32_t ld_dphi, const int32_t* tok_row, int32_t n_tok, int32_t mel,
                   int32_t half_rows, float dt, float w, void* hx_bf16, int32_t ld_hx, float* out, void* stream);
+
+/* ---- Flow encoder: the step before the solve (speech tokens -> mu).
+ *
+ * Replaces the flow encoder's chunk forward as the engine drives it (paths inside the reference):
+ *   t2w_encoder_create    the flow module's input_embedding, encoder (UpsampleConformerEncoderV2) and encoder_proj,
+ *                         weights cast once (the engine runs them in its activation dtype, token2wav_batch.py:184-206)
+ *   t2w_encode            BatchedToken2Wav._flow_encode + _encoder + _encoder_core + encoder_proj, and the cache trim
+ *                         of _flow_finish (token2wav_batch.py:42-79,365-399,402-478); a prompt setup
+ *                         (_setup_encoder_one / _setup_encoder_batched, token2wav_batch.py:556-616) is a window of a
+ *                         new stream with empty caches (its tokens plus the look-ahead silence tokens)
+ *   t2w_enc_stream_*      the per-stream flow_cache entries conformer_cnn_cache / conformer_att_cache
+ *                         (token2wav_batch.py:408-444): kept natively as key-slot lists over per-layer K/V pools
+ * Every window of a call has its own token count, cache length and final flag, so final windows never need the
+ * reference's merged-call padding (token2wav_batch.py:365-386). */
+typedef struct t2w_enc_config {
+  int32_t vocab, hidden, heads, head_dim, ffn, blocks1, blocks2, stride, lookahead, mel;
+  float eps_layer, eps_embed, eps_after, leaky_slope, max_period;
+} t2w_enc_config;
+
+/* Weight slots of t2w_encoder_create: T2W_E_COUNT global pointers, then (blocks1 + blocks2) * T2W_EL_COUNT per-layer
+ * pointers (encoders.0 .. encoders.{blocks1-1}, then up_encoders.0 ..; layer l at T2W_E_COUNT + l * T2W_EL_COUNT).
+ * fp32 device memory in the module's layout; names are the flow module's state-dict paths. */
+enum t2w_enc_weight_slot {
+  T2W_E_EMB = 0,                    /* input_embedding.weight [vocab, hidden] */
+  T2W_E_EMBED_W, T2W_E_EMBED_B,     /* encoder.embed.out.0 (Linear hidden -> hidden) */
+  T2W_E_EMBED_LN_W, T2W_E_EMBED_LN_B, /* encoder.embed.out.1 (LayerNorm, eps_embed) */
+  T2W_E_PL_C1_W, T2W_E_PL_C1_B,     /* encoder.pre_lookahead_layer.conv1 [hidden, hidden, lookahead + 1] */
+  T2W_E_PL_C2_W, T2W_E_PL_C2_B,     /* encoder.pre_lookahead_layer.conv2 [hidden, hidden, 3] */
+  T2W_E_UP_W, T2W_E_UP_B,           /* encoder.up_layer.conv [hidden, hidden, 2 stride + 1] */
+  T2W_E_UPEMB_W, T2W_E_UPEMB_B,     /* encoder.up_embed.out.0 */
+  T2W_E_UPEMB_LN_W, T2W_E_UPEMB_LN_B, /* encoder.up_embed.out.1 */
+  T2W_E_AFTER_W, T2W_E_AFTER_B,     /* encoder.after_norm (eps_after) */
+  T2W_E_PROJ_W, T2W_E_PROJ_B,       /* encoder_proj [mel, hidden] */
+  T2W_E_COUNT
+};
+enum t2w_enc_layer_slot {
+  T2W_EL_Q_W = 0, T2W_EL_Q_B, T2W_EL_K_W, T2W_EL_K_B, T2W_EL_V_W, T2W_EL_V_B, /* self_attn.linear_q / _k / _v */
+  T2W_EL_OUT_W, T2W_EL_OUT_B,       /* self_attn.linear_out */
+  T2W_EL_POS_W,                     /* self_attn.linear_pos.weight [hidden, hidden] (no bias) */
+  T2W_EL_POS_U, T2W_EL_POS_V,       /* self_attn.pos_bias_u / pos_bias_v [heads, head_dim] */
+  T2W_EL_FF1_W, T2W_EL_FF1_B, T2W_EL_FF2_W, T2W_EL_FF2_B, /* feed_forward.w_1 / w_2 */
+  T2W_EL_NMHA_W, T2W_EL_NMHA_B, T2W_EL_NFF_W, T2W_EL_NFF_B, /* norm_mha / norm_ff (eps_layer) */
+  T2W_EL_COUNT
+};
+
+typedef struct t2w_encoder t2w_encoder;
+
+/* Build an encoder on the current device.  max_frames bounds a window's frames and every attention's key count after
+ * the upsampling (a stream's second-stack cache plus stride * its window), and sizes the relative-position tables
+ * (linear_pos of the sinusoid at every relative position -(max_frames - 1) .. max_frames - 1, computed once here in
+ * fp32 and stored bf16).  n_slots1 / n_slots2: key slots of each first- / second-stack layer's K/V pool; n_streams:
+ * live streams at most.  `stream` orders the set-up work; the call synchronises it before returning. */
+T2W_API int t2w_encoder_create(const t2w_enc_config* cfg, const float* const* weights, int32_t n_weights,
+                               int32_t max_frames, int32_t n_slots1, int32_t n_slots2, int32_t n_streams, void* stream,
+                               t2w_encoder** out);
+T2W_API int t2w_encoder_destroy(t2w_encoder* e);
+
+/* A stream with empty caches (a prompt setup's state: no keys, zero conv caches, zeroed on `stream`) and trim length
+ * `keep` (the prompt's mel frames, stride * its tokens).  T2W_ERR_EXHAUSTED when n_streams are live. */
+T2W_API int t2w_enc_stream_new(t2w_encoder* e, int32_t keep, void* stream, int32_t* handle);
+T2W_API int t2w_enc_stream_release(t2w_encoder* e, int32_t handle);
+/* Cached key frames of the first and second stack (the reference cache's time length is 2 * keys1 = keys2 after a
+ * setup; see t2w_encode for how they advance) and the trim length. */
+T2W_API int t2w_enc_stream_get(const t2w_encoder* e, int32_t handle, int32_t* keys1, int32_t* keys2, int32_t* keep);
+/* Key slots in use in the first- and second-stack pools, live streams. */
+T2W_API int t2w_enc_usage(const t2w_encoder* e, int32_t* slots1, int32_t* slots2, int32_t* streams);
+
+/* One window per stream.  Window i has n_tokens[i] tokens: its T_i = n_tokens[i] - lookahead frames plus the
+ * look-ahead tokens, or, when final[i] != 0, T_i = n_tokens[i] frames followed by `lookahead` zero frames (the
+ * reference's last_chunk padding).  A window whose caches are kept (final[i] == 0) needs T_i >= 2.  mu receives
+ * stride * T_i rows of `mel` floats per window, windows in call order (encoder_proj of the after_norm output,
+ * token-major: the rows t2w_solve_cached takes as mu).  After the call each stream's caches have advanced as the
+ * reference advances them: conv caches = the last frames of [cache | new]; first stack keys = the first
+ * min(K1, (keep + 100) / 2) of [cached | new] when 2 K1 > keep + 100, else all K1 (the reference's first-stack
+ * cache is tiled twice along time, cut to its first keep and last 100 frames, and read back as the first half);
+ * second stack keys = [cached | new] cut to the first keep and last 100 (token2wav_batch.py:33-39,395).
+ * tokens: host, the windows' tokens concatenated (each < vocab).  Asynchronous on `stream`; the host arrays are read
+ * before the call returns. */
+typedef struct t2w_enc_batch {
+  int32_t n_streams;
+  const int32_t* handle;   /* host [n] stream handles, pairwise distinct */
+  const int32_t* n_tokens; /* host [n] */
+  const uint8_t* final;    /* host [n] */
+  const int32_t* tokens;   /* host [sum n_tokens] */
+  float* mu;               /* device [sum stride * T_i, mel] */
+} t2w_enc_batch;
+T2W_API size_t t2w_enc_workspace_bytes(const t2w_encoder* e, const t2w_enc_batch* b);
+T2W_API int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* workspace, size_t workspace_bytes, void* stream);
+/* Synchronise the encoder's error word: T2W_OK, or T2W_ERR_TIMEOUT if a kernel gave up on a wait (then cleared). */
+T2W_API int t2w_enc_check(t2w_encoder* e);
+
+/* Single encoder kernels (test entry points).
+ * Relative-position attention (RelPositionMultiHeadedAttention of the conformer layers with the zero-pad rel_shift):
+ * for sequence s with T queries at rows q_row[s] .. of qkv4 (bf16 [rows, 4 H]: [q + pos_bias_u | q + pos_bias_v | k | v]
+ * per row, H = heads * 64) and K keys, key j from pool row kv_idx[kv_off[s] + j] (bf16 [pool_rows, 2 H]: [k | v]),
+ * query i at position K - T + i: score = ((q_i + u) . k_j + (q_i + v) . P[(K - T + i) - j]) / 8 over all K keys, with
+ * P the relative-position table (bf16 [2 max_frames - 1, H], row r + max_frames - 1 = linear_pos(pe(r))).
+ * out bf16 [rows, H].  q_row / T / K / kv_off: host [n_seq]; kv_idx: host [n_idx].  They are copied from host memory
+ * that lives only for the call, so a stream under capture is refused (T2W_ERR_INVALID, nothing enqueued). */
+T2W_API int t2w_enc_relattn(const void* qkv4_bf16, int32_t rows, int32_t heads, const void* pool_bf16, int32_t pool_rows,
+                            const void* pos_bf16, int32_t max_frames, int32_t n_seq, const int32_t* q_row,
+                            const int32_t* T, const int32_t* K, const int32_t* kv_off, const int32_t* kv_idx,
+                            int32_t n_idx, void* out_bf16, void* stream);
+/* The relative-position table of t2w_encoder_create: pos[r + max_frames - 1] = bf16(W pe(r)) for |r| < max_frames,
+ * W fp32 [H, H] (linear_pos.weight), pe(r) = [sin(r w_0), cos(r w_0), sin(r w_1), ...], w_m = max_period^(-2m / H). */
+T2W_API int t2w_enc_pos_table(const float* w, int32_t H, int32_t max_frames, float max_period, void* pos_bf16,
+                              void* stream);
+/* Row LayerNorm of the encoder: y = LN(x) * w + b (eps; w, b fp32 [C]) for fp32 x [rows, C]; writes fp32 y into
+ * out_f32 (may alias x) and / or bf16 y into out_bf16 (either may be NULL); rows whose pad[r] != 0 get zeros. */
+T2W_API int t2w_enc_ln(const float* x, const float* w, const float* b, float eps, int32_t rows, int32_t C, float* out_f32,
+                       void* out_bf16, const uint8_t* pad, void* stream);
 
 #ifdef __cplusplus
 }

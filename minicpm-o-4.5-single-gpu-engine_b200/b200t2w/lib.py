@@ -18,7 +18,7 @@ STATUS = {-1: "invalid argument or shape", -2: "CUDA error", -3: "out of device 
           -7: "Token2Wav cache pool exhausted (key slots, conv-cache row slots or cache handles)"}
 PREC = {"bf16": 0, "fp8": 1}
 FLAG_GRAPH = 1
-EPI = {"f32": 0, "bf16": 1, "gelu": 2, "resid": 3, "qkv": 4, "gelu_fp8": 8}
+EPI = {"f32": 0, "bf16": 1, "gelu": 2, "resid": 3, "qkv": 4, "silu": 5, "leaky": 6, "gelu_fp8": 8}
 KERNEL_CLASSES = ["pack", "gemm_in", "ln_mod", "gemm_qkv", "attn", "gemm_proj", "gemm_conv1", "ln_mish", "gemm_conv2",
                   "gemm_fc1", "gemm_fc2", "gemm_final", "euler"]
 W_GLOBAL = ["estimator.t_embedder.mlp.0.weight", "estimator.t_embedder.mlp.0.bias", "estimator.t_embedder.mlp.2.weight",
@@ -66,6 +66,35 @@ class CachedBatch(ctypes.Structure):
                 ("chunk_len", ctypes.POINTER(ctypes.c_int32)), ("keep", ctypes.POINTER(ctypes.c_uint8)),
                 ("noise", ctypes.c_void_p), ("noise_frames", ctypes.c_int32), ("temperature", ctypes.c_float),
                 ("mu", ctypes.c_void_p), ("cond", ctypes.c_void_p), ("spk", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
+
+class EncConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("vocab", "hidden", "heads", "head_dim", "ffn", "blocks1", "blocks2",
+                                              "stride", "lookahead", "mel")] + \
+               [(n, ctypes.c_float) for n in ("eps_layer", "eps_embed", "eps_after", "leaky_slope", "max_period")]
+
+
+class EncBatch(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_int32), ("handle", ctypes.POINTER(ctypes.c_int32)),
+                ("n_tokens", ctypes.POINTER(ctypes.c_int32)), ("final", ctypes.POINTER(ctypes.c_uint8)),
+                ("tokens", ctypes.POINTER(ctypes.c_int32)), ("mu", ctypes.c_void_p)]
+
+
+# Flow-encoder weight slots (include/t2w_b200.h t2w_enc_weight_slot / t2w_enc_layer_slot): state-dict paths of the flow
+# module (input_embedding, encoder.*, encoder_proj).
+E_GLOBAL = ["input_embedding.weight", "encoder.embed.out.0.weight", "encoder.embed.out.0.bias",
+            "encoder.embed.out.1.weight", "encoder.embed.out.1.bias", "encoder.pre_lookahead_layer.conv1.weight",
+            "encoder.pre_lookahead_layer.conv1.bias", "encoder.pre_lookahead_layer.conv2.weight",
+            "encoder.pre_lookahead_layer.conv2.bias", "encoder.up_layer.conv.weight", "encoder.up_layer.conv.bias",
+            "encoder.up_embed.out.0.weight", "encoder.up_embed.out.0.bias", "encoder.up_embed.out.1.weight",
+            "encoder.up_embed.out.1.bias", "encoder.after_norm.weight", "encoder.after_norm.bias",
+            "encoder_proj.weight", "encoder_proj.bias"]
+E_LAYER = ["self_attn.linear_q.weight", "self_attn.linear_q.bias", "self_attn.linear_k.weight",
+           "self_attn.linear_k.bias", "self_attn.linear_v.weight", "self_attn.linear_v.bias",
+           "self_attn.linear_out.weight", "self_attn.linear_out.bias", "self_attn.linear_pos.weight",
+           "self_attn.pos_bias_u", "self_attn.pos_bias_v", "feed_forward.w_1.weight", "feed_forward.w_1.bias",
+           "feed_forward.w_2.weight", "feed_forward.w_2.bias", "norm_mha.weight", "norm_mha.bias", "norm_ff.weight",
+           "norm_ff.bias"]
 
 
 _P = ctypes.c_void_p
@@ -120,6 +149,20 @@ _SIGS = {
     "t2w_ln_mish_e4m3": ([_P, _P, _P, _F, _I, _I, _P, _P, _I, ctypes.c_int64, _P, _P], ctypes.c_int),
     "t2w_attn_varlen_e4m3": ([_P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _P, _P, _P],
                              ctypes.c_int),
+    "t2w_encoder_create": ([ctypes.POINTER(EncConfig), ctypes.POINTER(_P), _I, _I, _I, _I, _I, _P, ctypes.POINTER(_P)],
+                           ctypes.c_int),
+    "t2w_encoder_destroy": ([_P], ctypes.c_int),
+    "t2w_enc_stream_new": ([_P, _I, _P, ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_enc_stream_release": ([_P, _I], ctypes.c_int),
+    "t2w_enc_stream_get": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_enc_usage": ([_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_enc_workspace_bytes": ([_P, ctypes.POINTER(EncBatch)], ctypes.c_size_t),
+    "t2w_encode": ([_P, ctypes.POINTER(EncBatch), _P, ctypes.c_size_t, _P], ctypes.c_int),
+    "t2w_enc_check": ([_P], ctypes.c_int),
+    "t2w_enc_relattn": ([_P, _I, _I, _P, _I, _P, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                         ctypes.POINTER(_I), ctypes.POINTER(_I), _I, _P, _P], ctypes.c_int),
+    "t2w_enc_pos_table": ([_P, _I, _I, _F, _P, _P], ctypes.c_int),
+    "t2w_enc_ln": ([_P, _P, _P, _F, _I, _I, _P, _P, _P, _P], ctypes.c_int),
     "t2w_gemm_e4m3": ([_P, _I, _I, _P, _I, ctypes.c_int64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P,
                        ctypes.POINTER(_P), _F, _P], ctypes.c_int),
 }

@@ -324,6 +324,8 @@ T2W_DEV float mish(float y) {
   const float n = e * (e + 2.f);
   return y * __fdividef(n, n + 2.f);
 }
+// SiLU (swish) y sigmoid(y) = y / (1 + e^-y); for very negative y the exponential overflows to inf and y / inf = -0.
+T2W_DEV float silu(float y) { return __fdividef(y, 1.f + __expf(-y)); }
 // ---------------------------------------------------------------- cross-CTA flags (gpu scope)
 T2W_DEV int ld_acquire_gpu(const int* p) {
   int v;

@@ -165,6 +165,14 @@ T2W_DEV void epilogue_math(const DevArgs& p, int n0, int b, uint32_t (&raw)[64])
     } else if constexpr (EPI == T2W_EPI_GELU) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = make_float2(gelu_tanh(v[i].x), gelu_tanh(v[i].y));
+    } else if constexpr (EPI == T2W_EPI_SILU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = make_float2(silu(v[i].x), silu(v[i].y));
+    } else if constexpr (EPI == T2W_EPI_LEAKY) {
+      const float slope = p.qk_eps;  // the leaky ReLU's negative slope travels in the q/k-norm eps field
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        v[i] = make_float2(v[i].x > 0.f ? v[i].x : slope * v[i].x, v[i].y > 0.f ? v[i].y : slope * v[i].y);
     }
 #pragma unroll
     for (int i = 0; i < 32; ++i) raw[i] = pack_bf16x2(v[i].x, v[i].y);
@@ -799,6 +807,8 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
       case T2W_EPI_F32: return launch_pair_impl<T2W_EPI_F32>(a, st, tmA, tmW, tmC);
       case T2W_EPI_BF16: return launch_pair_impl<T2W_EPI_BF16>(a, st, tmA, tmW, tmC);
       case T2W_EPI_GELU: return launch_pair_impl<T2W_EPI_GELU>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_SILU: return launch_pair_impl<T2W_EPI_SILU>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_LEAKY: return launch_pair_impl<T2W_EPI_LEAKY>(a, st, tmA, tmW, tmC);
       case T2W_EPI_QKV: return launch_pair_impl<T2W_EPI_QKV>(a, st, tmA, tmW, tmC);
       case T2W_EPI_RESID: return launch_pair_impl<T2W_EPI_RESID>(a, st, tmA, tmW, tmC);
       default: return T2W_ERR_INVALID;
@@ -809,6 +819,8 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
       case T2W_EPI_F32: return launch_impl<256, T2W_EPI_F32, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_BF16: return launch_impl<256, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_GELU: return launch_impl<256, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_SILU: return launch_impl<256, T2W_EPI_SILU, true>(a, st, tmA, tmW, tmC);
+      case T2W_EPI_LEAKY: return launch_impl<256, T2W_EPI_LEAKY, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_QKV: return launch_impl<256, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
       case T2W_EPI_RESID: return launch_impl<256, T2W_EPI_RESID, true>(a, st, tmA, tmW, tmC);
       default: return T2W_ERR_INVALID;
@@ -818,6 +830,8 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, const CUtensorMap* tmA, cons
     case T2W_EPI_F32: return launch_impl<128, T2W_EPI_F32, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_BF16: return launch_impl<128, T2W_EPI_BF16, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_GELU: return launch_impl<128, T2W_EPI_GELU, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_SILU: return launch_impl<128, T2W_EPI_SILU, true>(a, st, tmA, tmW, tmC);
+    case T2W_EPI_LEAKY: return launch_impl<128, T2W_EPI_LEAKY, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_QKV: return launch_impl<128, T2W_EPI_QKV, true>(a, st, tmA, tmW, tmC);
     case T2W_EPI_RESID: return launch_impl<128, T2W_EPI_RESID, true>(a, st, tmA, tmW, tmC);
     default: return T2W_ERR_INVALID;

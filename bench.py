@@ -358,6 +358,67 @@ def reference_gpu_fastdit(wl: Workload, steps: int, warm: int, dev) -> dict:
             "graph_calls": dict(fd.counts)}
 
 
+def reference_gpu_encoder(n: int, prompt_tokens: int, steps: int, warm: int, dev, batched_io: bool) -> dict:
+    """The reference's own flow-encoder path on this GPU in fp16, unmodified: ``BatchedToken2Wav._setup_encoder_batched``
+    for ``n`` prompts (one padded batch), then steady windows of 25 + 3 tokens through ``_flow_encode``'s steps
+    (``input_embedding``, ``_encoder`` with left-padded caches, ``encoder_proj``) and ``_flow_finish``'s trim
+    (engine/runtime/token2wav_batch.py:365-478,566-616), over the restated flow module.  ``batched_io``: the engine's
+    ``t2w_encoder_batched_io`` option (Triton cache gather / scatter, engine/runtime/encoder_io.py)."""
+    _reference_modules()
+    from engine.runtime import token2wav_batch as tb
+
+    from b200t2w.config import ENCODER
+    from oracle import encoder_oracle as eo
+
+    flow = eo.build_flow(ENCODER, seed=0).to(dev).half()
+    bt = tb.BatchedToken2Wav.__new__(tb.BatchedToken2Wav)
+    bt.flow, bt.fast, bt.enc_graphs, bt.encoder_batched_io = flow, None, None, batched_io
+    bt.profile = bt.trace = None
+    g = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, ENCODER.vocab, (1, prompt_tokens), generator=g).to(dev) for _ in range(n)]
+    feats = [(p, None, None, None, None) for p in prompts]
+    wins = [torch.randint(0, ENCODER.vocab, (n, 28), generator=g).to(dev) for _ in range(4)]
+    keep = 2 * prompt_tokens
+
+    class St:  # the parts of StreamState the encoder driver reads
+        def __init__(self, cnn, att):
+            self.flow_cache = {"conformer_cnn_cache": cnn, "conformer_att_cache": att}
+            self.prompt = type("Prompt", (), {"mels": torch.zeros(1, keep, 1)})()
+
+    st = torch.cuda.current_stream(dev)
+    with torch.inference_mode():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        encs = bt._setup_encoder_batched(feats)
+        e1.record(st)
+        e1.synchronize()
+        setup_ms = e0.elapsed_time(e1)
+        sts = [St(cnn, att) for _, cnn, att in encs]
+
+        def call(k):
+            h = flow.encoder_proj(bt._encoder(sts, flow.input_embedding(wins[k % 4]), False))
+            for s in sts:
+                c = s.flow_cache
+                c["conformer_att_cache"] = tb._trim(c["conformer_att_cache"], keep, 3)
+            return h
+
+        for k in range(max(warm, 4)):
+            call(k)
+        torch.cuda.synchronize(dev)
+        ms = []
+        for k in range(steps):
+            e0.record(st)
+            call(k)
+            e1.record(st)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+    m = statistics.median(ms)
+    return {"path": "BatchedToken2Wav._encoder + encoder_proj + _flow_finish trim (token2wav_batch.py:365-478), fp16, "
+                    + ("encoder_batched_io" if batched_io else "per-stream cache I/O"),
+            "streams": n, "ms_per_call": m, "mu_frames_per_s": n * 50 / (m / 1000), "setup_ms": setup_ms,
+            "setup_mu_frames_per_s": n * 2 * prompt_tokens / (setup_ms / 1000), "timed_calls": steps}
+
+
 def reference_gpu_arm(a) -> None:
     """``--impl reference --reference-gpu``: one JSON record of the reference's GPU PyTorch path at the target shape
     and at config 2 (a child process of the default arm; nothing of this build's library is loaded here)."""
@@ -378,6 +439,13 @@ def reference_gpu_arm(a) -> None:
                 rec[name + "_fastdit"] = reference_gpu_fastdit(wl, steps=3, warm=2, dev=dev)
             except Exception as e:
                 rec[name + "_fastdit"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    for io in (False, True):
+        key = "encoder_64" + ("_batched_io" if io else "")
+        try:
+            rec[key] = reference_gpu_encoder(64, 150, steps=5, warm=4, dev=dev, batched_io=io)
+        except Exception as e:
+            rec[key] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
     print(json.dumps(rec), flush=True)
 
 
@@ -752,6 +820,11 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
         w_ref = (ref_gpu.get("w32_fastdit") or {}).get("window_ms")
         if w_ours and w_ref:  # steady-state windows, 32 per call: FastDiT's graph-replayed window vs this build's call
             ref_gpu["steady_32_speedup_vs_fastdit_window"] = w_ref / w_ours
+        e_ours = (sub.get("encoder_64") or {}).get("ms_per_call")
+        for k in ("encoder_64", "encoder_64_batched_io"):  # the flow encoder's steady window call, 64 streams
+            e_ref = (ref_gpu.get(k) or {}).get("ms_per_call")
+            if e_ours and e_ref:
+                ref_gpu.setdefault("encoder_speedup", {})[k] = e_ref / e_ours
         if a.workload == "c2":
             ours["c2"] = statistics.median(batch_ms)
         for k, v in ours.items():

@@ -55,6 +55,8 @@ class RelPositionalEncoding(nn.Module):
         super().__init__()
         self.d, self.max_period = d, max_period
         self.xscale = math.sqrt(d)
+        # follows the module's device and dtype (.to / .half), as the encoding buffer of the real module does
+        self.register_buffer("anchor", torch.zeros(0), persistent=False)
 
     def position_encoding(self, offset, size: int) -> torch.Tensor:
         r = torch.arange(size - 1, -size, -1, dtype=torch.float32)[:, None]
@@ -62,7 +64,7 @@ class RelPositionalEncoding(nn.Module):
         pe = torch.zeros(2 * size - 1, self.d)
         pe[:, 0::2] = torch.sin(r * w)
         pe[:, 1::2] = torch.cos(r * w)
-        return pe[None]
+        return pe[None].to(self.anchor.device, self.anchor.dtype)
 
     def forward(self, x: torch.Tensor, offset=0):
         return x * self.xscale, self.position_encoding(offset, x.shape[1])

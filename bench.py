@@ -545,7 +545,7 @@ def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, see
     g = torch.Generator().manual_seed(seed)
     flow = eo.build_flow(ENCODER, seed=0)
     enc = B200FlowEncoder.from_flow(flow, device=dev, max_frames=2048, n_slots1=n * 512, n_slots2=n * 1024,
-                                    n_streams=n)
+                                    n_streams=n, use_graphs=True)
     prompts = [torch.randint(0, ENCODER.vocab, (prompt_tokens,), generator=g) for _ in range(n)]
     st = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -563,7 +563,7 @@ def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, see
         enc.encode_packed(handles, wins[k % 4], [False] * n, out=out)
         host_out.copy_(out, non_blocking=True)
 
-    for k in range(max(warmup, 4)):  # caches reach the trimmed length (keep + 100) after a few windows
+    for k in range(max(warmup, 4) + 2):  # caches reach the trimmed length after a few windows; then the capture
         call(k)
     torch.cuda.synchronize(dev)
     k1, k2, keep = enc.stream_info(handles[0])
@@ -581,7 +581,8 @@ def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, see
            "frac_of_bf16_peak": flop / (ms / 1000) / 1e12 / peak_tf,
            "setup_ms": setup_ms, "setup_mu_frames_per_s": n * 2 * prompt_tokens / (setup_ms / 1000),
            "h2d_bytes_per_call": n * W * 4, "d2h_bytes_per_call": n * 2 * T * ENCODER.mel * 4,
-           "note": "setup_ms is the first call (includes its workspace allocation)"}
+           "calls": enc.counts, "note": "setup_ms is the first call (includes its workspace allocation); steady "
+                                           "calls replay one CUDA graph per launch structure"}
     if cpu:
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)

@@ -426,6 +426,10 @@ T2W_API int t2w_encoder_destroy(t2w_encoder* e);
  * `keep` (the prompt's mel frames, stride * its tokens).  T2W_ERR_EXHAUSTED when n_streams are live. */
 T2W_API int t2w_enc_stream_new(t2w_encoder* e, int32_t keep, void* stream, int32_t* handle);
 T2W_API int t2w_enc_stream_release(t2w_encoder* e, int32_t handle);
+/* A new stream holding a copy of a stream's caches (keys in new slots of every layer's pool, the conv-cache frames,
+ * keep), enqueued on `stream`: the copy a request's stream takes of its prompt's flow_cache when the prompt is not
+ * adopted (BatchedToken2Wav.new_stream, token2wav_batch.py:267-279). */
+T2W_API int t2w_enc_stream_clone(t2w_encoder* e, int32_t handle, void* stream, int32_t* out);
 /* Cached key frames of the first and second stack (the reference cache's time length is 2 * keys1 = keys2 after a
  * setup; see t2w_encode for how they advance) and the trim length. */
 T2W_API int t2w_enc_stream_get(const t2w_encoder* e, int32_t handle, int32_t* keys1, int32_t* keys2, int32_t* keep);
@@ -452,7 +456,14 @@ typedef struct t2w_enc_batch {
   float* mu;               /* device [sum stride * T_i, mel] */
 } t2w_enc_batch;
 T2W_API size_t t2w_enc_workspace_bytes(const t2w_encoder* e, const t2w_enc_batch* b);
-T2W_API int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* workspace, size_t workspace_bytes, void* stream);
+/* flags T2W_FLAG_GRAPH: replay a CUDA graph per launch structure (the sizes of the call's lists, the workspace and mu
+ * buffers), captured the second time such a key is seen (the reference captures its encoder per bucket,
+ * EncoderGraphs, token2wav_batch.py:206,413); keep the workspace and mu buffers fixed between calls so keys repeat.
+ * A stream under capture with T2W_FLAG_GRAPH is refused (T2W_ERR_INVALID). */
+T2W_API int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* workspace, size_t workspace_bytes, uint32_t flags,
+                       void* stream);
+/* Counters: graph replays, graph captures, eager calls. */
+T2W_API int t2w_enc_counts(const t2w_encoder* e, int64_t* replays, int64_t* captures, int64_t* eager);
 /* Synchronise the encoder's error word: T2W_OK, or T2W_ERR_TIMEOUT if a kernel gave up on a wait (then cleared). */
 T2W_API int t2w_enc_check(t2w_encoder* e);
 

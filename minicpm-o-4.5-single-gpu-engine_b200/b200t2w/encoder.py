@@ -10,7 +10,9 @@ in the library (a stream is a handle; keys live in per-layer pools), so a call p
 * ``encode(handles, windows, finals)``: one window per stream (``_flow_encode``'s ``mu`` entries ``[mel, 2 T]``); the
   caches advance and are trimmed as ``_flow_finish`` trims them (``:388-399``).
 
-All arithmetic runs in the CUDA library; a missing library or a non-sm_100 device raises.
+Calls go through the torch custom ops ``torch.ops.b200t2w.enc_workspace_bytes`` / ``encode`` on the current torch
+stream; the encoder object and its streams through the ctypes binding.  All arithmetic runs in the CUDA library; a
+missing library or a non-sm_100 device raises.
 """
 
 from __future__ import annotations
@@ -21,6 +23,7 @@ from dataclasses import replace
 import torch
 
 from . import lib as L
+from . import ops as O
 from .config import ENCODER, EncoderConfig
 
 SILENCE_TOKEN = 4218  # engine/models/token2wav.py:39: the look-ahead tokens that close a prompt
@@ -56,7 +59,7 @@ class B200FlowEncoder:
     """
 
     def __init__(self, cfg: EncoderConfig, weights: dict, device="cuda", max_frames: int = 2048,
-                 n_slots1: int = 1 << 16, n_slots2: int = 1 << 17, n_streams: int = 1024):
+                 n_slots1: int = 1 << 16, n_slots2: int = 1 << 17, n_streams: int = 1024, use_graphs: bool = False):
         cfg.validate_for_kernels()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -86,6 +89,7 @@ class B200FlowEncoder:
         self._w = None  # the library holds its own copies
         self.handle = h
         self.max_frames = max_frames
+        self.use_graphs = use_graphs
         self._ws = None
 
     @classmethod
@@ -110,6 +114,14 @@ class B200FlowEncoder:
         h = ctypes.c_int32()
         with torch.cuda.device(self.device):
             L.call("t2w_enc_stream_new", self.handle, int(keep),
+                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(h))
+        return h.value
+
+    def clone(self, handle: int) -> int:
+        """A new stream with a copy of ``handle``'s caches (a request's stream from a prompt it does not adopt)."""
+        h = ctypes.c_int32()
+        with torch.cuda.device(self.device):
+            L.call("t2w_enc_stream_clone", self.handle, int(handle),
                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(h))
         return h.value
 
@@ -146,19 +158,17 @@ class B200FlowEncoder:
             out = torch.empty(n_out, self.cfg.mel, dtype=torch.float32, device=self.device)
         elif out.shape != (n_out, self.cfg.mel) or out.dtype != torch.float32 or not out.is_contiguous():
             raise ValueError(f"out must be a contiguous fp32 [{n_out}, {self.cfg.mel}] tensor")
-        hs = L.i32_array(handles)
-        nt = L.i32_array([len(w) for w in toks])
-        fin = (ctypes.c_uint8 * n)(*[1 if f else 0 for f in finals])
-        tk = L.i32_array(flat if flat else [0])
-        b = L.EncBatch(n, hs, nt, fin, tk, ctypes.c_void_p(out.data_ptr()))
+        h = int(self.handle.value)
+        hs = [int(x) for x in handles]
+        nt = [len(w) for w in toks]
+        fin = [1 if f else 0 for f in finals]
         with torch.cuda.device(self.device):
-            need = self.lib.t2w_enc_workspace_bytes(self.handle, ctypes.byref(b))
+            need = O.call("enc_workspace_bytes", h, hs, nt, fin, flat)
             if need == 0:
                 raise L.T2WError("t2w_enc_workspace_bytes", -1)
             if self._ws is None or self._ws.numel() < need:
                 self._ws = torch.empty(need + need // 4, dtype=torch.uint8, device=self.device)
-            L.call("t2w_encode", self.handle, ctypes.byref(b), ctypes.c_void_p(self._ws.data_ptr()),
-                   ctypes.c_size_t(self._ws.numel()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            O.call("encode", h, hs, nt, fin, flat, out, self._ws, bool(self.use_graphs))
         return out
 
     def encode(self, handles, windows, finals) -> list:
@@ -186,6 +196,13 @@ class B200FlowEncoder:
                 self.release(h)
             raise
         return handles, mus
+
+    @property
+    def counts(self) -> dict:
+        """Calls so far: graph replays, graph captures, eager calls."""
+        r, c, e = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        L.call("t2w_enc_counts", self.handle, ctypes.byref(r), ctypes.byref(c), ctypes.byref(e))
+        return {"replays": r.value, "captures": c.value, "eager": e.value}
 
     def check(self) -> None:
         L.check("t2w_enc_check", self.lib.t2w_enc_check(self.handle))

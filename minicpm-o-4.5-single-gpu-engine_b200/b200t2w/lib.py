@@ -154,10 +154,13 @@ _SIGS = {
     "t2w_encoder_destroy": ([_P], ctypes.c_int),
     "t2w_enc_stream_new": ([_P, _I, _P, ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_enc_stream_release": ([_P, _I], ctypes.c_int),
+    "t2w_enc_stream_clone": ([_P, _I, _P, ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_enc_stream_get": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_enc_usage": ([_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_enc_workspace_bytes": ([_P, ctypes.POINTER(EncBatch)], ctypes.c_size_t),
-    "t2w_encode": ([_P, ctypes.POINTER(EncBatch), _P, ctypes.c_size_t, _P], ctypes.c_int),
+    "t2w_encode": ([_P, ctypes.POINTER(EncBatch), _P, ctypes.c_size_t, ctypes.c_uint32, _P], ctypes.c_int),
+    "t2w_enc_counts": ([_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+                        ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "t2w_enc_check": ([_P], ctypes.c_int),
     "t2w_enc_relattn": ([_P, _I, _I, _P, _I, _P, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
                          ctypes.POINTER(_I), ctypes.POINTER(_I), _I, _P, _P], ctypes.c_int),

@@ -47,4 +47,5 @@ def call(name: str, *args):
 
 
 OPS = ("create", "destroy", "workspace_bytes", "solve_packed", "slots_create", "slots_destroy", "cached_workspace_bytes",
-       "solve_cached", "solve_slots", "ln_mod", "add_ln_mod", "ln_mish", "gemm", "attn_varlen", "euler_cfg")
+       "solve_cached", "solve_slots", "ln_mod", "add_ln_mod", "ln_mish", "gemm", "attn_varlen", "euler_cfg",
+       "enc_workspace_bytes", "encode")

@@ -6,9 +6,11 @@ calls of ``BatchedToken2Wav`` (``engine/runtime/token2wav_batch.py:221-309,508-5
 ``release_prompt``, and ``decode`` (one window per request -> samples).  ``B200Token2Wav`` provides those calls with the
 DiT/CFM solve on ``B200FastDiT``: a setup solves the prompt's frames with the prompt mel as condition and keeps its keys
 (trim length = the prompt's mel frames, as ``setup_many`` sets ``c.keep``), a window solves against the stream's caches
-and keeps its keys unless it is the stream's last (``keep = not last``, as ``_flow_encode`` sets it).  The stages on
-either side of the solve — the flow encoder (tokens -> ``mu``) and the HiFT vocoder (mel -> samples) — are outside
-this build; they are passed in as callables.
+and keeps its keys unless it is the stream's last (``keep = not last``, as ``_flow_encode`` sets it).  The flow encoder
+(tokens -> ``mu``) is either this build's ``B200FlowEncoder`` — then every prompt and request owns an encoder stream
+(its conformer caches), set up, copied or adopted, advanced and released with the DiT caches, and a decode call encodes
+all its windows in one call, as ``_flow_encode`` does — or any callable ``tokens -> mu``.  The HiFT vocoder (mel ->
+samples) is outside this build and is passed in as a callable.
 
 ``MultiGpuToken2Wav`` is the same surface over one ``B200Token2Wav`` per GPU, in place of the reference worker's single
 device (``torch.cuda.set_device(0)``, ``t2w_worker.py:804``): a request is placed on the least-loaded GPU when its prompt
@@ -29,11 +31,13 @@ from .scheduler import GpuPlacement
 
 @dataclass
 class B200Prompt:
-    """A set-up prompt: its estimator caches (until a stream adopts them), speaker vector and mel frames."""
+    """A set-up prompt: its estimator caches (until a stream adopts them), speaker vector and mel frames, and its flow
+    encoder stream when the encoder is a ``B200FlowEncoder``."""
     cache: object
     spk: torch.Tensor  # [1, mel] after the flow's speaker affine layer
     frames: int
     device: int = 0
+    enc: int | None = None
 
 
 @dataclass
@@ -44,6 +48,7 @@ class B200Stream:
     noise_seed: int = 0
     chunks: int = 0
     device: int = 0
+    enc: int | None = None
 
 
 class B200Token2Wav:
@@ -55,53 +60,79 @@ class B200Token2Wav:
     worker's ``setup_calls`` reads ``feats[3].shape[1]``."""
 
     def __init__(self, fast, encode, vocode, device_index: int = 0):
+        from .encoder import B200FlowEncoder
+
         self.fast, self.encode, self.vocode, self.device_index = fast, encode, vocode, device_index
+        self.flow = encode if isinstance(encode, B200FlowEncoder) else None
         self.dev = fast.device
+
+    @staticmethod
+    def _tokens(t) -> list:
+        return [int(x) for x in (t.flatten().tolist() if isinstance(t, torch.Tensor) else t)]
 
     def setup_many(self, feats_list: list) -> list:
         caches = [self.fast.new_cache() for _ in feats_list]
-        mus, conds, spks = [], [], []
-        for c, f in zip(caches, feats_list):
-            mel = f[3][0].t()  # [mel, frames]
-            c.keep = int(mel.shape[1])  # the trim length: the prompt's mel frames (token2wav_batch.py:544)
-            mu = self.encode(f[0])
-            if int(mu.shape[1]) != int(mel.shape[1]):
-                raise ValueError(f"prompt: the encoder gave {mu.shape[1]} frames for a {mel.shape[1]}-frame mel")
-            mus.append(mu)
-            conds.append(mel)
-            spks.append(f[2].reshape(1, -1))
-        spk = torch.cat(spks).to(self.dev, torch.float32)
+        handles = []
         try:
+            if self.flow is not None:  # every prompt through a new encoder stream, one call
+                handles, enc_mus = self.flow.setup([self._tokens(f[0]) for f in feats_list])
+            mus, conds, spks = [], [], []
+            for i, (c, f) in enumerate(zip(caches, feats_list)):
+                mel = f[3][0].t()  # [mel, frames]
+                c.keep = int(mel.shape[1])  # the trim length: the prompt's mel frames (token2wav_batch.py:544)
+                mu = enc_mus[i] if self.flow is not None else self.encode(f[0])
+                if int(mu.shape[1]) != int(mel.shape[1]):
+                    raise ValueError(f"prompt: the encoder gave {mu.shape[1]} frames for a {mel.shape[1]}-frame mel")
+                mus.append(mu)
+                conds.append(mel)
+                spks.append(f[2].reshape(1, -1))
+            spk = torch.cat(spks).to(self.dev, torch.float32)
             self.fast.solve(caches, mus, spk, conds, [True] * len(caches))
         except Exception:
             for c in caches:
                 self.fast.release(c)
+            for h in handles:
+                self.flow.release(h)
             raise
-        return [B200Prompt(c, spk[i:i + 1], int(m.shape[1]), self.device_index) for i, (c, m) in enumerate(zip(caches, conds))]
+        return [B200Prompt(c, spk[i:i + 1], int(m.shape[1]), self.device_index, handles[i] if handles else None)
+                for i, (c, m) in enumerate(zip(caches, conds))]
 
     def new_stream(self, prompt: B200Prompt, noise_seed: int = 0, adopt: bool = False) -> B200Stream:
         if adopt:  # the prompt is used once: its caches become the stream's
             cache, prompt.cache = prompt.cache, None
+            enc, prompt.enc = prompt.enc, None
         else:
             cache = self.fast.clone(prompt.cache)
-        return B200Stream(cache, prompt.spk, noise_seed, 0, self.device_index)
+            enc = self.flow.clone(prompt.enc) if prompt.enc is not None else None
+        return B200Stream(cache, prompt.spk, noise_seed, 0, self.device_index, enc)
 
     def release_stream(self, st: B200Stream) -> None:
         if st is not None and st.cache is not None:
             self.fast.release(st.cache)
             st.cache = None
+        if st is not None and st.enc is not None:
+            self.flow.release(st.enc)
+            st.enc = None
 
     def release_prompt(self, p: B200Prompt) -> None:
         if p is not None and p.cache is not None:
             self.fast.release(p.cache)
             p.cache = None
+        if p is not None and p.enc is not None:
+            self.flow.release(p.enc)
+            p.enc = None
 
     def decode(self, items: list) -> list:
-        """``items[i] = (stream, window tokens, last)`` -> samples per item (one solve for every window of the call)."""
+        """``items[i] = (stream, window tokens, last)`` -> samples per item (one encoder call and one solve for every
+        window of the call)."""
         if not items:
             return []
         sts = [it[0] for it in items]
-        mus = [self.encode(it[1]) for it in items]
+        if self.flow is not None:
+            mus = self.flow.encode([st.enc for st in sts], [self._tokens(it[1]) for it in items],
+                                   [bool(it[2]) for it in items])
+        else:
+            mus = [self.encode(it[1]) for it in items]
         spk = torch.cat([st.spk for st in sts])
         mels = self.fast.solve([st.cache for st in sts], mus, spk, None, [not bool(it[2]) for it in items])
         out = []

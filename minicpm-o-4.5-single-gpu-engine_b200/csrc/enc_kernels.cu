@@ -32,20 +32,24 @@ namespace {
 
 constexpr int kRQ = 128;              // queries per CTA
 constexpr int kRK = 32;               // keys per tile
-constexpr int kRBand = kRQ + kRK;     // band rows per tile (159 used)
+constexpr int kRBand = kRQ + kRK;     // band rows per tile at most (159 used)
+constexpr int kRBox = 32;             // rows of one position-table TMA box
 constexpr int kD = 64;
 constexpr int kQBytes = kRQ * kD * 2;        // 16 KB per Q tile (q + u, q + v)
 constexpr int kKBytes = kRK * kD * 2;        // 4 KB for K, 4 KB for V
-constexpr int kPBytes = kRBand * kD * 2;     // 20 KB of position rows
-constexpr int kStageBytes = 2 * kKBytes + kPBytes;
-constexpr int kRStages = 2;
-constexpr int kBarOff = 2 * kQBytes + kRStages * kStageBytes;  // 88 KB
+constexpr int kPBytes = kRBand * kD * 2;     // 20 KB of position rows at most
+constexpr int kKVStages = 4;                 // K / V gathers from the pool (HBM): four tiles in flight
+constexpr int kBStages = 2;                  // position bands (L2-resident table), freed as soon as S is computed
+constexpr int kKVOff = 2 * kQBytes;
+constexpr int kBOff = kKVOff + kKVStages * 2 * kKBytes;
+constexpr int kBarOff = kBOff + kBStages * kPBytes;  // 104 KB
 constexpr int kRSmem = 1024 + kBarOff + 256;
-constexpr int kRTmem = 256;  // S / P at [0, 32), band at [32, 192), O at [192, 256)
+constexpr int kRTmem = 256;  // S / P at [0, 32), band at [32, 32 + band rows), O at [192, 256)
+constexpr int kRThreads = 224;
 constexpr float kRescale = 8.f;
 
 struct RelBars {
-  uint64_t q_full, kv_full[kRStages], kv_empty[kRStages], s_full, p_full, o_done;
+  uint64_t q_full, kv_full[kKVStages], kv_empty[kKVStages], b_full[kBStages], b_empty[kBStages], s_full, p_full, o_done;
 };
 
 T2W_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -86,9 +90,28 @@ T2W_DEV void tmem_st32f(uint32_t taddr, const float (&f)[32]) {
       : "memory");
 }
 T2W_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 32 lanes x 32 columns without waiting: the caller issues tmem_ld_wait() before it reads the registers.
+T2W_DEV void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
 
-__global__ void __launch_bounds__(192, 2) k_relattn(const __grid_constant__ CUtensorMap tm_q,
-                                                    const __grid_constant__ CUtensorMap tm_pos, const RelArgs p) {
+// Band rows an item needs: its active query rows (up to 128 from q_pos) in whole warps, plus the tile's 32 keys.
+T2W_DEV int band_rows(const RelWork& w) {
+  const int ar = min(kRQ, w.T - w.q_pos);
+  return kRBox * ((ar + 31) / 32) + kRK;
+}
+
+__global__ void __launch_bounds__(kRThreads, 2) k_relattn(const __grid_constant__ CUtensorMap tm_q,
+                                                          const __grid_constant__ CUtensorMap tm_pos, const RelArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qu = smem;
@@ -101,9 +124,13 @@ __global__ void __launch_bounds__(192, 2) k_relattn(const __grid_constant__ CUte
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < kRStages; ++s) {
-      mbar_init(&bars->kv_full[s], 33);  // 32 cp.async arrivals (one per producer lane) + the TMA's expect_tx
+    for (int s = 0; s < kKVStages; ++s) {
+      mbar_init(&bars->kv_full[s], 32);  // one cp.async arrival per gathering lane
       mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&bars->b_full[s], 1);
+      mbar_init(&bars->b_empty[s], 1);
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->p_full, 4);
@@ -115,6 +142,7 @@ __global__ void __launch_bounds__(192, 2) k_relattn(const __grid_constant__ CUte
   pdl_wait();
   const RelWork w = p.work[blockIdx.x / p.heads];
   const int n_kt = (w.K + kRK - 1) / kRK;
+  const int nb = band_rows(w);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kRTmem);
     tmem_relinquish();
@@ -126,53 +154,63 @@ __global__ void __launch_bounds__(192, 2) k_relattn(const __grid_constant__ CUte
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    bool ok = true;
-    if (lane == 0) {
-      mbar_expect_tx(&bars->q_full, 2 * kQBytes);
-      tma_load_2d(qu, &tm_q, h * kD, w.q_row, &bars->q_full);
-      tma_load_2d(qv, &tm_q, H + h * kD, w.q_row, &bars->q_full);
-    }
+    // K / V gathers: the whole warp copies each 32-key tile from the pool with 16-byte cp.async into the 128-byte
+    // swizzled layout a TMA tile has (chunk c of row r at chunk c ^ (r % 8)); keys past K are zero-filled.  The slot
+    // of the next tile's key is loaded while this tile's copies are issued.
     const __nv_bfloat16* kcol = p.pool + h * kD;
     const __nv_bfloat16* vcol = p.pool + H + h * kD;
+    auto slot_of = [&](int key) { return key < w.K ? __ldg(p.kv_idx + w.kv_off + key) : 0; };
+    int nxt = slot_of(lane);
+    bool ok = true;
     for (int t = 0; t < n_kt && ok; ++t) {
-      const int st = t % kRStages;
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[st], ((t / kRStages) & 1) ^ 1u, p.err)))) break;
-      uint8_t* stage = smem + 2 * kQBytes + st * kStageBytes;
-      const int j0 = t * kRK;
-      if (lane == 0) {
-        mbar_expect_tx(&bars->kv_full[st], kPBytes);
-        const int rb = w.K - w.T + w.q_pos - j0 - (kRK - 1);
-        tma_load_2d(stage + 2 * kKBytes, &tm_pos, h * kD, rb + p.r0, &bars->kv_full[st]);
-      }
-      const int key = j0 + lane;
-      const bool valid = key < w.K;
-      const size_t slot = valid ? (size_t)__ldg(p.kv_idx + w.kv_off + key) : 0;
-      const __nv_bfloat16* ksrc = kcol + slot * p.pool_ld;
-      const __nv_bfloat16* vsrc = vcol + slot * p.pool_ld;
-      const uint32_t ks = smem_u32(stage), vs = ks + kKBytes;
-      const uint32_t nb = valid ? 16u : 0u;
+      const int st = t % kKVStages;
+      const int cur = nxt;
+      if (t + 1 < n_kt) nxt = slot_of((t + 1) * kRK + lane);
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[st], ((t / kKVStages) & 1) ^ 1u, p.err)))) break;
+      const bool valid = t * kRK + lane < w.K;
+      const __nv_bfloat16* ksrc = kcol + (size_t)cur * p.pool_ld;
+      const __nv_bfloat16* vsrc = vcol + (size_t)cur * p.pool_ld;
+      const uint32_t ks = smem_u32(smem + kKVOff + st * 2 * kKBytes), vs = ks + kKBytes;
+      const uint32_t nbytes = valid ? 16u : 0u;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint32_t off = lane * 128 + ((c ^ (lane & 7)) << 4);
-        cp_async16(ks + off, ksrc + 8 * c, nb);
-        cp_async16(vs + off, vsrc + 8 * c, nb);
+        cp_async16(ks + off, ksrc + 8 * c, nbytes);
+        cp_async16(vs + off, vsrc + 8 * c, nbytes);
       }
       cp_async_arrive_noinc(&bars->kv_full[st]);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // no copy of this warp lands after the CTA has moved on
+  } else if (warp == 6) {
+    if (lane == 0) {  // TMA: the Q tiles, then each tile's band of the position table in 32-row boxes
+      mbar_expect_tx(&bars->q_full, 2 * kQBytes);
+      tma_load_2d(qu, &tm_q, h * kD, w.q_row, &bars->q_full);
+      tma_load_2d(qv, &tm_q, H + h * kD, w.q_row, &bars->q_full);
+      for (int t = 0; t < n_kt; ++t) {
+        const int st = t % kBStages;
+        if (!mbar_wait(&bars->b_empty[st], ((t / kBStages) & 1) ^ 1u, p.err)) break;
+        uint8_t* band = smem + kBOff + st * kPBytes;
+        const int rb = w.K - w.T + w.q_pos - t * kRK - (kRK - 1) + p.r0;
+        mbar_expect_tx(&bars->b_full[st], nb * kD * 2);
+        for (int i = 0; i < nb / kRBox; ++i)
+          tma_load_2d(band + i * kRBox * kD * 2, &tm_pos, h * kD, rb + i * kRBox, &bars->b_full[st]);
+      }
+    }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16(kRQ, kRK);
-      constexpr uint32_t idesc_b = idesc_bf16(kRQ, kRBand);
+      const uint32_t idesc_b = idesc_bf16(kRQ, nb);
       constexpr uint32_t idesc_pv = idesc_bf16(kRQ, kD, /*b_mn_major=*/true);
       bool ok = mbar_wait(&bars->q_full, 0, p.err);
       const uint32_t q0 = smem_u32(qu), q1 = smem_u32(qv);
       for (int t = 0; t < n_kt && ok; ++t) {
-        const int st = t % kRStages;
-        if (!(ok = mbar_wait(&bars->kv_full[st], (t / kRStages) & 1, p.err))) break;
+        const int st = t % kKVStages, sb = t % kBStages;
+        if (!(ok = mbar_wait(&bars->kv_full[st], (t / kKVStages) & 1, p.err))) break;
+        if (!(ok = mbar_wait(&bars->b_full[sb], (t / kBStages) & 1, p.err))) break;
         fence_proxy_async_smem();  // the K / V rows were written by cp.async through the generic proxy
         tc_fence_after();
-        const uint32_t ks = smem_u32(smem + 2 * kQBytes + st * kStageBytes), vs = ks + kKBytes, ps = ks + 2 * kKBytes;
+        const uint32_t ks = smem_u32(smem + kKVOff + st * 2 * kKBytes), vs = ks + kKBytes;
+        const uint32_t ps = smem_u32(smem + kBOff + sb * kPBytes);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
           umma_f16(tmem, sdesc_sw128(q0 + 32 * kk, 1024, 16), sdesc_sw128(ks + 32 * kk, 1024, 16), idesc_s, kk ? 1u : 0u);
@@ -181,6 +219,7 @@ __global__ void __launch_bounds__(192, 2) k_relattn(const __grid_constant__ CUte
           umma_f16(tmem + 32, sdesc_sw128(q1 + 32 * kk, 1024, 16), sdesc_sw128(ps + 32 * kk, 1024, 16), idesc_b,
                    kk ? 1u : 0u);
         umma_commit(&bars->s_full);
+        umma_commit(&bars->b_empty[sb]);
         if (!(ok = mbar_wait(&bars->p_full, t & 1, p.err))) break;
         tc_fence_after();
 #pragma unroll
@@ -204,31 +243,42 @@ __global__ void __launch_bounds__(192, 2) k_relattn(const __grid_constant__ CUte
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full, t & 1, p.err)))) break;
       tc_fence_after();
       if (!idle) {
-        float s[32], b[64];
-        tmem_ld32(tmem + lanes, s);
-        tmem_ld32p(tmem + lanes + 32 + 32 * qw, b);
-        tmem_ld32p(tmem + lanes + 64 + 32 * qw, b + 32);
-        // shift the warp's band by this lane: b[x] <- b[x + lane] for x < 32
+        uint32_t sr[32], b[64];
+        float s[32];
+        // the scores and the warp's 64 band columns, three loads in flight and one wait
+        tmem_ld32_nowait(tmem + lanes, sr);
+        tmem_ld32_nowait(tmem + lanes + 32 + 32 * qw, b);
+        tmem_ld32_nowait(tmem + lanes + 64 + 32 * qw, b + 32);
+        tmem_ld_wait();
+        // shift the warp's band by this lane, b[x] <- b[x + lane] for x < 32: five stages of bitwise selects on the
+        // lane's bits (one LOP3 per element, no branches)
         {
-          const bool s16 = lane & 16, s8 = lane & 8, s4 = lane & 4, s2 = lane & 2, s1 = lane & 1;
+          const uint32_t m16 = 0u - ((lane >> 4) & 1u), m8 = 0u - ((lane >> 3) & 1u), m4 = 0u - ((lane >> 2) & 1u),
+                         m2 = 0u - ((lane >> 1) & 1u), m1 = 0u - (lane & 1u);
 #pragma unroll
-          for (int x = 0; x < 47; ++x) b[x] = s16 ? b[x + 16] : b[x];
+          for (int x = 0; x < 47; ++x) b[x] = (b[x + 16] & m16) | (b[x] & ~m16);
 #pragma unroll
-          for (int x = 0; x < 39; ++x) b[x] = s8 ? b[x + 8] : b[x];
+          for (int x = 0; x < 39; ++x) b[x] = (b[x + 8] & m8) | (b[x] & ~m8);
 #pragma unroll
-          for (int x = 0; x < 35; ++x) b[x] = s4 ? b[x + 4] : b[x];
+          for (int x = 0; x < 35; ++x) b[x] = (b[x + 4] & m4) | (b[x] & ~m4);
 #pragma unroll
-          for (int x = 0; x < 33; ++x) b[x] = s2 ? b[x + 2] : b[x];
+          for (int x = 0; x < 33; ++x) b[x] = (b[x + 2] & m2) | (b[x] & ~m2);
 #pragma unroll
-          for (int x = 0; x < 32; ++x) b[x] = s1 ? b[x + 1] : b[x];
+          for (int x = 0; x < 32; ++x) b[x] = (b[x + 1] & m1) | (b[x] & ~m1);
         }
         const int kb = t * kRK;
 #pragma unroll
-        for (int k = 0; k < kRK; ++k) s[k] = (kb + k < w.K) ? s[k] + b[kRK - 1 - k] : -INFINITY;
-        float mx = s[0];
+        for (int k = 0; k < kRK; ++k)
+          s[k] = (kb + k < w.K) ? __uint_as_float(sr[k]) + __uint_as_float(b[kRK - 1 - k]) : -INFINITY;
+        float mq[4];
 #pragma unroll
-        for (int k = 1; k < kRK; ++k) mx = fmaxf(mx, s[k]);
-        mx *= p.scale_log2;
+        for (int c = 0; c < 4; ++c) {
+          mq[c] = fmax3(s[8 * c], s[8 * c + 1], s[8 * c + 2]);
+          mq[c] = fmax3(mq[c], s[8 * c + 3], s[8 * c + 4]);
+          mq[c] = fmax3(mq[c], s[8 * c + 5], s[8 * c + 6]);
+          mq[c] = fmaxf(mq[c], s[8 * c + 7]);
+        }
+        float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
         const bool raise = mx > m + kRescale;
         const float m_old = m;
         m = raise ? mx : m;
@@ -478,7 +528,7 @@ inline int ck(cudaError_t e) {
 bool make_relattn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_pos, const void* qkv4, int rows, int H, const void* pos,
                         int max_frames) {
   return make_tmap_2d(tm_q, qkv4, 2, (uint64_t)rows, (uint64_t)4 * H, (uint64_t)8 * H, kRQ, kD) &&
-         make_tmap_2d(tm_pos, pos, 2, (uint64_t)(2 * max_frames - 1), (uint64_t)H, (uint64_t)2 * H, kRBand, kD);
+         make_tmap_2d(tm_pos, pos, 2, (uint64_t)(2 * max_frames - 1), (uint64_t)H, (uint64_t)2 * H, kRBox, kD);
 }
 
 int launch_relattn(const RelArgs& a, const CUtensorMap& tm_q, const CUtensorMap& tm_pos, cudaStream_t st) {
@@ -487,7 +537,7 @@ int launch_relattn(const RelArgs& a, const CUtensorMap& tm_q, const CUtensorMap&
     return T2W_ERR_INVALID;
   static std::atomic<uint64_t> attr_done{0};
   if (const int rc = ck(smem_attr_once(k_relattn, kRSmem, attr_done))) return rc;
-  return ck(launch_k(k_relattn, dim3(a.n_work * a.heads), dim3(192), kRSmem, st, tm_q, tm_pos, a));
+  return ck(launch_k(k_relattn, dim3(a.n_work * a.heads), dim3(kRThreads), kRSmem, st, tm_q, tm_pos, a));
 }
 
 int launch_pos_table(const float* w, int H, int max_frames, float max_period, __nv_bfloat16* pos, cudaStream_t st) {

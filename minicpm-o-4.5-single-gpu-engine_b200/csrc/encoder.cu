@@ -23,6 +23,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 #include "cache_registry.h"
@@ -94,6 +95,8 @@ struct t2w_encoder {
   std::vector<void*> allocs;
   __nv_bfloat16 *emb = nullptr, *w_embed = nullptr, *w_c1 = nullptr, *w_c2 = nullptr, *w_up = nullptr,
                 *w_upemb = nullptr, *w_proj = nullptr, *cnn = nullptr;
+  // K/V pools of the two stacks: [layers of the stack][slots][2 H], layer l's pool at l * slots * 2 H
+  __nv_bfloat16 *pool1 = nullptr, *pool2 = nullptr;
   float *b_embed = nullptr, *b_c1 = nullptr, *b_c2 = nullptr, *b_up = nullptr, *b_upemb = nullptr, *b_proj = nullptr;
   float *ln_e_w = nullptr, *ln_e_b = nullptr, *ln_u_w = nullptr, *ln_u_b = nullptr, *ln_a_w = nullptr,
         *ln_a_b = nullptr, *ones = nullptr;
@@ -113,6 +116,15 @@ struct t2w_encoder {
   };
   Staging staging[kStaging];
   int staging_next = 0;
+  // CUDA graphs of whole calls, per launch structure (sizes and buffers), captured the second time a key is seen
+  struct CachedGraph {
+    cudaGraphExec_t exec = nullptr;
+    cudaEvent_t done = nullptr;  // recorded after its latest launch: an evicted graph may still run on another stream
+  };
+  std::unordered_map<uint64_t, CachedGraph> graphs;
+  std::unordered_map<uint64_t, int> seen;
+  cudaStream_t cap_stream = nullptr;
+  int64_t n_replays = 0, n_captures = 0, n_eager = 0;
 
   EncRecord* find(int32_t handle) {
     if (handle < 0) return nullptr;
@@ -223,6 +235,8 @@ int create_impl(t2w_encoder* e, const float* const* W, cudaStream_t st) {
     return T2W_ERR_INVALID;
   const int nl = c.blocks1 + c.blocks2;
   e->L.resize(nl);
+  E_TRY(dalloc(e, &e->pool1, (size_t)c.blocks1 * e->n_slots1 * 2 * H));
+  E_TRY(dalloc(e, &e->pool2, (size_t)c.blocks2 * e->n_slots2 * 2 * H));
   const size_t rows_pos = (size_t)(2 * e->max_frames - 1);
   for (int l = 0; l < nl; ++l) {
     const float* const* lw = W + T2W_E_COUNT + (size_t)l * T2W_EL_COUNT;
@@ -257,8 +271,8 @@ int create_impl(t2w_encoder* e, const float* const* W, cudaStream_t st) {
     E_TRY(copy_f32(e, lw[T2W_EL_NFF_B], H, &y.nf_b));
     E_TRY(dalloc(e, &y.pos, rows_pos * H));
     E_TRY(launch_pos_table(lw[T2W_EL_POS_W], H, e->max_frames, c.max_period, y.pos, st));
-    const size_t slots = (size_t)(l < c.blocks1 ? e->n_slots1 : e->n_slots2);
-    E_TRY(dalloc(e, &y.pool, slots * 2 * H));
+    y.pool = l < c.blocks1 ? e->pool1 + (size_t)l * e->n_slots1 * 2 * H
+                           : e->pool2 + (size_t)(l - c.blocks1) * e->n_slots2 * 2 * H;
     if (!make_weight_maps(&y.tm_qkv, y.w_qkv, 4 * H, H) || !make_weight_maps(&y.tm_out, y.w_out, H, H) ||
         !make_weight_maps(&y.tm_ff1, y.w_ff1, F, H) || !make_weight_maps(&y.tm_ff2, y.w_ff2, H, F))
       return T2W_ERR_INVALID;
@@ -275,6 +289,14 @@ int create_impl(t2w_encoder* e, const float* const* W, cudaStream_t st) {
 }
 
 void free_all(t2w_encoder* e) {
+  for (auto& kv : e->graphs) {
+    if (kv.second.done) cudaEventSynchronize(kv.second.done);
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.done) cudaEventDestroy(kv.second.done);
+  }
+  e->graphs.clear();
+  if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
+  e->cap_stream = nullptr;
   for (void* p : e->allocs) cudaFree(p);
   e->allocs.clear();
   for (auto& sg : e->staging) {
@@ -567,6 +589,73 @@ int run_call(t2w_encoder* e, const EncPlan& pl, const EncLayout& Lo, void* ws, f
   return launch_gather_rows_f32(y3, kMel, at<int>(ws, Lo.out_src), pl.n_out, mu, st);
 }
 
+uint64_t mix(uint64_t h, uint64_t v) {
+  h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+  return h * 0xff51afd7ed558ccdull;
+}
+
+// The launches of a call depend only on the plan's sizes and the buffers (the index arrays are read from the
+// workspace, where upload() has just put this call's): one graph per such key.
+uint64_t call_key(const EncPlan& pl, const void* ws, const void* mu) {
+  uint64_t k = 0xE0C0DE5ull;
+  for (long long v : {(long long)pl.n, (long long)pl.M1, (long long)pl.M2, (long long)pl.n_out,
+                      (long long)pl.sc1_row.size(), (long long)pl.sc2_row.size(), (long long)pl.kv1.size(),
+                      (long long)pl.kv2.size(), (long long)pl.w1.size(), (long long)pl.w2.size()})
+    k = mix(k, (uint64_t)v);
+  return mix(mix(k, reinterpret_cast<uint64_t>(ws)), reinterpret_cast<uint64_t>(mu));
+}
+
+constexpr size_t kMaxGraphs = 64;
+
+template <class F>
+int replay(t2w_encoder* e, uint64_t key, cudaStream_t st, F&& enqueue) {
+  auto g = e->graphs.find(key);
+  if (g == e->graphs.end()) {
+    cudaStreamCaptureStatus cs;
+    E_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: use flags = 0
+    if (e->graphs.size() >= kMaxGraphs) {  // drop one, once its latest launch (on whichever stream) has finished
+      auto victim = e->graphs.begin();
+      E_CUDA(cudaEventSynchronize(victim->second.done));
+      cudaGraphExecDestroy(victim->second.exec);
+      cudaEventDestroy(victim->second.done);
+      e->graphs.erase(victim);
+    }
+    if (!e->cap_stream) E_CUDA(cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking));
+    E_CUDA(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue(e->cap_stream);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(e->cap_stream, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ec != cudaSuccess) {
+      set_cuda_error(ec);
+      return T2W_ERR_CUDA;
+    }
+    t2w_encoder::CachedGraph cg;
+    const cudaError_t ei = cudaGraphInstantiate(&cg.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) {
+      set_cuda_error(ei);
+      return T2W_ERR_CUDA;
+    }
+    const cudaError_t ee = cudaEventCreateWithFlags(&cg.done, cudaEventDisableTiming);
+    if (ee != cudaSuccess) {
+      cudaGraphExecDestroy(cg.exec);
+      set_cuda_error(ee);
+      return T2W_ERR_CUDA;
+    }
+    g = e->graphs.emplace(key, cg).first;
+    ++e->n_captures;
+  }
+  E_CUDA(cudaGraphLaunch(g->second.exec, st));
+  E_CUDA(cudaEventRecord(g->second.done, st));
+  ++e->n_replays;
+  return T2W_OK;
+}
+
 // The caches after a window (token2wav_batch.py:395 trims conformer_att_cache along time to its first keep and last
 // 100 frames; the first stack's cache is stored tiled twice and read back as the first half of the cut).
 void advance(t2w_encoder* e, EncRecord& r, const int32_t* new1, int T) {
@@ -668,6 +757,84 @@ int t2w_enc_stream_new(t2w_encoder* e, int32_t keep, void* stream, int32_t* hand
   return T2W_OK;
 }
 
+int t2w_enc_stream_clone(t2w_encoder* e, int32_t handle, void* stream, int32_t* out) {
+  if (!e || !out) return T2W_ERR_INVALID;
+  DeviceGuard g(e->device);
+  if (!g.ok) return T2W_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lk(e->mu);
+  EncRecord* src = e->find(handle);
+  if (!src) return T2W_ERR_INVALID;
+  const int n1 = (int)src->k1.size(), n2 = (int)src->k2.size();
+  std::vector<int32_t> ids((size_t)2 * (n1 + n2));  // [src1 | dst1 | src2 | dst2]
+  int32_t row;
+  if (!e->rows.take(1, &row)) return T2W_ERR_EXHAUSTED;
+  int32_t* dst1 = ids.data() + n1;
+  int32_t* dst2 = ids.data() + 2 * n1 + n2;
+  if (!e->s1.take(n1, dst1)) {
+    e->rows.give(&row, 1);
+    return T2W_ERR_EXHAUSTED;
+  }
+  if (!e->s2.take(n2, dst2)) {
+    e->s1.give(dst1, n1);
+    e->rows.give(&row, 1);
+    return T2W_ERR_EXHAUSTED;
+  }
+  std::copy(src->k1.begin(), src->k1.end(), ids.begin());
+  std::copy(src->k2.begin(), src->k2.end(), ids.begin() + 2 * n1);
+  auto undo = [&](int rc) {
+    e->s1.give(dst1, n1);
+    e->s2.give(dst2, n2);
+    e->rows.give(&row, 1);
+    return rc;
+  };
+  const int H = e->cfg.hidden;
+  if (!ids.empty()) {
+    int* d = nullptr;
+    cudaError_t ce = cudaMallocAsync(reinterpret_cast<void**>(&d), ids.size() * 4, st);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(d, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) {
+      set_cuda_error(ce);
+      return undo(T2W_ERR_CUDA);
+    }
+    int rc = launch_slot_copy(e->pool1, 2 * H, (long long)e->n_slots1 * 2 * H, e->cfg.blocks1, d, d + n1, n1, st);
+    if (!rc)
+      rc = launch_slot_copy(e->pool2, 2 * H, (long long)e->n_slots2 * 2 * H, e->cfg.blocks2, d + 2 * n1,
+                            d + 2 * n1 + n2, n2, st);
+    cudaFreeAsync(d, st);
+    if (rc) {
+      cudaStreamSynchronize(st);
+      return undo(rc);
+    }
+  }
+  const size_t fb = (size_t)kCacheFrames * H;
+  const cudaError_t cc = cudaMemcpyAsync(e->cnn + (size_t)row * fb, e->cnn + (size_t)src->row * fb, fb * 2,
+                                         cudaMemcpyDeviceToDevice, st);
+  if (cc != cudaSuccess) {
+    set_cuda_error(cc);
+    cudaStreamSynchronize(st);
+    return undo(T2W_ERR_CUDA);
+  }
+  uint32_t idx;
+  if (!e->vacant.empty()) {
+    idx = e->vacant.back();
+    e->vacant.pop_back();
+  } else {
+    idx = (uint32_t)e->recs.size();
+    e->recs.emplace_back();
+    src = e->find(handle);  // the records may have moved
+  }
+  EncRecord& r = e->recs[idx];
+  r.live = true;
+  r.generation = (r.generation + 1) & ((1u << (31 - kIndexBits)) - 1);
+  r.keep = src->keep;
+  r.row = row;
+  r.k1.assign(dst1, dst1 + n1);
+  r.k2.assign(dst2, dst2 + n2);
+  *out = (int32_t)((r.generation << kIndexBits) | idx);
+  return T2W_OK;
+}
+
 int t2w_enc_stream_release(t2w_encoder* e, int32_t handle) {
   if (!e) return T2W_ERR_INVALID;
   std::lock_guard<std::mutex> lk(e->mu);
@@ -713,7 +880,7 @@ size_t t2w_enc_workspace_bytes(const t2w_encoder* e, const t2w_enc_batch* b) {
   return layout_of(e->cfg, pl).total;
 }
 
-int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* ws, size_t ws_bytes, void* stream) {
+int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* ws, size_t ws_bytes, uint32_t flags, void* stream) {
   if (!e || !b || !ws || !b->mu) return T2W_ERR_INVALID;
   DeviceGuard g(e->device);
   if (!g.ok) return T2W_ERR_CUDA;
@@ -733,7 +900,16 @@ int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* ws, size_t ws_bytes
     return ws_bytes < Lo.total ? T2W_ERR_WORKSPACE : T2W_ERR_INVALID;
   }
   int rc = upload(e, pl, Lo, ws, st);
-  if (!rc) rc = run_call(e, pl, Lo, ws, b->mu, st);
+  if (!rc) {
+    const uint64_t key = call_key(pl, ws, b->mu);
+    if (e->seen.size() > 4096) e->seen.clear();
+    if ((flags & T2W_FLAG_GRAPH) && (e->graphs.count(key) || ++e->seen[key] >= 2)) {
+      rc = replay(e, key, st, [&](cudaStream_t cs) { return run_call(e, pl, Lo, ws, b->mu, cs); });
+    } else {
+      rc = run_call(e, pl, Lo, ws, b->mu, st);
+      if (!rc) ++e->n_eager;
+    }
+  }
   if (rc) {
     // launches may already be enqueued: the new slots stay unused but are given back only once they are idle
     cudaStreamSynchronize(st);
@@ -749,6 +925,14 @@ int t2w_encode(t2w_encoder* e, const t2w_enc_batch* b, void* ws, size_t ws_bytes
     f1 += T;
     f2 += 2 * T;
   }
+  return T2W_OK;
+}
+
+int t2w_enc_counts(const t2w_encoder* e, int64_t* replays, int64_t* captures, int64_t* eager) {
+  if (!e) return T2W_ERR_INVALID;
+  if (replays) *replays = e->n_replays;
+  if (captures) *captures = e->n_captures;
+  if (eager) *eager = e->n_eager;
   return T2W_OK;
 }
 

@@ -2,7 +2,8 @@
 //
 // The reference engine calls its solver from torch code (BatchedToken2Wav -> FastDiT.solve,
 // engine/runtime/token2wav_batch.py:335,356-357,518-519,549 -> engine/runtime/dit_fast.py:432-495).  These ops give
-// that call site the B200 solve as registered torch operators: tensors in, the current torch CUDA stream of the
+// that call site the B200 solve as registered torch operators (and the flow encoder before it, _flow_encode / _encoder,
+// token2wav_batch.py:365-478): tensors in, the current torch CUDA stream of the
 // tensors' device as the stream, a C-ABI call, and a RuntimeError carrying the status on failure.  No logic lives here:
 // every op is argument conversion around one t2w_* call (include/t2w_b200.h).  Solver and slot-pool objects cross the
 // boundary as int handles (their addresses), as the ctypes binding passes them.
@@ -247,6 +248,45 @@ void euler_cfg(at::Tensor& x, const at::Tensor& dphi, const at::Tensor& tok_row,
                                        static_cast<float*>(const_cast<void*>(ptr(out))), stream_of(x)));
 }
 
+// ---- flow encoder ---------------------------------------------------------------------------------------------------
+
+struct Enc {
+  std::vector<int32_t> h, n, tok;
+  std::vector<uint8_t> fin;
+  t2w_enc_batch b{};
+};
+
+Enc enc_batch(c10::IntArrayRef handles, c10::IntArrayRef n_tokens, c10::IntArrayRef final_, c10::IntArrayRef tokens) {
+  TORCH_CHECK(handles.size() == n_tokens.size() && handles.size() == final_.size(),
+              "encode: one handle, token count and final flag per window");
+  Enc e;
+  e.h = i32(handles);
+  e.n = i32(n_tokens);
+  e.tok = i32(tokens);
+  e.fin.assign(final_.begin(), final_.end());
+  e.b.n_streams = (int32_t)e.h.size();
+  e.b.handle = e.h.data();
+  e.b.n_tokens = e.n.data();
+  e.b.final = e.fin.data();
+  e.b.tokens = e.tok.data();
+  return e;
+}
+
+int64_t enc_workspace_bytes(int64_t encoder, c10::IntArrayRef handles, c10::IntArrayRef n_tokens,
+                            c10::IntArrayRef final_, c10::IntArrayRef tokens) {
+  Enc e = enc_batch(handles, n_tokens, final_, tokens);
+  return (int64_t)t2w_enc_workspace_bytes(handle<t2w_encoder>(encoder), &e.b);
+}
+
+void encode(int64_t encoder, c10::IntArrayRef handles, c10::IntArrayRef n_tokens, c10::IntArrayRef final_,
+            c10::IntArrayRef tokens, at::Tensor& mu, at::Tensor& workspace, bool graph) {
+  TORCH_CHECK(mu.scalar_type() == at::kFloat && mu.is_contiguous(), "encode: mu is contiguous fp32");
+  Enc e = enc_batch(handles, n_tokens, final_, tokens);
+  e.b.mu = mu.data_ptr<float>();
+  check("t2w_encode", t2w_encode(handle<t2w_encoder>(encoder), &e.b, workspace.data_ptr(), (size_t)workspace.numel(),
+                                 graph ? T2W_FLAG_GRAPH : 0u, stream_of(mu)));
+}
+
 }  // namespace
 
 TORCH_LIBRARY(b200t2w, m) {
@@ -279,4 +319,9 @@ TORCH_LIBRARY(b200t2w, m) {
   m.def("euler_cfg(Tensor(a!) x, Tensor dphi, Tensor tok_row, int half_rows, float dt, float w, Tensor(b!)? hx, "
         "Tensor(c!)? out) -> ()",
         &euler_cfg);
+  m.def("enc_workspace_bytes(int encoder, int[] handles, int[] n_tokens, int[] final, int[] tokens) -> int",
+        &enc_workspace_bytes);
+  m.def("encode(int encoder, int[] handles, int[] n_tokens, int[] final, int[] tokens, Tensor(a!) mu, "
+        "Tensor(b!) workspace, bool graph) -> ()",
+        &encode);
 }

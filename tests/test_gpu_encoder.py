@@ -262,3 +262,80 @@ def test_encoder_rejects_bad_calls():
         enc.encode([h2], [[1] * 8], [False])
     enc.encode([h], [[1] * 8], [False])  # still usable
     enc.check()
+
+
+def test_encoder_graph_replay_equals_eager():
+    """Steady windows through CUDA-graph replay (one graph per launch structure, captured on its second sight) give
+    the eager calls' mu bit for bit; finals and calls of other structures fall back to eager calls."""
+    torch.manual_seed(3)
+    flow = eo.build_flow(ENCODER_TINY, seed=0)
+    kw = dict(max_frames=512, n_slots1=2048, n_slots2=4096, n_streams=8)
+    eager = B200FlowEncoder.from_flow(flow, device="cuda", **kw)
+    graph = B200FlowEncoder.from_flow(flow, device="cuda", use_graphs=True, **kw)
+    prompts = [torch.randint(0, ENCODER_TINY.vocab, (n,)) for n in (30, 45, 52, 61)]
+    he, _ = eager.setup(prompts)
+    hg, _ = graph.setup(prompts)
+    out_e = torch.empty(4 * 50, ENCODER_TINY.mel, device="cuda")
+    out_g = torch.empty_like(out_e)
+    for r in range(8):
+        wins = [torch.randint(0, ENCODER_TINY.vocab, (28,)) for _ in range(4)]
+        eager.encode_packed(he, wins, [False] * 4, out=out_e)
+        graph.encode_packed(hg, wins, [False] * 4, out=out_g)
+        torch.cuda.synchronize()
+        assert torch.equal(out_e, out_g), r
+    fins = [torch.randint(0, ENCODER_TINY.vocab, (n,)) for n in (5, 9, 13, 20)]
+    a = eager.encode(he, fins, [True] * 4)
+    b = graph.encode(hg, fins, [True] * 4)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    c = graph.counts
+    print("graph encoder calls:", c)
+    assert c["replays"] >= 3 and c["captures"] >= 1
+    graph.check()
+
+
+def test_encode_op_equals_ctypes():
+    """``torch.ops.b200t2w.encode`` (what ``B200FlowEncoder`` calls) against the same C-ABI call made through ctypes,
+    on two encoders fed the same prompts and windows: bit for bit."""
+    torch.manual_seed(5)
+    flow = eo.build_flow(ENCODER_TINY, seed=0)
+    kw = dict(max_frames=512, n_slots1=2048, n_slots2=4096, n_streams=4)
+    a = B200FlowEncoder.from_flow(flow, device="cuda", **kw)
+    b = B200FlowEncoder.from_flow(flow, device="cuda", **kw)
+    prompts = [torch.randint(0, ENCODER_TINY.vocab, (n,)) for n in (25, 40)]
+    ha, _ = a.setup(prompts)
+    hb, _ = b.setup(prompts)
+    lib = L.load()
+    for r in range(3):
+        wins = [torch.randint(0, ENCODER_TINY.vocab, (28,)).tolist() for _ in range(2)]
+        out_a = a.encode_packed(ha, wins, [False, False])
+        out_b = torch.empty_like(out_a)
+        flat = [t for w in wins for t in w]
+        batch = L.EncBatch(2, L.i32_array(hb), L.i32_array([28, 28]), (ctypes.c_uint8 * 2)(0, 0), L.i32_array(flat),
+                           P(out_b))
+        need = lib.t2w_enc_workspace_bytes(b.handle, ctypes.byref(batch))
+        ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        L.call("t2w_encode", b.handle, ctypes.byref(batch), P(ws), ctypes.c_size_t(need), 0, S())
+        torch.cuda.synchronize()
+        assert torch.equal(out_a, out_b), r
+
+
+def test_stream_clone():
+    """A cloned stream (a request's copy of its prompt's encoder caches) encodes the same windows as the stream it was
+    copied from, bit for bit, and both advance independently; releasing both returns every slot."""
+    torch.manual_seed(8)
+    flow, enc = build(ENCODER_TINY, max_frames=512, n_slots1=2048, n_slots2=4096, n_streams=4)
+    (h,), _ = enc.setup([torch.randint(0, ENCODER_TINY.vocab, (70,))])
+    c = enc.clone(h)
+    assert enc.stream_info(c) == enc.stream_info(h)
+    for r in range(4):
+        w = torch.randint(0, ENCODER_TINY.vocab, (28,))
+        a, b = enc.encode([h, c], [w, w], [False, False])
+        assert torch.equal(a, b), r
+    w2 = torch.randint(0, ENCODER_TINY.vocab, (28,))
+    a = enc.encode([h], [w2], [False])[0]
+    b = enc.encode([c], [torch.randint(0, ENCODER_TINY.vocab, (28,))], [False])[0]
+    assert not torch.equal(a, b)
+    enc.release(h)
+    enc.release(c)
+    assert enc.usage() == (0, 0, 0)

@@ -142,3 +142,55 @@ def test_reference_worker_loop_across_two_gpus():
     assert {d for d in range(2) if parts[d][0].counts["eager"] + parts[d][0].counts["graph"]} == {0, 1}
     for fd, _ in parts:
         assert fd.pool.in_use() == 0
+
+
+def test_reference_worker_loop_with_b200_flow_encoder():
+    """The same loop with this build's flow encoder in place of the stand-in: prompts and windows are encoded by
+    ``B200FlowEncoder`` (each request owns an encoder stream, copied from its prompt or adopted, advanced by every
+    window, released with the request), then solved by ``B200FastDiT``.  Every window against the oracle's chain: the
+    restated flow encoder's streaming forward (``encode_prompt`` / ``encode_window``) feeding the oracle's streaming solve;
+    afterwards every encoder slot and stream is back."""
+    from b200t2w.config import ENCODER_TINY
+    from b200t2w.encoder import B200FlowEncoder
+    from oracle import encoder_oracle as eo
+
+    model = dit_oracle.build_model(TINY, seed=0, noise_frames=4096)
+    flow = eo.build_flow(ENCODER_TINY, seed=0)
+    fd = B200FastDiT(B200Solver(TINY, state_dict_from_module(model), device="cuda:0"), model.rand_noise[0], n_slots=4096,
+                     max_streams=8)
+    enc = B200FlowEncoder.from_flow(flow, device="cuda:0", max_frames=1024, n_slots1=4096, n_slots2=8192, n_streams=16,
+                                    use_graphs=True)
+    voc = lambda st, mel, last: mel.float().flatten().cpu().numpy()  # noqa: E731
+    bt = B200Token2Wav(fd, enc, voc, device_index=0)
+    g = torch.Generator().manual_seed(9)
+    reqs = {}
+    for seq, (ptok, wins) in {1: (60, (28, 28, 28, 10)), 2: (35, (28, 28, 7)), 3: (80, (28, 28, 28, 28, 12))}.items():
+        reqs[seq] = {"prompt_tokens": torch.randint(0, VOCAB, (ptok,), generator=g).tolist(),
+                     "mel": torch.randn(1, 2 * ptok, TINY.mel, generator=g), "spk": torch.randn(1, TINY.mel, generator=g),
+                     "windows": [torch.randint(0, VOCAB, (n,), generator=g).tolist() for n in wins]}
+    audio = run_loop(bt, reqs)
+    fd.solver.check()
+    enc.check()
+    for seq, r in reqs.items():
+        mu_p, est = eo.encode_prompt(flow, torch.tensor(r["prompt_tokens"]))
+        cache = dit_oracle.StreamCache(TINY, keep=r["mel"].shape[1])
+        spk = r["spk"][0]
+        ref = []
+        for i, w in enumerate([None] + r["windows"]):
+            last = i == len(r["windows"])
+            mu = mu_p if i == 0 else eo.encode_window(flow, est, torch.tensor(w), last)
+            T = mu.shape[1]
+            x0 = model.rand_noise[0, :, cache.length:cache.length + T]
+            m = dit_oracle.solve_window(model, cache, x0, mu, spk, r["mel"][0].t() if i == 0 else None,
+                                        keep_cache=not last)
+            if i > 0:
+                ref.append(m)
+        got = audio[seq]
+        assert len(got) == len(ref)
+        for k, (a, b) in enumerate(zip(got, ref)):
+            b = b.flatten()
+            e = float((torch.from_numpy(a) - b).norm() / b.norm())
+            print(f"request {seq} window {k} ({len(a) // TINY.mel} frames): rel-L2 vs oracle chain {e:.2e}")
+            assert e < TOL
+    assert enc.usage() == (0, 0, 0)
+    assert fd.pool.in_use() - fd.scratch == 0

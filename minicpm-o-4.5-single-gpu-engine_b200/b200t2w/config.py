@@ -179,3 +179,42 @@ ENCODER = EncoderConfig()
 
 ENCODER_TINY = replace(ENCODER, hidden=128, heads=2, ffn=256, blocks1=2, blocks2=2, spk_dim=32)
 """A small encoder with the same kernel shape class, for fast golden fixtures."""
+
+
+@dataclass(frozen=True)
+class HiFTConfig:
+    """The HiFT vocoder's hyper-parameters (``stepaudio2``'s ``HiFTGenerator``; the reference reads ``num_upsamples``,
+    ``num_kernels``, ``istft_params``, ``lrelu_slope``, ``audio_limit``, ``f0_upsamp.scale_factor`` and the source's
+    ``l_sin_gen`` fields off the module, ``engine/models/token2wav.py:112-245``).  The values are the published
+    CosyVoice2 ``hift.yaml`` (24 kHz, 512 base channels, upsampling 8 x 5 x 3 with an n_fft 16 / hop 4 iSTFT, 8
+    harmonics) and are UNVERIFIED against the checkpoint."""
+    mel: int = 80
+    channels: int = 512                      # base_channels (unverified)
+    upsample_rates: tuple = (8, 5, 3)
+    upsample_kernels: tuple = (16, 11, 7)
+    resblock_kernels: tuple = (3, 7, 11)
+    source_kernels: tuple = (7, 7, 11)       # source_resblock_kernel_sizes (unverified)
+    dilations: tuple = (1, 3, 5)             # every ResBlock's dilations
+    n_fft: int = 16
+    hop: int = 4
+    harmonics: int = 8                       # nb_harmonics
+    sample_rate: int = 24000
+    nsf_alpha: float = 0.1                   # sine amplitude
+    nsf_sigma: float = 0.003                 # additive noise std of voiced samples
+    voiced_threshold: float = 10.0
+    lrelu_slope: float = 0.1
+    audio_limit: float = 0.99
+    f0_channels: int = 512                   # ConvRNNF0Predictor cond_channels (unverified)
+    f0_layers: int = 5
+
+    @property
+    def upsample_scale(self) -> int:
+        """Waveform samples per mel frame: the product of the upsampling rates times the iSTFT hop (480)."""
+        return int(math.prod(self.upsample_rates)) * self.hop
+
+
+HIFT = HiFTConfig()
+"""The reference-config (unverified) vocoder."""
+
+HIFT_TINY = replace(HIFT, channels=256, f0_channels=128, f0_layers=2)
+"""A narrower vocoder with the same stage structure (stages of 128, 64 and 32 channels), for fast golden fixtures."""

@@ -488,6 +488,63 @@ T2W_API int t2w_enc_pos_table(const float* w, int32_t H, int32_t max_frames, flo
 T2W_API int t2w_enc_ln(const float* x, const float* w, const float* b, float eps, int32_t rows, int32_t C, float* out_f32,
                        void* out_bf16, const uint8_t* pad, void* stream);
 
+/* ---- HiFT vocoder: the step after the solve (mel -> 24 kHz waveform).
+ *
+ * Replaces (paths inside the reference):
+ *   t2w_hift_create      the flow's HiFTGenerator as Token2Wav loads it (engine/models/token2wav.py:249-264; weight
+ *                        normalisation folded into plain weights, as the reference's lean form does once)
+ *   t2w_vocode           BatchedToken2Wav._vocode (engine/runtime/token2wav_batch.py:813-848) over hift_forward /
+ *                        hift_forward_noise / _hift_decode / istft_overlap_add (engine/models/token2wav.py:112-245):
+ *                        each window's mel after its stream's 8 cached frames, f0 predictor, harmonic source, the
+ *                        decoder, the inverse STFT, the Hamming cross-fade with the previous window, the caches, and
+ *                        the output samples (the last 3840 held back unless the window is final; a stream's first
+ *                        window starts with 3840 samples of silence)
+ *   t2w_hift_stream_*    a stream's hift_cache (mel / source / speech tails, token2wav.py:287-292), kept in the library
+ * Strict fp32 (the reference runs Token2Wav with TF32 off: token2wav.py:44-57). */
+typedef struct t2w_hift_config {
+  int32_t mel, channels, f0_channels, f0_layers, harmonics, sample_rate, n_fft, hop;
+  int32_t up_rates[3], up_kernels[3], res_kernels[3], source_kernels[3], dilations[3];
+  float nsf_alpha, nsf_sigma, voiced_threshold, lrelu_slope, audio_limit;
+} t2w_hift_config;
+
+typedef struct t2w_hift t2w_hift;
+
+/* Weight order of t2w_hift_create (fp32 device pointers in the module's layouts; Conv1d [out, in, k],
+ * ConvTranspose1d [in, out, k]; state-dict paths of HiFTGenerator):
+ *   f0_predictor.condnet.{2l}.weight / .bias for l < f0_layers; f0_predictor.classifier.weight / .bias;
+ *   m_source.l_linear.weight / .bias; conv_pre.weight / .bias; ups.{0,1,2}.weight / .bias;
+ *   per stage s = 0..2: source_downs.s.weight / .bias, then source_resblocks.s: convs1.{0,1,2}.weight / .bias,
+ *     convs2.{0,1,2}.weight / .bias, activations1.{0,1,2}.alpha, activations2.{0,1,2}.alpha;
+ *   resblocks.{0..8} (stage s, kernel j at 3 s + j) in the same per-block order; conv_post.weight / .bias.
+ * max_frames bounds a window's mel frames (with the 8 cached ones, at most 512); n_streams: live streams at most. */
+T2W_API int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int32_t n_weights,
+                            int32_t max_frames, int32_t n_streams, t2w_hift** out);
+T2W_API int t2w_hift_destroy(t2w_hift* h);
+/* A stream with empty caches (its first window has no cached mel frames, source or speech). */
+T2W_API int t2w_hift_stream_new(t2w_hift* h, int32_t* handle);
+T2W_API int t2w_hift_stream_release(t2w_hift* h, int32_t handle);
+
+typedef struct t2w_vocode_batch {
+  int32_t n_streams;
+  const int32_t* handle;   /* host [n] stream handles, pairwise distinct */
+  const int32_t* T;        /* host [n] window mel frames (a window that is not final needs T >= 8 on its first call) */
+  const uint8_t* last;     /* host [n] final window */
+  const float* mel;        /* device [sum T, mel] fp32, token-major (the solve's output rows) */
+  const float* rand_ini;   /* device [n, harmonics + 1]: the source's initial phases (no effect on the output: the
+                            * reference's linear downsampling of the phase increments never reads sample 0) */
+  const float* noise;      /* device: per window [harmonics + 1][480 F_i] (channel-major, the reference's draw), windows
+                            * concatenated; F_i = T_i plus the 8 cached frames after a stream's first window */
+  float* out;              /* device [t2w_vocode_samples]: each window's output samples, windows in order */
+  float* source;           /* device [sum 480 F_i] or NULL: the windows' source signals */
+  float* speech;           /* device [sum 480 F_i] or NULL: the windows' full speech (after the cross-fade) */
+} t2w_vocode_batch;
+/* Output samples of a call (the sum), per window (per_stream, may be NULL) and each window's frames F_i (frames, may
+ * be NULL); -1 on an invalid batch. */
+T2W_API int64_t t2w_vocode_samples(const t2w_hift* h, int32_t n, const int32_t* handle, const int32_t* T,
+                                   const uint8_t* last, int64_t* per_stream, int32_t* frames);
+/* One window per stream; asynchronous on `stream` (the call's scratch is a stream-ordered allocation). */
+T2W_API int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

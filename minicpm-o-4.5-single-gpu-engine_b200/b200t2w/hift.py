@@ -1,0 +1,178 @@
+"""Host side of the B200 HiFT vocoder (mel -> 24 kHz waveform), through the C ABI of ``libt2w_b200.so``.
+
+The reference vocodes a decode call's windows in ``BatchedToken2Wav._vocode`` (``engine/runtime/token2wav_batch.py:
+813-848``) with ``hift_forward`` (``engine/models/token2wav.py:230-245``) and keeps each stream's ``hift_cache`` (mel /
+source / speech tails).  ``B200HiFT`` keeps those caches in the library: a stream is a handle; ``vocode(handles, mels,
+lasts)`` runs every window of the call in one library call and returns each window's samples exactly as ``_vocode``
+returns them (held-back tail, leading silence of a first window, the Hamming cross-fade).  The source noise of a
+stream's chunk is drawn here as the reference draws it (``hift_noise``: a generator seeded with the chunk's seed, the
+initial phases then the additive noise, on the vocoder's device).  All arithmetic runs in the CUDA library; a missing
+library or a non-sm_100 device raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import lib as L
+from .config import HIFT, HiFTConfig
+
+
+def chunk_noise_seed(noise_seed: int, chunk: int) -> int:
+    """A stream's chunk seed (engine/models/token2wav.py:108-109)."""
+    return (noise_seed * 1_000_003 + chunk) & ((1 << 63) - 1)
+
+
+def hift_weight_names(cfg: HiFTConfig) -> list:
+    """State-dict paths of a HiFTGenerator in the order ``t2w_hift_create`` takes them (include/t2w_b200.h)."""
+    n = []
+    for l in range(cfg.f0_layers):
+        n += [f"f0_predictor.condnet.{2 * l}.weight", f"f0_predictor.condnet.{2 * l}.bias"]
+    n += ["f0_predictor.classifier.weight", "f0_predictor.classifier.bias", "m_source.l_linear.weight",
+          "m_source.l_linear.bias", "conv_pre.weight", "conv_pre.bias"]
+    for s in range(3):
+        n += [f"ups.{s}.weight", f"ups.{s}.bias"]
+
+    def block(p):
+        out = []
+        for d in range(3):
+            out += [f"{p}.convs1.{d}.weight", f"{p}.convs1.{d}.bias"]
+        for d in range(3):
+            out += [f"{p}.convs2.{d}.weight", f"{p}.convs2.{d}.bias"]
+        out += [f"{p}.activations1.{d}.alpha" for d in range(3)]
+        out += [f"{p}.activations2.{d}.alpha" for d in range(3)]
+        return out
+
+    for s in range(3):
+        n += [f"source_downs.{s}.weight", f"source_downs.{s}.bias"] + block(f"source_resblocks.{s}")
+    for b in range(9):
+        n += block(f"resblocks.{b}")
+    n += ["conv_post.weight", "conv_post.bias"]
+    return n
+
+
+class B200HiFT:
+    """The HiFT vocoder on one sm_100 GPU.  ``weights``: fp32 state dict of a HiFTGenerator (weight normalisation
+    folded); ``max_frames``: a window's mel frames at most, with the 8 cached ones (<= 512)."""
+
+    def __init__(self, cfg: HiFTConfig, weights: dict, device="cuda", max_frames: int = 128, n_streams: int = 256):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("B200HiFT needs a CUDA device (no CPU fallback)")
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.device = torch.device("cuda", idx)
+        self.lib = L.load()
+        if not self.lib.t2w_device_ok(idx):
+            raise RuntimeError(f"cuda:{idx} is not an sm_100 GPU: the B200 kernels cannot run there")
+        names = hift_weight_names(cfg)
+        missing = [k for k in names if k not in weights]
+        if missing:
+            raise KeyError(f"HiFT weights lack {missing[:4]}")
+        c = L.HiftConfig()
+        c.mel, c.channels, c.f0_channels, c.f0_layers = cfg.mel, cfg.channels, cfg.f0_channels, cfg.f0_layers
+        c.harmonics, c.sample_rate, c.n_fft, c.hop = cfg.harmonics, cfg.sample_rate, cfg.n_fft, cfg.hop
+        for f, v in (("up_rates", cfg.upsample_rates), ("up_kernels", cfg.upsample_kernels),
+                     ("res_kernels", cfg.resblock_kernels), ("source_kernels", cfg.source_kernels),
+                     ("dilations", cfg.dilations)):
+            setattr(c, f, (ctypes.c_int32 * 3)(*v))
+        c.nsf_alpha, c.nsf_sigma, c.voiced_threshold = cfg.nsf_alpha, cfg.nsf_sigma, cfg.voiced_threshold
+        c.lrelu_slope, c.audio_limit = cfg.lrelu_slope, cfg.audio_limit
+        with torch.cuda.device(self.device):
+            w = [weights[k].detach().to(self.device, torch.float32).contiguous() for k in names]
+            ptrs = (ctypes.c_void_p * len(w))(*[t.data_ptr() for t in w])
+            h = ctypes.c_void_p()
+            L.call("t2w_hift_create", ctypes.byref(c), ptrs, len(w), max_frames, n_streams, ctypes.byref(h))
+        self.handle = h
+        self.max_frames = max_frames
+        self._seeds: dict = {}  # handle -> [noise seed, chunks so far]
+
+    @classmethod
+    def from_module(cls, hift, cfg: HiFTConfig = HIFT, **kw) -> "B200HiFT":
+        return cls(cfg, {k: v.detach().float() for k, v in hift.state_dict().items()}, **kw)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.t2w_hift_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def new_stream(self, noise_seed: int = 0) -> int:
+        h = ctypes.c_int32()
+        L.call("t2w_hift_stream_new", self.handle, ctypes.byref(h))
+        self._seeds[h.value] = [int(noise_seed), 0]
+        return h.value
+
+    def release(self, handle: int) -> None:
+        L.call("t2w_hift_stream_release", self.handle, int(handle))
+        self._seeds.pop(int(handle), None)
+
+    def _noise(self, seed: int, n_samples: int):
+        """``hift_noise`` for one row (the reference draws on the vocoder's device)."""
+        g = torch.Generator(device=self.device).manual_seed(int(seed))
+        dim = self.cfg.harmonics + 1
+        rand_ini = torch.rand(1, dim, device=self.device, generator=g)
+        noise = torch.randn(1, dim, n_samples, device=self.device, generator=g)
+        return rand_ini, noise
+
+    def vocode(self, handles, mels, lasts, noise=None) -> list:
+        """One window per stream: ``mels[i]`` [mel, T_i], ``lasts[i]`` the final flag.  Returns each window's samples
+        (device fp32 tensors, ``_vocode``'s output).  ``noise``: optional per-window (rand_ini [1, dim], noise [1, dim,
+        480 F_i]) in place of the seeded draws (tests)."""
+        if len(mels) != len(handles) or len(lasts) != len(handles):
+            raise ValueError("one mel and one final flag per stream")
+        Ts = [int(m.shape[1]) for m in mels]
+        packed = torch.cat([m.t() for m in mels]).to(self.device, torch.float32).contiguous()
+        return self.vocode_packed(handles, packed, Ts, lasts, noise)
+
+    def vocode_packed(self, handles, mel_rows: torch.Tensor, Ts, lasts, noise=None) -> list:
+        """``vocode`` on the windows' mel rows token-major ``[sum T_i, mel]`` (the solve's output layout)."""
+        n = len(handles)
+        hs = L.i32_array(handles)
+        ts = L.i32_array(Ts)
+        ls = (ctypes.c_uint8 * n)(*[1 if x else 0 for x in lasts])
+        per = (ctypes.c_int64 * n)()
+        frames = (ctypes.c_int32 * n)()
+        tot = self.lib.t2w_vocode_samples(self.handle, n, hs, ts, ls, per, frames)
+        if tot < 0:
+            raise L.T2WError("t2w_vocode_samples", -1)
+        dim = self.cfg.harmonics + 1
+        with torch.cuda.device(self.device):
+            if noise is None:
+                draws = []
+                for i, h in enumerate(handles):
+                    seed, chunks = self._seeds[int(h)]
+                    draws.append(self._noise(chunk_noise_seed(seed, chunks), 480 * frames[i]))
+            else:
+                draws = noise
+            rand_ini = torch.cat([d[0].reshape(1, dim) for d in draws]).to(self.device, torch.float32).contiguous()
+            nz = torch.cat([d[1].reshape(-1) for d in draws]).to(self.device, torch.float32).contiguous()
+            out = torch.empty(int(tot), dtype=torch.float32, device=self.device)
+            b = L.VocodeBatch(n, hs, ts, ls, ctypes.c_void_p(mel_rows.data_ptr()), ctypes.c_void_p(rand_ini.data_ptr()),
+                              ctypes.c_void_p(nz.data_ptr()), ctypes.c_void_p(out.data_ptr()), None, None)
+            L.call("t2w_vocode", self.handle, ctypes.byref(b), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        for h in handles:
+            self._seeds[int(h)][1] += 1
+        res, o = [], 0
+        for i in range(n):
+            res.append(out[o:o + per[i]])
+            o += per[i]
+        return res
+
+    def vocode_numpy(self, handles, mels, lasts) -> list:
+        """``vocode`` with one device-to-host copy for the call (the reference's ``_vocode`` returns numpy arrays)."""
+        outs = self.vocode(handles, mels, lasts)
+        flat = torch.cat(outs).cpu().numpy() if outs else np.zeros(0, np.float32)
+        res, o = [], 0
+        for x in outs:
+            res.append(flat[o:o + x.numel()])
+            o += x.numel()
+        return res

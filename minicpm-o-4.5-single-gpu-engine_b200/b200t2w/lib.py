@@ -97,6 +97,19 @@ E_LAYER = ["self_attn.linear_q.weight", "self_attn.linear_q.bias", "self_attn.li
            "norm_ff.bias"]
 
 
+class HiftConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("mel", "channels", "f0_channels", "f0_layers", "harmonics", "sample_rate",
+                                              "n_fft", "hop")] + \
+               [(n, ctypes.c_int32 * 3) for n in ("up_rates", "up_kernels", "res_kernels", "source_kernels", "dilations")] + \
+               [(n, ctypes.c_float) for n in ("nsf_alpha", "nsf_sigma", "voiced_threshold", "lrelu_slope", "audio_limit")]
+
+
+class VocodeBatch(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_int32), ("handle", ctypes.POINTER(ctypes.c_int32)),
+                ("T", ctypes.POINTER(ctypes.c_int32)), ("last", ctypes.POINTER(ctypes.c_uint8))] + \
+               [(n, ctypes.c_void_p) for n in ("mel", "rand_ini", "noise", "out", "source", "speech")]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _F = ctypes.c_float
@@ -166,6 +179,13 @@ _SIGS = {
                          ctypes.POINTER(_I), ctypes.POINTER(_I), _I, _P, _P], ctypes.c_int),
     "t2w_enc_pos_table": ([_P, _I, _I, _F, _P, _P], ctypes.c_int),
     "t2w_enc_ln": ([_P, _P, _P, _F, _I, _I, _P, _P, _P, _P], ctypes.c_int),
+    "t2w_hift_create": ([ctypes.POINTER(HiftConfig), ctypes.POINTER(_P), _I, _I, _I, ctypes.POINTER(_P)], ctypes.c_int),
+    "t2w_hift_destroy": ([_P], ctypes.c_int),
+    "t2w_hift_stream_new": ([_P, ctypes.POINTER(_I)], ctypes.c_int),
+    "t2w_hift_stream_release": ([_P, _I], ctypes.c_int),
+    "t2w_vocode_samples": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_uint8),
+                            ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_I)], ctypes.c_int64),
+    "t2w_vocode": ([_P, ctypes.POINTER(VocodeBatch), _P], ctypes.c_int),
     "t2w_gemm_e4m3": ([_P, _I, _I, _P, _I, ctypes.c_int64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P,
                        ctypes.POINTER(_P), _F, _P], ctypes.c_int),
 }
@@ -180,7 +200,7 @@ def header_symbols() -> list[str]:
         if f.endswith(".h"):
             src = open(os.path.join(INCLUDE, f)).read()
             src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-            out += re.findall(r"^\s*(?:T2W_API\s+)?(?:size_t|int|void)\s+(t2w_\w+)\s*\(", src, flags=re.M)
+            out += re.findall(r"^\s*(?:T2W_API\s+)?(?:size_t|int64_t|int|void)\s+(t2w_\w+)\s*\(", src, flags=re.M)
     return out
 
 

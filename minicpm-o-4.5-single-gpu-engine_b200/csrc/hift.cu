@@ -1,0 +1,1114 @@
+// The HiFT vocoder (mel -> 24 kHz waveform), the step after the solve, and its C ABI (t2w_hift_*, t2w_vocode).
+//
+// The reference runs the third-party HiFTGenerator through its own driver functions (hift_forward_noise,
+// _hift_decode, istft_overlap_add: engine/models/token2wav.py:112-245) and does the streaming bookkeeping in
+// BatchedToken2Wav._vocode (engine/runtime/token2wav_batch.py:813-848): the window's mel after 8 cached frames, the
+// source's first 3840 samples from the previous window, a Hamming cross-fade with the previous window's last 3840
+// speech samples, and the last 3840 samples held back unless the window is final.  Here one call runs every window of
+// the batch (each with its own frame count) and keeps the per-stream caches in the library.
+//
+// Layout: time-major fp32 rows [time, channels].  Each window is a segment at each rate (mel frames F; stage outputs at
+// 8 F, 40 F and 120 F + 1 rows) with zero rows around its data so every "same" convolution reads zeros past the
+// window's ends: mel rate [4 | F | 4], stage 0 [32 | 8 F | 32], stage 1 [160 | 40 F | 160], stage 2 [479 | 120 F + 1 |
+// 480] (the reflection-padded row leads stage 2's data).  Every segment length at stage i is its rate times (F + 8), so
+// output row u v + p of a transposed convolution's phase p lands in the next layout at a fixed offset.
+//
+// Precision: strict fp32 everywhere (the reference runs Token2Wav with TF32 off, strict_fp32, token2wav.py:44-57).
+// Convolutions: k_hconv, a tiled fp32 implicit-GEMM kernel (64 output rows x 64 output channels per block, 4 x 4 per
+// thread, 16-channel K chunks staged in shared memory) with a general row mapping — strided (source_downs), dilated
+// (ResBlocks), and the polyphase form of the transposed convolutions (each output phase p of rate u is a convolution
+// over the input with taps j = j0(p) + u q) — and fused epilogues: ELU (f0 predictor), |.| (its head), Snake (the
+// ResBlocks' second activation, applied to conv1's output), and the residual update x += conv2(.) that also writes the
+// next Snake of x for the following conv1.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace t2w;
+
+namespace {
+
+#define H_CUDA(call)                     \
+  do {                                   \
+    cudaError_t e_ = (call);             \
+    if (e_ != cudaSuccess) {             \
+      set_cuda_error(e_);                \
+      return T2W_ERR_CUDA;               \
+    }                                    \
+  } while (0)
+#define H_TRY(call)         \
+  do {                      \
+    int rc_ = (call);       \
+    if (rc_) return rc_;    \
+  } while (0)
+
+constexpr int kMelCache = 8;          // cached mel frames (engine/models/token2wav.py:35)
+constexpr int kSrcCache = 3840;       // cached source / speech samples (8 frames x 480)
+constexpr int kPadMel = 4;            // zero rows on each side of a window's mel frames
+constexpr int kNfft = 16, kHop = 4, kBins = kNfft / 2 + 1;
+
+// ---------------------------------------------------------------- generic fp32 convolution
+enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4 };
+
+struct ConvGeo {
+  const int* vrow = nullptr;  // virtual rows: (stream << 20) | v, v the index within the stream
+  int nv = 0;
+  const int* in_start = nullptr;  // per stream: global row of its input data, and the data's length
+  const int* in_len = nullptr;
+  const int* out_start = nullptr;  // per stream: global row of its output data
+  const float* in = nullptr;
+  int ld_in = 0, Cin = 0;
+  float* out = nullptr;
+  int ld_out = 0, Cout = 0;
+  const float* W = nullptr;  // [Cout][taps][Cin]
+  const float* bias = nullptr;
+  int taps = 1, stride = 1, off = 0, dil = 1;  // input index of tap q = stride v + off + dil q (outside [0, len): 0)
+  int u_out = 1, p_out = 0;                    // output index = u_out v + p_out
+  int epi = HE_NONE;
+  const float* alpha = nullptr;  // HE_SNAKE: this conv's Snake; HE_RESID: the next Snake (out2), per channel
+  const float* inv = nullptr;    // 1 / (alpha + 1e-9)
+  float* out2 = nullptr;         // HE_RESID: Snake(x_new) for the next conv (nullptr: none)
+};
+
+constexpr int kTM = 64, kTN = 64, kTK = 16;
+
+__device__ __forceinline__ float snake(float x, float a, float inv) {
+  const float s = sinf(x * a);
+  return x + inv * (s * s);
+}
+
+__global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
+  __shared__ float As[kTK][kTM + 4];
+  __shared__ float Ws[kTK][kTN + 4];
+  __shared__ int rowb[kTM];  // per tile row: global input row of the stream's data start, or -1
+  __shared__ int rowv[kTM];  // input index of tap 0 (before the tap offset), and the data length below
+  __shared__ int rowl[kTM];
+  pdl_wait();
+  pdl_launch();
+  const int tid = threadIdx.x;
+  const int r0 = blockIdx.x * kTM, c0 = blockIdx.y * kTN;
+  if (tid < kTM) {
+    const int r = r0 + tid;
+    if (r < g.nv) {
+      const int e = g.vrow[r], s = e >> 20, v = e & 0xFFFFF;
+      rowb[tid] = g.in_start[s];
+      rowv[tid] = g.stride * v + g.off;
+      rowl[tid] = g.in_len[s];
+    } else {
+      rowb[tid] = -1;
+      rowv[tid] = 0;
+      rowl[tid] = 0;
+    }
+  }
+  __syncthreads();
+  const int ty = tid >> 4, tx = tid & 15;
+  float acc[4][4] = {};
+  const int kchunks = (g.Cin + kTK - 1) / kTK;
+  for (int q = 0; q < g.taps; ++q) {
+    for (int kc = 0; kc < kchunks; ++kc) {
+      const int ci0 = kc * kTK;
+      // A: 64 rows x 16 input channels (4 per thread: one row, 4 consecutive channels)
+      {
+        const int rr = tid >> 2, cc = (tid & 3) * 4;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (rowb[rr] >= 0) {
+          const int idx = rowv[rr] + g.dil * q;
+          if (idx >= 0 && idx < rowl[rr]) {
+            const float* src = g.in + (size_t)(rowb[rr] + idx) * g.ld_in;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (ci0 + cc + u < g.Cin) v[u] = src[ci0 + cc + u];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) As[cc + u][rr] = v[u];
+      }
+      // W: 64 output channels x 16 input channels
+      {
+        const int oo = tid >> 2, cc = (tid & 3) * 4;
+        const int co = c0 + oo;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int ci = ci0 + cc + u;
+          Ws[cc + u][oo] = (co < g.Cout && ci < g.Cin) ? g.W[((size_t)co * g.taps + q) * g.Cin + ci] : 0.f;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < kTK; ++k) {
+        const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
+        const float4 w = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
+        const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + ty * 4 + i;
+    if (r >= g.nv) continue;
+    const int e = g.vrow[r], s = e >> 20, v = e & 0xFFFFF;
+    const size_t orow = (size_t)(g.out_start[s] + g.u_out * v + g.p_out);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int co = c0 + tx * 4 + j;
+      if (co >= g.Cout) continue;
+      float y = acc[i][j] + g.bias[co];
+      float* dst = g.out + orow * g.ld_out + co;
+      switch (g.epi) {
+        case HE_ELU: y = y > 0.f ? y : expm1f(y); break;
+        case HE_ABS: y = fabsf(y); break;
+        case HE_SNAKE: y = snake(y, g.alpha[co], g.inv[co]); break;
+        case HE_RESID: {
+          y = y + *dst;
+          if (g.out2) g.out2[orow * g.ld_out + co] = snake(y, g.alpha[co], g.inv[co]);
+          break;
+        }
+        default: break;
+      }
+      *dst = y;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- elementwise / layout kernels
+// The window's mel rows: [cached 8 frames (unless first) | window frames] into the mel-rate layout (token-major input).
+struct HRow {
+  int F, first, cache, mel_off;   // mel frames (with the cached ones), first window, cache row, window's input row
+  int mel0, s0, s1, s2;           // data start rows at the mel rate and the three stage rates
+  int smp0;                        // first sample of the window in the sample-rate arrays
+  int last;                        // final window
+  int out0, out_len;               // output samples: offset and count
+};
+
+__global__ void k_mel_in(const float* __restrict__ win_mel, const HRow* __restrict__ rows, const float* __restrict__ cache,
+                         int cache_ld, int C, float* __restrict__ mel) {
+  pdl_wait();
+  pdl_launch();
+  const HRow e = rows[blockIdx.y];
+  const int t = blockIdx.x;
+  if (t >= e.F) return;
+  const int nc = e.first ? 0 : kMelCache;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float v = t < nc ? cache[(size_t)e.cache * cache_ld + t * C + c] : win_mel[(size_t)(e.mel_off + t - nc) * C + c];
+    mel[(size_t)(e.mel0 + t) * C + c] = v;
+  }
+}
+
+// In place: x = leaky_relu(x, slope) over rows (data and zero rows alike: leaky(0) = 0).
+__global__ void k_leaky(float* __restrict__ x, long long n, float slope) {
+  pdl_wait();
+  pdl_launch();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    x[i] = v > 0.f ? v : v * slope;
+  }
+}
+
+// x_j = x + src (three copies for the three ResBlocks), and Snake_j(x_j) of each ResBlock's first activation.
+struct Snake3 {
+  const float *al[3], *inv[3];
+};
+__global__ void k_fanout(const float* __restrict__ x, const float* __restrict__ src, long long n, int C, float* x0,
+                         float* x1, float* x2, float* a0, float* a1, float* a2, const Snake3 sn) {
+  pdl_wait();
+  pdl_launch();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const float v = x[i] + src[i];
+    x0[i] = v;
+    x1[i] = v;
+    x2[i] = v;
+    a0[i] = snake(v, sn.al[0][c], sn.inv[0][c]);
+    a1[i] = snake(v, sn.al[1][c], sn.inv[1][c]);
+    a2[i] = snake(v, sn.al[2][c], sn.inv[2][c]);
+  }
+}
+
+// y = leaky_relu((x0 + x1 + x2) / 3, slope)
+__global__ void k_avg3(const float* __restrict__ x0, const float* __restrict__ x1, const float* __restrict__ x2,
+                       long long n, float slope, float* __restrict__ y) {
+  pdl_wait();
+  pdl_launch();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = ((x0[i] + x1[i]) + x2[i]) / 3.f;
+    y[i] = v > 0.f ? v : v * slope;
+  }
+}
+
+// out = Snake(x) (the source ResBlock's first activation of its input).
+__global__ void k_snake(const float* __restrict__ x, long long n, int C, const float* __restrict__ al,
+                        const float* __restrict__ inv, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    out[i] = snake(x[i], al[c], inv[c]);
+  }
+}
+
+// Stage 2's reflection pad: the row before the transposed conv's output = its second row.
+__global__ void k_reflect_row(float* __restrict__ x, const HRow* __restrict__ rows, int C) {
+  pdl_wait();
+  pdl_launch();
+  const HRow e = rows[blockIdx.x];
+  for (int c = threadIdx.x; c < C; c += blockDim.x) x[(size_t)e.s2 * C + c] = x[(size_t)(e.s2 + 2) * C + c];
+}
+
+// The harmonic source, per window: rad of frame k and harmonic h = frac(f0_k (h + 1) / sr); its cumulative phase over
+// frames (2 pi sum), interpolated linearly to samples after the x upsample_scale product (the reference's
+// F.interpolate(... * upsample_scale, scale_factor=upsample_scale, mode="linear")); the sine, voiced / unvoiced noise
+// mix, linear over harmonics, tanh.  One block per window: the frame phases in shared memory.
+constexpr int kMaxFrames = 512;
+constexpr int kMaxHarm = 16;
+__global__ void __launch_bounds__(256) k_source(const float* __restrict__ f0, const HRow* __restrict__ rows,
+                                               const float* __restrict__ noise, const float* __restrict__ lin_w,
+                                               float lin_b, int dim, float sr, float upscale, float sine_amp,
+                                               float noise_std, float vthr, const float* __restrict__ cache,
+                                               int cache_ld, int cache_src_off, float* __restrict__ src) {
+  __shared__ float ph[kMaxFrames * kMaxHarm];
+  __shared__ float f0s[kMaxFrames];
+  pdl_wait();
+  pdl_launch();
+  const HRow e = rows[blockIdx.x];
+  const int F = e.F;
+  for (int t = threadIdx.x; t < F; t += blockDim.x) f0s[t] = f0[e.mel0 + t];
+  __syncthreads();
+  // cumulative phase per harmonic (sequential over frames, one thread per harmonic)
+  if (threadIdx.x < dim) {
+    const int h = threadIdx.x;
+    float c = 0.f;
+    for (int t = 0; t < F; ++t) {
+      const float fn = f0s[t] * (float)(h + 1);
+      const float r = fn / sr;
+      c += r - floorf(r);
+      ph[t * dim + h] = (c * 2.f) * 3.14159265358979323846f * upscale;
+    }
+  }
+  __syncthreads();
+  const int N = F * (int)upscale;
+  const float scale = 1.f / upscale;
+  const bool cached = !e.first;
+  for (int n = threadIdx.x; n < N; n += blockDim.x) {
+    float out;
+    if (cached && n < kSrcCache) {
+      out = cache[(size_t)e.cache * cache_ld + cache_src_off + n];
+    } else {
+      float sx = scale * ((float)n + 0.5f) - 0.5f;
+      if (sx < 0.f) sx = 0.f;
+      const int i0 = (int)sx;
+      const int i1 = i0 + (i0 < F - 1 ? 1 : 0);
+      const float l1 = sx - (float)i0, l0 = 1.f - l1;
+      const float f = f0s[n / (int)upscale];
+      const float uv = (f > vthr) ? 1.f : 0.f;
+      const float namp = uv * noise_std + (1.f - uv) * sine_amp / 3.f;
+      float acc = lin_b;
+      for (int h = 0; h < dim; ++h) {
+        const float phase = l0 * ph[i0 * dim + h] + l1 * ph[i1 * dim + h];
+        const float sine = sinf(phase) * sine_amp * uv + namp * noise[(size_t)e.smp0 * dim + (size_t)h * N + n];
+        acc = fmaf(lin_w[h], sine, acc);
+      }
+      out = tanhf(acc);
+    }
+    src[e.smp0 + n] = out;
+  }
+}
+
+// STFT of the source (n_fft 16, hop 4, periodic Hann, center with reflect padding): frame t of the window into stage-2
+// row s2 + t, 9 real parts then 9 imaginary parts.
+__global__ void k_stft(const float* __restrict__ src, const HRow* __restrict__ rows, const float* __restrict__ tw,
+                       float* __restrict__ out, int ld_out, float upscale) {
+  pdl_wait();
+  pdl_launch();
+  const HRow e = rows[blockIdx.y];
+  const int N = e.F * (int)upscale;
+  const int frames = N / kHop + 1;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= frames) return;
+  float x[kNfft];
+#pragma unroll
+  for (int k = 0; k < kNfft; ++k) {
+    int j = kHop * t + k - kNfft / 2;
+    if (j < 0) j = -j;
+    if (j >= N) j = 2 * (N - 1) - j;
+    x[k] = src[e.smp0 + j] * tw[k];  // tw[0..15]: the window
+  }
+  float* o = out + (size_t)(e.s2 + t) * ld_out;
+#pragma unroll
+  for (int m = 0; m < kBins; ++m) {
+    float re = 0.f, im = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNfft; ++k) {
+      re = fmaf(x[k], tw[16 + ((m * k) & 15)], re);   // cos(2 pi m k / 16)
+      im = fmaf(-x[k], tw[32 + ((m * k) & 15)], im);  // -sin(2 pi m k / 16)
+    }
+    o[m] = re;
+    o[kBins + m] = im;
+  }
+}
+
+// magnitude / phase of conv_post's output -> inverse STFT (per-frame real inverse DFT, window, overlap-add, / the
+// summed squared window, centre trim), clamp; then the cross-fade with the previous window's speech, the caches and the
+// window's output samples.  One thread per sample.
+__global__ void k_istft_out(const float* __restrict__ y, int ld_y, const HRow* __restrict__ rows, const float* __restrict__ tw,
+                            const double* __restrict__ hamming, float audio_limit, float upscale, float* __restrict__ speech,
+                            const float* __restrict__ cache, int cache_ld, int cache_sp_off, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
+  const HRow e = rows[blockIdx.y];
+  const int N = e.F * (int)upscale;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const int j = n + kNfft / 2;  // position in the overlap-added signal
+  const int T = N / kHop + 1;
+  float acc = 0.f, env = 0.f;
+  for (int t = max(0, (j - kNfft + kHop) / kHop); t <= j / kHop && t < T; ++t) {
+    const int k = j - kHop * t;
+    if (k < 0 || k >= kNfft) continue;
+    const float* row = y + (size_t)(e.s2 + t) * ld_y;
+    float v = 0.f;
+#pragma unroll
+    for (int m = 0; m < kBins; ++m) {
+      const float mag = fminf(expf(row[m]), 100.f);
+      const float p = sinf(row[kBins + m]);
+      const float re = mag * cosf(p), im = mag * sinf(p);
+      const float c = tw[16 + ((m * k) & 15)], s = tw[32 + ((m * k) & 15)];
+      const float term = re * c - im * s;
+      v += (m == 0 || m == kBins - 1) ? ((m == 0) ? re : re * c) : 2.f * term;
+    }
+    v *= (1.f / kNfft);
+    acc = fmaf(v, tw[k], acc);
+    env = fmaf(tw[k], tw[k], env);
+  }
+  float sp = fminf(fmaxf(acc / env, -audio_limit), audio_limit);
+  const float* cache_row = cache + (size_t)e.cache * cache_ld;
+  if (!e.first && n < kSrcCache)  // cross-fade with the previous window's last speech samples (float64 window)
+    sp = (float)((double)sp * hamming[n] + (double)cache_row[cache_sp_off + n] * hamming[kSrcCache + n]);
+  speech[e.smp0 + n] = sp;
+  // output: held back tail (unless final), leading silence of a first window
+  if (e.last) {
+    out[e.out0 + n] = sp;
+  } else if (e.first) {
+    if (n + kSrcCache < N) out[e.out0 + kSrcCache + n] = sp;
+    if (n < kSrcCache) out[e.out0 + n] = 0.f;
+  } else if (n < N - kSrcCache) {
+    out[e.out0 + n] = sp;
+  }
+}
+
+// The caches after a window (after k_istft_out has written the speech): the last 8 mel frames, 3840 source and 3840
+// speech samples.  One block per window.
+__global__ void k_hift_caches(const HRow* __restrict__ rows, const float* __restrict__ mel, int C,
+                              const float* __restrict__ src, const float* __restrict__ speech, float* __restrict__ cache,
+                              int cache_ld, int mel_off, int src_off, int sp_off, float upscale) {
+  pdl_wait();
+  pdl_launch();
+  const HRow e = rows[blockIdx.x];
+  const int N = e.F * (int)upscale;
+  float* c = cache + (size_t)e.cache * cache_ld;
+  for (int i = threadIdx.x; i < kMelCache * C; i += blockDim.x) {
+    const int t = e.F - kMelCache + i / C;
+    c[mel_off + i] = t >= 0 ? mel[(size_t)(e.mel0 + t) * C + i % C] : 0.f;
+  }
+  for (int i = threadIdx.x; i < kSrcCache; i += blockDim.x) {
+    const int n = N - kSrcCache + i;
+    c[src_off + i] = n >= 0 ? src[e.smp0 + n] : 0.f;
+    c[sp_off + i] = n >= 0 ? speech[e.smp0 + n] : 0.f;
+  }
+}
+
+inline int ck(cudaError_t e) {
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  return T2W_OK;
+}
+
+int grid_for(long long n) {
+  const long long b = (n + 255) / 256;
+  return (int)std::min<long long>(b, 148ll * 16);
+}
+
+size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+// ---------------------------------------------------------------- runtime
+
+struct HConv {
+  float* W = nullptr;  // [Cout][taps][Cin]
+  float* b = nullptr;
+  int Cin = 0, Cout = 0, k = 0;
+};
+struct HRes {
+  HConv c1[3], c2[3];
+  float *a1 = nullptr, *i1 = nullptr, *a2 = nullptr, *i2 = nullptr;  // [3][C] alphas and 1 / (alpha + 1e-9)
+  int k = 0;
+};
+struct HStage {
+  int u = 0, k = 0, pad = 0, Cin = 0, Cout = 0;
+  std::vector<HConv> phase;  // polyphase weights of the transposed conv: phase p -> [Cout][nq][Cin]
+  std::vector<int> nq, c;    // taps and input offset of each phase
+  float* b = nullptr;
+  HConv down;
+  int down_stride = 1, down_pad = 0;
+  HRes src, res[3];
+};
+
+struct t2w_hift {
+  t2w_hift_config cfg{};
+  int device = 0, n_streams = 0, max_frames = 0;
+  std::vector<void*> allocs;
+  HConv f0c[8], f0head, pre, post;
+  int f0_layers = 0;
+  float* lin_w = nullptr;
+  float lin_b = 0.f;
+  HStage st[3];
+  float* tw = nullptr;        // window, cos and sin tables (48 floats)
+  double* hamming = nullptr;  // 7680
+  float* cache = nullptr;     // [n_streams][8 mel frames x C | 3840 source | 3840 speech]
+  int cache_ld = 0;
+  std::vector<int> row_free;
+  std::vector<uint8_t> row_live, row_first;
+  std::mutex mu;
+};
+
+namespace {
+
+template <class T>
+int halloc(t2w_hift* h, T** p, size_t n) {
+  void* q = nullptr;
+  const cudaError_t rc = cudaMalloc(&q, std::max<size_t>(n * sizeof(T), 16));
+  if (rc != cudaSuccess) {
+    set_cuda_error(rc);
+    return rc == cudaErrorMemoryAllocation ? T2W_ERR_OOM : T2W_ERR_CUDA;
+  }
+  h->allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return T2W_OK;
+}
+int up(t2w_hift* h, const std::vector<float>& v, float** dst) {
+  H_TRY(halloc(h, dst, v.size()));
+  H_CUDA(cudaMemcpy(*dst, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  return T2W_OK;
+}
+int down(const float* src, size_t n, std::vector<float>& out) {
+  out.resize(n);
+  H_CUDA(cudaMemcpy(out.data(), src, n * 4, cudaMemcpyDeviceToHost));
+  return T2W_OK;
+}
+// Conv1d weight [out, in, k] -> [out][k][in] (tap-major rows per output channel).
+int conv(t2w_hift* h, const float* w, const float* b, int Cout, int Cin, int k, HConv* c) {
+  std::vector<float> hw, hb, t((size_t)Cout * k * Cin);
+  H_TRY(down(w, (size_t)Cout * Cin * k, hw));
+  H_TRY(down(b, Cout, hb));
+  for (int o = 0; o < Cout; ++o)
+    for (int i = 0; i < Cin; ++i)
+      for (int j = 0; j < k; ++j) t[((size_t)o * k + j) * Cin + i] = hw[((size_t)o * Cin + i) * k + j];
+  c->Cin = Cin;
+  c->Cout = Cout;
+  c->k = k;
+  H_TRY(up(h, t, &c->W));
+  return up(h, hb, &c->b);
+}
+int snake_params(t2w_hift* h, const float* const* a, int C, float** al, float** inv) {
+  std::vector<float> va((size_t)3 * C), vi((size_t)3 * C);
+  for (int d = 0; d < 3; ++d) {
+    std::vector<float> x;
+    H_TRY(down(a[d], C, x));
+    for (int c = 0; c < C; ++c) {
+      va[(size_t)d * C + c] = x[c];
+      vi[(size_t)d * C + c] = 1.0f / (x[c] + 1e-9f);
+    }
+  }
+  H_TRY(up(h, va, al));
+  return up(h, vi, inv);
+}
+
+int create_impl(t2w_hift* h, const float* const* W) {
+  const t2w_hift_config& c = h->cfg;
+  const float* const* w = W;
+  int i = 0;
+  auto next = [&]() { return w[i++]; };
+  h->f0_layers = c.f0_layers;
+  for (int l = 0; l < c.f0_layers; ++l) {
+    const float* wt = next();
+    const float* bt = next();
+    H_TRY(conv(h, wt, bt, c.f0_channels, l == 0 ? c.mel : c.f0_channels, 3, &h->f0c[l]));
+  }
+  {
+    const float* wt = next();
+    const float* bt = next();
+    H_TRY(conv(h, wt, bt, 1, c.f0_channels, 1, &h->f0head));
+  }
+  {
+    std::vector<float> lw, lb;
+    H_TRY(down(next(), c.harmonics + 1, lw));
+    H_TRY(down(next(), 1, lb));
+    H_TRY(up(h, lw, &h->lin_w));
+    h->lin_b = lb[0];
+  }
+  {
+    const float* wt = next();
+    const float* bt = next();
+    H_TRY(conv(h, wt, bt, c.channels, c.mel, 7, &h->pre));
+  }
+  const int rates[3] = {c.up_rates[0], c.up_rates[1], c.up_rates[2]};
+  int cum = 1;
+  for (int s = 1; s < 3; ++s) cum *= rates[s];  // 15 for 8, 5, 3
+  for (int s = 0; s < 3; ++s) {
+    HStage& g = h->st[s];
+    g.u = rates[s];
+    g.k = c.up_kernels[s];
+    g.pad = (g.k - g.u) / 2;
+    g.Cin = c.channels >> s;
+    g.Cout = c.channels >> (s + 1);
+    // ConvTranspose1d weight [Cin, Cout, k]: output t = u m - pad + j reads input m; phase p = t mod u uses taps
+    // j = (p + pad) mod u + u q, input index m = (t + pad - j) / u = v + c_p - q for t = u v + p
+    std::vector<float> hw, hb;
+    H_TRY(down(next(), (size_t)g.Cin * g.Cout * g.k, hw));
+    H_TRY(down(next(), g.Cout, hb));
+    H_TRY(up(h, hb, &g.b));
+    g.phase.resize(g.u);
+    g.nq.resize(g.u);
+    g.c.resize(g.u);
+    for (int p = 0; p < g.u; ++p) {
+      const int j0 = (p + g.pad) % g.u;
+      const int nq = (g.k - j0 + g.u - 1) / g.u;
+      g.nq[p] = nq;
+      g.c[p] = (p + g.pad - j0) / g.u;
+      std::vector<float> t((size_t)g.Cout * nq * g.Cin);
+      for (int o = 0; o < g.Cout; ++o)
+        for (int q = 0; q < nq; ++q)
+          for (int ci = 0; ci < g.Cin; ++ci) t[((size_t)o * nq + q) * g.Cin + ci] = hw[((size_t)ci * g.Cout + o) * g.k + j0 + g.u * q];
+      g.phase[p].Cin = g.Cin;
+      g.phase[p].Cout = g.Cout;
+      g.phase[p].k = nq;
+      H_TRY(up(h, t, &g.phase[p].W));
+      g.phase[p].b = g.b;
+    }
+  }
+  // source_downs and source ResBlocks
+  for (int s = 0; s < 3; ++s) {
+    HStage& g = h->st[s];
+    const int u = s == 0 ? cum : (s == 1 ? rates[2] : 1);
+    const int k = u == 1 ? 1 : 2 * u;
+    g.down_stride = u;
+    g.down_pad = u == 1 ? 0 : u / 2;
+    const float* wt = next();
+    const float* bt = next();
+    H_TRY(conv(h, wt, bt, g.Cout, kNfft + 2, k, &g.down));
+    HRes& r = g.src;
+    r.k = c.source_kernels[s];
+    const float* a1[3];
+    const float* a2[3];
+    for (int d = 0; d < 3; ++d) {
+      const float* w1 = next();
+      const float* b1 = next();
+      H_TRY(conv(h, w1, b1, g.Cout, g.Cout, r.k, &r.c1[d]));
+    }
+    for (int d = 0; d < 3; ++d) {
+      const float* w2 = next();
+      const float* b2 = next();
+      H_TRY(conv(h, w2, b2, g.Cout, g.Cout, r.k, &r.c2[d]));
+    }
+    for (int d = 0; d < 3; ++d) a1[d] = next();
+    for (int d = 0; d < 3; ++d) a2[d] = next();
+    H_TRY(snake_params(h, a1, g.Cout, &r.a1, &r.i1));
+    H_TRY(snake_params(h, a2, g.Cout, &r.a2, &r.i2));
+  }
+  for (int s = 0; s < 3; ++s)
+    for (int j = 0; j < 3; ++j) {
+      HStage& g = h->st[s];
+      HRes& r = g.res[j];
+      r.k = c.res_kernels[j];
+      const float* a1[3];
+      const float* a2[3];
+      for (int d = 0; d < 3; ++d) {
+        const float* w1 = next();
+        const float* b1 = next();
+        H_TRY(conv(h, w1, b1, g.Cout, g.Cout, r.k, &r.c1[d]));
+      }
+      for (int d = 0; d < 3; ++d) {
+        const float* w2 = next();
+        const float* b2 = next();
+        H_TRY(conv(h, w2, b2, g.Cout, g.Cout, r.k, &r.c2[d]));
+      }
+      for (int d = 0; d < 3; ++d) a1[d] = next();
+      for (int d = 0; d < 3; ++d) a2[d] = next();
+      H_TRY(snake_params(h, a1, g.Cout, &r.a1, &r.i1));
+      H_TRY(snake_params(h, a2, g.Cout, &r.a2, &r.i2));
+    }
+  {
+    const float* wt = next();
+    const float* bt = next();
+    H_TRY(conv(h, wt, bt, kNfft + 2, c.channels >> 3, 7, &h->post));
+  }
+  // window (periodic Hann), cos / sin tables of 2 pi k / 16, Hamming cross-fade window (float64, as np.hamming)
+  std::vector<float> tw(48);
+  for (int k = 0; k < 16; ++k) {
+    tw[k] = (float)(0.5 - 0.5 * std::cos(2.0 * M_PI * k / 16.0));
+    tw[16 + k] = (float)std::cos(2.0 * M_PI * k / 16.0);
+    tw[32 + k] = (float)std::sin(2.0 * M_PI * k / 16.0);
+  }
+  H_TRY(up(h, tw, &h->tw));
+  std::vector<double> hm(2 * kSrcCache);
+  for (int n = 0; n < 2 * kSrcCache; ++n) hm[n] = 0.54 - 0.46 * std::cos(2.0 * M_PI * n / (2 * kSrcCache - 1));
+  H_TRY(halloc(h, &h->hamming, hm.size()));
+  H_CUDA(cudaMemcpy(h->hamming, hm.data(), hm.size() * 8, cudaMemcpyHostToDevice));
+  h->cache_ld = kMelCache * c.mel + 2 * kSrcCache;
+  H_TRY(halloc(h, &h->cache, (size_t)h->n_streams * h->cache_ld));
+  H_CUDA(cudaMemset(h->cache, 0, (size_t)h->n_streams * h->cache_ld * 4));
+  for (int r = h->n_streams - 1; r >= 0; --r) h->row_free.push_back(r);
+  h->row_live.assign(h->n_streams, 0);
+  h->row_first.assign(h->n_streams, 1);
+  return T2W_OK;
+}
+
+void free_all(t2w_hift* h) {
+  for (void* p : h->allocs) cudaFree(p);
+  h->allocs.clear();
+}
+
+// ---- a call's plan
+struct HPlan {
+  int n = 0;
+  std::vector<HRow> rows;
+  int R[4] = {};  // rows at the mel rate and the three stage rates
+  std::vector<int> vr_mel, vr_s[3], vr_stft;  // virtual rows: data rows of each rate, and the STFT frames
+  std::vector<int> start_mel, len_mel, start_s[3], len_s[3], start_up[3];
+  long long samples = 0, out_samples = 0;
+};
+
+int make_plan(t2w_hift* h, int n, const int32_t* handle, const int32_t* T, const uint8_t* last, HPlan& pl) {
+  pl = HPlan();
+  pl.n = n;
+  const int up = (int)(h->cfg.up_rates[0] * h->cfg.up_rates[1] * h->cfg.up_rates[2]) * kHop;  // 480
+  int rm = 0, r0 = 0, r1 = 0, r2 = 0, mel_off = 0;
+  long long smp = 0, outp = 0;
+  for (int i = 0; i < n; ++i) {
+    const int row = handle[i];
+    const bool first = h->row_first[row] != 0;
+    const int F = T[i] + (first ? 0 : kMelCache);
+    if (T[i] <= 0 || F > h->max_frames || (!last[i] && F < kMelCache)) return T2W_ERR_INVALID;
+    const int N = F * up;
+    HRow e{};
+    e.F = F;
+    e.first = first;
+    e.cache = row;
+    e.mel_off = mel_off;
+    e.mel0 = rm + kPadMel;
+    e.s0 = r0 + 8 * kPadMel;
+    e.s1 = r1 + 40 * kPadMel;
+    e.s2 = r2 + 120 * kPadMel - 1;
+    e.smp0 = (int)smp;
+    e.last = last[i] != 0;
+    e.out0 = (int)outp;
+    e.out_len = e.last ? N : (first ? N : N - kSrcCache);
+    pl.rows.push_back(e);
+    for (int t = 0; t < F; ++t) pl.vr_mel.push_back((i << 20) | t);
+    for (int t = 0; t < 8 * F; ++t) pl.vr_s[0].push_back((i << 20) | t);
+    for (int t = 0; t < 40 * F; ++t) pl.vr_s[1].push_back((i << 20) | t);
+    for (int t = 0; t < 120 * F + 1; ++t) pl.vr_s[2].push_back((i << 20) | t);
+    pl.start_mel.push_back(e.mel0);
+    pl.len_mel.push_back(F);
+    pl.start_s[0].push_back(e.s0);
+    pl.len_s[0].push_back(8 * F);
+    pl.start_s[1].push_back(e.s1);
+    pl.len_s[1].push_back(40 * F);
+    pl.start_s[2].push_back(e.s2);
+    pl.len_s[2].push_back(120 * F + 1);
+    // the transposed conv of stage s writes output row u v + p at the stage's data start (stage 2: after the
+    // reflection row)
+    pl.start_up[0].push_back(e.s0);
+    pl.start_up[1].push_back(e.s1);
+    pl.start_up[2].push_back(e.s2 + 1);
+    rm += F + 2 * kPadMel;
+    r0 += 8 * (F + 2 * kPadMel);
+    r1 += 40 * (F + 2 * kPadMel);
+    r2 += 120 * (F + 2 * kPadMel);
+    mel_off += T[i];
+    smp += N;
+    outp += e.out_len;
+  }
+  pl.R[0] = rm;
+  pl.R[1] = r0;
+  pl.R[2] = r1;
+  pl.R[3] = r2;
+  pl.samples = smp;
+  pl.out_samples = outp;
+  return T2W_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int32_t n_weights, int32_t max_frames,
+                    int32_t n_streams, t2w_hift** out) {
+  // window rows are tagged (stream << 20 | row) in 32-bit words: at most 2047 streams
+  if (!cfg || !weights || !out || n_streams <= 0 || n_streams > 2047 || max_frames < kMelCache + 1 || max_frames > 4096)
+    return T2W_ERR_INVALID;
+  const t2w_hift_config& c = *cfg;
+  if (c.mel <= 0 || c.channels % 64 || c.channels < 64 || c.f0_layers < 1 || c.f0_layers > 8 || c.harmonics + 1 > kMaxHarm ||
+      c.n_fft != kNfft || c.hop != kHop || c.up_rates[0] * c.up_rates[1] * c.up_rates[2] * kHop != 480 ||
+      c.up_rates[0] != 8 || c.up_rates[1] != 5 || c.up_rates[2] != 3)
+    return T2W_ERR_UNSUPPORTED;
+  for (int s = 0; s < 3; ++s)
+    if (c.up_kernels[s] - c.up_rates[s] < 0 || (c.up_kernels[s] - c.up_rates[s]) % 2 ||
+        c.up_kernels[s] - 2 * ((c.up_kernels[s] - c.up_rates[s]) / 2) != c.up_rates[s])
+      return T2W_ERR_UNSUPPORTED;
+  if (max_frames > kMaxFrames) return T2W_ERR_INVALID;
+  const int expect = 2 * c.f0_layers + 2 + 2 + 2 + 3 * 2 + 3 * (2 + 18) + 9 * 18 + 2;
+  if (n_weights != expect) return T2W_ERR_INVALID;
+  for (int i = 0; i < n_weights; ++i)
+    if (!weights[i]) return T2W_ERR_INVALID;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || !t2w_device_ok(dev)) return T2W_ERR_UNSUPPORTED;
+  t2w_hift* h = new t2w_hift();
+  h->cfg = c;
+  h->device = dev;
+  h->n_streams = n_streams;
+  h->max_frames = max_frames;
+  const int rc = create_impl(h, weights);
+  if (rc) {
+    free_all(h);
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return T2W_OK;
+}
+
+int t2w_hift_destroy(t2w_hift* h) {
+  if (!h) return T2W_ERR_INVALID;
+  cudaDeviceSynchronize();
+  free_all(h);
+  delete h;
+  return T2W_OK;
+}
+
+int t2w_hift_stream_new(t2w_hift* h, int32_t* handle) {
+  if (!h || !handle) return T2W_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(h->mu);
+  if (h->row_free.empty()) return T2W_ERR_EXHAUSTED;
+  const int r = h->row_free.back();
+  h->row_free.pop_back();
+  h->row_live[r] = 1;
+  h->row_first[r] = 1;
+  *handle = r;
+  return T2W_OK;
+}
+
+int t2w_hift_stream_release(t2w_hift* h, int32_t handle) {
+  if (!h || handle < 0 || handle >= h->n_streams) return T2W_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(h->mu);
+  if (!h->row_live[handle]) return T2W_ERR_INVALID;
+  h->row_live[handle] = 0;
+  h->row_free.push_back(handle);
+  return T2W_OK;
+}
+
+int64_t t2w_vocode_samples(const t2w_hift* h, int32_t n, const int32_t* handle, const int32_t* T, const uint8_t* last,
+                           int64_t* per_stream, int32_t* frames) {
+  if (!h || n <= 0 || !handle || !T || !last) return -1;
+  std::lock_guard<std::mutex> lk(const_cast<t2w_hift*>(h)->mu);
+  long long tot = 0;
+  for (int i = 0; i < n; ++i) {
+    if (handle[i] < 0 || handle[i] >= h->n_streams || !h->row_live[handle[i]] || T[i] <= 0) return -1;
+    const bool first = h->row_first[handle[i]] != 0;
+    const long long N = 480ll * (T[i] + (first ? 0 : kMelCache));
+    const long long o = last[i] ? N : (first ? N : N - kSrcCache);
+    if (per_stream) per_stream[i] = o;
+    if (frames) frames[i] = T[i] + (first ? 0 : kMelCache);
+    tot += o;
+  }
+  return tot;
+}
+
+int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
+  if (!h || !b || b->n_streams <= 0 || !b->handle || !b->T || !b->last || !b->mel || !b->rand_ini || !b->noise || !b->out)
+    return T2W_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lk(h->mu);
+  const int n = b->n_streams;
+  for (int i = 0; i < n; ++i) {
+    if (b->handle[i] < 0 || b->handle[i] >= h->n_streams || !h->row_live[b->handle[i]]) return T2W_ERR_INVALID;
+    for (int j = 0; j < i; ++j)
+      if (b->handle[j] == b->handle[i]) return T2W_ERR_INVALID;
+  }
+  HPlan pl;
+  H_TRY(make_plan(h, n, b->handle, b->T, b->last, pl));
+  const t2w_hift_config& c = h->cfg;
+  const int C0 = c.channels;
+  // device buffers for this call (stream-ordered allocations)
+  size_t meta = 0;
+  auto add = [&](size_t bytes) {
+    const size_t o = meta;
+    meta = a256(meta + bytes);
+    return o;
+  };
+  const size_t o_rows = add(pl.rows.size() * sizeof(HRow));
+  const size_t o_vm = add(pl.vr_mel.size() * 4), o_sm = add(n * 4), o_lm = add(n * 4);
+  size_t o_vs[3], o_ss[3], o_ls[3], o_su[3];
+  for (int s = 0; s < 3; ++s) {
+    o_vs[s] = add(pl.vr_s[s].size() * 4);
+    o_ss[s] = add(n * 4);
+    o_ls[s] = add(n * 4);
+    o_su[s] = add(n * 4);
+  }
+  const size_t meta_bytes = meta;
+  const size_t o_mel = add((size_t)pl.R[0] * c.mel * 4);
+  const size_t o_f0a = add((size_t)pl.R[0] * c.f0_channels * 4), o_f0b = add((size_t)pl.R[0] * c.f0_channels * 4);
+  const size_t o_f0 = add((size_t)pl.R[0] * 4);
+  const size_t o_src = add((size_t)pl.samples * 4), o_sp = add((size_t)pl.samples * 4);
+  const size_t o_stft = add((size_t)pl.R[3] * (kNfft + 2) * 4);
+  const size_t o_x0 = add((size_t)pl.R[0] * C0 * 4);
+  // per stage: x (ups output), xr[3] ResBlock streams, ar[3] / sd scratch of the stage's size
+  size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3];
+  for (int s = 0; s < 3; ++s) {
+    const size_t sz = (size_t)pl.R[s + 1] * (C0 >> (s + 1)) * 4;
+    o_xs[s] = add(sz);
+    for (int j = 0; j < 3; ++j) o_xr[s][j] = add(sz);
+    for (int j = 0; j < 3; ++j) o_ar[s][j] = add(sz);
+    o_sd[s] = add(sz);
+    o_ta[s] = add(sz);
+  }
+  const size_t o_post = add((size_t)pl.R[3] * (kNfft + 2) * 4);
+  const size_t total = meta;
+  uint8_t* ws = nullptr;
+  H_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), total, st));
+  auto P = [&](size_t o) { return ws + o; };
+  std::vector<uint8_t> img(meta_bytes);
+  auto put = [&](size_t o, const void* s, size_t bytes) {
+    if (bytes) std::memcpy(img.data() + o, s, bytes);
+  };
+  put(o_rows, pl.rows.data(), pl.rows.size() * sizeof(HRow));
+  put(o_vm, pl.vr_mel.data(), pl.vr_mel.size() * 4);
+  put(o_sm, pl.start_mel.data(), n * 4);
+  put(o_lm, pl.len_mel.data(), n * 4);
+  for (int s = 0; s < 3; ++s) {
+    put(o_vs[s], pl.vr_s[s].data(), pl.vr_s[s].size() * 4);
+    put(o_ss[s], pl.start_s[s].data(), n * 4);
+    put(o_ls[s], pl.len_s[s].data(), n * 4);
+    put(o_su[s], pl.start_up[s].data(), n * 4);
+  }
+  int rc = T2W_OK;
+  auto fail = [&](int r) {
+    cudaFreeAsync(ws, st);
+    return r;
+  };
+  {
+    const cudaError_t e1 = cudaMemcpyAsync(ws, img.data(), meta_bytes, cudaMemcpyHostToDevice, st);
+    // every activation buffer starts at zero: the zero rows around each window's data are the convolutions' padding
+    const cudaError_t e2 = cudaMemsetAsync(ws + meta_bytes, 0, total - meta_bytes, st);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) {
+      set_cuda_error(e1 != cudaSuccess ? e1 : e2);
+      return fail(T2W_ERR_CUDA);
+    }
+  }
+  const HRow* drows = reinterpret_cast<const HRow*>(P(o_rows));
+  float* mel = reinterpret_cast<float*>(P(o_mel));
+  auto run = [&](ConvGeo g) -> int {
+    if (g.nv <= 0) return T2W_OK;
+    dim3 grid((g.nv + kTM - 1) / kTM, (g.Cout + kTN - 1) / kTN);
+    return ck(launch_k(k_hconv, grid, dim3(256), 0, st, g));
+  };
+  auto geo = [&](const HConv& cv, const int* vr, int nv, const int* in_s, const int* in_l, const int* out_s,
+                 const float* in, float* outp, int epi) {
+    ConvGeo g;
+    g.vrow = vr;
+    g.nv = nv;
+    g.in_start = in_s;
+    g.in_len = in_l;
+    g.out_start = out_s;
+    g.in = in;
+    g.ld_in = cv.Cin;
+    g.Cin = cv.Cin;
+    g.out = outp;
+    g.ld_out = cv.Cout;
+    g.Cout = cv.Cout;
+    g.W = cv.W;
+    g.bias = cv.b;
+    g.taps = cv.k;
+    g.stride = 1;
+    g.off = -(cv.k / 2);
+    g.dil = 1;
+    g.epi = epi;
+    return g;
+  };
+  const int* vm = reinterpret_cast<const int*>(P(o_vm));
+  const int* sm = reinterpret_cast<const int*>(P(o_sm));
+  const int* lm = reinterpret_cast<const int*>(P(o_lm));
+  // 1. mel rows
+  {
+    dim3 grid(h->max_frames, n);
+    rc = ck(launch_k(k_mel_in, grid, dim3(128), 0, st, b->mel, drows, (const float*)h->cache, h->cache_ld, c.mel, mel));
+    if (rc) return fail(rc);
+  }
+  // 2. f0 predictor: convs + ELU, then |linear|
+  {
+    float* a = reinterpret_cast<float*>(P(o_f0a));
+    float* bb = reinterpret_cast<float*>(P(o_f0b));
+    const float* in = mel;
+    for (int l = 0; l < h->f0_layers; ++l) {
+      float* o = (l & 1) ? bb : a;
+      rc = run(geo(h->f0c[l], vm, (int)pl.vr_mel.size(), sm, lm, sm, in, o, HE_ELU));
+      if (rc) return fail(rc);
+      in = o;
+    }
+    rc = run(geo(h->f0head, vm, (int)pl.vr_mel.size(), sm, lm, sm, in, reinterpret_cast<float*>(P(o_f0)), HE_ABS));
+    if (rc) return fail(rc);
+  }
+  // 3. the harmonic source, 4. its STFT
+  float* src = reinterpret_cast<float*>(P(o_src));
+  float* stft = reinterpret_cast<float*>(P(o_stft));
+  {
+    rc = ck(launch_k(k_source, dim3(n), dim3(256), 0, st, (const float*)P(o_f0), drows, b->noise, (const float*)h->lin_w,
+                     h->lin_b, c.harmonics + 1, (float)c.sample_rate, 480.f, c.nsf_alpha, c.nsf_sigma, c.voiced_threshold,
+                     (const float*)h->cache, h->cache_ld, kMelCache * c.mel, src));
+    if (rc) return fail(rc);
+    dim3 grid((120 * h->max_frames + 1 + 127) / 128, n);
+    rc = ck(launch_k(k_stft, grid, dim3(128), 0, st, (const float*)src, drows, (const float*)h->tw, stft, kNfft + 2, 480.f));
+    if (rc) return fail(rc);
+  }
+  // 5. conv_pre
+  float* x = reinterpret_cast<float*>(P(o_x0));
+  rc = run(geo(h->pre, vm, (int)pl.vr_mel.size(), sm, lm, sm, mel, x, HE_NONE));
+  if (rc) return fail(rc);
+  // 6. stages
+  const int* vin = vm;
+  const int* s_in = sm;
+  const int* l_in = lm;
+  int nvin = (int)pl.vr_mel.size();
+  for (int s = 0; s < 3; ++s) {
+    HStage& g = h->st[s];
+    const int Cs = g.Cout;
+    const long long nel_in = (long long)pl.R[s] * g.Cin;
+    rc = ck(launch_k(k_leaky, dim3(grid_for(nel_in)), dim3(256), 0, st, x, nel_in, c.lrelu_slope));
+    if (rc) return fail(rc);
+    float* xs = reinterpret_cast<float*>(P(o_xs[s]));
+    const int* vs = reinterpret_cast<const int*>(P(o_vs[s]));
+    const int* ss = reinterpret_cast<const int*>(P(o_ss[s]));
+    const int* ls = reinterpret_cast<const int*>(P(o_ls[s]));
+    const int* su = reinterpret_cast<const int*>(P(o_su[s]));
+    // transposed conv, one launch per output phase over the input's data rows
+    for (int p = 0; p < g.u; ++p) {
+      ConvGeo cg = geo(g.phase[p], vin, nvin, s_in, l_in, su, x, xs, HE_NONE);
+      cg.off = g.c[p];
+      cg.dil = -1;
+      cg.u_out = g.u;
+      cg.p_out = p;
+      rc = run(cg);
+      if (rc) return fail(rc);
+    }
+    if (s == 2) {
+      rc = ck(launch_k(k_reflect_row, dim3(n), dim3(64), 0, st, xs, drows, Cs));
+      if (rc) return fail(rc);
+    }
+    // source branch: strided conv of the STFT, then its ResBlock (in place)
+    float* sd = reinterpret_cast<float*>(P(o_sd[s]));
+    float* ta = reinterpret_cast<float*>(P(o_ta[s]));
+    {
+      ConvGeo cg = geo(g.down, vs, (int)pl.vr_s[s].size(), reinterpret_cast<const int*>(P(o_ss[2])),
+                       reinterpret_cast<const int*>(P(o_ls[2])), ss, stft, sd, HE_NONE);
+      cg.stride = g.down_stride;
+      cg.off = -g.down_pad;
+      rc = run(cg);
+      if (rc) return fail(rc);
+    }
+    const long long nel = (long long)pl.R[s + 1] * Cs;
+    auto resblock = [&](HRes& r, float* xr, float* a_in, float* tmp) -> int {
+      // a_in holds Snake1_0(xr); per dilation: tmp = Snake2(conv1(a_in)); xr += conv2(tmp), a_in = Snake1_next(xr)
+      for (int dd = 0; dd < 3; ++dd) {
+        const int dl = h->cfg.dilations[dd];
+        ConvGeo c1 = geo(r.c1[dd], vs, (int)pl.vr_s[s].size(), ss, ls, ss, a_in, tmp, HE_SNAKE);
+        c1.dil = dl;
+        c1.off = -(r.k * dl - dl) / 2;
+        c1.alpha = r.a2 + dd * Cs;
+        c1.inv = r.i2 + dd * Cs;
+        H_TRY(run(c1));
+        ConvGeo c2 = geo(r.c2[dd], vs, (int)pl.vr_s[s].size(), ss, ls, ss, tmp, xr, HE_RESID);
+        c2.off = -(r.k - 1) / 2;
+        if (dd < 2) {
+          c2.alpha = r.a1 + (dd + 1) * Cs;
+          c2.inv = r.i1 + (dd + 1) * Cs;
+          c2.out2 = a_in;
+        }
+        H_TRY(run(c2));
+      }
+      return T2W_OK;
+    };
+    rc = ck(launch_k(k_snake, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)sd, nel, Cs, (const float*)g.src.a1,
+                     (const float*)g.src.i1, ta));
+    if (rc) return fail(rc);
+    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])));  // xr[0] as scratch before the fan-out
+    if (rc) return fail(rc);
+    float* xr[3] = {reinterpret_cast<float*>(P(o_xr[s][0])), reinterpret_cast<float*>(P(o_xr[s][1])),
+                    reinterpret_cast<float*>(P(o_xr[s][2]))};
+    float* ar[3] = {reinterpret_cast<float*>(P(o_ar[s][0])), reinterpret_cast<float*>(P(o_ar[s][1])),
+                    reinterpret_cast<float*>(P(o_ar[s][2]))};
+    // x_j = ups(x) + source branch for the three ResBlocks, with each block's first Snake of it
+    Snake3 sn;
+    for (int j = 0; j < 3; ++j) {
+      sn.al[j] = g.res[j].a1;
+      sn.inv[j] = g.res[j].i1;
+    }
+    rc = ck(launch_k(k_fanout, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs, xr[0],
+                     xr[1], xr[2], ar[0], ar[1], ar[2], sn));
+    if (rc) return fail(rc);
+    for (int j = 0; j < 3; ++j) {
+      rc = resblock(g.res[j], xr[j], ar[j], ta);
+      if (rc) return fail(rc);
+    }
+    // the stage's output (x0 + x1 + x2) / 3; after the last stage with leaky_relu(., 0.01), conv_post's input (the
+    // next stage applies its own leaky_relu at its start)
+    float* nx = reinterpret_cast<float*>(P(o_sd[s]));
+    rc = ck(launch_k(k_avg3, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xr[0], (const float*)xr[1],
+                     (const float*)xr[2], nel, s < 2 ? 1.0f : 0.01f, nx));
+    if (rc) return fail(rc);
+    x = nx;
+    vin = vs;
+    s_in = ss;
+    l_in = ls;
+    nvin = (int)pl.vr_s[s].size();
+  }
+  // 7. conv_post, inverse STFT, cross-fade, output, caches
+  float* post = reinterpret_cast<float*>(P(o_post));
+  {
+    const int* ss2 = reinterpret_cast<const int*>(P(o_ss[2]));
+    const int* ls2 = reinterpret_cast<const int*>(P(o_ls[2]));
+    rc = run(geo(h->post, reinterpret_cast<const int*>(P(o_vs[2])), (int)pl.vr_s[2].size(), ss2, ls2, ss2, x, post,
+                 HE_NONE));
+    if (rc) return fail(rc);
+  }
+  float* speech = reinterpret_cast<float*>(P(o_sp));
+  {
+    dim3 grid((480 * h->max_frames + 255) / 256, n);
+    rc = ck(launch_k(k_istft_out, grid, dim3(256), 0, st, (const float*)post, kNfft + 2, drows, (const float*)h->tw,
+                     (const double*)h->hamming, c.audio_limit, 480.f, speech, (const float*)h->cache, h->cache_ld,
+                     kMelCache * c.mel + kSrcCache, b->out));
+    if (rc) return fail(rc);
+    rc = ck(launch_k(k_hift_caches, dim3(n), dim3(256), 0, st, drows, (const float*)mel, c.mel, (const float*)src,
+                     (const float*)speech, h->cache, h->cache_ld, 0, kMelCache * c.mel, kMelCache * c.mel + kSrcCache,
+                     480.f));
+    if (rc) return fail(rc);
+  }
+  if (b->source) H_CUDA(cudaMemcpyAsync(b->source, src, (size_t)pl.samples * 4, cudaMemcpyDeviceToDevice, st));
+  if (b->speech) H_CUDA(cudaMemcpyAsync(b->speech, speech, (size_t)pl.samples * 4, cudaMemcpyDeviceToDevice, st));
+  cudaFreeAsync(ws, st);
+  for (int i = 0; i < n; ++i) h->row_first[b->handle[i]] = 0;
+  return T2W_OK;
+}
+
+}  // extern "C"

@@ -63,7 +63,7 @@ def args_():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="c5", choices=["c5", "c2", "target", "c3", "c4", "steady", "encoder"])
+    ap.add_argument("--workload", default="c5", choices=["c5", "c2", "target", "c3", "c4", "steady", "encoder", "hift"])
     ap.add_argument("--batch", type=int, default=64, help="streams per solve on a rank (c5) / windows per call (steady)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
@@ -419,6 +419,47 @@ def reference_gpu_encoder(n: int, prompt_tokens: int, steps: int, warm: int, dev
             "setup_mu_frames_per_s": n * 2 * prompt_tokens / (setup_ms / 1000), "timed_calls": steps}
 
 
+def reference_gpu_hift(n: int, steps: int, warm: int, dev, tf32: bool) -> dict:
+    """The reference's own vocoder path on this GPU, unmodified: ``BatchedToken2Wav._vocode``
+    (engine/runtime/token2wav_batch.py:813-848) with ``hift_forward`` (engine/models/token2wav.py:230-245), strict fp32
+    (cuDNN TF32 off, as the reference runs Token2Wav) or with its ``decode_tf32`` option, over the restated vocoder:
+    ``n`` streams, 50-frame windows, every call one window per stream."""
+    _reference_modules()
+    from types import SimpleNamespace
+
+    import numpy as np
+    from engine.models.token2wav import StreamState, strict_fp32
+    from engine.runtime import token2wav_batch as tb
+
+    from b200t2w.config import HIFT
+    from oracle import hift_oracle as ho
+
+    hift = ho.build_hift(HIFT, seed=0).to(dev)
+    bt = tb.BatchedToken2Wav.__new__(tb.BatchedToken2Wav)
+    bt.hift, bt.hift_graphs, bt.hift_decode_tf32 = hift, None, tf32
+    bt.t2w = SimpleNamespace(window=torch.from_numpy(np.hamming(2 * ho.SOURCE_CACHE)).to(dev))
+    sts = [StreamState(prompt=None, flow_cache={}, noise_seed=1000 + i,
+                       hift_cache=dict(mel=torch.zeros(1, HIFT.mel, 0, device=dev), source=torch.zeros(1, 1, 0, device=dev),
+                                       speech=torch.zeros(1, 0, device=dev))) for i in range(n)]
+    g = torch.Generator().manual_seed(13)
+    mels = [[(torch.randn(1, HIFT.mel, 50, generator=g) - 2.0).to(dev) for _ in range(n)] for _ in range(3)]
+    st = torch.cuda.current_stream(dev)
+    ms = []
+    with torch.inference_mode(), strict_fp32():
+        for k in range(warm + steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            bt._vocode([(s, None, False) for s in sts], mels[k % 3])
+            e1.record(st)
+            e1.synchronize()
+            if k >= warm:
+                ms.append(e0.elapsed_time(e1))
+    m = statistics.median(ms)
+    return {"path": "BatchedToken2Wav._vocode + hift_forward (token2wav_batch.py:813-848, token2wav.py:230-245), "
+                    + ("decode_tf32" if tf32 else "strict fp32"), "streams": n, "ms_per_call": m,
+            "mel_frames_per_s": n * 50 / (m / 1000), "timed_calls": steps}
+
+
 def reference_gpu_arm(a) -> None:
     """``--impl reference --reference-gpu``: one JSON record of the reference's GPU PyTorch path at the target shape
     and at config 2 (a child process of the default arm; nothing of this build's library is loaded here)."""
@@ -439,6 +480,13 @@ def reference_gpu_arm(a) -> None:
                 rec[name + "_fastdit"] = reference_gpu_fastdit(wl, steps=3, warm=2, dev=dev)
             except Exception as e:
                 rec[name + "_fastdit"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    for tf32 in (False, True):
+        key = "hift_64" + ("_tf32" if tf32 else "")
+        try:
+            rec[key] = reference_gpu_hift(64, steps=3, warm=2, dev=dev, tf32=tf32)
+        except Exception as e:
+            rec[key] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
     for io in (False, True):
         key = "encoder_64" + ("_batched_io" if io else "")
         try:
@@ -599,6 +647,72 @@ def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, see
         enc.release(h)
     enc.close()
     return rec
+
+
+def hift_flops(hcfg, F: int) -> float:
+    """Algorithmic FLOPs of one HiFT window of F mel frames (the convolutions; the source, STFT and iSTFT are O(samples)):
+    f0 predictor, conv_pre, the three transposed convs, the source branches (strided conv + ResBlock) and the three
+    ResBlocks of every stage, conv_post."""
+    C, Cf, mel = hcfg.channels, hcfg.f0_channels, hcfg.mel
+    fl = 2 * F * 3 * (mel * Cf + (hcfg.f0_layers - 1) * Cf * Cf) + 2 * F * Cf + 2 * F * 7 * mel * C
+    L, cin = F, C
+    for s, (u, k) in enumerate(zip(hcfg.upsample_rates, hcfg.upsample_kernels)):
+        cout = cin // 2
+        fl += 2 * L * cin * cout * k  # transposed conv: each input row meets every tap once
+        L *= u
+        Ls = L + (1 if s == 2 else 0)
+        ks = hcfg.source_kernels[s]
+        fl += 2 * Ls * cout * cout * 6 * ks + 2 * Ls * cout * (hcfg.n_fft + 2) * (1 if s == 2 else 2 * (15 if s == 0 else 3))
+        fl += sum(2 * Ls * cout * cout * 6 * kr for kr in hcfg.resblock_kernels)
+        cin = cout
+    fl += 2 * (L + 1) * cin * (hcfg.n_fft + 2) * 7
+    return float(fl)
+
+
+def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float) -> dict:
+    """The HiFT vocoder (row f4: mel -> 24 kHz waveform) at the reference config, random init, the upsampling stages on
+    TF32 tensor cores (the reference's decode_tf32 option; f0 predictor, source, conv_pre / conv_post fp32): ``n``
+    streams, every call one 50-frame window per stream (58 frames with the 8 cached ones once the stream has started),
+    the windows' mel from pinned host memory and every call's samples read back to pinned host memory inside the timed
+    region, calls back to back."""
+    from b200t2w.config import HIFT
+    from b200t2w.hift import B200HiFT
+    from oracle import hift_oracle as ho
+
+    g = torch.Generator().manual_seed(seed)
+    voc = B200HiFT.from_module(ho.build_hift(HIFT, seed=0), HIFT, device=dev, max_frames=64, n_streams=n)
+    hs = [voc.new_stream(1000 + i) for i in range(n)]
+    T = 50
+    mels = [(torch.randn(n * T, HIFT.mel, generator=g) - 2.0).pin_memory() for _ in range(3)]
+    dmel = torch.empty(n * T, HIFT.mel, device=dev)
+    host = torch.empty(n * 480 * (T + 8), dtype=torch.float32).pin_memory()
+
+    def call(k):
+        dmel.copy_(mels[k % 3], non_blocking=True)
+        outs = voc.vocode_packed(hs, dmel, [T] * n, [False] * n)
+        flat = torch.cat(outs)
+        host[:flat.numel()].copy_(flat, non_blocking=True)
+
+    for k in range(max(warmup, 2)):
+        call(k)
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for k in range(steps):
+        call(k)
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flop = n * hift_flops(HIFT, T + 8)
+    for h in hs:
+        voc.release(h)
+    voc.close()
+    return {"workload": f"HiFT vocoder, {n} streams, steady 50-frame windows (58 with the cached 8), upsampling stages "
+                        f"in TF32",
+            "ms_per_call": ms, "audio_s_per_s": n * T * 480 / 24000 / (ms / 1000),
+            "mel_frames_per_s": n * T / (ms / 1000), "tflops": flop / (ms / 1000) / 1e12,
+            "h2d_bytes_per_call": n * T * HIFT.mel * 4, "d2h_bytes_per_call": n * T * 480 * 4}
 
 
 def packed_record(solver, wl: Workload, steps: int, warm: int, flush: torch.Tensor, peak_tf: float) -> dict:
@@ -813,6 +927,8 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
             torch.cuda.empty_cache()
         sub["encoder_64"] = encoder_record(dev, 64, 150, steps=10, warmup=4, seed=12, peak_tf=peak_tf)
         torch.cuda.empty_cache()
+        sub["hift_64"] = hift_record(dev, 64, steps=5, warmup=2, seed=14, peak_tf=peak_tf)
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not a.no_reference_gpu:
         torch.cuda.empty_cache()
         ref_gpu = reference_gpu_child(a)
@@ -821,6 +937,11 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
         w_ref = (ref_gpu.get("w32_fastdit") or {}).get("window_ms")
         if w_ours and w_ref:  # steady-state windows, 32 per call: FastDiT's graph-replayed window vs this build's call
             ref_gpu["steady_32_speedup_vs_fastdit_window"] = w_ref / w_ours
+        h_ours = (sub.get("hift_64") or {}).get("ms_per_call")
+        for k in ("hift_64", "hift_64_tf32"):  # the vocoder's steady call, 64 streams
+            h_ref = (ref_gpu.get(k) or {}).get("ms_per_call")
+            if h_ours and h_ref:
+                ref_gpu.setdefault("hift_speedup", {})[k] = h_ref / h_ours
         e_ours = (sub.get("encoder_64") or {}).get("ms_per_call")
         for k in ("encoder_64", "encoder_64_batched_io"):  # the flow encoder's steady window call, 64 streams
             e_ref = (ref_gpu.get(k) or {}).get("ms_per_call")
@@ -895,6 +1016,14 @@ def main() -> None:
                                   "ms_per_step": rec["ms_per_call"], "higher_is_better": True, "dtype": "bf16",
                                   "data": "synthetic", "config": {"workload": rec["workload"]}, "encoder": rec}),
                       flush=True)
+        elif a.workload == "hift":
+            torch.cuda.set_device(local)
+            rec = hift_record(torch.device("cuda", local), a.batch, a.steps, a.warmup, seed=14, peak_tf=1414.0)
+            if rank == 0:
+                print(json.dumps({"metric": "HiFT mel frames/s (steady windows)", "value": rec["mel_frames_per_s"],
+                                  "unit": "mel frames/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+                                  "ms_per_step": rec["ms_per_call"], "higher_is_better": True, "dtype": "f32",
+                                  "data": "synthetic", "config": {"workload": rec["workload"]}, "hift": rec}), flush=True)
         elif a.workload == "steady":
             torch.cuda.set_device(local)
             rec = steady_record(REFERENCE, torch.device("cuda", local), a.batch, a.steps, a.warmup, seed=11 + rank,

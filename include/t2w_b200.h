@@ -500,11 +500,14 @@ T2W_API int t2w_enc_ln(const float* x, const float* w, const float* b, float eps
  *                        the output samples (the last 3840 held back unless the window is final; a stream's first
  *                        window starts with 3840 samples of silence)
  *   t2w_hift_stream_*    a stream's hift_cache (mel / source / speech tails, token2wav.py:287-292), kept in the library
- * Strict fp32 (the reference runs Token2Wav with TF32 off: token2wav.py:44-57). */
+ * Strict fp32 (the reference runs Token2Wav with TF32 off: token2wav.py:44-57) unless tf32 is set. */
 typedef struct t2w_hift_config {
   int32_t mel, channels, f0_channels, f0_layers, harmonics, sample_rate, n_fft, hop;
   int32_t up_rates[3], up_kernels[3], res_kernels[3], source_kernels[3], dilations[3];
   float nsf_alpha, nsf_sigma, voiced_threshold, lrelu_slope, audio_limit;
+  int32_t tf32; /* 0: strict fp32 everywhere; 1: the upsampling stages (transposed convs, source and main ResBlocks) on
+                 * TF32 tensor cores, the reference's decode_tf32 option (token2wav.py:160-210); the f0 predictor, the
+                 * source, conv_pre, source_downs and conv_post stay fp32 */
 } t2w_hift_config;
 
 typedef struct t2w_hift t2w_hift;
@@ -520,6 +523,8 @@ typedef struct t2w_hift t2w_hift;
 T2W_API int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int32_t n_weights,
                             int32_t max_frames, int32_t n_streams, t2w_hift** out);
 T2W_API int t2w_hift_destroy(t2w_hift* h);
+/* Synchronise the vocoder's error word: T2W_OK, or T2W_ERR_TIMEOUT if a kernel gave up on a wait (then cleared). */
+T2W_API int t2w_hift_check(t2w_hift* h);
 /* A stream with empty caches (its first window has no cached mel frames, source or speech). */
 T2W_API int t2w_hift_stream_new(t2w_hift* h, int32_t* handle);
 T2W_API int t2w_hift_stream_release(t2w_hift* h, int32_t handle);

@@ -56,9 +56,12 @@ def hift_weight_names(cfg: HiFTConfig) -> list:
 
 class B200HiFT:
     """The HiFT vocoder on one sm_100 GPU.  ``weights``: fp32 state dict of a HiFTGenerator (weight normalisation
-    folded); ``max_frames``: a window's mel frames at most, with the 8 cached ones (<= 512)."""
+    folded); ``max_frames``: a window's mel frames at most, with the 8 cached ones (<= 512).  ``tf32``: the upsampling
+    stages on TF32 tensor cores (the reference's ``decode_tf32`` option); False keeps every convolution in strict fp32
+    (the reference's default)."""
 
-    def __init__(self, cfg: HiFTConfig, weights: dict, device="cuda", max_frames: int = 128, n_streams: int = 256):
+    def __init__(self, cfg: HiFTConfig, weights: dict, device="cuda", max_frames: int = 128, n_streams: int = 256,
+                 tf32: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -81,6 +84,8 @@ class B200HiFT:
             setattr(c, f, (ctypes.c_int32 * 3)(*v))
         c.nsf_alpha, c.nsf_sigma, c.voiced_threshold = cfg.nsf_alpha, cfg.nsf_sigma, cfg.voiced_threshold
         c.lrelu_slope, c.audio_limit = cfg.lrelu_slope, cfg.audio_limit
+        c.tf32 = 1 if tf32 else 0
+        self.tf32 = bool(tf32)
         with torch.cuda.device(self.device):
             w = [weights[k].detach().to(self.device, torch.float32).contiguous() for k in names]
             ptrs = (ctypes.c_void_p * len(w))(*[t.data_ptr() for t in w])
@@ -104,6 +109,9 @@ class B200HiFT:
             self.close()
         except Exception:
             pass
+
+    def check(self) -> None:
+        L.check("t2w_hift_check", self.lib.t2w_hift_check(self.handle))
 
     def new_stream(self, noise_seed: int = 0) -> int:
         h = ctypes.c_int32()

@@ -101,7 +101,8 @@ class HiftConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("mel", "channels", "f0_channels", "f0_layers", "harmonics", "sample_rate",
                                               "n_fft", "hop")] + \
                [(n, ctypes.c_int32 * 3) for n in ("up_rates", "up_kernels", "res_kernels", "source_kernels", "dilations")] + \
-               [(n, ctypes.c_float) for n in ("nsf_alpha", "nsf_sigma", "voiced_threshold", "lrelu_slope", "audio_limit")]
+               [(n, ctypes.c_float) for n in ("nsf_alpha", "nsf_sigma", "voiced_threshold", "lrelu_slope", "audio_limit")] + \
+               [("tf32", ctypes.c_int32)]
 
 
 class VocodeBatch(ctypes.Structure):
@@ -181,6 +182,7 @@ _SIGS = {
     "t2w_enc_ln": ([_P, _P, _P, _F, _I, _I, _P, _P, _P, _P], ctypes.c_int),
     "t2w_hift_create": ([ctypes.POINTER(HiftConfig), ctypes.POINTER(_P), _I, _I, _I, ctypes.POINTER(_P)], ctypes.c_int),
     "t2w_hift_destroy": ([_P], ctypes.c_int),
+    "t2w_hift_check": ([_P], ctypes.c_int),
     "t2w_hift_stream_new": ([_P, ctypes.POINTER(_I)], ctypes.c_int),
     "t2w_hift_stream_release": ([_P, _I], ctypes.c_int),
     "t2w_vocode_samples": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_uint8),

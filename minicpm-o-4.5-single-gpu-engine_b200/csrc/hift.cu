@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tconv.h"
 
 using namespace t2w;
 
@@ -478,6 +479,8 @@ struct t2w_hift {
   double* hamming = nullptr;  // 7680
   float* cache = nullptr;     // [n_streams][8 mel frames x C | 3840 source | 3840 speech]
   int cache_ld = 0;
+  int tf32 = 0;               // the upsampling stages on the TF32 tensor-core convolution
+  int* err = nullptr;         // bounded-wait error word of the tensor-core kernels
   std::vector<int> row_free;
   std::vector<uint8_t> row_live, row_first;
   std::mutex mu;
@@ -587,10 +590,12 @@ int create_impl(t2w_hift* h, const float* const* W) {
       const int nq = (g.k - j0 + g.u - 1) / g.u;
       g.nq[p] = nq;
       g.c[p] = (p + g.pad - j0) / g.u;
+      // taps in ascending input offset: tap t reads input v + c_p - (nq - 1) + t, i.e. q = nq - 1 - t
       std::vector<float> t((size_t)g.Cout * nq * g.Cin);
       for (int o = 0; o < g.Cout; ++o)
-        for (int q = 0; q < nq; ++q)
-          for (int ci = 0; ci < g.Cin; ++ci) t[((size_t)o * nq + q) * g.Cin + ci] = hw[((size_t)ci * g.Cout + o) * g.k + j0 + g.u * q];
+        for (int tt = 0; tt < nq; ++tt)
+          for (int ci = 0; ci < g.Cin; ++ci)
+            t[((size_t)o * nq + tt) * g.Cin + ci] = hw[((size_t)ci * g.Cout + o) * g.k + j0 + g.u * (nq - 1 - tt)];
       g.phase[p].Cin = g.Cin;
       g.phase[p].Cout = g.Cout;
       g.phase[p].k = nq;
@@ -666,6 +671,8 @@ int create_impl(t2w_hift* h, const float* const* W) {
   for (int n = 0; n < 2 * kSrcCache; ++n) hm[n] = 0.54 - 0.46 * std::cos(2.0 * M_PI * n / (2 * kSrcCache - 1));
   H_TRY(halloc(h, &h->hamming, hm.size()));
   H_CUDA(cudaMemcpy(h->hamming, hm.data(), hm.size() * 8, cudaMemcpyHostToDevice));
+  H_TRY(halloc(h, &h->err, 1));
+  H_CUDA(cudaMemset(h->err, 0, 4));
   h->cache_ld = kMelCache * c.mel + 2 * kSrcCache;
   H_TRY(halloc(h, &h->cache, (size_t)h->n_streams * h->cache_ld));
   H_CUDA(cudaMemset(h->cache, 0, (size_t)h->n_streams * h->cache_ld * 4));
@@ -685,6 +692,8 @@ struct HPlan {
   int n = 0;
   std::vector<HRow> rows;
   int R[4] = {};  // rows at the mel rate and the three stage rates
+  int A[4] = {};  // allocated rows: the mel rate rounded up to 128, the stages its 8, 40 and 120 multiples
+  std::vector<uint8_t> pad[4];  // per allocated row: 1 unless it holds a window's data
   std::vector<int> vr_mel, vr_s[3], vr_stft;  // virtual rows: data rows of each rate, and the STFT frames
   std::vector<int> start_mel, len_mel, start_s[3], len_s[3], start_up[3];
   long long samples = 0, out_samples = 0;
@@ -745,6 +754,17 @@ int make_plan(t2w_hift* h, int n, const int32_t* handle, const int32_t* T, const
   pl.R[1] = r0;
   pl.R[2] = r1;
   pl.R[3] = r2;
+  pl.A[0] = (rm + 127) / 128 * 128;
+  pl.A[1] = 8 * pl.A[0];
+  pl.A[2] = 40 * pl.A[0];
+  pl.A[3] = 120 * pl.A[0];
+  for (int r = 0; r < 4; ++r) pl.pad[r].assign(pl.A[r], 1);
+  for (const HRow& e : pl.rows) {
+    for (int t = 0; t < e.F; ++t) pl.pad[0][e.mel0 + t] = 0;
+    for (int t = 0; t < 8 * e.F; ++t) pl.pad[1][e.s0 + t] = 0;
+    for (int t = 0; t < 40 * e.F; ++t) pl.pad[2][e.s1 + t] = 0;
+    for (int t = 0; t < 120 * e.F + 1; ++t) pl.pad[3][e.s2 + t] = 0;
+  }
   pl.samples = smp;
   pl.out_samples = outp;
   return T2W_OK;
@@ -780,6 +800,7 @@ int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int
   h->device = dev;
   h->n_streams = n_streams;
   h->max_frames = max_frames;
+  h->tf32 = c.tf32 ? 1 : 0;
   const int rc = create_impl(h, weights);
   if (rc) {
     free_all(h);
@@ -796,6 +817,17 @@ int t2w_hift_destroy(t2w_hift* h) {
   free_all(h);
   delete h;
   return T2W_OK;
+}
+
+int t2w_hift_check(t2w_hift* h) {
+  if (!h) return T2W_ERR_INVALID;
+  int v = 0;
+  H_CUDA(cudaMemcpy(&v, h->err, 4, cudaMemcpyDeviceToHost));
+  if (v) {
+    const int z = 0;
+    H_CUDA(cudaMemcpy(h->err, &z, 4, cudaMemcpyHostToDevice));
+  }
+  return v;
 }
 
 int t2w_hift_stream_new(t2w_hift* h, int32_t* handle) {
@@ -867,24 +899,26 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     o_ls[s] = add(n * 4);
     o_su[s] = add(n * 4);
   }
+  size_t o_pad[4];
+  for (int r = 0; r < 4; ++r) o_pad[r] = add(pl.A[r]);
   const size_t meta_bytes = meta;
-  const size_t o_mel = add((size_t)pl.R[0] * c.mel * 4);
-  const size_t o_f0a = add((size_t)pl.R[0] * c.f0_channels * 4), o_f0b = add((size_t)pl.R[0] * c.f0_channels * 4);
-  const size_t o_f0 = add((size_t)pl.R[0] * 4);
+  const size_t o_mel = add((size_t)pl.A[0] * c.mel * 4);
+  const size_t o_f0a = add((size_t)pl.A[0] * c.f0_channels * 4), o_f0b = add((size_t)pl.A[0] * c.f0_channels * 4);
+  const size_t o_f0 = add((size_t)pl.A[0] * 4);
   const size_t o_src = add((size_t)pl.samples * 4), o_sp = add((size_t)pl.samples * 4);
-  const size_t o_stft = add((size_t)pl.R[3] * (kNfft + 2) * 4);
-  const size_t o_x0 = add((size_t)pl.R[0] * C0 * 4);
+  const size_t o_stft = add((size_t)pl.A[3] * (kNfft + 2) * 4);
+  const size_t o_x0 = add((size_t)pl.A[0] * C0 * 4);
   // per stage: x (ups output), xr[3] ResBlock streams, ar[3] / sd scratch of the stage's size
   size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3];
   for (int s = 0; s < 3; ++s) {
-    const size_t sz = (size_t)pl.R[s + 1] * (C0 >> (s + 1)) * 4;
+    const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
     o_xs[s] = add(sz);
     for (int j = 0; j < 3; ++j) o_xr[s][j] = add(sz);
     for (int j = 0; j < 3; ++j) o_ar[s][j] = add(sz);
     o_sd[s] = add(sz);
     o_ta[s] = add(sz);
   }
-  const size_t o_post = add((size_t)pl.R[3] * (kNfft + 2) * 4);
+  const size_t o_post = add((size_t)pl.A[3] * (kNfft + 2) * 4);
   const size_t total = meta;
   uint8_t* ws = nullptr;
   H_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), total, st));
@@ -903,6 +937,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     put(o_ls[s], pl.len_s[s].data(), n * 4);
     put(o_su[s], pl.start_up[s].data(), n * 4);
   }
+  for (int r = 0; r < 4; ++r) put(o_pad[r], pl.pad[r].data(), pl.A[r]);
   int rc = T2W_OK;
   auto fail = [&](int r) {
     cudaFreeAsync(ws, st);
@@ -994,7 +1029,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   for (int s = 0; s < 3; ++s) {
     HStage& g = h->st[s];
     const int Cs = g.Cout;
-    const long long nel_in = (long long)pl.R[s] * g.Cin;
+    const long long nel_in = (long long)pl.A[s] * g.Cin;
     rc = ck(launch_k(k_leaky, dim3(grid_for(nel_in)), dim3(256), 0, st, x, nel_in, c.lrelu_slope));
     if (rc) return fail(rc);
     float* xs = reinterpret_cast<float*>(P(o_xs[s]));
@@ -1004,12 +1039,33 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     const int* su = reinterpret_cast<const int*>(P(o_su[s]));
     // transposed conv, one launch per output phase over the input's data rows
     for (int p = 0; p < g.u; ++p) {
-      ConvGeo cg = geo(g.phase[p], vin, nvin, s_in, l_in, su, x, xs, HE_NONE);
-      cg.off = g.c[p];
-      cg.dil = -1;
-      cg.u_out = g.u;
-      cg.p_out = p;
-      rc = run(cg);
+      if (h->tf32) {
+        TConvArgs t;
+        t.A = x;
+        t.lda = g.Cin;
+        t.rows_a = pl.A[s];
+        t.W = g.phase[p].W;
+        t.bias = g.b;
+        t.M = pl.A[s];
+        t.N = g.Cout;
+        t.Cin = g.Cin;
+        t.taps = g.nq[p];
+        t.tap_row0 = g.c[p] - (g.nq[p] - 1);
+        t.out = xs;
+        t.ldo = g.Cout;
+        t.row_mul = g.u;
+        t.row_add = p;
+        t.pad = reinterpret_cast<const uint8_t*>(P(o_pad[s + 1]));
+        t.err = h->err;
+        rc = launch_tconv(t, st);
+      } else {
+        ConvGeo cg = geo(g.phase[p], vin, nvin, s_in, l_in, su, x, xs, HE_NONE);
+        cg.off = g.c[p] - (g.nq[p] - 1);
+        cg.dil = 1;
+        cg.u_out = g.u;
+        cg.p_out = p;
+        rc = run(cg);
+      }
       if (rc) return fail(rc);
     }
     if (s == 2) {
@@ -1027,11 +1083,48 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       rc = run(cg);
       if (rc) return fail(rc);
     }
-    const long long nel = (long long)pl.R[s + 1] * Cs;
+    const long long nel = (long long)pl.A[s + 1] * Cs;
     auto resblock = [&](HRes& r, float* xr, float* a_in, float* tmp) -> int {
       // a_in holds Snake1_0(xr); per dilation: tmp = Snake2(conv1(a_in)); xr += conv2(tmp), a_in = Snake1_next(xr)
       for (int dd = 0; dd < 3; ++dd) {
         const int dl = h->cfg.dilations[dd];
+        if (h->tf32) {
+          TConvArgs t;
+          t.lda = Cs;
+          t.rows_a = pl.A[s + 1];
+          t.M = pl.A[s + 1];
+          t.N = Cs;
+          t.Cin = Cs;
+          t.taps = r.k;
+          t.ldo = Cs;
+          t.pad = reinterpret_cast<const uint8_t*>(P(o_pad[s + 1]));
+          t.err = h->err;
+          TConvArgs t1 = t;
+          t1.A = a_in;
+          t1.W = r.c1[dd].W;
+          t1.bias = r.c1[dd].b;
+          t1.tap_row0 = -(r.k * dl - dl) / 2;
+          t1.dil = dl;
+          t1.out = tmp;
+          t1.epi = TCONV_SNAKE;
+          t1.alpha = r.a2 + dd * Cs;
+          t1.inv = r.i2 + dd * Cs;
+          H_TRY(launch_tconv(t1, st));
+          TConvArgs t2 = t;
+          t2.A = tmp;
+          t2.W = r.c2[dd].W;
+          t2.bias = r.c2[dd].b;
+          t2.tap_row0 = -(r.k - 1) / 2;
+          t2.out = xr;
+          t2.epi = TCONV_RESID;
+          if (dd < 2) {
+            t2.alpha = r.a1 + (dd + 1) * Cs;
+            t2.inv = r.i1 + (dd + 1) * Cs;
+            t2.out2 = a_in;
+          }
+          H_TRY(launch_tconv(t2, st));
+          continue;
+        }
         ConvGeo c1 = geo(r.c1[dd], vs, (int)pl.vr_s[s].size(), ss, ls, ss, a_in, tmp, HE_SNAKE);
         c1.dil = dl;
         c1.off = -(r.k * dl - dl) / 2;

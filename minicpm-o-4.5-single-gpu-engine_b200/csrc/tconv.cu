@@ -1,0 +1,300 @@
+// TF32 tcgen05 implicit-GEMM convolution for the HiFT vocoder's upsampling stages (the transposed convolutions, the
+// source-branch and main ResBlocks): out[m, n] = sum_tap sum_c A[m + tap_row0 + tap * dil, c] W[n, tap * Cin + c].
+//
+// A is the time-major fp32 activation [rows, Cin] with zero rows around every window's data (the "same" padding), W
+// the fp32 weight [Cout, taps * Cin]; the tensor core reads both as TF32 (kind::tf32, K = 8 per instruction, fp32
+// accumulation in TMEM) — the reference's own reduced-precision option for these stages (decode_tf32,
+// engine/models/token2wav.py:160-210).  One persistent CTA per SM, warp-specialised as the bf16 GEMM: warp 0 the TMA
+// producer (128 x 32 A boxes and BN x 32 W boxes, 128-byte swizzle, one box pair per (tap, 32-channel block)), warp 1
+// the TMEM allocator and single-thread MMA issuer, warps 2-9 the epilogue (TMEM lane quarter w % 4, alternate 32-column
+// chunks), the accumulator double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.  Output rows:
+// row_mul * m + row_add (a transposed convolution's output phase writes every row_mul-th row of the next rate's layout);
+// rows flagged in `pad` are window padding and stay zero.  Epilogues (fp32, direct stores, one output row per thread):
+// bias; Snake(bias + acc) (the ResBlocks' conv1 with its second activation); x += bias + acc with Snake(x_new) into a
+// second buffer (conv2's residual and the next conv1's input).  No TMA multicast.
+#include <atomic>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tconv.h"
+
+namespace t2w {
+
+namespace {
+
+constexpr int kTBM = 128;
+constexpr int kTBK = 32;  // fp32 elements per 128-byte swizzle row
+constexpr int kTMaxSmem = 232448;
+
+template <int BN>
+struct TCfg {
+  static constexpr int A_BYTES = kTBM * kTBK * 4;  // 16 KB
+  static constexpr int B_BYTES = BN * kTBK * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int FIXED = 1024 + 256;
+  static constexpr int STAGES_FIT = (kTMaxSmem - FIXED) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+  static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED;
+  static_assert(STAGES >= 3, "stages");
+};
+
+struct TDev {
+  int M, N, Cin, taps, tap_row0, dil, tiles_n, num_tiles;
+  const float* bias;
+  float* out;
+  long long ldo;  // floats between consecutive output rows of the layout (row_mul * m + row_add indexes them)
+  int row_mul, row_add;
+  const uint8_t* pad;
+  int epi;
+  const float* alpha;
+  const float* inv;
+  float* out2;
+  int* err;
+};
+
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  // D fp32 (bits 4-5 = 1), A and B TF32 (format 2 at bits 7-9 and 10-12), both K-major, N >> 3, M >> 4
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+T2W_DEV void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ float snake_f(float x, float a, float inv) {
+  const float s = sinf(x * a);
+  return x + inv * (s * s);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
+                                                  const __grid_constant__ CUtensorMap tmW, const TDev p) {
+  using C = TCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+  }
+  pdl_wait();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_launch();
+  const uint32_t tmem = *tmem_slot;
+  const int kb_per_tap = p.Cin / kTBK;
+  const int num_kb = kb_per_tap * p.taps;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          const int tap = kb / kb_per_tap, kk = (kb - tap * kb_per_tap) * kTBK;
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, kk, m0 + p.tap_row0 + tap * p.dil, &full[stage]);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmW, tap * p.Cin + kk, n0, &full[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kTBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        if (!(ok = mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1u, p.err))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, p.err))) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES), b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kTBK / 8; ++k)
+            umma_tf32(d, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) break;
+      tc_fence_after();
+      if (half >= BN / 32) {  // a 32-column tile: the second half of the epilogue warps has no chunk of its own
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      const int m = m0 + q * 32 + lane;
+      const long long orow = (long long)p.row_mul * m + p.row_add;
+      const bool live = m < p.M && !p.pad[orow];
+#pragma unroll 1
+      for (int b = half; b < BN / 32; b += 2) {
+        float v[32];
+        tmem_ld32(taddr + 32 * b, v);
+        if (b + 2 >= BN / 32) {  // this warp's last load of the accumulator
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        if (m >= p.M) continue;
+        const int c0 = n0 + 32 * b;
+        float* dst = p.out + orow * p.ldo + c0;
+        if (p.epi == TCONV_RESID) {
+          if (!live) continue;  // padding rows keep their zeros
+          float* dst2 = p.out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = *reinterpret_cast<const float4*>(dst + 4 * j);
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
+            float4 y;
+            y.x = x.x + (v[4 * j] + bb.x);
+            y.y = x.y + (v[4 * j + 1] + bb.y);
+            y.z = x.z + (v[4 * j + 2] + bb.z);
+            y.w = x.w + (v[4 * j + 3] + bb.w);
+            reinterpret_cast<float4*>(dst)[j] = y;
+            if (dst2) {
+              const float4 a = __ldg(reinterpret_cast<const float4*>(p.alpha + c0) + j);
+              const float4 iv = __ldg(reinterpret_cast<const float4*>(p.inv + c0) + j);
+              reinterpret_cast<float4*>(dst2)[j] =
+                  make_float4(snake_f(y.x, a.x, iv.x), snake_f(y.y, a.y, iv.y), snake_f(y.z, a.z, iv.z),
+                              snake_f(y.w, a.w, iv.w));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (live) {
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
+              y = make_float4(v[4 * j] + bb.x, v[4 * j + 1] + bb.y, v[4 * j + 2] + bb.z, v[4 * j + 3] + bb.w);
+              if (p.epi == TCONV_SNAKE) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(p.alpha + c0) + j);
+                const float4 iv = __ldg(reinterpret_cast<const float4*>(p.inv + c0) + j);
+                y = make_float4(snake_f(y.x, a.x, iv.x), snake_f(y.y, a.y, iv.y), snake_f(y.z, a.z, iv.z),
+                                snake_f(y.w, a.w, iv.w));
+              }
+            }
+            reinterpret_cast<float4*>(dst)[j] = y;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int BN>
+int launch_impl(const TConvArgs& a, cudaStream_t st) {
+  using C = TCfg<BN>;
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t e = smem_attr_once(k_tconv<BN>, C::SMEM, attr_done);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  CUtensorMap ma, mw;
+  if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin, (uint64_t)a.lda * 4, kTBM, kTBK) ||
+      !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, (uint64_t)a.Cin * a.taps, (uint64_t)a.Cin * a.taps * 4, BN, kTBK))
+    return T2W_ERR_INVALID;
+  TDev p;
+  p.M = a.M;
+  p.N = a.N;
+  p.Cin = a.Cin;
+  p.taps = a.taps;
+  p.tap_row0 = a.tap_row0;
+  p.dil = a.dil;
+  p.tiles_n = a.N / BN;
+  p.num_tiles = (a.M / kTBM) * p.tiles_n;
+  p.bias = a.bias;
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.row_mul = a.row_mul;
+  p.row_add = a.row_add;
+  p.pad = a.pad;
+  p.epi = a.epi;
+  p.alpha = a.alpha;
+  p.inv = a.inv;
+  p.out2 = a.out2;
+  p.err = a.err;
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  e = launch_k(k_tconv<BN>, dim3(grid), dim3(320), C::SMEM, st, ma, mw, p);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  return T2W_OK;
+}
+
+}  // namespace
+
+int launch_tconv(const TConvArgs& a, cudaStream_t st) {
+  if (!a.A || !a.W || !a.bias || !a.out || !a.pad || a.M <= 0 || a.M % kTBM || a.Cin <= 0 || a.Cin % kTBK ||
+      a.taps < 1 || a.rows_a <= 0 || a.lda < a.Cin || a.lda % 4 || a.ldo % 4 || a.row_mul < 1 || a.row_add < 0 ||
+      (a.epi == TCONV_SNAKE && (!a.alpha || !a.inv)) || (a.out2 && (!a.alpha || !a.inv)) ||
+      (reinterpret_cast<uintptr_t>(a.out) & 15) || (reinterpret_cast<uintptr_t>(a.bias) & 15))
+    return T2W_ERR_INVALID;
+  if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms()) return launch_impl<256>(a, st);
+  if (a.N % 128 == 0) return launch_impl<128>(a, st);
+  if (a.N == 64) return launch_impl<64>(a, st);
+  if (a.N == 32) return launch_impl<32>(a, st);
+  return T2W_ERR_INVALID;
+}
+
+}  // namespace t2w

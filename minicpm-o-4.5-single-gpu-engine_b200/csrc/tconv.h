@@ -1,0 +1,33 @@
+// Internal launch interface of the TF32 convolution kernel (tconv.cu; not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace t2w {
+
+enum { TCONV_BIAS = 0, TCONV_SNAKE = 1, TCONV_RESID = 2 };
+
+// out[row_mul m + row_add, n] (ldo floats per row) = epilogue(bias[n] + sum_tap sum_c A[m + tap_row0 + tap dil, c]
+// W[n, tap Cin + c]) for m < M (M % 128 == 0), rows whose pad[row_mul m + row_add] != 0 zero (bias, snake) or
+// untouched (resid).  A fp32 [rows_a, lda] (rows outside [0, rows_a) read as zero), W fp32 [N, taps Cin], Cin % 32 == 0,
+// N a multiple of 128, or 64, or 32.
+struct TConvArgs {
+  const float* A = nullptr;
+  int lda = 0, rows_a = 0;
+  const float* W = nullptr;
+  const float* bias = nullptr;
+  int M = 0, N = 0, Cin = 0, taps = 1, tap_row0 = 0, dil = 1;
+  float* out = nullptr;
+  long long ldo = 0;
+  int row_mul = 1, row_add = 0;
+  const uint8_t* pad = nullptr;
+  int epi = TCONV_BIAS;
+  const float* alpha = nullptr;  // TCONV_SNAKE: this conv's Snake; TCONV_RESID with out2: the next Snake
+  const float* inv = nullptr;
+  float* out2 = nullptr;
+  int* err = nullptr;
+};
+int launch_tconv(const TConvArgs& a, cudaStream_t st);
+
+}  // namespace t2w

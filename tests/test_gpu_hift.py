@@ -37,11 +37,13 @@ def oracle_noise(hift, seed, frames):
     return r, nz.transpose(1, 2)
 
 
+@pytest.mark.parametrize("tf32", [False, True], ids=["fp32", "tf32"])
 @pytest.mark.parametrize("name,cfg", [("hift_tiny", HIFT_TINY), ("hift_reference", HIFT)])
-def test_vocode_vs_reference_driver_golden(golden_dir, name, cfg):
+def test_vocode_vs_reference_driver_golden(golden_dir, name, cfg, tf32):
+    """Strict fp32 (the reference's default) and the upsampling stages on TF32 tensor cores (its decode_tf32 option)."""
     rec = torch.load(os.path.join(golden_dir, f"{name}.pt"))
     hift = ho.build_hift(cfg, seed=0)
-    voc = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=128, n_streams=8)
+    voc = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=128, n_streams=8, tf32=tf32)
     hs = [voc.new_stream(s) for s in rec["noise_seeds"]]
     chunks = [0, 0, 0]
     worst = 0.0
@@ -57,21 +59,23 @@ def test_vocode_vs_reference_driver_golden(golden_dir, name, cfg):
         for w, o in zip(call, outs):
             e = rel(o, w["samples"])
             worst = max(worst, e)
-            print(f"{name} call {c} stream {w['stream']} ({w['mel'].shape[1]} frames, last={w['last']}): "
+            print(f"{name} tf32={tf32} call {c} stream {w['stream']} ({w['mel'].shape[1]} frames, last={w['last']}): "
                   f"{o.numel()} samples, rel-L2 {e:.2e}")
             assert o.numel() == w["samples"].numel() and e < TOL
-    print(f"{name}: worst window rel-L2 {worst:.2e}")
+    print(f"{name} tf32={tf32}: worst window rel-L2 {worst:.2e}")
+    voc.check()
     for h in hs:
         voc.release(h)
 
 
-def test_vocode_ragged_calls_vs_oracle():
+@pytest.mark.parametrize("tf32", [False, True], ids=["fp32", "tf32"])
+def test_vocode_ragged_calls_vs_oracle(tf32):
     """Six streams, calls mixing first windows of different lengths, steady windows and finals, some streams skipping
     calls; every window against the oracle's per-stream ``vocode_window``."""
     torch.manual_seed(4)
     cfg = HIFT_TINY
     hift = ho.build_hift(cfg, seed=0)
-    voc = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=128, n_streams=8)
+    voc = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=128, n_streams=8, tf32=tf32)
     seeds = [11, 22, 33, 44, 55, 66]
     hs = [voc.new_stream(s) for s in seeds]
     ors = [ho.HiftStream(cfg.mel) for _ in seeds]
@@ -91,7 +95,7 @@ def test_vocode_ragged_calls_vs_oracle():
         for (i, T, last), mel, o in zip(call, mels, outs):
             ref = ho.vocode_window(hift, ors[i], mel, chunk_noise_seed(seeds[i], ors[i].chunks), last)
             e = rel(o, ref)
-            print(f"call {c} stream {i} T={T} last={last}: rel-L2 {e:.2e}")
+            print(f"tf32={tf32} call {c} stream {i} T={T} last={last}: rel-L2 {e:.2e}")
             assert o.numel() == ref.numel() and e < TOL
 
 

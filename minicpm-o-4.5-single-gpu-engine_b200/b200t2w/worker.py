@@ -10,7 +10,9 @@ and keeps its keys unless it is the stream's last (``keep = not last``, as ``_fl
 (tokens -> ``mu``) is either this build's ``B200FlowEncoder`` — then every prompt and request owns an encoder stream
 (its conformer caches), set up, copied or adopted, advanced and released with the DiT caches, and a decode call encodes
 all its windows in one call, as ``_flow_encode`` does — or any callable ``tokens -> mu``.  The HiFT vocoder (mel ->
-samples) is outside this build and is passed in as a callable.
+samples) is likewise this build's ``B200HiFT`` — every request owns a vocoder stream (its mel / source / speech
+caches and its noise seed), and a decode call vocodes all its windows in one call, as ``_vocode`` does — or a callable
+``(stream, mel, last) -> samples``.
 
 ``MultiGpuToken2Wav`` is the same surface over one ``B200Token2Wav`` per GPU, in place of the reference worker's single
 device (``torch.cuda.set_device(0)``, ``t2w_worker.py:804``): a request is placed on the least-loaded GPU when its prompt
@@ -49,6 +51,7 @@ class B200Stream:
     chunks: int = 0
     device: int = 0
     enc: int | None = None
+    voc: int | None = None
 
 
 class B200Token2Wav:
@@ -61,9 +64,11 @@ class B200Token2Wav:
 
     def __init__(self, fast, encode, vocode, device_index: int = 0):
         from .encoder import B200FlowEncoder
+        from .hift import B200HiFT
 
         self.fast, self.encode, self.vocode, self.device_index = fast, encode, vocode, device_index
         self.flow = encode if isinstance(encode, B200FlowEncoder) else None
+        self.hift = vocode if isinstance(vocode, B200HiFT) else None
         self.dev = fast.device
 
     @staticmethod
@@ -104,7 +109,8 @@ class B200Token2Wav:
         else:
             cache = self.fast.clone(prompt.cache)
             enc = self.flow.clone(prompt.enc) if prompt.enc is not None else None
-        return B200Stream(cache, prompt.spk, noise_seed, 0, self.device_index, enc)
+        voc = self.hift.new_stream(noise_seed) if self.hift is not None else None
+        return B200Stream(cache, prompt.spk, noise_seed, 0, self.device_index, enc, voc)
 
     def release_stream(self, st: B200Stream) -> None:
         if st is not None and st.cache is not None:
@@ -113,6 +119,9 @@ class B200Token2Wav:
         if st is not None and st.enc is not None:
             self.flow.release(st.enc)
             st.enc = None
+        if st is not None and st.voc is not None:
+            self.hift.release(st.voc)
+            st.voc = None
 
     def release_prompt(self, p: B200Prompt) -> None:
         if p is not None and p.cache is not None:
@@ -135,6 +144,11 @@ class B200Token2Wav:
             mus = [self.encode(it[1]) for it in items]
         spk = torch.cat([st.spk for st in sts])
         mels = self.fast.solve([st.cache for st in sts], mus, spk, None, [not bool(it[2]) for it in items])
+        if self.hift is not None:  # every window's samples from one vocoder call and one device-to-host copy
+            out = self.hift.vocode_numpy([st.voc for st in sts], mels, [bool(it[2]) for it in items])
+            for st in sts:
+                st.chunks += 1
+            return out
         out = []
         for st, mel, it in zip(sts, mels, items):
             out.append(self.vocode(st, mel, bool(it[2])))

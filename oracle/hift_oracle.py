@@ -267,12 +267,14 @@ class HiftStream:
 
 
 @torch.no_grad()
-def vocode_window(hift, st: HiftStream, mel, seed: int, last: bool):
+def vocode_window(hift, st: HiftStream, mel, seed: int, last: bool, noise_fn=None):
     """One window's mel [80, T] -> its samples, as ``BatchedToken2Wav._vocode`` handles one stream: the mel after the
     cached frames, HiFT with the row's seeded noise, the cross-fade with the cached speech, the caches updated, and the
-    last 3840 samples held back (a first window shifted by 3840 samples of silence) unless the window is final."""
+    last 3840 samples held back (a first window shifted by 3840 samples of silence) unless the window is final.
+    ``noise_fn(seed, n_samples) -> (rand_ini [1, dim], noise [1, n, dim])`` draws the noise in place of the CPU
+    generator (the reference draws on the vocoder's device)."""
     M = torch.cat([st.mel, mel[None]], dim=2)
-    rand_ini, noise = hift_noise(hift, seed, hift_samples(hift, M.shape[2]))
+    rand_ini, noise = (noise_fn or (lambda s, n: hift_noise(hift, s, n)))(seed, hift_samples(hift, M.shape[2]))
     speech, source = hift_forward_noise(hift, M, st.source, rand_ini, noise)
     first = st.source.shape[2] == 0
     window = torch.from_numpy(np.hamming(2 * SOURCE_CACHE))  # float64, as the reference keeps it

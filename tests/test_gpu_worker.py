@@ -194,3 +194,66 @@ def test_reference_worker_loop_with_b200_flow_encoder():
             assert e < TOL
     assert enc.usage() == (0, 0, 0)
     assert fd.pool.in_use() - fd.scratch == 0
+
+
+def test_reference_worker_loop_full_token2wav_chain():
+    """Token2Wav end to end on this build: the reference's ``WorkerLoop`` drives ``B200Token2Wav`` with the B200 flow
+    encoder, the B200 DiT solve and the B200 HiFT vocoder (TF32 upsampling stages).  Every window's samples against the
+    oracle chain: the restated flow encoder's streaming forward -> the oracle's streaming solve -> the restated vocoder's
+    ``vocode_window`` with the same source noise (drawn on the GPU from each chunk's seed, as the reference draws it);
+    afterwards every encoder, solver and vocoder stream is back."""
+    from b200t2w.config import ENCODER_TINY, HIFT_TINY
+    from b200t2w.encoder import B200FlowEncoder
+    from b200t2w.hift import B200HiFT, chunk_noise_seed
+    from oracle import encoder_oracle as eo
+    from oracle import hift_oracle as ho
+
+    model = dit_oracle.build_model(TINY, seed=0, noise_frames=4096)
+    flow = eo.build_flow(ENCODER_TINY, seed=0)
+    hift = ho.build_hift(HIFT_TINY, seed=0)
+    fd = B200FastDiT(B200Solver(TINY, state_dict_from_module(model), device="cuda:0"), model.rand_noise[0], n_slots=4096,
+                     max_streams=8)
+    enc = B200FlowEncoder.from_flow(flow, device="cuda:0", max_frames=1024, n_slots1=4096, n_slots2=8192, n_streams=16)
+    voc = B200HiFT.from_module(hift, HIFT_TINY, device="cuda:0", max_frames=128, n_streams=16)
+    bt = B200Token2Wav(fd, enc, voc, device_index=0)
+    g = torch.Generator().manual_seed(17)
+    reqs = {}
+    for seq, (ptok, wins) in {1: (40, (28, 28, 10)), 2: (55, (28, 28, 28, 5))}.items():
+        reqs[seq] = {"prompt_tokens": torch.randint(0, VOCAB, (ptok,), generator=g).tolist(),
+                     "mel": torch.randn(1, 2 * ptok, TINY.mel, generator=g), "spk": torch.randn(1, TINY.mel, generator=g),
+                     "windows": [torch.randint(0, VOCAB, (n,), generator=g).tolist() for n in wins]}
+    audio = run_loop(bt, reqs)
+    fd.solver.check()
+    enc.check()
+    voc.check()
+
+    def gpu_noise(seed, n):
+        gen = torch.Generator(device="cuda:0").manual_seed(int(seed))
+        r = torch.rand(1, HIFT_TINY.harmonics + 1, device="cuda:0", generator=gen)
+        z = torch.randn(1, HIFT_TINY.harmonics + 1, n, device="cuda:0", generator=gen)
+        return r.cpu(), z.cpu().transpose(1, 2)
+
+    for seq, r in reqs.items():
+        mu_p, est = eo.encode_prompt(flow, torch.tensor(r["prompt_tokens"]))
+        cache = dit_oracle.StreamCache(TINY, keep=r["mel"].shape[1])
+        hst = ho.HiftStream(HIFT_TINY.mel)
+        spk = r["spk"][0]
+        x0 = model.rand_noise[0, :, cache.length:cache.length + mu_p.shape[1]]
+        dit_oracle.solve_window(model, cache, x0, mu_p, spk, r["mel"][0].t(), keep_cache=True)
+        got = audio[seq]
+        assert len(got) == len(r["windows"])
+        for k, w in enumerate(r["windows"]):
+            last = k == len(r["windows"]) - 1
+            mu = eo.encode_window(flow, est, torch.tensor(w), last)
+            x0 = model.rand_noise[0, :, cache.length:cache.length + mu.shape[1]]
+            mel = dit_oracle.solve_window(model, cache, x0, mu, spk, None, keep_cache=not last)
+            ref = ho.vocode_window(hift, hst, mel, chunk_noise_seed(seq, k), last, noise_fn=gpu_noise)
+            a = torch.from_numpy(got[k])
+            e = float((a - ref).norm() / ref.norm())
+            print(f"request {seq} window {k}: {a.numel()} samples, rel-L2 vs oracle chain {e:.2e}")
+            # the chain's tolerance: the solve's bf16 mel (2e-3 of the oracle's) moves the vocoder's f0 and with it the
+            # phase the source integrates, so the waveform moves by several times the mel's error (each stage alone is
+            # checked at its own tolerance in its test)
+            assert a.numel() == ref.numel() and e < 3e-2
+    assert enc.usage() == (0, 0, 0)
+    assert fd.pool.in_use() - fd.scratch == 0

@@ -54,7 +54,7 @@ constexpr int kPadMel = 4;            // zero rows on each side of a window's me
 constexpr int kNfft = 16, kHop = 4, kBins = kNfft / 2 + 1;
 
 // ---------------------------------------------------------------- generic fp32 convolution
-enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4 };
+enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4, HE_LEAKY = 5 };
 
 struct ConvGeo {
   const int* vrow = nullptr;  // virtual rows: (stream << 20) | v, v the index within the stream
@@ -73,85 +73,77 @@ struct ConvGeo {
   int epi = HE_NONE;
   const float* alpha = nullptr;  // HE_SNAKE: this conv's Snake; HE_RESID: the next Snake (out2), per channel
   const float* inv = nullptr;    // 1 / (alpha + 1e-9)
-  float* out2 = nullptr;         // HE_RESID: Snake(x_new) for the next conv (nullptr: none)
+  float* out2 = nullptr;         // HE_RESID / HE_NONE: Snake of the output for the next conv (nullptr: none)
+  float slope = 0.f;             // HE_LEAKY
 };
 
-constexpr int kTM = 64, kTN = 64, kTK = 16;
+constexpr int kTK = 16;
 
 __device__ __forceinline__ float snake(float x, float a, float inv) {
   const float s = sinf(x * a);
   return x + inv * (s * s);
 }
 
+// TM x TN outputs per block, 256 threads of 4 x 4; K = taps * Cin flattened (tap-major), 16 per shared-memory chunk, so
+// narrow inputs (18 STFT channels, 80 mel channels) waste no chunk lanes.
+template <int TM, int TN>
 __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
-  __shared__ float As[kTK][kTM + 4];
-  __shared__ float Ws[kTK][kTN + 4];
-  __shared__ int rowb[kTM];  // per tile row: global input row of the stream's data start, or -1
-  __shared__ int rowv[kTM];  // input index of tap 0 (before the tap offset), and the data length below
-  __shared__ int rowl[kTM];
+  constexpr int TX = TN / 4;  // threads across columns
+  __shared__ float As[kTK][TM + 4];
+  __shared__ float Ws[kTK][TN + 4];
+  __shared__ int rowb[TM];  // per tile row: global input row of the stream's data start, or -1
+  __shared__ int rowv[TM];  // input index of tap 0
+  __shared__ int rowl[TM];  // the stream's input data length
   pdl_wait();
   pdl_launch();
   const int tid = threadIdx.x;
-  const int r0 = blockIdx.x * kTM, c0 = blockIdx.y * kTN;
-  if (tid < kTM) {
-    const int r = r0 + tid;
+  const int r0 = blockIdx.x * TM, c0 = blockIdx.y * TN;
+  for (int t = tid; t < TM; t += 256) {
+    const int r = r0 + t;
     if (r < g.nv) {
       const int e = g.vrow[r], s = e >> 20, v = e & 0xFFFFF;
-      rowb[tid] = g.in_start[s];
-      rowv[tid] = g.stride * v + g.off;
-      rowl[tid] = g.in_len[s];
+      rowb[t] = g.in_start[s];
+      rowv[t] = g.stride * v + g.off;
+      rowl[t] = g.in_len[s];
     } else {
-      rowb[tid] = -1;
-      rowv[tid] = 0;
-      rowl[tid] = 0;
+      rowb[t] = -1;
+      rowv[t] = 0;
+      rowl[t] = 0;
     }
   }
   __syncthreads();
-  const int ty = tid >> 4, tx = tid & 15;
+  const int ty = tid / TX, tx = tid % TX;
   float acc[4][4] = {};
-  const int kchunks = (g.Cin + kTK - 1) / kTK;
-  for (int q = 0; q < g.taps; ++q) {
-    for (int kc = 0; kc < kchunks; ++kc) {
-      const int ci0 = kc * kTK;
-      // A: 64 rows x 16 input channels (4 per thread: one row, 4 consecutive channels)
-      {
-        const int rr = tid >> 2, cc = (tid & 3) * 4;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (rowb[rr] >= 0) {
-          const int idx = rowv[rr] + g.dil * q;
-          if (idx >= 0 && idx < rowl[rr]) {
-            const float* src = g.in + (size_t)(rowb[rr] + idx) * g.ld_in;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (ci0 + cc + u < g.Cin) v[u] = src[ci0 + cc + u];
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) As[cc + u][rr] = v[u];
+  const int K = g.taps * g.Cin;
+  for (int k0 = 0; k0 < K; k0 += kTK) {
+    // A: TM rows x 16 of K
+    for (int i = tid; i < TM * kTK; i += 256) {
+      const int rr = i / kTK, kk = i % kTK, k = k0 + kk;
+      float v = 0.f;
+      if (k < K && rowb[rr] >= 0) {
+        const int q = k / g.Cin, ci = k - q * g.Cin;
+        const int idx = rowv[rr] + g.dil * q;
+        if (idx >= 0 && idx < rowl[rr]) v = g.in[(size_t)(rowb[rr] + idx) * g.ld_in + ci];
       }
-      // W: 64 output channels x 16 input channels
-      {
-        const int oo = tid >> 2, cc = (tid & 3) * 4;
-        const int co = c0 + oo;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int ci = ci0 + cc + u;
-          Ws[cc + u][oo] = (co < g.Cout && ci < g.Cin) ? g.W[((size_t)co * g.taps + q) * g.Cin + ci] : 0.f;
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int k = 0; k < kTK; ++k) {
-        const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
-        const float4 w = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
-        const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
-      }
-      __syncthreads();
+      As[kk][rr] = v;
     }
+    // W: TN output channels x 16 of K
+    for (int i = tid; i < TN * kTK; i += 256) {
+      const int oo = i / kTK, kk = i % kTK, k = k0 + kk, co = c0 + oo;
+      Ws[kk][oo] = (co < g.Cout && k < K) ? g.W[(size_t)co * K + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kTK; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
+      const float4 w = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+    }
+    __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -169,12 +161,15 @@ __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
         case HE_ELU: y = y > 0.f ? y : expm1f(y); break;
         case HE_ABS: y = fabsf(y); break;
         case HE_SNAKE: y = snake(y, g.alpha[co], g.inv[co]); break;
+        case HE_LEAKY: y = y > 0.f ? y : y * g.slope; break;
         case HE_RESID: {
           y = y + *dst;
           if (g.out2) g.out2[orow * g.ld_out + co] = snake(y, g.alpha[co], g.inv[co]);
           break;
         }
-        default: break;
+        default:
+          if (g.out2) g.out2[orow * g.ld_out + co] = snake(y, g.alpha[co], g.inv[co]);
+          break;
       }
       *dst = y;
     }
@@ -202,16 +197,6 @@ __global__ void k_mel_in(const float* __restrict__ win_mel, const HRow* __restri
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
     const float v = t < nc ? cache[(size_t)e.cache * cache_ld + t * C + c] : win_mel[(size_t)(e.mel_off + t - nc) * C + c];
     mel[(size_t)(e.mel0 + t) * C + c] = v;
-  }
-}
-
-// In place: x = leaky_relu(x, slope) over rows (data and zero rows alike: leaky(0) = 0).
-__global__ void k_leaky(float* __restrict__ x, long long n, float slope) {
-  pdl_wait();
-  pdl_launch();
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const float v = x[i];
-    x[i] = v > 0.f ? v : v * slope;
   }
 }
 
@@ -243,17 +228,6 @@ __global__ void k_avg3(const float* __restrict__ x0, const float* __restrict__ x
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const float v = ((x0[i] + x1[i]) + x2[i]) / 3.f;
     y[i] = v > 0.f ? v : v * slope;
-  }
-}
-
-// out = Snake(x) (the source ResBlock's first activation of its input).
-__global__ void k_snake(const float* __restrict__ x, long long n, int C, const float* __restrict__ al,
-                        const float* __restrict__ inv, float* __restrict__ out) {
-  pdl_wait();
-  pdl_launch();
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    out[i] = snake(x[i], al[c], inv[c]);
   }
 }
 
@@ -944,11 +918,24 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     return r;
   };
   {
-    const cudaError_t e1 = cudaMemcpyAsync(ws, img.data(), meta_bytes, cudaMemcpyHostToDevice, st);
-    // every activation buffer starts at zero: the zero rows around each window's data are the convolutions' padding
-    const cudaError_t e2 = cudaMemsetAsync(ws + meta_bytes, 0, total - meta_bytes, st);
-    if (e1 != cudaSuccess || e2 != cudaSuccess) {
-      set_cuda_error(e1 != cudaSuccess ? e1 : e2);
+    cudaError_t e1 = cudaMemcpyAsync(ws, img.data(), meta_bytes, cudaMemcpyHostToDevice, st);
+    // buffers whose rows around the windows' data must read as zero and that no kernel writes in full: the mel rows and
+    // conv_pre's output (read by the transposed conv's tensor-map loads), the source branch and its Snake (added to
+    // every row by the fan-out; read by the ResBlock convs), and the transposed conv's output when the fp32 kernel,
+    // which writes data rows only, makes it
+    auto zero = [&](size_t off, size_t bytes) {
+      if (e1 == cudaSuccess) e1 = cudaMemsetAsync(ws + off, 0, bytes, st);
+    };
+    zero(o_mel, (size_t)pl.A[0] * c.mel * 4);
+    zero(o_x0, (size_t)pl.A[0] * C0 * 4);
+    for (int s = 0; s < 3; ++s) {
+      const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
+      zero(o_sd[s], sz);
+      zero(o_ta[s], sz);
+      if (!h->tf32) zero(o_xs[s], sz);
+    }
+    if (e1 != cudaSuccess) {
+      set_cuda_error(e1);
       return fail(T2W_ERR_CUDA);
     }
   }
@@ -956,8 +943,12 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   float* mel = reinterpret_cast<float*>(P(o_mel));
   auto run = [&](ConvGeo g) -> int {
     if (g.nv <= 0) return T2W_OK;
-    dim3 grid((g.nv + kTM - 1) / kTM, (g.Cout + kTN - 1) / kTN);
-    return ck(launch_k(k_hconv, grid, dim3(256), 0, st, g));
+    if (g.Cout <= 32) {
+      dim3 grid((g.nv + 127) / 128, (g.Cout + 31) / 32);
+      return ck(launch_k(k_hconv<128, 32>, grid, dim3(256), 0, st, g));
+    }
+    dim3 grid((g.nv + 63) / 64, (g.Cout + 63) / 64);
+    return ck(launch_k(k_hconv<64, 64>, grid, dim3(256), 0, st, g));
   };
   auto geo = [&](const HConv& cv, const int* vr, int nv, const int* in_s, const int* in_l, const int* out_s,
                  const float* in, float* outp, int epi) {
@@ -1019,8 +1010,12 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   }
   // 5. conv_pre
   float* x = reinterpret_cast<float*>(P(o_x0));
-  rc = run(geo(h->pre, vm, (int)pl.vr_mel.size(), sm, lm, sm, mel, x, HE_NONE));
-  if (rc) return fail(rc);
+  {
+    ConvGeo cg = geo(h->pre, vm, (int)pl.vr_mel.size(), sm, lm, sm, mel, x, HE_LEAKY);  // stage 0's leaky_relu fused
+    cg.slope = c.lrelu_slope;
+    rc = run(cg);
+    if (rc) return fail(rc);
+  }
   // 6. stages
   const int* vin = vm;
   const int* s_in = sm;
@@ -1029,9 +1024,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   for (int s = 0; s < 3; ++s) {
     HStage& g = h->st[s];
     const int Cs = g.Cout;
-    const long long nel_in = (long long)pl.A[s] * g.Cin;
-    rc = ck(launch_k(k_leaky, dim3(grid_for(nel_in)), dim3(256), 0, st, x, nel_in, c.lrelu_slope));
-    if (rc) return fail(rc);
+    // x already holds leaky_relu(x) (conv_pre's epilogue, or the previous stage's average)
     float* xs = reinterpret_cast<float*>(P(o_xs[s]));
     const int* vs = reinterpret_cast<const int*>(P(o_vs[s]));
     const int* ss = reinterpret_cast<const int*>(P(o_ss[s]));
@@ -1080,6 +1073,9 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                        reinterpret_cast<const int*>(P(o_ls[2])), ss, stft, sd, HE_NONE);
       cg.stride = g.down_stride;
       cg.off = -g.down_pad;
+      cg.alpha = g.src.a1;  // the source ResBlock's first Snake of the branch, written beside it
+      cg.inv = g.src.i1;
+      cg.out2 = ta;
       rc = run(cg);
       if (rc) return fail(rc);
     }
@@ -1142,9 +1138,6 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       }
       return T2W_OK;
     };
-    rc = ck(launch_k(k_snake, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)sd, nel, Cs, (const float*)g.src.a1,
-                     (const float*)g.src.i1, ta));
-    if (rc) return fail(rc);
     rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])));  // xr[0] as scratch before the fan-out
     if (rc) return fail(rc);
     float* xr[3] = {reinterpret_cast<float*>(P(o_xr[s][0])), reinterpret_cast<float*>(P(o_xr[s][1])),
@@ -1164,11 +1157,11 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       rc = resblock(g.res[j], xr[j], ar[j], ta);
       if (rc) return fail(rc);
     }
-    // the stage's output (x0 + x1 + x2) / 3; after the last stage with leaky_relu(., 0.01), conv_post's input (the
-    // next stage applies its own leaky_relu at its start)
+    // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before
+    // the next stage's transposed conv, leaky_relu(., 0.01) before conv_post
     float* nx = reinterpret_cast<float*>(P(o_sd[s]));
     rc = ck(launch_k(k_avg3, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xr[0], (const float*)xr[1],
-                     (const float*)xr[2], nel, s < 2 ? 1.0f : 0.01f, nx));
+                     (const float*)xr[2], nel, s < 2 ? c.lrelu_slope : 0.01f, nx));
     if (rc) return fail(rc);
     x = nx;
     vin = vs;

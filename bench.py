@@ -210,6 +210,7 @@ def cpu_oracle_time(cfg: DiTConfig, streams: list, reps: int, warm: int) -> tupl
     from oracle import dit_oracle
 
     threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
     torch.set_num_threads(threads)
     model = dit_oracle.build_model(cfg, seed=0)
     ts = []
@@ -219,6 +220,7 @@ def cpu_oracle_time(cfg: DiTConfig, streams: list, reps: int, warm: int) -> tupl
         dit_oracle.solve_packed(model, s["x0"], s["mu"], s["cond"], s["spk"], s["P"], s["T"])
         if i >= warm:
             ts.append(time.perf_counter() - t0)
+    torch.set_num_threads(prev)  # the launch-bound records after this one keep the host's default pool
     return ts, threads
 
 
@@ -419,11 +421,13 @@ def reference_gpu_encoder(n: int, prompt_tokens: int, steps: int, warm: int, dev
             "setup_mu_frames_per_s": n * 2 * prompt_tokens / (setup_ms / 1000), "timed_calls": steps}
 
 
-def reference_gpu_hift(n: int, steps: int, warm: int, dev, tf32: bool) -> dict:
+def reference_gpu_hift(n: int, steps: int, warm: int, dev, tf32: bool, graphs: bool = False) -> dict:
     """The reference's own vocoder path on this GPU, unmodified: ``BatchedToken2Wav._vocode``
     (engine/runtime/token2wav_batch.py:813-848) with ``hift_forward`` (engine/models/token2wav.py:230-245), strict fp32
     (cuDNN TF32 off, as the reference runs Token2Wav) or with its ``decode_tf32`` option, over the restated vocoder:
-    ``n`` streams, 50-frame windows, every call one window per stream."""
+    ``n`` streams, 50-frame windows, every call one window per stream.  ``graphs``: its ``t2w_graphs`` option, the
+    vocoder replayed from ``HiFTGraphs`` (engine/runtime/hift_graph.py:22-88; default row buckets, 64 rows in slices of
+    16), the warm-up calls capturing the graphs."""
     _reference_modules()
     from types import SimpleNamespace
 
@@ -437,6 +441,10 @@ def reference_gpu_hift(n: int, steps: int, warm: int, dev, tf32: bool) -> dict:
     hift = ho.build_hift(HIFT, seed=0).to(dev)
     bt = tb.BatchedToken2Wav.__new__(tb.BatchedToken2Wav)
     bt.hift, bt.hift_graphs, bt.hift_decode_tf32 = hift, None, tf32
+    if graphs:
+        from engine.runtime.hift_graph import HiFTGraphs
+
+        bt.hift_graphs = HiFTGraphs(hift, decode_tf32=tf32)
     bt.t2w = SimpleNamespace(window=torch.from_numpy(np.hamming(2 * ho.SOURCE_CACHE)).to(dev))
     sts = [StreamState(prompt=None, flow_cache={}, noise_seed=1000 + i,
                        hift_cache=dict(mel=torch.zeros(1, HIFT.mel, 0, device=dev), source=torch.zeros(1, 1, 0, device=dev),
@@ -455,9 +463,11 @@ def reference_gpu_hift(n: int, steps: int, warm: int, dev, tf32: bool) -> dict:
             if k >= warm:
                 ms.append(e0.elapsed_time(e1))
     m = statistics.median(ms)
-    return {"path": "BatchedToken2Wav._vocode + hift_forward (token2wav_batch.py:813-848, token2wav.py:230-245), "
-                    + ("decode_tf32" if tf32 else "strict fp32"), "streams": n, "ms_per_call": m,
-            "mel_frames_per_s": n * 50 / (m / 1000), "timed_calls": steps}
+    return {"path": "BatchedToken2Wav._vocode + " + ("HiFTGraphs replay (hift_graph.py:22-88)" if graphs else
+                                                      "hift_forward (token2wav.py:230-245)")
+                    + " (token2wav_batch.py:813-848), " + ("decode_tf32" if tf32 else "strict fp32"),
+            "streams": n, "ms_per_call": m, "mel_frames_per_s": n * 50 / (m / 1000), "timed_calls": steps,
+            **({"graph_counts": dict(bt.hift_graphs.counts)} if graphs else {})}
 
 
 def reference_gpu_arm(a) -> None:
@@ -480,13 +490,14 @@ def reference_gpu_arm(a) -> None:
                 rec[name + "_fastdit"] = reference_gpu_fastdit(wl, steps=3, warm=2, dev=dev)
             except Exception as e:
                 rec[name + "_fastdit"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
-    for tf32 in (False, True):
-        key = "hift_64" + ("_tf32" if tf32 else "")
-        try:
-            rec[key] = reference_gpu_hift(64, steps=3, warm=2, dev=dev, tf32=tf32)
-        except Exception as e:
-            rec[key] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
-        torch.cuda.empty_cache()
+    for graphs in (False, True):
+        for tf32 in (False, True):
+            key = "hift_64" + ("_graphs" if graphs else "") + ("_tf32" if tf32 else "")
+            try:
+                rec[key] = reference_gpu_hift(64, steps=3, warm=2, dev=dev, tf32=tf32, graphs=graphs)
+            except Exception as e:
+                rec[key] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+            torch.cuda.empty_cache()
     for io in (False, True):
         key = "encoder_64" + ("_batched_io" if io else "")
         try:
@@ -633,6 +644,7 @@ def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, see
                                            "calls replay one CUDA graph per launch structure"}
     if cpu:
         threads = os.cpu_count() or 1
+        prev = torch.get_num_threads()
         torch.set_num_threads(threads)
         _, s = eo.encode_prompt(flow, prompts[0])
         ts = []
@@ -640,6 +652,7 @@ def encoder_record(dev, n: int, prompt_tokens: int, steps: int, warmup: int, see
             t0 = time.perf_counter()
             eo.encode_window(flow, s, torch.tensor(wins[k % 4][0]), False)
             ts.append(time.perf_counter() - t0)
+        torch.set_num_threads(prev)
         cpu_s = statistics.median(ts[2:])
         rec["cpu_baseline"] = {"value": 2 * T / cpu_s, "unit": "mu frames/s", "cores": threads, "kind": "port",
                                "sample": "1 stream's steady window, fp32 CPU oracle (median of 3 after 2 warm-up)"}
@@ -689,8 +702,7 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float)
 
     def call(k):
         dmel.copy_(mels[k % 3], non_blocking=True)
-        outs = voc.vocode_packed(hs, dmel, [T] * n, [False] * n)
-        flat = torch.cat(outs)
+        flat, _ = voc.vocode_packed(hs, dmel, [T] * n, [False] * n, flat=True)
         host[:flat.numel()].copy_(flat, non_blocking=True)
 
     for k in range(max(warmup, 2)):
@@ -699,8 +711,10 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float)
     st = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
+    t0 = time.perf_counter()
     for k in range(steps):
         call(k)
+    host_ms = (time.perf_counter() - t0) * 1000 / steps
     e1.record(st)
     e1.synchronize()
     ms = e0.elapsed_time(e1) / steps
@@ -710,7 +724,7 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float)
     voc.close()
     return {"workload": f"HiFT vocoder, {n} streams, steady 50-frame windows (58 with the cached 8), upsampling stages "
                         f"in TF32",
-            "ms_per_call": ms, "audio_s_per_s": n * T * 480 / 24000 / (ms / 1000),
+            "ms_per_call": ms, "host_enqueue_ms_per_call": host_ms, "audio_s_per_s": n * T * 480 / 24000 / (ms / 1000),
             "mel_frames_per_s": n * T / (ms / 1000), "tflops": flop / (ms / 1000) / 1e12,
             "h2d_bytes_per_call": n * T * HIFT.mel * 4, "d2h_bytes_per_call": n * T * 480 * 4}
 
@@ -938,7 +952,7 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
         if w_ours and w_ref:  # steady-state windows, 32 per call: FastDiT's graph-replayed window vs this build's call
             ref_gpu["steady_32_speedup_vs_fastdit_window"] = w_ref / w_ours
         h_ours = (sub.get("hift_64") or {}).get("ms_per_call")
-        for k in ("hift_64", "hift_64_tf32"):  # the vocoder's steady call, 64 streams
+        for k in ("hift_64", "hift_64_tf32", "hift_64_graphs", "hift_64_graphs_tf32"):  # the vocoder's steady call
             h_ref = (ref_gpu.get(k) or {}).get("ms_per_call")
             if h_ours and h_ref:
                 ref_gpu.setdefault("hift_speedup", {})[k] = h_ref / h_ours

@@ -507,7 +507,9 @@ typedef struct t2w_hift_config {
   float nsf_alpha, nsf_sigma, voiced_threshold, lrelu_slope, audio_limit;
   int32_t tf32; /* 0: strict fp32 everywhere; 1: the upsampling stages (transposed convs, source and main ResBlocks) on
                  * TF32 tensor cores, the reference's decode_tf32 option (token2wav.py:160-210); the f0 predictor, the
-                 * source, conv_pre, source_downs and conv_post stay fp32 */
+                 * source, conv_pre, source_downs and conv_post stay fp32 — the f0 layers after the first and
+                 * conv_post on the tensor cores in split form (3xTF32: operands as pairs of TF32 values, hi + lo,
+                 * fp32-level accuracy), the rest on CUDA cores */
 } t2w_hift_config;
 
 typedef struct t2w_hift t2w_hift;
@@ -549,6 +551,33 @@ T2W_API int64_t t2w_vocode_samples(const t2w_hift* h, int32_t n, const int32_t* 
                                    const uint8_t* last, int64_t* per_stream, int32_t* frames);
 /* One window per stream; asynchronous on `stream` (the call's scratch is a stream-ordered allocation). */
 T2W_API int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream);
+
+/* Test entry: one launch of the vocoder's tensor-core convolution (the kernel behind the tf32 stages and the split-form
+ * layers), for numerics tests against a plain fp32 / fp64 convolution.
+ *   out[row_mul m + row_add, n] = epi(bias[n] + sum_tap sum_c A[m + tap_row0 + tap dil, c] W[n, tap Cin + c]),
+ * m < M (M % 128 == 0), A rows outside [0, rows_a) read as zero, rows with pad[row_mul m + row_add] != 0 written as zero
+ * (epi 0 bias, 1 Snake with alpha / inv, 3 ELU) or left as they are (2: out += ..., and Snake(out) into out2 when
+ * out2 != NULL).  Cin % 32 == 0; N % 128 == 0, 64 or 32.  split_in: A rows are [hi | lo] (2 Cin floats) and W has
+ * [W_hi | W_lo | W_hi] per tap (3 Cin columns); split_out: the output rows are written as [hi | lo] (2 N floats).
+ * Asynchronous on `stream`; a bounded wait that gives up writes T2W_ERR_TIMEOUT into *err (device int). */
+typedef struct t2w_tconv_args {
+  const float* A;
+  int32_t lda, rows_a;
+  const float* W;
+  const float* bias;
+  int32_t M, N, Cin, taps, tap_row0, dil;
+  float* out;
+  int64_t ldo;
+  int32_t row_mul, row_add;
+  const uint8_t* pad;
+  int32_t epi;
+  const float* alpha;
+  const float* inv;
+  float* out2;
+  int32_t split_in, split_out;
+  int32_t* err;
+} t2w_tconv_args;
+T2W_API int t2w_test_tconv(const t2w_tconv_args* a, void* stream);
 
 #ifdef __cplusplus
 }

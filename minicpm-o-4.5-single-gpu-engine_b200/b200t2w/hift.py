@@ -94,6 +94,7 @@ class B200HiFT:
         self.handle = h
         self.max_frames = max_frames
         self._seeds: dict = {}  # handle -> [noise seed, chunks so far]
+        self._gens: dict = {}  # handle -> its device generator, re-seeded for every chunk
 
     @classmethod
     def from_module(cls, hift, cfg: HiFTConfig = HIFT, **kw) -> "B200HiFT":
@@ -117,32 +118,36 @@ class B200HiFT:
         h = ctypes.c_int32()
         L.call("t2w_hift_stream_new", self.handle, ctypes.byref(h))
         self._seeds[h.value] = [int(noise_seed), 0]
+        self._gens[h.value] = torch.Generator(device=self.device)
         return h.value
 
     def release(self, handle: int) -> None:
         L.call("t2w_hift_stream_release", self.handle, int(handle))
         self._seeds.pop(int(handle), None)
+        self._gens.pop(int(handle), None)
 
-    def _noise(self, seed: int, n_samples: int):
-        """``hift_noise`` for one row (the reference draws on the vocoder's device)."""
-        g = torch.Generator(device=self.device).manual_seed(int(seed))
-        dim = self.cfg.harmonics + 1
-        rand_ini = torch.rand(1, dim, device=self.device, generator=g)
-        noise = torch.randn(1, dim, n_samples, device=self.device, generator=g)
-        return rand_ini, noise
+    def _draw(self, g: torch.Generator, seed: int, rand_ini: torch.Tensor, noise: torch.Tensor) -> None:
+        """``hift_noise`` for one row, in place: ``rand_ini`` [1, dim] then ``noise`` [1, dim, n] drawn as a fresh
+        generator seeded with ``seed`` draws them (``manual_seed`` restarts a CUDA generator's Philox offset at 0, and
+        ``uniform_`` / ``normal_`` are what ``torch.rand`` / ``torch.randn`` fill with)."""
+        g.manual_seed(int(seed))
+        rand_ini.uniform_(0.0, 1.0, generator=g)
+        noise.normal_(0.0, 1.0, generator=g)
 
-    def vocode(self, handles, mels, lasts, noise=None) -> list:
+    def vocode(self, handles, mels, lasts, noise=None, source=None) -> list:
         """One window per stream: ``mels[i]`` [mel, T_i], ``lasts[i]`` the final flag.  Returns each window's samples
         (device fp32 tensors, ``_vocode``'s output).  ``noise``: optional per-window (rand_ini [1, dim], noise [1, dim,
-        480 F_i]) in place of the seeded draws (tests)."""
+        480 F_i]) in place of the seeded draws (tests).  ``source``: optional device fp32 tensor of sum 480 F_i floats
+        that receives the windows' harmonic source signals, back to back."""
         if len(mels) != len(handles) or len(lasts) != len(handles):
             raise ValueError("one mel and one final flag per stream")
         Ts = [int(m.shape[1]) for m in mels]
         packed = torch.cat([m.t() for m in mels]).to(self.device, torch.float32).contiguous()
-        return self.vocode_packed(handles, packed, Ts, lasts, noise)
+        return self.vocode_packed(handles, packed, Ts, lasts, noise, source=source)
 
-    def vocode_packed(self, handles, mel_rows: torch.Tensor, Ts, lasts, noise=None) -> list:
-        """``vocode`` on the windows' mel rows token-major ``[sum T_i, mel]`` (the solve's output layout)."""
+    def vocode_packed(self, handles, mel_rows: torch.Tensor, Ts, lasts, noise=None, flat: bool = False, source=None):
+        """``vocode`` on the windows' mel rows token-major ``[sum T_i, mel]`` (the solve's output layout).  ``flat``:
+        return ``(samples, counts)``, every window's samples back to back in one device tensor, instead of the list."""
         n = len(handles)
         hs = L.i32_array(handles)
         ts = L.i32_array(Ts)
@@ -154,21 +159,32 @@ class B200HiFT:
             raise L.T2WError("t2w_vocode_samples", -1)
         dim = self.cfg.harmonics + 1
         with torch.cuda.device(self.device):
-            if noise is None:
-                draws = []
+            if noise is None:  # every row's draws straight into the packed buffers the library reads
+                samples = [480 * frames[i] for i in range(n)]
+                rand_ini = torch.empty(n, dim, dtype=torch.float32, device=self.device)
+                nz = torch.empty(dim * sum(samples), dtype=torch.float32, device=self.device)
+                o = 0
                 for i, h in enumerate(handles):
                     seed, chunks = self._seeds[int(h)]
-                    draws.append(self._noise(chunk_noise_seed(seed, chunks), 480 * frames[i]))
+                    self._draw(self._gens[int(h)], chunk_noise_seed(seed, chunks), rand_ini[i:i + 1],
+                               nz[o:o + dim * samples[i]].view(1, dim, samples[i]))
+                    o += dim * samples[i]
             else:
-                draws = noise
-            rand_ini = torch.cat([d[0].reshape(1, dim) for d in draws]).to(self.device, torch.float32).contiguous()
-            nz = torch.cat([d[1].reshape(-1) for d in draws]).to(self.device, torch.float32).contiguous()
+                rand_ini = torch.cat([d[0].reshape(1, dim) for d in noise]).to(self.device, torch.float32).contiguous()
+                nz = torch.cat([d[1].reshape(-1) for d in noise]).to(self.device, torch.float32).contiguous()
             out = torch.empty(int(tot), dtype=torch.float32, device=self.device)
+            if source is not None and (source.dtype != torch.float32 or source.device != self.device or
+                                       source.numel() < 480 * sum(frames[i] for i in range(n)) or
+                                       not source.is_contiguous()):
+                raise ValueError("source: a contiguous fp32 tensor on the vocoder's device of sum 480 F_i floats")
+            src = ctypes.c_void_p(source.data_ptr()) if source is not None else None
             b = L.VocodeBatch(n, hs, ts, ls, ctypes.c_void_p(mel_rows.data_ptr()), ctypes.c_void_p(rand_ini.data_ptr()),
-                              ctypes.c_void_p(nz.data_ptr()), ctypes.c_void_p(out.data_ptr()), None, None)
+                              ctypes.c_void_p(nz.data_ptr()), ctypes.c_void_p(out.data_ptr()), src, None)
             L.call("t2w_vocode", self.handle, ctypes.byref(b), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         for h in handles:
             self._seeds[int(h)][1] += 1
+        if flat:
+            return out, list(per)
         res, o = [], 0
         for i in range(n):
             res.append(out[o:o + per[i]])

@@ -111,6 +111,16 @@ class VocodeBatch(ctypes.Structure):
                [(n, ctypes.c_void_p) for n in ("mel", "rand_ini", "noise", "out", "source", "speech")]
 
 
+class TConvArgs(ctypes.Structure):
+    _fields_ = [("A", ctypes.c_void_p), ("lda", ctypes.c_int32), ("rows_a", ctypes.c_int32), ("W", ctypes.c_void_p),
+                ("bias", ctypes.c_void_p)] + \
+               [(n, ctypes.c_int32) for n in ("M", "N", "Cin", "taps", "tap_row0", "dil")] + \
+               [("out", ctypes.c_void_p), ("ldo", ctypes.c_int64), ("row_mul", ctypes.c_int32),
+                ("row_add", ctypes.c_int32), ("pad", ctypes.c_void_p), ("epi", ctypes.c_int32),
+                ("alpha", ctypes.c_void_p), ("inv", ctypes.c_void_p), ("out2", ctypes.c_void_p),
+                ("split_in", ctypes.c_int32), ("split_out", ctypes.c_int32), ("err", ctypes.c_void_p)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _F = ctypes.c_float
@@ -188,6 +198,7 @@ _SIGS = {
     "t2w_vocode_samples": ([_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_uint8),
                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_I)], ctypes.c_int64),
     "t2w_vocode": ([_P, ctypes.POINTER(VocodeBatch), _P], ctypes.c_int),
+    "t2w_test_tconv": ([ctypes.POINTER(TConvArgs), _P], ctypes.c_int),
     "t2w_gemm_e4m3": ([_P, _I, _I, _P, _I, ctypes.c_int64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P,
                        ctypes.POINTER(_P), _F, _P], ctypes.c_int),
 }

@@ -54,11 +54,11 @@ constexpr int kPadMel = 4;            // zero rows on each side of a window's me
 constexpr int kNfft = 16, kHop = 4, kBins = kNfft / 2 + 1;
 
 // ---------------------------------------------------------------- generic fp32 convolution
-enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4, HE_LEAKY = 5 };
+enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4, HE_LEAKY = 5, HE_ELU_SPLIT = 6 };
 
 struct ConvGeo {
-  const int* vrow = nullptr;  // virtual rows: (stream << 20) | v, v the index within the stream
-  int nv = 0;
+  const int* vstart = nullptr;  // virtual rows: stream s owns [vstart[s], vstart[s + 1]), v = row - vstart[s]
+  int nstreams = 0, nv = 0;     // nv = vstart[nstreams]
   const int* in_start = nullptr;  // per stream: global row of its input data, and the data's length
   const int* in_len = nullptr;
   const int* out_start = nullptr;  // per stream: global row of its output data
@@ -79,6 +79,23 @@ struct ConvGeo {
 
 constexpr int kTK = 16;
 
+// The stream of virtual row r: the last s with vstart[s] <= r (vstart ascending, vstart[0] = 0 <= r < vstart[n]).
+__device__ __forceinline__ int stream_of(const int* __restrict__ vstart, int n, int r) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (vstart[mid] <= r)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+// fp32 rounded to the nearest TF32 value (half of the dropped unit added to the bit pattern, then the 13 low mantissa
+// bits cleared); a value's split form for the tensor-core convolution is hi = tf32_rn(x), lo = tf32_rn(x - hi).
+__device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
+
 __device__ __forceinline__ float snake(float x, float a, float inv) {
   const float s = sinf(x * a);
   return x + inv * (s * s);
@@ -94,6 +111,7 @@ __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
   __shared__ int rowb[TM];  // per tile row: global input row of the stream's data start, or -1
   __shared__ int rowv[TM];  // input index of tap 0
   __shared__ int rowl[TM];  // the stream's input data length
+  __shared__ int rowo[TM];  // output row, or -1 past the last virtual row
   pdl_wait();
   pdl_launch();
   const int tid = threadIdx.x;
@@ -101,14 +119,16 @@ __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
   for (int t = tid; t < TM; t += 256) {
     const int r = r0 + t;
     if (r < g.nv) {
-      const int e = g.vrow[r], s = e >> 20, v = e & 0xFFFFF;
+      const int s = stream_of(g.vstart, g.nstreams, r), v = r - g.vstart[s];
       rowb[t] = g.in_start[s];
       rowv[t] = g.stride * v + g.off;
       rowl[t] = g.in_len[s];
+      rowo[t] = g.out_start[s] + g.u_out * v + g.p_out;
     } else {
       rowb[t] = -1;
       rowv[t] = 0;
       rowl[t] = 0;
+      rowo[t] = -1;
     }
   }
   __syncthreads();
@@ -147,10 +167,8 @@ __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int r = r0 + ty * 4 + i;
-    if (r >= g.nv) continue;
-    const int e = g.vrow[r], s = e >> 20, v = e & 0xFFFFF;
-    const size_t orow = (size_t)(g.out_start[s] + g.u_out * v + g.p_out);
+    if (r0 + ty * 4 + i >= g.nv) continue;
+    const size_t orow = (size_t)rowo[ty * 4 + i];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int co = c0 + tx * 4 + j;
@@ -159,6 +177,13 @@ __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
       float* dst = g.out + orow * g.ld_out + co;
       switch (g.epi) {
         case HE_ELU: y = y > 0.f ? y : expm1f(y); break;
+        case HE_ELU_SPLIT: {  // [hi | lo] of the ELU output (ld_out = 2 Cout) for a split-form tensor-core conv
+          y = y > 0.f ? y : expm1f(y);
+          const float hi = tf32_rn(y);
+          dst[g.Cout] = tf32_rn(y - hi);
+          y = hi;
+          break;
+        }
         case HE_ABS: y = fabsf(y); break;
         case HE_SNAKE: y = snake(y, g.alpha[co], g.inv[co]); break;
         case HE_LEAKY: y = y > 0.f ? y : y * g.slope; break;
@@ -221,14 +246,36 @@ __global__ void k_fanout(const float* __restrict__ x, const float* __restrict__ 
 }
 
 // y = leaky_relu((x0 + x1 + x2) / 3, slope)
+// split: y holds [hi | lo] rows of 2 C floats (the input of a split-form tensor-core conv), else C floats per row.
 __global__ void k_avg3(const float* __restrict__ x0, const float* __restrict__ x1, const float* __restrict__ x2,
-                       long long n, float slope, float* __restrict__ y) {
+                       long long n, int C, int split, float slope, float* __restrict__ y) {
   pdl_wait();
   pdl_launch();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const float v = ((x0[i] + x1[i]) + x2[i]) / 3.f;
-    y[i] = v > 0.f ? v : v * slope;
+    float v = ((x0[i] + x1[i]) + x2[i]) / 3.f;
+    v = v > 0.f ? v : v * slope;
+    if (split) {
+      const long long r = i / C, c = i - r * C;
+      const float hi = tf32_rn(v);
+      y[r * 2 * C + c] = hi;
+      y[r * 2 * C + C + c] = tf32_rn(v - hi);
+    } else {
+      y[i] = v;
+    }
   }
+}
+
+// The f0 predictor's head, |w . x + b| per data row of the mel-rate layout (one warp per row; padding rows skipped).
+__global__ void k_f0_head(const float* __restrict__ x, int ld, int C, const float* __restrict__ w,
+                          const float* __restrict__ b, const uint8_t* __restrict__ pad, int rows, float* __restrict__ f0) {
+  pdl_wait();
+  pdl_launch();
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= rows || pad[r]) return;
+  float acc = 0.f;
+  for (int c = lane; c < C; c += 32) acc = fmaf(x[(size_t)r * ld + c], w[c], acc);
+  acc = warp_sum(acc);
+  if (lane == 0) f0[r] = fabsf(acc + b[0]);
 }
 
 // Stage 2's reflection pad: the row before the transposed conv's output = its second row.
@@ -446,6 +493,12 @@ struct t2w_hift {
   std::vector<void*> allocs;
   HConv f0c[8], f0head, pre, post;
   int f0_layers = 0;
+  // split-form (3xTF32) weights [Cout][taps][W_hi | W_lo | W_hi] of the f0 layers after the first and of conv_post
+  // (its 18 outputs padded to 32), for the tensor-core convolution where the reference keeps fp32
+  float* f0s[8] = {};
+  float* post_ws = nullptr;
+  float* post_bs = nullptr;
+  int f0_tc = 0, post_tc = 0;  // those layers run on the tensor cores
   float* lin_w = nullptr;
   float lin_b = 0.f;
   HStage st[3];
@@ -458,6 +511,20 @@ struct t2w_hift {
   std::vector<int> row_free;
   std::vector<uint8_t> row_live, row_first;
   std::mutex mu;
+  // pinned host images of the calls' plans, rotated between uploads (a copy from pageable memory would first
+  // synchronise the stream, so the host could not plan a call while the previous one runs)
+  static constexpr int kStaging = 2;
+  struct Staging {
+    void* host = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+    bool used = false;
+  };
+  Staging staging[kStaging];
+  int staging_next = 0;
+  // the calls' scratch: a stream-ordered pool of this vocoder's own that keeps its memory reserved between calls (the
+  // default pool hands freed memory back at the next synchronisation, and remapping it costs every call milliseconds)
+  cudaMemPool_t pool = nullptr;
 };
 
 namespace {
@@ -498,6 +565,41 @@ int conv(t2w_hift* h, const float* w, const float* b, int Cout, int Cin, int k, 
   H_TRY(up(h, t, &c->W));
   return up(h, hb, &c->b);
 }
+// fp32 -> nearest TF32 value (the device tf32_rn, on the host).
+float tf32_rn_host(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  u = (u + 0x1000u) & 0xFFFFE000u;
+  float r;
+  std::memcpy(&r, &u, 4);
+  return r;
+}
+
+// Split-form weights of a [Cout][k][Cin] conv for the tensor-core convolution: [n_pad][k][W_hi | W_lo | W_hi] (W_hi
+// the weight rounded to TF32, W_lo the remainder rounded to TF32; rows past Cout zero) and the bias padded to n_pad
+// (b == nullptr: the layer keeps its own bias).
+int split_weights(t2w_hift* h, const HConv& cv, int n_pad, float** W, float** b) {
+  std::vector<float> w, bb;
+  H_TRY(down(cv.W, (size_t)cv.Cout * cv.k * cv.Cin, w));
+  H_TRY(down(cv.b, cv.Cout, bb));
+  std::vector<float> t((size_t)n_pad * cv.k * 3 * cv.Cin, 0.f), tb(n_pad, 0.f);
+  for (int o = 0; o < cv.Cout; ++o) {
+    tb[o] = bb[o];
+    for (int j = 0; j < cv.k; ++j) {
+      float* d = &t[((size_t)o * cv.k + j) * 3 * cv.Cin];
+      for (int i = 0; i < cv.Cin; ++i) {
+        const float x = w[((size_t)o * cv.k + j) * cv.Cin + i];
+        const float hi = tf32_rn_host(x);
+        d[i] = hi;
+        d[cv.Cin + i] = tf32_rn_host(x - hi);
+        d[2 * cv.Cin + i] = hi;
+      }
+    }
+  }
+  H_TRY(up(h, t, W));
+  return b ? up(h, tb, b) : T2W_OK;
+}
+
 int snake_params(t2w_hift* h, const float* const* a, int C, float** al, float** inv) {
   std::vector<float> va((size_t)3 * C), vi((size_t)3 * C);
   for (int d = 0; d < 3; ++d) {
@@ -633,6 +735,14 @@ int create_impl(t2w_hift* h, const float* const* W) {
     const float* bt = next();
     H_TRY(conv(h, wt, bt, kNfft + 2, c.channels >> 3, 7, &h->post));
   }
+  // the fp32 layers outside the upsampling stages on the tensor cores in split form, where their shapes allow
+  if (h->tf32) {
+    const int fc = c.f0_channels;
+    h->f0_tc = c.f0_layers > 1 && (fc % 128 == 0 || fc == 64 || fc == 32);
+    for (int l = 1; l < c.f0_layers && h->f0_tc; ++l) H_TRY(split_weights(h, h->f0c[l], fc, &h->f0s[l], nullptr));
+    h->post_tc = (c.channels >> 3) % 32 == 0 && kNfft + 2 <= 32;
+    if (h->post_tc) H_TRY(split_weights(h, h->post, 32, &h->post_ws, &h->post_bs));
+  }
   // window (periodic Hann), cos / sin tables of 2 pi k / 16, Hamming cross-fade window (float64, as np.hamming)
   std::vector<float> tw(48);
   for (int k = 0; k < 16; ++k) {
@@ -647,6 +757,15 @@ int create_impl(t2w_hift* h, const float* const* W) {
   H_CUDA(cudaMemcpy(h->hamming, hm.data(), hm.size() * 8, cudaMemcpyHostToDevice));
   H_TRY(halloc(h, &h->err, 1));
   H_CUDA(cudaMemset(h->err, 0, 4));
+  {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = h->device;
+    H_CUDA(cudaMemPoolCreate(&h->pool, &props));
+    uint64_t keep = UINT64_MAX;
+    H_CUDA(cudaMemPoolSetAttribute(h->pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  }
   h->cache_ld = kMelCache * c.mel + 2 * kSrcCache;
   H_TRY(halloc(h, &h->cache, (size_t)h->n_streams * h->cache_ld));
   H_CUDA(cudaMemset(h->cache, 0, (size_t)h->n_streams * h->cache_ld * 4));
@@ -659,6 +778,13 @@ int create_impl(t2w_hift* h, const float* const* W) {
 void free_all(t2w_hift* h) {
   for (void* p : h->allocs) cudaFree(p);
   h->allocs.clear();
+  for (auto& sg : h->staging) {
+    if (sg.host) cudaFreeHost(sg.host);
+    if (sg.done) cudaEventDestroy(sg.done);
+    sg = t2w_hift::Staging();
+  }
+  if (h->pool) cudaMemPoolDestroy(h->pool);
+  h->pool = nullptr;
 }
 
 // ---- a call's plan
@@ -667,8 +793,7 @@ struct HPlan {
   std::vector<HRow> rows;
   int R[4] = {};  // rows at the mel rate and the three stage rates
   int A[4] = {};  // allocated rows: the mel rate rounded up to 128, the stages its 8, 40 and 120 multiples
-  std::vector<uint8_t> pad[4];  // per allocated row: 1 unless it holds a window's data
-  std::vector<int> vr_mel, vr_s[3], vr_stft;  // virtual rows: data rows of each rate, and the STFT frames
+  std::vector<int> vs_mel, vs_s[3];  // virtual rows (the windows' data rows back to back) per rate: prefix offsets
   std::vector<int> start_mel, len_mel, start_s[3], len_s[3], start_up[3];
   long long samples = 0, out_samples = 0;
 };
@@ -676,6 +801,8 @@ struct HPlan {
 int make_plan(t2w_hift* h, int n, const int32_t* handle, const int32_t* T, const uint8_t* last, HPlan& pl) {
   pl = HPlan();
   pl.n = n;
+  pl.vs_mel.assign(1, 0);
+  for (int s = 0; s < 3; ++s) pl.vs_s[s].assign(1, 0);
   const int up = (int)(h->cfg.up_rates[0] * h->cfg.up_rates[1] * h->cfg.up_rates[2]) * kHop;  // 480
   int rm = 0, r0 = 0, r1 = 0, r2 = 0, mel_off = 0;
   long long smp = 0, outp = 0;
@@ -699,10 +826,10 @@ int make_plan(t2w_hift* h, int n, const int32_t* handle, const int32_t* T, const
     e.out0 = (int)outp;
     e.out_len = e.last ? N : (first ? N : N - kSrcCache);
     pl.rows.push_back(e);
-    for (int t = 0; t < F; ++t) pl.vr_mel.push_back((i << 20) | t);
-    for (int t = 0; t < 8 * F; ++t) pl.vr_s[0].push_back((i << 20) | t);
-    for (int t = 0; t < 40 * F; ++t) pl.vr_s[1].push_back((i << 20) | t);
-    for (int t = 0; t < 120 * F + 1; ++t) pl.vr_s[2].push_back((i << 20) | t);
+    pl.vs_mel.push_back(pl.vs_mel.back() + F);
+    pl.vs_s[0].push_back(pl.vs_s[0].back() + 8 * F);
+    pl.vs_s[1].push_back(pl.vs_s[1].back() + 40 * F);
+    pl.vs_s[2].push_back(pl.vs_s[2].back() + 120 * F + 1);
     pl.start_mel.push_back(e.mel0);
     pl.len_mel.push_back(F);
     pl.start_s[0].push_back(e.s0);
@@ -732,16 +859,20 @@ int make_plan(t2w_hift* h, int n, const int32_t* handle, const int32_t* T, const
   pl.A[1] = 8 * pl.A[0];
   pl.A[2] = 40 * pl.A[0];
   pl.A[3] = 120 * pl.A[0];
-  for (int r = 0; r < 4; ++r) pl.pad[r].assign(pl.A[r], 1);
-  for (const HRow& e : pl.rows) {
-    for (int t = 0; t < e.F; ++t) pl.pad[0][e.mel0 + t] = 0;
-    for (int t = 0; t < 8 * e.F; ++t) pl.pad[1][e.s0 + t] = 0;
-    for (int t = 0; t < 40 * e.F; ++t) pl.pad[2][e.s1 + t] = 0;
-    for (int t = 0; t < 120 * e.F + 1; ++t) pl.pad[3][e.s2 + t] = 0;
-  }
   pl.samples = smp;
   pl.out_samples = outp;
   return T2W_OK;
+}
+
+// The per-row padding flags of each rate (1 unless the row holds a window's data), written into dst[r] (A[r] bytes).
+void fill_pads(const HPlan& pl, uint8_t* const dst[4]) {
+  for (int r = 0; r < 4; ++r) std::memset(dst[r], 1, pl.A[r]);
+  for (const HRow& e : pl.rows) {
+    std::memset(dst[0] + e.mel0, 0, e.F);
+    std::memset(dst[1] + e.s0, 0, 8 * e.F);
+    std::memset(dst[2] + e.s1, 0, 40 * e.F);
+    std::memset(dst[3] + e.s2, 0, 120 * e.F + 1);
+  }
 }
 
 }  // namespace
@@ -865,10 +996,10 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     return o;
   };
   const size_t o_rows = add(pl.rows.size() * sizeof(HRow));
-  const size_t o_vm = add(pl.vr_mel.size() * 4), o_sm = add(n * 4), o_lm = add(n * 4);
+  const size_t o_vm = add((n + 1) * 4), o_sm = add(n * 4), o_lm = add(n * 4);
   size_t o_vs[3], o_ss[3], o_ls[3], o_su[3];
   for (int s = 0; s < 3; ++s) {
-    o_vs[s] = add(pl.vr_s[s].size() * 4);
+    o_vs[s] = add((n + 1) * 4);
     o_ss[s] = add(n * 4);
     o_ls[s] = add(n * 4);
     o_su[s] = add(n * 4);
@@ -877,7 +1008,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   for (int r = 0; r < 4; ++r) o_pad[r] = add(pl.A[r]);
   const size_t meta_bytes = meta;
   const size_t o_mel = add((size_t)pl.A[0] * c.mel * 4);
-  const size_t o_f0a = add((size_t)pl.A[0] * c.f0_channels * 4), o_f0b = add((size_t)pl.A[0] * c.f0_channels * 4);
+  // the f0 layers' activations, [hi | lo] pairs (2 x f0_channels floats per row) when they feed the split-form convs
+  const size_t o_f0a = add((size_t)pl.A[0] * c.f0_channels * 8), o_f0b = add((size_t)pl.A[0] * c.f0_channels * 8);
   const size_t o_f0 = add((size_t)pl.A[0] * 4);
   const size_t o_src = add((size_t)pl.samples * 4), o_sp = add((size_t)pl.samples * 4);
   const size_t o_stft = add((size_t)pl.A[3] * (kNfft + 2) * 4);
@@ -892,41 +1024,69 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     o_sd[s] = add(sz);
     o_ta[s] = add(sz);
   }
-  const size_t o_post = add((size_t)pl.A[3] * (kNfft + 2) * 4);
+  const int post_ld = h->post_tc ? 32 : kNfft + 2;  // conv_post's output (18 columns; 32 on the tensor cores)
+  const size_t o_post = add((size_t)pl.A[3] * post_ld * 4);
+  // stage 2's output as [hi | lo] pairs, conv_post's input in split form
+  const size_t o_xps = h->post_tc ? add((size_t)pl.A[3] * (C0 >> 3) * 8) : 0;
   const size_t total = meta;
   uint8_t* ws = nullptr;
-  H_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), total, st));
+  H_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), total, h->pool, st));
   auto P = [&](size_t o) { return ws + o; };
-  std::vector<uint8_t> img(meta_bytes);
+  // the plan's image in a pinned staging buffer, rewritten only after the copy that last read it has completed
+  t2w_hift::Staging& sg = h->staging[h->staging_next];
+  h->staging_next = (h->staging_next + 1) % t2w_hift::kStaging;
+  cudaError_t se = cudaSuccess;
+  if (sg.used) se = cudaEventSynchronize(sg.done);
+  if (se == cudaSuccess && sg.cap < meta_bytes) {
+    if (sg.host) cudaFreeHost(sg.host);
+    sg.host = nullptr;
+    sg.cap = 0;
+    const size_t cap = std::max<size_t>(meta_bytes + meta_bytes / 4, 1 << 16);
+    se = cudaMallocHost(&sg.host, cap);
+    if (se == cudaSuccess) sg.cap = cap;
+  }
+  if (se == cudaSuccess && !sg.done) se = cudaEventCreateWithFlags(&sg.done, cudaEventDisableTiming);
+  if (se != cudaSuccess) {
+    set_cuda_error(se);
+    cudaFreeAsync(ws, st);
+    return T2W_ERR_CUDA;
+  }
+  uint8_t* img = static_cast<uint8_t*>(sg.host);
   auto put = [&](size_t o, const void* s, size_t bytes) {
-    if (bytes) std::memcpy(img.data() + o, s, bytes);
+    if (bytes) std::memcpy(img + o, s, bytes);
   };
   put(o_rows, pl.rows.data(), pl.rows.size() * sizeof(HRow));
-  put(o_vm, pl.vr_mel.data(), pl.vr_mel.size() * 4);
+  put(o_vm, pl.vs_mel.data(), (n + 1) * 4);
   put(o_sm, pl.start_mel.data(), n * 4);
   put(o_lm, pl.len_mel.data(), n * 4);
   for (int s = 0; s < 3; ++s) {
-    put(o_vs[s], pl.vr_s[s].data(), pl.vr_s[s].size() * 4);
+    put(o_vs[s], pl.vs_s[s].data(), (n + 1) * 4);
     put(o_ss[s], pl.start_s[s].data(), n * 4);
     put(o_ls[s], pl.len_s[s].data(), n * 4);
     put(o_su[s], pl.start_up[s].data(), n * 4);
   }
-  for (int r = 0; r < 4; ++r) put(o_pad[r], pl.pad[r].data(), pl.A[r]);
+  {
+    uint8_t* const pads[4] = {img + o_pad[0], img + o_pad[1], img + o_pad[2], img + o_pad[3]};
+    fill_pads(pl, pads);
+  }
   int rc = T2W_OK;
   auto fail = [&](int r) {
     cudaFreeAsync(ws, st);
     return r;
   };
   {
-    cudaError_t e1 = cudaMemcpyAsync(ws, img.data(), meta_bytes, cudaMemcpyHostToDevice, st);
+    cudaError_t e1 = cudaMemcpyAsync(ws, img, meta_bytes, cudaMemcpyHostToDevice, st);
+    if (e1 == cudaSuccess) e1 = cudaEventRecord(sg.done, st);
+    if (e1 == cudaSuccess) sg.used = true;
     // buffers whose rows around the windows' data must read as zero and that no kernel writes in full: the mel rows and
     // conv_pre's output (read by the transposed conv's tensor-map loads), the source branch and its Snake (added to
     // every row by the fan-out; read by the ResBlock convs), and the transposed conv's output when the fp32 kernel,
-    // which writes data rows only, makes it
+    // which writes data rows only, makes it; and the first f0 layer's output when the split-form convs read it
     auto zero = [&](size_t off, size_t bytes) {
       if (e1 == cudaSuccess) e1 = cudaMemsetAsync(ws + off, 0, bytes, st);
     };
     zero(o_mel, (size_t)pl.A[0] * c.mel * 4);
+    if (h->f0_tc) zero(o_f0a, (size_t)pl.A[0] * c.f0_channels * 8);
     zero(o_x0, (size_t)pl.A[0] * C0 * 4);
     for (int s = 0; s < 3; ++s) {
       const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
@@ -953,7 +1113,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   auto geo = [&](const HConv& cv, const int* vr, int nv, const int* in_s, const int* in_l, const int* out_s,
                  const float* in, float* outp, int epi) {
     ConvGeo g;
-    g.vrow = vr;
+    g.vstart = vr;
+    g.nstreams = n;
     g.nv = nv;
     g.in_start = in_s;
     g.in_len = in_l;
@@ -982,18 +1143,49 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     rc = ck(launch_k(k_mel_in, grid, dim3(128), 0, st, b->mel, drows, (const float*)h->cache, h->cache_ld, c.mel, mel));
     if (rc) return fail(rc);
   }
-  // 2. f0 predictor: convs + ELU, then |linear|
+  // 2. f0 predictor: convs + ELU, then |linear|.  On the tensor cores (split form, fp32-level accuracy) every layer
+  // after the first: the first (80 mel channels) writes its ELU output as [hi | lo] pairs, the middle layers read and
+  // write pairs, the last writes plain fp32 for the head.
   {
     float* a = reinterpret_cast<float*>(P(o_f0a));
     float* bb = reinterpret_cast<float*>(P(o_f0b));
     const float* in = mel;
+    const int fc = c.f0_channels;
+    const uint8_t* pad0 = reinterpret_cast<const uint8_t*>(P(o_pad[0]));
     for (int l = 0; l < h->f0_layers; ++l) {
       float* o = (l & 1) ? bb : a;
-      rc = run(geo(h->f0c[l], vm, (int)pl.vr_mel.size(), sm, lm, sm, in, o, HE_ELU));
+      const bool split_out = h->f0_tc && l + 1 < h->f0_layers;
+      if (l == 0 || !h->f0_tc) {
+        ConvGeo cg = geo(h->f0c[l], vm, pl.vs_mel[n], sm, lm, sm, in, o, split_out ? HE_ELU_SPLIT : HE_ELU);
+        if (split_out) cg.ld_out = 2 * fc;
+        rc = run(cg);
+      } else {
+        TConvArgs t;
+        t.A = in;
+        t.lda = 2 * fc;
+        t.rows_a = pl.A[0];
+        t.W = h->f0s[l];
+        t.bias = h->f0c[l].b;
+        t.M = pl.A[0];
+        t.N = fc;
+        t.Cin = fc;
+        t.taps = 3;
+        t.tap_row0 = -1;
+        t.out = o;
+        t.ldo = split_out ? 2 * fc : fc;
+        t.pad = pad0;
+        t.epi = TCONV_ELU;
+        t.split_in = 1;
+        t.split_out = split_out;
+        t.err = h->err;
+        rc = launch_tconv(t, st);
+      }
       if (rc) return fail(rc);
       in = o;
     }
-    rc = run(geo(h->f0head, vm, (int)pl.vr_mel.size(), sm, lm, sm, in, reinterpret_cast<float*>(P(o_f0)), HE_ABS));
+    const int ld = h->f0c[h->f0_layers - 1].Cout;
+    rc = ck(launch_k(k_f0_head, dim3((pl.A[0] + 7) / 8), dim3(256), 0, st, in, ld, fc, (const float*)h->f0head.W,
+                     (const float*)h->f0head.b, pad0, pl.A[0], reinterpret_cast<float*>(P(o_f0))));
     if (rc) return fail(rc);
   }
   // 3. the harmonic source, 4. its STFT
@@ -1011,7 +1203,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   // 5. conv_pre
   float* x = reinterpret_cast<float*>(P(o_x0));
   {
-    ConvGeo cg = geo(h->pre, vm, (int)pl.vr_mel.size(), sm, lm, sm, mel, x, HE_LEAKY);  // stage 0's leaky_relu fused
+    ConvGeo cg = geo(h->pre, vm, pl.vs_mel[n], sm, lm, sm, mel, x, HE_LEAKY);  // stage 0's leaky_relu fused
     cg.slope = c.lrelu_slope;
     rc = run(cg);
     if (rc) return fail(rc);
@@ -1020,7 +1212,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   const int* vin = vm;
   const int* s_in = sm;
   const int* l_in = lm;
-  int nvin = (int)pl.vr_mel.size();
+  int nvin = pl.vs_mel[n];
   for (int s = 0; s < 3; ++s) {
     HStage& g = h->st[s];
     const int Cs = g.Cout;
@@ -1069,7 +1261,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     float* sd = reinterpret_cast<float*>(P(o_sd[s]));
     float* ta = reinterpret_cast<float*>(P(o_ta[s]));
     {
-      ConvGeo cg = geo(g.down, vs, (int)pl.vr_s[s].size(), reinterpret_cast<const int*>(P(o_ss[2])),
+      ConvGeo cg = geo(g.down, vs, pl.vs_s[s][n], reinterpret_cast<const int*>(P(o_ss[2])),
                        reinterpret_cast<const int*>(P(o_ls[2])), ss, stft, sd, HE_NONE);
       cg.stride = g.down_stride;
       cg.off = -g.down_pad;
@@ -1121,13 +1313,13 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
           H_TRY(launch_tconv(t2, st));
           continue;
         }
-        ConvGeo c1 = geo(r.c1[dd], vs, (int)pl.vr_s[s].size(), ss, ls, ss, a_in, tmp, HE_SNAKE);
+        ConvGeo c1 = geo(r.c1[dd], vs, pl.vs_s[s][n], ss, ls, ss, a_in, tmp, HE_SNAKE);
         c1.dil = dl;
         c1.off = -(r.k * dl - dl) / 2;
         c1.alpha = r.a2 + dd * Cs;
         c1.inv = r.i2 + dd * Cs;
         H_TRY(run(c1));
-        ConvGeo c2 = geo(r.c2[dd], vs, (int)pl.vr_s[s].size(), ss, ls, ss, tmp, xr, HE_RESID);
+        ConvGeo c2 = geo(r.c2[dd], vs, pl.vs_s[s][n], ss, ls, ss, tmp, xr, HE_RESID);
         c2.off = -(r.k - 1) / 2;
         if (dd < 2) {
           c2.alpha = r.a1 + (dd + 1) * Cs;
@@ -1159,29 +1351,51 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     }
     // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before
     // the next stage's transposed conv, leaky_relu(., 0.01) before conv_post
-    float* nx = reinterpret_cast<float*>(P(o_sd[s]));
+    const int split = s == 2 && h->post_tc;  // conv_post on the tensor cores reads [hi | lo] pairs
+    float* nx = reinterpret_cast<float*>(P(split ? o_xps : o_sd[s]));
     rc = ck(launch_k(k_avg3, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xr[0], (const float*)xr[1],
-                     (const float*)xr[2], nel, s < 2 ? c.lrelu_slope : 0.01f, nx));
+                     (const float*)xr[2], nel, Cs, split, s < 2 ? c.lrelu_slope : 0.01f, nx));
     if (rc) return fail(rc);
     x = nx;
     vin = vs;
     s_in = ss;
     l_in = ls;
-    nvin = (int)pl.vr_s[s].size();
+    nvin = pl.vs_s[s][n];
   }
   // 7. conv_post, inverse STFT, cross-fade, output, caches
   float* post = reinterpret_cast<float*>(P(o_post));
   {
     const int* ss2 = reinterpret_cast<const int*>(P(o_ss[2]));
     const int* ls2 = reinterpret_cast<const int*>(P(o_ls[2]));
-    rc = run(geo(h->post, reinterpret_cast<const int*>(P(o_vs[2])), (int)pl.vr_s[2].size(), ss2, ls2, ss2, x, post,
-                 HE_NONE));
+    if (h->post_tc) {
+      const int cin = C0 >> 3;
+      TConvArgs t;
+      t.A = x;
+      t.lda = 2 * cin;
+      t.rows_a = pl.A[3];
+      t.W = h->post_ws;
+      t.bias = h->post_bs;
+      t.M = pl.A[3];
+      t.N = 32;
+      t.Cin = cin;
+      t.taps = h->post.k;
+      t.tap_row0 = -(h->post.k / 2);
+      t.out = post;
+      t.ldo = post_ld;
+      t.pad = reinterpret_cast<const uint8_t*>(P(o_pad[3]));
+      t.split_in = 1;
+      t.err = h->err;
+      rc = launch_tconv(t, st);
+    } else {
+      rc = run(geo(h->post, reinterpret_cast<const int*>(P(o_vs[2])), pl.vs_s[2][n], ss2, ls2, ss2, x, post,
+                   HE_NONE));
+    }
     if (rc) return fail(rc);
   }
   float* speech = reinterpret_cast<float*>(P(o_sp));
   {
     dim3 grid((480 * h->max_frames + 255) / 256, n);
-    rc = ck(launch_k(k_istft_out, grid, dim3(256), 0, st, (const float*)post, kNfft + 2, drows, (const float*)h->tw,
+    rc = ck(launch_k(k_istft_out, grid, dim3(256), 0, st, (const float*)post, post_ld, drows, (const float*)h->tw,
                      (const double*)h->hamming, c.audio_limit, 480.f, speech, (const float*)h->cache, h->cache_ld,
                      kMelCache * c.mel + kSrcCache, b->out));
     if (rc) return fail(rc);
@@ -1195,6 +1409,35 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   cudaFreeAsync(ws, st);
   for (int i = 0; i < n; ++i) h->row_first[b->handle[i]] = 0;
   return T2W_OK;
+}
+
+int t2w_test_tconv(const t2w_tconv_args* a, void* stream) {
+  if (!a) return T2W_ERR_INVALID;
+  TConvArgs t;
+  t.A = a->A;
+  t.lda = a->lda;
+  t.rows_a = a->rows_a;
+  t.W = a->W;
+  t.bias = a->bias;
+  t.M = a->M;
+  t.N = a->N;
+  t.Cin = a->Cin;
+  t.taps = a->taps;
+  t.tap_row0 = a->tap_row0;
+  t.dil = a->dil;
+  t.out = a->out;
+  t.ldo = a->ldo;
+  t.row_mul = a->row_mul;
+  t.row_add = a->row_add;
+  t.pad = a->pad;
+  t.epi = a->epi;
+  t.alpha = a->alpha;
+  t.inv = a->inv;
+  t.out2 = a->out2;
+  t.split_in = a->split_in;
+  t.split_out = a->split_out;
+  t.err = a->err;
+  return launch_tconv(t, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

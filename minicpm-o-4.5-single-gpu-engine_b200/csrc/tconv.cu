@@ -1,17 +1,27 @@
-// TF32 tcgen05 implicit-GEMM convolution for the HiFT vocoder's upsampling stages (the transposed convolutions, the
-// source-branch and main ResBlocks): out[m, n] = sum_tap sum_c A[m + tap_row0 + tap * dil, c] W[n, tap * Cin + c].
+// TF32 tcgen05 implicit-GEMM convolution for the HiFT vocoder: out[m, n] = sum_tap sum_c A[m + tap_row0 + tap * dil, c]
+// W[n, tap * Cin + c].
 //
 // A is the time-major fp32 activation [rows, Cin] with zero rows around every window's data (the "same" padding), W
 // the fp32 weight [Cout, taps * Cin]; the tensor core reads both as TF32 (kind::tf32, K = 8 per instruction, fp32
-// accumulation in TMEM) — the reference's own reduced-precision option for these stages (decode_tf32,
-// engine/models/token2wav.py:160-210).  One persistent CTA per SM, warp-specialised as the bf16 GEMM: warp 0 the TMA
-// producer (128 x 32 A boxes and BN x 32 W boxes, 128-byte swizzle, one box pair per (tap, 32-channel block)), warp 1
-// the TMEM allocator and single-thread MMA issuer, warps 2-9 the epilogue (TMEM lane quarter w % 4, alternate 32-column
-// chunks), the accumulator double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.  Output rows:
-// row_mul * m + row_add (a transposed convolution's output phase writes every row_mul-th row of the next rate's layout);
-// rows flagged in `pad` are window padding and stay zero.  Epilogues (fp32, direct stores, one output row per thread):
-// bias; Snake(bias + acc) (the ResBlocks' conv1 with its second activation); x += bias + acc with Snake(x_new) into a
-// second buffer (conv2's residual and the next conv1's input).  No TMA multicast.
+// accumulation in TMEM) — the reference's own reduced-precision option for the upsampling stages (decode_tf32,
+// engine/models/token2wav.py:145-210).  Where the reference keeps fp32 (the f0 predictor, conv_post) the same kernel runs
+// in split form (3xTF32): the operands arrive as hi + lo pairs of TF32-exact values (hi the value rounded to TF32, lo
+// the remainder rounded to TF32) and the K loop runs hi W_hi + hi W_lo + lo W_hi, which leaves the lo x lo term and
+// the pairs' own rounding, about 3 x 2^-24 relative per product: fp32-level accuracy on the tensor core.
+//
+// One persistent CTA per SM, warp-specialised: warp 0 the TMA producer (128 x 32 A boxes and BN x 32 W boxes, 128-byte
+// swizzle, one box pair per (tap, segment, 32-channel block)), warp 1 the TMEM allocator and single-thread MMA issuer,
+// warps 2-9 the epilogue (TMEM lane quarter w % 4, alternate 32-column chunks), the accumulator double-buffered in TMEM
+// so a tile's epilogue overlaps the next tile's MMAs.  Each epilogue thread owns one output row (the TMEM lane it
+// reads) and stores its 32-column chunk directly; a residual update first TMA-loads the warp's 32 x 32 block of the
+// residual into a swizzled shared-memory box (issued before the accumulator is ready) and reads its row from there,
+// instead of 32 scattered row reads per warp.  (Staging the outputs through the box and writing them with TMA stores
+// measured slower for the bias and Snake epilogues.)
+// Output rows: row_mul * m + row_add (a transposed convolution's output phase writes every row_mul-th row of the next
+// rate's layout, a tensor map whose row pitch is row_mul rows); rows flagged in `pad` are window padding and stay zero.
+// Epilogues: bias; Snake(bias + acc) (the ResBlocks' conv1 with its second activation); x += bias + acc with
+// Snake(x_new) into a second buffer (conv2's residual and the next conv1's input); ELU(bias + acc) (the f0 predictor),
+// optionally written as a hi / lo pair for the next split-form layer.  No TMA multicast.
 #include <atomic>
 
 #include "common.cuh"
@@ -25,31 +35,37 @@ namespace {
 constexpr int kTBM = 128;
 constexpr int kTBK = 32;  // fp32 elements per 128-byte swizzle row
 constexpr int kTMaxSmem = 232448;
+constexpr int kEpiWarps = 8;
+constexpr int kEBox = 32 * 32 * 4;  // one epilogue warp's 32 x 32 fp32 staging box
 
 template <int BN>
 struct TCfg {
   static constexpr int A_BYTES = kTBM * kTBK * 4;  // 16 KB
   static constexpr int B_BYTES = BN * kTBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int FIXED = 1024 + 256;
-  static constexpr int STAGES_FIT = (kTMaxSmem - FIXED) / STAGE_BYTES;
+  static constexpr int EPI_BYTES = kEpiWarps * kEBox;
+  static constexpr int FIXED = 1024 + 512;
+  static constexpr int STAGES_FIT = (kTMaxSmem - FIXED - EPI_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + FIXED;
   static_assert(STAGES >= 3, "stages");
+  static_assert(SMEM <= kTMaxSmem, "shared memory");
 };
 
 struct TDev {
   int M, N, Cin, taps, tap_row0, dil, tiles_n, num_tiles;
+  int split_in, split_out;
   const float* bias;
   float* out;
+  float* out2;
+  const uint8_t* pad;
   long long ldo;  // floats between consecutive output rows of the layout (row_mul * m + row_add indexes them)
   int row_mul, row_add;
-  const uint8_t* pad;
   int epi;
   const float* alpha;
   const float* inv;
-  float* out2;
+  int has_out2;
   int* err;
 };
 
@@ -72,19 +88,30 @@ __device__ __forceinline__ float snake_f(float x, float a, float inv) {
   return x + inv * (s * s);
 }
 
+// 16-byte chunk `c` of row `r` of a 128-byte-row box staged with the 128-byte swizzle (chunk index XOR row % 8).
+__device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int c) {
+  return reinterpret_cast<float4*>(box + r * 128 + ((c ^ (r & 7)) << 4));
+}
+// fp32 rounded to the nearest TF32 value (half of the dropped unit added to the bit pattern, then the 13 low mantissa
+// bits cleared): a split x = hi + lo with hi = tf32_rn(x), lo = tf32_rn(x - hi) leaves |x - hi - lo| <= 2^-24 |x|.
+__device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
+
 template <int BN>
 __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
-                                                  const __grid_constant__ CUtensorMap tmW, const TDev p) {
+                                                  const __grid_constant__ CUtensorMap tmW,
+                                                  const __grid_constant__ CUtensorMap tmO, const TDev p) {
   using C = TCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint8_t* sE = sB + C::STAGES * C::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + C::EPI_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* ebar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + kEpiWarps);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -95,9 +122,11 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 8);
     }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&ebar[w], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmO);
   }
   pdl_wait();
   if (warp == 1) {
@@ -109,7 +138,9 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
   tc_fence_after();
   pdl_launch();
   const uint32_t tmem = *tmem_slot;
-  const int kb_per_tap = p.Cin / kTBK;
+  const int kb_per_seg = p.Cin / kTBK;
+  const int segs = p.split_in ? 3 : 1;
+  const int kb_per_tap = kb_per_seg * segs;
   const int num_kb = kb_per_tap * p.taps;
 
   if (warp == 0) {
@@ -122,9 +153,12 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-          const int tap = kb / kb_per_tap, kk = (kb - tap * kb_per_tap) * kTBK;
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, kk, m0 + p.tap_row0 + tap * p.dil, &full[stage]);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmW, tap * p.Cin + kk, n0, &full[stage]);
+          // segment 0: hi x W_hi, 1: hi x W_lo, 2: lo x W_hi (split form); the plain form has segment 0 only
+          const int tap = kb / kb_per_tap, r = kb - tap * kb_per_tap, seg = r / kb_per_seg;
+          const int kk = (r - seg * kb_per_seg) * kTBK;
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, (seg == 2 ? p.Cin : 0) + kk, m0 + p.tap_row0 + tap * p.dil,
+                      &full[stage]);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmW, (tap * segs + seg) * p.Cin + kk, n0, &full[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -162,14 +196,32 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
       }
     }
   } else {
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int ew = warp - 2;
+    const int q = warp & 3;  // the TMEM lane quarter this warp may read
+    const int half = ew >> 2;
+    uint8_t* box = sE + ew * kEBox;
+    uint64_t* eb = &ebar[ew];
+    uint32_t eph = 0;
+    const bool resid = p.epi == TCONV_RESID;
+    bool pending = false;  // a residual load of this warp in flight
+    auto load_resid = [&](int c0, int r0) {
+      if (lane == 0) {
+        mbar_expect_tx(eb, kEBox);
+        tma_load_2d(box, &tmO, c0, r0, eb);
+      }
+      pending = true;
+    };
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
+      const int r0 = m0 + q * 32;  // this warp's first row of the tile
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) break;
+      if (resid && half < BN / 32) load_resid(n0 + 32 * half, r0);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) {
+        if (pending) mbar_wait(eb, eph, p.err);
+        break;
+      }
       tc_fence_after();
       if (half >= BN / 32) {  // a 32-column tile: the second half of the epilogue warps has no chunk of its own
         tc_fence_before();
@@ -177,11 +229,13 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
         if (lane == 0) mbar_arrive(&tempty[acc]);
         continue;
       }
-      const int m = m0 + q * 32 + lane;
-      const long long orow = (long long)p.row_mul * m + p.row_add;
-      const bool live = m < p.M && !p.pad[orow];
+      const long long orow = (long long)p.row_mul * (r0 + lane) + p.row_add;
+      const bool live = !p.pad[orow];
+      bool ok = true;
 #pragma unroll 1
       for (int b = half; b < BN / 32; b += 2) {
+        const int c0 = n0 + 32 * b;
+        if (resid && b != half) load_resid(c0, r0);
         float v[32];
         tmem_ld32(taddr + 32 * b, v);
         if (b + 2 >= BN / 32) {  // this warp's last load of the accumulator
@@ -189,21 +243,19 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[acc]);
         }
-        if (m >= p.M) continue;
-        const int c0 = n0 + 32 * b;
         float* dst = p.out + orow * p.ldo + c0;
-        if (p.epi == TCONV_RESID) {
-          if (!live) continue;  // padding rows keep their zeros
-          float* dst2 = p.out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
+        if (resid) {
+          ok = __all_sync(0xffffffffu, mbar_wait(eb, eph, p.err));
+          eph ^= 1u;
+          pending = false;
+          if (!ok) break;
+          float* dst2 = p.has_out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 x = *reinterpret_cast<const float4*>(dst + 4 * j);
+          for (int j = 0; j < 8 && live; ++j) {  // padding rows keep their (zero) values
+            const float4 x = *box_chunk(box, lane, j);
             const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
-            float4 y;
-            y.x = x.x + (v[4 * j] + bb.x);
-            y.y = x.y + (v[4 * j + 1] + bb.y);
-            y.z = x.z + (v[4 * j + 2] + bb.z);
-            y.w = x.w + (v[4 * j + 3] + bb.w);
+            const float4 y = make_float4(x.x + (v[4 * j] + bb.x), x.y + (v[4 * j + 1] + bb.y),
+                                         x.z + (v[4 * j + 2] + bb.z), x.w + (v[4 * j + 3] + bb.w));
             reinterpret_cast<float4*>(dst)[j] = y;
             if (dst2) {
               const float4 a = __ldg(reinterpret_cast<const float4*>(p.alpha + c0) + j);
@@ -213,6 +265,8 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
                               snake_f(y.w, a.w, iv.w));
             }
           }
+          fence_proxy_async_smem();  // every lane's reads of the box come before the next load overwrites it
+          __syncwarp();
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -225,12 +279,22 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
                 const float4 iv = __ldg(reinterpret_cast<const float4*>(p.inv + c0) + j);
                 y = make_float4(snake_f(y.x, a.x, iv.x), snake_f(y.y, a.y, iv.y), snake_f(y.z, a.z, iv.z),
                                 snake_f(y.w, a.w, iv.w));
+              } else if (p.epi == TCONV_ELU) {
+                y = make_float4(y.x > 0.f ? y.x : expm1f(y.x), y.y > 0.f ? y.y : expm1f(y.y),
+                                y.z > 0.f ? y.z : expm1f(y.z), y.w > 0.f ? y.w : expm1f(y.w));
               }
+            }
+            if (p.split_out) {  // [hi | lo]: the lo half N columns to the right
+              const float4 hi = make_float4(tf32_rn(y.x), tf32_rn(y.y), tf32_rn(y.z), tf32_rn(y.w));
+              reinterpret_cast<float4*>(dst + p.N)[j] =
+                  make_float4(tf32_rn(y.x - hi.x), tf32_rn(y.y - hi.y), tf32_rn(y.z - hi.z), tf32_rn(y.w - hi.w));
+              y = hi;
             }
             reinterpret_cast<float4*>(dst)[j] = y;
           }
         }
       }
+      if (!ok) break;
     }
   }
   __syncthreads();
@@ -249,9 +313,15 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
   }
-  CUtensorMap ma, mw;
-  if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin, (uint64_t)a.lda * 4, kTBM, kTBK) ||
-      !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, (uint64_t)a.Cin * a.taps, (uint64_t)a.Cin * a.taps * 4, BN, kTBK))
+  const int segs = a.split_in ? 3 : 1;
+  const uint64_t out_cols = (uint64_t)a.N * (a.split_out ? 2 : 1);
+  const uint64_t out_pitch = (uint64_t)a.row_mul * a.ldo * 4;
+  CUtensorMap ma, mw, mo;
+  if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin * (a.split_in ? 2 : 1), (uint64_t)a.lda * 4, kTBM,
+                    kTBK) ||
+      !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, (uint64_t)a.Cin * a.taps * segs, (uint64_t)a.Cin * a.taps * segs * 4,
+                    BN, kTBK) ||
+      !make_tmap_2d(&mo, a.out + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M, out_cols, out_pitch, 32, 32))
     return T2W_ERR_INVALID;
   TDev p;
   p.M = a.M;
@@ -262,19 +332,22 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.dil = a.dil;
   p.tiles_n = a.N / BN;
   p.num_tiles = (a.M / kTBM) * p.tiles_n;
+  p.split_in = a.split_in;
+  p.split_out = a.split_out;
   p.bias = a.bias;
   p.out = a.out;
+  p.out2 = a.out2;
+  p.pad = a.pad;
   p.ldo = a.ldo;
   p.row_mul = a.row_mul;
   p.row_add = a.row_add;
-  p.pad = a.pad;
   p.epi = a.epi;
   p.alpha = a.alpha;
   p.inv = a.inv;
-  p.out2 = a.out2;
+  p.has_out2 = a.out2 != nullptr;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  e = launch_k(k_tconv<BN>, dim3(grid), dim3(320), C::SMEM, st, ma, mw, p);
+  e = launch_k(k_tconv<BN>, dim3(grid), dim3(320), C::SMEM, st, ma, mw, mo, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -286,9 +359,13 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
 
 int launch_tconv(const TConvArgs& a, cudaStream_t st) {
   if (!a.A || !a.W || !a.bias || !a.out || !a.pad || a.M <= 0 || a.M % kTBM || a.Cin <= 0 || a.Cin % kTBK ||
-      a.taps < 1 || a.rows_a <= 0 || a.lda < a.Cin || a.lda % 4 || a.ldo % 4 || a.row_mul < 1 || a.row_add < 0 ||
-      (a.epi == TCONV_SNAKE && (!a.alpha || !a.inv)) || (a.out2 && (!a.alpha || !a.inv)) ||
-      (reinterpret_cast<uintptr_t>(a.out) & 15) || (reinterpret_cast<uintptr_t>(a.bias) & 15))
+      a.taps < 1 || a.rows_a <= 0 || a.lda < a.Cin * (a.split_in ? 2 : 1) || a.lda % 4 || a.ldo % 4 ||
+      a.ldo < (long long)a.N * (a.split_out ? 2 : 1) || a.row_mul < 1 || a.row_add < 0 || a.row_add >= a.row_mul ||
+      a.epi < TCONV_BIAS || a.epi > TCONV_ELU || (a.epi == TCONV_SNAKE && (!a.alpha || !a.inv)) ||
+      (a.out2 && (a.epi != TCONV_RESID || !a.alpha || !a.inv)) ||
+      (a.split_out && (a.epi == TCONV_RESID || a.epi == TCONV_SNAKE)) ||
+      (reinterpret_cast<uintptr_t>(a.out) & 15) || (a.out2 && (reinterpret_cast<uintptr_t>(a.out2) & 15)) ||
+      (reinterpret_cast<uintptr_t>(a.bias) & 15))
     return T2W_ERR_INVALID;
   if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms()) return launch_impl<256>(a, st);
   if (a.N % 128 == 0) return launch_impl<128>(a, st);

@@ -109,3 +109,57 @@ def test_vocode_rejects_bad_calls():
         voc.vocode([h], [torch.zeros(cfg.mel, 5)], [False])
     with pytest.raises(L.T2WError):  # the same stream twice
         voc.vocode([h, h], [torch.zeros(cfg.mel, 20)] * 2, [False, False])
+
+
+def test_seeded_noise_matches_reference_draws():
+    """Without ``noise=`` every window's source noise is the reference's ``hift_noise`` on the vocoder's device: a CUDA
+    generator seeded with the chunk seed, ``rand(1, dim)`` then ``randn(1, dim, 480 F)`` (engine/models/token2wav.py:
+    112-121).  The same windows vocoded with those draws passed explicitly give bit-identical samples."""
+    cfg = HIFT_TINY
+    hift = ho.build_hift(cfg, seed=0)
+    dim = cfg.harmonics + 1
+    a = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=64, n_streams=4)
+    b = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=64, n_streams=4)
+    seeds = [7, 123456789, 2 ** 40 + 3]
+    ha = [a.new_stream(s) for s in seeds]
+    hb = [b.new_stream(s) for s in seeds]
+    g = torch.Generator().manual_seed(9)
+    for c, (Ts, lasts) in enumerate((([50, 20, 50], [False, False, True]), ([50, 50], [False, True]))):
+        n = len(Ts)
+        mels = [torch.randn(cfg.mel, T, generator=g) - 2.0 for T in Ts]
+        noise = []
+        for i in range(n):
+            F = Ts[i] + (8 if c else 0)
+            gen = torch.Generator(device="cuda").manual_seed(chunk_noise_seed(seeds[i], c))
+            noise.append((torch.rand(1, dim, device="cuda", generator=gen),
+                          torch.randn(1, dim, 480 * F, device="cuda", generator=gen)))
+        oa = a.vocode(ha[:n], mels, lasts)
+        ob = b.vocode(hb[:n], mels, lasts, noise=noise)
+        for x, y in zip(oa, ob):
+            assert x.numel() == y.numel() and torch.equal(x, y)
+    a.close()
+    b.close()
+
+
+def test_tf32_mode_source_is_fp32_accurate():
+    """With ``tf32`` the f0 predictor runs on the tensor cores in split form (3xTF32), where the reference keeps fp32:
+    the harmonic source it drives (f0 -> phase -> sines) against the strict-fp32 build's, both windows of a stream (the
+    second with its cached mel frames).  The source integrates f0 into a phase of hundreds of radians per window, so
+    it magnifies f0 differences: the split layers' 1.2e-5 per layer (``tests/test_gpu_tconv.py``, against plain TF32's
+    8e-4) shows here as ~4e-4; bound 1e-3."""
+    cfg = HIFT
+    hift = ho.build_hift(cfg, seed=0)
+    vs = {t: B200HiFT.from_module(hift, cfg, device="cuda", max_frames=64, n_streams=4, tf32=t) for t in (False, True)}
+    hs = {t: [v.new_stream(s) for s in (3, 4)] for t, v in vs.items()}
+    g = torch.Generator().manual_seed(21)
+    for c in range(2):
+        mels = [torch.randn(cfg.mel, 50, generator=g) - 2.0 for _ in range(2)]
+        F = 50 + (8 if c else 0)
+        noise = [oracle_noise(hift, chunk_noise_seed(s, c), F) for s in (3, 4)]
+        src = {}
+        for t, v in vs.items():
+            src[t] = torch.empty(2 * 480 * F, device="cuda")
+            v.vocode(hs[t], mels, [False, False], noise=noise, source=src[t])
+        e = rel(src[True], src[False])
+        print(f"window {c}: source rel-L2 tf32 vs strict {e:.2e}")
+        assert e < 1e-3

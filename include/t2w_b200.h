@@ -556,9 +556,10 @@ T2W_API int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream);
  * layers), for numerics tests against a plain fp32 / fp64 convolution.
  *   out[row_mul m + row_add, n] = epi(bias[n] + sum_tap sum_c A[m + tap_row0 + tap dil, c] W[n, tap Cin + c]),
  * m < M (M % 128 == 0), A rows outside [0, rows_a) read as zero, rows with pad[row_mul m + row_add] != 0 written as zero
- * (epi 0 bias, 1 Snake with alpha / inv, 3 ELU) or left as they are (2: out += ..., and Snake(out) into out2 when
- * out2 != NULL).  Cin % 32 == 0; N % 128 == 0, 64 or 32.  split_in: A rows are [hi | lo] (2 Cin floats) and W has
- * [W_hi | W_lo | W_hi] per tap (3 Cin columns); split_out: the output rows are written as [hi | lo] (2 N floats).
+ * (epi 0 bias, 1 Snake with alpha / inv, 3 ELU) or left as they are (2: out += ...); with epi 0 or 2 and out2 != NULL
+ * Snake(out) into out2 too.  Cin % 4 == 0, W [N, taps Cp] with Cp = Cin rounded up to 32 (the columns past Cin zero);
+ * N % 128 == 0, 64 or 32.  split_in (Cin % 32 == 0): A rows are [hi | lo] (2 Cin floats) and W has [W_hi | W_lo | W_hi]
+ * per tap (3 Cin columns); split_out: the output rows are written as [hi | lo] (2 N floats).
  * Asynchronous on `stream`; a bounded wait that gives up writes T2W_ERR_TIMEOUT into *err (device int). */
 typedef struct t2w_tconv_args {
   const float* A;

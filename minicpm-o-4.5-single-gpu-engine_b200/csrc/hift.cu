@@ -52,6 +52,7 @@ constexpr int kMelCache = 8;          // cached mel frames (engine/models/token2
 constexpr int kSrcCache = 3840;       // cached source / speech samples (8 frames x 480)
 constexpr int kPadMel = 4;            // zero rows on each side of a window's mel frames
 constexpr int kNfft = 16, kHop = 4, kBins = kNfft / 2 + 1;
+constexpr int kStftLd = 20;  // floats per STFT frame row: the 18 channels, 2 zero (rows of 80 bytes for tensor maps)
 
 // ---------------------------------------------------------------- generic fp32 convolution
 enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4, HE_LEAKY = 5, HE_ELU_SPLIT = 6 };
@@ -484,6 +485,10 @@ struct HStage {
   float* b = nullptr;
   HConv down;
   int down_stride = 1, down_pad = 0;
+  // source_down on the tensor cores: a 3-tap conv over the STFT rows grouped by the stride (space to depth, S frames of
+  // kStftLd floats per group row); weights [Cout][taps][roundup(S kStftLd, 32)]
+  float* down_tc = nullptr;
+  int down_taps = 0, down_q0 = 0;
   HRes src, res[3];
 };
 
@@ -600,6 +605,33 @@ int split_weights(t2w_hift* h, const HConv& cv, int n_pad, float** W, float** b)
   return b ? up(h, tb, b) : T2W_OK;
 }
 
+// source_down of stage s as a conv over the STFT rows grouped by its stride S.  The call layout puts stage s's output
+// row R (R = e.s_s + v, make_plan) over STFT row S R + delta + v-relative taps: e.s2 = S e.s_s - 1 for stages 0 and 1
+// (delta = -1), e.s2 = e.s_2 for stage 2 (delta = 0).  Output v reads frames S v + t - pad (t < k), i.e. rows
+// S R + d + t with d = delta - pad, which are group row R + q, frame j of it, for S q + j = d + t: taps q from
+// floor(d / S) to floor((d + k - 1) / S), weight [o][q - q0][j kStftLd + c] = W[o][c][S q + j - d].
+int grouped_down(t2w_hift* h, HStage& g, int s) {
+  const int S = g.down_stride, k = g.down.k, Cin = g.down.Cin, Cout = g.down.Cout;
+  const int d = (s == 2 ? 0 : -1) - g.down_pad;
+  auto fdiv = [](int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); };
+  const int q0 = fdiv(d, S), q1 = fdiv(d + k - 1, S), taps = q1 - q0 + 1;
+  const int cg = S * kStftLd, cp = (cg + 31) / 32 * 32;
+  std::vector<float> w;
+  H_TRY(down(g.down.W, (size_t)Cout * k * Cin, w));  // [o][t][c]
+  std::vector<float> t((size_t)Cout * taps * cp, 0.f);
+  for (int o = 0; o < Cout; ++o)
+    for (int qi = 0; qi < taps; ++qi)
+      for (int j = 0; j < S; ++j) {
+        const int tap = S * (q0 + qi) + j - d;
+        if (tap < 0 || tap >= k) continue;
+        for (int c = 0; c < Cin; ++c)
+          t[((size_t)o * taps + qi) * cp + j * kStftLd + c] = w[((size_t)o * k + tap) * Cin + c];
+      }
+  g.down_taps = taps;
+  g.down_q0 = q0;
+  return up(h, t, &g.down_tc);
+}
+
 int snake_params(t2w_hift* h, const float* const* a, int C, float** al, float** inv) {
   std::vector<float> va((size_t)3 * C), vi((size_t)3 * C);
   for (int d = 0; d < 3; ++d) {
@@ -689,6 +721,7 @@ int create_impl(t2w_hift* h, const float* const* W) {
     const float* wt = next();
     const float* bt = next();
     H_TRY(conv(h, wt, bt, g.Cout, kNfft + 2, k, &g.down));
+    if (h->tf32) H_TRY(grouped_down(h, g, s));
     HRes& r = g.src;
     r.k = c.source_kernels[s];
     const float* a1[3];
@@ -1012,7 +1045,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   const size_t o_f0a = add((size_t)pl.A[0] * c.f0_channels * 8), o_f0b = add((size_t)pl.A[0] * c.f0_channels * 8);
   const size_t o_f0 = add((size_t)pl.A[0] * 4);
   const size_t o_src = add((size_t)pl.samples * 4), o_sp = add((size_t)pl.samples * 4);
-  const size_t o_stft = add((size_t)pl.A[3] * (kNfft + 2) * 4);
+  const size_t o_stft = add((size_t)pl.A[3] * kStftLd * 4);
   const size_t o_x0 = add((size_t)pl.A[0] * C0 * 4);
   // per stage: x (ups output), xr[3] ResBlock streams, ar[3] / sd scratch of the stage's size
   size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3];
@@ -1088,11 +1121,15 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     zero(o_mel, (size_t)pl.A[0] * c.mel * 4);
     if (h->f0_tc) zero(o_f0a, (size_t)pl.A[0] * c.f0_channels * 8);
     zero(o_x0, (size_t)pl.A[0] * C0 * 4);
-    for (int s = 0; s < 3; ++s) {
-      const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
-      zero(o_sd[s], sz);
-      zero(o_ta[s], sz);
-      if (!h->tf32) zero(o_xs[s], sz);
+    if (h->tf32) {
+      zero(o_stft, (size_t)pl.A[3] * kStftLd * 4);  // the source_down tensor maps read padding rows and channels
+    } else {
+      for (int s = 0; s < 3; ++s) {
+        const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
+        zero(o_sd[s], sz);
+        zero(o_ta[s], sz);
+        zero(o_xs[s], sz);
+      }
     }
     if (e1 != cudaSuccess) {
       set_cuda_error(e1);
@@ -1197,7 +1234,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      (const float*)h->cache, h->cache_ld, kMelCache * c.mel, src));
     if (rc) return fail(rc);
     dim3 grid((120 * h->max_frames + 1 + 127) / 128, n);
-    rc = ck(launch_k(k_stft, grid, dim3(128), 0, st, (const float*)src, drows, (const float*)h->tw, stft, kNfft + 2, 480.f));
+    rc = ck(launch_k(k_stft, grid, dim3(128), 0, st, (const float*)src, drows, (const float*)h->tw, stft, kStftLd, 480.f));
     if (rc) return fail(rc);
   }
   // 5. conv_pre
@@ -1260,9 +1297,32 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     // source branch: strided conv of the STFT, then its ResBlock (in place)
     float* sd = reinterpret_cast<float*>(P(o_sd[s]));
     float* ta = reinterpret_cast<float*>(P(o_ta[s]));
-    {
+    if (h->tf32) {  // TF32 (the source branch is part of the reference's decode_tf32 stages)
+      const int S = g.down_stride;
+      TConvArgs t;
+      t.A = stft;  // viewed as rows of S frames
+      t.lda = S * kStftLd;
+      t.rows_a = pl.A[3] / S;
+      t.W = g.down_tc;
+      t.bias = g.down.b;
+      t.M = pl.A[s + 1];
+      t.N = Cs;
+      t.Cin = S * kStftLd;
+      t.taps = g.down_taps;
+      t.tap_row0 = g.down_q0;
+      t.out = sd;
+      t.ldo = Cs;
+      t.pad = reinterpret_cast<const uint8_t*>(P(o_pad[s + 1]));
+      t.alpha = g.src.a1;  // the source ResBlock's first Snake of the branch, written beside it
+      t.inv = g.src.i1;
+      t.out2 = ta;
+      t.err = h->err;
+      rc = launch_tconv(t, st);
+      if (rc) return fail(rc);
+    } else {
       ConvGeo cg = geo(g.down, vs, pl.vs_s[s][n], reinterpret_cast<const int*>(P(o_ss[2])),
                        reinterpret_cast<const int*>(P(o_ls[2])), ss, stft, sd, HE_NONE);
+      cg.ld_in = kStftLd;
       cg.stride = g.down_stride;
       cg.off = -g.down_pad;
       cg.alpha = g.src.a1;  // the source ResBlock's first Snake of the branch, written beside it

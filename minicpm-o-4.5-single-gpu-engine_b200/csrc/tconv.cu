@@ -148,7 +148,8 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
   tc_fence_after();
   pdl_launch();
   const uint32_t tmem = *tmem_slot;
-  const int kb_per_seg = p.Cin / kTBK;
+  const int kb_per_seg = (p.Cin + kTBK - 1) / kTBK;  // channels past Cin in the last block read as zero
+  const int cpad = kb_per_seg * kTBK;                  // W's columns per (tap, segment)
   const int segs = p.split_in ? 3 : 1;
   const int kb_per_tap = kb_per_seg * segs;
   const int num_kb = kb_per_tap * p.taps;
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           const int kk = (r - seg * kb_per_seg) * kTBK;
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, (seg == 2 ? p.Cin : 0) + kk, m0 + p.tap_row0 + tap * p.dil,
                       &full[stage]);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmW, (tap * segs + seg) * p.Cin + kk, n0, &full[stage]);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmW, (tap * segs + seg) * cpad + kk, n0, &full[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -280,10 +281,16 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 y = make_float4(0.f, 0.f, 0.f, 0.f), z = y;
             if (live) {
               const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
               y = make_float4(v[4 * j] + bb.x, v[4 * j + 1] + bb.y, v[4 * j + 2] + bb.z, v[4 * j + 3] + bb.w);
+              if (p.has_out2) {  // bias epilogue: the next ResBlock's first Snake of the output beside it
+                const float4 a = __ldg(reinterpret_cast<const float4*>(p.alpha + c0) + j);
+                const float4 iv = __ldg(reinterpret_cast<const float4*>(p.inv + c0) + j);
+                z = make_float4(snake_f(y.x, a.x, iv.x), snake_f(y.y, a.y, iv.y), snake_f(y.z, a.z, iv.z),
+                                snake_f(y.w, a.w, iv.w));
+              }
               if (p.epi == TCONV_SNAKE) {
                 const float4 a = __ldg(reinterpret_cast<const float4*>(p.alpha + c0) + j);
                 const float4 iv = __ldg(reinterpret_cast<const float4*>(p.inv + c0) + j);
@@ -301,6 +308,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
               y = hi;
             }
             reinterpret_cast<float4*>(dst)[j] = y;
+            if (p.has_out2) reinterpret_cast<float4*>(p.out2 + orow * p.ldo + c0)[j] = z;
           }
         }
       }
@@ -327,10 +335,10 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   const uint64_t out_cols = (uint64_t)a.N * (a.split_out ? 2 : 1);
   const uint64_t out_pitch = (uint64_t)a.row_mul * a.ldo * 4;
   CUtensorMap ma, mw, mo;
+  const uint64_t cpad = (uint64_t)(a.Cin + kTBK - 1) / kTBK * kTBK;
   if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin * (a.split_in ? 2 : 1), (uint64_t)a.lda * 4, kTBM,
                     kTBK) ||
-      !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, (uint64_t)a.Cin * a.taps * segs, (uint64_t)a.Cin * a.taps * segs * 4,
-                    BN, kTBK) ||
+      !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, cpad * a.taps * segs, cpad * a.taps * segs * 4, BN, kTBK) ||
       !make_tmap_2d(&mo, a.out + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M, out_cols, out_pitch, 32, 32))
     return T2W_ERR_INVALID;
   TDev p;
@@ -368,11 +376,12 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
 }  // namespace
 
 int launch_tconv(const TConvArgs& a, cudaStream_t st) {
-  if (!a.A || !a.W || !a.bias || !a.out || !a.pad || a.M <= 0 || a.M % kTBM || a.Cin <= 0 || a.Cin % kTBK ||
+  if (!a.A || !a.W || !a.bias || !a.out || !a.pad || a.M <= 0 || a.M % kTBM || a.Cin <= 0 || a.Cin % 4 ||
+      (a.split_in && a.Cin % kTBK) ||
       a.taps < 1 || a.rows_a <= 0 || a.lda < a.Cin * (a.split_in ? 2 : 1) || a.lda % 4 || a.ldo % 4 ||
       a.ldo < (long long)a.N * (a.split_out ? 2 : 1) || a.row_mul < 1 || a.row_add < 0 || a.row_add >= a.row_mul ||
       a.epi < TCONV_BIAS || a.epi > TCONV_ELU || (a.epi == TCONV_SNAKE && (!a.alpha || !a.inv)) ||
-      (a.out2 && (a.epi != TCONV_RESID || !a.alpha || !a.inv)) ||
+      (a.out2 && ((a.epi != TCONV_RESID && a.epi != TCONV_BIAS) || a.split_out || !a.alpha || !a.inv)) ||
       (a.split_out && (a.epi == TCONV_RESID || a.epi == TCONV_SNAKE)) ||
       (reinterpret_cast<uintptr_t>(a.out) & 15) || (a.out2 && (reinterpret_cast<uintptr_t>(a.out2) & 15)) ||
       (reinterpret_cast<uintptr_t>(a.bias) & 15))

@@ -9,11 +9,12 @@ namespace t2w {
 enum { TCONV_BIAS = 0, TCONV_SNAKE = 1, TCONV_RESID = 2, TCONV_ELU = 3 };
 
 // out[row_mul m + row_add, n] (ldo floats per row) = epilogue(bias[n] + sum_tap sum_c A[m + tap_row0 + tap dil, c]
-// W[n, tap Cin + c]) for m < M (M % 128 == 0), rows whose pad[row_mul m + row_add] != 0 zero (bias, snake, elu) or
-// untouched (resid).  A fp32 [rows_a, lda] (rows outside [0, rows_a) read as zero), W fp32 [N, taps Cin], Cin % 32 == 0,
-// N a multiple of 128, or 64, or 32.
+// W[n, tap Cp + c]) for m < M (M % 128 == 0), rows whose pad[row_mul m + row_add] != 0 zero (bias, snake, elu) or
+// untouched (resid).  A fp32 [rows_a, lda] (rows outside [0, rows_a) read as zero), Cin % 4 == 0, W fp32 [N, taps Cp]
+// with Cp = Cin rounded up to 32 (the columns past Cin of each tap zero), N a multiple of 128, or 64, or 32.  out2 with
+// the bias or resid epilogue: Snake(out) (alpha / inv) into out2 as well.
 //
-// split_in (3xTF32, fp32-level accuracy): A holds [hi | lo] (2 Cin floats per row: hi = a rounded to TF32, lo = a - hi
+// split_in (3xTF32, fp32-level accuracy; Cin % 32 == 0): A holds [hi | lo] (2 Cin floats per row: hi = a rounded to TF32, lo = a - hi
 // rounded to TF32) and W per tap [W_hi | W_lo | W_hi] (3 Cin columns per tap), so the sum is
 // hi W_hi + hi W_lo + lo W_hi.  split_out: the epilogue writes the output in that [hi | lo] form (2 N columns; bias /
 // elu only).
@@ -28,7 +29,7 @@ struct TConvArgs {
   int row_mul = 1, row_add = 0;
   const uint8_t* pad = nullptr;
   int epi = TCONV_BIAS;
-  const float* alpha = nullptr;  // TCONV_SNAKE: this conv's Snake; TCONV_RESID with out2: the next Snake
+  const float* alpha = nullptr;  // TCONV_SNAKE: this conv's Snake; with out2: the next Snake
   const float* inv = nullptr;
   float* out2 = nullptr;
   int split_in = 0, split_out = 0;

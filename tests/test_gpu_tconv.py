@@ -170,7 +170,7 @@ def test_rejects_bad_shapes():
     out = torch.zeros(M, N, device="cuda")
     lib = L.load()
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    for kw in ({"M": 200}, {"Cin": 48}, {"N": 96}, {"ldo": 32}, {"row_add": 1}):
+    for kw in ({"M": 200}, {"Cin": 50}, {"N": 96}, {"ldo": 32}, {"row_add": 1}):
         p = dict(M=M, N=N, Cin=Cin, ldo=N, row_add=0)
         p.update(kw)
         args = L.TConvArgs(ctypes.c_void_p(a.data_ptr()), Cin, M, ctypes.c_void_p(w.data_ptr()),
@@ -178,3 +178,28 @@ def test_rejects_bad_shapes():
                            ctypes.c_void_p(out.data_ptr()), p["ldo"], 1, p["row_add"], ctypes.c_void_p(pad.data_ptr()),
                            BIAS, None, None, None, 0, 0, None)
         assert lib.t2w_test_tconv(ctypes.byref(args), st) == -1, kw
+
+
+@pytest.mark.parametrize("cin", [20, 60, 300])
+def test_narrow_input_bias_with_next_snake(cin):
+    """Inputs whose channel count is not a multiple of 32 (the STFT rows grouped by the source_down strides: 20, 3 x 20,
+    15 x 20 floats), W padded per tap to a multiple of 32 columns; bias epilogue with Snake(out) into out2."""
+    M, N, taps = 2048, 128, 3
+    cp = (cin + 31) // 32 * 32
+    a, w, b, pad = case(M, N, cin, taps, 1, seed=50 + cin)
+    wp = torch.zeros(N, taps, cp, device="cuda")
+    wp[:, :, :cin] = w.view(N, taps, cin)
+    g = torch.Generator(device="cuda").manual_seed(51)
+    alpha = torch.rand(N, device="cuda", generator=g) + 0.5
+    inv = 1.0 / (alpha + 1e-9)
+    out = torch.full((M, N), 4.0, device="cuda")
+    out2 = torch.full((M, N), 4.0, device="cuda")
+    run(a, cin, M, wp.reshape(N, taps * cp).contiguous(), b, M, N, cin, taps, -1, 1, out, N, pad, alpha=alpha, inv=inv,
+        out2=out2)
+    ref = conv_ref(a, w, b, M, taps, -1, 1)
+    ref[pad.bool()] = 0
+    s = snake(ref, alpha.double(), inv.double())
+    e1, e2 = rel(out, ref), rel(out2, s)
+    print(f"Cin={cin}: out rel-L2 {e1:.2e}, out2 rel-L2 {e2:.2e}")
+    assert e1 < 3e-3 and e2 < 3e-3
+    assert torch.all(out[pad.bool()] == 0) and torch.all(out2[pad.bool()] == 0)

@@ -577,6 +577,7 @@ typedef struct t2w_tconv_args {
   float* out2;
   int32_t split_in, split_out;
   int32_t* err;
+  const float* resid_in; /* epi 2: out = resid_in + ... (padding rows copied from resid_in); NULL: out in place */
 } t2w_tconv_args;
 T2W_API int t2w_test_tconv(const t2w_tconv_args* a, void* stream);
 

@@ -118,7 +118,8 @@ class TConvArgs(ctypes.Structure):
                [("out", ctypes.c_void_p), ("ldo", ctypes.c_int64), ("row_mul", ctypes.c_int32),
                 ("row_add", ctypes.c_int32), ("pad", ctypes.c_void_p), ("epi", ctypes.c_int32),
                 ("alpha", ctypes.c_void_p), ("inv", ctypes.c_void_p), ("out2", ctypes.c_void_p),
-                ("split_in", ctypes.c_int32), ("split_out", ctypes.c_int32), ("err", ctypes.c_void_p)]
+                ("split_in", ctypes.c_int32), ("split_out", ctypes.c_int32), ("err", ctypes.c_void_p),
+                ("resid_in", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p

@@ -75,6 +75,7 @@ struct ConvGeo {
   const float* alpha = nullptr;  // HE_SNAKE: this conv's Snake; HE_RESID: the next Snake (out2), per channel
   const float* inv = nullptr;    // 1 / (alpha + 1e-9)
   float* out2 = nullptr;         // HE_RESID / HE_NONE: Snake of the output for the next conv (nullptr: none)
+  const float* resid = nullptr;  // HE_RESID: the residual's buffer (same layout as out; nullptr: out itself)
   float slope = 0.f;             // HE_LEAKY
 };
 
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(256) k_hconv(const ConvGeo g) {
         case HE_SNAKE: y = snake(y, g.alpha[co], g.inv[co]); break;
         case HE_LEAKY: y = y > 0.f ? y : y * g.slope; break;
         case HE_RESID: {
-          y = y + *dst;
+          y = y + (g.resid ? g.resid[orow * g.ld_out + co] : *dst);
           if (g.out2) g.out2[orow * g.ld_out + co] = snake(y, g.alpha[co], g.inv[co]);
           break;
         }
@@ -230,16 +231,16 @@ __global__ void k_mel_in(const float* __restrict__ win_mel, const HRow* __restri
 struct Snake3 {
   const float *al[3], *inv[3];
 };
-__global__ void k_fanout(const float* __restrict__ x, const float* __restrict__ src, long long n, int C, float* x0,
-                         float* x1, float* x2, float* a0, float* a1, float* a2, const Snake3 sn) {
+// xb = ups(x) + source branch (every row), the three ResBlocks' first Snakes of it; each ResBlock's first residual
+// update reads xb and writes its own stream, so xb is not copied three times.
+__global__ void k_fanout(const float* x, const float* __restrict__ src, long long n, int C, float* xb,
+                         float* a0, float* a1, float* a2, const Snake3 sn) {
   pdl_wait();
   pdl_launch();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int c = (int)(i % C);
     const float v = x[i] + src[i];
-    x0[i] = v;
-    x1[i] = v;
-    x2[i] = v;
+    xb[i] = v;
     a0[i] = snake(v, sn.al[0][c], sn.inv[0][c]);
     a1[i] = snake(v, sn.al[1][c], sn.inv[1][c]);
     a2[i] = snake(v, sn.al[2][c], sn.inv[2][c]);
@@ -290,9 +291,11 @@ __global__ void k_reflect_row(float* __restrict__ x, const HRow* __restrict__ ro
 // The harmonic source, per window: rad of frame k and harmonic h = frac(f0_k (h + 1) / sr); its cumulative phase over
 // frames (2 pi sum), interpolated linearly to samples after the x upsample_scale product (the reference's
 // F.interpolate(... * upsample_scale, scale_factor=upsample_scale, mode="linear")); the sine, voiced / unvoiced noise
-// mix, linear over harmonics, tanh.  One block per window: the frame phases in shared memory.
+// mix, linear over harmonics, tanh.  Grid (sample chunks of kSrcChunk, windows): every block of a window rebuilds the
+// window's frame phases in shared memory (F sequential steps per harmonic) and writes its chunk of samples.
 constexpr int kMaxFrames = 512;
 constexpr int kMaxHarm = 16;
+constexpr int kSrcChunk = 1024;
 __global__ void __launch_bounds__(256) k_source(const float* __restrict__ f0, const HRow* __restrict__ rows,
                                                const float* __restrict__ noise, const float* __restrict__ lin_w,
                                                float lin_b, int dim, float sr, float upscale, float sine_amp,
@@ -302,8 +305,17 @@ __global__ void __launch_bounds__(256) k_source(const float* __restrict__ f0, co
   __shared__ float f0s[kMaxFrames];
   pdl_wait();
   pdl_launch();
-  const HRow e = rows[blockIdx.x];
+  const HRow e = rows[blockIdx.y];
   const int F = e.F;
+  const int N = F * (int)upscale;
+  const int n0 = blockIdx.x * kSrcChunk;
+  if (n0 >= N) return;
+  const bool cached = !e.first;
+  if (cached && n0 + kSrcChunk <= kSrcCache) {  // the whole chunk comes from the cached source tail
+    for (int n = n0 + threadIdx.x; n < n0 + kSrcChunk; n += blockDim.x)
+      src[e.smp0 + n] = cache[(size_t)e.cache * cache_ld + cache_src_off + n];
+    return;
+  }
   for (int t = threadIdx.x; t < F; t += blockDim.x) f0s[t] = f0[e.mel0 + t];
   __syncthreads();
   // cumulative phase per harmonic (sequential over frames, one thread per harmonic)
@@ -318,10 +330,9 @@ __global__ void __launch_bounds__(256) k_source(const float* __restrict__ f0, co
     }
   }
   __syncthreads();
-  const int N = F * (int)upscale;
   const float scale = 1.f / upscale;
-  const bool cached = !e.first;
-  for (int n = threadIdx.x; n < N; n += blockDim.x) {
+  const int n1 = min(N, n0 + kSrcChunk);
+  for (int n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
     float out;
     if (cached && n < kSrcCache) {
       out = cache[(size_t)e.cache * cache_ld + cache_src_off + n];
@@ -1229,7 +1240,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   float* src = reinterpret_cast<float*>(P(o_src));
   float* stft = reinterpret_cast<float*>(P(o_stft));
   {
-    rc = ck(launch_k(k_source, dim3(n), dim3(256), 0, st, (const float*)P(o_f0), drows, b->noise, (const float*)h->lin_w,
+    const dim3 sgrid((480 * h->max_frames + kSrcChunk - 1) / kSrcChunk, n);
+    rc = ck(launch_k(k_source, sgrid, dim3(256), 0, st, (const float*)P(o_f0), drows, b->noise, (const float*)h->lin_w,
                      h->lin_b, c.harmonics + 1, (float)c.sample_rate, 480.f, c.nsf_alpha, c.nsf_sigma, c.voiced_threshold,
                      (const float*)h->cache, h->cache_ld, kMelCache * c.mel, src));
     if (rc) return fail(rc);
@@ -1332,8 +1344,9 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       if (rc) return fail(rc);
     }
     const long long nel = (long long)pl.A[s + 1] * Cs;
-    auto resblock = [&](HRes& r, float* xr, float* a_in, float* tmp) -> int {
-      // a_in holds Snake1_0(xr); per dilation: tmp = Snake2(conv1(a_in)); xr += conv2(tmp), a_in = Snake1_next(xr)
+    auto resblock = [&](HRes& r, float* xr, float* a_in, float* tmp, const float* base) -> int {
+      // a_in holds Snake1_0(x); per dilation: tmp = Snake2(conv1(a_in)); xr = x + conv2(tmp), a_in = Snake1_next(xr),
+      // x = base for the first dilation when given (xr written out of place), else xr itself
       for (int dd = 0; dd < 3; ++dd) {
         const int dl = h->cfg.dilations[dd];
         if (h->tf32) {
@@ -1364,6 +1377,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
           t2.bias = r.c2[dd].b;
           t2.tap_row0 = -(r.k - 1) / 2;
           t2.out = xr;
+          if (dd == 0) t2.resid_in = base;
           t2.epi = TCONV_RESID;
           if (dd < 2) {
             t2.alpha = r.a1 + (dd + 1) * Cs;
@@ -1381,6 +1395,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
         H_TRY(run(c1));
         ConvGeo c2 = geo(r.c2[dd], vs, pl.vs_s[s][n], ss, ls, ss, tmp, xr, HE_RESID);
         c2.off = -(r.k - 1) / 2;
+        if (dd == 0) c2.resid = base;
         if (dd < 2) {
           c2.alpha = r.a1 + (dd + 1) * Cs;
           c2.inv = r.i1 + (dd + 1) * Cs;
@@ -1390,23 +1405,23 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       }
       return T2W_OK;
     };
-    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])));  // xr[0] as scratch before the fan-out
+    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])), nullptr);  // xr[0]: scratch before the fan-out
     if (rc) return fail(rc);
     float* xr[3] = {reinterpret_cast<float*>(P(o_xr[s][0])), reinterpret_cast<float*>(P(o_xr[s][1])),
                     reinterpret_cast<float*>(P(o_xr[s][2]))};
     float* ar[3] = {reinterpret_cast<float*>(P(o_ar[s][0])), reinterpret_cast<float*>(P(o_ar[s][1])),
                     reinterpret_cast<float*>(P(o_ar[s][2]))};
-    // x_j = ups(x) + source branch for the three ResBlocks, with each block's first Snake of it
+    // xs += source branch (the three ResBlocks' common input, in place), with each block's first Snake of it
     Snake3 sn;
     for (int j = 0; j < 3; ++j) {
       sn.al[j] = g.res[j].a1;
       sn.inv[j] = g.res[j].i1;
     }
-    rc = ck(launch_k(k_fanout, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs, xr[0],
-                     xr[1], xr[2], ar[0], ar[1], ar[2], sn));
+    rc = ck(launch_k(k_fanout, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs, xs,
+                     ar[0], ar[1], ar[2], sn));
     if (rc) return fail(rc);
     for (int j = 0; j < 3; ++j) {
-      rc = resblock(g.res[j], xr[j], ar[j], ta);
+      rc = resblock(g.res[j], xr[j], ar[j], ta, xs);
       if (rc) return fail(rc);
     }
     // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before
@@ -1497,6 +1512,7 @@ int t2w_test_tconv(const t2w_tconv_args* a, void* stream) {
   t.split_in = a->split_in;
   t.split_out = a->split_out;
   t.err = a->err;
+  t.resid_in = a->resid_in;
   return launch_tconv(t, static_cast<cudaStream_t>(stream));
 }
 

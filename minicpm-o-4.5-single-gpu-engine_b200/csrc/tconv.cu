@@ -14,7 +14,8 @@
 // warps 2-9 the epilogue (TMEM lane quarter w % 4, alternate 32-column chunks), the accumulator double-buffered in TMEM
 // so a tile's epilogue overlaps the next tile's MMAs.  Each epilogue thread owns one output row (the TMEM lane it
 // reads) and stores its 32-column chunk directly; a residual update first TMA-loads the warp's 32 x 32 block of the
-// residual into a swizzled shared-memory box (issued before the accumulator is ready) and reads its row from there,
+// residual (out itself, or another buffer of the same layout) into a swizzled shared-memory box (issued before the
+// accumulator is ready) and reads its row from there,
 // instead of 32 scattered row reads per warp.  (Staging the outputs through the box and writing them with TMA stores
 // measured slower for the bias and Snake epilogues.)
 // Output rows: row_mul * m + row_add (a transposed convolution's output phase writes every row_mul-th row of the next
@@ -59,6 +60,7 @@ struct TDev {
   const float* bias;
   float* out;
   float* out2;
+  int resid_oop;  // the residual is read from another buffer than out
   const uint8_t* pad;
   long long ldo;  // floats between consecutive output rows of the layout (row_mul * m + row_add indexes them)
   int row_mul, row_add;
@@ -109,7 +111,7 @@ __device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__fl
 template <int BN>
 __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
                                                   const __grid_constant__ CUtensorMap tmW,
-                                                  const __grid_constant__ CUtensorMap tmO, const TDev p) {
+                                                  const __grid_constant__ CUtensorMap tmR, const TDev p) {
   using C = TCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
-    tma_prefetch_desc(&tmO);
+    tma_prefetch_desc(&tmR);
   }
   pdl_wait();
   if (warp == 1) {
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
     auto load_resid = [&](int c0, int r0) {
       if (lane == 0) {
         mbar_expect_tx(eb, kEBox);
-        tma_load_2d(box, &tmO, c0, r0, eb);
+        tma_load_2d(box, &tmR, c0, r0, eb);
       }
       pending = true;
     };
@@ -261,8 +263,12 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           pending = false;
           if (!ok) break;
           float* dst2 = p.has_out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
+          if (!live && p.resid_oop) {  // a padding row of an out-of-place update: the residual's (zero) row
 #pragma unroll
-          for (int j = 0; j < 8 && live; ++j) {  // padding rows keep their (zero) values
+            for (int j = 0; j < 8; ++j) reinterpret_cast<float4*>(dst)[j] = *box_chunk(box, lane, j);
+          }
+#pragma unroll
+          for (int j = 0; j < 8 && live; ++j) {  // padding rows of an in-place update keep their (zero) values
             const float4 x = *box_chunk(box, lane, j);
             const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
             const float4 y = make_float4(x.x + (v[4 * j] + bb.x), x.y + (v[4 * j + 1] + bb.y),
@@ -334,12 +340,13 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   const int segs = a.split_in ? 3 : 1;
   const uint64_t out_cols = (uint64_t)a.N * (a.split_out ? 2 : 1);
   const uint64_t out_pitch = (uint64_t)a.row_mul * a.ldo * 4;
-  CUtensorMap ma, mw, mo;
+  CUtensorMap ma, mw, mr;
   const uint64_t cpad = (uint64_t)(a.Cin + kTBK - 1) / kTBK * kTBK;
   if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin * (a.split_in ? 2 : 1), (uint64_t)a.lda * 4, kTBM,
                     kTBK) ||
       !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, cpad * a.taps * segs, cpad * a.taps * segs * 4, BN, kTBK) ||
-      !make_tmap_2d(&mo, a.out + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M, out_cols, out_pitch, 32, 32))
+      !make_tmap_2d(&mr, (a.resid_in ? a.resid_in : a.out) + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M, out_cols,
+                    out_pitch, 32, 32))
     return T2W_ERR_INVALID;
   TDev p;
   p.M = a.M;
@@ -355,6 +362,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.bias = a.bias;
   p.out = a.out;
   p.out2 = a.out2;
+  p.resid_oop = a.resid_in != nullptr && a.resid_in != a.out;
   p.pad = a.pad;
   p.ldo = a.ldo;
   p.row_mul = a.row_mul;
@@ -365,7 +373,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.has_out2 = a.out2 != nullptr;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  e = launch_k(k_tconv<BN>, dim3(grid), dim3(320), C::SMEM, st, ma, mw, mo, p);
+  e = launch_k(k_tconv<BN>, dim3(grid), dim3(320), C::SMEM, st, ma, mw, mr, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -384,6 +392,7 @@ int launch_tconv(const TConvArgs& a, cudaStream_t st) {
       (a.out2 && ((a.epi != TCONV_RESID && a.epi != TCONV_BIAS) || a.split_out || !a.alpha || !a.inv)) ||
       (a.split_out && (a.epi == TCONV_RESID || a.epi == TCONV_SNAKE)) ||
       (reinterpret_cast<uintptr_t>(a.out) & 15) || (a.out2 && (reinterpret_cast<uintptr_t>(a.out2) & 15)) ||
+      (a.resid_in && (a.epi != TCONV_RESID || (reinterpret_cast<uintptr_t>(a.resid_in) & 15))) ||
       (reinterpret_cast<uintptr_t>(a.bias) & 15))
     return T2W_ERR_INVALID;
   if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms()) return launch_impl<256>(a, st);

@@ -32,6 +32,7 @@ struct TConvArgs {
   const float* alpha = nullptr;  // TCONV_SNAKE: this conv's Snake; with out2: the next Snake
   const float* inv = nullptr;
   float* out2 = nullptr;
+  const float* resid_in = nullptr;  // TCONV_RESID: out = resid_in + bias + conv (padding rows copied), else out in place
   int split_in = 0, split_out = 0;
   int* err = nullptr;
 };

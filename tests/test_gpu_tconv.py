@@ -60,11 +60,12 @@ def snake(x, a, inv):
 
 
 def run(A, lda, rows_a, W, bias, M, N, Cin, taps, tap_row0, dil, out, ldo, pad, epi=BIAS, row_mul=1, row_add=0,
-        alpha=None, inv=None, out2=None, split_in=0, split_out=0):
+        alpha=None, inv=None, out2=None, split_in=0, split_out=0, resid_in=None):
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
     args = L.TConvArgs(ptr(A), lda, rows_a, ptr(W), ptr(bias), M, N, Cin, taps, tap_row0, dil, ptr(out), ldo, row_mul,
-                       row_add, ptr(pad), epi, ptr(alpha), ptr(inv), ptr(out2), split_in, split_out, ptr(err))
+                       row_add, ptr(pad), epi, ptr(alpha), ptr(inv), ptr(out2), split_in, split_out, ptr(err),
+                       ptr(resid_in))
     L.call("t2w_test_tconv", ctypes.byref(args), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -118,9 +119,12 @@ def test_snake_epilogue_transposed_phase():
     assert torch.all(out[0::3] == 5.0) and torch.all(out[2::3] == 5.0)
 
 
+@pytest.mark.parametrize("oop", [False, True], ids=["in_place", "out_of_place"])
 @pytest.mark.parametrize("N", [64, 256])
-def test_residual_epilogue_with_next_snake(N):
-    """out += bias + conv and out2 = Snake(out), padding rows of both untouched: conv2 of a ResBlock."""
+def test_residual_epilogue_with_next_snake(N, oop):
+    """out += bias + conv and out2 = Snake(out), padding rows of both untouched: conv2 of a ResBlock.  Out of place:
+    out = resid_in + bias + conv with resid_in's (zero) padding rows copied (a ResBlock's first update of the stage's
+    common input)."""
     M = 19200 if N == 256 else 4096
     Cin, taps, dil = N, 3, 1
     a, w, b, pad = case(M, N, Cin, taps, dil, seed=21 + N)
@@ -129,9 +133,10 @@ def test_residual_epilogue_with_next_snake(N):
     x0[pad.bool()] = 0
     alpha = torch.rand(N, device="cuda", generator=g) + 0.5
     inv = 1.0 / (alpha + 1e-9)
-    out = x0.clone()
+    out = torch.full((M, N), 6.0, device="cuda") if oop else x0.clone()
     out2 = torch.full((M, N), 3.0, device="cuda")
-    run(a, Cin, M, w, b, M, N, Cin, taps, -1, dil, out, N, pad, epi=RESID, alpha=alpha, inv=inv, out2=out2)
+    run(a, Cin, M, w, b, M, N, Cin, taps, -1, dil, out, N, pad, epi=RESID, alpha=alpha, inv=inv, out2=out2,
+        resid_in=x0 if oop else None)
     y = x0.double() + conv_ref(a, w, b, M, taps, -1, dil)
     y[pad.bool()] = 0
     s = snake(y, alpha.double(), inv.double())
@@ -176,7 +181,7 @@ def test_rejects_bad_shapes():
         args = L.TConvArgs(ctypes.c_void_p(a.data_ptr()), Cin, M, ctypes.c_void_p(w.data_ptr()),
                            ctypes.c_void_p(b.data_ptr()), p["M"], p["N"], p["Cin"], 1, 0, 1,
                            ctypes.c_void_p(out.data_ptr()), p["ldo"], 1, p["row_add"], ctypes.c_void_p(pad.data_ptr()),
-                           BIAS, None, None, None, 0, 0, None)
+                           BIAS, None, None, None, 0, 0, None, None)
         assert lib.t2w_test_tconv(ctypes.byref(args), st) == -1, kw
 
 

@@ -1085,7 +1085,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     if (sg.host) cudaFreeHost(sg.host);
     sg.host = nullptr;
     sg.cap = 0;
-    const size_t cap = std::max<size_t>(meta_bytes + meta_bytes / 4, 1 << 16);
+    const size_t cap = std::max<size_t>(2 * meta_bytes, 1 << 16);  // room for longer windows before it grows again
     se = cudaMallocHost(&sg.host, cap);
     if (se == cudaSuccess) sg.cap = cap;
   }

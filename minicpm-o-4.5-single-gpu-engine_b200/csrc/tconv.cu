@@ -54,9 +54,30 @@ struct TCfg {
   static_assert(SMEM <= kTMaxSmem, "shared memory");
 };
 
+// Tap-reuse form (taps > 1, (taps - 1) dil + 128 <= 256): one A box per 32-channel block covers every tap's rows
+// (128 + (taps - 1) dil of them) and each tap's MMAs read it from a row offset; W streams per (tap, block) through its
+// own ring.  A traffic per tile drops from taps x 128 rows to 128 + (taps - 1) dil rows per channel block.  The
+// operand descriptor of a tap simply starts tap x dil 128-byte rows into the box, with the matrix base offset field
+// left 0: the 128-byte swizzle the TMA wrote is a function of the absolute shared-memory address bits, and the MMA
+// reads it back from any row start (measured: every offset 1-12 rows exact; setting the field to the start's row
+// phase breaks every offset that is not a multiple of 8).
+constexpr int kUARows = 256;
+constexpr int kUABytes = kUARows * kTBK * 4;  // 32 KB
+constexpr int kUASlots = 2;
+template <int BN>
+struct TCfgU {
+  static constexpr int B_BYTES = BN * kTBK * 4;
+  static constexpr int WFIT = (kTMaxSmem - TCfg<BN>::FIXED - TCfg<BN>::EPI_BYTES - kUASlots * kUABytes) / B_BYTES;
+  static constexpr int WSTAGES = WFIT > 8 ? 8 : WFIT;
+  static constexpr int SMEM = kUASlots * kUABytes + WSTAGES * B_BYTES + TCfg<BN>::EPI_BYTES + TCfg<BN>::FIXED;
+  static_assert(WSTAGES >= 3, "stages");
+  static_assert(SMEM <= kTMaxSmem, "shared memory");
+};
+
 struct TDev {
   int M, N, Cin, taps, tap_row0, dil, tiles_n, num_tiles;
   int split_in, split_out;
+  int urows;  // tap-reuse form: rows of the A box (0: one 128-row A box per tap)
   const float* bias;
   float* out;
   float* out2;
@@ -108,27 +129,36 @@ __device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int c) {
 // bits cleared): a split x = hi + lo with hi = tf32_rn(x), lo = tf32_rn(x - hi) leaves |x - hi - lo| <= 2^-24 |x|.
 __device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
 
-template <int BN>
+template <int BN, bool UNION>
 __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
                                                   const __grid_constant__ CUtensorMap tmW,
                                                   const __grid_constant__ CUtensorMap tmR, const TDev p) {
   using C = TCfg<BN>;
+  using CU = TCfgU<BN>;
+  constexpr int NST = UNION ? CU::WSTAGES : C::STAGES;        // W (and, in the per-tap form, A) ring depth
+  constexpr int A_RING = UNION ? kUASlots * kUABytes : C::STAGES * C::A_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint8_t* sE = sB + C::STAGES * C::B_BYTES;
+  uint8_t* sB = smem + A_RING;
+  uint8_t* sE = sB + NST * C::B_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sE + C::EPI_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* empty = full + NST;
+  uint64_t* tfull = empty + NST;
   uint64_t* tempty = tfull + 2;
   uint64_t* ebar = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + kEpiWarps);
+  uint64_t* afull = ebar + kEpiWarps;  // tap-reuse form: the A slots
+  uint64_t* aempty = afull + kUASlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + kUASlots);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kUASlots; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -156,7 +186,73 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
   const int kb_per_tap = kb_per_seg * segs;
   const int num_kb = kb_per_tap * p.taps;
 
-  if (warp == 0) {
+  if (UNION && warp == 0) {
+    if (lane == 0) {
+      int stage = 0, as = 0;
+      uint32_t phase = 0, aph = 0;
+      bool ok = true;
+      const uint32_t abytes = (uint32_t)p.urows * kTBK * 4;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
+        for (int cb = 0; cb < kb_per_seg && ok; ++cb) {
+          if (!(ok = mbar_wait(&aempty[as], aph ^ 1u, p.err))) break;
+          mbar_expect_tx(&afull[as], abytes);
+          tma_load_2d(sA + as * kUABytes, &tmA, cb * kTBK, m0 + p.tap_row0, &afull[as]);
+          if (++as == kUASlots) {
+            as = 0;
+            aph ^= 1u;
+          }
+          for (int tap = 0; tap < p.taps; ++tap) {
+            if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
+            mbar_expect_tx(&full[stage], C::B_BYTES);
+            tma_load_2d(sB + stage * C::B_BYTES, &tmW, tap * cpad + cb * kTBK, n0, &full[stage]);
+            if (++stage == NST) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+    }
+  } else if (UNION && warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kTBM, BN);
+      int stage = 0, as = 0;
+      uint32_t phase = 0, aph = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        if (!(ok = mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1u, p.err))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int cb = 0; cb < kb_per_seg && ok; ++cb) {
+          if (!(ok = mbar_wait(&afull[as], aph, p.err))) break;
+          const uint32_t a_slot = smem_u32(sA + as * kUABytes);
+          for (int tap = 0; tap < p.taps; ++tap) {
+            if (!(ok = mbar_wait(&full[stage], phase, p.err))) break;
+            tc_fence_after();
+            const uint32_t a0 = a_slot + (uint32_t)(tap * p.dil) * 128u, b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+            for (int k = 0; k < kTBK / 8; ++k)
+              umma_tf32(d, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
+                        (cb | tap | k) != 0 ? 1u : 0u);
+            umma_commit(&empty[stage]);
+            if (++stage == NST) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          umma_commit(&aempty[as]);  // after the block's last MMA (commit tracks every MMA issued before it)
+          if (++as == kUASlots) {
+            as = 0;
+            aph ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -172,7 +268,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, (seg == 2 ? p.Cin : 0) + kk, m0 + p.tap_row0 + tap * p.dil,
                       &full[stage]);
           tma_load_2d(sB + stage * C::B_BYTES, &tmW, (tap * segs + seg) * cpad + kk, n0, &full[stage]);
-          if (++stage == C::STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
@@ -200,7 +296,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
             umma_tf32(d, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
                       (kb | k) != 0 ? 1u : 0u);
           umma_commit(&empty[stage]);
-          if (++stage == C::STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
@@ -328,11 +424,11 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
   }
 }
 
-template <int BN>
+template <int BN, bool UNION>
 int launch_impl(const TConvArgs& a, cudaStream_t st) {
-  using C = TCfg<BN>;
+  constexpr int SMEM = UNION ? TCfgU<BN>::SMEM : TCfg<BN>::SMEM;
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t e = smem_attr_once(k_tconv<BN>, C::SMEM, attr_done);
+  cudaError_t e = smem_attr_once(k_tconv<BN, UNION>, SMEM, attr_done);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -342,8 +438,9 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   const uint64_t out_pitch = (uint64_t)a.row_mul * a.ldo * 4;
   CUtensorMap ma, mw, mr;
   const uint64_t cpad = (uint64_t)(a.Cin + kTBK - 1) / kTBK * kTBK;
-  if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin * (a.split_in ? 2 : 1), (uint64_t)a.lda * 4, kTBM,
-                    kTBK) ||
+  const int urows = UNION ? ((a.taps - 1) * a.dil + kTBM + 7) / 8 * 8 : 0;  // every tap's rows of a 128-row tile
+  if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin * (a.split_in ? 2 : 1), (uint64_t)a.lda * 4,
+                    UNION ? urows : kTBM, kTBK) ||
       !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, cpad * a.taps * segs, cpad * a.taps * segs * 4, BN, kTBK) ||
       !make_tmap_2d(&mr, (a.resid_in ? a.resid_in : a.out) + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M, out_cols,
                     out_pitch, 32, 32))
@@ -359,6 +456,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.num_tiles = (a.M / kTBM) * p.tiles_n;
   p.split_in = a.split_in;
   p.split_out = a.split_out;
+  p.urows = urows;
   p.bias = a.bias;
   p.out = a.out;
   p.out2 = a.out2;
@@ -373,7 +471,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.has_out2 = a.out2 != nullptr;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  e = launch_k(k_tconv<BN>, dim3(grid), dim3(320), C::SMEM, st, ma, mw, mr, p);
+  e = launch_k(k_tconv<BN, UNION>, dim3(grid), dim3(320), SMEM, st, ma, mw, mr, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -395,10 +493,12 @@ int launch_tconv(const TConvArgs& a, cudaStream_t st) {
       (a.resid_in && (a.epi != TCONV_RESID || (reinterpret_cast<uintptr_t>(a.resid_in) & 15))) ||
       (reinterpret_cast<uintptr_t>(a.bias) & 15))
     return T2W_ERR_INVALID;
-  if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms()) return launch_impl<256>(a, st);
-  if (a.N % 128 == 0) return launch_impl<128>(a, st);
-  if (a.N == 64) return launch_impl<64>(a, st);
-  if (a.N == 32) return launch_impl<32>(a, st);
+  const bool u = !a.split_in && a.taps > 1 && (long long)(a.taps - 1) * a.dil + kTBM <= kUARows;
+  if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms())
+    return u ? launch_impl<256, true>(a, st) : launch_impl<256, false>(a, st);
+  if (a.N % 128 == 0) return u ? launch_impl<128, true>(a, st) : launch_impl<128, false>(a, st);
+  if (a.N == 64) return u ? launch_impl<64, true>(a, st) : launch_impl<64, false>(a, st);
+  if (a.N == 32) return u ? launch_impl<32, true>(a, st) : launch_impl<32, false>(a, st);
   return T2W_ERR_INVALID;
 }
 

@@ -510,6 +510,10 @@ typedef struct t2w_hift_config {
                  * source, conv_pre, source_downs and conv_post stay fp32 — the f0 layers after the first and
                  * conv_post on the tensor cores in split form (3xTF32: operands as pairs of TF32 values, hi + lo,
                  * fp32-level accuracy), the rest on CUDA cores */
+  uint32_t tf32_parts; /* with tf32 set: which parts run on TF32, bit 3 s + p for stage s (0-2) and part p (0 the
+                        * transposed conv, 1 the source branch, 2 the ResBlocks) — the reference's per-stage lists
+                        * (tf32_stages, token2wav.py:145-158); 0 means every part (tf32 = 1 alone); the parts left out
+                        * run in fp32 on CUDA cores */
 } t2w_hift_config;
 
 typedef struct t2w_hift t2w_hift;

@@ -26,6 +26,28 @@ def chunk_noise_seed(noise_seed: int, chunk: int) -> int:
     return (noise_seed * 1_000_003 + chunk) & ((1 << 63) - 1)
 
 
+PARTS = ("ups", "src", "res")  # a stage's transposed convolution, its source branch, its ResBlocks
+
+
+def tf32_parts(spec, stages: int = 3) -> int:
+    """The ``t2w_hift_config.tf32_parts`` mask (bit 3 s + p) of a ``decode_tf32`` value as the reference reads it
+    (``tf32_stages``, engine/models/token2wav.py:145-158): True for every part of every stage, False / None / empty for
+    none, else a list of stage indices (all parts of that stage) and ``"<stage>:<part>"`` entries, part one of
+    ``ups``, ``src``, ``res``."""
+    if spec is True:
+        return (1 << (3 * stages)) - 1
+    if not spec:
+        return 0
+    mask = 0
+    for e in spec:
+        i, _, part = str(e).partition(":")
+        if not 0 <= int(i) < stages or part not in ("",) + PARTS:
+            raise ValueError(f"tf32 entry {e!r}: a stage index < {stages} or '<stage>:<part>' with a part of {PARTS}")
+        for q in ((PARTS.index(part),) if part else range(3)):
+            mask |= 1 << (3 * int(i) + q)
+    return mask
+
+
 def hift_weight_names(cfg: HiFTConfig) -> list:
     """State-dict paths of a HiFTGenerator in the order ``t2w_hift_create`` takes them (include/t2w_b200.h)."""
     n = []
@@ -57,8 +79,9 @@ def hift_weight_names(cfg: HiFTConfig) -> list:
 class B200HiFT:
     """The HiFT vocoder on one sm_100 GPU.  ``weights``: fp32 state dict of a HiFTGenerator (weight normalisation
     folded); ``max_frames``: a window's mel frames at most, with the 8 cached ones (<= 512).  ``tf32``: the upsampling
-    stages on TF32 tensor cores (the reference's ``decode_tf32`` option); False keeps every convolution in strict fp32
-    (the reference's default)."""
+    stages on TF32 tensor cores, the reference's ``decode_tf32`` option and values (True, or a list of stages and
+    ``"<stage>:<part>"`` entries, ``tf32_parts``); False keeps every convolution in strict fp32 (the reference's
+    default)."""
 
     def __init__(self, cfg: HiFTConfig, weights: dict, device="cuda", max_frames: int = 128, n_streams: int = 256,
                  tf32: bool = True):
@@ -84,8 +107,11 @@ class B200HiFT:
             setattr(c, f, (ctypes.c_int32 * 3)(*v))
         c.nsf_alpha, c.nsf_sigma, c.voiced_threshold = cfg.nsf_alpha, cfg.nsf_sigma, cfg.voiced_threshold
         c.lrelu_slope, c.audio_limit = cfg.lrelu_slope, cfg.audio_limit
-        c.tf32 = 1 if tf32 else 0
-        self.tf32 = bool(tf32)
+        mask = tf32_parts(tf32)
+        c.tf32 = 1 if mask else 0
+        c.tf32_parts = mask
+        self.tf32 = bool(mask)
+        self.tf32_parts = mask
         with torch.cuda.device(self.device):
             w = [weights[k].detach().to(self.device, torch.float32).contiguous() for k in names]
             ptrs = (ctypes.c_void_p * len(w))(*[t.data_ptr() for t in w])

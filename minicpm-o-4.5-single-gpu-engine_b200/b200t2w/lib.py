@@ -102,7 +102,7 @@ class HiftConfig(ctypes.Structure):
                                               "n_fft", "hop")] + \
                [(n, ctypes.c_int32 * 3) for n in ("up_rates", "up_kernels", "res_kernels", "source_kernels", "dilations")] + \
                [(n, ctypes.c_float) for n in ("nsf_alpha", "nsf_sigma", "voiced_threshold", "lrelu_slope", "audio_limit")] + \
-               [("tf32", ctypes.c_int32)]
+               [("tf32", ctypes.c_int32), ("tf32_parts", ctypes.c_uint32)]
 
 
 class VocodeBatch(ctypes.Structure):

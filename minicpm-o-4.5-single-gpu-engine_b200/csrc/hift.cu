@@ -522,7 +522,8 @@ struct t2w_hift {
   double* hamming = nullptr;  // 7680
   float* cache = nullptr;     // [n_streams][8 mel frames x C | 3840 source | 3840 speech]
   int cache_ld = 0;
-  int tf32 = 0;               // the upsampling stages on the TF32 tensor-core convolution
+  int tf32 = 0;               // some upsampling-stage part on the TF32 tensor-core convolution
+  uint32_t tc_parts = 0;      // those parts: bit 3 s + p (p 0 transposed conv, 1 source branch, 2 ResBlocks)
   int* err = nullptr;         // bounded-wait error word of the tensor-core kernels
   std::vector<int> row_free;
   std::vector<uint8_t> row_live, row_first;
@@ -949,7 +950,8 @@ int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int
   h->device = dev;
   h->n_streams = n_streams;
   h->max_frames = max_frames;
-  h->tf32 = c.tf32 ? 1 : 0;
+  h->tc_parts = c.tf32 ? (c.tf32_parts ? (c.tf32_parts & 0x1FFu) : 0x1FFu) : 0u;
+  h->tf32 = h->tc_parts != 0;
   const int rc = create_impl(h, weights);
   if (rc) {
     free_all(h);
@@ -1132,15 +1134,19 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     zero(o_mel, (size_t)pl.A[0] * c.mel * 4);
     if (h->f0_tc) zero(o_f0a, (size_t)pl.A[0] * c.f0_channels * 8);
     zero(o_x0, (size_t)pl.A[0] * C0 * 4);
-    if (h->tf32) {
+    // (the parts on CUDA cores write data rows only; with some part on the tensor cores, whose tensor maps read
+    // padding rows, the ResBlock streams of a CUDA-core ResBlock part too, as the average of them feeds the next stage)
+    if (h->tc_parts & 0x92u)
       zero(o_stft, (size_t)pl.A[3] * kStftLd * 4);  // the source_down tensor maps read padding rows and channels
-    } else {
-      for (int s = 0; s < 3; ++s) {
-        const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
+    for (int s = 0; s < 3; ++s) {
+      const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
+      if (!(h->tc_parts >> (3 * s + 1) & 1u)) {
         zero(o_sd[s], sz);
         zero(o_ta[s], sz);
-        zero(o_xs[s], sz);
       }
+      if (!(h->tc_parts >> (3 * s) & 1u)) zero(o_xs[s], sz);
+      if (h->tf32 && !(h->tc_parts >> (3 * s + 2) & 1u))
+        for (int j = 0; j < 3; ++j) zero(o_xr[s][j], sz);
     }
     if (e1 != cudaSuccess) {
       set_cuda_error(e1);
@@ -1271,9 +1277,11 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     const int* ss = reinterpret_cast<const int*>(P(o_ss[s]));
     const int* ls = reinterpret_cast<const int*>(P(o_ls[s]));
     const int* su = reinterpret_cast<const int*>(P(o_su[s]));
+    const bool ups_tc = h->tc_parts >> (3 * s) & 1u, src_tc = h->tc_parts >> (3 * s + 1) & 1u,
+               res_tc = h->tc_parts >> (3 * s + 2) & 1u;
     // transposed conv, one launch per output phase over the input's data rows
     for (int p = 0; p < g.u; ++p) {
-      if (h->tf32) {
+      if (ups_tc) {
         TConvArgs t;
         t.A = x;
         t.lda = g.Cin;
@@ -1309,7 +1317,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     // source branch: strided conv of the STFT, then its ResBlock (in place)
     float* sd = reinterpret_cast<float*>(P(o_sd[s]));
     float* ta = reinterpret_cast<float*>(P(o_ta[s]));
-    if (h->tf32) {  // TF32 (the source branch is part of the reference's decode_tf32 stages)
+    if (src_tc) {  // TF32 (the source branch is part of the reference's decode_tf32 stages)
       const int S = g.down_stride;
       TConvArgs t;
       t.A = stft;  // viewed as rows of S frames
@@ -1344,12 +1352,12 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       if (rc) return fail(rc);
     }
     const long long nel = (long long)pl.A[s + 1] * Cs;
-    auto resblock = [&](HRes& r, float* xr, float* a_in, float* tmp, const float* base) -> int {
+    auto resblock = [&](HRes& r, float* xr, float* a_in, float* tmp, const float* base, bool tc) -> int {
       // a_in holds Snake1_0(x); per dilation: tmp = Snake2(conv1(a_in)); xr = x + conv2(tmp), a_in = Snake1_next(xr),
       // x = base for the first dilation when given (xr written out of place), else xr itself
       for (int dd = 0; dd < 3; ++dd) {
         const int dl = h->cfg.dilations[dd];
-        if (h->tf32) {
+        if (tc) {
           TConvArgs t;
           t.lda = Cs;
           t.rows_a = pl.A[s + 1];
@@ -1405,7 +1413,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       }
       return T2W_OK;
     };
-    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])), nullptr);  // xr[0]: scratch before the fan-out
+    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])), nullptr, src_tc);  // xr[0]: scratch
     if (rc) return fail(rc);
     float* xr[3] = {reinterpret_cast<float*>(P(o_xr[s][0])), reinterpret_cast<float*>(P(o_xr[s][1])),
                     reinterpret_cast<float*>(P(o_xr[s][2]))};
@@ -1421,7 +1429,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      ar[0], ar[1], ar[2], sn));
     if (rc) return fail(rc);
     for (int j = 0; j < 3; ++j) {
-      rc = resblock(g.res[j], xr[j], ar[j], ta, xs);
+      rc = resblock(g.res[j], xr[j], ar[j], ta, xs, res_tc);
       if (rc) return fail(rc);
     }
     // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before

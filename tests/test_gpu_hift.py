@@ -37,10 +37,13 @@ def oracle_noise(hift, seed, frames):
     return r, nz.transpose(1, 2)
 
 
-@pytest.mark.parametrize("tf32", [False, True], ids=["fp32", "tf32"])
+@pytest.mark.parametrize("tf32", [False, True, [1, 2, "0:src", "0:res"], ["2:res", "1:ups"]],
+                         ids=["fp32", "tf32", "tf32_but_0ups", "tf32_2res_1ups"])
 @pytest.mark.parametrize("name,cfg", [("hift_tiny", HIFT_TINY), ("hift_reference", HIFT)])
 def test_vocode_vs_reference_driver_golden(golden_dir, name, cfg, tf32):
-    """Strict fp32 (the reference's default) and the upsampling stages on TF32 tensor cores (its decode_tf32 option)."""
+    """Strict fp32 (the reference's default), the upsampling stages on TF32 tensor cores (its decode_tf32 option), and
+    two of its per-part lists (the parts left out on CUDA cores in fp32, their padding rows zeroed for the tensor-core
+    parts that read them)."""
     rec = torch.load(os.path.join(golden_dir, f"{name}.pt"))
     hift = ho.build_hift(cfg, seed=0)
     voc = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=128, n_streams=8, tf32=tf32)
@@ -68,7 +71,7 @@ def test_vocode_vs_reference_driver_golden(golden_dir, name, cfg, tf32):
         voc.release(h)
 
 
-@pytest.mark.parametrize("tf32", [False, True], ids=["fp32", "tf32"])
+@pytest.mark.parametrize("tf32", [False, True, ["0:ups", "1:src", "2:res"]], ids=["fp32", "tf32", "tf32_mixed"])
 def test_vocode_ragged_calls_vs_oracle(tf32):
     """Six streams, calls mixing first windows of different lengths, steady windows and finals, some streams skipping
     calls; every window against the oracle's per-stream ``vocode_window``."""

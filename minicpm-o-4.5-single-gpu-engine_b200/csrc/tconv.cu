@@ -11,13 +11,14 @@
 //
 // One persistent CTA per SM, warp-specialised: warp 0 the TMA producer (128 x 32 A boxes and BN x 32 W boxes, 128-byte
 // swizzle, one box pair per (tap, segment, 32-channel block)), warp 1 the TMEM allocator and single-thread MMA issuer,
-// warps 2-9 the epilogue (TMEM lane quarter w % 4, alternate 32-column chunks), the accumulator double-buffered in TMEM
-// so a tile's epilogue overlaps the next tile's MMAs.  Each epilogue thread owns one output row (the TMEM lane it
-// reads) and stores its 32-column chunk directly; a residual update first TMA-loads the warp's 32 x 32 block of the
-// residual (out itself, or another buffer of the same layout) into a swizzled shared-memory box (issued before the
-// accumulator is ready) and reads its row from there,
-// instead of 32 scattered row reads per warp.  (Staging the outputs through the box and writing them with TMA stores
-// measured slower for the bias and Snake epilogues.)
+// warps 2-17 the epilogue (TMEM lane quarter w % 4, every fourth 16-column chunk: four warps per quarter, since with two
+// the epilogue's instruction latency, not the MMAs, set the pace of the 1-7-tap convolutions), the accumulator
+// double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.  Each epilogue thread owns one output row
+// (the TMEM lane it reads) and stores its 16-column chunk directly; a residual update first TMA-loads the warp's
+// 32 x 16 block of the residual (out itself, or another buffer of the same layout) into a swizzled shared-memory box
+// (issued before the accumulator is ready) and reads its row from there, instead of 32 scattered row reads per warp.
+// (Staging the outputs through the box and writing them with TMA stores measured slower for the bias and Snake
+// epilogues.)
 // Output rows: row_mul * m + row_add (a transposed convolution's output phase writes every row_mul-th row of the next
 // rate's layout, a tensor map whose row pitch is row_mul rows); rows flagged in `pad` are window padding and stay zero.
 // Epilogues: bias; Snake(bias + acc) (the ResBlocks' conv1 with its second activation); x += bias + acc with
@@ -36,8 +37,10 @@ namespace {
 constexpr int kTBM = 128;
 constexpr int kTBK = 32;  // fp32 elements per 128-byte swizzle row
 constexpr int kTMaxSmem = 232448;
-constexpr int kEpiWarps = 8;
-constexpr int kEBox = 32 * 32 * 4;  // one epilogue warp's 32 x 32 fp32 staging box
+constexpr int kEpiWarps = 16;         // four per TMEM lane quarter
+constexpr int kEC = 16;               // columns per epilogue chunk
+constexpr int kEBox = 32 * kEC * 4;   // one epilogue warp's 32 x 16 fp32 residual box (64-byte rows, 64-byte swizzle)
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct TCfg {
@@ -61,15 +64,23 @@ struct TCfg {
 // left 0: the 128-byte swizzle the TMA wrote is a function of the absolute shared-memory address bits, and the MMA
 // reads it back from any row start (measured: every offset 1-12 rows exact; setting the field to the start's row
 // phase breaks every offset that is not a multiple of 8).
-constexpr int kUARows = 256;
-constexpr int kUABytes = kUARows * kTBK * 4;  // 32 KB
+//
+// MH = 2 (BN <= 128): a CTA tile is two 128-row halves that share every W box, each half its own TMEM accumulator: a
+// (tap, block) step issues 8 MMAs instead of 4.  Each step of the pipeline costs ~220 ns beyond its MMAs (measured:
+// doubling a step's MMAs added 100 ns to its 325), so twice the MMA work per step pays that once per 256 rows.
 constexpr int kUASlots = 2;
-template <int BN>
+template <int MH>
+constexpr int ua_rows() { return MH == 2 ? 192 : 256; }  // A box capacity: 128 + (taps - 1) dil rows at most
+template <int BN, int MH>
 struct TCfgU {
   static constexpr int B_BYTES = BN * kTBK * 4;
-  static constexpr int WFIT = (kTMaxSmem - TCfg<BN>::FIXED - TCfg<BN>::EPI_BYTES - kUASlots * kUABytes) / B_BYTES;
+  static constexpr int ABOX = ua_rows<MH>() * kTBK * 4;  // one half's A box
+  static constexpr int ASLOT = MH * ABOX;                // a channel block's A boxes
+  static constexpr int WFIT = (kTMaxSmem - TCfg<BN>::FIXED - TCfg<BN>::EPI_BYTES - kUASlots * ASLOT) / B_BYTES;
   static constexpr int WSTAGES = WFIT > 8 ? 8 : WFIT;
-  static constexpr int SMEM = kUASlots * kUABytes + WSTAGES * B_BYTES + TCfg<BN>::EPI_BYTES + TCfg<BN>::FIXED;
+  static constexpr int SMEM = kUASlots * ASLOT + WSTAGES * B_BYTES + TCfg<BN>::EPI_BYTES + TCfg<BN>::FIXED;
+  static constexpr int TMEM_COLS = (2 * MH * BN <= 128) ? 128 : (2 * MH * BN <= 256) ? 256 : 512;
+  static_assert(2 * MH * BN <= 512, "TMEM");
   static_assert(WSTAGES >= 3, "stages");
   static_assert(SMEM <= kTMaxSmem, "shared memory");
 };
@@ -121,22 +132,26 @@ __device__ __forceinline__ float snake_f(float x, float a, float inv) {
   return x + inv * (s * s);
 }
 
-// 16-byte chunk `c` of row `r` of a 128-byte-row box staged with the 128-byte swizzle (chunk index XOR row % 8).
+// 16-byte chunk `c` (0-3) of row `r` of a 64-byte-row box staged with the 64-byte swizzle (chunk index XOR bits 7-8
+// of the row's byte offset, (r / 2) % 4).
 __device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int c) {
-  return reinterpret_cast<float4*>(box + r * 128 + ((c ^ (r & 7)) << 4));
+  return reinterpret_cast<float4*>(box + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 // fp32 rounded to the nearest TF32 value (half of the dropped unit added to the bit pattern, then the 13 low mantissa
 // bits cleared): a split x = hi + lo with hi = tf32_rn(x), lo = tf32_rn(x - hi) leaves |x - hi - lo| <= 2^-24 |x|.
 __device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
 
-template <int BN, bool UNION>
-__global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
+template <int BN, bool UNION, int MH>
+__global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
                                                   const __grid_constant__ CUtensorMap tmW,
                                                   const __grid_constant__ CUtensorMap tmR, const TDev p) {
+  static_assert(MH == 1 || UNION, "two-half tiles in the tap-reuse form only");
   using C = TCfg<BN>;
-  using CU = TCfgU<BN>;
+  using CU = TCfgU<BN, MH>;
+  constexpr int TM = kTBM * MH;                                // rows per CTA tile
   constexpr int NST = UNION ? CU::WSTAGES : C::STAGES;        // W (and, in the per-tap form, A) ring depth
-  constexpr int A_RING = UNION ? kUASlots * kUABytes : C::STAGES * C::A_BYTES;
+  constexpr int A_RING = UNION ? kUASlots * CU::ASLOT : C::STAGES * C::A_BYTES;
+  constexpr int TMEM_COLS = UNION ? CU::TMEM_COLS : C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -162,7 +177,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     for (int w = 0; w < kEpiWarps; ++w) mbar_init(&ebar[w], 1);
     fence_mbar_init();
@@ -172,7 +187,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
   }
   pdl_wait();
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -193,11 +208,13 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
       bool ok = true;
       const uint32_t abytes = (uint32_t)p.urows * kTBK * 4;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
+        const int m0 = (tile / p.tiles_n) * TM, n0 = (tile % p.tiles_n) * BN;
         for (int cb = 0; cb < kb_per_seg && ok; ++cb) {
           if (!(ok = mbar_wait(&aempty[as], aph ^ 1u, p.err))) break;
-          mbar_expect_tx(&afull[as], abytes);
-          tma_load_2d(sA + as * kUABytes, &tmA, cb * kTBK, m0 + p.tap_row0, &afull[as]);
+          mbar_expect_tx(&afull[as], MH * abytes);
+#pragma unroll
+          for (int h = 0; h < MH; ++h)
+            tma_load_2d(sA + as * CU::ASLOT + h * CU::ABOX, &tmA, cb * kTBK, m0 + h * kTBM + p.tap_row0, &afull[as]);
           if (++as == kUASlots) {
             as = 0;
             aph ^= 1u;
@@ -225,18 +242,22 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
         const int acc = it & 1;
         if (!(ok = mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1u, p.err))) break;
         tc_fence_after();
-        const uint32_t d = tmem + acc * BN;
+        const uint32_t d = tmem + acc * MH * BN;
         for (int cb = 0; cb < kb_per_seg && ok; ++cb) {
           if (!(ok = mbar_wait(&afull[as], aph, p.err))) break;
-          const uint32_t a_slot = smem_u32(sA + as * kUABytes);
+          const uint32_t a_slot = smem_u32(sA + as * CU::ASLOT);
           for (int tap = 0; tap < p.taps; ++tap) {
             if (!(ok = mbar_wait(&full[stage], phase, p.err))) break;
             tc_fence_after();
-            const uint32_t a0 = a_slot + (uint32_t)(tap * p.dil) * 128u, b0 = smem_u32(sB + stage * C::B_BYTES);
+            const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
-            for (int k = 0; k < kTBK / 8; ++k)
-              umma_tf32(d, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
-                        (cb | tap | k) != 0 ? 1u : 0u);
+            for (int h = 0; h < MH; ++h) {
+              const uint32_t a0 = a_slot + h * CU::ABOX + (uint32_t)(tap * p.dil) * 128u;
+#pragma unroll
+              for (int k = 0; k < kTBK / 8; ++k)
+                umma_tf32(d + h * BN, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
+                          (cb | tap | k) != 0 ? 1u : 0u);
+            }
             umma_commit(&empty[stage]);
             if (++stage == NST) {
               stage = 0;
@@ -258,7 +279,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
+        const int m0 = (tile / p.tiles_n) * TM, n0 = (tile % p.tiles_n) * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
@@ -307,7 +328,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
   } else {
     const int ew = warp - 2;
     const int q = warp & 3;  // the TMEM lane quarter this warp may read
-    const int half = ew >> 2;
+    const int grp = ew >> 2;  // this warp's chunks: grp, grp + 4, ... of the tile's 16-column chunks
     uint8_t* box = sE + ew * kEBox;
     uint64_t* eb = &ebar[ew];
     uint32_t eph = 0;
@@ -323,31 +344,33 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
-      const int m0 = (tile / p.tiles_n) * kTBM, n0 = (tile % p.tiles_n) * BN;
-      const int r0 = m0 + q * 32;  // this warp's first row of the tile
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if (resid && half < BN / 32) load_resid(n0 + 32 * half, r0);
+      const int m0 = (tile / p.tiles_n) * TM, n0 = (tile % p.tiles_n) * BN;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * MH * BN;
+      if (resid && grp < BN / kEC) load_resid(n0 + kEC * grp, m0 + q * 32);
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], (it >> 1) & 1, p.err))) {
         if (pending) mbar_wait(eb, eph, p.err);
         break;
       }
       tc_fence_after();
-      if (half >= BN / 32) {  // a 32-column tile: the second half of the epilogue warps has no chunk of its own
+      if (grp >= BN / kEC) {  // a 32-column tile: two of the four warp groups have no chunk of their own
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
         continue;
       }
-      const long long orow = (long long)p.row_mul * (r0 + lane) + p.row_add;
-      const bool live = !p.pad[orow];
       bool ok = true;
 #pragma unroll 1
-      for (int b = half; b < BN / 32; b += 2) {
-        const int c0 = n0 + 32 * b;
-        if (resid && b != half) load_resid(c0, r0);
-        float v[32];
-        tmem_ld32(taddr + 32 * b, v);
-        if (b + 2 >= BN / 32) {  // this warp's last load of the accumulator
+      for (int h = 0; h < MH && ok; ++h) {
+      const int r0 = m0 + h * kTBM + q * 32;  // this warp's first row of the half
+      const long long orow = (long long)p.row_mul * (r0 + lane) + p.row_add;
+      const bool live = !p.pad[orow];
+#pragma unroll 1
+      for (int b = grp; b < BN / kEC; b += 4) {
+        const int c0 = n0 + kEC * b;
+        if (resid && (h != 0 || b != grp)) load_resid(c0, r0);
+        float v[kEC];
+        tmem_ld16(taddr + h * BN + kEC * b, v);
+        if (h == MH - 1 && b + 4 >= BN / kEC) {  // this warp's last load of the accumulator
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -361,10 +384,10 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           float* dst2 = p.has_out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
           if (!live && p.resid_oop) {  // a padding row of an out-of-place update: the residual's (zero) row
 #pragma unroll
-            for (int j = 0; j < 8; ++j) reinterpret_cast<float4*>(dst)[j] = *box_chunk(box, lane, j);
+            for (int j = 0; j < kEC / 4; ++j) reinterpret_cast<float4*>(dst)[j] = *box_chunk(box, lane, j);
           }
 #pragma unroll
-          for (int j = 0; j < 8 && live; ++j) {  // padding rows of an in-place update keep their (zero) values
+          for (int j = 0; j < kEC / 4 && live; ++j) {  // padding rows of an in-place update keep their (zero) values
             const float4 x = *box_chunk(box, lane, j);
             const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
             const float4 y = make_float4(x.x + (v[4 * j] + bb.x), x.y + (v[4 * j + 1] + bb.y),
@@ -382,7 +405,7 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           __syncwarp();
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < kEC / 4; ++j) {
             float4 y = make_float4(0.f, 0.f, 0.f, 0.f), z = y;
             if (live) {
               const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
@@ -414,21 +437,22 @@ __global__ void __launch_bounds__(320, 1) k_tconv(const __grid_constant__ CUtens
           }
         }
       }
+      }
       if (!ok) break;
     }
   }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
-template <int BN, bool UNION>
+template <int BN, bool UNION, int MH>
 int launch_impl(const TConvArgs& a, cudaStream_t st) {
-  constexpr int SMEM = UNION ? TCfgU<BN>::SMEM : TCfg<BN>::SMEM;
+  constexpr int SMEM = UNION ? TCfgU<BN, MH>::SMEM : TCfg<BN>::SMEM;
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t e = smem_attr_once(k_tconv<BN, UNION>, SMEM, attr_done);
+  cudaError_t e = smem_attr_once(k_tconv<BN, UNION, MH>, SMEM, attr_done);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -442,8 +466,8 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   if (!make_tmap_2d(&ma, a.A, 4, (uint64_t)a.rows_a, (uint64_t)a.Cin * (a.split_in ? 2 : 1), (uint64_t)a.lda * 4,
                     UNION ? urows : kTBM, kTBK) ||
       !make_tmap_2d(&mw, a.W, 4, (uint64_t)a.N, cpad * a.taps * segs, cpad * a.taps * segs * 4, BN, kTBK) ||
-      !make_tmap_2d(&mr, (a.resid_in ? a.resid_in : a.out) + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M, out_cols,
-                    out_pitch, 32, 32))
+      !make_tmap_2d_ex(&mr, (a.resid_in ? a.resid_in : a.out) + (long long)a.row_add * a.ldo, 4, (uint64_t)a.M,
+                       out_cols, out_pitch, 32, kEC, kEC * 4))
     return T2W_ERR_INVALID;
   TDev p;
   p.M = a.M;
@@ -453,7 +477,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.tap_row0 = a.tap_row0;
   p.dil = a.dil;
   p.tiles_n = a.N / BN;
-  p.num_tiles = (a.M / kTBM) * p.tiles_n;
+  p.num_tiles = (a.M / (kTBM * MH)) * p.tiles_n;
   p.split_in = a.split_in;
   p.split_out = a.split_out;
   p.urows = urows;
@@ -471,7 +495,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.has_out2 = a.out2 != nullptr;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  e = launch_k(k_tconv<BN, UNION>, dim3(grid), dim3(320), SMEM, st, ma, mw, mr, p);
+  e = launch_k(k_tconv<BN, UNION, MH>, dim3(grid), dim3(kThreads), SMEM, st, ma, mw, mr, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -493,12 +517,19 @@ int launch_tconv(const TConvArgs& a, cudaStream_t st) {
       (a.resid_in && (a.epi != TCONV_RESID || (reinterpret_cast<uintptr_t>(a.resid_in) & 15))) ||
       (reinterpret_cast<uintptr_t>(a.bias) & 15))
     return T2W_ERR_INVALID;
-  const bool u = !a.split_in && a.taps > 1 && (long long)(a.taps - 1) * a.dil + kTBM <= kUARows;
+  // the tap-reuse form when every tap's rows fit one A box; with two 128-row halves per tile when they fit the smaller
+  // boxes of that form and M is a multiple of 256 (tiles of up to 128 columns)
+  const long long ext = (long long)(a.taps - 1) * a.dil + kTBM;
+  const bool u = !a.split_in && a.taps > 1 && ext <= ua_rows<1>();
+  const bool u2 = u && ext <= ua_rows<2>() && a.M % (2 * kTBM) == 0;
   if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms())
-    return u ? launch_impl<256, true>(a, st) : launch_impl<256, false>(a, st);
-  if (a.N % 128 == 0) return u ? launch_impl<128, true>(a, st) : launch_impl<128, false>(a, st);
-  if (a.N == 64) return u ? launch_impl<64, true>(a, st) : launch_impl<64, false>(a, st);
-  if (a.N == 32) return u ? launch_impl<32, true>(a, st) : launch_impl<32, false>(a, st);
+    return u ? launch_impl<256, true, 1>(a, st) : launch_impl<256, false, 1>(a, st);
+  if (a.N % 128 == 0)
+    return u2 ? launch_impl<128, true, 2>(a, st) : u ? launch_impl<128, true, 1>(a, st) : launch_impl<128, false, 1>(a, st);
+  if (a.N == 64)
+    return u2 ? launch_impl<64, true, 2>(a, st) : u ? launch_impl<64, true, 1>(a, st) : launch_impl<64, false, 1>(a, st);
+  if (a.N == 32)
+    return u2 ? launch_impl<32, true, 2>(a, st) : u ? launch_impl<32, true, 1>(a, st) : launch_impl<32, false, 1>(a, st);
   return T2W_ERR_INVALID;
 }
 

@@ -120,7 +120,7 @@ def test_snake_epilogue_transposed_phase():
 
 
 @pytest.mark.parametrize("oop", [False, True], ids=["in_place", "out_of_place"])
-@pytest.mark.parametrize("N", [64, 256])
+@pytest.mark.parametrize("N", [64, 128, 256])
 def test_residual_epilogue_with_next_snake(N, oop):
     """out += bias + conv and out2 = Snake(out), padding rows of both untouched: conv2 of a ResBlock.  Out of place:
     out = resid_in + bias + conv with resid_in's (zero) padding rows copied (a ResBlock's first update of the stage's
@@ -143,6 +143,34 @@ def test_residual_epilogue_with_next_snake(N, oop):
     s[pad.bool()] = 3.0
     e1, e2 = rel(out, y), rel(out2, s)
     print(f"resid N={N}: out rel-L2 {e1:.2e}, out2 rel-L2 {e2:.2e}")
+    assert e1 < 3e-3 and e2 < 3e-3
+    assert torch.all(out[pad.bool()] == 0) and torch.all(out2[pad.bool()] == 3.0)
+
+
+@pytest.mark.parametrize("M,taps,dil", [(2048, 11, 5), (2176, 3, 1), (2048, 11, 7), (2048, 1, 1), (2304, 7, 3)],
+                         ids=["two_halves", "one_half_odd_M", "one_half_wide_halo", "per_tap", "two_halves_9x256"])
+@pytest.mark.parametrize("N", [64, 128])
+def test_tile_forms(M, taps, dil, N):
+    """The kernel's tile forms at the vocoder's widths: 256-row tiles of two halves sharing each W box (M a multiple
+    of 256, 128 + (taps - 1) dil <= 192), one 128-row half in the tap-reuse form (M not a multiple of 256, or a wider
+    halo), one A box per tap (a single tap); residual update with the next Snake, padding rows."""
+    Cin = N
+    r0 = -((taps - 1) * dil) // 2
+    a, w, b, pad = case(M, N, Cin, taps, dil, seed=60 + taps + N)
+    g = torch.Generator(device="cuda").manual_seed(61)
+    x0 = torch.randn(M, N, device="cuda", generator=g)
+    x0[pad.bool()] = 0
+    alpha = torch.rand(N, device="cuda", generator=g) + 0.5
+    inv = 1.0 / (alpha + 1e-9)
+    out = x0.clone()
+    out2 = torch.full((M, N), 3.0, device="cuda")
+    run(a, Cin, M, w, b, M, N, Cin, taps, r0, dil, out, N, pad, epi=RESID, alpha=alpha, inv=inv, out2=out2)
+    y = x0.double() + conv_ref(a, w, b, M, taps, r0, dil)
+    y[pad.bool()] = 0
+    s = snake(y, alpha.double(), inv.double())
+    s[pad.bool()] = 3.0
+    e1, e2 = rel(out, y), rel(out2, s)
+    print(f"M={M} taps={taps} dil={dil} N={N}: out rel-L2 {e1:.2e}, out2 rel-L2 {e2:.2e}")
     assert e1 < 3e-3 and e2 < 3e-3
     assert torch.all(out[pad.bool()] == 0) and torch.all(out2[pad.bool()] == 3.0)
 

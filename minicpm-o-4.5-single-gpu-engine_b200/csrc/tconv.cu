@@ -57,7 +57,7 @@ struct TCfg {
   static_assert(SMEM <= kTMaxSmem, "shared memory");
 };
 
-// Tap-reuse form (taps > 1, (taps - 1) dil + 128 <= 256): one A box per 32-channel block covers every tap's rows
+// Tap-reuse form (128 + (taps - 1) dil <= 256): one A box per 32-channel block covers every tap's rows
 // (128 + (taps - 1) dil of them) and each tap's MMAs read it from a row offset; W streams per (tap, block) through its
 // own ring.  A traffic per tile drops from taps x 128 rows to 128 + (taps - 1) dil rows per channel block.  The
 // operand descriptor of a tap simply starts tap x dil 128-byte rows into the box, with the matrix base offset field
@@ -68,17 +68,23 @@ struct TCfg {
 // MH = 2 (BN <= 128): a CTA tile is two 128-row halves that share every W box, each half its own TMEM accumulator: a
 // (tap, block) step issues 8 MMAs instead of 4.  Each step of the pipeline costs ~220 ns beyond its MMAs (measured:
 // doubling a step's MMAs added 100 ns to its 325), so twice the MMA work per step pays that once per 256 rows.
+//
+// SPLIT (split form, MH = 1): a channel block's A boxes are its hi and lo parts, a step's W boxes W_hi and W_lo, and a
+// step issues hi W_hi, hi W_lo and lo W_hi (12 MMAs).
 constexpr int kUASlots = 2;
-template <int MH>
-constexpr int ua_rows() { return MH == 2 ? 192 : 256; }  // A box capacity: 128 + (taps - 1) dil rows at most
-template <int BN, int MH>
+template <int MH, bool SPLIT = false>
+constexpr int ua_rows() { return (MH == 2 || SPLIT) ? 192 : 256; }  // A box capacity: 128 + (taps - 1) dil rows at most
+template <int BN, int MH, bool SPLIT = false>
 struct TCfgU {
   static constexpr int B_BYTES = BN * kTBK * 4;
-  static constexpr int ABOX = ua_rows<MH>() * kTBK * 4;  // one half's A box
-  static constexpr int ASLOT = MH * ABOX;                // a channel block's A boxes
-  static constexpr int WFIT = (kTMaxSmem - TCfg<BN>::FIXED - TCfg<BN>::EPI_BYTES - kUASlots * ASLOT) / B_BYTES;
+  static constexpr int NA = SPLIT ? 2 : 1;                     // A boxes per half and channel block (hi, lo)
+  static constexpr int NW = SPLIT ? 2 : 1;                     // W boxes per step (W_hi, W_lo)
+  static constexpr int ABOX = ua_rows<MH, SPLIT>() * kTBK * 4;  // one A box
+  static constexpr int ASLOT = MH * NA * ABOX;                 // a channel block's A boxes
+  static constexpr int WSTEP = NW * B_BYTES;
+  static constexpr int WFIT = (kTMaxSmem - TCfg<BN>::FIXED - TCfg<BN>::EPI_BYTES - kUASlots * ASLOT) / WSTEP;
   static constexpr int WSTAGES = WFIT > 8 ? 8 : WFIT;
-  static constexpr int SMEM = kUASlots * ASLOT + WSTAGES * B_BYTES + TCfg<BN>::EPI_BYTES + TCfg<BN>::FIXED;
+  static constexpr int SMEM = kUASlots * ASLOT + WSTAGES * WSTEP + TCfg<BN>::EPI_BYTES + TCfg<BN>::FIXED;
   static constexpr int TMEM_COLS = (2 * MH * BN <= 128) ? 128 : (2 * MH * BN <= 256) ? 256 : 512;
   static_assert(2 * MH * BN <= 512, "TMEM");
   static_assert(WSTAGES >= 3, "stages");
@@ -141,13 +147,15 @@ __device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int c) {
 // bits cleared): a split x = hi + lo with hi = tf32_rn(x), lo = tf32_rn(x - hi) leaves |x - hi - lo| <= 2^-24 |x|.
 __device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
 
-template <int BN, bool UNION, int MH>
+template <int BN, bool UNION, int MH, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
                                                   const __grid_constant__ CUtensorMap tmW,
                                                   const __grid_constant__ CUtensorMap tmR, const TDev p) {
   static_assert(MH == 1 || UNION, "two-half tiles in the tap-reuse form only");
+  static_assert(!SPLIT || (UNION && MH == 1), "split form in the tap-reuse path: one half per tile");
   using C = TCfg<BN>;
-  using CU = TCfgU<BN, MH>;
+  using CU = TCfgU<BN, MH, SPLIT>;
+  constexpr int WSTEP = UNION ? CU::WSTEP : C::B_BYTES;
   constexpr int TM = kTBM * MH;                                // rows per CTA tile
   constexpr int NST = UNION ? CU::WSTAGES : C::STAGES;        // W (and, in the per-tap form, A) ring depth
   constexpr int A_RING = UNION ? kUASlots * CU::ASLOT : C::STAGES * C::A_BYTES;
@@ -156,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + A_RING;
-  uint8_t* sE = sB + NST * C::B_BYTES;
+  uint8_t* sE = sB + NST * WSTEP;
   uint64_t* full = reinterpret_cast<uint64_t*>(sE + C::EPI_BYTES);
   uint64_t* empty = full + NST;
   uint64_t* tfull = empty + NST;
@@ -211,18 +219,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
         const int m0 = (tile / p.tiles_n) * TM, n0 = (tile % p.tiles_n) * BN;
         for (int cb = 0; cb < kb_per_seg && ok; ++cb) {
           if (!(ok = mbar_wait(&aempty[as], aph ^ 1u, p.err))) break;
-          mbar_expect_tx(&afull[as], MH * abytes);
+          mbar_expect_tx(&afull[as], MH * CU::NA * abytes);
 #pragma unroll
           for (int h = 0; h < MH; ++h)
-            tma_load_2d(sA + as * CU::ASLOT + h * CU::ABOX, &tmA, cb * kTBK, m0 + h * kTBM + p.tap_row0, &afull[as]);
+#pragma unroll
+            for (int sa = 0; sa < CU::NA; ++sa)  // split form: hi at channel cb, lo Cin channels on
+              tma_load_2d(sA + as * CU::ASLOT + (h * CU::NA + sa) * CU::ABOX, &tmA, sa * p.Cin + cb * kTBK,
+                          m0 + h * kTBM + p.tap_row0, &afull[as]);
           if (++as == kUASlots) {
             as = 0;
             aph ^= 1u;
           }
           for (int tap = 0; tap < p.taps; ++tap) {
             if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, p.err))) break;
-            mbar_expect_tx(&full[stage], C::B_BYTES);
-            tma_load_2d(sB + stage * C::B_BYTES, &tmW, tap * cpad + cb * kTBK, n0, &full[stage]);
+            mbar_expect_tx(&full[stage], CU::WSTEP);
+#pragma unroll
+            for (int sw = 0; sw < CU::NW; ++sw)  // split form: W_hi, W_lo of the tap's [W_hi | W_lo | W_hi]
+              tma_load_2d(sB + stage * CU::WSTEP + sw * C::B_BYTES, &tmW, (tap * segs + sw) * cpad + cb * kTBK, n0,
+                          &full[stage]);
             if (++stage == NST) {
               stage = 0;
               phase ^= 1u;
@@ -249,14 +263,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
           for (int tap = 0; tap < p.taps; ++tap) {
             if (!(ok = mbar_wait(&full[stage], phase, p.err))) break;
             tc_fence_after();
-            const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+            const uint32_t b_step = smem_u32(sB + stage * CU::WSTEP);
 #pragma unroll
             for (int h = 0; h < MH; ++h) {
-              const uint32_t a0 = a_slot + h * CU::ABOX + (uint32_t)(tap * p.dil) * 128u;
 #pragma unroll
-              for (int k = 0; k < kTBK / 8; ++k)
-                umma_tf32(d + h * BN, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
-                          (cb | tap | k) != 0 ? 1u : 0u);
+              for (int pr = 0; pr < (SPLIT ? 3 : 1); ++pr) {  // split form: (hi, W_hi), (hi, W_lo), (lo, W_hi)
+                const int sa = pr == 2 ? 1 : 0, sw = pr == 1 ? 1 : 0;
+                const uint32_t a0 = a_slot + (h * CU::NA + sa) * CU::ABOX + (uint32_t)(tap * p.dil) * 128u;
+                const uint32_t b0 = b_step + sw * C::B_BYTES;
+#pragma unroll
+                for (int k = 0; k < kTBK / 8; ++k)
+                  umma_tf32(d + h * BN, sdesc_sw128(a0 + 32 * k, 1024, 16), sdesc_sw128(b0 + 32 * k, 1024, 16), idesc,
+                            (cb | tap | pr | k) != 0 ? 1u : 0u);
+              }
             }
             umma_commit(&empty[stage]);
             if (++stage == NST) {
@@ -367,7 +386,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
 #pragma unroll 1
       for (int b = grp; b < BN / kEC; b += 4) {
         const int c0 = n0 + kEC * b;
-        if (resid && (h != 0 || b != grp)) load_resid(c0, r0);
         float v[kEC];
         tmem_ld16(taddr + h * BN + kEC * b, v);
         if (h == MH - 1 && b + 4 >= BN / kEC) {  // this warp's last load of the accumulator
@@ -381,14 +399,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
           eph ^= 1u;
           pending = false;
           if (!ok) break;
+          float4 xb[kEC / 4];  // this row's residual chunk, out of the box before the next load refills it
+#pragma unroll
+          for (int j = 0; j < kEC / 4; ++j) xb[j] = *box_chunk(box, lane, j);
+          fence_proxy_async_smem();  // every lane's reads of the box come before the next load overwrites it
+          __syncwarp();
+          if (b + 4 < BN / kEC)
+            load_resid(c0 + 4 * kEC, r0);  // this half's next chunk
+          else if (h + 1 < MH)
+            load_resid(n0 + kEC * grp, r0 + kTBM);  // the next half's first chunk
           float* dst2 = p.has_out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
           if (!live && p.resid_oop) {  // a padding row of an out-of-place update: the residual's (zero) row
 #pragma unroll
-            for (int j = 0; j < kEC / 4; ++j) reinterpret_cast<float4*>(dst)[j] = *box_chunk(box, lane, j);
+            for (int j = 0; j < kEC / 4; ++j) reinterpret_cast<float4*>(dst)[j] = xb[j];
           }
 #pragma unroll
           for (int j = 0; j < kEC / 4 && live; ++j) {  // padding rows of an in-place update keep their (zero) values
-            const float4 x = *box_chunk(box, lane, j);
+            const float4 x = xb[j];
             const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + c0) + j);
             const float4 y = make_float4(x.x + (v[4 * j] + bb.x), x.y + (v[4 * j + 1] + bb.y),
                                          x.z + (v[4 * j + 2] + bb.z), x.w + (v[4 * j + 3] + bb.w));
@@ -401,8 +428,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
                               snake_f(y.w, a.w, iv.w));
             }
           }
-          fence_proxy_async_smem();  // every lane's reads of the box come before the next load overwrites it
-          __syncwarp();
         } else {
 #pragma unroll
           for (int j = 0; j < kEC / 4; ++j) {
@@ -448,11 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
   }
 }
 
-template <int BN, bool UNION, int MH>
+template <int BN, bool UNION, int MH, bool SPLIT = false>
 int launch_impl(const TConvArgs& a, cudaStream_t st) {
-  constexpr int SMEM = UNION ? TCfgU<BN, MH>::SMEM : TCfg<BN>::SMEM;
+  constexpr int SMEM = UNION ? TCfgU<BN, MH, SPLIT>::SMEM : TCfg<BN>::SMEM;
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t e = smem_attr_once(k_tconv<BN, UNION, MH>, SMEM, attr_done);
+  cudaError_t e = smem_attr_once(k_tconv<BN, UNION, MH, SPLIT>, SMEM, attr_done);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -495,7 +520,7 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.has_out2 = a.out2 != nullptr;
   p.err = a.err;
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  e = launch_k(k_tconv<BN, UNION, MH>, dim3(grid), dim3(kThreads), SMEM, st, ma, mw, mr, p);
+  e = launch_k(k_tconv<BN, UNION, MH, SPLIT>, dim3(grid), dim3(kThreads), SMEM, st, ma, mw, mr, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -520,8 +545,14 @@ int launch_tconv(const TConvArgs& a, cudaStream_t st) {
   // the tap-reuse form when every tap's rows fit one A box; with two 128-row halves per tile when they fit the smaller
   // boxes of that form and M is a multiple of 256 (tiles of up to 128 columns)
   const long long ext = (long long)(a.taps - 1) * a.dil + kTBM;
-  const bool u = !a.split_in && a.taps > 1 && ext <= ua_rows<1>();
+  const bool u = !a.split_in && ext <= ua_rows<1>();
   const bool u2 = u && ext <= ua_rows<2>() && a.M % (2 * kTBM) == 0;
+  if (a.split_in && ext <= ua_rows<1, true>()) {  // the split form's tap-reuse path (tiles of up to 128 columns)
+    if (a.N % 128 == 0 && !(a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms()))
+      return launch_impl<128, true, 1, true>(a, st);
+    if (a.N == 64) return launch_impl<64, true, 1, true>(a, st);
+    if (a.N == 32) return launch_impl<32, true, 1, true>(a, st);
+  }
   if (a.N % 128 == 0 && a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms())
     return u ? launch_impl<256, true, 1>(a, st) : launch_impl<256, false, 1>(a, st);
   if (a.N % 128 == 0)

@@ -682,7 +682,7 @@ def hift_flops(hcfg, F: int) -> float:
     return float(fl)
 
 
-def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float) -> dict:
+def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float, split_fp32: bool = False) -> dict:
     """The HiFT vocoder (row f4: mel -> 24 kHz waveform) at the reference config, random init, the upsampling stages on
     TF32 tensor cores (the reference's decode_tf32 option; f0 predictor, source, conv_pre / conv_post fp32): ``n``
     streams, every call one 50-frame window per stream (58 frames with the 8 cached ones once the stream has started),
@@ -693,7 +693,8 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float)
     from oracle import hift_oracle as ho
 
     g = torch.Generator().manual_seed(seed)
-    voc = B200HiFT.from_module(ho.build_hift(HIFT, seed=0), HIFT, device=dev, max_frames=64, n_streams=n)
+    voc = B200HiFT.from_module(ho.build_hift(HIFT, seed=0), HIFT, device=dev, max_frames=64, n_streams=n,
+                               split_fp32=split_fp32)
     hs = [voc.new_stream(1000 + i) for i in range(n)]
     T = 50
     mels = [(torch.randn(n * T, HIFT.mel, generator=g) - 2.0).pin_memory() for _ in range(3)]
@@ -722,8 +723,9 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float)
     for h in hs:
         voc.release(h)
     voc.close()
-    return {"workload": f"HiFT vocoder, {n} streams, steady 50-frame windows (58 with the cached 8), upsampling stages "
-                        f"in TF32",
+    return {"workload": f"HiFT vocoder, {n} streams, steady 50-frame windows (58 with the cached 8), "
+                        + ("every convolution in split form (3xTF32, fp32-level)" if split_fp32 else
+                           "upsampling stages in TF32"),
             "ms_per_call": ms, "host_enqueue_ms_per_call": host_ms, "audio_s_per_s": n * T * 480 / 24000 / (ms / 1000),
             "mel_frames_per_s": n * T / (ms / 1000), "tflops": flop / (ms / 1000) / 1e12,
             "h2d_bytes_per_call": n * T * HIFT.mel * 4, "d2h_bytes_per_call": n * T * 480 * 4}
@@ -943,6 +945,8 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
         torch.cuda.empty_cache()
         sub["hift_64"] = hift_record(dev, 64, steps=5, warmup=2, seed=14, peak_tf=peak_tf)
         torch.cuda.empty_cache()
+        sub["hift_64_split_fp32"] = hift_record(dev, 64, steps=5, warmup=2, seed=14, peak_tf=peak_tf, split_fp32=True)
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not a.no_reference_gpu:
         torch.cuda.empty_cache()
         ref_gpu = reference_gpu_child(a)
@@ -956,6 +960,11 @@ def packed_job(a, rank: int, world: int, local: int) -> None:
             h_ref = (ref_gpu.get(k) or {}).get("ms_per_call")
             if h_ours and h_ref:
                 ref_gpu.setdefault("hift_speedup", {})[k] = h_ref / h_ours
+        h32 = (sub.get("hift_64_split_fp32") or {}).get("ms_per_call")
+        for k in ("hift_64", "hift_64_graphs"):  # fp32 numerics on both sides: the reference's default precision
+            h_ref = (ref_gpu.get(k) or {}).get("ms_per_call")
+            if h32 and h_ref:
+                ref_gpu.setdefault("hift_speedup_fp32", {})[k] = h_ref / h32
         e_ours = (sub.get("encoder_64") or {}).get("ms_per_call")
         for k in ("encoder_64", "encoder_64_batched_io"):  # the flow encoder's steady window call, 64 streams
             e_ref = (ref_gpu.get(k) or {}).get("ms_per_call")

@@ -505,11 +505,13 @@ typedef struct t2w_hift_config {
   int32_t mel, channels, f0_channels, f0_layers, harmonics, sample_rate, n_fft, hop;
   int32_t up_rates[3], up_kernels[3], res_kernels[3], source_kernels[3], dilations[3];
   float nsf_alpha, nsf_sigma, voiced_threshold, lrelu_slope, audio_limit;
-  int32_t tf32; /* 0: strict fp32 everywhere; 1: the upsampling stages (transposed convs, source and main ResBlocks) on
-                 * TF32 tensor cores, the reference's decode_tf32 option (token2wav.py:160-210); the f0 predictor, the
-                 * source, conv_pre, source_downs and conv_post stay fp32 — the f0 layers after the first and
-                 * conv_post on the tensor cores in split form (3xTF32: operands as pairs of TF32 values, hi + lo,
-                 * fp32-level accuracy), the rest on CUDA cores */
+  int32_t tf32; /* 0: strict fp32 everywhere (CUDA cores); 2: every convolution on the tensor cores in split form
+                 * (3xTF32: operands as pairs of TF32 values, hi W_hi + hi W_lo + lo W_hi; fp32-level products, the
+                 * reference's strict-fp32 numerics at tensor-core speed; tf32_parts ignored);
+                 * 1: the upsampling stages (transposed convs, source and main ResBlocks) on
+                 * TF32 tensor cores, the reference's decode_tf32 option (token2wav.py:160-210); the f0 predictor,
+                 * conv_pre and conv_post stay at fp32 level (on the tensor cores: the split form, or the mel rows
+                 * tripled as [hi | lo | hi] against [W_hi | W_hi | W_lo]), the source on CUDA cores */
   uint32_t tf32_parts; /* with tf32 set: which parts run on TF32, bit 3 s + p for stage s (0-2) and part p (0 the
                         * transposed conv, 1 the source branch, 2 the ResBlocks) — the reference's per-stage lists
                         * (tf32_stages, token2wav.py:145-158); 0 means every part (tf32 = 1 alone); the parts left out

@@ -81,10 +81,12 @@ class B200HiFT:
     folded); ``max_frames``: a window's mel frames at most, with the 8 cached ones (<= 512).  ``tf32``: the upsampling
     stages on TF32 tensor cores, the reference's ``decode_tf32`` option and values (True, or a list of stages and
     ``"<stage>:<part>"`` entries, ``tf32_parts``); False keeps every convolution in strict fp32 (the reference's
-    default)."""
+    default) on CUDA cores.  ``split_fp32``: every convolution on the tensor cores in split form instead (operands as
+    pairs of TF32 values, hi W_hi + hi W_lo + lo W_hi: fp32-level products, the reference's fp32 numerics at
+    tensor-core speed); ``tf32`` is then ignored."""
 
     def __init__(self, cfg: HiFTConfig, weights: dict, device="cuda", max_frames: int = 128, n_streams: int = 256,
-                 tf32: bool = True):
+                 tf32=True, split_fp32: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -107,11 +109,12 @@ class B200HiFT:
             setattr(c, f, (ctypes.c_int32 * 3)(*v))
         c.nsf_alpha, c.nsf_sigma, c.voiced_threshold = cfg.nsf_alpha, cfg.nsf_sigma, cfg.voiced_threshold
         c.lrelu_slope, c.audio_limit = cfg.lrelu_slope, cfg.audio_limit
-        mask = tf32_parts(tf32)
-        c.tf32 = 1 if mask else 0
+        mask = 0 if split_fp32 else tf32_parts(tf32)
+        c.tf32 = 2 if split_fp32 else (1 if mask else 0)
         c.tf32_parts = mask
         self.tf32 = bool(mask)
         self.tf32_parts = mask
+        self.split_fp32 = bool(split_fp32)
         with torch.cuda.device(self.device):
             w = [weights[k].detach().to(self.device, torch.float32).contiguous() for k in names]
             ptrs = (ctypes.c_void_p * len(w))(*[t.data_ptr() for t in w])

@@ -53,6 +53,7 @@ constexpr int kSrcCache = 3840;       // cached source / speech samples (8 frame
 constexpr int kPadMel = 4;            // zero rows on each side of a window's mel frames
 constexpr int kNfft = 16, kHop = 4, kBins = kNfft / 2 + 1;
 constexpr int kStftLd = 20;  // floats per STFT frame row: the 18 channels, 2 zero (rows of 80 bytes for tensor maps)
+constexpr int kStftLd3 = 56;  // the tensor-core fp32 mode's tripled STFT rows: [hi 18 | lo 18 | hi 18 | 2 zero]
 
 // ---------------------------------------------------------------- generic fp32 convolution
 enum HEpi { HE_NONE = 0, HE_ELU = 1, HE_ABS = 2, HE_SNAKE = 3, HE_RESID = 4, HE_LEAKY = 5, HE_ELU_SPLIT = 6 };
@@ -213,8 +214,9 @@ struct HRow {
   int out0, out_len;               // output samples: offset and count
 };
 
+// mel3 (may be null): the rows tripled as [hi | lo | hi] (3 C floats a row), the input of the tensor-core convs.
 __global__ void k_mel_in(const float* __restrict__ win_mel, const HRow* __restrict__ rows, const float* __restrict__ cache,
-                         int cache_ld, int C, float* __restrict__ mel) {
+                         int cache_ld, int C, float* __restrict__ mel, float* __restrict__ mel3) {
   pdl_wait();
   pdl_launch();
   const HRow e = rows[blockIdx.y];
@@ -224,6 +226,13 @@ __global__ void k_mel_in(const float* __restrict__ win_mel, const HRow* __restri
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
     const float v = t < nc ? cache[(size_t)e.cache * cache_ld + t * C + c] : win_mel[(size_t)(e.mel_off + t - nc) * C + c];
     mel[(size_t)(e.mel0 + t) * C + c] = v;
+    if (mel3) {
+      float* r = mel3 + (size_t)(e.mel0 + t) * 3 * C;
+      const float hi = tf32_rn(v);
+      r[c] = hi;
+      r[C + c] = tf32_rn(v - hi);
+      r[2 * C + c] = hi;
+    }
   }
 }
 
@@ -232,18 +241,29 @@ struct Snake3 {
   const float *al[3], *inv[3];
 };
 // xb = ups(x) + source branch (every row), the three ResBlocks' first Snakes of it; each ResBlock's first residual
-// update reads xb and writes its own stream, so xb is not copied three times.
-__global__ void k_fanout(const float* x, const float* __restrict__ src, long long n, int C, float* xb,
+// update reads xb and writes its own stream, so xb is not copied three times.  split: the Snakes as [hi | lo] rows of
+// 2 C floats (the split-form convs' input).
+__global__ void k_fanout(const float* x, const float* __restrict__ src, long long n, int C, int split, float* xb,
                          float* a0, float* a1, float* a2, const Snake3 sn) {
   pdl_wait();
   pdl_launch();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
+    const long long r = i / C;
+    const int c = (int)(i - r * C);
     const float v = x[i] + src[i];
     xb[i] = v;
-    a0[i] = snake(v, sn.al[0][c], sn.inv[0][c]);
-    a1[i] = snake(v, sn.al[1][c], sn.inv[1][c]);
-    a2[i] = snake(v, sn.al[2][c], sn.inv[2][c]);
+    float* const a[3] = {a0, a1, a2};
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const float y = snake(v, sn.al[k][c], sn.inv[k][c]);
+      if (split) {
+        const float hi = tf32_rn(y);
+        a[k][r * 2 * C + c] = hi;
+        a[k][r * 2 * C + C + c] = tf32_rn(y - hi);
+      } else {
+        a[k][i] = y;
+      }
+    }
   }
 }
 
@@ -359,8 +379,9 @@ __global__ void __launch_bounds__(256) k_source(const float* __restrict__ f0, co
 
 // STFT of the source (n_fft 16, hop 4, periodic Hann, center with reflect padding): frame t of the window into stage-2
 // row s2 + t, 9 real parts then 9 imaginary parts.
+// x3: the frame row tripled as [hi 18 | lo 18 | hi 18] (the tensor-core fp32 mode's source_down input).
 __global__ void k_stft(const float* __restrict__ src, const HRow* __restrict__ rows, const float* __restrict__ tw,
-                       float* __restrict__ out, int ld_out, float upscale) {
+                       float* __restrict__ out, int ld_out, float upscale, int x3) {
   pdl_wait();
   pdl_launch();
   const HRow e = rows[blockIdx.y];
@@ -385,8 +406,18 @@ __global__ void k_stft(const float* __restrict__ src, const HRow* __restrict__ r
       re = fmaf(x[k], tw[16 + ((m * k) & 15)], re);   // cos(2 pi m k / 16)
       im = fmaf(-x[k], tw[32 + ((m * k) & 15)], im);  // -sin(2 pi m k / 16)
     }
-    o[m] = re;
-    o[kBins + m] = im;
+    if (x3) {
+      const float hr = tf32_rn(re), hm = tf32_rn(im);
+      o[m] = hr;
+      o[kBins + m] = hm;
+      o[2 * kBins + m] = tf32_rn(re - hr);
+      o[3 * kBins + m] = tf32_rn(im - hm);
+      o[4 * kBins + m] = hr;
+      o[5 * kBins + m] = hm;
+    } else {
+      o[m] = re;
+      o[kBins + m] = im;
+    }
   }
 }
 
@@ -483,6 +514,7 @@ struct HConv {
   float* W = nullptr;  // [Cout][taps][Cin]
   float* b = nullptr;
   int Cin = 0, Cout = 0, k = 0;
+  float* Ws = nullptr;  // split form [Cout][k][W_hi | W_lo | W_hi] (the tensor-core fp32 mode)
 };
 struct HRes {
   HConv c1[3], c2[3];
@@ -500,6 +532,7 @@ struct HStage {
   // kStftLd floats per group row); weights [Cout][taps][roundup(S kStftLd, 32)]
   float* down_tc = nullptr;
   int down_taps = 0, down_q0 = 0;
+  float* down_x3 = nullptr;  // the same over tripled STFT rows [hi | lo | hi] (the tensor-core fp32 mode)
   HRes src, res[3];
 };
 
@@ -515,6 +548,10 @@ struct t2w_hift {
   float* post_ws = nullptr;
   float* post_bs = nullptr;
   int f0_tc = 0, post_tc = 0;  // those layers run on the tensor cores
+  // conv_pre and the first f0 layer over the mel rows tripled [hi | lo | hi] (80 channels: no split form), weights
+  // [Cout][k][W_hi | W_hi | W_lo, padded to a multiple of 32]: fp32-level products on the tensor cores
+  float *pre_x3 = nullptr, *f00_x3 = nullptr;
+  int x3 = 0;  // every convolution on the tensor cores in split form (3xTF32, fp32-level): tf32 = 2
   float* lin_w = nullptr;
   float lin_b = 0.f;
   HStage st[3];
@@ -622,12 +659,14 @@ int split_weights(t2w_hift* h, const HConv& cv, int n_pad, float** W, float** b)
 // (delta = -1), e.s2 = e.s_2 for stage 2 (delta = 0).  Output v reads frames S v + t - pad (t < k), i.e. rows
 // S R + d + t with d = delta - pad, which are group row R + q, frame j of it, for S q + j = d + t: taps q from
 // floor(d / S) to floor((d + k - 1) / S), weight [o][q - q0][j kStftLd + c] = W[o][c][S q + j - d].
-int grouped_down(t2w_hift* h, HStage& g, int s) {
+// x3: over the tripled STFT rows (kStftLd3 floats a frame), the frame's weights [W_hi | W_hi | W_lo].
+int grouped_down(t2w_hift* h, HStage& g, int s, bool x3 = false) {
   const int S = g.down_stride, k = g.down.k, Cin = g.down.Cin, Cout = g.down.Cout;
   const int d = (s == 2 ? 0 : -1) - g.down_pad;
   auto fdiv = [](int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); };
   const int q0 = fdiv(d, S), q1 = fdiv(d + k - 1, S), taps = q1 - q0 + 1;
-  const int cg = S * kStftLd, cp = (cg + 31) / 32 * 32;
+  const int ld = x3 ? kStftLd3 : kStftLd;
+  const int cg = S * ld, cp = (cg + 31) / 32 * 32;
   std::vector<float> w;
   H_TRY(down(g.down.W, (size_t)Cout * k * Cin, w));  // [o][t][c]
   std::vector<float> t((size_t)Cout * taps * cp, 0.f);
@@ -636,12 +675,44 @@ int grouped_down(t2w_hift* h, HStage& g, int s) {
       for (int j = 0; j < S; ++j) {
         const int tap = S * (q0 + qi) + j - d;
         if (tap < 0 || tap >= k) continue;
-        for (int c = 0; c < Cin; ++c)
-          t[((size_t)o * taps + qi) * cp + j * kStftLd + c] = w[((size_t)o * k + tap) * Cin + c];
+        for (int c = 0; c < Cin; ++c) {
+          const float x = w[((size_t)o * k + tap) * Cin + c];
+          float* dd = &t[((size_t)o * taps + qi) * cp + j * ld];
+          if (x3) {
+            const float hi = tf32_rn_host(x);
+            dd[c] = hi;
+            dd[Cin + c] = hi;
+            dd[2 * Cin + c] = tf32_rn_host(x - hi);
+          } else {
+            dd[c] = x;
+          }
+        }
       }
   g.down_taps = taps;
   g.down_q0 = q0;
-  return up(h, t, &g.down_tc);
+  return up(h, t, x3 ? &g.down_x3 : &g.down_tc);
+}
+
+// Weights of a [Cout][k][Cin] conv over rows tripled as [hi | lo | hi] (ld = 3 Cin floats): per tap [W_hi | W_hi |
+// W_lo], padded to a multiple of 32 columns, so a plain TF32 conv over the tripled rows sums hi W_hi + lo W_hi +
+// hi W_lo.
+int x3_weights(t2w_hift* h, const HConv& cv, float** W) {
+  std::vector<float> w;
+  H_TRY(down(cv.W, (size_t)cv.Cout * cv.k * cv.Cin, w));
+  const int cp = (3 * cv.Cin + 31) / 32 * 32;
+  std::vector<float> t((size_t)cv.Cout * cv.k * cp, 0.f);
+  for (int o = 0; o < cv.Cout; ++o)
+    for (int j = 0; j < cv.k; ++j) {
+      float* d = &t[((size_t)o * cv.k + j) * cp];
+      for (int i = 0; i < cv.Cin; ++i) {
+        const float x = w[((size_t)o * cv.k + j) * cv.Cin + i];
+        const float hi = tf32_rn_host(x);
+        d[i] = hi;
+        d[cv.Cin + i] = hi;
+        d[2 * cv.Cin + i] = tf32_rn_host(x - hi);
+      }
+    }
+  return up(h, t, W);
 }
 
 int snake_params(t2w_hift* h, const float* const* a, int C, float** al, float** inv) {
@@ -787,6 +858,23 @@ int create_impl(t2w_hift* h, const float* const* W) {
     for (int l = 1; l < c.f0_layers && h->f0_tc; ++l) H_TRY(split_weights(h, h->f0c[l], fc, &h->f0s[l], nullptr));
     h->post_tc = (c.channels >> 3) % 32 == 0 && kNfft + 2 <= 32;
     if (h->post_tc) H_TRY(split_weights(h, h->post, 32, &h->post_ws, &h->post_bs));
+    if ((3 * c.mel) % 4 == 0) {  // conv_pre and f0 layer 1 over the tripled mel rows
+      H_TRY(x3_weights(h, h->pre, &h->pre_x3));
+      H_TRY(x3_weights(h, h->f0c[0], &h->f00_x3));
+    }
+  }
+  if (h->x3) {  // every stage convolution in split form
+    for (int s = 0; s < 3; ++s) {
+      HStage& g = h->st[s];
+      for (auto& ph : g.phase) H_TRY(split_weights(h, ph, ph.Cout, &ph.Ws, nullptr));
+      H_TRY(grouped_down(h, g, s, true));
+      HRes* rs[4] = {&g.src, &g.res[0], &g.res[1], &g.res[2]};
+      for (HRes* r : rs)
+        for (int d = 0; d < 3; ++d) {
+          H_TRY(split_weights(h, r->c1[d], r->c1[d].Cout, &r->c1[d].Ws, nullptr));
+          H_TRY(split_weights(h, r->c2[d], r->c2[d].Cout, &r->c2[d].Ws, nullptr));
+        }
+    }
   }
   // window (periodic Hann), cos / sin tables of 2 pi k / 16, Hamming cross-fade window (float64, as np.hamming)
   std::vector<float> tw(48);
@@ -930,6 +1018,7 @@ int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int
   if (!cfg || !weights || !out || n_streams <= 0 || n_streams > 2047 || max_frames < kMelCache + 1 || max_frames > 4096)
     return T2W_ERR_INVALID;
   const t2w_hift_config& c = *cfg;
+  if (c.tf32 < 0 || c.tf32 > 2) return T2W_ERR_INVALID;
   if (c.mel <= 0 || c.channels % 64 || c.channels < 64 || c.f0_layers < 1 || c.f0_layers > 8 || c.harmonics + 1 > kMaxHarm ||
       c.n_fft != kNfft || c.hop != kHop || c.up_rates[0] * c.up_rates[1] * c.up_rates[2] * kHop != 480 ||
       c.up_rates[0] != 8 || c.up_rates[1] != 5 || c.up_rates[2] != 3)
@@ -950,7 +1039,8 @@ int t2w_hift_create(const t2w_hift_config* cfg, const float* const* weights, int
   h->device = dev;
   h->n_streams = n_streams;
   h->max_frames = max_frames;
-  h->tc_parts = c.tf32 ? (c.tf32_parts ? (c.tf32_parts & 0x1FFu) : 0x1FFu) : 0u;
+  h->x3 = c.tf32 == 2;
+  h->tc_parts = h->x3 ? 0x1FFu : c.tf32 ? (c.tf32_parts ? (c.tf32_parts & 0x1FFu) : 0x1FFu) : 0u;
   h->tf32 = h->tc_parts != 0;
   const int rc = create_impl(h, weights);
   if (rc) {
@@ -1058,17 +1148,23 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   const size_t o_f0a = add((size_t)pl.A[0] * c.f0_channels * 8), o_f0b = add((size_t)pl.A[0] * c.f0_channels * 8);
   const size_t o_f0 = add((size_t)pl.A[0] * 4);
   const size_t o_src = add((size_t)pl.samples * 4), o_sp = add((size_t)pl.samples * 4);
-  const size_t o_stft = add((size_t)pl.A[3] * kStftLd * 4);
-  const size_t o_x0 = add((size_t)pl.A[0] * C0 * 4);
+  const int fc = c.f0_channels;
+  auto tc_n = [](int N) { return N % 128 == 0 || N == 64 || N == 32; };  // widths the tensor-core conv takes
+  const bool pre_tc = h->pre_x3 && tc_n(C0), f00_tc = h->f00_x3 && tc_n(fc);
+  const size_t o_mel3 = (pre_tc || f00_tc) ? add((size_t)pl.A[0] * 3 * c.mel * 4) : 0;
+  const int stft_ld = h->x3 ? kStftLd3 : kStftLd;
+  const size_t o_stft = add((size_t)pl.A[3] * stft_ld * 4);
+  const int xsm = h->x3 ? 2 : 1;  // the fp32 tensor-core mode keeps conv inputs as [hi | lo] pairs: twice the floats
+  const size_t o_x0 = add((size_t)pl.A[0] * C0 * 4 * xsm);
   // per stage: x (ups output), xr[3] ResBlock streams, ar[3] / sd scratch of the stage's size
   size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3];
   for (int s = 0; s < 3; ++s) {
     const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
     o_xs[s] = add(sz);
     for (int j = 0; j < 3; ++j) o_xr[s][j] = add(sz);
-    for (int j = 0; j < 3; ++j) o_ar[s][j] = add(sz);
-    o_sd[s] = add(sz);
-    o_ta[s] = add(sz);
+    for (int j = 0; j < 3; ++j) o_ar[s][j] = add(sz * xsm);
+    o_sd[s] = add(sz * xsm);
+    o_ta[s] = add(sz * xsm);
   }
   const int post_ld = h->post_tc ? 32 : kNfft + 2;  // conv_post's output (18 columns; 32 on the tensor cores)
   const size_t o_post = add((size_t)pl.A[3] * post_ld * 4);
@@ -1137,7 +1233,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     // (the parts on CUDA cores write data rows only; with some part on the tensor cores, whose tensor maps read
     // padding rows, the ResBlock streams of a CUDA-core ResBlock part too, as the average of them feeds the next stage)
     if (h->tc_parts & 0x92u)
-      zero(o_stft, (size_t)pl.A[3] * kStftLd * 4);  // the source_down tensor maps read padding rows and channels
+      zero(o_stft, (size_t)pl.A[3] * stft_ld * 4);  // the source_down tensor maps read padding rows and channels
+    if (o_mel3) zero(o_mel3, (size_t)pl.A[0] * 3 * c.mel * 4);
     for (int s = 0; s < 3; ++s) {
       const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
       if (!(h->tc_parts >> (3 * s + 1) & 1u)) {
@@ -1194,22 +1291,41 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   // 1. mel rows
   {
     dim3 grid(h->max_frames, n);
-    rc = ck(launch_k(k_mel_in, grid, dim3(128), 0, st, b->mel, drows, (const float*)h->cache, h->cache_ld, c.mel, mel));
+    rc = ck(launch_k(k_mel_in, grid, dim3(128), 0, st, b->mel, drows, (const float*)h->cache, h->cache_ld, c.mel, mel,
+                     o_mel3 ? reinterpret_cast<float*>(P(o_mel3)) : nullptr));
     if (rc) return fail(rc);
   }
-  // 2. f0 predictor: convs + ELU, then |linear|.  On the tensor cores (split form, fp32-level accuracy) every layer
-  // after the first: the first (80 mel channels) writes its ELU output as [hi | lo] pairs, the middle layers read and
-  // write pairs, the last writes plain fp32 for the head.
+  // 2. f0 predictor: convs + ELU, then |linear|.  On the tensor cores (fp32-level accuracy): the first layer over the
+  // tripled mel rows (80 channels), the others in split form; the first writes its ELU output as [hi | lo] pairs, the
+  // middle layers read and write pairs, the last writes plain fp32 for the head.
+  const uint8_t* pad0 = reinterpret_cast<const uint8_t*>(P(o_pad[0]));
   {
     float* a = reinterpret_cast<float*>(P(o_f0a));
     float* bb = reinterpret_cast<float*>(P(o_f0b));
     const float* in = mel;
-    const int fc = c.f0_channels;
-    const uint8_t* pad0 = reinterpret_cast<const uint8_t*>(P(o_pad[0]));
     for (int l = 0; l < h->f0_layers; ++l) {
       float* o = (l & 1) ? bb : a;
       const bool split_out = h->f0_tc && l + 1 < h->f0_layers;
-      if (l == 0 || !h->f0_tc) {
+      if (l == 0 && f00_tc) {
+        TConvArgs t;
+        t.A = reinterpret_cast<const float*>(P(o_mel3));
+        t.lda = 3 * c.mel;
+        t.rows_a = pl.A[0];
+        t.W = h->f00_x3;
+        t.bias = h->f0c[0].b;
+        t.M = pl.A[0];
+        t.N = fc;
+        t.Cin = 3 * c.mel;
+        t.taps = 3;
+        t.tap_row0 = -1;
+        t.out = o;
+        t.ldo = split_out ? 2 * fc : fc;
+        t.pad = pad0;
+        t.epi = TCONV_ELU;
+        t.split_out = split_out;
+        t.err = h->err;
+        rc = launch_tconv(t, st);
+      } else if (l == 0 || !h->f0_tc) {
         ConvGeo cg = geo(h->f0c[l], vm, pl.vs_mel[n], sm, lm, sm, in, o, split_out ? HE_ELU_SPLIT : HE_ELU);
         if (split_out) cg.ld_out = 2 * fc;
         rc = run(cg);
@@ -1252,12 +1368,34 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      (const float*)h->cache, h->cache_ld, kMelCache * c.mel, src));
     if (rc) return fail(rc);
     dim3 grid((120 * h->max_frames + 1 + 127) / 128, n);
-    rc = ck(launch_k(k_stft, grid, dim3(128), 0, st, (const float*)src, drows, (const float*)h->tw, stft, kStftLd, 480.f));
+    rc = ck(launch_k(k_stft, grid, dim3(128), 0, st, (const float*)src, drows, (const float*)h->tw, stft, stft_ld, 480.f,
+                     h->x3));
     if (rc) return fail(rc);
   }
   // 5. conv_pre
   float* x = reinterpret_cast<float*>(P(o_x0));
-  {
+  if (pre_tc) {  // over the tripled mel rows: fp32-level products on the tensor cores; the fp32 mode writes pairs
+    TConvArgs t;
+    t.A = reinterpret_cast<const float*>(P(o_mel3));
+    t.lda = 3 * c.mel;
+    t.rows_a = pl.A[0];
+    t.W = h->pre_x3;
+    t.bias = h->pre.b;
+    t.M = pl.A[0];
+    t.N = C0;
+    t.Cin = 3 * c.mel;
+    t.taps = h->pre.k;
+    t.tap_row0 = -(h->pre.k / 2);
+    t.out = x;
+    t.ldo = (long long)C0 * xsm;
+    t.pad = pad0;
+    t.epi = TCONV_LEAKY;  // stage 0's leaky_relu fused
+    t.slope = c.lrelu_slope;
+    t.split_out = h->x3;
+    t.err = h->err;
+    rc = launch_tconv(t, st);
+    if (rc) return fail(rc);
+  } else {
     ConvGeo cg = geo(h->pre, vm, pl.vs_mel[n], sm, lm, sm, mel, x, HE_LEAKY);  // stage 0's leaky_relu fused
     cg.slope = c.lrelu_slope;
     rc = run(cg);
@@ -1284,9 +1422,10 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       if (ups_tc) {
         TConvArgs t;
         t.A = x;
-        t.lda = g.Cin;
+        t.lda = g.Cin * xsm;
         t.rows_a = pl.A[s];
-        t.W = g.phase[p].W;
+        t.W = h->x3 ? g.phase[p].Ws : g.phase[p].W;
+        t.split_in = h->x3;
         t.bias = g.b;
         t.M = pl.A[s];
         t.N = g.Cout;
@@ -1321,13 +1460,13 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       const int S = g.down_stride;
       TConvArgs t;
       t.A = stft;  // viewed as rows of S frames
-      t.lda = S * kStftLd;
+      t.lda = S * stft_ld;
       t.rows_a = pl.A[3] / S;
-      t.W = g.down_tc;
+      t.W = h->x3 ? g.down_x3 : g.down_tc;
       t.bias = g.down.b;
       t.M = pl.A[s + 1];
       t.N = Cs;
-      t.Cin = S * kStftLd;
+      t.Cin = S * stft_ld;
       t.taps = g.down_taps;
       t.tap_row0 = g.down_q0;
       t.out = sd;
@@ -1336,6 +1475,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       t.alpha = g.src.a1;  // the source ResBlock's first Snake of the branch, written beside it
       t.inv = g.src.i1;
       t.out2 = ta;
+      t.split_out2 = h->x3;
+      t.ldo2 = (long long)Cs * xsm;
       t.err = h->err;
       rc = launch_tconv(t, st);
       if (rc) return fail(rc);
@@ -1368,9 +1509,14 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
           t.ldo = Cs;
           t.pad = reinterpret_cast<const uint8_t*>(P(o_pad[s + 1]));
           t.err = h->err;
+          // the fp32 tensor-core mode: the Snake outputs (conv inputs) as [hi | lo] pairs, the convs in split form
+          t.lda = Cs * xsm;
+          t.split_in = h->x3;
           TConvArgs t1 = t;
           t1.A = a_in;
-          t1.W = r.c1[dd].W;
+          t1.W = h->x3 ? r.c1[dd].Ws : r.c1[dd].W;
+          t1.ldo = (long long)Cs * xsm;
+          t1.split_out = h->x3;
           t1.bias = r.c1[dd].b;
           t1.tap_row0 = -(r.k * dl - dl) / 2;
           t1.dil = dl;
@@ -1381,7 +1527,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
           H_TRY(launch_tconv(t1, st));
           TConvArgs t2 = t;
           t2.A = tmp;
-          t2.W = r.c2[dd].W;
+          t2.W = h->x3 ? r.c2[dd].Ws : r.c2[dd].W;
           t2.bias = r.c2[dd].b;
           t2.tap_row0 = -(r.k - 1) / 2;
           t2.out = xr;
@@ -1391,6 +1537,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
             t2.alpha = r.a1 + (dd + 1) * Cs;
             t2.inv = r.i1 + (dd + 1) * Cs;
             t2.out2 = a_in;
+            t2.split_out2 = h->x3;
+            t2.ldo2 = (long long)Cs * xsm;
           }
           H_TRY(launch_tconv(t2, st));
           continue;
@@ -1413,7 +1561,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       }
       return T2W_OK;
     };
-    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_xr[s][0])), nullptr, src_tc);  // xr[0]: scratch
+    rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_ar[s][0])), nullptr, src_tc);  // ar[0]: scratch
     if (rc) return fail(rc);
     float* xr[3] = {reinterpret_cast<float*>(P(o_xr[s][0])), reinterpret_cast<float*>(P(o_xr[s][1])),
                     reinterpret_cast<float*>(P(o_xr[s][2]))};
@@ -1425,8 +1573,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       sn.al[j] = g.res[j].a1;
       sn.inv[j] = g.res[j].i1;
     }
-    rc = ck(launch_k(k_fanout, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs, xs,
-                     ar[0], ar[1], ar[2], sn));
+    rc = ck(launch_k(k_fanout, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs,
+                     h->x3, xs, ar[0], ar[1], ar[2], sn));
     if (rc) return fail(rc);
     for (int j = 0; j < 3; ++j) {
       rc = resblock(g.res[j], xr[j], ar[j], ta, xs, res_tc);
@@ -1434,7 +1582,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     }
     // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before
     // the next stage's transposed conv, leaky_relu(., 0.01) before conv_post
-    const int split = s == 2 && h->post_tc;  // conv_post on the tensor cores reads [hi | lo] pairs
+    // conv_post on the tensor cores, and every transposed conv of the fp32 tensor-core mode, read [hi | lo] pairs
+    const int split = (s == 2 && h->post_tc) || (s < 2 && h->x3);
     float* nx = reinterpret_cast<float*>(P(split ? o_xps : o_sd[s]));
     rc = ck(launch_k(k_avg3, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xr[0], (const float*)xr[1],
                      (const float*)xr[2], nel, Cs, split, s < 2 ? c.lrelu_slope : 0.01f, nx));

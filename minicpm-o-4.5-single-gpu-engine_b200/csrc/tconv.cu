@@ -93,7 +93,9 @@ struct TCfgU {
 
 struct TDev {
   int M, N, Cin, taps, tap_row0, dil, tiles_n, num_tiles;
-  int split_in, split_out;
+  int split_in, split_out, split_out2;
+  float slope;  // TCONV_LEAKY
+  long long ldo2;
   int urows;  // tap-reuse form: rows of the A box (0: one 128-row A box per tap)
   const float* bias;
   float* out;
@@ -146,6 +148,16 @@ __device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int c) {
 // fp32 rounded to the nearest TF32 value (half of the dropped unit added to the bit pattern, then the 13 low mantissa
 // bits cleared): a split x = hi + lo with hi = tf32_rn(x), lo = tf32_rn(x - hi) leaves |x - hi - lo| <= 2^-24 |x|.
 __device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
+// Four outputs j of a row chunk: plain, or as the split form's [hi | lo] pair (the lo part n columns to the right).
+__device__ __forceinline__ void store4(float* row, int j, float4 y, bool split, int n) {
+  if (split) {
+    const float4 hi = make_float4(tf32_rn(y.x), tf32_rn(y.y), tf32_rn(y.z), tf32_rn(y.w));
+    reinterpret_cast<float4*>(row + n)[j] =
+        make_float4(tf32_rn(y.x - hi.x), tf32_rn(y.y - hi.y), tf32_rn(y.z - hi.z), tf32_rn(y.w - hi.w));
+    y = hi;
+  }
+  reinterpret_cast<float4*>(row)[j] = y;
+}
 
 template <int BN, bool UNION, int MH, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ CUtensorMap tmA,
@@ -408,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
             load_resid(c0 + 4 * kEC, r0);  // this half's next chunk
           else if (h + 1 < MH)
             load_resid(n0 + kEC * grp, r0 + kTBM);  // the next half's first chunk
-          float* dst2 = p.has_out2 ? p.out2 + orow * p.ldo + c0 : nullptr;
+          float* dst2 = p.has_out2 ? p.out2 + orow * p.ldo2 + c0 : nullptr;
           if (!live && p.resid_oop) {  // a padding row of an out-of-place update: the residual's (zero) row
 #pragma unroll
             for (int j = 0; j < kEC / 4; ++j) reinterpret_cast<float4*>(dst)[j] = xb[j];
@@ -423,9 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
             if (dst2) {
               const float4 a = __ldg(reinterpret_cast<const float4*>(p.alpha + c0) + j);
               const float4 iv = __ldg(reinterpret_cast<const float4*>(p.inv + c0) + j);
-              reinterpret_cast<float4*>(dst2)[j] =
-                  make_float4(snake_f(y.x, a.x, iv.x), snake_f(y.y, a.y, iv.y), snake_f(y.z, a.z, iv.z),
-                              snake_f(y.w, a.w, iv.w));
+              store4(dst2, j,
+                     make_float4(snake_f(y.x, a.x, iv.x), snake_f(y.y, a.y, iv.y), snake_f(y.z, a.z, iv.z),
+                                 snake_f(y.w, a.w, iv.w)),
+                     p.split_out2, p.N);
             }
           }
         } else {
@@ -449,16 +462,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tconv(const __grid_constant__ C
               } else if (p.epi == TCONV_ELU) {
                 y = make_float4(y.x > 0.f ? y.x : expm1f(y.x), y.y > 0.f ? y.y : expm1f(y.y),
                                 y.z > 0.f ? y.z : expm1f(y.z), y.w > 0.f ? y.w : expm1f(y.w));
+              } else if (p.epi == TCONV_LEAKY) {
+                y = make_float4(y.x > 0.f ? y.x : y.x * p.slope, y.y > 0.f ? y.y : y.y * p.slope,
+                                y.z > 0.f ? y.z : y.z * p.slope, y.w > 0.f ? y.w : y.w * p.slope);
               }
             }
-            if (p.split_out) {  // [hi | lo]: the lo half N columns to the right
-              const float4 hi = make_float4(tf32_rn(y.x), tf32_rn(y.y), tf32_rn(y.z), tf32_rn(y.w));
-              reinterpret_cast<float4*>(dst + p.N)[j] =
-                  make_float4(tf32_rn(y.x - hi.x), tf32_rn(y.y - hi.y), tf32_rn(y.z - hi.z), tf32_rn(y.w - hi.w));
-              y = hi;
-            }
-            reinterpret_cast<float4*>(dst)[j] = y;
-            if (p.has_out2) reinterpret_cast<float4*>(p.out2 + orow * p.ldo + c0)[j] = z;
+            store4(dst, j, y, p.split_out, p.N);
+            if (p.has_out2) store4(p.out2 + orow * p.ldo2 + c0, j, z, p.split_out2, p.N);
           }
         }
       }
@@ -505,6 +515,9 @@ int launch_impl(const TConvArgs& a, cudaStream_t st) {
   p.num_tiles = (a.M / (kTBM * MH)) * p.tiles_n;
   p.split_in = a.split_in;
   p.split_out = a.split_out;
+  p.split_out2 = a.split_out2;
+  p.slope = a.slope;
+  p.ldo2 = a.ldo2 ? a.ldo2 : a.ldo;
   p.urows = urows;
   p.bias = a.bias;
   p.out = a.out;
@@ -535,9 +548,10 @@ int launch_tconv(const TConvArgs& a, cudaStream_t st) {
       (a.split_in && a.Cin % kTBK) ||
       a.taps < 1 || a.rows_a <= 0 || a.lda < a.Cin * (a.split_in ? 2 : 1) || a.lda % 4 || a.ldo % 4 ||
       a.ldo < (long long)a.N * (a.split_out ? 2 : 1) || a.row_mul < 1 || a.row_add < 0 || a.row_add >= a.row_mul ||
-      a.epi < TCONV_BIAS || a.epi > TCONV_ELU || (a.epi == TCONV_SNAKE && (!a.alpha || !a.inv)) ||
-      (a.out2 && ((a.epi != TCONV_RESID && a.epi != TCONV_BIAS) || a.split_out || !a.alpha || !a.inv)) ||
-      (a.split_out && (a.epi == TCONV_RESID || a.epi == TCONV_SNAKE)) ||
+      a.epi < TCONV_BIAS || a.epi > TCONV_LEAKY || (a.epi == TCONV_SNAKE && (!a.alpha || !a.inv)) ||
+      (a.out2 && ((a.epi != TCONV_RESID && a.epi != TCONV_BIAS) || !a.alpha || !a.inv)) ||
+      (a.split_out && a.epi == TCONV_RESID) || (a.split_out2 && !a.out2) || a.ldo2 % 4 ||
+      (a.out2 && (a.ldo2 ? a.ldo2 : a.ldo) < (long long)a.N * (a.split_out2 ? 2 : 1)) ||
       (reinterpret_cast<uintptr_t>(a.out) & 15) || (a.out2 && (reinterpret_cast<uintptr_t>(a.out2) & 15)) ||
       (a.resid_in && (a.epi != TCONV_RESID || (reinterpret_cast<uintptr_t>(a.resid_in) & 15))) ||
       (reinterpret_cast<uintptr_t>(a.bias) & 15))
@@ -548,8 +562,7 @@ int launch_tconv(const TConvArgs& a, cudaStream_t st) {
   const bool u = !a.split_in && ext <= ua_rows<1>();
   const bool u2 = u && ext <= ua_rows<2>() && a.M % (2 * kTBM) == 0;
   if (a.split_in && ext <= ua_rows<1, true>()) {  // the split form's tap-reuse path (tiles of up to 128 columns)
-    if (a.N % 128 == 0 && !(a.N >= 256 && (long long)(a.M / kTBM) * (a.N / 256) >= num_sms()))
-      return launch_impl<128, true, 1, true>(a, st);
+    if (a.N % 128 == 0) return launch_impl<128, true, 1, true>(a, st);
     if (a.N == 64) return launch_impl<64, true, 1, true>(a, st);
     if (a.N == 32) return launch_impl<32, true, 1, true>(a, st);
   }

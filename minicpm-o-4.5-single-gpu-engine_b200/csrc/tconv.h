@@ -6,7 +6,7 @@
 
 namespace t2w {
 
-enum { TCONV_BIAS = 0, TCONV_SNAKE = 1, TCONV_RESID = 2, TCONV_ELU = 3 };
+enum { TCONV_BIAS = 0, TCONV_SNAKE = 1, TCONV_RESID = 2, TCONV_ELU = 3, TCONV_LEAKY = 4 };
 
 // out[row_mul m + row_add, n] (ldo floats per row) = epilogue(bias[n] + sum_tap sum_c A[m + tap_row0 + tap dil, c]
 // W[n, tap Cp + c]) for m < M (M % 128 == 0), rows whose pad[row_mul m + row_add] != 0 zero (bias, snake, elu) or
@@ -16,8 +16,8 @@ enum { TCONV_BIAS = 0, TCONV_SNAKE = 1, TCONV_RESID = 2, TCONV_ELU = 3 };
 //
 // split_in (3xTF32, fp32-level accuracy; Cin % 32 == 0): A holds [hi | lo] (2 Cin floats per row: hi = a rounded to TF32, lo = a - hi
 // rounded to TF32) and W per tap [W_hi | W_lo | W_hi] (3 Cin columns per tap), so the sum is
-// hi W_hi + hi W_lo + lo W_hi.  split_out: the epilogue writes the output in that [hi | lo] form (2 N columns; bias /
-// elu only).
+// hi W_hi + hi W_lo + lo W_hi.  split_out: the epilogue writes the output in that [hi | lo] form (2 N columns; not the
+// residual update, whose stream stays plain); split_out2 the same for out2 (row stride ldo2, 0: ldo).
 struct TConvArgs {
   const float* A = nullptr;
   int lda = 0, rows_a = 0;
@@ -33,7 +33,9 @@ struct TConvArgs {
   const float* inv = nullptr;
   float* out2 = nullptr;
   const float* resid_in = nullptr;  // TCONV_RESID: out = resid_in + bias + conv (padding rows copied), else out in place
-  int split_in = 0, split_out = 0;
+  int split_in = 0, split_out = 0, split_out2 = 0;
+  long long ldo2 = 0;
+  float slope = 0.f;  // TCONV_LEAKY: the negative-side slope
   int* err = nullptr;
 };
 int launch_tconv(const TConvArgs& a, cudaStream_t st);

@@ -166,3 +166,33 @@ def test_tf32_mode_source_is_fp32_accurate():
         e = rel(src[True], src[False])
         print(f"window {c}: source rel-L2 tf32 vs strict {e:.2e}")
         assert e < 1e-3
+
+
+@pytest.mark.parametrize("name,cfg", [("hift_tiny", HIFT_TINY), ("hift_reference", HIFT)])
+def test_split_fp32_mode_vs_reference_driver_golden(golden_dir, name, cfg):
+    """``split_fp32``: every convolution on the tensor cores in split form (3xTF32), the reference's strict-fp32
+    numerics (its default) at tensor-core speed.  Against the reference driver's fp32 golden fixtures, calls mixing
+    first, steady and final windows: measured 1.4e-5 (tiny) / 2.1e-4 (reference config), bound 5e-4 — against the TF32
+    mode's 8e-4 / 1.6e-3 and the CUDA-core strict mode's 3e-6 / 1e-5; most of it is the f0 predictor's split-form
+    rounding (1e-5 a layer) carried into the source's phase."""
+    rec = torch.load(os.path.join(golden_dir, f"{name}.pt"))
+    hift = ho.build_hift(cfg, seed=0)
+    voc = B200HiFT.from_module(hift, cfg, device="cuda", max_frames=128, n_streams=8, split_fp32=True)
+    hs = [voc.new_stream(s) for s in rec["noise_seeds"]]
+    chunks = [0, 0, 0]
+    worst = 0.0
+    for call in rec["calls"]:
+        noise = []
+        for w in call:
+            i = w["stream"]
+            F = w["mel"].shape[1] + (0 if chunks[i] == 0 else 8)
+            noise.append(oracle_noise(hift, chunk_noise_seed(rec["noise_seeds"][i], chunks[i]), F))
+            chunks[i] += 1
+        outs = voc.vocode([hs[w["stream"]] for w in call], [w["mel"] for w in call], [w["last"] for w in call],
+                          noise=noise)
+        for w, o in zip(call, outs):
+            e = rel(o, w["samples"])
+            worst = max(worst, e)
+            assert o.numel() == w["samples"].numel() and e < 5e-4, e
+    print(f"{name} split_fp32: worst window rel-L2 {worst:.2e}")
+    voc.check()

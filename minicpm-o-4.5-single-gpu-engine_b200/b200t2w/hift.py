@@ -129,6 +129,15 @@ class B200HiFT:
     def from_module(cls, hift, cfg: HiFTConfig = HIFT, **kw) -> "B200HiFT":
         return cls(cfg, {k: v.detach().float() for k, v in hift.state_dict().items()}, **kw)
 
+    @classmethod
+    def for_decode_tf32(cls, hift, decode_tf32=False, cfg: HiFTConfig = HIFT, **kw) -> "B200HiFT":
+        """The vocoder for a reference config's ``t2w_hift_decode_tf32`` value (engine/runtime/t2w_worker.py:654,
+        ``BatchedToken2Wav(hift_decode_tf32=...)``): False / None — the reference's strict fp32 — gives the split-form
+        fp32 mode on the tensor cores; True or a list of stages / ``"<stage>:<part>"`` the same TF32 parts."""
+        if not decode_tf32:
+            return cls.from_module(hift, cfg, split_fp32=True, **kw)
+        return cls.from_module(hift, cfg, tf32=decode_tf32, **kw)
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             self.lib.t2w_hift_destroy(self.handle)

@@ -27,3 +27,26 @@ def test_stage_and_part_entries():
 def test_rejects_unknown_entries(bad):
     with pytest.raises((ValueError, AssertionError)):
         tf32_parts(bad)
+
+
+def test_decode_tf32_config_to_vocoder_mode():
+    """``B200HiFT.for_decode_tf32``: the reference's default (False / None, strict fp32) maps to the split-form fp32
+    mode on the tensor cores, True and stage lists to the same TF32 parts (checked without a GPU: the constructor's
+    arguments are recorded)."""
+    import torch
+
+    from b200t2w.hift import B200HiFT
+
+    calls = []
+
+    class Rec(B200HiFT):
+        def __init__(self, cfg, weights, **kw):
+            calls.append(kw)
+
+        def __del__(self):
+            pass
+
+    m = torch.nn.Linear(2, 2)
+    for v in (False, None, True, [1, "0:src"]):
+        Rec.for_decode_tf32(m, v)
+    assert calls == [{"split_fp32": True}, {"split_fp32": True}, {"tf32": True}, {"tf32": [1, "0:src"]}]

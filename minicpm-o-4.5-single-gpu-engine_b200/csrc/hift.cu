@@ -99,6 +99,17 @@ __device__ __forceinline__ int stream_of(const int* __restrict__ vstart, int n, 
 // bits cleared); a value's split form for the tensor-core convolution is hi = tf32_rn(x), lo = tf32_rn(x - hi).
 __device__ __forceinline__ float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
 
+// Snake with the sine of the tensor-core paths: the argument reduced to [-pi, pi] with 2 pi split into two floats
+// (Cody-Waite), then the hardware approximation __sinf (about 2^-21 absolute there), as the convolution epilogues do.
+__device__ __forceinline__ float snake_fast(float x, float a, float inv) {
+  const float xa = x * a;
+  const float nn = rintf(xa * 0.159154943091895336f);
+  float r = fmaf(-nn, 6.28318548202514648f, xa);
+  r = fmaf(-nn, -1.74845553146951715e-07f, r);
+  const float sv = __sinf(r);
+  return x + inv * (sv * sv);
+}
+
 __device__ __forceinline__ float snake(float x, float a, float inv) {
   const float s = sinf(x * a);
   return x + inv * (s * s);
@@ -241,48 +252,71 @@ struct Snake3 {
   const float *al[3], *inv[3];
 };
 // xb = ups(x) + source branch (every row), the three ResBlocks' first Snakes of it; each ResBlock's first residual
-// update reads xb and writes its own stream, so xb is not copied three times.  split: the Snakes as [hi | lo] rows of
-// 2 C floats (the split-form convs' input).
-__global__ void k_fanout(const float* x, const float* __restrict__ src, long long n, int C, int split, float* xb,
-                         float* a0, float* a1, float* a2, const Snake3 sn) {
+// update reads xb and writes its own stream, so xb is not copied three times.  Four consecutive channels per thread
+// (C % 4 == 0).  split: the Snakes as [hi | lo] rows of 2 C floats (the split-form convs' input).  fast: the Snakes'
+// sine as on the tensor-core paths (snake_fast), else sinf.
+__global__ void k_fanout(const float* x, const float* __restrict__ src, long long n, int C, int split, int fast,
+                         float* xb, float* a0, float* a1, float* a2, const Snake3 sn) {
   pdl_wait();
   pdl_launch();
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / C;
+  const long long n4 = n >> 2;
+  for (long long i4 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i4 < n4; i4 += (long long)gridDim.x * blockDim.x) {
+    const long long i = i4 << 2, r = i / C;
     const int c = (int)(i - r * C);
-    const float v = x[i] + src[i];
-    xb[i] = v;
+    const float4 xv = reinterpret_cast<const float4*>(x)[i4], sv = reinterpret_cast<const float4*>(src)[i4];
+    const float v[4] = {xv.x + sv.x, xv.y + sv.y, xv.z + sv.z, xv.w + sv.w};
+    reinterpret_cast<float4*>(xb)[i4] = make_float4(v[0], v[1], v[2], v[3]);
     float* const a[3] = {a0, a1, a2};
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      const float y = snake(v, sn.al[k][c], sn.inv[k][c]);
+      const float4 al = *reinterpret_cast<const float4*>(sn.al[k] + c);
+      const float4 iv = *reinterpret_cast<const float4*>(sn.inv[k] + c);
+      const float alv[4] = {al.x, al.y, al.z, al.w}, ivv[4] = {iv.x, iv.y, iv.z, iv.w};
+      float y[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) y[q] = fast ? snake_fast(v[q], alv[q], ivv[q]) : snake(v[q], alv[q], ivv[q]);
       if (split) {
-        const float hi = tf32_rn(y);
-        a[k][r * 2 * C + c] = hi;
-        a[k][r * 2 * C + C + c] = tf32_rn(y - hi);
+        float hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          hi[q] = tf32_rn(y[q]);
+          lo[q] = tf32_rn(y[q] - hi[q]);
+        }
+        *reinterpret_cast<float4*>(a[k] + r * 2 * C + c) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(a[k] + r * 2 * C + C + c) = make_float4(lo[0], lo[1], lo[2], lo[3]);
       } else {
-        a[k][i] = y;
+        *reinterpret_cast<float4*>(a[k] + i) = make_float4(y[0], y[1], y[2], y[3]);
       }
     }
   }
 }
 
-// y = leaky_relu((x0 + x1 + x2) / 3, slope)
+// y = leaky_relu((x0 + x1 + x2) / 3, slope), four consecutive channels per thread (C % 4 == 0).
 // split: y holds [hi | lo] rows of 2 C floats (the input of a split-form tensor-core conv), else C floats per row.
 __global__ void k_avg3(const float* __restrict__ x0, const float* __restrict__ x1, const float* __restrict__ x2,
                        long long n, int C, int split, float slope, float* __restrict__ y) {
   pdl_wait();
   pdl_launch();
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    float v = ((x0[i] + x1[i]) + x2[i]) / 3.f;
-    v = v > 0.f ? v : v * slope;
+  const long long n4 = n >> 2;
+  for (long long i4 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i4 < n4; i4 += (long long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(x0)[i4], b = reinterpret_cast<const float4*>(x1)[i4],
+                 c3 = reinterpret_cast<const float4*>(x2)[i4];
+    float v[4] = {((a.x + b.x) + c3.x) / 3.f, ((a.y + b.y) + c3.y) / 3.f, ((a.z + b.z) + c3.z) / 3.f,
+                  ((a.w + b.w) + c3.w) / 3.f};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = v[q] > 0.f ? v[q] : v[q] * slope;
     if (split) {
-      const long long r = i / C, c = i - r * C;
-      const float hi = tf32_rn(v);
-      y[r * 2 * C + c] = hi;
-      y[r * 2 * C + C + c] = tf32_rn(v - hi);
+      const long long i = i4 << 2, r = i / C, c = i - r * C;
+      float hi[4], lo[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        hi[q] = tf32_rn(v[q]);
+        lo[q] = tf32_rn(v[q] - hi[q]);
+      }
+      *reinterpret_cast<float4*>(y + r * 2 * C + c) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<float4*>(y + r * 2 * C + C + c) = make_float4(lo[0], lo[1], lo[2], lo[3]);
     } else {
-      y[i] = v;
+      reinterpret_cast<float4*>(y)[i4] = make_float4(v[0], v[1], v[2], v[3]);
     }
   }
 }
@@ -1573,8 +1607,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       sn.al[j] = g.res[j].a1;
       sn.inv[j] = g.res[j].i1;
     }
-    rc = ck(launch_k(k_fanout, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs,
-                     h->x3, xs, ar[0], ar[1], ar[2], sn));
+    rc = ck(launch_k(k_fanout, dim3(grid_for(nel / 4)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs,
+                     h->x3, res_tc ? 1 : 0, xs, ar[0], ar[1], ar[2], sn));
     if (rc) return fail(rc);
     for (int j = 0; j < 3; ++j) {
       rc = resblock(g.res[j], xr[j], ar[j], ta, xs, res_tc);
@@ -1585,7 +1619,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     // conv_post on the tensor cores, and every transposed conv of the fp32 tensor-core mode, read [hi | lo] pairs
     const int split = (s == 2 && h->post_tc) || (s < 2 && h->x3);
     float* nx = reinterpret_cast<float*>(P(split ? o_xps : o_sd[s]));
-    rc = ck(launch_k(k_avg3, dim3(grid_for(nel)), dim3(256), 0, st, (const float*)xr[0], (const float*)xr[1],
+    rc = ck(launch_k(k_avg3, dim3(grid_for(nel / 4)), dim3(256), 0, st, (const float*)xr[0], (const float*)xr[1],
                      (const float*)xr[2], nel, Cs, split, s < 2 ? c.lrelu_slope : 0.01f, nx));
     if (rc) return fail(rc);
     x = nx;

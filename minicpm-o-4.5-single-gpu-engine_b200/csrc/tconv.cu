@@ -1,29 +1,33 @@
 // TF32 tcgen05 implicit-GEMM convolution for the HiFT vocoder: out[m, n] = sum_tap sum_c A[m + tap_row0 + tap * dil, c]
-// W[n, tap * Cin + c].
+// W[n, tap * Cp + c].
 //
 // A is the time-major fp32 activation [rows, Cin] with zero rows around every window's data (the "same" padding), W
-// the fp32 weight [Cout, taps * Cin]; the tensor core reads both as TF32 (kind::tf32, K = 8 per instruction, fp32
+// the fp32 weight [Cout, taps * Cp]; the tensor core reads both as TF32 (kind::tf32, K = 8 per instruction, fp32
 // accumulation in TMEM) — the reference's own reduced-precision option for the upsampling stages (decode_tf32,
-// engine/models/token2wav.py:145-210).  Where the reference keeps fp32 (the f0 predictor, conv_post) the same kernel runs
-// in split form (3xTF32): the operands arrive as hi + lo pairs of TF32-exact values (hi the value rounded to TF32, lo
-// the remainder rounded to TF32) and the K loop runs hi W_hi + hi W_lo + lo W_hi, which leaves the lo x lo term and
-// the pairs' own rounding, about 3 x 2^-24 relative per product: fp32-level accuracy on the tensor core.
+// engine/models/token2wav.py:145-210).  Where fp32 is wanted (the f0 predictor and conv_post in every tensor-core mode,
+// every convolution in the fp32 tensor-core mode) the same kernel runs in split form (3xTF32): the operands arrive as
+// hi + lo pairs of TF32-exact values (hi the value rounded to TF32, lo the remainder rounded to TF32) and the K loop
+// runs hi W_hi + hi W_lo + lo W_hi, which leaves the lo x lo term and the pairs' own rounding, about 3 x 2^-24 relative
+// per product: fp32-level accuracy on the tensor core.
 //
-// One persistent CTA per SM, warp-specialised: warp 0 the TMA producer (128 x 32 A boxes and BN x 32 W boxes, 128-byte
-// swizzle, one box pair per (tap, segment, 32-channel block)), warp 1 the TMEM allocator and single-thread MMA issuer,
-// warps 2-17 the epilogue (TMEM lane quarter w % 4, every fourth 16-column chunk: four warps per quarter, since with two
-// the epilogue's instruction latency, not the MMAs, set the pace of the 1-7-tap convolutions), the accumulator
-// double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.  Each epilogue thread owns one output row
-// (the TMEM lane it reads) and stores its 16-column chunk directly; a residual update first TMA-loads the warp's
+// One persistent CTA per SM, warp-specialised: warp 0 the TMA producer, warp 1 the TMEM allocator and single-thread MMA
+// issuer, warps 2-17 the epilogue (TMEM lane quarter w % 4, every fourth 16-column chunk: four warps per quarter, since
+// with two the epilogue's instruction latency, not the MMAs, set the pace of the 1-7-tap convolutions), the
+// accumulator double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.  Main loop, in one of two
+// forms: tap reuse (the usual one) — one A box per 32-channel block covers every tap's rows and each tap's MMAs read it
+// from a row offset, W streaming per (tap, block) through its own ring, with tiles of two 128-row halves sharing each W
+// box where the halo fits (8 MMAs a step), and the split form's hi / lo boxes where it is used; or one 128 x 32 A box
+// and one BN x 32 W box per (tap, segment, block), 128-byte swizzle throughout.  Each epilogue thread owns one output
+// row (the TMEM lane it reads) and stores its 16-column chunk directly; a residual update first TMA-loads the warp's
 // 32 x 16 block of the residual (out itself, or another buffer of the same layout) into a swizzled shared-memory box
 // (issued before the accumulator is ready) and reads its row from there, instead of 32 scattered row reads per warp.
-// (Staging the outputs through the box and writing them with TMA stores measured slower for the bias and Snake
-// epilogues.)
+// (Staging the outputs through the box, as TMA stores or as 64-byte row segments, measured slower overall.)
 // Output rows: row_mul * m + row_add (a transposed convolution's output phase writes every row_mul-th row of the next
 // rate's layout, a tensor map whose row pitch is row_mul rows); rows flagged in `pad` are window padding and stay zero.
-// Epilogues: bias; Snake(bias + acc) (the ResBlocks' conv1 with its second activation); x += bias + acc with
-// Snake(x_new) into a second buffer (conv2's residual and the next conv1's input); ELU(bias + acc) (the f0 predictor),
-// optionally written as a hi / lo pair for the next split-form layer.  No TMA multicast.
+// Epilogues: bias (optionally with Snake(out) into a second buffer); Snake(bias + acc) (the ResBlocks' conv1); x +=
+// bias + acc with Snake(x_new) into a second buffer (conv2's residual and the next conv1's input; x read from out itself
+// or, out of place, from another buffer); ELU (the f0 predictor); leaky ReLU (conv_pre); outputs and second outputs
+// optionally as hi / lo pairs for a split-form consumer.  No TMA multicast.
 #include <atomic>
 
 #include "common.cuh"

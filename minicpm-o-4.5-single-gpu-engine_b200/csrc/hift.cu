@@ -13,13 +13,16 @@
 // 480] (the reflection-padded row leads stage 2's data).  Every segment length at stage i is its rate times (F + 8), so
 // output row u v + p of a transposed convolution's phase p lands in the next layout at a fixed offset.
 //
-// Precision: strict fp32 everywhere (the reference runs Token2Wav with TF32 off, strict_fp32, token2wav.py:44-57).
-// Convolutions: k_hconv, a tiled fp32 implicit-GEMM kernel (64 output rows x 64 output channels per block, 4 x 4 per
-// thread, 16-channel K chunks staged in shared memory) with a general row mapping — strided (source_downs), dilated
-// (ResBlocks), and the polyphase form of the transposed convolutions (each output phase p of rate u is a convolution
-// over the input with taps j = j0(p) + u q) — and fused epilogues: ELU (f0 predictor), |.| (its head), Snake (the
-// ResBlocks' second activation, applied to conv1's output), and the residual update x += conv2(.) that also writes the
-// next Snake of x for the following conv1.
+// Precision, per the config's tf32 field: 0 strict fp32 on CUDA cores (the reference runs Token2Wav with TF32 off,
+// strict_fp32, token2wav.py:44-57); 1 the reference's decode_tf32 option (all upsampling-stage parts, or the listed
+// ones) on TF32 tensor cores, the f0 predictor, conv_pre and conv_post at fp32 level on the tensor cores (split form,
+// or the mel rows tripled as [hi | lo | hi]); 2 every convolution at fp32 level on the tensor cores.  Tensor-core
+// convolutions: tconv.cu.  CUDA-core convolutions: k_hconv, a tiled fp32 implicit-GEMM kernel (64 output rows x 64
+// output channels per block, 4 x 4 per thread, 16-channel K chunks staged in shared memory) with a general row mapping
+// — strided (source_downs), dilated (ResBlocks), and the polyphase form of the transposed convolutions (each output
+// phase p of rate u is a convolution over the input with taps j = j0(p) + u q) — and fused epilogues: ELU (f0
+// predictor), |.| (its head), Snake (the ResBlocks' second activation, applied to conv1's output), and the residual
+// update x += conv2(.) that also writes the next Snake of x for the following conv1.
 #include <algorithm>
 #include <cmath>
 #include <cstring>

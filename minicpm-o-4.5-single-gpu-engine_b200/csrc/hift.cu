@@ -460,50 +460,77 @@ __global__ void k_stft(const float* __restrict__ src, const HRow* __restrict__ r
 
 // magnitude / phase of conv_post's output -> inverse STFT (per-frame real inverse DFT, window, overlap-add, / the
 // summed squared window, centre trim), clamp; then the cross-fade with the previous window's speech, the caches and the
-// window's output samples.  One thread per sample.
-__global__ void k_istft_out(const float* __restrict__ y, int ld_y, const HRow* __restrict__ rows, const float* __restrict__ tw,
-                            const double* __restrict__ hamming, float audio_limit, float upscale, float* __restrict__ speech,
-                            const float* __restrict__ cache, int cache_ld, int cache_sp_off, float* __restrict__ out) {
+// window's output samples.  A block per 1024 output samples: the bins of the frames they overlap once (exp, sin, the
+// complex value: 4 transcendentals per frame and bin rather than per sample), then the frames' inverse DFT values, then
+// the overlap-add per sample, every sum in the order of the per-sample form.
+constexpr int kIstftChunk = 1024;                                // output samples per block
+constexpr int kIstftFrames = (kIstftChunk + kNfft) / kHop + 2;     // frames a chunk's samples overlap, at most
+__global__ void __launch_bounds__(256) k_istft_out(const float* __restrict__ y, int ld_y, const HRow* __restrict__ rows,
+                                                   const float* __restrict__ tw, const double* __restrict__ hamming,
+                                                   float audio_limit, float upscale, float* __restrict__ speech,
+                                                   const float* __restrict__ cache, int cache_ld, int cache_sp_off,
+                                                   float* __restrict__ out) {
+  __shared__ float spec[kIstftFrames][2 * kBins];  // the chunk's frames: bins as re, im
+  __shared__ float fv[kIstftFrames][kNfft];        // the frames' inverse DFT values (before the window)
   pdl_wait();
   pdl_launch();
   const HRow e = rows[blockIdx.y];
   const int N = e.F * (int)upscale;
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  const int j = n + kNfft / 2;  // position in the overlap-added signal
+  const int n0 = blockIdx.x * kIstftChunk;
+  if (n0 >= N) return;
+  const int n1 = min(N, n0 + kIstftChunk);
   const int T = N / kHop + 1;
-  float acc = 0.f, env = 0.f;
-  for (int t = max(0, (j - kNfft + kHop) / kHop); t <= j / kHop && t < T; ++t) {
-    const int k = j - kHop * t;
-    if (k < 0 || k >= kNfft) continue;
-    const float* row = y + (size_t)(e.s2 + t) * ld_y;
+  // frames t with 0 <= j - hop t < n_fft for some j = n + n_fft / 2 of the chunk
+  const int t_lo = max(0, (n0 + kNfft / 2 - kNfft + kHop) / kHop), t_hi = min(T - 1, (n1 - 1 + kNfft / 2) / kHop);
+  const int nf = t_hi - t_lo + 1;
+  // 1. each frame's bins once: magnitude exp (clipped at 100), phase sin, the complex value
+  for (int i = threadIdx.x; i < nf * kBins; i += blockDim.x) {
+    const int tt = i / kBins, m = i - tt * kBins;
+    const float* row = y + (size_t)(e.s2 + t_lo + tt) * ld_y;
+    const float mag = fminf(expf(row[m]), 100.f);
+    const float ph = sinf(row[kBins + m]);
+    spec[tt][m] = mag * cosf(ph);
+    spec[tt][kBins + m] = mag * sinf(ph);
+  }
+  __syncthreads();
+  // 2. each frame's real inverse DFT at its 16 positions
+  for (int i = threadIdx.x; i < nf * kNfft; i += blockDim.x) {
+    const int tt = i / kNfft, k = i - tt * kNfft;
     float v = 0.f;
 #pragma unroll
     for (int m = 0; m < kBins; ++m) {
-      const float mag = fminf(expf(row[m]), 100.f);
-      const float p = sinf(row[kBins + m]);
-      const float re = mag * cosf(p), im = mag * sinf(p);
-      const float c = tw[16 + ((m * k) & 15)], s = tw[32 + ((m * k) & 15)];
-      const float term = re * c - im * s;
+      const float re = spec[tt][m], im = spec[tt][kBins + m];
+      const float c = tw[16 + ((m * k) & 15)], sn = tw[32 + ((m * k) & 15)];
+      const float term = re * c - im * sn;
       v += (m == 0 || m == kBins - 1) ? ((m == 0) ? re : re * c) : 2.f * term;
     }
-    v *= (1.f / kNfft);
-    acc = fmaf(v, tw[k], acc);
-    env = fmaf(tw[k], tw[k], env);
+    fv[tt][k] = v * (1.f / kNfft);
   }
-  float sp = fminf(fmaxf(acc / env, -audio_limit), audio_limit);
-  const float* cache_row = cache + (size_t)e.cache * cache_ld;
-  if (!e.first && n < kSrcCache)  // cross-fade with the previous window's last speech samples (float64 window)
-    sp = (float)((double)sp * hamming[n] + (double)cache_row[cache_sp_off + n] * hamming[kSrcCache + n]);
-  speech[e.smp0 + n] = sp;
-  // output: held back tail (unless final), leading silence of a first window
-  if (e.last) {
-    out[e.out0 + n] = sp;
-  } else if (e.first) {
-    if (n + kSrcCache < N) out[e.out0 + kSrcCache + n] = sp;
-    if (n < kSrcCache) out[e.out0 + n] = 0.f;
-  } else if (n < N - kSrcCache) {
-    out[e.out0 + n] = sp;
+  __syncthreads();
+  // 3. per sample: overlap-add of its frames through the window, / the summed squared window, clamp
+  for (int n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
+    const int j = n + kNfft / 2;  // position in the overlap-added signal
+    float acc = 0.f, env = 0.f;
+    for (int t = max(0, (j - kNfft + kHop) / kHop); t <= j / kHop && t < T; ++t) {
+      const int k = j - kHop * t;
+      if (k < 0 || k >= kNfft) continue;
+      acc = fmaf(fv[t - t_lo][k], tw[k], acc);
+      env = fmaf(tw[k], tw[k], env);
+    }
+    float sp = fminf(fmaxf(acc / env, -audio_limit), audio_limit);
+    const float* cache_row = cache + (size_t)e.cache * cache_ld;
+    if (!e.first && n < kSrcCache)  // cross-fade with the previous window's last speech samples (float64 window)
+      sp = (float)((double)sp * hamming[n] + (double)cache_row[cache_sp_off + n] * hamming[kSrcCache + n]);
+    speech[e.smp0 + n] = sp;
+    // output: held back tail (unless final), leading silence of a first window
+    if (e.last) {
+      out[e.out0 + n] = sp;
+    } else if (e.first) {
+      if (n + kSrcCache < N) out[e.out0 + kSrcCache + n] = sp;
+      if (n < kSrcCache) out[e.out0 + n] = 0.f;
+    } else if (n < N - kSrcCache) {
+      out[e.out0 + n] = sp;
+    }
   }
 }
 
@@ -1663,7 +1690,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   }
   float* speech = reinterpret_cast<float*>(P(o_sp));
   {
-    dim3 grid((480 * h->max_frames + 255) / 256, n);
+    dim3 grid((480 * h->max_frames + kIstftChunk - 1) / kIstftChunk, n);
     rc = ck(launch_k(k_istft_out, grid, dim3(256), 0, st, (const float*)post, post_ld, drows, (const float*)h->tw,
                      (const double*)h->hamming, c.audio_limit, 480.f, speech, (const float*)h->cache, h->cache_ld,
                      kMelCache * c.mel + kSrcCache, b->out));

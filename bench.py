@@ -682,7 +682,8 @@ def hift_flops(hcfg, F: int) -> float:
     return float(fl)
 
 
-def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float, split_fp32: bool = False) -> dict:
+def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float, split_fp32: bool = False,
+                use_graphs: bool = False) -> dict:
     """The HiFT vocoder (row f4: mel -> 24 kHz waveform) at the reference config, random init, the upsampling stages on
     TF32 tensor cores (the reference's decode_tf32 option; f0 predictor, source, conv_pre / conv_post fp32): ``n``
     streams, every call one 50-frame window per stream (58 frames with the 8 cached ones once the stream has started),
@@ -694,7 +695,7 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float,
 
     g = torch.Generator().manual_seed(seed)
     voc = B200HiFT.from_module(ho.build_hift(HIFT, seed=0), HIFT, device=dev, max_frames=64, n_streams=n,
-                               split_fp32=split_fp32)
+                               split_fp32=split_fp32, use_graphs=use_graphs)
     hs = [voc.new_stream(1000 + i) for i in range(n)]
     T = 50
     mels = [(torch.randn(n * T, HIFT.mel, generator=g) - 2.0).pin_memory() for _ in range(3)]
@@ -706,7 +707,7 @@ def hift_record(dev, n: int, steps: int, warmup: int, seed: int, peak_tf: float,
         flat, _ = voc.vocode_packed(hs, dmel, [T] * n, [False] * n, flat=True)
         host[:flat.numel()].copy_(flat, non_blocking=True)
 
-    for k in range(max(warmup, 2)):
+    for k in range(max(warmup, 3)):
         call(k)
     torch.cuda.synchronize(dev)
     st = torch.cuda.current_stream(dev)

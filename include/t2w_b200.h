@@ -550,6 +550,12 @@ typedef struct t2w_vocode_batch {
   float* out;              /* device [t2w_vocode_samples]: each window's output samples, windows in order */
   float* source;           /* device [sum 480 F_i] or NULL: the windows' source signals */
   float* speech;           /* device [sum 480 F_i] or NULL: the windows' full speech (after the cross-fade) */
+  uint32_t flags;          /* T2W_FLAG_GRAPH: replay a CUDA graph per launch structure (the call's sizes: stream count,
+                            * frames, samples), captured the second time a structure is seen; the mel and noise are
+                            * copied into the graph's own workspace first and the samples out of it after (the
+                            * reference's t2w_graphs option, HiFTGraphs, engine/runtime/hift_graph.py:22-88).  Calls
+                            * replaying one graph must be ordered on the GPU (one stream, or synchronised); a caller
+                            * that is itself capturing passes 0. */
 } t2w_vocode_batch;
 /* Output samples of a call (the sum), per window (per_stream, may be NULL) and each window's frames F_i (frames, may
  * be NULL); -1 on an invalid batch. */
@@ -557,6 +563,8 @@ T2W_API int64_t t2w_vocode_samples(const t2w_hift* h, int32_t n, const int32_t* 
                                    const uint8_t* last, int64_t* per_stream, int32_t* frames);
 /* One window per stream; asynchronous on `stream` (the call's scratch is a stream-ordered allocation). */
 T2W_API int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream);
+/* Counters: graph replays, graph captures, eager calls. */
+T2W_API int t2w_hift_counts(const t2w_hift* h, int64_t* graph_replays, int64_t* graph_captures, int64_t* eager_calls);
 
 /* Test entry: one launch of the vocoder's tensor-core convolution (the kernel behind the tf32 stages and the split-form
  * layers), for numerics tests against a plain fp32 / fp64 convolution.

@@ -83,10 +83,12 @@ class B200HiFT:
     ``"<stage>:<part>"`` entries, ``tf32_parts``); False keeps every convolution in strict fp32 (the reference's
     default) on CUDA cores.  ``split_fp32``: every convolution on the tensor cores in split form instead (operands as
     pairs of TF32 values, hi W_hi + hi W_lo + lo W_hi: fp32-level products, the reference's fp32 numerics at
-    tensor-core speed); ``tf32`` is then ignored."""
+    tensor-core speed); ``tf32`` is then ignored.  ``use_graphs``: each call replays a CUDA graph of its launches per
+    call structure (the reference's ``t2w_graphs`` / ``HiFTGraphs``), captured the second time a structure is seen;
+    calls then have to stay ordered on one stream."""
 
     def __init__(self, cfg: HiFTConfig, weights: dict, device="cuda", max_frames: int = 128, n_streams: int = 256,
-                 tf32=True, split_fp32: bool = False):
+                 tf32=True, split_fp32: bool = False, use_graphs: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -115,6 +117,7 @@ class B200HiFT:
         self.tf32 = bool(mask)
         self.tf32_parts = mask
         self.split_fp32 = bool(split_fp32)
+        self.use_graphs = bool(use_graphs)
         with torch.cuda.device(self.device):
             w = [weights[k].detach().to(self.device, torch.float32).contiguous() for k in names]
             ptrs = (ctypes.c_void_p * len(w))(*[t.data_ptr() for t in w])
@@ -151,6 +154,13 @@ class B200HiFT:
 
     def check(self) -> None:
         L.check("t2w_hift_check", self.lib.t2w_hift_check(self.handle))
+
+    @property
+    def counts(self) -> dict:
+        """Calls so far: graph replays, graph captures, eager calls."""
+        v = [ctypes.c_int64() for _ in range(3)]
+        L.call("t2w_hift_counts", self.handle, *[ctypes.byref(x) for x in v])
+        return {"replays": v[0].value, "captures": v[1].value, "eager": v[2].value}
 
     def new_stream(self, noise_seed: int = 0) -> int:
         h = ctypes.c_int32()
@@ -217,7 +227,8 @@ class B200HiFT:
                 raise ValueError("source: a contiguous fp32 tensor on the vocoder's device of sum 480 F_i floats")
             src = ctypes.c_void_p(source.data_ptr()) if source is not None else None
             b = L.VocodeBatch(n, hs, ts, ls, ctypes.c_void_p(mel_rows.data_ptr()), ctypes.c_void_p(rand_ini.data_ptr()),
-                              ctypes.c_void_p(nz.data_ptr()), ctypes.c_void_p(out.data_ptr()), src, None)
+                              ctypes.c_void_p(nz.data_ptr()), ctypes.c_void_p(out.data_ptr()), src, None,
+                              1 if self.use_graphs else 0)
             L.call("t2w_vocode", self.handle, ctypes.byref(b), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         for h in handles:
             self._seeds[int(h)][1] += 1

@@ -108,7 +108,8 @@ class HiftConfig(ctypes.Structure):
 class VocodeBatch(ctypes.Structure):
     _fields_ = [("n_streams", ctypes.c_int32), ("handle", ctypes.POINTER(ctypes.c_int32)),
                 ("T", ctypes.POINTER(ctypes.c_int32)), ("last", ctypes.POINTER(ctypes.c_uint8))] + \
-               [(n, ctypes.c_void_p) for n in ("mel", "rand_ini", "noise", "out", "source", "speech")]
+               [(n, ctypes.c_void_p) for n in ("mel", "rand_ini", "noise", "out", "source", "speech")] + \
+               [("flags", ctypes.c_uint32)]
 
 
 class TConvArgs(ctypes.Structure):
@@ -200,6 +201,8 @@ _SIGS = {
                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_I)], ctypes.c_int64),
     "t2w_vocode": ([_P, ctypes.POINTER(VocodeBatch), _P], ctypes.c_int),
     "t2w_test_tconv": ([ctypes.POINTER(TConvArgs), _P], ctypes.c_int),
+    "t2w_hift_counts": ([_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+                         ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "t2w_gemm_e4m3": ([_P, _I, _I, _P, _I, ctypes.c_int64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P,
                        ctypes.POINTER(_P), _F, _P], ctypes.c_int),
 }

@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 #include "common.cuh"
@@ -643,6 +644,17 @@ struct t2w_hift {
   // the calls' scratch: a stream-ordered pool of this vocoder's own that keeps its memory reserved between calls (the
   // default pool hands freed memory back at the next synchronisation, and remapping it costs every call milliseconds)
   cudaMemPool_t pool = nullptr;
+  // CUDA graphs of whole calls (T2W_FLAG_GRAPH), one per launch structure (the call's sizes), captured the second time
+  // a structure is seen; each owns the workspace its launches address
+  struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    uint8_t* ws = nullptr;
+    cudaEvent_t done = nullptr;  // recorded after its latest launch
+  };
+  std::unordered_map<uint64_t, Graph> graphs;
+  std::unordered_map<uint64_t, int> seen;
+  cudaStream_t cap_stream = nullptr;
+  int64_t n_replays = 0, n_captures = 0, n_eager = 0;
 };
 
 namespace {
@@ -982,6 +994,14 @@ void free_all(t2w_hift* h) {
   }
   if (h->pool) cudaMemPoolDestroy(h->pool);
   h->pool = nullptr;
+  for (auto& kv : h->graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.ws) cudaFree(kv.second.ws);
+    if (kv.second.done) cudaEventDestroy(kv.second.done);
+  }
+  h->graphs.clear();
+  if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
+  h->cap_stream = nullptr;
 }
 
 // ---- a call's plan
@@ -1234,10 +1254,70 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   const size_t o_post = add((size_t)pl.A[3] * post_ld * 4);
   // stage 2's output as [hi | lo] pairs, conv_post's input in split form
   const size_t o_xps = h->post_tc ? add((size_t)pl.A[3] * (C0 >> 3) * 8) : 0;
+  // a graph call reads the window's mel and noise from, and writes its samples to, buffers of its own workspace
+  const bool graph = (b->flags & T2W_FLAG_GRAPH) != 0;
+  long long mel_rows = 0;
+  for (int i = 0; i < n; ++i) mel_rows += b->T[i];
+  const int dim = c.harmonics + 1;
+  const size_t o_gmel = graph ? add((size_t)mel_rows * c.mel * 4) : 0;
+  const size_t o_gnoise = graph ? add((size_t)pl.samples * dim * 4) : 0;
+  const size_t o_gout = graph ? add((size_t)pl.out_samples * 4) : 0;
   const size_t total = meta;
+  // the launches depend only on the call's sizes (every window's rows, handles and padding flags are data in the
+  // workspace): one graph per size key, captured the second time the key is seen
+  t2w_hift::Graph* hg = nullptr;
+  bool capture = false;
+  uint64_t key = 0;
+  if (graph) {
+    key = 0x41F7ull;
+    for (long long v : {(long long)n, (long long)pl.A[0], (long long)pl.vs_mel[n], (long long)pl.vs_s[0][n],
+                        (long long)pl.vs_s[1][n], (long long)pl.vs_s[2][n], pl.samples, pl.out_samples, mel_rows})
+      key = (key ^ ((uint64_t)v + 0x9e3779b97f4a7c15ull + (key << 6) + (key >> 2))) * 0xff51afd7ed558ccdull;
+    auto it = h->graphs.find(key);
+    if (it != h->graphs.end()) {
+      hg = &it->second;
+    } else {
+      cudaStreamCaptureStatus cs;
+      H_CUDA(cudaStreamIsCapturing(st, &cs));
+      if (cs != cudaStreamCaptureStatusNone) return T2W_ERR_INVALID;  // the caller is capturing: flags = 0
+      if (h->seen.size() > 4096) h->seen.clear();
+      if (++h->seen[key] >= 2) {
+        if (h->graphs.size() >= 16) {  // drop one, once its latest launch has finished
+          auto victim = h->graphs.begin();
+          H_CUDA(cudaEventSynchronize(victim->second.done));
+          cudaGraphExecDestroy(victim->second.exec);
+          cudaFree(victim->second.ws);
+          cudaEventDestroy(victim->second.done);
+          h->graphs.erase(victim);
+        }
+        t2w_hift::Graph ng;
+        H_CUDA(cudaMalloc(reinterpret_cast<void**>(&ng.ws), total));
+        const cudaError_t ee = cudaEventCreateWithFlags(&ng.done, cudaEventDisableTiming);
+        if (ee != cudaSuccess) {
+          cudaFree(ng.ws);
+          set_cuda_error(ee);
+          return T2W_ERR_CUDA;
+        }
+        hg = &h->graphs.emplace(key, ng).first->second;
+        capture = true;
+      }
+    }
+  }
   uint8_t* ws = nullptr;
-  H_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), total, h->pool, st));
+  if (hg)
+    ws = hg->ws;
+  else
+    H_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), total, h->pool, st));
   auto P = [&](size_t o) { return ws + o; };
+  auto drop_graph = [&]() {  // a capture that failed leaves no entry behind
+    if (capture) {
+      if (hg->exec) cudaGraphExecDestroy(hg->exec);
+      cudaFree(hg->ws);
+      cudaEventDestroy(hg->done);
+      h->graphs.erase(key);
+      hg = nullptr;
+    }
+  };
   // the plan's image in a pinned staging buffer, rewritten only after the copy that last read it has completed
   t2w_hift::Staging& sg = h->staging[h->staging_next];
   h->staging_next = (h->staging_next + 1) % t2w_hift::kStaging;
@@ -1254,7 +1334,10 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   if (se == cudaSuccess && !sg.done) se = cudaEventCreateWithFlags(&sg.done, cudaEventDisableTiming);
   if (se != cudaSuccess) {
     set_cuda_error(se);
-    cudaFreeAsync(ws, st);
+    if (hg)
+      drop_graph();
+    else
+      cudaFreeAsync(ws, st);
     return T2W_ERR_CUDA;
   }
   uint8_t* img = static_cast<uint8_t*>(sg.host);
@@ -1275,15 +1358,36 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     uint8_t* const pads[4] = {img + o_pad[0], img + o_pad[1], img + o_pad[2], img + o_pad[3]};
     fill_pads(pl, pads);
   }
-  int rc = T2W_OK;
-  auto fail = [&](int r) {
-    cudaFreeAsync(ws, st);
-    return r;
-  };
   {
-    cudaError_t e1 = cudaMemcpyAsync(ws, img, meta_bytes, cudaMemcpyHostToDevice, st);
-    if (e1 == cudaSuccess) e1 = cudaEventRecord(sg.done, st);
-    if (e1 == cudaSuccess) sg.used = true;
+    cudaError_t e0 = cudaMemcpyAsync(ws, img, meta_bytes, cudaMemcpyHostToDevice, st);
+    if (e0 == cudaSuccess) e0 = cudaEventRecord(sg.done, st);
+    if (e0 == cudaSuccess) sg.used = true;
+    if (graph && e0 == cudaSuccess)
+      e0 = cudaMemcpyAsync(ws + o_gmel, b->mel, (size_t)mel_rows * c.mel * 4, cudaMemcpyDeviceToDevice, st);
+    if (graph && e0 == cudaSuccess)
+      e0 = cudaMemcpyAsync(ws + o_gnoise, b->noise, (size_t)pl.samples * dim * 4, cudaMemcpyDeviceToDevice, st);
+    if (e0 != cudaSuccess) {
+      set_cuda_error(e0);
+      if (hg)
+        drop_graph();
+      else
+        cudaFreeAsync(ws, st);
+      return T2W_ERR_CUDA;
+    }
+  }
+  const float* in_mel = graph ? reinterpret_cast<const float*>(ws + o_gmel) : b->mel;
+  const float* in_noise = graph ? reinterpret_cast<const float*>(ws + o_gnoise) : b->noise;
+  float* out_samples = graph ? reinterpret_cast<float*>(ws + o_gout) : b->out;
+  const HRow* drows = reinterpret_cast<const HRow*>(P(o_rows));
+  float* mel = reinterpret_cast<float*>(P(o_mel));
+  float* src = reinterpret_cast<float*>(P(o_src));
+  float* speech = reinterpret_cast<float*>(P(o_sp));
+  // every launch of the call, on `st` (the caller's stream, or the capture stream of a graph)
+  auto enqueue = [&](cudaStream_t st) -> int {
+  int rc = T2W_OK;
+  auto fail = [](int r) { return r; };
+  {
+    cudaError_t e1 = cudaSuccess;
     // buffers whose rows around the windows' data must read as zero and that no kernel writes in full: the mel rows and
     // conv_pre's output (read by the transposed conv's tensor-map loads), the source branch and its Snake (added to
     // every row by the fan-out; read by the ResBlock convs), and the transposed conv's output when the fp32 kernel,
@@ -1314,8 +1418,6 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       return fail(T2W_ERR_CUDA);
     }
   }
-  const HRow* drows = reinterpret_cast<const HRow*>(P(o_rows));
-  float* mel = reinterpret_cast<float*>(P(o_mel));
   auto run = [&](ConvGeo g) -> int {
     if (g.nv <= 0) return T2W_OK;
     if (g.Cout <= 32) {
@@ -1355,7 +1457,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   // 1. mel rows
   {
     dim3 grid(h->max_frames, n);
-    rc = ck(launch_k(k_mel_in, grid, dim3(128), 0, st, b->mel, drows, (const float*)h->cache, h->cache_ld, c.mel, mel,
+    rc = ck(launch_k(k_mel_in, grid, dim3(128), 0, st, in_mel, drows, (const float*)h->cache, h->cache_ld, c.mel, mel,
                      o_mel3 ? reinterpret_cast<float*>(P(o_mel3)) : nullptr));
     if (rc) return fail(rc);
   }
@@ -1423,11 +1525,10 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     if (rc) return fail(rc);
   }
   // 3. the harmonic source, 4. its STFT
-  float* src = reinterpret_cast<float*>(P(o_src));
   float* stft = reinterpret_cast<float*>(P(o_stft));
   {
     const dim3 sgrid((480 * h->max_frames + kSrcChunk - 1) / kSrcChunk, n);
-    rc = ck(launch_k(k_source, sgrid, dim3(256), 0, st, (const float*)P(o_f0), drows, b->noise, (const float*)h->lin_w,
+    rc = ck(launch_k(k_source, sgrid, dim3(256), 0, st, (const float*)P(o_f0), drows, in_noise, (const float*)h->lin_w,
                      h->lin_b, c.harmonics + 1, (float)c.sample_rate, 480.f, c.nsf_alpha, c.nsf_sigma, c.voiced_threshold,
                      (const float*)h->cache, h->cache_ld, kMelCache * c.mel, src));
     if (rc) return fail(rc);
@@ -1688,22 +1789,65 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     }
     if (rc) return fail(rc);
   }
-  float* speech = reinterpret_cast<float*>(P(o_sp));
   {
     dim3 grid((480 * h->max_frames + kIstftChunk - 1) / kIstftChunk, n);
     rc = ck(launch_k(k_istft_out, grid, dim3(256), 0, st, (const float*)post, post_ld, drows, (const float*)h->tw,
                      (const double*)h->hamming, c.audio_limit, 480.f, speech, (const float*)h->cache, h->cache_ld,
-                     kMelCache * c.mel + kSrcCache, b->out));
+                     kMelCache * c.mel + kSrcCache, out_samples));
     if (rc) return fail(rc);
     rc = ck(launch_k(k_hift_caches, dim3(n), dim3(256), 0, st, drows, (const float*)mel, c.mel, (const float*)src,
                      (const float*)speech, h->cache, h->cache_ld, 0, kMelCache * c.mel, kMelCache * c.mel + kSrcCache,
                      480.f));
     if (rc) return fail(rc);
   }
+  return T2W_OK;
+  };
+  int rc = T2W_OK;
+  if (capture) {
+    if (!h->cap_stream) rc = cudaStreamCreateWithFlags(&h->cap_stream, cudaStreamNonBlocking) ? T2W_ERR_CUDA : T2W_OK;
+    if (!rc) rc = cudaStreamBeginCapture(h->cap_stream, cudaStreamCaptureModeThreadLocal) ? T2W_ERR_CUDA : T2W_OK;
+    if (!rc) {
+      const int re = enqueue(h->cap_stream);
+      cudaGraph_t gr = nullptr;
+      const cudaError_t ec = cudaStreamEndCapture(h->cap_stream, &gr);
+      rc = re ? re : (ec != cudaSuccess ? T2W_ERR_CUDA : T2W_OK);
+      if (!rc && cudaGraphInstantiate(&hg->exec, gr, 0) != cudaSuccess) rc = T2W_ERR_CUDA;
+      if (gr) cudaGraphDestroy(gr);
+    }
+    if (rc) {
+      drop_graph();
+      return rc;
+    }
+    ++h->n_captures;
+  }
+  if (hg) {
+    H_CUDA(cudaGraphLaunch(hg->exec, st));
+    ++h->n_replays;
+  } else {
+    rc = enqueue(st);
+    if (rc) {
+      cudaFreeAsync(ws, st);
+      return rc;
+    }
+    ++h->n_eager;
+  }
+  if (graph)
+    H_CUDA(cudaMemcpyAsync(b->out, out_samples, (size_t)pl.out_samples * 4, cudaMemcpyDeviceToDevice, st));
   if (b->source) H_CUDA(cudaMemcpyAsync(b->source, src, (size_t)pl.samples * 4, cudaMemcpyDeviceToDevice, st));
   if (b->speech) H_CUDA(cudaMemcpyAsync(b->speech, speech, (size_t)pl.samples * 4, cudaMemcpyDeviceToDevice, st));
-  cudaFreeAsync(ws, st);
+  if (hg)
+    H_CUDA(cudaEventRecord(hg->done, st));
+  else
+    cudaFreeAsync(ws, st);
   for (int i = 0; i < n; ++i) h->row_first[b->handle[i]] = 0;
+  return T2W_OK;
+}
+
+int t2w_hift_counts(const t2w_hift* h, int64_t* replays, int64_t* captures, int64_t* eager) {
+  if (!h) return T2W_ERR_INVALID;
+  if (replays) *replays = h->n_replays;
+  if (captures) *captures = h->n_captures;
+  if (eager) *eager = h->n_eager;
   return T2W_OK;
 }
 

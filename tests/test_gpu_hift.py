@@ -197,3 +197,32 @@ def test_split_fp32_mode_vs_reference_driver_golden(golden_dir, name, cfg):
             assert o.numel() == w["samples"].numel() and e < 5e-4, e
     print(f"{name} split_fp32: worst window rel-L2 {worst:.2e}")
     voc.check()
+
+
+@pytest.mark.parametrize("split_fp32", [False, True], ids=["tf32", "split_fp32"])
+def test_graph_replay_equals_eager(split_fp32):
+    """``use_graphs`` (the reference's ``t2w_graphs`` / ``HiFTGraphs``): a stream's first windows, steady windows that
+    repeat a call structure (captured on its second sight, replayed after) and finals, bit-identical to the eager
+    vocoder's samples with the same seeded noise; the counters show the captures and replays."""
+    cfg = HIFT_TINY
+    hift = ho.build_hift(cfg, seed=0)
+    kw = dict(device="cuda", max_frames=64, n_streams=8, split_fp32=split_fp32)
+    vg = B200HiFT.from_module(hift, cfg, use_graphs=True, **kw)
+    ve = B200HiFT.from_module(hift, cfg, **kw)
+    seeds = [5, 6, 7]
+    hg = [vg.new_stream(s) for s in seeds]
+    he = [ve.new_stream(s) for s in seeds]
+    g = torch.Generator().manual_seed(8)
+    plan = [[50, 50, 50]] + [[50, 50, 50]] * 4 + [[12, 30, 7]]
+    for c, Ts in enumerate(plan):
+        last = c == len(plan) - 1
+        mels = [torch.randn(cfg.mel, T, generator=g) - 2.0 for T in Ts]
+        og = vg.vocode(hg, mels, [last] * 3)
+        oe = ve.vocode(he, mels, [last] * 3)
+        for a, b in zip(og, oe):
+            assert a.numel() == b.numel() and torch.equal(a, b), c
+    cnt = vg.counts
+    print(f"split_fp32={split_fp32}: {cnt}")
+    assert cnt["captures"] >= 1 and cnt["replays"] >= 3
+    assert ve.counts["replays"] == 0
+    vg.check()

@@ -595,6 +595,15 @@ typedef struct t2w_tconv_args {
 } t2w_tconv_args;
 T2W_API int t2w_test_tconv(const t2w_tconv_args* a, void* stream);
 
+/* Test entry: one launch of the slot-pool (gathered-key) attention the steady-state solve runs, for numerics tests.
+ * work: host [n_work][5] (q_row, k_row, q_pos, P, L): the queries q_row .. q_row + P - q_pos - 1 of qkv (bf16 [rows,
+ * 3 heads 64]) attend the L keys pool[kv_idx[k_row + j]] (K at column h 64, V at heads 64 + h 64 of bf16 rows of
+ * pool_ld); out bf16 [rows, heads 64].  kv_idx: host [n_idx], every entry < pool_rows.  pair != 0: the paired form
+ * (two items per 128-row tile; every item's queries within 64 rows).  Synchronises the stream. */
+T2W_API int t2w_test_attn_gathered(const void* qkv_bf16, int32_t rows, int32_t heads, int32_t n_work, const int32_t* work,
+                                   const void* pool_bf16, int32_t pool_rows, int32_t pool_ld, const int32_t* kv_idx,
+                                   int32_t n_idx, int32_t pair, void* out_bf16, int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -201,6 +201,8 @@ _SIGS = {
                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_I)], ctypes.c_int64),
     "t2w_vocode": ([_P, ctypes.POINTER(VocodeBatch), _P], ctypes.c_int),
     "t2w_test_tconv": ([ctypes.POINTER(TConvArgs), _P], ctypes.c_int),
+    "t2w_test_attn_gathered": ([_P, _I, _I, _I, ctypes.POINTER(_I), _P, _I, _I, ctypes.POINTER(_I), _I, _I, _P, _P, _P],
+                               ctypes.c_int),
     "t2w_hift_counts": ([_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
                          ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "t2w_gemm_e4m3": ([_P, _I, _I, _P, _I, ctypes.c_int64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P,

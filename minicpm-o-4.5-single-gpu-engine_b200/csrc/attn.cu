@@ -19,6 +19,15 @@
 // With two S buffers the issuer computes S_{t+1} (and S_{t+2} once P_t V_t is issued) while the softmax works on tile
 // t, so the softmax warps run from tile to tile without waiting on the tensor core.  Tensor-core ops of one issuing
 // thread run in issue order, so S_{t+2} never overwrites P_t before P_t V_t has read it.  No TMA multicast.
+//
+// Paired form (gathered keys, every item's queries within 64 rows: the steady-state windows): a pipeline's work item
+// is two (query tile, head) items A and B laid out block-diagonally in the same 128-row MMA tiles.  Query rows 0-63
+// are A's queries, 64-127 B's (two 64-row TMA boxes); each 64-key tile holds 32 keys of A (smem rows 0-31) and the
+// same-numbered 32 keys of B (rows 32-63).  S = Q K^T then holds A x A's keys in rows 0-63 / columns 0-31 and B x B's
+// keys in rows 64-127 / columns 32-63; each softmax thread reads its item's 32 columns and writes P for them with
+// zeros over the other item's 32, so O = P V takes rows 0-63 from A's values alone and rows 64-127 from B's.  The
+// MMA shapes, TMEM regions and barriers are those of the single form; a 50-frame window then keeps all four softmax
+// warps busy and a CTA runs four windows' heads at once instead of two.
 #include <mutex>
 #include <vector>
 
@@ -37,9 +46,13 @@ constexpr int kKVBytes = kKTile * kD * 2;      // 8 KB each for K and V
 constexpr int kStages = 4;                     // K/V ring per pipeline
 constexpr int kPipeBytes = kQBytes + kStages * 2 * kKVBytes;  // 80 KB
 constexpr int kMaxCtaItems = 512;  // items per CTA staged in shared memory (the grid grows to keep within it)
+constexpr int kPairRows = 64;      // paired form: query rows of each of the two items
+constexpr int kPairKeys = 32;      // paired form: keys of each item per 64-key tile
 struct ItemEntry {
   AttnWork w;
   int h, n_kt;
+  AttnWork w2;  // paired form: item B (h2 = -1 when the pair's second item does not exist)
+  int h2;
 };
 constexpr int kSmem = 2 * kPipeBytes + 1024 + 512 + kMaxCtaItems * (int)sizeof(ItemEntry);
 constexpr int kTmemCols = 512;  // pipeline p: S/P buffers at 192 p + {0, 64}, O at 192 p + 128
@@ -55,6 +68,7 @@ constexpr long long kPipeStagger = 2400;
 struct DevArgs {
   const AttnWork* work;
   int n_items, heads;
+  int n_flat;       // paired form: (work, head) items; n_items = the pairs
   void* out;        // bf16, or e4m3 with out_sf (the FP8 path's proj input)
   uint8_t* out_sf;  // e4m3 output: UE8M0 scale atoms (one byte per row and 32-column block, sf_offset layout)
   int ldo;
@@ -113,7 +127,7 @@ T2W_DEV int item_tiles(const AttnWork& w) {
   return (kmax + kKTile - 1) / kKTile;
 }
 
-template <bool E4M3, bool GATHER>
+template <bool E4M3, bool GATHER, bool PAIR>
 __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtensorMap tm_q,
                                                  const __grid_constant__ CUtensorMap tm_kv, const DevArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -157,9 +171,26 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
     const int item = (i & 1) + 2 * blockIdx.x + (i >> 1) * stride;
     if (item < p.n_items) {
       ItemEntry e;
-      e.w = p.work[item / p.heads];
-      e.h = item % p.heads;
-      e.n_kt = item_tiles<GATHER>(e.w);
+      if constexpr (PAIR) {
+        const int f = 2 * item;
+        e.w = p.work[f / p.heads];
+        e.h = f % p.heads;
+        if (f + 1 < p.n_flat) {
+          e.w2 = p.work[(f + 1) / p.heads];
+          e.h2 = (f + 1) % p.heads;
+        } else {
+          e.w2 = e.w;
+          e.h2 = -1;
+        }
+        const int kmax = max(e.w.L, e.h2 >= 0 ? e.w2.L : 0);
+        e.n_kt = (kmax + kPairKeys - 1) / kPairKeys;
+      } else {
+        e.w = p.work[item / p.heads];
+        e.h = item % p.heads;
+        e.n_kt = item_tiles<GATHER>(e.w);
+        e.w2 = e.w;
+        e.h2 = -1;
+      }
       items[i] = e;
     }
   }
@@ -203,10 +234,14 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       // The slot indices of the next tile's keys (the next item's first tile after an item's last) are loaded while
       // this tile's copies are issued, so the index load's latency is off the producer's path.
       auto slot_of = [&](const AttnWork& w, int key) { return key < w.L ? __ldg(p.kv_idx + w.k_row + key) : 0; };
+      // the key this lane copies into smem row lane + 32 half of tile j, and the item it belongs to (paired form:
+      // half 0 = item A's key 32 j + lane, half 1 = item B's key of the same number)
+      auto key_of = [&](int j, int half) { return PAIR ? j * kPairKeys + lane : j * kKTile + lane + 32 * half; };
+      auto work_of = [&](const ItemEntry& e, int half) -> const AttnWork& { return (PAIR && half) ? e.w2 : e.w; };
       int nxt[2] = {0, 0};
       if (q + 2 * (int)blockIdx.x < p.n_items) {
-        nxt[0] = slot_of(items[q].w, lane);
-        nxt[1] = slot_of(items[q].w, lane + 32);
+        nxt[0] = slot_of(work_of(items[q], 0), key_of(0, 0));
+        nxt[1] = slot_of(work_of(items[q], 1), key_of(0, 1));
       }
       for (int k = 0; ok; ++k) {
         if (q + 2 * (int)blockIdx.x + k * stride >= p.n_items) break;
@@ -215,21 +250,28 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         if (lane == 0) {
           if ((ok = mbar_wait(&b.q_free, (k & 1) ^ 1u, p.err))) {
             mbar_expect_tx(&b.q_full, kQBytes);
-            tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+            if constexpr (PAIR) {  // tm_q has 64-row boxes here: A's queries into rows 0-63, B's into 64-127
+              tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+              tma_load_2d(base + kQBytes / 2, &tm_q, (e.h2 >= 0 ? e.h2 : e.h) * kD, e.w2.q_row, &b.q_full);
+            } else {
+              tma_load_2d(base, &tm_q, e.h * kD, e.w.q_row, &b.q_full);
+            }
           }
         }
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        const __nv_bfloat16* kcol = p.pool + e.h * kD;
-        const __nv_bfloat16* vcol = p.pool + H + e.h * kD;
+        const int hB = (PAIR && e.h2 >= 0) ? e.h2 : e.h;
+        const __nv_bfloat16* kcol[2] = {p.pool + e.h * kD, p.pool + hB * kD};
+        const __nv_bfloat16* vcol[2] = {p.pool + H + e.h * kD, p.pool + H + hB * kD};
+        const bool has_b = !PAIR || e.h2 >= 0;
         for (int j = 0; j < e.n_kt; ++j, ++t) {
           const int cur[2] = {nxt[0], nxt[1]};
           if (j + 1 < e.n_kt) {
-            nxt[0] = slot_of(e.w, (j + 1) * kKTile + lane);
-            nxt[1] = slot_of(e.w, (j + 1) * kKTile + lane + 32);
+            nxt[0] = slot_of(work_of(e, 0), key_of(j + 1, 0));
+            nxt[1] = slot_of(work_of(e, 1), key_of(j + 1, 1));
           } else if (has_next_item) {
-            const AttnWork& wn = items[2 * (k + 1) + q].w;
-            nxt[0] = slot_of(wn, lane);
-            nxt[1] = slot_of(wn, lane + 32);
+            const ItemEntry& en = items[2 * (k + 1) + q];
+            nxt[0] = slot_of(work_of(en, 0), key_of(0, 0));
+            nxt[1] = slot_of(work_of(en, 1), key_of(0, 1));
           }
           const int st = t % kStages;
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err)))) break;
@@ -237,11 +279,11 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             const int r = lane + 32 * half;
-            const int key = j * kKTile + r;
-            const bool valid = key < e.w.L;
+            const int key = key_of(j, half);
+            const bool valid = key < work_of(e, half).L && (half == 0 || has_b);
             const size_t slot = (size_t)cur[half];
-            const __nv_bfloat16* ksrc = kcol + slot * p.pool_ld;
-            const __nv_bfloat16* vsrc = vcol + slot * p.pool_ld;
+            const __nv_bfloat16* ksrc = kcol[half] + slot * p.pool_ld;
+            const __nv_bfloat16* vsrc = vcol[half] + slot * p.pool_ld;
             const uint32_t nb = valid ? 16u : 0u;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -316,6 +358,8 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
     const int q = (warp - 4) >> 2;  // pipeline
     const int qw = warp & 3;        // TMEM lane quarter
     const int r = qw * 32 + lane;   // query row of the tile
+    const int sub = PAIR ? (qw >> 1) : 0;  // paired form: this row's item (A: rows 0-63, B: rows 64-127)
+    const int rs = r - kPairRows * sub;    // query row within its item
     PipeBars& b = bars[q];
     const uint32_t lanes = (uint32_t)(qw * 32) << 16;
     const uint32_t preg = tmem + 192 * q + lanes, oreg = preg + 128;
@@ -343,7 +387,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
       const float l = pd.l;
       if (lim > 0) {
         const float inv = 1.f / l;
-        const int row = w.q_row + r;
+        const int row = w.q_row + rs;
         if constexpr (E4M3) {
           // two 32-column blocks per head, each with its own power-of-two scale
           uint8_t* dst = static_cast<uint8_t*>(p.out) + (size_t)row * p.ldo + h * kD;
@@ -385,11 +429,12 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
     for (int k = 0; ok; ++k) {
       const int item = q + 2 * blockIdx.x + k * stride;
       if (item >= p.n_items) break;
-      const AttnWork w = items[2 * k + q].w;
-      const int h = items[2 * k + q].h;
-      const int n_kt = items[2 * k + q].n_kt;
-      const int pos = w.q_pos + r;
-      const int lim = GATHER ? (pos < w.P ? w.L : 0) : (pos < w.P ? w.P : (pos < w.L ? w.L : 0));
+      const ItemEntry& ie = items[2 * k + q];
+      const AttnWork w = (PAIR && sub) ? ie.w2 : ie.w;
+      const int h = (PAIR && sub) ? ie.h2 : ie.h;
+      const int n_kt = ie.n_kt;
+      const int pos = w.q_pos + rs;
+      const int lim = (PAIR && h < 0) ? 0 : GATHER ? (pos < w.P ? w.L : 0) : (pos < w.P ? w.P : (pos < w.L ? w.L : 0));
       // A warp whose 32 query rows all lie past the item's queries (a 50-frame window fills 50 rows of the 128-row
       // tile; a sequence's last tile is partial) computes no softmax: its rows' P and O are never stored, so whatever
       // the TMEM holds there only reaches those rows' discarded outputs.  It still takes part in every barrier.
@@ -406,6 +451,45 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         tc_fence_after();
         const uint32_t sbuf = preg + 64 * (t & 1);
         if (!idle) {
+        bool raise;
+        float m_old;
+        float2 rsq[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        if constexpr (PAIR) {
+          // the row's own item's 32 keys of the tile (columns 32 sub ..), P over them and zeros over the other item's
+          float sv[32];
+          tmem_ld32(sbuf + kPairKeys * sub, sv);
+          const int kb = j * kPairKeys;
+          if (!__all_sync(0xffffffffu, kb + kPairKeys <= lim)) {
+#pragma unroll
+            for (int i = 0; i < kPairKeys; ++i)
+              if (kb + i >= lim) sv[i] = -INFINITY;
+          }
+          float mq[2];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            mq[c] = fmax3(sv[16 * c], sv[16 * c + 1], sv[16 * c + 2]);
+#pragma unroll
+            for (int i = 3; i < 15; i += 2) mq[c] = fmax3(mq[c], sv[16 * c + i], sv[16 * c + i + 1]);
+            mq[c] = fmaxf(mq[c], sv[16 * c + 15]);
+          }
+          const float mx = fmaxf(mq[0], mq[1]) * p.scale_log2;
+          raise = mx > m + kRescaleThreshold;
+          m_old = m;
+          m = raise ? mx : m;
+          const float m_use = (m == -INFINITY) ? 0.f : m;
+          const float2 c2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_use, -m_use);
+          uint32_t u[32];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 a = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), c2, nm2);
+            const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
+            rsq[i & 3] = __fadd2_rn(rsq[i & 3], e);
+            const uint32_t pk = pack_bf16x2(e.x, e.y);
+            u[i] = sub ? 0u : pk;
+            u[16 + i] = sub ? pk : 0u;
+          }
+          tmem_st32(sbuf, u);
+        } else {
         uint32_t sr[64];
         tmem_ld64_nowait(sbuf, sr);
         tmem_ld_wait();
@@ -429,13 +513,12 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
         }
         float mx = fmax3(fmaxf(mq[0], mq[1]), mq[2], mq[3]) * p.scale_log2;
         // raise the reference max only when it grows by more than the threshold (p <= 2^8 fits bf16 comfortably)
-        const bool raise = mx > m + kRescaleThreshold;
-        const float m_old = m;
+        raise = mx > m + kRescaleThreshold;
+        m_old = m;
         m = raise ? mx : m;
         const float m_use = (m == -INFINITY) ? 0.f : m;
         // P = 2^(S c - m) as bf16 pairs, written back over the scores
         const float2 c2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_use, -m_use);
-        float2 rsq[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint32_t u[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -445,6 +528,7 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
           u[i] = pack_bf16x2(e.x, e.y);
         }
         tmem_st32(sbuf, u);
+        }
         // O holds P_{<j} V_{<j} relative to the old reference max: rescale it (rare) once P_{j-1} V_{j-1} is done.
         // S_t's completion implies every tensor op issued before it, so the skipped waits of o_done never fall two
         // phases behind.
@@ -500,33 +584,45 @@ bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int
          make_tmap_2d(tm_kv, qkv, 2, (uint64_t)rows, cols, cols * 2, kKTile, kD);
 }
 
+bool make_attn_pair_tmap(CUtensorMap* tm_q, const void* qkv, int rows, int heads) {
+  const uint64_t cols = 3ull * heads * kD;
+  return make_tmap_2d(tm_q, qkv, 2, (uint64_t)rows, cols, cols * 2, kPairRows, kD);
+}
+
 namespace {
 
-template <bool E4M3, bool GATHER>
+template <bool E4M3, bool GATHER, bool PAIR>
 int launch_attn_impl(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, const CUtensorMap* tm_kv) {
   static std::atomic<uint64_t> attr_done{0};
   {
-    const cudaError_t e = smem_attr_once(k_attn<E4M3, GATHER>, kSmem, attr_done);
+    const cudaError_t e = smem_attr_once(k_attn<E4M3, GATHER, PAIR>, kSmem, attr_done);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return T2W_ERR_CUDA;
     }
   }
   CUtensorMap mq, mkv;
-  if (!tm_q || !tm_kv) {
+  if constexpr (PAIR) {  // the query map with 64-row boxes; the gathered form reads no key map
+    if (!tm_q) {
+      if (!make_attn_pair_tmap(&mq, a.qkv, a.rows, a.heads)) return T2W_ERR_INVALID;
+      tm_q = &mq;
+    }
+    tm_kv = tm_q;
+  } else if (!tm_q || !tm_kv) {
     if (!make_attn_tmaps(&mq, &mkv, a.qkv, a.rows, a.heads)) return T2W_ERR_INVALID;
     tm_q = &mq;
     tm_kv = &mkv;
   }
-  const int n_items = a.n_work * a.heads;
-  DevArgs p{a.work,    n_items,  a.heads, a.out,  a.out_sf, a.heads * kD, a.scale_log2,
+  const int n_flat = a.n_work * a.heads;
+  const int n_items = PAIR ? (n_flat + 1) / 2 : n_flat;
+  DevArgs p{a.work,    n_items,  a.heads, n_flat, a.out,  a.out_sf, a.heads * kD, a.scale_log2,
             a.err,     a.pool,   a.kv_idx, a.pool_ld, a.pf, a.pf_bytes};
   int grid = (n_items + 1) / 2;
   if (grid > num_sms()) grid = num_sms();
   // each CTA stages at most kMaxCtaItems items in shared memory
   const int min_grid = (n_items + kMaxCtaItems - 1) / kMaxCtaItems;
   if (grid < min_grid) grid = min_grid;
-  cudaError_t e = launch_k(k_attn<E4M3, GATHER>, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
+  cudaError_t e = launch_k(k_attn<E4M3, GATHER, PAIR>, dim3(grid), dim3(384), kSmem, st, *tm_q, *tm_kv, p);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return T2W_ERR_CUDA;
@@ -544,9 +640,12 @@ int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q, con
     if (a.out_sf || !a.kv_idx || a.pool_ld < 2 * a.heads * kD || a.pool_ld % 8 ||
         (reinterpret_cast<uintptr_t>(a.pool) & 15))
       return T2W_ERR_INVALID;
-    return launch_attn_impl<false, true>(a, st, tm_q, tm_kv);
+    if (a.pair) return launch_attn_impl<false, true, true>(a, st, a.tm_q_pair, nullptr);
+    return launch_attn_impl<false, true, false>(a, st, tm_q, tm_kv);
   }
-  return a.out_sf ? launch_attn_impl<true, false>(a, st, tm_q, tm_kv) : launch_attn_impl<false, false>(a, st, tm_q, tm_kv);
+  if (a.pair) return T2W_ERR_INVALID;  // the paired form reads gathered keys only
+  return a.out_sf ? launch_attn_impl<true, false, false>(a, st, tm_q, tm_kv)
+                  : launch_attn_impl<false, false, false>(a, st, tm_q, tm_kv);
 }
 
 }  // namespace t2w
@@ -629,4 +728,57 @@ extern "C" int t2w_attn_varlen_noalloc(const void* qkv, int32_t rows, int32_t he
   a.out = out;
   a.scale_log2 = (float)(1.4426950408889634 / 8.0);
   return launch_attn(a, st);
+}
+
+// Test entry: the gathered (slot-pool) attention on host-given work and key lists, in the single or the paired form.
+extern "C" int t2w_test_attn_gathered(const void* qkv, int32_t rows, int32_t heads, int32_t n_work, const int32_t* work,
+                                      const void* pool, int32_t pool_rows, int32_t pool_ld, const int32_t* kv_idx,
+                                      int32_t n_idx, int32_t pair, void* out, int32_t* err, void* stream) {
+  using namespace t2w;
+  if (!qkv || !pool || !out || !work || !kv_idx || rows <= 0 || heads <= 0 || n_work <= 0 || pool_rows <= 0 ||
+      n_idx <= 0)
+    return T2W_ERR_INVALID;
+  std::vector<AttnWork> w(n_work);
+  for (int i = 0; i < n_work; ++i) {
+    w[i] = AttnWork{work[5 * i], work[5 * i + 1], work[5 * i + 2], work[5 * i + 3], work[5 * i + 4]};
+    const AttnWork& x = w[i];
+    const int nq = x.P - x.q_pos;  // this tile's queries
+    if (x.q_row < 0 || x.q_pos < 0 || nq <= 0 || nq > (pair ? 64 : 128) || x.q_row + nq > rows || x.L <= 0 ||
+        x.k_row < 0 || (int64_t)x.k_row + x.L > n_idx)
+      return T2W_ERR_INVALID;
+  }
+  for (int j = 0; j < n_idx; ++j)
+    if (kv_idx[j] < 0 || kv_idx[j] >= pool_rows) return T2W_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  AttnWork* dw = nullptr;
+  int* di = nullptr;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&dw), w.size() * sizeof(AttnWork));
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&di), (size_t)n_idx * 4);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dw, w.data(), w.size() * sizeof(AttnWork), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(di, kv_idx, (size_t)n_idx * 4, cudaMemcpyHostToDevice, st);
+  int rc = T2W_OK;
+  if (e == cudaSuccess) {
+    AttnArgs a;
+    a.qkv = qkv;
+    a.rows = rows;
+    a.heads = heads;
+    a.work = dw;
+    a.n_work = n_work;
+    a.out = out;
+    a.scale_log2 = (float)(1.4426950408889634 / 8.0);
+    a.pool = static_cast<const __nv_bfloat16*>(pool);
+    a.kv_idx = di;
+    a.pool_ld = pool_ld;
+    a.err = err;
+    a.pair = pair != 0;
+    rc = launch_attn(a, st);
+    e = cudaStreamSynchronize(st);
+  }
+  cudaFree(dw);
+  cudaFree(di);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return T2W_ERR_CUDA;
+  }
+  return rc;
 }

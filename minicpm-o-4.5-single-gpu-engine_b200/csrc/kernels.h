@@ -135,9 +135,17 @@ struct AttnArgs {
   int* err = nullptr;
   const void* pf = nullptr;  // L2 prefetch of the next GEMM's weights (64 KB per CTA of the first CTAs)
   unsigned pf_bytes = 0;
+  // Paired form (gathered keys only): two (query tile, head) items share each 128-row MMA tile, block-diagonally.
+  // Every work item's queries must lie within 64 rows (P - q_pos <= 64); rows past 64 would not be computed, so the
+  // caller checks this on its host copy of the work list.  tm_q_pair: the query map with 64-row boxes
+  // (make_attn_pair_tmap), or nullptr to make one per launch.
+  bool pair = false;
+  const CUtensorMap* tm_q_pair = nullptr;
 };
 // Tensor maps of the attention kernel over a qkv buffer: 128-row query boxes and 64-row key / value boxes.
 bool make_attn_tmaps(CUtensorMap* tm_q, CUtensorMap* tm_kv, const void* qkv, int rows, int heads);
+// The paired form's query map: 64-row boxes.
+bool make_attn_pair_tmap(CUtensorMap* tm_q, const void* qkv, int rows, int heads);
 int launch_attn(const AttnArgs& a, cudaStream_t st, const CUtensorMap* tm_q = nullptr, const CUtensorMap* tm_kv = nullptr);
 
 // Slot-pool (steady-state) kernels, slots.cu.  A conv row: a CFG row's window starts at buffer row seg_row (its two

@@ -137,6 +137,7 @@ struct Plan {
   uint64_t key = 0;
   // slot-pool (steady-state) solves only: gathered attention key lists, conv rows, and the new keys' (row, slot)
   bool slots = false;
+  bool pair_attn = false;  // every window within 64 frames: attention in its paired form
   std::vector<int> kv_idx, tok_qrow, tok_slot;
   std::vector<ConvRow> conv_rows;
   // solves over library-kept caches: x0 gathered on the device from the flow's noise at column tok_col[token]
@@ -312,6 +313,15 @@ bool make_plan_slots(const t2w_config& c, int n, const int* T, const int* kv_len
     row += T[i];
   }
   pl.n_work = (int)pl.work.size();
+  // Windows of up to 64 frames: two (window, head) items share each 128-row attention tile (measured on steady calls
+  // of 32 and 64 windows of 50 frames; T2W_ATTN_PAIR=0 keeps one item per tile).
+  static const bool pair_ok = [] {
+    const char* e = getenv("T2W_ATTN_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  pl.pair_attn = pair_ok;
+  for (const AttnWork& w : pl.work)
+    if (w.P - w.q_pos > 64) pl.pair_attn = false;
   return true;
 }
 
@@ -431,8 +441,9 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
       !make_tmap_2d(&st_f, f, 2, R, F, F * 2, 32, 64) || !make_tmap_2d(&st_qkv, qkv, 2, R, 3 * H, 3 * H * 2, 32, 64) ||
       !make_tmap_2d(&st_h, h, 4, R, H, H * 4, 32, 32))
     return T2W_ERR_INVALID;
-  CUtensorMap tm_att_q, tm_att_kv;
+  CUtensorMap tm_att_q, tm_att_kv, tm_att_pair;
   if (!make_attn_tmaps(&tm_att_q, &tm_att_kv, qkv, R, c.heads)) return T2W_ERR_INVALID;
+  if (pl.pair_attn && !make_attn_pair_tmap(&tm_att_pair, qkv, R, c.heads)) return T2W_ERR_INVALID;
   const bool fp8 = s->precision == T2W_PREC_FP8;
   if (pl.slots && (!sp || fp8)) return T2W_ERR_UNSUPPORTED;  // the slot-pool solve runs the bf16 path
   const int* kv_idx_d = pl.slots ? at<int>(ws, L.kv_idx) : nullptr;
@@ -642,6 +653,8 @@ int enqueue_solve(t2w_solver* s, const Plan& pl, const t2w_batch& b, void* ws, c
         at_use.pool = kvp;
         at_use.kv_idx = kv_idx_d;
         at_use.pool_ld = 2 * H;
+        at_use.pair = pl.pair_attn;
+        at_use.tm_q_pair = pl.pair_attn ? &tm_att_pair : nullptr;
       }
       T2W_TRY(P.tick(T2W_KC_ATTN, st));
       T2W_TRY(launch_attn(at_use, st, &tm_att_q, &tm_att_kv));
@@ -896,7 +909,7 @@ int run_slot_plan(t2w_solver* s, t2w_slots* p, const Plan& pl, const t2w_batch& 
   uint64_t key = 0x510750175107ull;
   for (long long v : {(long long)pl.n_streams, (long long)pl.n_tok, (long long)pl.half_rows, (long long)pl.rows,
                       (long long)pl.n_work, (long long)pl.kv_idx.size(), (long long)pl.conv_rows.size(),
-                      (long long)pl.tok_slot.size(), (long long)pl.gather})
+                      (long long)pl.tok_slot.size(), (long long)pl.gather, (long long)pl.pair_attn})
     key = mix(key, (uint64_t)v);
   for (const void* q : {(const void*)ws, (const void*)pb.x0, (const void*)pb.mu, (const void*)pb.cond,
                         (const void*)pb.spk, (const void*)pb.out, (const void*)p->kv, (const void*)p->cnn})

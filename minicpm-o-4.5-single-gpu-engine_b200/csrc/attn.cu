@@ -279,21 +279,20 @@ __global__ void __launch_bounds__(384, 1) k_attn(const __grid_constant__ CUtenso
           const int st = t % kStages;
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b.kv_empty[st], ((t / kStages) & 1) ^ 1u, p.err)))) break;
           const uint32_t ks = smem_u32(base + kQBytes + st * 2 * kKVBytes), vs = ks + kKVBytes;
+          // eight consecutive lanes copy one key row's eight 16-byte chunks, so each copy instruction reads four whole
+          // 128-byte rows; a row's slot comes from the lane that loaded it (lane R % 32 holds row R's in cur[R / 32])
+          const int c = lane & 7;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int r = lane + 32 * half;
-            const int key = key_of(j, half);
+          for (int i = 0; i < 16; ++i) {
+            const int R = 4 * i + (lane >> 3);  // smem row of this lane's chunk
+            const int half = i >> 3;            // R / 32
+            const size_t slot = (size_t)__shfl_sync(0xffffffffu, cur[half], R & 31);
+            const int key = PAIR ? j * kPairKeys + (R & 31) : j * kKTile + R;
             const bool valid = key < work_of(e, half).L && (half == 0 || has_b);
-            const size_t slot = (size_t)cur[half];
-            const __nv_bfloat16* ksrc = kcol[half] + slot * p.pool_ld;
-            const __nv_bfloat16* vsrc = vcol[half] + slot * p.pool_ld;
+            const uint32_t off = R * 128 + ((c ^ (R & 7)) << 4);
             const uint32_t nb = valid ? 16u : 0u;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const uint32_t off = r * 128 + ((c ^ (r & 7)) << 4);
-              cp_async16(ks + off, ksrc + 8 * c, nb);
-              cp_async16(vs + off, vsrc + 8 * c, nb);
-            }
+            cp_async16(ks + off, kcol[half] + slot * p.pool_ld + 8 * c, nb);
+            cp_async16(vs + off, vcol[half] + slot * p.pool_ld + 8 * c, nb);
           }
           cp_async_arrive_noinc(&b.kv_full[st]);
         }

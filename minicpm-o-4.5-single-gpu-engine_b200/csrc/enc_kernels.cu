@@ -167,16 +167,18 @@ __global__ void __launch_bounds__(kRThreads, 2) k_relattn(const __grid_constant_
       const int cur = nxt;
       if (t + 1 < n_kt) nxt = slot_of((t + 1) * kRK + lane);
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[st], ((t / kKVStages) & 1) ^ 1u, p.err)))) break;
-      const bool valid = t * kRK + lane < w.K;
-      const __nv_bfloat16* ksrc = kcol + (size_t)cur * p.pool_ld;
-      const __nv_bfloat16* vsrc = vcol + (size_t)cur * p.pool_ld;
       const uint32_t ks = smem_u32(smem + kKVOff + st * 2 * kKBytes), vs = ks + kKBytes;
-      const uint32_t nbytes = valid ? 16u : 0u;
+      // eight consecutive lanes copy one key row's eight 16-byte chunks (four whole 128-byte rows per copy
+      // instruction); row R's slot comes from lane R, which loaded it
+      const int c = lane & 7;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t off = lane * 128 + ((c ^ (lane & 7)) << 4);
-        cp_async16(ks + off, ksrc + 8 * c, nbytes);
-        cp_async16(vs + off, vsrc + 8 * c, nbytes);
+      for (int i = 0; i < kRK / 4; ++i) {
+        const int R = 4 * i + (lane >> 3);
+        const size_t slot = (size_t)__shfl_sync(0xffffffffu, cur, R);
+        const uint32_t nbytes = (t * kRK + R < w.K) ? 16u : 0u;
+        const uint32_t off = R * 128 + ((c ^ (R & 7)) << 4);
+        cp_async16(ks + off, kcol + slot * p.pool_ld + 8 * c, nbytes);
+        cp_async16(vs + off, vcol + slot * p.pool_ld + 8 * c, nbytes);
       }
       cp_async_arrive_noinc(&bars->kv_full[st]);
     }

@@ -1042,7 +1042,9 @@ def main() -> None:
                       flush=True)
         elif a.workload == "hift":
             torch.cuda.set_device(local)
-            rec = hift_record(torch.device("cuda", local), a.batch, a.steps, a.warmup, seed=14, peak_tf=1414.0)
+            pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+            peak_tf = json.load(open(pk)).get("bf16_tflops_sustained", 1400.0) if os.path.exists(pk) else 1400.0
+            rec = hift_record(torch.device("cuda", local), a.batch, a.steps, a.warmup, seed=14, peak_tf=peak_tf)
             if rank == 0:
                 print(json.dumps({"metric": "HiFT mel frames/s (steady windows)", "value": rec["mel_frames_per_s"],
                                   "unit": "mel frames/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,

@@ -556,6 +556,9 @@ typedef struct t2w_vocode_batch {
                             * reference's t2w_graphs option, HiFTGraphs, engine/runtime/hift_graph.py:22-88).  Calls
                             * replaying one graph must be ordered on the GPU (one stream, or synchronised); a caller
                             * that is itself capturing passes 0. */
+  void* noise_ready;       /* a cudaEvent_t, or NULL: the call waits for it (on `stream`) before it first reads `noise`,
+                            * so the caller may draw the noise on another stream while the call's first kernels (mel
+                            * input, conv_pre, the f0 predictor) run. */
 } t2w_vocode_batch;
 /* Output samples of a call (the sum), per window (per_stream, may be NULL) and each window's frames F_i (frames, may
  * be NULL); -1 on an invalid batch. */

@@ -127,6 +127,7 @@ class B200HiFT:
         self.max_frames = max_frames
         self._seeds: dict = {}  # handle -> [noise seed, chunks so far]
         self._gens: dict = {}  # handle -> its device generator, re-seeded for every chunk
+        self._side = None  # the stream the seeded noise is drawn on (created on first use)
 
     @classmethod
     def from_module(cls, hift, cfg: HiFTConfig = HIFT, **kw) -> "B200HiFT":
@@ -174,6 +175,11 @@ class B200HiFT:
         self._seeds.pop(int(handle), None)
         self._gens.pop(int(handle), None)
 
+    def _draw_stream(self) -> torch.cuda.Stream:
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        return self._side
+
     def _draw(self, g: torch.Generator, seed: int, rand_ini: torch.Tensor, noise: torch.Tensor) -> None:
         """``hift_noise`` for one row, in place: ``rand_ini`` [1, dim] then ``noise`` [1, dim, n] drawn as a fresh
         generator seeded with ``seed`` draws them (``manual_seed`` restarts a CUDA generator's Philox offset at 0, and
@@ -206,17 +212,28 @@ class B200HiFT:
         if tot < 0:
             raise L.T2WError("t2w_vocode_samples", -1)
         dim = self.cfg.harmonics + 1
+        ready = None
         with torch.cuda.device(self.device):
-            if noise is None:  # every row's draws straight into the packed buffers the library reads
+            if noise is None:
+                # every row's draws straight into the packed buffers the library reads, on a stream of their own: the
+                # call waits for them only before its harmonic source, so they overlap its first kernels
+                main = torch.cuda.current_stream()
+                side = main if torch.cuda.is_current_stream_capturing() else self._draw_stream()
                 samples = [480 * frames[i] for i in range(n)]
-                rand_ini = torch.empty(n, dim, dtype=torch.float32, device=self.device)
-                nz = torch.empty(dim * sum(samples), dtype=torch.float32, device=self.device)
-                o = 0
-                for i, h in enumerate(handles):
-                    seed, chunks = self._seeds[int(h)]
-                    self._draw(self._gens[int(h)], chunk_noise_seed(seed, chunks), rand_ini[i:i + 1],
-                               nz[o:o + dim * samples[i]].view(1, dim, samples[i]))
-                    o += dim * samples[i]
+                with torch.cuda.stream(side):
+                    rand_ini = torch.empty(n, dim, dtype=torch.float32, device=self.device)
+                    nz = torch.empty(dim * sum(samples), dtype=torch.float32, device=self.device)
+                    o = 0
+                    for i, h in enumerate(handles):
+                        seed, chunks = self._seeds[int(h)]
+                        self._draw(self._gens[int(h)], chunk_noise_seed(seed, chunks), rand_ini[i:i + 1],
+                                   nz[o:o + dim * samples[i]].view(1, dim, samples[i]))
+                        o += dim * samples[i]
+                if side is not main:
+                    ready = torch.cuda.Event()
+                    ready.record(side)
+                    rand_ini.record_stream(main)  # the buffers live until the vocoder's stream has read them
+                    nz.record_stream(main)
             else:
                 rand_ini = torch.cat([d[0].reshape(1, dim) for d in noise]).to(self.device, torch.float32).contiguous()
                 nz = torch.cat([d[1].reshape(-1) for d in noise]).to(self.device, torch.float32).contiguous()
@@ -228,7 +245,8 @@ class B200HiFT:
             src = ctypes.c_void_p(source.data_ptr()) if source is not None else None
             b = L.VocodeBatch(n, hs, ts, ls, ctypes.c_void_p(mel_rows.data_ptr()), ctypes.c_void_p(rand_ini.data_ptr()),
                               ctypes.c_void_p(nz.data_ptr()), ctypes.c_void_p(out.data_ptr()), src, None,
-                              1 if self.use_graphs else 0)
+                              1 if self.use_graphs else 0,
+                              ctypes.c_void_p(ready.cuda_event) if ready is not None else None)
             L.call("t2w_vocode", self.handle, ctypes.byref(b), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         for h in handles:
             self._seeds[int(h)][1] += 1

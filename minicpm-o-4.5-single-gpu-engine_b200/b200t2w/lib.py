@@ -109,7 +109,7 @@ class VocodeBatch(ctypes.Structure):
     _fields_ = [("n_streams", ctypes.c_int32), ("handle", ctypes.POINTER(ctypes.c_int32)),
                 ("T", ctypes.POINTER(ctypes.c_int32)), ("last", ctypes.POINTER(ctypes.c_uint8))] + \
                [(n, ctypes.c_void_p) for n in ("mel", "rand_ini", "noise", "out", "source", "speech")] + \
-               [("flags", ctypes.c_uint32)]
+               [("flags", ctypes.c_uint32), ("noise_ready", ctypes.c_void_p)]
 
 
 class TConvArgs(ctypes.Structure):

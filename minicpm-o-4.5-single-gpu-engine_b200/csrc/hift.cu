@@ -1364,6 +1364,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     if (e0 == cudaSuccess) sg.used = true;
     if (graph && e0 == cudaSuccess)
       e0 = cudaMemcpyAsync(ws + o_gmel, b->mel, (size_t)mel_rows * c.mel * 4, cudaMemcpyDeviceToDevice, st);
+    if (graph && e0 == cudaSuccess && b->noise_ready)  // the caller's noise draws, before the copy reads them
+      e0 = cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(b->noise_ready), 0);
     if (graph && e0 == cudaSuccess)
       e0 = cudaMemcpyAsync(ws + o_gnoise, b->noise, (size_t)pl.samples * dim * 4, cudaMemcpyDeviceToDevice, st);
     if (e0 != cudaSuccess) {
@@ -1528,6 +1530,10 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   float* stft = reinterpret_cast<float*>(P(o_stft));
   {
     const dim3 sgrid((480 * h->max_frames + kSrcChunk - 1) / kSrcChunk, n);
+    if (!graph && b->noise_ready) {  // eager: the caller's noise draws (another stream) before the first read of them
+      rc = ck(cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(b->noise_ready), 0));
+      if (rc) return fail(rc);
+    }
     rc = ck(launch_k(k_source, sgrid, dim3(256), 0, st, (const float*)P(o_f0), drows, in_noise, (const float*)h->lin_w,
                      h->lin_b, c.harmonics + 1, (float)c.sample_rate, 480.f, c.nsf_alpha, c.nsf_sigma, c.voiced_threshold,
                      (const float*)h->cache, h->cache_ld, kMelCache * c.mel, src));

@@ -655,6 +655,9 @@ struct t2w_hift {
   std::unordered_map<uint64_t, int> seen;
   cudaStream_t cap_stream = nullptr;
   int64_t n_replays = 0, n_captures = 0, n_eager = 0;
+  // a call's f0 predictor, harmonic source and STFT run on `side`, beside conv_pre and stage 0's transposed conv
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
 };
 
 namespace {
@@ -1002,6 +1005,11 @@ void free_all(t2w_hift* h) {
   h->graphs.clear();
   if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
   h->cap_stream = nullptr;
+  if (h->side) cudaStreamDestroy(h->side);
+  if (h->fork_ev) cudaEventDestroy(h->fork_ev);
+  if (h->join_ev) cudaEventDestroy(h->join_ev);
+  h->side = nullptr;
+  h->fork_ev = h->join_ev = nullptr;
 }
 
 // ---- a call's plan
@@ -1204,6 +1212,19 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     for (int j = 0; j < i; ++j)
       if (b->handle[j] == b->handle[i]) return T2W_ERR_INVALID;
   }
+  if (!h->side) {  // once: the second stream of the call's independent branch, and its fork / join events
+    cudaError_t e = cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->fork_ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->join_ev, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      if (h->side) cudaStreamDestroy(h->side);
+      if (h->fork_ev) cudaEventDestroy(h->fork_ev);
+      h->side = nullptr;
+      h->fork_ev = nullptr;
+      return T2W_ERR_CUDA;
+    }
+  }
   HPlan pl;
   H_TRY(make_plan(h, n, b->handle, b->T, b->last, pl));
   const t2w_hift_config& c = h->cfg;
@@ -1387,7 +1408,16 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   // every launch of the call, on `st` (the caller's stream, or the capture stream of a graph)
   auto enqueue = [&](cudaStream_t st) -> int {
   int rc = T2W_OK;
-  auto fail = [](int r) { return r; };
+  const cudaStream_t st_main = st;
+  bool forked = false;  // the second stream has work the caller's stream has not waited for
+  auto fail = [&](int r) {
+    if (forked) {  // join before returning: the caller frees or drops the workspace on its own stream
+      cudaEventRecord(h->join_ev, h->side);
+      cudaStreamWaitEvent(st_main, h->join_ev, 0);
+      forked = false;
+    }
+    return r;
+  };
   {
     cudaError_t e1 = cudaSuccess;
     // buffers whose rows around the windows' data must read as zero and that no kernel writes in full: the mel rows and
@@ -1463,6 +1493,15 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      o_mel3 ? reinterpret_cast<float*>(P(o_mel3)) : nullptr));
     if (rc) return fail(rc);
   }
+  // 2 - 4 run on the vocoder's second stream, beside 5 and stage 0's transposed conv, which do not depend on them and
+  // share no buffer with them (every buffer of the workspace has its own range); stage 0's source branch, their
+  // first reader, waits for them.  (Graph capture follows the fork and the join.)
+  rc = ck(cudaEventRecord(h->fork_ev, st_main));
+  if (rc) return fail(rc);
+  rc = ck(cudaStreamWaitEvent(h->side, h->fork_ev, 0));
+  if (rc) return fail(rc);
+  forked = true;
+  st = h->side;
   // 2. f0 predictor: convs + ELU, then |linear|.  On the tensor cores (fp32-level accuracy): the first layer over the
   // tripled mel rows (80 channels), the others in split form; the first writes its ELU output as [hi | lo] pairs, the
   // middle layers read and write pairs, the last writes plain fp32 for the head.
@@ -1543,6 +1582,9 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      h->x3));
     if (rc) return fail(rc);
   }
+  rc = ck(cudaEventRecord(h->join_ev, st));
+  st = st_main;
+  if (rc) return fail(rc);  // (the join's wait comes at stage 0's source branch; fail() waits for the side here)
   // 5. conv_pre
   float* x = reinterpret_cast<float*>(P(o_x0));
   if (pre_tc) {  // over the tripled mel rows: fp32-level products on the tensor cores; the fp32 mode writes pairs
@@ -1623,6 +1665,11 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     if (s == 2) {
       rc = ck(launch_k(k_reflect_row, dim3(n), dim3(64), 0, st, xs, drows, Cs));
       if (rc) return fail(rc);
+    }
+    if (s == 0) {  // the f0 predictor, source and STFT (second stream) are done
+      rc = ck(cudaStreamWaitEvent(st, h->join_ev, 0));
+      if (rc) return fail(rc);
+      forked = false;
     }
     // source branch: strided conv of the STFT, then its ResBlock (in place)
     float* sd = reinterpret_cast<float*>(P(o_sd[s]));

@@ -1493,9 +1493,10 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      o_mel3 ? reinterpret_cast<float*>(P(o_mel3)) : nullptr));
     if (rc) return fail(rc);
   }
-  // 2 - 4 run on the vocoder's second stream, beside 5 and stage 0's transposed conv, which do not depend on them and
-  // share no buffer with them (every buffer of the workspace has its own range); stage 0's source branch, their
-  // first reader, waits for them.  (Graph capture follows the fork and the join.)
+  // 2 - 4 and every stage's source branch run on the vocoder's second stream, beside conv_pre and the stages'
+  // transposed convs and ResBlocks, which share no buffer with them (every buffer of the workspace has its own range;
+  // a stage's source-branch buffers are read or reused only from its fan-out on); each fan-out waits for its stage's
+  // source branch.  (Graph capture follows the fork and the joins.)
   rc = ck(cudaEventRecord(h->fork_ev, st_main));
   if (rc) return fail(rc);
   rc = ck(cudaStreamWaitEvent(h->side, h->fork_ev, 0));
@@ -1582,9 +1583,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
                      h->x3));
     if (rc) return fail(rc);
   }
-  rc = ck(cudaEventRecord(h->join_ev, st));
-  st = st_main;
-  if (rc) return fail(rc);  // (the join's wait comes at stage 0's source branch; fail() waits for the side here)
+  st = st_main;  // the second stream goes on with stage 0's source branch
   // 5. conv_pre
   float* x = reinterpret_cast<float*>(P(o_x0));
   if (pre_tc) {  // over the tripled mel rows: fp32-level products on the tensor cores; the fp32 mode writes pairs
@@ -1666,12 +1665,9 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       rc = ck(launch_k(k_reflect_row, dim3(n), dim3(64), 0, st, xs, drows, Cs));
       if (rc) return fail(rc);
     }
-    if (s == 0) {  // the f0 predictor, source and STFT (second stream) are done
-      rc = ck(cudaStreamWaitEvent(st, h->join_ev, 0));
-      if (rc) return fail(rc);
-      forked = false;
-    }
-    // source branch: strided conv of the STFT, then its ResBlock (in place)
+    // source branch (second stream): strided conv of the STFT, then its ResBlock (in place)
+    st = h->side;
+    forked = true;
     float* sd = reinterpret_cast<float*>(P(o_sd[s]));
     float* ta = reinterpret_cast<float*>(P(o_ta[s]));
     if (src_tc) {  // TF32 (the source branch is part of the reference's decode_tf32 stages)
@@ -1780,7 +1776,12 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       return T2W_OK;
     };
     rc = resblock(g.src, sd, ta, reinterpret_cast<float*>(P(o_ar[s][0])), nullptr, src_tc);  // ar[0]: scratch
+    if (!rc) rc = ck(cudaEventRecord(h->join_ev, st));
+    st = st_main;
     if (rc) return fail(rc);
+    rc = ck(cudaStreamWaitEvent(st, h->join_ev, 0));  // the fan-out below reads sd and reuses ar[0]
+    if (rc) return fail(rc);
+    forked = false;
     float* xr[3] = {reinterpret_cast<float*>(P(o_xr[s][0])), reinterpret_cast<float*>(P(o_xr[s][1])),
                     reinterpret_cast<float*>(P(o_xr[s][2]))};
     float* ar[3] = {reinterpret_cast<float*>(P(o_ar[s][0])), reinterpret_cast<float*>(P(o_ar[s][1])),

@@ -658,6 +658,9 @@ struct t2w_hift {
   // a call's f0 predictor, harmonic source and STFT run on `side`, beside conv_pre and stage 0's transposed conv
   cudaStream_t side = nullptr;
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  // stages 0 and 1: ResBlocks 1 and 2 on streams of their own, beside ResBlock 0
+  cudaStream_t res_st[2] = {nullptr, nullptr};
+  cudaEvent_t res_ev[2] = {nullptr, nullptr};
 };
 
 namespace {
@@ -1010,6 +1013,12 @@ void free_all(t2w_hift* h) {
   if (h->join_ev) cudaEventDestroy(h->join_ev);
   h->side = nullptr;
   h->fork_ev = h->join_ev = nullptr;
+  for (int k = 0; k < 2; ++k) {
+    if (h->res_st[k]) cudaStreamDestroy(h->res_st[k]);
+    if (h->res_ev[k]) cudaEventDestroy(h->res_ev[k]);
+    h->res_st[k] = nullptr;
+    h->res_ev[k] = nullptr;
+  }
 }
 
 // ---- a call's plan
@@ -1212,16 +1221,27 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     for (int j = 0; j < i; ++j)
       if (b->handle[j] == b->handle[i]) return T2W_ERR_INVALID;
   }
-  if (!h->side) {  // once: the second stream of the call's independent branch, and its fork / join events
+  if (!h->side) {  // once: the streams of the call's independent branches, and their fork / join events
     cudaError_t e = cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->fork_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->join_ev, cudaEventDisableTiming);
+    for (int k = 0; k < 2; ++k) {
+      if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->res_st[k], cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->res_ev[k], cudaEventDisableTiming);
+    }
     if (e != cudaSuccess) {
       set_cuda_error(e);
       if (h->side) cudaStreamDestroy(h->side);
       if (h->fork_ev) cudaEventDestroy(h->fork_ev);
+      if (h->join_ev) cudaEventDestroy(h->join_ev);
       h->side = nullptr;
-      h->fork_ev = nullptr;
+      h->fork_ev = h->join_ev = nullptr;
+      for (int k = 0; k < 2; ++k) {
+        if (h->res_st[k]) cudaStreamDestroy(h->res_st[k]);
+        if (h->res_ev[k]) cudaEventDestroy(h->res_ev[k]);
+        h->res_st[k] = nullptr;
+        h->res_ev[k] = nullptr;
+      }
       return T2W_ERR_CUDA;
     }
   }
@@ -1262,7 +1282,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   const int xsm = h->x3 ? 2 : 1;  // the fp32 tensor-core mode keeps conv inputs as [hi | lo] pairs: twice the floats
   const size_t o_x0 = add((size_t)pl.A[0] * C0 * 4 * xsm);
   // per stage: x (ups output), xr[3] ResBlock streams, ar[3] / sd scratch of the stage's size
-  size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3];
+  // (stages 0 and 1: tx[2], the scratch of ResBlocks 1 and 2, which run beside ResBlock 0 and its scratch ta)
+  size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3], o_tx[3][2];
   for (int s = 0; s < 3; ++s) {
     const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
     o_xs[s] = add(sz);
@@ -1270,6 +1291,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     for (int j = 0; j < 3; ++j) o_ar[s][j] = add(sz * xsm);
     o_sd[s] = add(sz * xsm);
     o_ta[s] = add(sz * xsm);
+    for (int k = 0; k < 2; ++k) o_tx[s][k] = s < 2 ? add(sz * xsm) : o_ta[s];
   }
   const int post_ld = h->post_tc ? 32 : kNfft + 2;  // conv_post's output (18 columns; 32 on the tensor cores)
   const size_t o_post = add((size_t)pl.A[3] * post_ld * 4);
@@ -1409,12 +1431,20 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   auto enqueue = [&](cudaStream_t st) -> int {
   int rc = T2W_OK;
   const cudaStream_t st_main = st;
-  bool forked = false;  // the second stream has work the caller's stream has not waited for
+  bool forked = false;      // the second stream has work the caller's stream has not waited for
+  bool res_forked = false;  // so have the ResBlock streams
   auto fail = [&](int r) {
     if (forked) {  // join before returning: the caller frees or drops the workspace on its own stream
       cudaEventRecord(h->join_ev, h->side);
       cudaStreamWaitEvent(st_main, h->join_ev, 0);
       forked = false;
+    }
+    if (res_forked) {
+      for (int k = 0; k < 2; ++k) {
+        cudaEventRecord(h->res_ev[k], h->res_st[k]);
+        cudaStreamWaitEvent(st_main, h->res_ev[k], 0);
+      }
+      res_forked = false;
     }
     return r;
   };
@@ -1440,6 +1470,8 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       if (!(h->tc_parts >> (3 * s + 1) & 1u)) {
         zero(o_sd[s], sz);
         zero(o_ta[s], sz);
+        if (s < 2)
+          for (int k = 0; k < 2; ++k) zero(o_tx[s][k], sz);
       }
       if (!(h->tc_parts >> (3 * s) & 1u)) zero(o_xs[s], sz);
       if (h->tf32 && !(h->tc_parts >> (3 * s + 2) & 1u))
@@ -1795,9 +1827,27 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     rc = ck(launch_k(k_fanout, dim3(grid_for(nel / 4)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs,
                      h->x3, res_tc ? 1 : 0, xs, ar[0], ar[1], ar[2], sn));
     if (rc) return fail(rc);
-    for (int j = 0; j < 3; ++j) {
-      rc = resblock(g.res[j], xr[j], ar[j], ta, xs, res_tc);
+    // the three ResBlocks read xs and write their own streams; in stages 0 and 1 (few row tiles at small batches)
+    // ResBlocks 1 and 2 run on streams of their own, each with scratch of its own
+    const bool par = s < 2;
+    if (par) {
+      rc = ck(cudaEventRecord(h->fork_ev, st));
+      for (int k = 0; k < 2 && !rc; ++k) rc = ck(cudaStreamWaitEvent(h->res_st[k], h->fork_ev, 0));
       if (rc) return fail(rc);
+      res_forked = true;
+    }
+    for (int j = 0; j < 3; ++j) {
+      float* tmp = (par && j > 0) ? reinterpret_cast<float*>(P(o_tx[s][j - 1])) : ta;
+      if (par && j > 0) st = h->res_st[j - 1];
+      rc = resblock(g.res[j], xr[j], ar[j], tmp, xs, res_tc);
+      if (!rc && par && j > 0) rc = ck(cudaEventRecord(h->res_ev[j - 1], st));
+      st = st_main;
+      if (rc) return fail(rc);
+    }
+    if (par) {  // the average below reads all three
+      for (int k = 0; k < 2 && !rc; ++k) rc = ck(cudaStreamWaitEvent(st, h->res_ev[k], 0));
+      if (rc) return fail(rc);
+      res_forked = false;
     }
     // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before
     // the next stage's transposed conv, leaky_relu(., 0.01) before conv_post

@@ -658,7 +658,7 @@ struct t2w_hift {
   // a call's f0 predictor, harmonic source and STFT run on `side`, beside conv_pre and stage 0's transposed conv
   cudaStream_t side = nullptr;
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
-  // stages 0 and 1: ResBlocks 1 and 2 on streams of their own, beside ResBlock 0
+  // every stage: ResBlocks 1 and 2 on streams of their own, beside ResBlock 0
   cudaStream_t res_st[2] = {nullptr, nullptr};
   cudaEvent_t res_ev[2] = {nullptr, nullptr};
 };
@@ -1282,7 +1282,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
   const int xsm = h->x3 ? 2 : 1;  // the fp32 tensor-core mode keeps conv inputs as [hi | lo] pairs: twice the floats
   const size_t o_x0 = add((size_t)pl.A[0] * C0 * 4 * xsm);
   // per stage: x (ups output), xr[3] ResBlock streams, ar[3] / sd scratch of the stage's size
-  // (stages 0 and 1: tx[2], the scratch of ResBlocks 1 and 2, which run beside ResBlock 0 and its scratch ta)
+  // (tx[2]: the scratch of ResBlocks 1 and 2, which run beside ResBlock 0 and its scratch ta)
   size_t o_xs[3], o_xr[3][3], o_ar[3][3], o_sd[3], o_ta[3], o_tx[3][2];
   for (int s = 0; s < 3; ++s) {
     const size_t sz = (size_t)pl.A[s + 1] * (C0 >> (s + 1)) * 4;
@@ -1291,7 +1291,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     for (int j = 0; j < 3; ++j) o_ar[s][j] = add(sz * xsm);
     o_sd[s] = add(sz * xsm);
     o_ta[s] = add(sz * xsm);
-    for (int k = 0; k < 2; ++k) o_tx[s][k] = s < 2 ? add(sz * xsm) : o_ta[s];
+    for (int k = 0; k < 2; ++k) o_tx[s][k] = add(sz * xsm);
   }
   const int post_ld = h->post_tc ? 32 : kNfft + 2;  // conv_post's output (18 columns; 32 on the tensor cores)
   const size_t o_post = add((size_t)pl.A[3] * post_ld * 4);
@@ -1470,8 +1470,7 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
       if (!(h->tc_parts >> (3 * s + 1) & 1u)) {
         zero(o_sd[s], sz);
         zero(o_ta[s], sz);
-        if (s < 2)
-          for (int k = 0; k < 2; ++k) zero(o_tx[s][k], sz);
+        for (int k = 0; k < 2; ++k) zero(o_tx[s][k], sz);
       }
       if (!(h->tc_parts >> (3 * s) & 1u)) zero(o_xs[s], sz);
       if (h->tf32 && !(h->tc_parts >> (3 * s + 2) & 1u))
@@ -1827,28 +1826,23 @@ int t2w_vocode(t2w_hift* h, const t2w_vocode_batch* b, void* stream) {
     rc = ck(launch_k(k_fanout, dim3(grid_for(nel / 4)), dim3(256), 0, st, (const float*)xs, (const float*)sd, nel, Cs,
                      h->x3, res_tc ? 1 : 0, xs, ar[0], ar[1], ar[2], sn));
     if (rc) return fail(rc);
-    // the three ResBlocks read xs and write their own streams; in stages 0 and 1 (few row tiles at small batches)
-    // ResBlocks 1 and 2 run on streams of their own, each with scratch of its own
-    const bool par = s < 2;
-    if (par) {
-      rc = ck(cudaEventRecord(h->fork_ev, st));
-      for (int k = 0; k < 2 && !rc; ++k) rc = ck(cudaStreamWaitEvent(h->res_st[k], h->fork_ev, 0));
-      if (rc) return fail(rc);
-      res_forked = true;
-    }
+    // the three ResBlocks read xs and write their own streams: ResBlocks 1 and 2 run on streams of their own, beside
+    // ResBlock 0, each with scratch of its own (at small batches a ResBlock's convs cover few row tiles)
+    rc = ck(cudaEventRecord(h->fork_ev, st));
+    for (int k = 0; k < 2 && !rc; ++k) rc = ck(cudaStreamWaitEvent(h->res_st[k], h->fork_ev, 0));
+    if (rc) return fail(rc);
+    res_forked = true;
     for (int j = 0; j < 3; ++j) {
-      float* tmp = (par && j > 0) ? reinterpret_cast<float*>(P(o_tx[s][j - 1])) : ta;
-      if (par && j > 0) st = h->res_st[j - 1];
+      float* tmp = j > 0 ? reinterpret_cast<float*>(P(o_tx[s][j - 1])) : ta;
+      if (j > 0) st = h->res_st[j - 1];
       rc = resblock(g.res[j], xr[j], ar[j], tmp, xs, res_tc);
-      if (!rc && par && j > 0) rc = ck(cudaEventRecord(h->res_ev[j - 1], st));
+      if (!rc && j > 0) rc = ck(cudaEventRecord(h->res_ev[j - 1], st));
       st = st_main;
       if (rc) return fail(rc);
     }
-    if (par) {  // the average below reads all three
-      for (int k = 0; k < 2 && !rc; ++k) rc = ck(cudaStreamWaitEvent(st, h->res_ev[k], 0));
-      if (rc) return fail(rc);
-      res_forked = false;
-    }
+    for (int k = 0; k < 2 && !rc; ++k) rc = ck(cudaStreamWaitEvent(st, h->res_ev[k], 0));  // the average reads all three
+    if (rc) return fail(rc);
+    res_forked = false;
     // the stage's output (x0 + x1 + x2) / 3 with the activation in front of what reads it: leaky_relu(., 0.1) before
     // the next stage's transposed conv, leaky_relu(., 0.01) before conv_post
     // conv_post on the tensor cores, and every transposed conv of the fp32 tensor-core mode, read [hi | lo] pairs

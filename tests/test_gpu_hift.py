@@ -226,3 +226,33 @@ def test_graph_replay_equals_eager(split_fp32):
     assert cnt["captures"] >= 1 and cnt["replays"] >= 3
     assert ve.counts["replays"] == 0
     vg.check()
+
+
+@pytest.mark.parametrize("split_fp32", [False, True], ids=["tf32", "split_fp32"])
+def test_caller_stream_equals_default_stream(split_fp32):
+    """A call forks its independent branches (the f0 predictor, source and STFT, every stage's source branch, two of
+    each stage's three ResBlocks, the seeded draws) onto streams of the vocoder's own and joins them back: called from
+    a non-blocking stream of the caller's, with back-to-back calls and no synchronisation between them, the samples
+    equal the default-stream calls' bit for bit."""
+    cfg = HIFT_TINY
+    hift = ho.build_hift(cfg, seed=0)
+    kw = dict(device="cuda", max_frames=64, n_streams=8, split_fp32=split_fp32)
+    va = B200HiFT.from_module(hift, cfg, **kw)
+    vb = B200HiFT.from_module(hift, cfg, **kw)
+    seeds = [3, 4, 9]
+    ha = [va.new_stream(s) for s in seeds]
+    hb = [vb.new_stream(s) for s in seeds]
+    g = torch.Generator().manual_seed(12)
+    plan = [[50, 50, 50], [50, 50, 50], [50, 50, 50], [20, 45, 9]]
+    calls = [[torch.randn(cfg.mel, T, generator=g) - 2.0 for T in Ts] for Ts in plan]
+    ref = [va.vocode(ha, m, [c == len(plan) - 1] * 3) for c, m in enumerate(calls)]
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        got = [vb.vocode(hb, m, [c == len(plan) - 1] * 3) for c, m in enumerate(calls)]
+    side.synchronize()
+    for c, (ra, rb) in enumerate(zip(ref, got)):
+        for a, b in zip(ra, rb):
+            assert a.numel() == b.numel() and torch.equal(a, b), c
+    va.check()
+    vb.check()
